@@ -1,0 +1,85 @@
+"""ctypes binding of ``lib/libh3b.so`` (declared in ``include/h3b.h``).
+
+There is no fallback: if the library is missing or does not load, every op raises. A nonzero return code from the
+library becomes ``RuntimeError(h3b_last_error())``, the way the reference's ``TORCH_CHECK`` failures surface.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "lib" / "libh3b.so"
+
+P = ctypes.c_void_p
+I32 = ctypes.c_int
+I64 = ctypes.c_int64
+F32 = ctypes.c_float
+SZ = ctypes.c_size_t
+
+
+class Epilogue(ctypes.Structure):
+    """Mirror of ``h3b_epilogue``."""
+    _fields_ = [
+        ("alpha", F32),
+        ("alpha_dev", P),
+        ("row_scale", P),
+        ("col_scale", P),
+        ("col_scale_scalar", I32),
+        ("bias", P),
+        ("act", I32),
+        ("residual", P),
+        ("ldr", I64),
+        ("gate", P),
+        ("D", P),
+        ("ldd", I64),
+    ]
+
+
+# name -> argtypes (restype is int unless listed in _RESTYPES)
+SIGNATURES: dict[str, list] = {
+    "h3b_last_error": [],
+    "h3b_version": [],
+    "h3b_resid_norm_quant": [P, P, P, P, I64, P, I32, P, P, P, I64, P, P, P, P, F32, I64, I32, P],
+    "h3b_quant_fp8_rows": [P, I64, I64, I32, P, P, P],
+    "h3b_amax_bf16": [P, I64, I64, I32, P, P],
+    "h3b_quant_nvfp4_tensor": [P, I64, I64, I32, P, P, P, P, P],
+    "h3b_quant_nvfp4_workspace_bytes": [],
+    "h3b_quant_nvfp4": [P, I64, I64, I32, P, P, P, P, P],
+    "h3b_pack_weight_fp8": [P, I64, I32, I32, P, P, P, P],
+    "h3b_pack_weight_nvfp4": [P, I64, I32, P, P, P, P, P],
+    "h3b_gemm_fp8": [P, P, I64, I64, I64, ctypes.POINTER(Epilogue), P],
+    "h3b_gemm_nvfp4": [P, P, P, P, I64, I64, I64, ctypes.POINTER(Epilogue), P],
+    "h3b_device_status": [ctypes.POINTER(I32)],
+    "h3b_reset_device_status": [],
+}
+_RESTYPES = {"h3b_last_error": ctypes.c_char_p, "h3b_version": ctypes.c_char_p,
+             "h3b_quant_nvfp4_workspace_bytes": SZ}
+
+_lib: ctypes.CDLL | None = None
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library, with argument types set. Raises if it was not built."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"h3b: {LIB_PATH} is missing; build it with `python fasth3-gb300_b200/build.py` "
+                               "(there is no CPU fallback)")
+        handle = ctypes.CDLL(str(LIB_PATH), mode=os.RTLD_NOW | os.RTLD_GLOBAL)
+        for name, argtypes in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.argtypes = argtypes
+            fn.restype = _RESTYPES.get(name, ctypes.c_int)
+        _lib = handle
+    return _lib
+
+
+def check(rc: int) -> None:
+    if rc != 0:
+        msg = lib().h3b_last_error().decode(errors="replace")
+        raise RuntimeError(f"h3b error {rc}: {msg}")
+
+
+def call(name: str, *args) -> None:
+    check(getattr(lib(), name)(*args))

@@ -1,0 +1,26 @@
+// Error reporting and version of the h3b C ABI.
+#include "common.cuh"
+
+#include <cstring>
+
+namespace h3b {
+
+namespace {
+thread_local char g_last_error[512] = {0};
+}
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+void clear_error() { g_last_error[0] = 0; }
+
+}  // namespace h3b
+
+extern "C" const char* h3b_last_error(void) { return h3b::g_last_error; }
+
+extern "C" const char* h3b_version(void) { return "h3b 0.1 sm_100a"; }

@@ -1,0 +1,468 @@
+// Persistent, warp-specialized tcgen05 GEMMs for the DiT linears: FP8 (kind::f8f6f4, e4m3 x e4m3) and NVFP4
+// (kind::mxf4nvf4 block16, e2m1 x e2m1 with ue4m3 scales per 16 K-elements), fp32 accumulators in tensor memory,
+// and a fused epilogue (scales, bias, GELU-tanh, gated residual, bf16 store).
+//
+// CTA = 6 warps, one CTA per SM (the shared-memory footprint forbids two):
+//   warp 0   TMA producer: A/B tiles (128-byte swizzle) and, for NVFP4, the scale-factor atoms (bulk copies)
+//   warp 1   TMEM allocator + MMA issuer (one thread): SMEM->TMEM scale copies, 4 MMAs per 128-byte K block
+//   warps 2-5 epilogue: TMEM -> registers -> epilogue math -> global (warp w reads TMEM lanes 32*(w%4)..+31)
+// Two accumulator buffers in TMEM let the epilogue of tile j overlap the main loop of tile j+1.
+// Every mbarrier wait is bounded (2 s); on expiry the CTA records H3B_ETIMEOUT in a device status word, the other
+// roles abandon their loops, in-flight copies and MMAs are drained (again bounded) and TMEM is freed.
+#include "common.cuh"
+#include "sm100.cuh"
+
+#include <cudaTypedefs.h>
+#include <algorithm>
+
+namespace h3b {
+
+__device__ int g_gemm_status = 0;
+
+namespace {
+
+using namespace sm100;
+
+constexpr int BM = 128;
+constexpr int KB_BYTES = 128;  // one swizzle atom of K per stage
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+template <bool FP4, int BN>
+struct Cfg {
+  static constexpr int kStages = FP4 ? 4 : 4;
+  static constexpr int kABytes = BM * KB_BYTES;
+  static constexpr int kBBytes = BN * KB_BYTES;
+  static constexpr int kSfaBytes = FP4 ? 2048 : 0;  // 4 atoms: 128 rows x 16 scales
+  static constexpr int kSfbBytes = FP4 ? 4096 : 0;  // 2 row groups x 4 atoms
+  static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
+  static constexpr int kAccCols = BN;
+  static constexpr int kSfaCol = 2 * BN;        // TMEM column of the A scales (16 columns)
+  static constexpr int kSfbCol = 2 * BN + 16;   // TMEM column of the B scales (32 columns)
+  static constexpr int kTmemCols = 512;
+  static constexpr int kElemsPerKB = FP4 ? 256 : 128;
+  // barriers + bookkeeping after the stages
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256;
+  static_assert(2 * BN + (FP4 ? 48 : 0) <= kTmemCols, "TMEM budget");
+  static_assert(kStageBytes % 1024 == 0, "stages must keep 1024-byte alignment");
+};
+
+struct Epi {
+  float alpha;
+  const float* alpha_dev;
+  const float* row_scale;
+  const float* col_scale;
+  int col_scalar;
+  const bf16* bias;
+  int act;
+  const bf16* residual;
+  int64_t ldr;
+  const bf16* gate;
+  bf16* D;
+  int64_t ldd;
+};
+
+struct Problem {
+  int M, N, K;
+  int m_blocks, n_blocks, k_blocks;
+  int num_tiles;
+  const uint8_t* sfa;  // NVFP4 scale atoms
+  const uint8_t* sfb;
+  int sfb_groups;      // 128-row groups present in the B scale buffer
+};
+
+__device__ __forceinline__ void tile_coords(int tile, const Problem& p, int& mb, int& nb) {
+  constexpr int GN = 8;  // n-blocks per raster group: the group's B tiles stay in L2 while A streams
+  const int per_group = p.m_blocks * GN;
+  const int g = tile / per_group;
+  const int in = tile - g * per_group;
+  const int gn = min(GN, p.n_blocks - g * GN);
+  mb = in / gn;
+  nb = g * GN + (in - mb * gn);
+}
+
+__device__ __forceinline__ float gelu_tanh(float v) {
+  float t;
+  const float u = 0.7978845608028654f * (v + 0.044715f * v * v * v);
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u));
+  return 0.5f * v * (1.f + t);
+}
+
+template <bool FP4, int BN>
+__global__ void __launch_bounds__(192, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Problem p,
+                const Epi e) {
+  using C = Cfg<FP4, BN>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* acc_full = empty + C::kStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_base_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_base_slot;
+
+  auto fail = [&]() {
+    *abort_flag = 1;
+    atomicExch(&g_gemm_status, H3B_ETIMEOUT);
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;  // loads armed but possibly not consumed, for the error-path drain
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, p, mb, nb);
+        const int m0 = mb * BM, n0 = nb * BN;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag, kWaitLimitNs)) {
+            fail();
+            ok = false;
+            break;
+          }
+          uint8_t* sA = smem + stage * C::kStageBytes;
+          uint8_t* sB = sA + C::kABytes;
+          mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
+          tma_load_2d(sA, &tmA, kb * KB_BYTES, m0, &full[stage]);
+          tma_load_2d(sB, &tmB, kb * KB_BYTES, n0, &full[stage]);
+          if constexpr (FP4) {
+            uint8_t* sSFA = sB + C::kBBytes;
+            uint8_t* sSFB = sSFA + C::kSfaBytes;
+            const size_t kstride = (size_t)(p.K / 64) * 512;  // bytes per 128-row group
+            bulk_load(sSFA, p.sfa + (size_t)mb * kstride + (size_t)kb * 2048, 2048, &full[stage]);
+            const int g0 = n0 >> 7;
+            const int g1 = min(g0 + 1, p.sfb_groups - 1);
+            bulk_load(sSFB, p.sfb + (size_t)g0 * kstride + (size_t)kb * 2048, 2048, &full[stage]);
+            bulk_load(sSFB + 2048, p.sfb + (size_t)g1 * kstride + (size_t)kb * 2048, 2048, &full[stage]);
+          }
+          issued = min(issued + 1, C::kStages);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // drain: every armed stage completes its transaction bytes once its copies land
+        for (int i = 0; i < C::kStages; ++i) {
+          int s = stage - 1 - i;
+          uint32_t ph = phase;
+          if (s < 0) {
+            s += C::kStages;
+            ph ^= 1;
+          }
+          if (i < issued) {
+            volatile int no_abort = 0;
+            mbar_wait_bounded(&full[s], ph, &no_abort, kWaitLimitNs / 4);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = FP4 ? idesc_nvf4(BN) : idesc_e4m3(BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t acc_phase[2] = {0, 0};
+      int j = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++j) {
+        int mb, nb;
+        tile_coords(tile, p, mb, nb);
+        const int buf = j & 1;
+        if (!mbar_wait_bounded(&acc_empty[buf], acc_phase[buf] ^ 1, abort_flag, kWaitLimitNs)) {
+          fail();
+          break;
+        }
+        acc_phase[buf] ^= 1;
+        tc_fence_after();
+        const uint32_t d = tmem + buf * C::kAccCols;
+        // NVFP4 B tiles of 192 rows start mid-atom on odd n-blocks: the first 64 rows sit in columns 2-3 of the atom
+        const uint32_t sfb_shift = (FP4 && (BN % 128) != 0) ? (uint32_t)(((nb * BN) & 127) >> 5) : 0u;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait_bounded(&full[stage], phase, abort_flag, kWaitLimitNs)) {
+            fail();
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint8_t* sA = smem + stage * C::kStageBytes;
+          uint8_t* sB = sA + C::kABytes;
+          const uint64_t da = desc_k_sw128(smem_addr(sA));
+          const uint64_t db = desc_k_sw128(smem_addr(sB));
+          if constexpr (FP4) {
+            const uint32_t sSFA = smem_addr(sB + C::kBBytes);
+            const uint32_t sSFB = sSFA + C::kSfaBytes;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              tmem_cp_32x128_x4(tmem + C::kSfaCol + 4 * i, desc_sf_atom(sSFA + 512 * i));
+              tmem_cp_32x128_x4(tmem + C::kSfbCol + 8 * i, desc_sf_atom(sSFB + 512 * i));
+              tmem_cp_32x128_x4(tmem + C::kSfbCol + 8 * i + 4, desc_sf_atom(sSFB + 2048 + 512 * i));
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              mma_nvf4(d, da + 2 * i, db + 2 * i, idesc, (kb | i) != 0, tmem + C::kSfaCol + 4 * i,
+                       tmem + C::kSfbCol + 8 * i + sfb_shift);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) mma_e4m3(d, da + 2 * i, db + 2 * i, idesc, (kb | i) != 0);
+          }
+          tc_commit(&empty[stage]);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&acc_full[buf]);
+      }
+      // drain: wait until every MMA and copy issued above has finished before TMEM is freed
+      tc_commit(drain);
+      volatile int no_abort = 0;
+      if (!mbar_wait_bounded(drain, 0, &no_abort, kWaitLimitNs)) fail();
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const float alpha = e.alpha * (e.alpha_dev ? *e.alpha_dev : 1.f);
+    uint32_t acc_phase[2] = {0, 0};
+    int j = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++j) {
+      int mb, nb;
+      tile_coords(tile, p, mb, nb);
+      const int buf = j & 1;
+      const bool got = mbar_wait_bounded(&acc_full[buf], acc_phase[buf], abort_flag, kWaitLimitNs);
+      if (!__all_sync(0xffffffffu, got)) {
+        if (lane == 0) fail();
+        break;
+      }
+      acc_phase[buf] ^= 1;
+      __syncwarp();
+      tc_fence_after();
+      const int m = mb * BM + q * 32 + lane;
+      const bool row_ok = m < p.M;
+      const float rs = alpha * ((e.row_scale && row_ok) ? e.row_scale[m] : 1.f);
+      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + buf * C::kAccCols;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld_32cols(tbase + c0, r);
+        tmem_ld_wait();
+        const int n0 = nb * BN + c0;
+        if (!row_ok || n0 >= p.N) continue;
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int n = min(n0 + i, p.N - 1);
+          float x = __uint_as_float(r[i]) * rs;
+          if (e.col_scale) x *= e.col_scale[e.col_scalar ? 0 : n];
+          if (e.bias) x += __bfloat162float(e.bias[n]);
+          if (e.act == H3B_ACT_GELU_TANH) x = gelu_tanh(x);
+          v[i] = x;
+        }
+        if (e.residual) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            const int n = n0 + i;
+            if (n < p.N) {
+              float res[8], g[8];
+              load8(e.residual + (int64_t)m * e.ldr + n, res);
+              load8(e.gate + n, g);
+#pragma unroll
+              for (int u = 0; u < 8; ++u) v[i + u] = res[u] + g[u] * v[i + u];
+            }
+          }
+        }
+        bf16* dst = e.D + (int64_t)m * e.ldd + n0;
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          if (n0 + i < p.N) {
+            float w[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) w[u] = v[i + u];
+            store8(dst + i, w);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// Row-major byte matrix [rows, cols_bytes] as a 2D tensor map with box {128 bytes, box_rows}, 128-byte swizzle.
+int make_tmap(CUtensorMap* m, const void* base, int64_t rows, int64_t cols_bytes, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(H3B_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)cols_bytes, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols_bytes};
+  cuuint32_t box[2] = {(cuuint32_t)KB_BYTES, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(H3B_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return H3B_OK;
+}
+
+int num_sms() {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
+template <bool FP4, int BN>
+int run_gemm(const void* A, const uint8_t* sfa, const void* B, const uint8_t* sfb, int64_t M, int64_t N, int64_t K,
+             const h3b_epilogue* epi, cudaStream_t stream) {
+  using C = Cfg<FP4, BN>;
+  const int64_t kbytes = FP4 ? K / 2 : K;
+  CUtensorMap ta, tb;
+  int rc = make_tmap(&ta, A, M, kbytes, BM);
+  if (rc) return rc;
+  rc = make_tmap(&tb, B, N, kbytes, BN);
+  if (rc) return rc;
+  Problem p;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.m_blocks = (int)((M + BM - 1) / BM);
+  p.n_blocks = (int)((N + BN - 1) / BN);
+  p.k_blocks = (int)(K / C::kElemsPerKB);
+  p.num_tiles = p.m_blocks * p.n_blocks;
+  p.sfa = sfa;
+  p.sfb = sfb;
+  p.sfb_groups = (int)((N + 127) / 128);
+  Epi e{epi->alpha,
+        epi->alpha_dev,
+        epi->row_scale,
+        epi->col_scale,
+        epi->col_scale_scalar,
+        static_cast<const bf16*>(epi->bias),
+        epi->act,
+        static_cast<const bf16*>(epi->residual),
+        epi->ldr,
+        static_cast<const bf16*>(epi->gate),
+        static_cast<bf16*>(epi->D),
+        epi->ldd};
+  auto kern = gemm_kernel<FP4, BN>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) != cudaSuccess)
+      return set_error(H3B_ECUDA, "gemm: cannot reserve %d bytes of shared memory", C::kSmemBytes);
+    attr_set = true;
+  }
+  const int grid = std::min(p.num_tiles, num_sms());
+  kern<<<grid, 192, C::kSmemBytes, stream>>>(ta, tb, p, e);
+  H3B_LAUNCH_CHECK("gemm");
+  return H3B_OK;
+}
+
+int check_epilogue(const h3b_epilogue* epi, int64_t N) {
+  H3B_REQUIRE(epi && epi->D, "gemm: epilogue and its output D are required");
+  H3B_REQUIRE(epi->ldd >= N && epi->ldd % 8 == 0 && aligned(epi->D, 16), "gemm: ldd >= N, multiple of 8, D 16-byte aligned");
+  H3B_REQUIRE(epi->act == H3B_ACT_NONE || epi->act == H3B_ACT_GELU_TANH, "gemm: act %d", epi->act);
+  H3B_REQUIRE(!epi->residual || (epi->gate && epi->ldr >= N && epi->ldr % 8 == 0 && aligned(epi->residual, 16) &&
+                                 aligned(epi->gate, 16)),
+              "gemm: residual needs gate, ldr >= N (multiple of 8) and 16-byte alignment");
+  return H3B_OK;
+}
+
+}  // namespace
+}  // namespace h3b
+
+using namespace h3b;
+
+extern "C" int h3b_gemm_fp8(const void* A, const void* B, int64_t M, int64_t N, int64_t K, const h3b_epilogue* epi,
+                            cudaStream_t stream) {
+  clear_error();
+  H3B_REQUIRE(A && B, "gemm_fp8: null operand");
+  H3B_REQUIRE(K > 0 && K % 128 == 0, "gemm_fp8: K must be a positive multiple of 128 (got %lld)", (long long)K);
+  H3B_REQUIRE(N > 0 && N % 16 == 0 && M >= 0, "gemm_fp8: N must be a positive multiple of 16");
+  H3B_REQUIRE(aligned(A, 16) && aligned(B, 16), "gemm_fp8: A and B must be 16-byte aligned");
+  if (int rc = check_epilogue(epi, N)) return rc;
+  if (M == 0) return H3B_OK;
+  return run_gemm<false, 256>(A, nullptr, B, nullptr, M, N, K, epi, stream);
+}
+
+extern "C" int h3b_gemm_nvfp4(const void* A, const uint8_t* sfa, const void* B, const uint8_t* sfb, int64_t M,
+                              int64_t N, int64_t K, const h3b_epilogue* epi, cudaStream_t stream) {
+  clear_error();
+  H3B_REQUIRE(A && B && sfa && sfb, "gemm_nvfp4: null operand");
+  H3B_REQUIRE(K > 0 && K % 256 == 0, "gemm_nvfp4: K must be a positive multiple of 256 (got %lld)", (long long)K);
+  H3B_REQUIRE(N > 0 && N % 16 == 0 && M >= 0, "gemm_nvfp4: N must be a positive multiple of 16");
+  H3B_REQUIRE(aligned(A, 16) && aligned(B, 16) && aligned(sfa, 16) && aligned(sfb, 16),
+              "gemm_nvfp4: operands and scales must be 16-byte aligned");
+  if (int rc = check_epilogue(epi, N)) return rc;
+  if (M == 0) return H3B_OK;
+  return run_gemm<true, 192>(A, sfa, B, sfb, M, N, K, epi, stream);
+}
+
+extern "C" int h3b_device_status(int* status) {
+  clear_error();
+  H3B_REQUIRE(status, "device_status: null pointer");
+  if (cudaMemcpyFromSymbol(status, g_gemm_status, sizeof(int)) != cudaSuccess)
+    return set_error(H3B_ECUDA, "device_status: read failed");
+  return H3B_OK;
+}
+
+extern "C" int h3b_reset_device_status(void) {
+  clear_error();
+  const int zero = 0;
+  if (cudaMemcpyToSymbol(g_gemm_status, &zero, sizeof(int)) != cudaSuccess)
+    return set_error(H3B_ECUDA, "reset_device_status: write failed");
+  return H3B_OK;
+}

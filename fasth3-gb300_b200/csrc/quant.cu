@@ -1,0 +1,345 @@
+// Activation quantizers of the DiT block: gated residual + RMSNorm/LayerNorm + adaLN modulate + FP8/NVFP4 row
+// quantization, the plain per-token FP8 quantizer, and the per-tensor NVFP4 quantizer.
+//
+// Built with --use_fast_math like the reference extension (fastvideo/models/dits/h3fast/__init__.py:42), and every
+// per-element expression below is written in the same operand order as the reference kernel
+// (fastvideo/models/dits/h3fast/h3fast.cu:188-265): with the same flags the compiler emits the same approximate
+// reciprocal, rsqrt and contractions, which is what makes the quantized bytes bit-identical to the reference's.
+// The row sum of squares uses the reference's reduction tree (8 contiguous elements per thread summed in order,
+// warp butterfly, warp partials butterflied again), so its rounding is the same too.
+#include "common.cuh"
+
+namespace h3b {
+namespace {
+
+struct RowArgs {
+  const bf16* x;
+  const bf16* y;
+  const float* sy;
+  const bf16* gate;
+  int64_t gate_ld;
+  const int32_t* idx;
+  const bf16* nw;
+  const bf16* shift;
+  const bf16* scale;
+  int64_t tab_ld;
+  bf16* xo;
+  uint8_t* h;
+  uint8_t* hsf;
+  float* hs;
+  float eps;
+  int64_t rows;
+};
+
+// One CTA per row, C/8 threads, thread t owns elements [8t, 8t+8).
+template <int C, bool BRANCH, int NORM, bool FP4>
+__global__ void __launch_bounds__(C / 8) resid_norm_quant_kernel(const RowArgs a) {
+  constexpr int NW = C / 8 / 32;
+  __shared__ float stage[32];
+  const int t = threadIdx.x;
+  const int64_t r = blockIdx.x;
+  const int64_t tab = a.idx ? (int64_t)a.idx[r] : 0;
+  float v[8];
+  load8(a.x + r * C + t * 8, v);
+  if constexpr (BRANCH) {
+    float b[8], g[8];
+    load8(a.y + r * C + t * 8, b);
+    load8(a.gate + tab * a.gate_ld + t * 8, g);
+    const float s = a.sy[r];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = to_bf16_and_back(v[i] + g[i] * (s * b[i]));
+    store8(a.xo + r * C + t * 8, v);
+  }
+  if constexpr (NORM == H3B_NORM_NONE) {
+    return;
+  } else {
+    float sc[8], sf[8];
+    load8(a.scale + tab * a.tab_ld + t * 8, sc);
+    load8(a.shift + tab * a.tab_ld + t * 8, sf);
+    float am = 0.f;
+    if constexpr (NORM == H3B_NORM_RMS) {
+      float wv[8];
+      load8(a.nw + t * 8, wv);
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
+      ss = block_allreduce<NW, false>(ss, stage);
+      const float rs = rsqrtf(ss / C + a.eps);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        v[i] = v[i] * rs * wv[i] * (1.f + sc[i]) + sf[i];
+        am = fmaxf(am, fabsf(v[i]));
+      }
+    } else {  // LayerNorm without affine parameters, two passes over the registers
+      float s1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s1 += v[i];
+      const float mean = block_allreduce<NW, false>(s1, stage) / C;
+      float s2 = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        v[i] -= mean;
+        s2 += v[i] * v[i];
+      }
+      const float rs = rsqrtf(block_allreduce<NW, false>(s2, stage) / C + a.eps);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        v[i] = v[i] * rs * (1.f + sc[i]) + sf[i];
+        am = fmaxf(am, fabsf(v[i]));
+      }
+    }
+    am = block_allreduce<NW, true>(am, stage);
+    if constexpr (FP4) {
+      const float s = fmaxf(am / kFp4Range, kMinScaleFp4);
+      const float gs = 1.f / s;
+      // a 16-element block spans lanes t and t^1
+      float vmax = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) vmax = fmaxf(vmax, fabsf(v[i]));
+      vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
+      uint32_t bits;
+      const float m = nvfp4_block_scale(vmax, gs, &bits);
+      const uint32_t lo = e2m1x4(v[0] * m, v[1] * m, v[2] * m, v[3] * m);
+      const uint32_t hi = e2m1x4(v[4] * m, v[5] * m, v[6] * m, v[7] * m);
+      *reinterpret_cast<uint32_t*>(a.h + r * (C / 2) + t * 4) = lo | (hi << 16);
+      if ((t & 1) == 0) a.hsf[sf_atom_offset(r, t >> 1, C / 16)] = (uint8_t)bits;
+      if (t == 0) a.hs[r] = s;
+    } else {
+      const float s = fmaxf(am / kFp8Max, kMinScaleFp8);
+      const float inv = 1.f / s;
+      uint2 o;
+      o.x = e4m3x4(v[0] * inv, v[1] * inv, v[2] * inv, v[3] * inv);
+      o.y = e4m3x4(v[4] * inv, v[5] * inv, v[6] * inv, v[7] * inv);
+      *reinterpret_cast<uint2*>(a.h + r * C + t * 8) = o;
+      if (t == 0) a.hs[r] = s;
+    }
+  }
+}
+
+template <int C>
+int launch_resid_norm_quant(const RowArgs& a, bool branch, int norm, bool fp4, cudaStream_t st) {
+  const dim3 grid((unsigned)a.rows), block(C / 8);
+#define H3B_RNQ(B, N, Q) resid_norm_quant_kernel<C, B, N, Q><<<grid, block, 0, st>>>(a)
+  if (norm == H3B_NORM_NONE) {
+    H3B_RNQ(true, H3B_NORM_NONE, false);
+  } else if (norm == H3B_NORM_RMS) {
+    if (branch) {
+      if (fp4) H3B_RNQ(true, H3B_NORM_RMS, true); else H3B_RNQ(true, H3B_NORM_RMS, false);
+    } else {
+      if (fp4) H3B_RNQ(false, H3B_NORM_RMS, true); else H3B_RNQ(false, H3B_NORM_RMS, false);
+    }
+  } else {
+    if (branch) {
+      if (fp4) H3B_RNQ(true, H3B_NORM_LAYER, true); else H3B_RNQ(true, H3B_NORM_LAYER, false);
+    } else {
+      if (fp4) H3B_RNQ(false, H3B_NORM_LAYER, true); else H3B_RNQ(false, H3B_NORM_LAYER, false);
+    }
+  }
+#undef H3B_RNQ
+  H3B_LAUNCH_CHECK("resid_norm_quant");
+  return H3B_OK;
+}
+
+// ------------------------------------------------------------------------------------------- plain FP8 per row
+// One CTA per row; the row is read twice (amax, then quantize; the second read is served from L1/L2). Max is exact
+// in any order, so the bytes do not depend on the thread layout.
+__global__ void __launch_bounds__(256) quant_fp8_rows_kernel(const bf16* __restrict__ x, int64_t ld, int K,
+                                                             uint8_t* __restrict__ q, float* __restrict__ s_out) {
+  __shared__ float stage[32];
+  const int64_t r = blockIdx.x;
+  const bf16* row = x + r * ld;
+  float am = 0.f;
+  for (int c = threadIdx.x * 8; c < K; c += 256 * 8) {
+    float f[8];
+    load8(row + c, f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(f[i]));
+  }
+  am = block_allreduce<8, true>(am, stage);
+  const float s = fmaxf(am / kFp8Max, kMinScaleFp8);
+  const float inv = 1.f / s;
+  for (int c = threadIdx.x * 8; c < K; c += 256 * 8) {
+    float f[8];
+    load8(row + c, f);
+    uint2 o;
+    o.x = e4m3x4(f[0] * inv, f[1] * inv, f[2] * inv, f[3] * inv);
+    o.y = e4m3x4(f[4] * inv, f[5] * inv, f[6] * inv, f[7] * inv);
+    *reinterpret_cast<uint2*>(q + r * K + c) = o;
+  }
+  if (threadIdx.x == 0) s_out[r] = s;
+}
+
+// ------------------------------------------------------------------------------------------- per-tensor amax
+__global__ void __launch_bounds__(256) amax_kernel(const bf16* __restrict__ x, int64_t ld, int64_t rows, int K,
+                                                   float* __restrict__ amax) {
+  __shared__ float stage[32];
+  const int chunks = K / 8;
+  const int64_t total = rows * chunks;
+  float am = 0.f;
+  for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < total; i += (int64_t)gridDim.x * 256) {
+    const int64_t r = i / chunks;
+    const int c = (int)(i - r * chunks);
+    float f[8];
+    load8_nc(x + r * ld + c * 8, f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) am = fmaxf(am, fabsf(f[j]));
+  }
+  am = block_allreduce<8, true>(am, stage);
+  if (threadIdx.x == 0 && am > 0.f) atomicMax(reinterpret_cast<int*>(amax), __float_as_int(am));
+}
+
+// ------------------------------------------------------------------------------------------- per-tensor NVFP4
+// Thread i owns 64 consecutive elements (four 16-element blocks) of one row: row = i / (K/64), group = i % (K/64),
+// so a warp reads 4 KB of one row contiguously and writes its four block scales as one 32-bit word.
+__global__ void __launch_bounds__(256) quant_nvfp4_tensor_kernel(const bf16* __restrict__ x, int64_t ld, int64_t rows,
+                                                                 int K, const float* __restrict__ amax,
+                                                                 uint8_t* __restrict__ q, uint8_t* __restrict__ sf,
+                                                                 float* __restrict__ s_out) {
+  const float s = fmaxf(*amax / kFp4Range, kMinScaleFp4);
+  const float gs = 1.f / s;
+  const int groups = K / 64;
+  const int64_t rows_pad = (rows + 127) / 128 * 128;
+  const int64_t total = rows_pad * groups;
+  const int64_t sf_cols = K / 16;
+  if (blockIdx.x == 0 && threadIdx.x == 0) s_out[0] = s;
+  for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < total; i += (int64_t)gridDim.x * 256) {
+    const int64_t r = i / groups;
+    const int g = (int)(i - r * groups);
+    uint32_t sfw = 0;
+    if (r < rows) {
+      const bf16* src = x + r * ld + g * 64;
+      uint32_t codes[8];
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        float f[8], e[8];
+        load8_nc(src + b * 16, f);
+        load8_nc(src + b * 16 + 8, e);
+        float vmax = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) vmax = fmaxf(vmax, fmaxf(fabsf(f[j]), fabsf(e[j])));
+        uint32_t bits;
+        const float m = nvfp4_block_scale(vmax, gs, &bits);
+        codes[2 * b] = e2m1x4(f[0] * m, f[1] * m, f[2] * m, f[3] * m) |
+                       (e2m1x4(f[4] * m, f[5] * m, f[6] * m, f[7] * m) << 16);
+        codes[2 * b + 1] = e2m1x4(e[0] * m, e[1] * m, e[2] * m, e[3] * m) |
+                           (e2m1x4(e[4] * m, e[5] * m, e[6] * m, e[7] * m) << 16);
+        sfw |= bits << (8 * b);
+      }
+      uint4* dst = reinterpret_cast<uint4*>(q + r * (K / 2) + g * 32);
+      dst[0] = make_uint4(codes[0], codes[1], codes[2], codes[3]);
+      dst[1] = make_uint4(codes[4], codes[5], codes[6], codes[7]);
+    }
+    // the four scale columns 4g..4g+3 of row r are adjacent bytes of one atom row
+    *reinterpret_cast<uint32_t*>(sf + sf_atom_offset(r, (int64_t)g * 4, sf_cols)) = sfw;
+  }
+}
+
+int grid_for(int64_t work, int per_block) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t need = (work + per_block - 1) / per_block;
+  const int64_t cap = (int64_t)sms * 8;  // 8 resident 256-thread CTAs per SM
+  return (int)(need < cap ? (need > 0 ? need : 1) : cap);
+}
+
+}  // namespace
+
+int quant_nvfp4_tensor_launch(const bf16* x, int64_t ld, int64_t rows, int K, const float* amax, uint8_t* q,
+                              uint8_t* sf, float* s_out, cudaStream_t st) {
+  const int64_t work = (rows + 127) / 128 * 128 * (K / 64);
+  quant_nvfp4_tensor_kernel<<<grid_for(work, 256), 256, 0, st>>>(x, ld, rows, K, amax, q, sf, s_out);
+  H3B_LAUNCH_CHECK("quant_nvfp4_tensor");
+  return H3B_OK;
+}
+
+int amax_launch(const bf16* x, int64_t ld, int64_t rows, int K, float* amax, cudaStream_t st) {
+  amax_kernel<<<grid_for(rows * (K / 8), 256), 256, 0, st>>>(x, ld, rows, K, amax);
+  H3B_LAUNCH_CHECK("amax");
+  return H3B_OK;
+}
+
+}  // namespace h3b
+
+using namespace h3b;
+
+extern "C" int h3b_resid_norm_quant(const void* x, const void* y, const float* sy, const void* gate, int64_t gate_ld,
+                                    const int32_t* idx, int norm, const void* nw, const void* shift,
+                                    const void* scale, int64_t tab_ld, void* xo, void* h, uint8_t* hsf, float* hs,
+                                    float eps, int64_t rows, int C, cudaStream_t stream) {
+  clear_error();
+  H3B_REQUIRE(x != nullptr && rows >= 0, "resid_norm_quant: x is null or rows < 0");
+  H3B_REQUIRE(norm == H3B_NORM_NONE || norm == H3B_NORM_RMS || norm == H3B_NORM_LAYER, "resid_norm_quant: norm %d",
+              norm);
+  const bool branch = y != nullptr;
+  H3B_REQUIRE(branch || norm != H3B_NORM_NONE, "resid_norm_quant: nothing to do (no y and no norm)");
+  H3B_REQUIRE(!branch || (sy && gate && xo), "resid_norm_quant: the branch needs sy, gate and xo");
+  H3B_REQUIRE(norm == H3B_NORM_NONE || (shift && scale && h && hs), "resid_norm_quant: the norm needs shift, scale, h, hs");
+  H3B_REQUIRE(norm != H3B_NORM_RMS || nw, "resid_norm_quant: RMSNorm needs nw");
+  H3B_REQUIRE(aligned(x, 16) && (!y || aligned(y, 16)) && (!xo || aligned(xo, 16)) && (!h || aligned(h, 8)),
+              "resid_norm_quant: x, y, xo need 16-byte and h 8-byte alignment");
+  H3B_REQUIRE((gate_ld % 8) == 0 && (tab_ld % 8) == 0, "resid_norm_quant: gate_ld and tab_ld must be multiples of 8");
+  if (rows == 0) return H3B_OK;
+  RowArgs a{static_cast<const bf16*>(x), static_cast<const bf16*>(y), sy, static_cast<const bf16*>(gate), gate_ld,
+            idx, static_cast<const bf16*>(nw), static_cast<const bf16*>(shift), static_cast<const bf16*>(scale),
+            tab_ld, static_cast<bf16*>(xo), static_cast<uint8_t*>(h), hsf, hs, eps, rows};
+  const bool fp4 = hsf != nullptr;
+  switch (C) {
+    case 3072: return launch_resid_norm_quant<3072>(a, branch, norm, fp4, stream);
+    case 4096: return launch_resid_norm_quant<4096>(a, branch, norm, fp4, stream);
+    case 5120: return launch_resid_norm_quant<5120>(a, branch, norm, fp4, stream);
+    case 5376: return launch_resid_norm_quant<5376>(a, branch, norm, fp4, stream);
+    default: return set_error(H3B_EINVAL, "resid_norm_quant: unsupported width C=%d (3072, 4096, 5120, 5376)", C);
+  }
+}
+
+extern "C" int h3b_quant_fp8_rows(const void* x, int64_t ld, int64_t rows, int K, void* q, float* s,
+                                  cudaStream_t stream) {
+  clear_error();
+  H3B_REQUIRE(x && q && s, "quant_fp8_rows: null pointer");
+  H3B_REQUIRE(K > 0 && K % 8 == 0 && ld % 8 == 0 && ld >= K, "quant_fp8_rows: K and ld must be multiples of 8, ld >= K");
+  H3B_REQUIRE(aligned(x, 16) && aligned(q, 8), "quant_fp8_rows: x needs 16-byte and q 8-byte alignment");
+  if (rows == 0) return H3B_OK;
+  quant_fp8_rows_kernel<<<(unsigned)rows, 256, 0, stream>>>(static_cast<const bf16*>(x), ld, K,
+                                                             static_cast<uint8_t*>(q), s);
+  H3B_LAUNCH_CHECK("quant_fp8_rows");
+  return H3B_OK;
+}
+
+extern "C" int h3b_amax_bf16(const void* x, int64_t ld, int64_t rows, int K, float* amax, cudaStream_t stream) {
+  clear_error();
+  H3B_REQUIRE(x && amax, "amax_bf16: null pointer");
+  H3B_REQUIRE(K > 0 && K % 8 == 0 && ld % 8 == 0 && ld >= K && aligned(x, 16), "amax_bf16: K, ld multiples of 8; x 16-byte aligned");
+  if (rows == 0) return H3B_OK;
+  return amax_launch(static_cast<const bf16*>(x), ld, rows, K, amax, stream);
+}
+
+extern "C" int h3b_quant_nvfp4_tensor(const void* x, int64_t ld, int64_t rows, int K, const float* amax, void* q,
+                                      uint8_t* sf, float* s_out, cudaStream_t stream) {
+  clear_error();
+  H3B_REQUIRE(x && amax && q && sf && s_out, "quant_nvfp4_tensor: null pointer");
+  H3B_REQUIRE(K > 0 && K % 64 == 0 && ld % 8 == 0 && ld >= K, "quant_nvfp4_tensor: K multiple of 64, ld multiple of 8");
+  H3B_REQUIRE(aligned(x, 16) && aligned(q, 16) && aligned(sf, 4), "quant_nvfp4_tensor: x, q 16-byte and sf 4-byte aligned");
+  if (rows == 0) return H3B_OK;
+  return quant_nvfp4_tensor_launch(static_cast<const bf16*>(x), ld, rows, K, amax, static_cast<uint8_t*>(q), sf,
+                                   s_out, stream);
+}
+
+extern "C" size_t h3b_quant_nvfp4_workspace_bytes(void) { return 256; }
+
+extern "C" int h3b_quant_nvfp4(const void* x, int64_t ld, int64_t rows, int K, void* q, uint8_t* sf, float* s_out,
+                               void* workspace, cudaStream_t stream) {
+  clear_error();
+  H3B_REQUIRE(workspace && aligned(workspace, 256), "quant_nvfp4: workspace must be non-null and 256-byte aligned");
+  H3B_REQUIRE(x && q && sf && s_out, "quant_nvfp4: null pointer");
+  H3B_REQUIRE(K > 0 && K % 64 == 0 && ld % 8 == 0 && ld >= K, "quant_nvfp4: K multiple of 64, ld multiple of 8");
+  H3B_REQUIRE(aligned(x, 16) && aligned(q, 16) && aligned(sf, 4), "quant_nvfp4: x, q 16-byte and sf 4-byte aligned");
+  float* amax = static_cast<float*>(workspace);
+  if (cudaMemsetAsync(amax, 0, sizeof(float), stream) != cudaSuccess)
+    return set_error(H3B_ECUDA, "quant_nvfp4: memset of the workspace failed");
+  if (rows == 0) return H3B_OK;
+  int rc = amax_launch(static_cast<const bf16*>(x), ld, rows, K, amax, stream);
+  if (rc) return rc;
+  return quant_nvfp4_tensor_launch(static_cast<const bf16*>(x), ld, rows, K, amax, static_cast<uint8_t*>(q), sf,
+                                   s_out, stream);
+}

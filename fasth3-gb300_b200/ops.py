@@ -1,0 +1,181 @@
+"""Tensor-level ops over the h3b C ABI, with the reference extension's names and argument meaning.
+
+Every op writes into caller-allocated buffers (the reference ops do the same, fastvideo/models/dits/h3fast/h3fast.cu:
+831-1073), runs on the current CUDA stream and raises ``RuntimeError`` on a bad argument. CUDA tensors only: there is
+no CPU path.
+"""
+from __future__ import annotations
+
+import torch
+
+from ._lib import Epilogue, call, lib
+
+FP8 = torch.float8_e4m3fn
+NORMS = {"none": 0, "rms": 1, "layer": 2}
+ACTS = {None: 0, "none": 0, "gelu_tanh": 1}
+GRAN = {"tensor": 0, "channel": 1}
+
+
+def _p(t: torch.Tensor | None) -> int | None:
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise RuntimeError("h3b ops take CUDA tensors only (no CPU fallback)")
+    return t.data_ptr()
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _contig(t: torch.Tensor, name: str) -> None:
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+
+
+def sf_rows(rows: int) -> int:
+    """Rows of a block-scale buffer: padded to the 128-row atom."""
+    return (rows + 127) // 128 * 128
+
+
+# ------------------------------------------------------------------------------------------------- row quantizers
+def resid_norm_quant(x: torch.Tensor, y: torch.Tensor | None, sy: torch.Tensor | None, gate: torch.Tensor | None,
+                     idx: torch.Tensor | None, nw: torch.Tensor | None, shift: torch.Tensor | None,
+                     scale: torch.Tensor | None, xo: torch.Tensor, h: torch.Tensor | None, hsf: torch.Tensor | None,
+                     hs: torch.Tensor | None, eps: float, norm: str | None = None) -> None:
+    """Gated residual and/or norm + adaLN modulate + FP8/NVFP4 row quantization (h3fast.cu:831-858 semantics).
+
+    Passing no ``y`` skips the residual; passing no ``nw`` skips the norm unless ``norm="layer"`` (LayerNorm without
+    affine parameters, which needs no weight). ``hsf`` given selects NVFP4 (``h`` then holds [rows, C/2] codes).
+    """
+    C = x.shape[-1]
+    _contig(x, "x")
+    rows = x.numel() // C
+    if norm is None:
+        norm = "rms" if nw is not None else "none"
+    gate_ld = gate.stride(0) if gate is not None else 0
+    tab_ld = scale.stride(0) if scale is not None else 0
+    if idx is not None and idx.dtype != torch.int32:
+        raise RuntimeError("idx must be int32")
+    call("h3b_resid_norm_quant", _p(x), _p(y), _p(sy), _p(gate), gate_ld, _p(idx), NORMS[norm], _p(nw), _p(shift),
+         _p(scale), tab_ld, _p(xo), _p(h), _p(hsf), _p(hs), float(eps), rows, C, _stream(x))
+
+
+def quant_fp8_rows(x: torch.Tensor, q: torch.Tensor, s: torch.Tensor) -> None:
+    """Per-token FP8: s[r] = max(amax_r/448, 1/(448*512)), q = e4m3(x / s[r])."""
+    K = x.shape[-1]
+    rows = x.numel() // K
+    call("h3b_quant_fp8_rows", _p(x), x.stride(-2) if x.dim() > 1 else K, rows, K, _p(q), _p(s), _stream(x))
+
+
+def amax(x: torch.Tensor, out: torch.Tensor) -> None:
+    """Folds max|x| into out[0] (atomic max; out must start at 0 or a partial maximum)."""
+    K = x.shape[-1]
+    call("h3b_amax_bf16", _p(x), x.stride(-2) if x.dim() > 1 else K, x.numel() // K, K, _p(out), _stream(x))
+
+
+def quant_nvfp4_tensor(x: torch.Tensor, amax_dev: torch.Tensor, q: torch.Tensor, sf: torch.Tensor,
+                       s_out: torch.Tensor) -> None:
+    """NVFP4 with a per-tensor global scale from a device amax: s = max(amax/2688, 1e-12)."""
+    K = x.shape[-1]
+    call("h3b_quant_nvfp4_tensor", _p(x), x.stride(-2) if x.dim() > 1 else K, x.numel() // K, K, _p(amax_dev), _p(q),
+         _p(sf), _p(s_out), _stream(x))
+
+
+def workspace_bytes() -> int:
+    return int(lib().h3b_quant_nvfp4_workspace_bytes())
+
+
+def quant_nvfp4(x: torch.Tensor, q: torch.Tensor, sf: torch.Tensor, s_out: torch.Tensor,
+                workspace: torch.Tensor) -> None:
+    """amax pass + per-tensor NVFP4 quantization in one call (workspace: >= workspace_bytes(), 256-aligned)."""
+    K = x.shape[-1]
+    call("h3b_quant_nvfp4", _p(x), x.stride(-2) if x.dim() > 1 else K, x.numel() // K, K, _p(q), _p(sf), _p(s_out),
+         _p(workspace), _stream(x))
+
+
+# ------------------------------------------------------------------------------------------------- weight packing
+def quantize_fp8_weight(weight: torch.Tensor, granularity: str = "tensor",
+                        workspace: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """``(fp8 weight, float32 scale)`` of a dense bf16 ``[out, in]`` weight; the same contract as
+    ``quantize_fp8_weight`` (patches/fastvideo-a01c50a.patch:384-394). Allocates its outputs like the reference."""
+    _contig(weight, "weight")
+    if weight.dtype != torch.bfloat16:
+        raise RuntimeError("weight must be bf16")
+    N, K = weight.shape
+    wq = torch.empty(N, K, device=weight.device, dtype=FP8)
+    ws = torch.empty(N if granularity == "channel" else 1, device=weight.device, dtype=torch.float32)
+    if workspace is None and granularity == "tensor":
+        workspace = torch.empty(256, device=weight.device, dtype=torch.uint8)
+    call("h3b_pack_weight_fp8", _p(weight), N, K, GRAN[granularity], _p(wq), _p(ws), _p(workspace), _stream(weight))
+    return wq, ws
+
+
+def pack_nvfp4_weight(weight: torch.Tensor, workspace: torch.Tensor | None = None
+                      ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """``(codes uint8 [N, K/2], block scales uint8 [pad128(N), K/16] in the 128x4 layout, fp32 [1] tensor scale)``."""
+    _contig(weight, "weight")
+    N, K = weight.shape
+    wq = torch.empty(N, K // 2, device=weight.device, dtype=torch.uint8)
+    wsf = torch.empty(sf_rows(N), K // 16, device=weight.device, dtype=torch.uint8)
+    ws = torch.empty(1, device=weight.device, dtype=torch.float32)
+    if workspace is None:
+        workspace = torch.empty(256, device=weight.device, dtype=torch.uint8)
+    call("h3b_pack_weight_nvfp4", _p(weight), N, K, _p(wq), _p(wsf), _p(ws), _p(workspace), _stream(weight))
+    return wq, wsf, ws
+
+
+# ------------------------------------------------------------------------------------------------- GEMMs
+def _epilogue(out: torch.Tensor, alpha: float, alpha_dev, row_scale, col_scale, bias, act, residual, gate) -> Epilogue:
+    e = Epilogue()
+    e.alpha = float(alpha)
+    e.alpha_dev = _p(alpha_dev)
+    e.row_scale = _p(row_scale)
+    e.col_scale = _p(col_scale)
+    e.col_scale_scalar = int(col_scale is not None and col_scale.numel() == 1)
+    e.bias = _p(bias)
+    e.act = ACTS[act]
+    e.residual = _p(residual)
+    e.ldr = residual.stride(0) if residual is not None else 0
+    e.gate = _p(gate)
+    e.D = _p(out)
+    e.ldd = out.stride(0)
+    return e
+
+
+def gemm_fp8(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor, *, scale_a: torch.Tensor | None = None,
+             scale_b: torch.Tensor | None = None, bias: torch.Tensor | None = None, act: str | None = None,
+             residual: torch.Tensor | None = None, gate: torch.Tensor | None = None, alpha: float = 1.0,
+             alpha_dev: torch.Tensor | None = None) -> torch.Tensor:
+    """out = epilogue(a @ w^T) for e4m3 a [M, K], w [N, K]: the ``torch._scaled_mm(a, w.t(), scale_a, scale_b)``
+    call of H3FastRunner._gemm (fastvideo/models/dits/h3fast/__init__.py:389) with the epilogue fused in."""
+    _contig(a, "a")
+    _contig(w, "w")
+    M, K = a.shape
+    N = w.shape[0]
+    e = _epilogue(out, alpha, alpha_dev, scale_a, scale_b, bias, act, residual, gate)
+    call("h3b_gemm_fp8", _p(a), _p(w), M, N, K, e, _stream(a))
+    return out
+
+
+def gemm_nvfp4(a: torch.Tensor, a_sf: torch.Tensor, w: torch.Tensor, w_sf: torch.Tensor, out: torch.Tensor, *,
+               alpha: float = 1.0, alpha_dev: torch.Tensor | None = None, scale_a: torch.Tensor | None = None,
+               scale_b: torch.Tensor | None = None, bias: torch.Tensor | None = None, act: str | None = None,
+               residual: torch.Tensor | None = None, gate: torch.Tensor | None = None) -> torch.Tensor:
+    """out = epilogue(alpha * sum e2m1(a) sfA e2m1(w) sfB) for packed a [M, K/2], w [N, K/2] and their 128x4 block
+    scales: FlashInfer's ``mm_fp4(a, w.T, a_sf, w_sf.T, alpha, bf16, out, block_size=16)`` as called at
+    fastvideo/models/dits/h3fast/__init__.py:402, with the epilogue fused in."""
+    _contig(a, "a")
+    _contig(w, "w")
+    M, K = a.shape[0], a.shape[1] * 2
+    N = w.shape[0]
+    e = _epilogue(out, alpha, alpha_dev, scale_a, scale_b, bias, act, residual, gate)
+    call("h3b_gemm_nvfp4", _p(a), _p(a_sf), _p(w), _p(w_sf), M, N, K, e, _stream(a))
+    return out
+
+
+def device_status() -> int:
+    import ctypes
+    v = ctypes.c_int(0)
+    call("h3b_device_status", ctypes.byref(v))
+    return int(v.value)

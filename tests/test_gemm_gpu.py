@@ -1,0 +1,214 @@
+"""GPU parity of the tcgen05 GEMMs and their fused epilogues.
+
+Oracle: the reference's dequantize-then-matmul in fp32 (its CPU torch path), the epilogue applied in fp32, then
+rounded to bf16 like the kernel's output. Tolerance: rel-Frobenius <= 1e-3 for both FP8 and NVFP4 (the north star
+allows 2e-2 for NVFP4; operands are the same quantized codes on both sides, so only the accumulation order and the
+bf16 output rounding differ).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from cases import outlier_matrix
+from oracle import quant as oq
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+TOL = 1e-3
+
+
+def rel(a: torch.Tensor, b: torch.Tensor) -> float:
+    a, b = a.double(), b.double()
+    return float((a - b).norm() / b.norm().clamp_min(1e-30))
+
+
+def gelu_tanh(v: torch.Tensor) -> torch.Tensor:
+    return torch.nn.functional.gelu(v, approximate="tanh")
+
+
+def epilogue_ref(acc, alpha=1.0, row=None, col=None, bias=None, act=None, residual=None, gate=None):
+    v = acc * alpha
+    if row is not None:
+        v = v * row[:, None]
+    if col is not None:
+        v = v * (col if col.numel() > 1 else col.reshape(1))[None, :]
+    if bias is not None:
+        v = v + bias.float()[None, :]
+    if act == "gelu_tanh":
+        v = gelu_tanh(v)
+    if residual is not None:
+        v = residual.float() + gate.float()[None, :] * v
+    return v.bfloat16().float()
+
+
+def fp8_operands(M, N, K, seed):
+    g = torch.Generator().manual_seed(seed)
+    a = torch.randn(M, K, generator=g).clamp(-448, 448).to(torch.float8_e4m3fn)
+    w = (torch.randn(N, K, generator=g) * 4).clamp(-448, 448).to(torch.float8_e4m3fn)
+    return a, w
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 128), (2048, 3072, 3072), (300, 512, 256), (128, 272, 384),
+                                   (1, 16, 128), (777, 1040, 640)])
+def test_fp8_gemm_plain(ops, M, N, K):
+    a, w = fp8_operands(M, N, K, seed=M + N + K)
+    out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    ops.gemm_fp8(a.to(DEV), w.to(DEV), out)
+    torch.cuda.synchronize()
+    ref = epilogue_ref(a.float() @ w.float().T)
+    assert rel(out.cpu().float(), ref) < TOL
+
+
+@pytest.mark.parametrize("epi", ["scales_bias", "gelu", "residual", "all"])
+def test_fp8_gemm_epilogues(ops, epi):
+    M, N, K = 640, 768, 512
+    a, w = fp8_operands(M, N, K, seed=3)
+    g = torch.Generator().manual_seed(4)
+    row = torch.rand(M, generator=g) + 0.5
+    col = torch.rand(N, generator=g) * 0.01
+    bias = torch.randn(N, generator=g).bfloat16()
+    res = torch.randn(M, N, generator=g).bfloat16()
+    gate = (torch.randn(N, generator=g) * 0.5).bfloat16()
+    kw = {}
+    if epi in ("scales_bias", "all", "gelu"):
+        kw.update(row=row, col=col)
+    if epi in ("scales_bias", "all"):
+        kw.update(bias=bias)
+    if epi in ("gelu", "all"):
+        kw.update(act="gelu_tanh")
+    if epi in ("residual", "all"):
+        kw.update(residual=res, gate=gate)
+    out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    d = lambda t: None if t is None else t.to(DEV)  # noqa: E731
+    ops.gemm_fp8(a.to(DEV), w.to(DEV), out, scale_a=d(kw.get("row")), scale_b=d(kw.get("col")),
+                 bias=d(kw.get("bias")), act=kw.get("act"), residual=d(kw.get("residual")), gate=d(kw.get("gate")))
+    torch.cuda.synchronize()
+    ref = epilogue_ref(a.float() @ w.float().T, **kw)
+    assert rel(out.cpu().float(), ref) < TOL, epi
+
+
+def test_fp8_gemm_residual_in_place(ops):
+    # the gated residual may write over its own residual input (the block's x <- x + gate * proj(y) update)
+    M, N, K = 256, 512, 256
+    a, w = fp8_operands(M, N, K, seed=8)
+    res = torch.randn(M, N, generator=torch.Generator().manual_seed(9)).bfloat16()
+    gate = torch.full((N,), 0.25).bfloat16()
+    x = res.to(DEV).clone()
+    ops.gemm_fp8(a.to(DEV), w.to(DEV), x, residual=x, gate=gate.to(DEV))
+    torch.cuda.synchronize()
+    ref = epilogue_ref(a.float() @ w.float().T, residual=res, gate=gate)
+    assert rel(x.cpu().float(), ref) < TOL
+
+
+def test_fp8_linear_config1_end_to_end(ops):
+    """per-token e4m3 activations, per-channel e4m3 weights, Y = dequant(Xq) dequant(Wq)^T + 0."""
+    M, N, K = 2048, 3072, 3072
+    x = outlier_matrix(M, K, 0, 0.01, 20.0)
+    w = (torch.randn(N, K, generator=torch.Generator().manual_seed(1)) * 0.02).bfloat16()
+    bias = torch.zeros(N, dtype=torch.bfloat16)
+    xd = x.to(DEV)
+    q = torch.empty(M, K, device=DEV, dtype=torch.float8_e4m3fn)
+    s = torch.empty(M, device=DEV)
+    ops.quant_fp8_rows(xd, q, s)
+    wq, ws = ops.quantize_fp8_weight(w.to(DEV), "channel")
+    y = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    ops.gemm_fp8(q, wq, y, scale_a=s, scale_b=ws, bias=bias.to(DEV))
+    torch.cuda.synchronize()
+    # oracle: CPU quantization (codes agree outside the ambiguity window) then dequant-matmul in fp32
+    codes, s_ref, _ = oq.quant_fp8_rows(x.float().numpy())
+    xq = torch.from_numpy(oq.e4m3_decode(codes)) * torch.from_numpy(s_ref)[:, None]
+    rq, rs = oq.quantize_fp8_weight(w, "channel")
+    ref = (xq @ (rq.float() * rs[:, None]).T + bias.float()).bfloat16().float()
+    assert rel(y.cpu().float(), ref) < TOL
+    # and the linear as a whole stays at FP8's error level against the unquantized product
+    assert rel(y.cpu().float(), x.float() @ w.float().T) < 0.05
+
+
+def nvfp4_operands(ops, M, N, K, seed):
+    x = outlier_matrix(M, K, seed, 0.005, 30.0)
+    w = (torch.randn(N, K, generator=torch.Generator().manual_seed(seed + 1)) * 0.02).bfloat16()
+    qa = torch.empty(M, K // 2, device=DEV, dtype=torch.uint8)
+    sfa = torch.empty(ops.sf_rows(M), K // 16, device=DEV, dtype=torch.uint8)
+    sa = torch.empty(1, device=DEV)
+    ops.quant_nvfp4(x.to(DEV), qa, sfa, sa, torch.empty(256, device=DEV, dtype=torch.uint8))
+    qw, sfw, sw = ops.pack_nvfp4_weight(w.to(DEV))
+    torch.cuda.synchronize()
+    a_deq = torch.from_numpy(oq.dequant_nvfp4(qa.cpu().numpy(), sfa.cpu().numpy(), M, K, 1.0))
+    w_deq = torch.from_numpy(oq.dequant_nvfp4(qw.cpu().numpy(), sfw.cpu().numpy(), N, K, 1.0))
+    return (qa, sfa, sa, qw, sfw, sw), a_deq, w_deq, x, w
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 192, 256), (256, 384, 512), (300, 400, 768), (1000, 13824, 5120),
+                                   (129, 5120, 1024)])
+def test_nvfp4_gemm(ops, M, N, K):
+    (qa, sfa, sa, qw, sfw, sw), a_deq, w_deq, _, _ = nvfp4_operands(ops, M, N, K, seed=M + K)
+    out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    ops.gemm_nvfp4(qa, sfa, qw, sfw, out, alpha_dev=sa, scale_b=sw)
+    torch.cuda.synchronize()
+    ref = epilogue_ref(a_deq @ w_deq.T, alpha=sa.item() * sw.item())
+    assert rel(out.cpu().float(), ref) < TOL
+
+
+def test_nvfp4_gemm_epilogue_gelu_residual(ops):
+    M, N, K = 384, 576, 512
+    (qa, sfa, sa, qw, sfw, sw), a_deq, w_deq, _, _ = nvfp4_operands(ops, M, N, K, seed=21)
+    g = torch.Generator().manual_seed(22)
+    bias = torch.randn(N, generator=g).bfloat16()
+    res = torch.randn(M, N, generator=g).bfloat16()
+    gate = torch.randn(N, generator=g).bfloat16()
+    out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    ops.gemm_nvfp4(qa, sfa, qw, sfw, out, alpha_dev=sa, scale_b=sw, bias=bias.to(DEV), act="gelu_tanh",
+                   residual=res.to(DEV), gate=gate.to(DEV))
+    torch.cuda.synchronize()
+    ref = epilogue_ref(a_deq @ w_deq.T, alpha=sa.item() * sw.item(), bias=bias, act="gelu_tanh", residual=res,
+                       gate=gate)
+    assert rel(out.cpu().float(), ref) < TOL
+
+
+def test_nvfp4_config2_full_size_sampled_rows(ops):
+    """BASELINE config 2 at full size (32768 x 13824 x 5120): the whole GEMM runs on the GPU; 64 sampled rows are
+    checked against the dequantize-then-matmul oracle, plus a checksum of every row against the oracle's row sums."""
+    M, N, K = 32768, 13824, 5120
+    x = outlier_matrix(M, K, 2, 0.005, 30.0)
+    w = (torch.randn(N, K, generator=torch.Generator().manual_seed(3)) * 0.02).bfloat16()
+    qa = torch.empty(M, K // 2, device=DEV, dtype=torch.uint8)
+    sfa = torch.empty(ops.sf_rows(M), K // 16, device=DEV, dtype=torch.uint8)
+    sa = torch.empty(1, device=DEV)
+    ops.quant_nvfp4(x.to(DEV), qa, sfa, sa, torch.empty(256, device=DEV, dtype=torch.uint8))
+    qw, sfw, sw = ops.pack_nvfp4_weight(w.to(DEV))
+    out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    ops.gemm_nvfp4(qa, sfa, qw, sfw, out, alpha_dev=sa, scale_b=sw)
+    torch.cuda.synchronize()
+    rows = torch.randperm(M, generator=torch.Generator().manual_seed(4))[:64]
+    a_deq = torch.from_numpy(oq.dequant_nvfp4(qa[rows].cpu().numpy(), _sf_rows(sfa, rows, K), 64, K, 1.0))
+    w_deq = torch.from_numpy(oq.dequant_nvfp4(qw.cpu().numpy(), sfw.cpu().numpy(), N, K, 1.0))
+    ref = epilogue_ref(a_deq @ w_deq.T, alpha=sa.item() * sw.item())
+    assert rel(out[rows.to(DEV)].cpu().float(), ref) < TOL
+    # linearity checksum over all rows: out @ 1 == A_deq @ (W_deq^T @ 1) * alpha (fp32, loose: bf16 rounding)
+    wsum = (w_deq.sum(0) * sa.item() * sw.item()).to(DEV)
+    a_all = _dequant_gpu(qa, sfa, M, K)
+    want = a_all @ wsum
+    got = out.float().sum(1)
+    assert rel(got, want) < 5e-3
+
+
+def _sf_rows(sfa: torch.Tensor, rows: torch.Tensor, K: int) -> np.ndarray:
+    """The scale bytes of the selected rows, re-laid out as a dense 128x4 buffer for those rows."""
+    full = sfa.cpu().numpy()
+    n_all = full.shape[0]
+    bits = oq.unswizzle_sf(full, n_all, K // 16)[rows.numpy()]
+    return oq.swizzle_sf(bits)
+
+
+def _dequant_gpu(q: torch.Tensor, sf: torch.Tensor, rows: int, K: int) -> torch.Tensor:
+    """Dequantize NVFP4 on the GPU with plain torch ops (test-side reference only)."""
+    lut = torch.tensor(oq.E2M1_VALUES, device=q.device)
+    codes = torch.stack([q & 15, q >> 4], -1).reshape(rows, K)
+    vals = lut[codes.long()].view(rows, K // 16, 16)
+    r = torch.arange(rows, device=q.device)[:, None]
+    c = torch.arange(K // 16, device=q.device)[None, :]
+    off = (r >> 7) * (K // 64) * 512 + (c >> 2) * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4 + (c & 3)
+    s = sf.reshape(-1)[off].view(torch.float8_e4m3fn).float()
+    return (vals * s[..., None]).reshape(rows, K)
