@@ -13,6 +13,7 @@ import torch
 
 from cases import outlier_matrix
 from oracle import quant as oq
+from test_oracle import assert_codes
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -116,10 +117,14 @@ def test_fp8_linear_config1_end_to_end(ops):
     y = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
     ops.gemm_fp8(q, wq, y, scale_a=s, scale_b=ws, bias=bias.to(DEV))
     torch.cuda.synchronize()
-    # oracle: CPU quantization (codes agree outside the ambiguity window) then dequant-matmul in fp32
-    codes, s_ref, _ = oq.quant_fp8_rows(x.float().numpy())
-    xq = torch.from_numpy(oq.e4m3_decode(codes)) * torch.from_numpy(s_ref)[:, None]
+    # the activation codes agree with the CPU oracle outside its ambiguity window and the weight bytes exactly ...
+    codes, s_ref, amb = oq.quant_fp8_rows(x.float().numpy())
+    assert_codes(q.view(torch.uint8).cpu().numpy(), codes, amb, "config 1 activation codes")
+    np.testing.assert_allclose(s.cpu().numpy(), s_ref, rtol=2e-7)
     rq, rs = oq.quantize_fp8_weight(w, "channel")
+    assert torch.equal(wq.cpu().view(torch.uint8), rq.view(torch.uint8)) and torch.equal(ws.cpu(), rs)
+    # ... and the GEMM equals dequantize-then-matmul in fp32 of those operands
+    xq = q.cpu().float() * s.cpu()[:, None]
     ref = (xq @ (rq.float() * rs[:, None]).T + bias.float()).bfloat16().float()
     assert rel(y.cpu().float(), ref) < TOL
     # and the linear as a whole stays at FP8's error level against the unquantized product

@@ -82,13 +82,17 @@ def _f(t: torch.Tensor) -> np.ndarray:
     return t.float().numpy()
 
 
-def assert_codes(got: np.ndarray, want: np.ndarray, amb: np.ndarray, what: str, max_amb_frac: float = 1e-3):
-    """Equal everywhere outside the ambiguity mask; the mask itself must stay a tiny fraction."""
+def assert_codes(got: np.ndarray, want: np.ndarray, amb: np.ndarray, what: str, max_soft_frac: float = 5e-3,
+                 max_amb_frac: float = 2e-2):
+    """Equal everywhere outside the ambiguity mask; inside it (values within DELTA of a rounding boundary, where the
+    reference's fast-math divisions may round either way -- with bf16 inputs many values sit exactly on a tie) only a
+    small fraction may differ, and the mask itself must stay a small fraction of the codes."""
     assert got.shape == want.shape, (what, got.shape, want.shape)
     diff = got != want
     hard = diff & ~amb
     assert not hard.any(), f"{what}: {int(hard.sum())} of {got.size} codes differ outside the ambiguity window"
     assert amb.mean() <= max_amb_frac, f"{what}: ambiguity window covers {amb.mean():.2e} of the codes"
+    assert diff.mean() <= max_soft_frac, f"{what}: {diff.mean():.2e} of the codes differ inside the window"
 
 
 def assert_scales(got: np.ndarray, want: np.ndarray, what: str, rtol: float = 4e-7):
@@ -133,5 +137,7 @@ def test_oracle_matches_reference_tensor_nvfp4(name):
     assert_codes(oq.unswizzle_sf(sf, rows, K // 16), oq.unswizzle_sf(gold["sf"], rows, K // 16), sf_amb,
                  f"{name} block scales")
     assert_codes(oq.unpack_nibbles(q), oq.unpack_nibbles(gold["q"]), amb, f"{name} nibbles")
-    # padding rows of the scale buffer are zero in both
-    np.testing.assert_array_equal(sf.reshape(-1)[rows * K // 16:].any(), False)
+    # padding rows of the scale buffer (interleaved inside the 128-row atoms) are zero in both
+    pad = sf.shape[0]
+    assert not oq.unswizzle_sf(sf, pad, K // 16)[rows:].any()
+    assert not oq.unswizzle_sf(gold["sf"], pad, K // 16)[rows:].any()
