@@ -18,7 +18,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -59,61 +58,71 @@ def _profile_traffic(name: str) -> float | None:
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms while the timed region runs."""
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    """SM clock and clock-event (throttle) reasons sampled through NVML every 10 ms while the timed region runs (the
+    same fields as nvidia-smi's clocks.sm / clocks_event_reasons.*; reads only, no settings are touched)."""
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap",
+               0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
-        self.lines: list[str] = []
-        self.thread = None
+    def __init__(self, device_index: int):
+        self.device_index = device_index
+        self.samples: list[tuple[float, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._nvml = None
+        self._handle = None
+
+    def _open(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        self._nvml = pynvml
+        p = torch.cuda.get_device_properties(self.device_index)
+        try:
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            self._handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:  # noqa: BLE001
+            self._handle = pynvml.nvmlDeviceGetHandleByIndex(self.device_index)
+        self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+
+    def _reasons(self) -> int:
+        nv = self._nvml
+        fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        return int(fn(self._handle))
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append((self._nvml.nvmlDeviceGetClockInfo(self._handle, self._nvml.NVML_CLOCK_SM),
+                                     self._reasons()))
+            except Exception:  # noqa: BLE001
+                pass
+            self._stop.wait(0.01)
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-        except (FileNotFoundError, OSError):
-            self.proc = None
+            self._open()
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        except Exception:  # noqa: BLE001
+            self._thread = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-            if self.thread is not None:
-                self.thread.join(timeout=2)
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=2)
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 8:
-                continue
-            try:
-                sm.append(float(parts[0]))
-                mx.append(float(parts[1]))
-            except ValueError:
-                continue
-            for nm, val in zip(names, parts[4:8]):
-                if val.lower() == "active":
-                    reasons.add(nm)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0, "source": "nvml"}
+        reasons = set()
+        for _, bits in self.samples:
+            for bit, name in self.REASONS.items():
+                if bits & bit:
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(self.samples), "source": "nvml, 10 ms"}
 
 
 def _dist():
@@ -171,6 +180,42 @@ def run_reference(args) -> None:
             "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": r["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def fp8_linear_secondary(ops, dev, stream, args) -> dict:
+    """The FP8 linear of BASELINE config 3's QKV projection (32760 x 15360 x 5120): per-token FP8 quantization of a
+    bf16 activation + tcgen05 e4m3 GEMM with the row and per-channel scales fused. Reported beside the headline."""
+    import torch
+    Mf, Nf, Kf = 32760, 15360, 5120
+    g = torch.Generator(device=dev).manual_seed(7)
+    x = torch.randn(Mf, Kf, device=dev, generator=g).bfloat16()
+    w = (torch.randn(Nf, Kf, device=dev, generator=g) * 0.02).bfloat16()
+    wq, wsc = ops.quantize_fp8_weight(w, "channel")
+    del w
+    q = torch.empty(Mf, Kf, device=dev, dtype=torch.float8_e4m3fn)
+    s = torch.empty(Mf, device=dev)
+    y = torch.empty(Mf, Nf, device=dev, dtype=torch.bfloat16)
+    for _ in range(3):
+        ops.quant_fp8_rows(x, q, s)
+        ops.gemm_fp8(q, wq, y, scale_a=s, scale_b=wsc)
+    torch.cuda.synchronize()
+    n = max(3, min(args.steps, 10))
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3 * n)]
+    for i in range(n):
+        ev[3 * i].record(stream)
+        ops.quant_fp8_rows(x, q, s)
+        ev[3 * i + 1].record(stream)
+        ops.gemm_fp8(q, wq, y, scale_a=s, scale_b=wsc)
+        ev[3 * i + 2].record(stream)
+    torch.cuda.synchronize()
+    qms = sum(ev[3 * i].elapsed_time(ev[3 * i + 1]) for i in range(n)) / n
+    gms = sum(ev[3 * i + 1].elapsed_time(ev[3 * i + 2]) for i in range(n)) / n
+    flop = 2.0 * Mf * Nf * Kf
+    del x, q, y, wq
+    torch.cuda.empty_cache()
+    return {"shape": [Mf, Nf, Kf], "tflops": flop / ((qms + gms) * 1e-3) / 1e12,
+            "gemm_tflops": flop / (gms * 1e-3) / 1e12, "gemm_ms": gms, "quant_ms": qms,
+            "quant_gbs": (Mf * Kf * 3 + Mf * 4) / (qms * 1e-3) / 1e9}
 
 
 def run_ours(args) -> None:
@@ -255,6 +300,8 @@ def run_ours(args) -> None:
     barrier()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
 
+    fp8 = fp8_linear_secondary(ops, dev, stream, args) if not args.no_fp8 else None
+
     if ws > 1:
         t = torch.tensor([total_ms, e2e_ms, gemm_ms, quant_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -290,6 +337,9 @@ def run_ours(args) -> None:
             "clocks": clocks.summary(),
             "gpu_launches": launches_per_step * args.steps,
         }
+        if fp8 is not None:
+            fp8["gemm_frac_of_2x_bf16"] = fp8["gemm_tflops"] / (2.0 * peaks["bf16"])
+            line["fp8_linear"] = fp8
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
@@ -300,10 +350,11 @@ def run_ours(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-fp8", action="store_true", help="skip the secondary FP8 linear measurement")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

@@ -296,10 +296,11 @@ extern "C" int h3b_resid_norm_quant(const void* x, const void* y, const float* s
 extern "C" int h3b_quant_fp8_rows(const void* x, int64_t ld, int64_t rows, int K, void* q, float* s,
                                   cudaStream_t stream) {
   clear_error();
-  H3B_REQUIRE(x && q && s, "quant_fp8_rows: null pointer");
   H3B_REQUIRE(K > 0 && K % 8 == 0 && ld % 8 == 0 && ld >= K, "quant_fp8_rows: K and ld must be multiples of 8, ld >= K");
-  H3B_REQUIRE(aligned(x, 16) && aligned(q, 8), "quant_fp8_rows: x needs 16-byte and q 8-byte alignment");
+  H3B_REQUIRE(rows >= 0, "quant_fp8_rows: rows < 0");
   if (rows == 0) return H3B_OK;
+  H3B_REQUIRE(x && q && s, "quant_fp8_rows: null pointer");
+  H3B_REQUIRE(aligned(x, 16) && aligned(q, 8), "quant_fp8_rows: x needs 16-byte and q 8-byte alignment");
   quant_fp8_rows_kernel<<<(unsigned)rows, 256, 0, stream>>>(static_cast<const bf16*>(x), ld, K,
                                                              static_cast<uint8_t*>(q), s);
   H3B_LAUNCH_CHECK("quant_fp8_rows");
@@ -308,9 +309,9 @@ extern "C" int h3b_quant_fp8_rows(const void* x, int64_t ld, int64_t rows, int K
 
 extern "C" int h3b_amax_bf16(const void* x, int64_t ld, int64_t rows, int K, float* amax, cudaStream_t stream) {
   clear_error();
-  H3B_REQUIRE(x && amax, "amax_bf16: null pointer");
-  H3B_REQUIRE(K > 0 && K % 8 == 0 && ld % 8 == 0 && ld >= K && aligned(x, 16), "amax_bf16: K, ld multiples of 8; x 16-byte aligned");
-  if (rows == 0) return H3B_OK;
+  H3B_REQUIRE(K > 0 && K % 8 == 0 && ld % 8 == 0 && ld >= K, "amax_bf16: K and ld must be multiples of 8, ld >= K");
+  if (rows <= 0) return H3B_OK;
+  H3B_REQUIRE(x && amax && aligned(x, 16), "amax_bf16: null pointer or x not 16-byte aligned");
   return amax_launch(static_cast<const bf16*>(x), ld, rows, K, amax, stream);
 }
 
