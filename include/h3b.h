@@ -78,6 +78,17 @@ size_t h3b_quant_nvfp4_workspace_bytes(void);
 int h3b_quant_nvfp4(const void* x, int64_t ld, int64_t rows, int K, void* q, uint8_t* sf, float* s_out,
                     void* workspace, cudaStream_t stream);
 
+/* h3b_quant_nvfp4 for callers that cannot allocate device memory (no counterpart in the reference). A host that
+ * only hands the library the tensors it owns -- a plugin running inside an engine whose device memory is planned up
+ * front, or a foreign-language host with a fixed buffer set -- cannot call cudaMalloc for a workspace mid-run. This
+ * variant keeps its scratch in a 256-byte static device array (present on every GPU that loads the library until the
+ * process exits) and allocates nothing. The first call on each device looks up the array's device address; make that
+ * first call before any stream capture. Every call on a device shares the array and zeroes it first, so calls that
+ * overlap on the GPU (e.g. on two streams) race and must be serialized by the caller. Same arguments and results as
+ * h3b_quant_nvfp4 without the workspace; a build whose scratch need exceeds the array is rejected with H3B_EINVAL. */
+int h3b_quant_nvfp4_noalloc(const void* x, int64_t ld, int64_t rows, int K, void* q, uint8_t* sf, float* s_out,
+                            cudaStream_t stream);
+
 /* ---------------------------------------------------------------------------------------------------------------
  * Offline weight packing.
  * FP8: replaces quantize_fp8_weight (patches/fastvideo-a01c50a.patch:384-394):
