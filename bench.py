@@ -218,6 +218,66 @@ def fp8_linear_secondary(ops, dev, stream, args) -> dict:
             "quant_gbs": (Mf * Kf * 3 + Mf * 4) / (qms * 1e-3) / 1e9}
 
 
+def vsa_config4_secondary(ops, dev, stream, args) -> dict:
+    """Q/K/V bf16 [40, 32768, 128] N(0,1) on an 8x64x64 token grid cut into 4x4x4 tiles (512
+    tiles of 64): per-tile E4M3 quantization + tile means, fp32 tile scores, top-32 of 512 per query tile, FP8 VSA
+    fine step. Fine-step algorithmic work 4 * S * (k*64) * D * H = 1.374 TFLOP."""
+    import math
+
+    import torch
+    H, T, Hh, Ww, D, k = 40, 8, 64, 64, 128, 32
+    S = T * Hh * Ww
+    n = S // 64
+    g = torch.Generator(device=dev).manual_seed(11)
+    q, kk, v = (torch.randn(H, S, D, device=dev, generator=g).bfloat16() for _ in range(3))
+    grid = torch.arange(S, device=dev).view(T // 4, 4, Hh // 4, 4, Ww // 4, 4)
+    perm = grid.permute(0, 2, 4, 1, 3, 5).reshape(-1).to(torch.int32)
+    vbs = torch.full((n,), 64, device=dev, dtype=torch.int32)
+    tile_row0 = (torch.arange(n, device=dev) * 64).to(torch.int32)
+    qb, kb, vb = (torch.empty(H, S, D, device=dev, dtype=torch.uint8) for _ in range(3))
+    qs, ks, vs = (torch.empty(H, n, device=dev) for _ in range(3))
+    vs_head = torch.zeros(H, device=dev)
+    qp, kp, vp = (torch.empty(H, n, D, device=dev) for _ in range(3))
+    sc = torch.empty(H, n, n, device=dev)
+    idx = torch.empty(1, H, n, n, device=dev, dtype=torch.int32)
+    num = torch.zeros(1, H, n, device=dev, dtype=torch.int32)
+    out = torch.empty(1, H, S, D, device=dev, dtype=torch.bfloat16)
+    sm_scale = 1.0 / math.sqrt(D)
+
+    def stages(ev=None):
+        marks = [lambda: ops.vsa_tile_quant(q, kk, v, perm, tile_row0, vbs, qb, kb, vb, qs, ks, vs, qp, kp, vp, n,
+                                            vs_head=vs_head),
+                 lambda: ops.tile_scores(qp, kp, sc, sm_scale),
+                 lambda: ops.topk_rows(sc, n, n, 0, [0], [n], [k], idx, num, False),
+                 lambda: ops.vsa_fp8(qb, kb, vb, idx, num, vbs, sm_scale * math.log2(math.e), vs, vs_head,
+                                     q_scale_blk=qs, k_scale_blk=ks, out=out)]
+        for i, f in enumerate(marks):
+            if ev is not None:
+                ev[i].record(stream)
+            f()
+        if ev is not None:
+            ev[4].record(stream)
+
+    for _ in range(3):
+        stages()
+    torch.cuda.synchronize()
+    reps = max(3, min(args.steps, 10))
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(reps)]
+    for r in range(reps):
+        stages(evs[r])
+    torch.cuda.synchronize()
+    names = ["tile_quant", "tile_scores", "topk", "vsa_fp8"]
+    ms = {nm: sum(e[i].elapsed_time(e[i + 1]) for e in evs) / reps for i, nm in enumerate(names)}
+    flop = 4.0 * S * (k * 64) * D * H
+    total = sum(ms.values())
+    res = {"shape": [H, S, D], "k": k, "tiles": n, "ms": ms, "ms_total": total,
+           "fine_tflops": flop / (ms["vsa_fp8"] * 1e-3) / 1e12,
+           "tile_quant_gbs": (3 * H * S * D * 2 + 3 * H * S * D) / (ms["tile_quant"] * 1e-3) / 1e9}
+    del q, kk, v, qb, kb, vb, sc, idx, out
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_ours(args) -> None:
     import torch
     import torch.distributed as dist
@@ -301,6 +361,7 @@ def run_ours(args) -> None:
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
 
     fp8 = fp8_linear_secondary(ops, dev, stream, args) if not args.no_fp8 else None
+    vsa = vsa_config4_secondary(ops, dev, stream, args) if not args.no_vsa else None
 
     if ws > 1:
         t = torch.tensor([total_ms, e2e_ms, gemm_ms, quant_ms], device=dev, dtype=torch.float64)
@@ -340,6 +401,9 @@ def run_ours(args) -> None:
         if fp8 is not None:
             fp8["gemm_frac_of_2x_bf16"] = fp8["gemm_tflops"] / (2.0 * peaks["bf16"])
             line["fp8_linear"] = fp8
+        if vsa is not None:
+            vsa["fine_frac_of_2x_bf16"] = vsa["fine_tflops"] / (2.0 * peaks["bf16"])
+            line["vsa_config4"] = vsa
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
@@ -355,6 +419,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-fp8", action="store_true", help="skip the secondary FP8 linear measurement")
+    ap.add_argument("--no-vsa", action="store_true", help="skip the secondary VSA (config 4) measurement")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

@@ -51,6 +51,15 @@ SIGNATURES: dict[str, list] = {
     "h3b_pack_weight_nvfp4": [P, I64, I32, P, P, P, P, P],
     "h3b_gemm_fp8": [P, P, I64, I64, I64, ctypes.POINTER(Epilogue), P],
     "h3b_gemm_nvfp4": [P, P, P, P, I64, I64, I64, ctypes.POINTER(Epilogue), P],
+    "h3b_qkv_prologue8": [P, P, P, I64, P, P, P, P, P, P, P, F32, F32, P, P, P, P, P, P, P, P, P, P, I32, I64, I32,
+                          I32, F32, P],
+    "h3b_vsa_tile_quant": [P, P, P, I32, I64, P, P, P, P, P, P, P, P, P, P, P, P, P, I64, I32, I32, P],
+    "h3b_vsa_fp8": [P, P, P, P, P, P, P, P, P, P, F32, P, P, I32, I32, I32, I64, P],
+    "h3b_vsa_status": [ctypes.POINTER(I32), I32],
+    "h3b_tile_scores": [P, P, I32, I32, F32, P, P],
+    "h3b_topk_rows": [P, I32, I32, I32, I32, I32, P, P, P, P, P, I32, P],
+    "h3b_compressed_branch": [P, P, I32, I32, P, P],
+    "h3b_attn_gate_quant": [P, P, P, P, P, I64, I32, I32, P, P, P, I64, I32, P, P, P, I32, P, P],
     "h3b_device_status": [ctypes.POINTER(I32)],
     "h3b_reset_device_status": [],
 }

@@ -22,7 +22,7 @@ LIB = HERE / "lib" / "libh3b.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-I", str(ROOT / "include"), "-I", str(CSRC),
           "--expt-relaxed-constexpr"]
-FAST_MATH = {"quant.cu"}
+FAST_MATH = {"quant.cu", "vsa_prologue.cu", "gate_quant.cu"}
 
 
 def nvcc() -> str:

@@ -1,0 +1,135 @@
+// Attention output -> next GEMM's input: gather each compact token row from the attention kernel's heads-first padded
+// layout, optionally merge it with a dense-pass output by log-sum-exp, add gate * compressed-branch output, and
+// quantize the row to FP8 (row scale) or NVFP4 (row global scale + ue4m3 block scales).
+//
+// Semantics of attn_gate_quant (fastvideo/models/dits/h3fast/h3fast.cu:688-741). Built with --use_fast_math and the
+// reference's expression order, one CTA per row with W/8 threads (thread t owns elements 8t..8t+7 of head t/16), so
+// the quantized bytes are bit-identical to the reference's.
+#include "common.cuh"
+
+namespace h3b {
+namespace {
+
+constexpr int D = 128;
+
+struct GateArgs {
+  const bf16* ob;
+  const bf16* g;
+  const float* sg;
+  const bf16* oc;
+  const int32_t* slot;
+  int64_t rows_pad;
+  int n_tiles;
+  int tile;
+  uint8_t* a;
+  uint8_t* asf;
+  float* sa;
+  const bf16* o1;
+  const float* lse1a;
+  const float* lse1b;
+  int n1;
+  const float* lse2;
+  int64_t rows;
+};
+
+template <int W, bool GATE, bool FP4, bool MERGE>
+__global__ void __launch_bounds__(W / 8) gate_quant_kernel(const GateArgs p) {
+  constexpr int NW = W / 8 / 32, H = W / D;
+  __shared__ float stage[32];
+  const int64_t r = blockIdx.x;
+  const int t = threadIdx.x, h = t / (D / 8), d0 = (t % (D / 8)) * 8;
+  const int sl = p.slot[r];
+  float o[8];
+  load8(p.ob + ((size_t)h * p.rows_pad + sl) * D + d0, o);
+  if constexpr (MERGE) {
+    float od[8];
+    load8(p.o1 + ((size_t)r * H + h) * D + d0, od);
+    const float l1 = (r < p.n1 ? p.lse1a[(size_t)h * p.n1 + r] : p.lse1b[(size_t)h * (p.rows - p.n1) + (r - p.n1)]) *
+                     1.4426950408889634f;
+    const float l2 = r < p.n1 ? -INFINITY : p.lse2[(size_t)h * p.rows_pad + sl];
+    const float m = fmaxf(l1, l2);
+    const float w1 = m == -INFINITY ? 0.f : exp2f(l1 - m), w2 = m == -INFINITY ? 0.f : exp2f(l2 - m);
+    const float inv = (w1 + w2) > 0.f ? 1.f / (w1 + w2) : 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = (w1 * od[i] + (w2 > 0.f ? w2 * o[i] : 0.f)) * inv;
+  }
+  if constexpr (GATE) {
+    float gv[8], cv[8];
+    load8(p.g + r * W + t * 8, gv);
+    load8(p.oc + ((size_t)h * p.n_tiles + sl / p.tile) * D + d0, cv);
+    const float s = p.sg[r];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] += cv[i] * (s * gv[i]);
+  }
+  float am = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(o[i]));
+  am = block_allreduce<NW, true>(am, stage);
+  if constexpr (FP4) {
+    const float s = fmaxf(am / kFp4Range, kMinScaleFp4);
+    const float gs = 1.f / s;
+    float vmax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) vmax = fmaxf(vmax, fabsf(o[i]));
+    vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
+    uint32_t bits;
+    const float m = nvfp4_block_scale(vmax, gs, &bits);
+    const uint32_t lo = e2m1x4(o[0] * m, o[1] * m, o[2] * m, o[3] * m);
+    const uint32_t hi = e2m1x4(o[4] * m, o[5] * m, o[6] * m, o[7] * m);
+    *reinterpret_cast<uint32_t*>(p.a + r * (W / 2) + t * 4) = lo | (hi << 16);
+    if ((t & 1) == 0) p.asf[sf_atom_offset(r, t >> 1, W / 16)] = (uint8_t)bits;
+    if (t == 0) p.sa[r] = s;
+  } else {
+    const float s = fmaxf(am / kFp8Max, kMinScaleFp8);
+    const float inv = 1.f / s;
+    uint2 u;
+    u.x = e4m3x4(o[0] * inv, o[1] * inv, o[2] * inv, o[3] * inv);
+    u.y = e4m3x4(o[4] * inv, o[5] * inv, o[6] * inv, o[7] * inv);
+    *reinterpret_cast<uint2*>(p.a + r * W + t * 8) = u;
+    if (t == 0) p.sa[r] = s;
+  }
+}
+
+template <int W>
+int launch(const GateArgs& p, bool gate, bool fp4, bool merge, cudaStream_t st) {
+  const dim3 grid((unsigned)p.rows), block(W / 8);
+#define H3B_GQ(G, Q, M) gate_quant_kernel<W, G, Q, M><<<grid, block, 0, st>>>(p)
+  if (gate) {
+    if (fp4) { if (merge) H3B_GQ(true, true, true); else H3B_GQ(true, true, false); }
+    else { if (merge) H3B_GQ(true, false, true); else H3B_GQ(true, false, false); }
+  } else {
+    if (fp4) { if (merge) H3B_GQ(false, true, true); else H3B_GQ(false, true, false); }
+    else { if (merge) H3B_GQ(false, false, true); else H3B_GQ(false, false, false); }
+  }
+#undef H3B_GQ
+  H3B_LAUNCH_CHECK("attn_gate_quant");
+  return H3B_OK;
+}
+
+}  // namespace
+}  // namespace h3b
+
+using namespace h3b;
+
+extern "C" int h3b_attn_gate_quant(const void* ob, const void* g, const float* sg, const void* oc,
+                                   const int32_t* slot, int64_t rows_pad, int n_tiles, int tile, void* a, uint8_t* asf,
+                                   float* sa, int64_t rows, int W, const void* o1, const float* lse1a,
+                                   const float* lse1b, int n1, const float* lse2, cudaStream_t stream) {
+  clear_error();
+  H3B_REQUIRE(ob && slot && a && sa, "attn_gate_quant: null pointer");
+  const bool gate = g != nullptr, merge = o1 != nullptr;
+  H3B_REQUIRE(!gate || (sg && oc), "attn_gate_quant: the gate needs sg and oc");
+  H3B_REQUIRE(!merge || (lse1a && lse1b && lse2 && n1 >= 0 && n1 <= rows), "attn_gate_quant: merge needs o1, lse1a, "
+              "lse1b, lse2 and 0 <= n1 <= rows");
+  H3B_REQUIRE(tile > 0 && n_tiles > 0, "attn_gate_quant: bad tiles");
+  if (rows == 0) return H3B_OK;
+  GateArgs p{static_cast<const bf16*>(ob), static_cast<const bf16*>(g), sg, static_cast<const bf16*>(oc), slot,
+             rows_pad, n_tiles, tile, static_cast<uint8_t*>(a), asf, sa, static_cast<const bf16*>(o1), lse1a, lse1b,
+             n1, lse2, rows};
+  const bool fp4 = asf != nullptr;
+  switch (W) {
+    case 5120: return launch<5120>(p, gate, fp4, merge, stream);
+    case 7168: return launch<7168>(p, gate, fp4, merge, stream);
+    default: return set_error(H3B_EINVAL, "attn_gate_quant: unsupported width W=%d (5120, 7168)", W);
+  }
+}

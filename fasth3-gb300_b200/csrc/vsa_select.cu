@@ -1,0 +1,200 @@
+// VSA coarse step: tile scores from the tile means, top-k key-tile selection per query tile, and the compressed
+// (mean-pooled) attention branch.
+//
+// Scores are defined bit-exactly: sc[h,i,j] = fmul(sum_d, scale) with sum_d accumulated over d = 0..127 in order with
+// separately rounded products and sums (no fused multiply-add), so a float32 CPU restatement reproduces every bit and
+// the selected tile indices are reproducible. The reference scores with cuBLAS (TF32 by default,
+// fastvideo/models/dits/h3fast/__init__.py:146-149, 498-500), which no other implementation can reproduce bit for bit.
+//
+// Selection follows topk_rows (fastvideo/models/dits/h3fast/h3fast.cu:524-588): prefix tiles kept, per span the k
+// largest keys under the order-preserving uint32 map of the float bits, ties broken toward the lowest column, the kept
+// columns written in ascending order.
+#include "common.cuh"
+
+namespace h3b {
+namespace {
+
+constexpr int D = 128;
+
+// ------------------------------------------------------------------------------------------------ scores
+// Block = 16x16 outputs of one head, 256 threads, one output per thread; q/k tile means staged in shared memory.
+__global__ void __launch_bounds__(256) scores_kernel(const float* __restrict__ qp, const float* __restrict__ kp,
+                                                     int n, float scale, float* __restrict__ sc) {
+  __shared__ float sq[16][D + 1];
+  __shared__ float sk[16][D + 1];
+  const int h = blockIdx.z;
+  const int i0 = blockIdx.y * 16, j0 = blockIdx.x * 16;
+  const float* qh = qp + (size_t)h * n * D;
+  const float* kh = kp + (size_t)h * n * D;
+  for (int e = threadIdx.x; e < 16 * D; e += 256) {
+    const int r = e / D, d = e % D;
+    sq[r][d] = (i0 + r < n) ? qh[(size_t)(i0 + r) * D + d] : 0.f;
+    sk[r][d] = (j0 + r < n) ? kh[(size_t)(j0 + r) * D + d] : 0.f;
+  }
+  __syncthreads();
+  const int ti = threadIdx.x / 16, tj = threadIdx.x % 16;
+  float acc = 0.f;
+#pragma unroll 8
+  for (int d = 0; d < D; ++d) acc = __fadd_rn(acc, __fmul_rn(sq[ti][d], sk[tj][d]));
+  if (i0 + ti < n && j0 + tj < n) sc[((size_t)h * n + i0 + ti) * n + j0 + tj] = __fmul_rn(acc, scale);
+}
+
+// ------------------------------------------------------------------------------------------------ top-k
+struct Spans {
+  int n;
+  int start[4];
+  int end[4];
+  int k[4];
+};
+
+__device__ __forceinline__ uint32_t order_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// One warp per (head, query tile). PER = keys per lane (span length <= 32 * PER).
+template <int PER>
+__global__ void __launch_bounds__(128) topk_kernel(const float* __restrict__ scores, int n, int n_ext, int prefix,
+                                                   Spans sp, int rows, int* __restrict__ idx, int* __restrict__ num,
+                                                   int split) {
+  const int row = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int hh = row / n, q = row - hh * n;
+  int* out = idx + ((size_t)hh * n_ext + q) * n;
+  const float* srow = scores + (size_t)row * n;
+  if (q < prefix) {
+    if (!split)
+      for (int c = lane; c < n; c += 32) out[c] = c;
+    if (lane == 0) num[(size_t)hh * n_ext + q] = split ? 0 : n;
+    return;
+  }
+  int cnt = 0;
+  if (!split) {
+    for (int c = lane; c < prefix; c += 32) out[c] = c;
+    cnt = prefix;
+  }
+  const uint32_t below = (1u << lane) - 1u;
+  for (int s = 0; s < sp.n; ++s) {
+    const int start = sp.start[s], len = sp.end[s] - start, k = sp.k[s];
+    if (k >= len) {
+      for (int c = lane; c < len; c += 32) out[cnt + c] = start + c;
+      cnt += len;
+      continue;
+    }
+    uint32_t key[PER];
+#pragma unroll
+    for (int p = 0; p < PER; ++p) {
+      const int c = p * 32 + lane;
+      key[p] = c < len ? order_key(srow[start + c]) : 0u;
+    }
+    // the largest threshold t with count(key >= t) >= k, found bit by bit from the top
+    uint32_t t = 0;
+#pragma unroll 1
+    for (int b = 31; b >= 0; --b) {
+      const uint32_t cand = t | (1u << b);
+      int c = 0;
+#pragma unroll
+      for (int p = 0; p < PER; ++p) c += key[p] >= cand ? 1 : 0;
+      if (__reduce_add_sync(0xffffffffu, c) >= k) t = cand;
+    }
+    int above = 0;
+#pragma unroll
+    for (int p = 0; p < PER; ++p) above += key[p] > t ? 1 : 0;
+    const int ties_needed = k - __reduce_add_sync(0xffffffffu, above);
+    int ties_seen = 0;
+#pragma unroll
+    for (int p = 0; p < PER; ++p) {
+      const int c = p * 32 + lane;
+      const bool valid = c < len;
+      const bool eq = valid && key[p] == t;
+      const uint32_t eq_mask = __ballot_sync(0xffffffffu, eq);
+      const bool keep = (valid && key[p] > t) || (eq && ties_seen + __popc(eq_mask & below) < ties_needed);
+      ties_seen += __popc(eq_mask);
+      const uint32_t keep_mask = __ballot_sync(0xffffffffu, keep);
+      if (keep) out[cnt + __popc(keep_mask & below)] = start + c;
+      cnt += __popc(keep_mask);
+    }
+  }
+  if (lane == 0) num[(size_t)hh * n_ext + q] = cnt;
+}
+
+// ------------------------------------------------------------------------------------------------ compressed branch
+// oc[h,i,:] = softmax_j(sc[h,i,:]) @ vp[h,:,:] in fp32, stored bf16. One CTA (128 threads) per (head, query tile).
+__global__ void __launch_bounds__(128) compressed_kernel(const float* __restrict__ sc, const float* __restrict__ vp,
+                                                         int n, bf16* __restrict__ oc) {
+  extern __shared__ float p[];
+  __shared__ float stage[32];
+  const int h = blockIdx.y, i = blockIdx.x;
+  const float* row = sc + ((size_t)h * n + i) * n;
+  float m = -INFINITY;
+  for (int j = threadIdx.x; j < n; j += 128) m = fmaxf(m, row[j]);
+  m = block_allreduce<4, true>(m, stage);
+  float s = 0.f;
+  for (int j = threadIdx.x; j < n; j += 128) {
+    const float e = __expf(row[j] - m);
+    p[j] = e;
+    s += e;
+  }
+  s = block_allreduce<4, false>(s, stage);  // also orders the p[] writes before the reads below
+  const float inv = 1.f / s;
+  const float* vh = vp + (size_t)h * n * D;
+  float acc = 0.f;
+  for (int j = 0; j < n; ++j) acc += p[j] * vh[(size_t)j * D + threadIdx.x];
+  oc[((size_t)h * n + i) * D + threadIdx.x] = __float2bfloat16_rn(acc * inv);
+}
+
+}  // namespace
+}  // namespace h3b
+
+using namespace h3b;
+
+extern "C" int h3b_tile_scores(const float* qp, const float* kp, int heads, int n, float scale, float* sc,
+                               cudaStream_t stream) {
+  clear_error();
+  H3B_REQUIRE(heads > 0 && n > 0, "tile_scores: heads and n must be positive");
+  H3B_REQUIRE(qp && kp && sc, "tile_scores: null pointer");
+  const dim3 grid((n + 15) / 16, (n + 15) / 16, heads);
+  scores_kernel<<<grid, 256, 0, stream>>>(qp, kp, n, scale, sc);
+  H3B_LAUNCH_CHECK("tile_scores");
+  return H3B_OK;
+}
+
+extern "C" int h3b_topk_rows(const float* scores, int heads, int n, int n_ext, int prefix, int n_spans,
+                             const int* starts, const int* ends, const int* ks, int* idx, int* num, int split,
+                             cudaStream_t stream) {
+  clear_error();
+  H3B_REQUIRE(scores && idx && num && (n_spans == 0 || (starts && ends && ks)), "topk_rows: null pointer");
+  H3B_REQUIRE(n > 0 && n_ext >= n && prefix >= 0 && prefix <= n && heads > 0, "topk_rows: bad n / n_ext / prefix");
+  H3B_REQUIRE(n_spans >= 0 && n_spans <= 4, "topk_rows: at most 4 spans");
+  Spans sp{};
+  sp.n = n_spans;
+  int longest = 0;
+  for (int s = 0; s < n_spans; ++s) {  // host arrays
+    H3B_REQUIRE(starts[s] >= 0 && ends[s] <= n && starts[s] <= ends[s] && ks[s] >= 0, "topk_rows: bad span %d", s);
+    sp.start[s] = starts[s];
+    sp.end[s] = ends[s];
+    sp.k[s] = ks[s];
+    longest = longest > ends[s] - starts[s] ? longest : ends[s] - starts[s];
+  }
+  const int rows = heads * n;
+  const int grid = (rows + 3) / 4;
+#define H3B_TOPK(P) topk_kernel<P><<<grid, 128, 0, stream>>>(scores, n, n_ext, prefix, sp, rows, idx, num, split)
+  if (longest <= 16 * 32) H3B_TOPK(16);
+  else if (longest <= 32 * 32) H3B_TOPK(32);
+  else if (longest <= 64 * 32) H3B_TOPK(64);
+  else if (longest <= 160 * 32) H3B_TOPK(160);
+  else return set_error(H3B_EINVAL, "topk_rows: span of %d tiles is too long (max 5120)", longest);
+#undef H3B_TOPK
+  H3B_LAUNCH_CHECK("topk_rows");
+  return H3B_OK;
+}
+
+extern "C" int h3b_compressed_branch(const float* sc, const float* vp, int heads, int n, void* oc,
+                                     cudaStream_t stream) {
+  clear_error();
+  H3B_REQUIRE(sc && vp && oc && heads > 0 && n > 0, "compressed_branch: bad arguments");
+  H3B_REQUIRE((size_t)n * sizeof(float) <= 48 * 1024, "compressed_branch: n = %d tiles exceeds 12288", n);
+  compressed_kernel<<<dim3(n, heads), 128, n * sizeof(float), stream>>>(sc, vp, n, static_cast<bf16*>(oc));
+  H3B_LAUNCH_CHECK("compressed_branch");
+  return H3B_OK;
+}

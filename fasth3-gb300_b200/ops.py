@@ -179,3 +179,84 @@ def device_status() -> int:
     v = ctypes.c_int(0)
     call("h3b_device_status", ctypes.byref(v))
     return int(v.value)
+
+
+# ------------------------------------------------------------------------------------------------- VSA coarse step
+def _i32_array(vals):
+    import ctypes
+    arr = (ctypes.c_int * max(1, len(vals)))(*[int(v) for v in vals])
+    return arr
+
+
+def qkv_prologue8(q, k, v, s1, tile_row0, vbs, wq, wk, cosb, sinb, inv_sq, inv_sk, qb, kb, vb, vs_blk, vs_head, qp,
+                  kp, vp, heads, n_tiles, tile, eps, qc=None, kc=None, vc=None, qs_blk=None, ks_blk=None) -> None:
+    """The reference op's argument order (h3fast.cu:889-927): RMSNorm + RoPE + tile means + E4M3 Q/K/V. 64-token
+    tiles only; the compact dense-prefix copies (qc/kc/vc) are not supported. With qs_blk/ks_blk the Q/K scales are
+    per (head, tile) instead of the static inv_sq/inv_sk."""
+    if tile != 64:
+        raise RuntimeError("qkv_prologue8: 64-token tiles only")
+    if qc is not None or kc is not None or vc is not None:
+        raise RuntimeError("qkv_prologue8: the dense-prefix write-back (qc/kc/vc) is not supported")
+    rows_pad = vb.shape[-2]
+    n_ext = vs_blk.shape[-1]
+    call("h3b_qkv_prologue8", _p(q), _p(k), _p(v), q.stride(0), _p(s1), _p(tile_row0), _p(vbs), _p(wq), _p(wk),
+         _p(cosb), _p(sinb), float(inv_sq), float(inv_sk), _p(qb), _p(kb), _p(vb), _p(qs_blk), _p(ks_blk), _p(vs_blk),
+         _p(vs_head), _p(qp), _p(kp), _p(vp), int(heads), rows_pad, int(n_tiles), n_ext, float(eps), _stream(q))
+
+
+def vsa_tile_quant(q, k, v, perm, tile_row0, vbs, qb, kb, vb, qs_blk, ks_blk, vs_blk, qp, kp, vp, n_tiles,
+                   vs_head=None) -> None:
+    """BASELINE config 4's prologue: head-major q/k/v [heads, S, 128] gathered into 64-token tiles through ``perm``,
+    per-tile E4M3 Q/K/V, tile means; ``vs_head`` (zeroed by the caller) receives the per-head max V scale."""
+    heads, seqlen = q.shape[-3], q.shape[-2]
+    call("h3b_vsa_tile_quant", _p(q), _p(k), _p(v), heads, seqlen, _p(perm), _p(tile_row0), _p(vbs), _p(qb), _p(kb),
+         _p(vb), _p(qs_blk), _p(ks_blk), _p(vs_blk), _p(vs_head), _p(qp), _p(kp), _p(vp), vb.shape[-2], int(n_tiles),
+         vs_blk.shape[-1], _stream(q))
+
+
+def vsa_fp8(q8, k8, v8, q2k_idx, q2k_num, vbs, qk_coef, v_scale_blk, v_scale_head, lse=None, q_scale_blk=None,
+            k_scale_blk=None, out=None):
+    """FP8 block-sparse attention over the selected 64-key tiles, the reference op's arguments
+    (h3fast.cu:860-862 / h3attn8.cu): returns ``out`` bf16 [1, heads, rows_pad, 128]. With q_scale_blk/k_scale_blk
+    the Q/K scales are per tile and qk_coef is softmax scale * log2(e) only."""
+    heads, rows_pad = q8.shape[-3], q8.shape[-2]
+    n_ext = q2k_num.shape[-1]
+    n = q2k_idx.shape[-1]
+    if out is None:
+        out = torch.zeros(1, heads, rows_pad, 128, device=q8.device, dtype=torch.bfloat16)
+    call("h3b_vsa_fp8", _p(q8), _p(k8), _p(v8), _p(q2k_idx), _p(q2k_num), _p(vbs), _p(q_scale_blk), _p(k_scale_blk),
+         _p(v_scale_blk), _p(v_scale_head), float(qk_coef), _p(out), _p(lse), heads, n, n_ext, rows_pad, _stream(q8))
+    return out
+
+
+def vsa_status(reset: bool = False) -> int:
+    import ctypes
+    v = ctypes.c_int(0)
+    call("h3b_vsa_status", ctypes.byref(v), int(reset))
+    return int(v.value)
+
+
+def tile_scores(qp: torch.Tensor, kp: torch.Tensor, sc: torch.Tensor, scale: float) -> None:
+    heads, n = qp.shape[0], qp.shape[1]
+    call("h3b_tile_scores", _p(qp), _p(kp), heads, n, float(scale), _p(sc), _stream(qp))
+
+
+def topk_rows(scores, n, n_ext, prefix, starts, ends, ks, idx, num, split) -> None:
+    """The reference op's arguments (h3fast.cu:929-957)."""
+    heads = scores.numel() // (n * n)
+    call("h3b_topk_rows", _p(scores), heads, int(n), int(n_ext), int(prefix), len(starts), _i32_array(starts),
+         _i32_array(ends), _i32_array(ks), _p(idx), _p(num), int(bool(split)), _stream(scores))
+
+
+def compressed_branch(sc: torch.Tensor, vp: torch.Tensor, oc: torch.Tensor) -> None:
+    heads, n = vp.shape[0], vp.shape[1]
+    call("h3b_compressed_branch", _p(sc), _p(vp), heads, n, _p(oc), _stream(sc))
+
+
+def attn_gate_quant(ob, g, sg, oc, slot, n_tiles, tile, a, asf, sa, rows, o1=None, lse1a=None, lse1b=None,
+                    lse2=None) -> None:
+    """The reference op's arguments (h3fast.cu:1003-1029)."""
+    W = ob.shape[-3] * ob.shape[-1]
+    n1 = lse1a.shape[-1] if lse1a is not None else 0
+    call("h3b_attn_gate_quant", _p(ob), _p(g), _p(sg), _p(oc), _p(slot), ob.shape[-2], int(n_tiles), int(tile),
+         _p(a), _p(asf), _p(sa), int(rows), W, _p(o1), _p(lse1a), _p(lse1b), n1, _p(lse2), _stream(ob))

@@ -143,6 +143,71 @@ int h3b_gemm_fp8(const void* A, const void* B, int64_t M, int64_t N, int64_t K, 
 int h3b_gemm_nvfp4(const void* A, const uint8_t* sfa, const void* B, const uint8_t* sfb, int64_t M, int64_t N,
                    int64_t K, const h3b_epilogue* epi, cudaStream_t stream);
 
+/* ---------------------------------------------------------------------------------------------------------------
+ * VSA coarse step and prologue and the attention-output gate (a10).
+ * ------------------------------------------------------------------------------------------------------------- */
+
+/* Replaces qkv_prologue8_op (fastvideo/models/dits/h3fast/h3fast.cu:889-927; kernel :376-510) for 64-token tiles.
+ * q/k/v: bf16 rows [rows, heads*128] with row stride ld, in compact tile order; s1: deferred GEMM row scale [rows];
+ * tile_row0/vbs: first row and row count of each tile [n_tiles]; wq/wk: RMSNorm weights bf16 [128]; cosb/sinb: bf16
+ * [rows, 96] (RoPE on the first 96 dims, rotate-half pairs (d, d+48)). Outputs, heads-first and padded to rows_pad =
+ * n_ext*64 rows per head: qb/kb/vb e4m3 [heads, rows_pad, 128]; vs_blk [heads, n_ext] V scale per tile
+ * (max(amax/448, 1e-30)); vs_head [heads] folded with an atomic max (caller zeroes; may be NULL); qp/kp/vp fp32
+ * [heads, n_tiles, 128] tile means. Q/K scales: static (inv_sq, inv_sk: 1/scale) when qs_blk == NULL, else one scale
+ * per (head, tile) like V, written to qs_blk/ks_blk [heads, n_ext]. */
+int h3b_qkv_prologue8(const void* q, const void* k, const void* v, int64_t ld, const float* s1,
+                      const int32_t* tile_row0, const int32_t* vbs, const void* wq, const void* wk, const void* cosb,
+                      const void* sinb, float inv_sq, float inv_sk, void* qb, void* kb, void* vb, float* qs_blk,
+                      float* ks_blk, float* vs_blk, float* vs_head, float* qp, float* kp, float* vp, int heads,
+                      int64_t rows_pad, int n_tiles, int n_ext, float eps, cudaStream_t stream);
+
+/* BASELINE config 4's prologue (no reference counterpart for its layout; the tile and scale math are qkv_prologue8's):
+ * q/k/v bf16 [heads, seqlen, 128] in token order; perm [rows] maps tile-ordered rows to tokens (NULL = identity);
+ * per-tile E4M3 scales for Q, K and V (max(amax/448, 1e-30)); vs_head [heads] (caller zeroes) takes the per-head
+ * maximum of the V scales; other outputs as h3b_qkv_prologue8. */
+int h3b_vsa_tile_quant(const void* q, const void* k, const void* v, int heads, int64_t seqlen, const int32_t* perm,
+                       const int32_t* tile_row0, const int32_t* vbs, void* qb, void* kb, void* vb, float* qs_blk,
+                       float* ks_blk, float* vs_blk, float* vs_head, float* qp, float* kp, float* vp, int64_t rows_pad,
+                       int n_tiles, int n_ext, cudaStream_t stream);
+
+/* FP8 block-sparse VSA attention, fine step (replaces vsa_fp8_op, fastvideo/models/dits/h3fast/h3attn8.cu:1-42 and
+ * vsa_fp8.cuh:782-871). qb/kb/vb e4m3 [heads, rows_pad, 128] (rows_pad = n_ext*64, tile order);
+ * idx/num from h3b_topk_rows ([heads, n_ext, n], [heads, n_ext], padding tiles num 0); vbs [n_ext] valid rows per
+ * tile; Q/K scales either per tile (qs_blk/ks_blk [heads, n_ext]) or folded into qk_coef; V per tile vs_blk and the
+ * per-head maximum vs_head [heads]; qk_coef = softmax scale * log2(e) (* static Q and K scales). Output bf16
+ * [heads, rows_pad, 128] (rows past vbs untouched), optional log2-domain LSE [heads, rows_pad]. n <= 4096, n_ext even. */
+int h3b_vsa_fp8(const void* qb, const void* kb, const void* vb, const int32_t* idx, const int32_t* num,
+                const int32_t* vbs, const float* qs_blk, const float* ks_blk, const float* vs_blk, const float* vs_head,
+                float qk_coef, void* out, float* lse, int heads, int n, int n_ext, int64_t rows_pad,
+                cudaStream_t stream);
+/* Status word of the attention kernel's bounded waits (0 = none); reset != 0 clears it. Synchronizes the device. */
+int h3b_vsa_status(int* status, int reset);
+
+/* Tile scores sc[h, i, j] = scale * sum_d qp[h,i,d] kp[h,j,d] in fp32 with a fixed order (d ascending, products and
+ * sums rounded separately), replacing the runner's torch.baddbmm (fastvideo/models/dits/h3fast/__init__.py:498-500,
+ * TF32 there) with a bit-reproducible definition. qp/kp [heads, n, 128], sc [heads, n, n]. */
+int h3b_tile_scores(const float* qp, const float* kp, int heads, int n, float scale, float* sc, cudaStream_t stream);
+
+/* Replaces topk_rows_op (fastvideo/models/dits/h3fast/h3fast.cu:929-957; kernel :524-588). scores [heads*n, n];
+ * spans given as HOST arrays starts/ends/ks [n_spans <= 4]; idx [heads, n_ext, n], num [heads, n_ext]. Prefix query
+ * tiles are dense (or empty with split); per span the k largest (ties to the lowest column), ascending. */
+int h3b_topk_rows(const float* scores, int heads, int n, int n_ext, int prefix, int n_spans, const int* starts,
+                  const int* ends, const int* ks, int* idx, int* num, int split, cudaStream_t stream);
+
+/* The compressed (mean-pooled) attention branch: oc[h,i,:] = softmax_j(sc[h,i,:]) @ vp[h,:,:], stored bf16
+ * [heads, n, 128] (fastvideo/models/dits/h3fast/__init__.py:505-511). */
+int h3b_compressed_branch(const float* sc, const float* vp, int heads, int n, void* oc, cudaStream_t stream);
+
+/* Replaces attn_gate_quant_op (fastvideo/models/dits/h3fast/h3fast.cu:1003-1029; kernel :688-741): row r of the
+ * output gathers ob [heads, rows_pad, 128] at slot[r]; with o1 it is merged with o1 [rows, heads, 128] by log-sum-exp
+ * (lse1a [heads, n1] for rows < n1, lse1b [heads, rows-n1] for the rest, natural log; lse2 [heads, rows_pad], log2);
+ * with g it adds oc[h, slot/tile] * (sg[r] * g[r]) (g bf16 [rows, W]); then FP8 (asf == NULL: a [rows, W], sa row
+ * scale) or NVFP4 (a [rows, W/2] codes, asf 128x4 scales, sa row global scale). W = heads*128 in {5120, 7168}. */
+int h3b_attn_gate_quant(const void* ob, const void* g, const float* sg, const void* oc, const int32_t* slot,
+                        int64_t rows_pad, int n_tiles, int tile, void* a, uint8_t* asf, float* sa, int64_t rows, int W,
+                        const void* o1, const float* lse1a, const float* lse1b, int n1, const float* lse2,
+                        cudaStream_t stream);
+
 /* Status word written by kernels whose bounded waits expired (0 = none since the last reset); reset with
  * h3b_reset_device_status. Both synchronize the current device. */
 int h3b_device_status(int* status);

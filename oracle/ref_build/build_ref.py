@@ -63,6 +63,7 @@ def load():
         P, I64, F = ctypes.c_void_p, ctypes.c_int64, ctypes.c_float
         _cdll.h3ref_resid_norm_quant_5120.argtypes = [P, P, P, P, I64, P, P, P, P, I64, P, P, P, P, F, I64, P]
         _cdll.h3ref_quant_nvfp4_tensor.argtypes = [P, I64, ctypes.c_int, P, P, P, P, P]
+        _cdll.h3ref_attn_gate_quant_5120.argtypes = [P, P, P, P, P, I64, ctypes.c_int, ctypes.c_int, P, P, P, I64, P]
     return _mod, _cdll
 
 

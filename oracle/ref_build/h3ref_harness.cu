@@ -90,3 +90,24 @@ extern "C" int h3ref_quant_nvfp4_tensor(const void* x, int64_t rows, int K, floa
                                                                         (uint8_t*)q, sf, s_out);
   return (int)cudaGetLastError();
 }
+
+extern "C" int h3ref_attn_gate_quant_5120(const void* ob, const void* g, const float* sg, const void* oc,
+                                          const int* slot, int64_t rows_pad, int n_tiles, int tile, void* a,
+                                          uint8_t* asf, float* sa, int64_t rows, cudaStream_t st) {
+  constexpr int W = 5120;
+  const bool gate = g != nullptr, fp4 = asf != nullptr;
+#define H3REF_G(G, Q)                                                                                               \
+  attn_gate_quant<W, G, Q, false><<<(unsigned)rows, W / 8, 0, st>>>(                                                \
+      (const bf16*)ob, (const bf16*)g, sg, (const bf16*)oc, slot, rows_pad, n_tiles, tile, (fp8s*)a, asf, sa, nullptr, \
+      nullptr, nullptr, 0, nullptr)
+  if (gate) {
+    if (fp4) H3REF_G(true, true);
+    else H3REF_G(true, false);
+  } else if (fp4) {
+    H3REF_G(false, true);
+  } else {
+    H3REF_G(false, false);
+  }
+#undef H3REF_G
+  return (int)cudaGetLastError();
+}

@@ -45,3 +45,61 @@ CASES = {
     "nvfp4_tensor_x5120": ("nvfp4", dict(rows=32, K=5120, seed=8, frac=0.005, mult=30.0, std=1.0)),
     "nvfp4_tensor_w5120": ("nvfp4", dict(rows=64, K=5120, seed=9, frac=0.0, mult=1.0, std=0.02)),
 }
+
+
+def vbs_pattern(n_tiles: int) -> torch.Tensor:
+    """Variable tile sizes like the reference's test geometry (tests/test_kernels.py:21-25)."""
+    vbs = torch.full((n_tiles,), 64, dtype=torch.int32)
+    vbs[::10] = 16
+    vbs[3::11] = 32
+    vbs[0] = 16
+    return vbs
+
+
+def topk_inputs(heads: int, n: int, seed: int, quantize: float) -> torch.Tensor:
+    """Scores [heads*n, n]; rounded to multiples of 1/quantize so that ties occur."""
+    g = torch.Generator().manual_seed(seed)
+    s = torch.randn(heads * n, n, generator=g)
+    return (s * quantize).round() / quantize
+
+
+def prologue_inputs(heads: int, n_tiles: int, seed: int) -> dict[str, torch.Tensor]:
+    """The reference test's prologue inputs (tests/test_kernels.py:40-47) on a variable-size tile geometry."""
+    g = torch.Generator().manual_seed(seed)
+    vbs = vbs_pattern(n_tiles)
+    rows = int(vbs.sum())
+    W = heads * 128
+    d = {
+        "q": torch.randn(rows, W, generator=g).bfloat16(), "k": torch.randn(rows, W, generator=g).bfloat16(),
+        "v": torch.randn(rows, W, generator=g).bfloat16(), "s1": torch.rand(rows, generator=g) + 0.5,
+        "wq": torch.randn(128, generator=g).bfloat16(), "wk": torch.randn(128, generator=g).bfloat16(),
+    }
+    ang = torch.rand(rows, 48, generator=g) * 6.28
+    d["cos"] = torch.cat([ang.cos()] * 2, -1).bfloat16()
+    d["sin"] = torch.cat([ang.sin()] * 2, -1).bfloat16()
+    d["vbs"] = vbs
+    d["tile_row0"] = (vbs.cumsum(0) - vbs).to(torch.int32)
+    return d
+
+
+def gate_inputs(heads: int, vbs: list[int], seed: int) -> dict[str, torch.Tensor]:
+    g = torch.Generator().manual_seed(seed)
+    vbs_t = torch.tensor(vbs, dtype=torch.int32)
+    n_tiles = len(vbs)
+    rows = int(vbs_t.sum())
+    W = heads * 128
+    slot = torch.cat([torch.arange(int(v)) + i * 64 for i, v in enumerate(vbs)]).to(torch.int32)
+    return {"ob": torch.randn(1, heads, n_tiles * 64, 128, generator=g).bfloat16(),
+            "g": torch.randn(rows, W, generator=g).bfloat16(), "sg": torch.rand(rows, generator=g) + 0.5,
+            "oc": torch.randn(heads, n_tiles, 128, generator=g).bfloat16(), "slot": slot}
+
+
+TOPK_CASES = {
+    "topk_prefix_spans": dict(heads=4, n=96, seed=21, quantize=4.0, prefix=8, spans=[(8, 50, 9), (50, 96, 10)],
+                              split=False),
+    "topk_split": dict(heads=3, n=64, seed=22, quantize=2.0, prefix=4, spans=[(4, 64, 12)], split=True),
+    "topk_c4": dict(heads=2, n=512, seed=23, quantize=0.0, prefix=0, spans=[(0, 512, 32)], split=False),
+}
+PROLOGUE_CASES = {"prologue8_h2": dict(heads=2, n_tiles=10, seed=24)}
+GATE_CASES = {"gate5120_fp8": dict(heads=40, vbs=[16, 32], seed=25, fp4=False),
+              "gate5120_fp4": dict(heads=40, vbs=[16, 32], seed=26, fp4=True)}

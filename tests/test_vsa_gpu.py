@@ -1,0 +1,346 @@
+"""GPU parity of the VSA coarse step, prologue and attention-output gate.
+
+Bit-exact against the reference kernels (golden outputs and, where oracle/_ref is present, live runs) for the
+prologue, top-k selection and gate-quant; bit-exact against the CPU oracle for the tile scores and for the indices
+selected from them; within tolerance for the compressed branch.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from cases import (GATE_CASES, PROLOGUE_CASES, TOPK_CASES, gate_inputs, prologue_inputs, topk_inputs, vbs_pattern)
+from oracle import quant as oq
+from oracle import vsa as ov
+from test_oracle import _golden, assert_codes
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _ref():
+    from oracle.ref_build.build_ref import load
+    mod, cdll = load()
+    if mod is None:
+        pytest.skip("oracle/_ref/h3ref.so not present (built only where the reference sources are)")
+    return mod, cdll
+
+
+# ------------------------------------------------------------------------------------------------ top-k
+def run_topk(ops, sc, heads, n, prefix, spans, split):
+    idx = torch.full((1, heads, n, n), -1, device=DEV, dtype=torch.int32)
+    num = torch.zeros(1, heads, n, device=DEV, dtype=torch.int32)
+    ops.topk_rows(sc.to(DEV), n, n, prefix, [a for a, _, _ in spans], [b for _, b, _ in spans],
+                  [c for _, _, c in spans], idx, num, split)
+    torch.cuda.synchronize()
+    return idx.cpu().numpy()[0], num.cpu().numpy()[0]
+
+
+@pytest.mark.parametrize("name", list(TOPK_CASES))
+def test_topk_bit_exact_vs_reference_golden(ops, name):
+    p = TOPK_CASES[name]
+    gold = _golden(name)
+    sc = topk_inputs(p["heads"], p["n"], p["seed"], p["quantize"] or 1e6)
+    idx, num = run_topk(ops, sc, p["heads"], p["n"], p["prefix"], p["spans"], p["split"])
+    np.testing.assert_array_equal(num, gold["num"][0])
+    for h in range(p["heads"]):
+        for q in range(p["n"]):
+            c = num[h, q]
+            np.testing.assert_array_equal(idx[h, q, :c], gold["idx"][0, h, q, :c])
+
+
+@pytest.mark.parametrize("n,k,quantize", [(512, 32, 0.0), (768, 154, 1.0), (2016, 404, 8.0), (37, 5, 0.5)])
+def test_topk_vs_oracle_and_live_reference(ops, n, k, quantize):
+    heads = 3
+    sc = topk_inputs(heads, n, 7 + n, quantize or 1e6)
+    spans = [(0, n, k)]
+    idx, num = run_topk(ops, sc, heads, n, 0, spans, False)
+    oidx, onum = ov.topk_rows(sc.numpy(), n, n, 0, spans, False)
+    np.testing.assert_array_equal(num, onum)
+    assert (num == k).all()
+    np.testing.assert_array_equal(idx[:, :, :k], oidx[:, :, :k])
+    assert (np.diff(idx[:, :, :k], axis=-1) > 0).all()
+    mod = _ref()[0]
+    ridx = torch.full((1, heads, n, n), -1, device=DEV, dtype=torch.int32)
+    rnum = torch.zeros(1, heads, n, device=DEV, dtype=torch.int32)
+    mod.topk_rows(sc.to(DEV), n, n, 0, [0], [n], [k], ridx, rnum, False)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(idx[:, :, :k], ridx.cpu().numpy()[0][:, :, :k])
+
+
+# ------------------------------------------------------------------------------------------------ scores
+def test_tile_scores_bit_exact_and_selection_end_to_end(ops):
+    """C4's coarse step on a reduced head count: tile means -> scores (bit-exact) -> top-32 of 512 (bit-exact)."""
+    heads, n = 4, 512
+    g = torch.Generator().manual_seed(40)
+    qp = torch.randn(heads, n, 128, generator=g) * 0.1
+    kp = torch.randn(heads, n, 128, generator=g) * 0.1
+    sc = torch.empty(heads, n, n, device=DEV)
+    scale = 1.0 / math.sqrt(128)
+    ops.tile_scores(qp.to(DEV), kp.to(DEV), sc, scale)
+    torch.cuda.synchronize()
+    ref = ov.tile_scores(qp.numpy(), kp.numpy(), scale)
+    np.testing.assert_array_equal(sc.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+    idx, num = run_topk(ops, sc, heads, n, 0, [(0, n, 32)], False)
+    oidx, _ = ov.topk_rows(ref.reshape(-1, n), n, n, 0, [(0, n, 32)], False)
+    np.testing.assert_array_equal(idx[:, :, :32], oidx[:, :, :32])
+
+
+def test_compressed_branch(ops):
+    heads, n = 3, 200
+    g = torch.Generator().manual_seed(41)
+    sc = torch.randn(heads, n, n, generator=g) * 2
+    vp = torch.randn(heads, n, 128, generator=g)
+    oc = torch.empty(heads, n, 128, device=DEV, dtype=torch.bfloat16)
+    ops.compressed_branch(sc.to(DEV), vp.to(DEV), oc)
+    torch.cuda.synchronize()
+    ref = torch.from_numpy(ov.compressed_branch(sc.numpy(), vp.numpy()))
+    err = float((oc.cpu().float() - ref).norm() / ref.norm())
+    assert err < 4e-3
+
+
+# ------------------------------------------------------------------------------------------------ prologue
+def run_prologue(ops, d, heads, n_tiles, s_q, s_k, per_tile=False):
+    d = {k: v.to(DEV) for k, v in d.items()}
+    n_ext = n_tiles + n_tiles % 2
+    rows_pad = n_ext * 64
+    z = lambda *sh, dt=torch.uint8: torch.zeros(*sh, device=DEV, dtype=dt)  # noqa: E731
+    qb, kb, vb = z(1, heads, rows_pad, 128), z(1, heads, rows_pad, 128), z(1, heads, rows_pad, 128)
+    vs_blk = torch.ones(heads, n_ext, device=DEV)
+    vs_head = torch.zeros(heads, device=DEV)
+    qp, kp, vp = (z(heads, n_tiles, 128, dt=torch.float32) for _ in range(3))
+    qs = torch.ones(heads, n_ext, device=DEV) if per_tile else None
+    ks = torch.ones(heads, n_ext, device=DEV) if per_tile else None
+    ops.qkv_prologue8(d["q"], d["k"], d["v"], d["s1"], d["tile_row0"], d["vbs"], d["wq"], d["wk"], d["cos"], d["sin"],
+                      1.0 / s_q, 1.0 / s_k, qb, kb, vb, vs_blk, vs_head, qp, kp, vp, heads, n_tiles, 64, 1e-5,
+                      qs_blk=qs, ks_blk=ks)
+    torch.cuda.synchronize()
+    out = {"qb": qb, "kb": kb, "vb": vb, "vs_blk": vs_blk, "vs_head": vs_head, "qp": qp, "kp": kp, "vp": vp}
+    if per_tile:
+        out.update(qs=qs, ks=ks)
+    return {k: v.cpu().numpy() for k, v in out.items()}
+
+
+def static_scales(d):
+    bound = math.sqrt(128) / 448.0
+    return bound * d["wq"].float().abs().max().item(), bound * d["wk"].float().abs().max().item()
+
+
+@pytest.mark.parametrize("name", list(PROLOGUE_CASES))
+def test_prologue_bit_exact_vs_reference_golden(ops, name):
+    p = PROLOGUE_CASES[name]
+    gold = _golden(name)
+    d = prologue_inputs(p["heads"], p["n_tiles"], p["seed"])
+    s_q, s_k = static_scales(d)
+    out = run_prologue(ops, d, p["heads"], p["n_tiles"], s_q, s_k)
+    for key in ("qb", "kb", "vb", "vs_blk", "vs_head", "qp", "kp", "vp"):
+        np.testing.assert_array_equal(out[key].reshape(gold[key].shape).view(np.uint8),
+                                      gold[key].view(np.uint8), err_msg=key)
+
+
+def test_prologue_bit_exact_vs_live_reference_40_heads(ops):
+    mod, _ = _ref()
+    heads, n_tiles = 40, 23
+    d = prologue_inputs(heads, n_tiles, 99)
+    s_q, s_k = static_scales(d)
+    out = run_prologue(ops, d, heads, n_tiles, s_q, s_k)
+    dd = {k: v.to(DEV) for k, v in d.items()}
+    n_ext = n_tiles + 1
+    z = lambda *sh, dt=torch.uint8: torch.zeros(*sh, device=DEV, dtype=dt)  # noqa: E731
+    qb, kb, vb = z(1, heads, n_ext * 64, 128), z(1, heads, n_ext * 64, 128), z(1, heads, n_ext * 64, 128)
+    vs_blk = torch.ones(heads, n_ext, device=DEV)
+    vs_head = torch.zeros(heads, device=DEV)
+    qp, kp, vp = (z(heads, n_tiles, 128, dt=torch.float32) for _ in range(3))
+    mod.qkv_prologue8(dd["q"], dd["k"], dd["v"], dd["s1"], dd["tile_row0"], dd["vbs"], dd["wq"], dd["wk"], dd["cos"],
+                      dd["sin"], 1.0 / s_q, 1.0 / s_k, qb, kb, vb, vs_blk, vs_head, qp, kp, vp, heads, n_tiles, 64,
+                      1e-5, None, None, None)
+    torch.cuda.synchronize()
+    ref = {"qb": qb, "kb": kb, "vb": vb, "vs_blk": vs_blk, "vs_head": vs_head, "qp": qp, "kp": kp, "vp": vp}
+    for key, t in ref.items():
+        np.testing.assert_array_equal(out[key].reshape(t.shape).view(np.uint8), t.cpu().numpy().view(np.uint8),
+                                      err_msg=key)
+
+
+def test_prologue_vs_oracle_within_one_e4m3_step(ops):
+    heads, n_tiles = 2, 12
+    d = prologue_inputs(heads, n_tiles, 5)
+    s_q, s_k = static_scales(d)
+    out = run_prologue(ops, d, heads, n_tiles, s_q, s_k)
+    f = lambda t: t.float().numpy()  # noqa: E731
+    ref = ov.qkv_prologue8(f(d["q"]), f(d["k"]), f(d["v"]), d["s1"].numpy(), d["tile_row0"].numpy(), d["vbs"].numpy(),
+                           f(d["wq"]), f(d["wk"]), f(d["cos"]), f(d["sin"]), heads, s_q, s_k)
+    for key in ("qb", "kb", "vb"):
+        got = oq.e4m3_decode(out[key].reshape(heads, -1, 128))
+        want = oq.e4m3_decode(ref[key])
+        close = np.abs(got - want) <= np.maximum(np.abs(want), 2 ** -6) * 0.126
+        assert close.mean() > 0.999, (key, close.mean())
+    np.testing.assert_allclose(out["vs_blk"], ref["vs_blk"], rtol=1e-2)
+
+
+def test_tile_quant_config4_vs_oracle(ops):
+    """BASELINE config 4's prologue on a reduced head count: 8x64x64 token grid, 4x4x4 tiles (512 tiles)."""
+    heads, T, Hh, Ww = 2, 8, 64, 64
+    g = torch.Generator().manual_seed(42)
+    S = T * Hh * Ww
+    q = torch.randn(heads, S, 128, generator=g).bfloat16()
+    k = torch.randn(heads, S, 128, generator=g).bfloat16()
+    v = torch.randn(heads, S, 128, generator=g).bfloat16()
+    perm = tile_permutation(T, Hh, Ww)
+    n_tiles = S // 64
+    vbs = torch.full((n_tiles,), 64, dtype=torch.int32)
+    tile_row0 = (torch.arange(n_tiles) * 64).to(torch.int32)
+    qb, kb, vb = (torch.zeros(heads, S, 128, device=DEV, dtype=torch.uint8) for _ in range(3))
+    qs, ks, vs = (torch.zeros(heads, n_tiles, device=DEV) for _ in range(3))
+    qp, kp, vp = (torch.zeros(heads, n_tiles, 128, device=DEV) for _ in range(3))
+    ops.vsa_tile_quant(q.to(DEV), k.to(DEV), v.to(DEV), perm.to(DEV), tile_row0.to(DEV), vbs.to(DEV), qb, kb, vb, qs,
+                       ks, vs, qp, kp, vp, n_tiles)
+    torch.cuda.synchronize()
+    ref = ov.vsa_tile_quant(q.float().numpy(), k.float().numpy(), v.float().numpy(), perm.numpy(),
+                            tile_row0.numpy(), vbs.numpy(), n_tiles)
+    for name, t, amb in (("qb", qb, "qamb"), ("kb", kb, "kamb"), ("vb", vb, "vamb")):
+        assert_codes(t.cpu().numpy(), ref[name], ref[amb], name)
+    for name, t in (("qs", qs), ("ks", ks), ("vs", vs)):
+        np.testing.assert_allclose(t.cpu().numpy(), ref[name], rtol=2e-7)
+    for name, t in (("qp", qp), ("kp", kp), ("vp", vp)):  # 64-row tiles: exact
+        np.testing.assert_array_equal(t.cpu().numpy(), ref[name])
+
+
+def tile_permutation(T: int, H: int, W: int, t=4, h=4, w=4) -> torch.Tensor:
+    """Tile-ordered row -> token index for a T x H x W token grid cut into t x h x w cubes (tiles in (T, H, W) order,
+    tokens inside a tile in (t, h, w) order)."""
+    grid = torch.arange(T * H * W).view(T // t, t, H // h, h, W // w, w)
+    return grid.permute(0, 2, 4, 1, 3, 5).reshape(-1).to(torch.int32)
+
+
+# ------------------------------------------------------------------------------------------------ gate + requant
+def run_gate(ops, d, heads, vbs, fp4):
+    d = {k: v.to(DEV) for k, v in d.items()}
+    rows = int(sum(vbs))
+    W = heads * 128
+    a = torch.zeros(rows, W // 2 if fp4 else W, device=DEV, dtype=torch.uint8)
+    asf = torch.zeros(ops.sf_rows(rows), W // 16, device=DEV, dtype=torch.uint8) if fp4 else None
+    sa = torch.zeros(rows, device=DEV)
+    ops.attn_gate_quant(d["ob"], d["g"], d["sg"], d["oc"], d["slot"], len(vbs), 64, a, asf, sa, rows)
+    torch.cuda.synchronize()
+    out = {"a": a.cpu().numpy(), "sa": sa.cpu().numpy()}
+    if fp4:
+        out["asf"] = asf.cpu().numpy()
+    return out
+
+
+@pytest.mark.parametrize("name", list(GATE_CASES))
+def test_gate_quant_bit_exact_vs_reference_golden(ops, name):
+    p = GATE_CASES[name]
+    gold = _golden(name)
+    out = run_gate(ops, gate_inputs(p["heads"], p["vbs"], p["seed"]), p["heads"], p["vbs"], p["fp4"])
+    for key in gold:
+        np.testing.assert_array_equal(out[key].view(np.uint8), gold[key].view(np.uint8), err_msg=key)
+
+
+@pytest.mark.parametrize("fp4", [False, True])
+def test_gate_quant_vs_oracle_and_live_reference_7168(ops, fp4):
+    heads, vbs = 56, [16, 64, 32, 64, 48]
+    d = gate_inputs(heads, vbs, 77 + fp4)
+    out = run_gate(ops, d, heads, vbs, fp4)
+    f = lambda t: t.float().numpy()  # noqa: E731
+    rows = int(sum(vbs))
+    ref = ov.attn_gate_quant(f(d["ob"])[0], d["slot"].numpy(), rows, f(d["g"]), d["sg"].numpy(), f(d["oc"]), fp4=fp4)
+    np.testing.assert_allclose(out["sa"], ref["s"], rtol=4e-7)
+    if fp4:
+        assert_codes(oq.unpack_nibbles(out["a"]), ref["codes"], ref["amb"], "gate nibbles")
+    else:
+        assert_codes(out["a"], ref["codes"], ref["amb"], "gate fp8")
+    mod, _ = _ref()
+    dd = {k: v.to(DEV) for k, v in d.items()}
+    W = heads * 128
+    a = torch.zeros(rows, W // 2 if fp4 else W, device=DEV, dtype=torch.uint8)
+    asf = torch.zeros(ops.sf_rows(rows), W // 16, device=DEV, dtype=torch.uint8) if fp4 else None
+    sa = torch.zeros(rows, device=DEV)
+    mod.attn_gate_quant(dd["ob"], dd["g"], dd["sg"], dd["oc"], dd["slot"], len(vbs), 64,
+                        a if fp4 else a.view(torch.float8_e4m3fn), asf, sa, rows, None, None, None, None)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out["a"], a.cpu().numpy())
+    np.testing.assert_array_equal(out["sa"].view(np.uint32), sa.cpu().numpy().view(np.uint32))
+    if fp4:
+        np.testing.assert_array_equal(out["asf"], asf.cpu().numpy())
+
+
+def test_vbs_pattern_matches_reference_geometry():
+    v = vbs_pattern(23)
+    assert v[0] == 16 and v[3] == 32 and v[10] == 16 and v[14] == 32 and v[1] == 64
+
+
+# ------------------------------------------------------------------------------------------------ fine step (a9)
+def vsa_pipeline(ops, heads, T, Hh, Ww, k, seed, vbs_override=None):
+    """BASELINE config 4's path on a reduced grid: tile quant -> scores -> top-k -> FP8 VSA attention."""
+    g = torch.Generator().manual_seed(seed)
+    if vbs_override is None:
+        S = T * Hh * Ww
+        perm = tile_permutation(T, Hh, Ww)
+        vbs = torch.full((S // 64,), 64, dtype=torch.int32)
+    else:  # variable tiles over tokens already in tile order
+        vbs = vbs_override
+        S = int(vbs.sum())
+        perm = torch.arange(S, dtype=torch.int32)
+    q = torch.randn(heads, S, 128, generator=g).bfloat16()
+    kk = torch.randn(heads, S, 128, generator=g).bfloat16()
+    v = torch.randn(heads, S, 128, generator=g).bfloat16()
+    n = len(vbs)
+    n_ext = n + n % 2
+    tile_row0 = (vbs.cumsum(0) - vbs).to(torch.int32)
+    rows_pad = n_ext * 64
+    vbs_ext = torch.cat([vbs, torch.zeros(n_ext - n, dtype=torch.int32)])
+    d = lambda *sh, dt=torch.float32: torch.zeros(*sh, device=DEV, dtype=dt)  # noqa: E731
+    qb, kb, vb = (d(heads, rows_pad, 128, dt=torch.uint8) for _ in range(3))
+    qs, ks, vs = (torch.ones(heads, n_ext, device=DEV) for _ in range(3))
+    vs_head = d(heads)
+    qp, kp, vp = (d(heads, n, 128) for _ in range(3))
+    ops.vsa_tile_quant(q.to(DEV), kk.to(DEV), v.to(DEV), perm.to(DEV), tile_row0.to(DEV), vbs.to(DEV), qb, kb, vb, qs,
+                       ks, vs, qp, kp, vp, n, vs_head=vs_head)
+    sc = d(heads, n, n)
+    sm_scale = 1.0 / math.sqrt(128)
+    ops.tile_scores(qp, kp, sc, sm_scale)
+    idx = torch.full((1, heads, n_ext, n), -1, device=DEV, dtype=torch.int32)
+    num = torch.zeros(1, heads, n_ext, device=DEV, dtype=torch.int32)
+    ops.topk_rows(sc, n, n_ext, 0, [0], [n], [k], idx, num, False)
+    lse = d(heads, rows_pad)
+    out = ops.vsa_fp8(qb, kb, vb, idx, num, vbs_ext.to(DEV), sm_scale * math.log2(math.e), vs, vs_head, lse=lse,
+                      q_scale_blk=qs, k_scale_blk=ks)
+    torch.cuda.synchronize()
+    assert ops.vsa_status(reset=True) == 0
+    deq = lambda codes, s: (oq.e4m3_decode(codes.cpu().numpy()).reshape(heads, n_ext, 64, 128)  # noqa: E731
+                            * s.cpu().numpy()[:, :, None, None]).reshape(heads, rows_pad, 128)
+    ref = ov.vsa_fine(deq(qb, qs), deq(kb, ks), deq(vb, vs), idx.cpu().numpy()[0], num.cpu().numpy()[0],
+                      vbs_ext.numpy(), sm_scale)
+    valid = np.zeros((heads, rows_pad), dtype=bool)
+    for t in range(n):
+        valid[:, t * 64:t * 64 + int(vbs[t])] = True
+    got = out.cpu().float().numpy()[0]
+    return got, ref, valid, idx.cpu().numpy()[0], num.cpu().numpy()[0], lse.cpu().numpy()
+
+
+def _rel(a, b):
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def test_vsa_fp8_small_config4(ops):
+    got, ref, valid, idx, num, _ = vsa_pipeline(ops, heads=2, T=8, Hh=16, Ww=16, k=8, seed=50)
+    assert (num[:, :32] == 8).all()
+    assert _rel(got[valid], ref[valid]) < 1e-2  # 2e-2; two-term P gives ~2^-8
+
+
+def test_vsa_fp8_variable_tiles_and_odd_count(ops):
+    vbs = vbs_pattern(37)
+    got, ref, valid, idx, num, lse = vsa_pipeline(ops, heads=3, T=0, Hh=0, Ww=0, k=6, seed=51, vbs_override=vbs)
+    assert _rel(got[valid], ref[valid]) < 1e-2  # 2e-2; two-term P gives ~2^-8
+    assert np.isfinite(lse[valid]).all()
+
+
+@pytest.mark.parametrize("k", [32, 128])
+def test_vsa_fp8_config4_geometry(ops, k):
+    """512 tiles (8x64x64 tokens in 4x4x4 cubes), top-32 and a denser top-128, on 2 of the 40 heads."""
+    got, ref, valid, idx, num, _ = vsa_pipeline(ops, heads=2, T=8, Hh=64, Ww=64, k=k, seed=52 + k)
+    assert _rel(got[valid], ref[valid]) < 1e-2  # 2e-2; two-term P gives ~2^-8
