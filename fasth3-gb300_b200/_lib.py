@@ -18,6 +18,16 @@ F32 = ctypes.c_float
 SZ = ctypes.c_size_t
 
 
+class VsaArgs(ctypes.Structure):
+    """Mirror of ``h3b_vsa_args``."""
+    _fields_ = [
+        ("q", P), ("k", P), ("v", P), ("out", P), ("lse", P), ("idx", P), ("num", P), ("vbs_q", P), ("vbs_kv", P),
+        ("qs", P), ("ks", P), ("vs", P), ("vs_head", P), ("qk_coef", F32), ("heads", I32), ("n_q_ext", I32),
+        ("n_kv", I32), ("idx_ld", I32), ("q_scale_ld", I32), ("kv_scale_ld", I32), ("rows_chunk_q", I64),
+        ("rows_chunk_kv", I64), ("chunks_q", I32), ("chunks_kv", I32),
+    ]
+
+
 class Epilogue(ctypes.Structure):
     """Mirror of ``h3b_epilogue``."""
     _fields_ = [
@@ -56,6 +66,7 @@ SIGNATURES: dict[str, list] = {
     "h3b_vsa_tile_quant": [P, P, P, I32, I64, P, P, P, P, P, P, P, P, P, P, P, P, P, I64, I32, I32, P],
     "h3b_vsa_fp8": [P, P, P, P, P, P, P, P, P, P, F32, P, P, I32, I32, I32, I64, P],
     "h3b_vsa_status": [ctypes.POINTER(I32), I32],
+    "h3b_vsa_fp8_ex": [ctypes.POINTER(VsaArgs), P],
     "h3b_tile_scores": [P, P, I32, I32, F32, P, P],
     "h3b_topk_rows": [P, I32, I32, I32, I32, I32, P, P, P, P, P, I32, P],
     "h3b_compressed_branch": [P, P, I32, I32, P, P],

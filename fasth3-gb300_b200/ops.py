@@ -260,3 +260,26 @@ def attn_gate_quant(ob, g, sg, oc, slot, n_tiles, tile, a, asf, sa, rows, o1=Non
     n1 = lse1a.shape[-1] if lse1a is not None else 0
     call("h3b_attn_gate_quant", _p(ob), _p(g), _p(sg), _p(oc), _p(slot), ob.shape[-2], int(n_tiles), int(tile),
          _p(a), _p(asf), _p(sa), int(rows), W, _p(o1), _p(lse1a), _p(lse1b), n1, _p(lse2), _stream(ob))
+
+
+def vsa_fp8_ex(q, k, v, out, idx, num, vbs_q, vbs_kv, vs, vs_head, qk_coef, heads, n_q_ext, n_kv, rows_chunk_q,
+               rows_chunk_kv, chunks_q=1, chunks_kv=1, qs=None, ks=None, lse=None, idx_ld=None, q_scale_ld=None,
+               kv_scale_ld=None):
+    """General FP8 block-sparse attention (h3b_vsa_fp8_ex): chunked [chunks * heads, rows_chunk, 128] layouts (the
+    all-to-all layout of sequence parallelism) and separate key/value tiles (cross-attention)."""
+    import ctypes
+
+    from ._lib import VsaArgs
+    x = VsaArgs()
+    for name, t in (("q", q), ("k", k), ("v", v), ("out", out), ("lse", lse), ("idx", idx), ("num", num),
+                    ("vbs_q", vbs_q), ("vbs_kv", vbs_kv), ("qs", qs), ("ks", ks), ("vs", vs), ("vs_head", vs_head)):
+        setattr(x, name, _p(t))
+    x.qk_coef = float(qk_coef)
+    x.heads, x.n_q_ext, x.n_kv = int(heads), int(n_q_ext), int(n_kv)
+    x.idx_ld = int(idx_ld if idx_ld is not None else n_kv)
+    x.q_scale_ld = int(q_scale_ld if q_scale_ld is not None else n_q_ext)
+    x.kv_scale_ld = int(kv_scale_ld if kv_scale_ld is not None else n_kv)
+    x.rows_chunk_q, x.rows_chunk_kv = int(rows_chunk_q), int(rows_chunk_kv)
+    x.chunks_q, x.chunks_kv = int(chunks_q), int(chunks_kv)
+    call("h3b_vsa_fp8_ex", ctypes.byref(x), _stream(q))
+    return out

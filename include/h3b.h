@@ -180,6 +180,40 @@ int h3b_vsa_fp8(const void* qb, const void* kb, const void* vb, const int32_t* i
                 const int32_t* vbs, const float* qs_blk, const float* ks_blk, const float* vs_blk, const float* vs_head,
                 float qk_coef, void* out, float* lse, int heads, int n, int n_ext, int64_t rows_pad,
                 cudaStream_t stream);
+
+/* The general form of h3b_vsa_fp8 (no reference counterpart: it adds the layouts the sequence-parallel block and the
+ * cross-attention need). Q/out are [chunks_q * heads, rows_chunk_q, 128] and K/V [chunks_kv * heads, rows_chunk_kv,
+ * 128]: query tile t of head h is plane (t / (rows_chunk_q/64)) * heads + h, row (t % (rows_chunk_q/64)) * 64 -- one
+ * chunk is the plain heads-first layout, P chunks is what an all-to-all over P ranks delivers. Key tiles may be a
+ * different tensor (cross-attention). idx row (h, t) starts at (h * n_q_ext + t) * idx_ld; num [h * n_q_ext + t];
+ * qs [h * q_scale_ld + t]; ks/vs [h * kv_scale_ld + b]; lse indexed like out rows. */
+typedef struct h3b_vsa_args {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* out;
+  float* lse;
+  const int32_t* idx;
+  const int32_t* num;
+  const int32_t* vbs_q;  /* [n_q_ext] */
+  const int32_t* vbs_kv; /* [n_kv] */
+  const float* qs;       /* or NULL: static Q/K scales folded into qk_coef */
+  const float* ks;
+  const float* vs;
+  const float* vs_head;  /* [heads] */
+  float qk_coef;
+  int heads;
+  int n_q_ext;           /* even */
+  int n_kv;              /* <= 4096 */
+  int idx_ld;
+  int q_scale_ld;
+  int kv_scale_ld;
+  int64_t rows_chunk_q;
+  int64_t rows_chunk_kv;
+  int chunks_q;
+  int chunks_kv;
+} h3b_vsa_args;
+int h3b_vsa_fp8_ex(const h3b_vsa_args* args, cudaStream_t stream);
 /* Status word of the attention kernel's bounded waits (0 = none); reset != 0 clears it. Synchronizes the device. */
 int h3b_vsa_status(int* status, int reset);
 

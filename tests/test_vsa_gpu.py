@@ -344,3 +344,64 @@ def test_vsa_fp8_config4_geometry(ops, k):
     """512 tiles (8x64x64 tokens in 4x4x4 cubes), top-32 and a denser top-128, on 2 of the 40 heads."""
     got, ref, valid, idx, num, _ = vsa_pipeline(ops, heads=2, T=8, Hh=64, Ww=64, k=k, seed=52 + k)
     assert _rel(got[valid], ref[valid]) < 1e-2  # north-star bar: 2e-2; two-term P gives ~2^-8
+
+
+def test_vsa_fp8_chunked_layout_matches_plain(ops):
+    """The all-to-all layout ([chunks * heads, rows_chunk, 128], chunks = 4) gives the same bytes as the plain one."""
+    heads, n_ext, P = 2, 16, 4
+    rows = n_ext * 64
+    g = torch.Generator().manual_seed(60)
+    q8, k8, v8 = (torch.randint(0, 120, (heads, rows, 128), generator=g, dtype=torch.uint8) for _ in range(3))
+    scales = [torch.rand(heads, n_ext, generator=g) * 0.01 + 0.01 for _ in range(3)]
+    vs_head = scales[2].amax(1)
+    idx = torch.stack([torch.randperm(n_ext, generator=g)[:5].sort().values for _ in range(heads * n_ext)])
+    idx = idx.view(1, heads, n_ext, 5).to(torch.int32)
+    num = torch.full((1, heads, n_ext), 5, dtype=torch.int32)
+    vbs = torch.full((n_ext,), 64, dtype=torch.int32)
+    dv = lambda t: t.to(DEV)  # noqa: E731
+    plain = torch.zeros(heads, rows, 128, device=DEV, dtype=torch.bfloat16)
+    ops.vsa_fp8_ex(dv(q8), dv(k8), dv(v8), plain, dv(idx), dv(num), dv(vbs), dv(vbs), dv(scales[2]), dv(vs_head),
+                   0.1, heads, n_ext, n_ext, rows, rows, qs=dv(scales[0]), ks=dv(scales[1]), idx_ld=5)
+    chunk = lambda t: t.view(heads, P, rows // P, 128).permute(1, 0, 2, 3).contiguous()  # noqa: E731
+    out = torch.zeros(P, heads, rows // P, 128, device=DEV, dtype=torch.bfloat16)
+    ops.vsa_fp8_ex(dv(chunk(q8)), dv(chunk(k8)), dv(chunk(v8)), out, dv(idx), dv(num), dv(vbs), dv(vbs),
+                   dv(scales[2]), dv(vs_head), 0.1, heads, n_ext, n_ext, rows // P, rows // P, chunks_q=P, chunks_kv=P,
+                   qs=dv(scales[0]), ks=dv(scales[1]), idx_ld=5)
+    torch.cuda.synchronize()
+    assert torch.equal(out.permute(1, 0, 2, 3).reshape(heads, rows, 128), plain)
+
+
+def test_vsa_fp8_cross_attention_dense_text(ops):
+    """Cross-attention: 600 query rows (10 tiles) over 512 text keys (8 tiles), every tile selected: dense attention."""
+    heads, n_q, n_kv = 3, 10, 8
+    g = torch.Generator().manual_seed(61)
+    q = torch.randn(heads, n_q * 64, 128, generator=g)
+    kt = torch.randn(heads, n_kv * 64, 128, generator=g)
+    vt = torch.randn(heads, n_kv * 64, 128, generator=g)
+
+    def quant(x, n):  # per (head, tile) e4m3 with scale amax/448
+        xt = x.view(heads, n, 64, 128)
+        s = (xt.abs().amax((2, 3)) / 448).clamp_min(1e-30)
+        codes = (xt / s[:, :, None, None]).clamp(-448, 448).to(torch.float8_e4m3fn)
+        return codes.view(torch.uint8).view(heads, n * 64, 128), s
+
+    (q8, qs), (k8, ks), (v8, vs) = quant(q, n_q), quant(kt, n_kv), quant(vt, n_kv)
+    idx = torch.arange(n_kv, dtype=torch.int32).repeat(heads * n_q).view(1, heads, n_q, n_kv)
+    num = torch.full((1, heads, n_q), n_kv, dtype=torch.int32)
+    vbs_q = torch.full((n_q,), 64, dtype=torch.int32)
+    vbs_q[-1] = 24  # a partial last query tile
+    vbs_kv = torch.full((n_kv,), 64, dtype=torch.int32)
+    out = torch.zeros(heads, n_q * 64, 128, device=DEV, dtype=torch.bfloat16)
+    sm = 1.0 / math.sqrt(128)
+    dv = lambda t: t.to(DEV)  # noqa: E731
+    ops.vsa_fp8_ex(dv(q8), dv(k8), dv(v8), out, dv(idx), dv(num), dv(vbs_q), dv(vbs_kv), dv(vs), dv(vs.amax(1)),
+                   sm * math.log2(math.e), heads, n_q, n_kv, n_q * 64, n_kv * 64, qs=dv(qs), ks=dv(ks))
+    torch.cuda.synchronize()
+    deq = lambda c, s, n: (c.view(torch.float8_e4m3fn).float().view(heads, n, 64, 128)  # noqa: E731
+                           * s[:, :, None, None]).view(heads, n * 64, 128).double()
+    qd, kd, vd = deq(q8, qs, n_q), deq(k8, ks, n_kv), deq(v8, vs, n_kv)
+    ref = torch.softmax(qd @ kd.transpose(1, 2) * sm, -1) @ vd
+    rows = n_q * 64 - 40
+    err = float((out.cpu().double()[:, :rows] - ref[:, :rows]).norm() / ref[:, :rows].norm())
+    assert err < 1e-2
+    assert (out.cpu()[:, rows:] == 0).all()  # rows past vbs_q are not written (buffer was zero)
