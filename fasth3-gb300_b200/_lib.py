@@ -57,6 +57,7 @@ SIGNATURES: dict[str, list] = {
     "h3b_quant_nvfp4_workspace_bytes": [],
     "h3b_quant_nvfp4": [P, I64, I64, I32, P, P, P, P, P],
     "h3b_quant_nvfp4_noalloc": [P, I64, I64, I32, P, P, P, P],
+    "h3b_quant_nvfp4_rows": [P, I64, I64, I32, P, P, P, P],
     "h3b_pack_weight_fp8": [P, I64, I32, I32, P, P, P, P],
     "h3b_pack_weight_nvfp4": [P, I64, I32, P, P, P, P, P],
     "h3b_gemm_fp8": [P, P, I64, I64, I64, ctypes.POINTER(Epilogue), P],

@@ -344,3 +344,58 @@ extern "C" int h3b_quant_nvfp4(const void* x, int64_t ld, int64_t rows, int K, v
   return quant_nvfp4_tensor_launch(static_cast<const bf16*>(x), ld, rows, K, amax, static_cast<uint8_t*>(q), sf,
                                    s_out, stream);
 }
+
+// ------------------------------------------------------------------------------------------- per-row NVFP4, any K
+// One CTA per row: amax pass, then the 16-element block quantizer of h3fast.cu:121-138 with the row's global factor
+// gs = 1/s, s = max(amax/(448*6), 1e-12) (the reference's per-row NVFP4 form, as in swiglu_quant's FP4 output).
+namespace h3b {
+namespace {
+__global__ void __launch_bounds__(256) quant_nvfp4_rows_kernel(const bf16* __restrict__ x, int64_t ld, int K,
+                                                               uint8_t* __restrict__ q, uint8_t* __restrict__ sf,
+                                                               float* __restrict__ s_rows) {
+  __shared__ float stage[32];
+  const int64_t r = blockIdx.x;
+  const bf16* row = x + r * ld;
+  float am = 0.f;
+  for (int c = threadIdx.x * 8; c < K; c += 256 * 8) {
+    float f[8];
+    load8(row + c, f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(f[i]));
+  }
+  am = block_allreduce<8, true>(am, stage);
+  const float s = fmaxf(am / kFp4Range, kMinScaleFp4);
+  const float gs = 1.f / s;
+  const int blocks = K / 16;
+  for (int b = threadIdx.x; b < blocks; b += 256) {
+    float f[8], e[8];
+    load8(row + b * 16, f);
+    load8(row + b * 16 + 8, e);
+    float vmax = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) vmax = fmaxf(vmax, fmaxf(fabsf(f[j]), fabsf(e[j])));
+    uint32_t bits;
+    const float m = nvfp4_block_scale(vmax, gs, &bits);
+    uint2 o;
+    o.x = e2m1x4(f[0] * m, f[1] * m, f[2] * m, f[3] * m) | (e2m1x4(f[4] * m, f[5] * m, f[6] * m, f[7] * m) << 16);
+    o.y = e2m1x4(e[0] * m, e[1] * m, e[2] * m, e[3] * m) | (e2m1x4(e[4] * m, e[5] * m, e[6] * m, e[7] * m) << 16);
+    *reinterpret_cast<uint2*>(q + r * (K / 2) + b * 8) = o;
+    sf[sf_atom_offset(r, b, blocks)] = (uint8_t)bits;
+  }
+  if (threadIdx.x == 0) s_rows[r] = s;
+}
+}  // namespace
+}  // namespace h3b
+
+extern "C" int h3b_quant_nvfp4_rows(const void* x, int64_t ld, int64_t rows, int K, void* q, uint8_t* sf,
+                                    float* s_rows, cudaStream_t stream) {
+  clear_error();
+  H3B_REQUIRE(K > 0 && K % 64 == 0 && ld % 8 == 0 && ld >= K, "quant_nvfp4_rows: K multiple of 64, ld multiple of 8");
+  if (rows <= 0) return H3B_OK;
+  H3B_REQUIRE(x && q && sf && s_rows, "quant_nvfp4_rows: null pointer");
+  H3B_REQUIRE(aligned(x, 16) && aligned(q, 8), "quant_nvfp4_rows: x 16-byte, q 8-byte aligned");
+  quant_nvfp4_rows_kernel<<<(unsigned)rows, 256, 0, stream>>>(static_cast<const bf16*>(x), ld, K,
+                                                               static_cast<uint8_t*>(q), sf, s_rows);
+  H3B_LAUNCH_CHECK("quant_nvfp4_rows");
+  return H3B_OK;
+}

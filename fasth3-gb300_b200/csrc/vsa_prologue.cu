@@ -63,7 +63,7 @@ __global__ void __launch_bounds__(NWARP * 32) prologue_kernel(const ProArgs a) {
   float wqv[4], wkv[4];
   const int partner = l < HALF_LANES ? l + HALF_LANES : (l < 2 * HALF_LANES ? l - HALF_LANES : l);
   const float sign = l < HALF_LANES ? -1.f : 1.f;
-  const bool rot = l < 2 * HALF_LANES;
+  const bool rot = l < 2 * HALF_LANES && a.cosb != nullptr;
   if constexpr (ROWS) {
     const uint2 uq = *reinterpret_cast<const uint2*>(a.wq + l * 4), uk = *reinterpret_cast<const uint2*>(a.wk + l * 4);
     const __nv_bfloat162* hq = reinterpret_cast<const __nv_bfloat162*>(&uq);
@@ -238,9 +238,9 @@ extern "C" int h3b_qkv_prologue8(const void* q, const void* k, const void* v, in
                                  float* kp, float* vp, int heads, int64_t rows_pad, int n_tiles, int n_ext, float eps,
                                  cudaStream_t stream) {
   clear_error();
-  H3B_REQUIRE(q && k && v && s1 && tile_row0 && vbs && wq && wk && cosb && sinb && qb && kb && vb && vs_blk && qp &&
-                  kp && vp,
+  H3B_REQUIRE(q && k && v && s1 && tile_row0 && vbs && wq && wk && qb && kb && vb && vs_blk && qp && kp && vp,
               "qkv_prologue8: null pointer");
+  H3B_REQUIRE((cosb == nullptr) == (sinb == nullptr), "qkv_prologue8: give both or neither of cosb/sinb");
   H3B_REQUIRE(heads > 0 && n_tiles > 0 && n_ext >= n_tiles && rows_pad >= (int64_t)n_ext * TILE,
               "qkv_prologue8: bad heads / tiles / padding");
   H3B_REQUIRE(ld % 4 == 0 && aligned(q, 8) && aligned(k, 8) && aligned(v, 8), "qkv_prologue8: 8-byte aligned rows");

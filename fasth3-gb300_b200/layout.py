@@ -1,0 +1,82 @@
+"""Token layout of the DiT latent for the VSA path: the compact tile order of FastH3's runner (_get_layout,
+fastvideo/models/dits/h3fast/__init__.py:183-260), built here from the latent grid directly.
+
+Tokens of a T x H x W latent are grouped into 4 x 4 x 4 cubes (64-token tiles; cubes on the far edges are smaller,
+e.g. 48 tokens when the last time slab has 3 frames). Tiles are ordered (t, h, w); tokens inside a tile (t, h, w).
+``perm[i]`` is the token of tile-ordered row i; ``vbs[t]`` the valid rows of tile t; ``tile_row0[t]`` its first
+compact row; ``slot[i] = tile(i) * 64 + offset`` the row's place in the padded heads-first attention layout. The
+tile list is padded with empty tiles to a multiple of ``pad_to`` (2 x ranks, so every rank holds an even count).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+TILE = 64
+
+
+@dataclass
+class TileLayout:
+    grid: tuple[int, int, int]
+    perm: torch.Tensor       # int64 [rows]: tile-ordered row -> token
+    vbs: torch.Tensor        # int32 [n_ext]
+    tile_row0: torch.Tensor  # int32 [n_ext]
+    slot: torch.Tensor       # int32 [rows]
+    n_tiles: int             # real tiles
+    n_ext: int               # padded tile count
+    rows: int
+
+    def shard(self, first: int, last: int) -> "TileLayout":
+        """The layout of tiles [first, last) as a standalone layout (rows renumbered from 0)."""
+        vbs = self.vbs[first:last].clone()
+        row0 = (vbs.cumsum(0) - vbs).to(torch.int32)
+        r0 = int(self.tile_row0[first]) if first < len(self.tile_row0) else self.rows
+        rows = int(vbs.sum())
+        perm = self.perm[r0:r0 + rows].clone()
+        slot = torch.cat([torch.arange(int(v)) + i * TILE for i, v in enumerate(vbs.tolist())]).to(torch.int32) \
+            if rows else torch.zeros(0, dtype=torch.int32)
+        real = min(max(self.n_tiles - first, 0), last - first)
+        return TileLayout(self.grid, perm, vbs, row0, slot, real, last - first, rows)
+
+
+def tile_layout(T: int, H: int, W: int, pad_to: int = 2, cube=(4, 4, 4)) -> TileLayout:
+    ct, ch, cw = cube
+    nt, nh, nw = math.ceil(T / ct), math.ceil(H / ch), math.ceil(W / cw)
+    tok = torch.arange(T * H * W).view(T, H, W)
+    perm, vbs = [], []
+    for a in range(nt):
+        for b in range(nh):
+            for c in range(nw):
+                block = tok[a * ct:(a + 1) * ct, b * ch:(b + 1) * ch, c * cw:(c + 1) * cw].reshape(-1)
+                perm.append(block)
+                vbs.append(block.numel())
+    n = len(vbs)
+    n_ext = (n + pad_to - 1) // pad_to * pad_to
+    vbs = torch.tensor(vbs + [0] * (n_ext - n), dtype=torch.int32)
+    perm = torch.cat(perm)
+    row0 = (vbs.cumsum(0) - vbs).to(torch.int32)
+    slot = torch.cat([torch.arange(int(v)) + i * TILE for i, v in enumerate(vbs.tolist())]).to(torch.int32)
+    return TileLayout((T, H, W), perm, vbs, row0, slot, n, n_ext, int(perm.numel()))
+
+
+def rope_3d(layout: TileLayout, rot_dims: int = 96, theta: float = 10000.0) -> tuple[torch.Tensor, torch.Tensor]:
+    """cos/sin [rows, rot_dims] (bf16) in tile order for rotate-half RoPE on the first ``rot_dims`` dims, the pairs
+    (d, d + rot_dims/2) (the reference's RoPE form, tests/test_kernels.py:49-52). The rot_dims/2 frequencies are split
+    evenly over the (t, h, w) axes."""
+    T, H, W = layout.grid
+    half = rot_dims // 2
+    per_axis = half // 3
+    t = layout.perm // (H * W)
+    h = (layout.perm // W) % H
+    w = layout.perm % W
+    ang = []
+    for pos in (t, h, w):
+        freqs = theta ** (-torch.arange(per_axis, dtype=torch.float64) / per_axis)
+        ang.append(pos.double()[:, None] * freqs[None, :])
+    a = torch.cat(ang, 1)
+    a = torch.cat([a, torch.zeros(a.shape[0], half - a.shape[1], dtype=torch.float64)], 1)
+    cos = torch.cat([a.cos(), a.cos()], 1)
+    sin = torch.cat([a.sin(), a.sin()], 1)
+    return cos.to(torch.bfloat16), sin.to(torch.bfloat16)

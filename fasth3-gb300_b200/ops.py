@@ -82,6 +82,13 @@ def quant_nvfp4_tensor(x: torch.Tensor, amax_dev: torch.Tensor, q: torch.Tensor,
          _p(sf), _p(s_out), _stream(x))
 
 
+def quant_nvfp4_rows(x: torch.Tensor, q: torch.Tensor, sf: torch.Tensor, s_rows: torch.Tensor) -> None:
+    """Per-row NVFP4 (global scale per row, s_rows[r] = max(amax_r/2688, 1e-12)) for any K multiple of 64."""
+    K = x.shape[-1]
+    call("h3b_quant_nvfp4_rows", _p(x), x.stride(-2) if x.dim() > 1 else K, x.numel() // K, K, _p(q), _p(sf),
+         _p(s_rows), _stream(x))
+
+
 def workspace_bytes() -> int:
     return int(lib().h3b_quant_nvfp4_workspace_bytes())
 

@@ -72,6 +72,13 @@ int h3b_amax_bf16(const void* x, int64_t ld, int64_t rows, int K, float* amax, c
 int h3b_quant_nvfp4_tensor(const void* x, int64_t ld, int64_t rows, int K, const float* amax, void* q, uint8_t* sf,
                            float* s_out, cudaStream_t stream);
 
+/* Per-row NVFP4 quantizer of a bf16 matrix [rows, K] (leading dim ld), any K multiple of 64: s_rows[r] =
+ * max(amax_r/(448*6), 1e-12), block math of h3fast.cu:121-138 with gs = 1/s_rows[r] (the reference's per-row FP4
+ * output of swiglu_quant / attn_gate_quant / resid_norm_quant, here for the FFN intermediate of any width). The padding
+ * rows of sf are not written. */
+int h3b_quant_nvfp4_rows(const void* x, int64_t ld, int64_t rows, int K, void* q, uint8_t* sf, float* s_rows,
+                         cudaStream_t stream);
+
 /* One call of the two above: amax pass then quantization. `workspace` is device scratch of at least
  * h3b_quant_nvfp4_workspace_bytes() bytes, 256-byte aligned; the call zeroes it itself. */
 size_t h3b_quant_nvfp4_workspace_bytes(void);
@@ -155,6 +162,7 @@ int h3b_gemm_nvfp4(const void* A, const uint8_t* sfa, const void* B, const uint8
  * (max(amax/448, 1e-30)); vs_head [heads] folded with an atomic max (caller zeroes; may be NULL); qp/kp/vp fp32
  * [heads, n_tiles, 128] tile means. Q/K scales: static (inv_sq, inv_sk: 1/scale) when qs_blk == NULL, else one scale
  * per (head, tile) like V, written to qs_blk/ks_blk [heads, n_ext]. */
+/* cosb == sinb == NULL skips the rotation (cross-attention queries and text keys). */
 int h3b_qkv_prologue8(const void* q, const void* k, const void* v, int64_t ld, const float* s1,
                       const int32_t* tile_row0, const int32_t* vbs, const void* wq, const void* wk, const void* cosb,
                       const void* sinb, float inv_sq, float inv_sk, void* qb, void* kb, void* vb, float* qs_blk,
