@@ -278,6 +278,80 @@ def vsa_config4_secondary(ops, dev, stream, args) -> dict:
     return res
 
 
+def fp8_chain_secondary(pkg, dev, stream, args) -> dict:
+    """the FP8 block chain on 32760 tokens x 5120 (16.145 TFLOP of GEMMs per pass)."""
+    import torch
+    chain = pkg.runner.Fp8BlockChain.random(dev, seed=13)
+    g = torch.Generator(device=dev).manual_seed(17)
+    rows = 32760
+    x0 = torch.randn(rows, 5120, device=dev, generator=g).bfloat16()
+    tabs = (torch.randn(6, 5120, device=dev, generator=g) * 0.1).bfloat16()
+    x = x0.clone()
+    for _ in range(3):
+        x.copy_(x0)
+        chain(x, tabs)
+    torch.cuda.synchronize()
+    n = max(3, min(args.steps, 10))
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * n)]
+    for i in range(n):
+        x.copy_(x0)  # every pass starts from the same stream (the copy is outside the timed interval)
+        ev[2 * i].record(stream)
+        chain(x, tabs)
+        ev[2 * i + 1].record(stream)
+    torch.cuda.synchronize()
+    ms = sum(ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(n)) / n
+    flop = chain.flop(rows)
+    del chain, x, x0
+    torch.cuda.empty_cache()
+    return {"rows": rows, "ms": ms, "tflops": flop / (ms * 1e-3) / 1e12, "gemm_tflop": flop / 1e12,
+            "launches_per_pass": 8}
+
+
+def dit_step_secondary(pkg, dev, stream, args, ws) -> dict:
+    """one 50-block DiT step on the 31x48x84 latent (124,992 tokens) with cross-attention to 512
+    text tokens, NVFP4 linears, FP8 VSA self-attention (top-32 of 2016 tiles), sequence-parallel over the ranks of
+    this job (head all-to-all over NCCL). Timed with CUDA events, max over ranks (strong scaling: fixed tokens)."""
+    import torch
+    import torch.distributed as dist
+    cfg = pkg.model.DiTConfig(blocks=50, fmt="nvfp4")
+    m = pkg.model.DiTModel.random(cfg, device=dev, seed=0)
+    grid = (31, 48, 84)
+    S = grid[0] * grid[1] * grid[2]
+    g = torch.Generator(device=dev).manual_seed(21)
+    x = torch.randn(1, S, cfg.hidden, device=dev, generator=g).bfloat16()
+    ctx = torch.randn(1, cfg.text_len, cfg.text_dim, device=dev, generator=g).bfloat16()
+    temb = m.timestep_embedding(0.5)
+    meta = pkg.runner.VsaMeta(grid=grid, topk=32)
+    sp = pkg.sp.SeqParallel() if ws > 1 else None
+    r = pkg.runner.H3FastRunner(m, sp)
+    for _ in range(2):
+        out = r.forward(x, temb, None, None, meta, context=ctx)
+    torch.cuda.synchronize()
+    reps = max(2, min(args.steps, 3))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(reps):
+        out = r.forward(x, temb, None, None, meta, context=ctx)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    if ws > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    finite = bool(torch.isfinite(out.float()).all())
+    lin = 2.0 * S * (6 * cfg.hidden ** 2 + 2 * cfg.hidden * cfg.ffn) * cfg.blocks
+    del r, m, x, out
+    torch.cuda.empty_cache()
+    return {"grid": list(grid), "tokens": S, "blocks": cfg.blocks, "topk": 32, "n_gpus": ws, "ms_per_step": ms,
+            "steps": reps, "linear_tflop_per_step": lin / 1e12, "linear_share_tflops": lin / (ms * 1e-3) / 1e12,
+            "output_finite": finite, "scaling": "strong", "parallelism": f"sp{ws}"}
+
+
 def run_ours(args) -> None:
     import torch
     import torch.distributed as dist
@@ -360,8 +434,13 @@ def run_ours(args) -> None:
     barrier()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
 
+    pkg = __graft_entry__.load_package()
     fp8 = fp8_linear_secondary(ops, dev, stream, args) if not args.no_fp8 else None
+    chain = fp8_chain_secondary(pkg, dev, stream, args) if not args.no_fp8 else None
     vsa = vsa_config4_secondary(ops, dev, stream, args) if not args.no_vsa else None
+    del x, y, qa, sfa
+    torch.cuda.empty_cache()
+    dit = dit_step_secondary(pkg, dev, stream, args, ws) if not args.no_dit else None
 
     if ws > 1:
         t = torch.tensor([total_ms, e2e_ms, gemm_ms, quant_ms], device=dev, dtype=torch.float64)
@@ -404,6 +483,11 @@ def run_ours(args) -> None:
         if vsa is not None:
             vsa["fine_frac_of_2x_bf16"] = vsa["fine_tflops"] / (2.0 * peaks["bf16"])
             line["vsa_config4"] = vsa
+        if chain is not None:
+            chain["frac_of_2x_bf16"] = chain["tflops"] / (2.0 * peaks["bf16"])
+            line["fp8_block_chain_config3"] = chain
+        if dit is not None:
+            line["dit_step_config5"] = dit
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
@@ -420,6 +504,7 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-fp8", action="store_true", help="skip the secondary FP8 linear measurement")
     ap.add_argument("--no-vsa", action="store_true", help="skip the secondary VSA (config 4) measurement")
+    ap.add_argument("--no-dit", action="store_true", help="skip the secondary 50-block DiT step (config 5)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

@@ -65,6 +65,7 @@ SIGNATURES: dict[str, list] = {
     "h3b_qkv_prologue8": [P, P, P, I64, P, P, P, P, P, P, P, F32, F32, P, P, P, P, P, P, P, P, P, P, I32, I64, I32,
                           I32, F32, P],
     "h3b_vsa_tile_quant": [P, P, P, I32, I64, P, P, P, P, P, P, P, P, P, P, P, P, P, I64, I32, I32, P],
+    "h3b_head_tile_quant": [P, I64, P, P, P, P, P, P, P, I32, I64, I32, I32, F32, P],
     "h3b_vsa_fp8": [P, P, P, P, P, P, P, P, P, P, F32, P, P, I32, I32, I32, I64, P],
     "h3b_vsa_status": [ctypes.POINTER(I32), I32],
     "h3b_vsa_fp8_ex": [ctypes.POINTER(VsaArgs), P],

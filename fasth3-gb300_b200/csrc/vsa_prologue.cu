@@ -50,70 +50,83 @@ struct ProArgs {
   float eps;
 };
 
+__device__ __forceinline__ void unpack4(uint2 u, float (&f)[4]) {
+  const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u);
+  float2 t = __bfloat1622float2(b[0]);
+  f[0] = t.x;
+  f[1] = t.y;
+  t = __bfloat1622float2(b[1]);
+  f[2] = t.x;
+  f[3] = t.y;
+}
+
+// bf16-exact floats -> packed bf16 (lossless: every value passed here is already a bf16 value)
+__device__ __forceinline__ uint2 pack4(const float (&f)[4]) {
+  uint2 u;
+  __nv_bfloat162 lo = __floats2bfloat162_rn(f[0], f[1]), hi = __floats2bfloat162_rn(f[2], f[3]);
+  u.x = *reinterpret_cast<uint32_t*>(&lo);
+  u.y = *reinterpret_cast<uint32_t*>(&hi);
+  return u;
+}
+
+// Rows are loaded for all of a warp's rows before any arithmetic (eight rows x three 8-byte loads in flight per lane),
+// and the rounded bf16 values are kept packed until the quantization pass; the arithmetic per element and the order of
+// every float32 sum are those of the reference kernel.
 template <bool ROWS, bool TILE_QK>
-__global__ void __launch_bounds__(NWARP * 32) prologue_kernel(const ProArgs a) {
+__global__ void __launch_bounds__(NWARP * 32, 2) prologue_kernel(const ProArgs a) {
   __shared__ float sp[3][NWARP][D];
   __shared__ float red[32];
   const int h = blockIdx.x % a.heads, ti = blockIdx.x / a.heads;
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
   const int row0 = a.tile_row0[ti], n = a.vbs[ti];
   float pq[4] = {0.f, 0.f, 0.f, 0.f}, pk[4] = {0.f, 0.f, 0.f, 0.f}, pv[4] = {0.f, 0.f, 0.f, 0.f};
-  float qs[RPW][4], ks[RPW][4], vs[RPW][4];
+  uint2 rq[RPW], rk[RPW], rv[RPW];
+  float s1v[RPW];
   float qmax = 0.f, kmax = 0.f, vmax = 0.f;
   float wqv[4], wkv[4];
   const int partner = l < HALF_LANES ? l + HALF_LANES : (l < 2 * HALF_LANES ? l - HALF_LANES : l);
   const float sign = l < HALF_LANES ? -1.f : 1.f;
   const bool rot = l < 2 * HALF_LANES && a.cosb != nullptr;
   if constexpr (ROWS) {
-    const uint2 uq = *reinterpret_cast<const uint2*>(a.wq + l * 4), uk = *reinterpret_cast<const uint2*>(a.wk + l * 4);
-    const __nv_bfloat162* hq = reinterpret_cast<const __nv_bfloat162*>(&uq);
-    const __nv_bfloat162* hk = reinterpret_cast<const __nv_bfloat162*>(&uk);
+    unpack4(*reinterpret_cast<const uint2*>(a.wq + l * 4), wqv);
+    unpack4(*reinterpret_cast<const uint2*>(a.wk + l * 4), wkv);
+  }
+  // ---- loads
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      float2 t = __bfloat1622float2(hq[j]);
-      wqv[2 * j] = t.x;
-      wqv[2 * j + 1] = t.y;
-      t = __bfloat1622float2(hk[j]);
-      wkv[2 * j] = t.x;
-      wkv[2 * j + 1] = t.y;
+  for (int u = 0; u < RPW; ++u) {
+    const int i = w + u * NWARP;
+    rq[u] = rk[u] = rv[u] = make_uint2(0u, 0u);
+    s1v[u] = 0.f;
+    if (i < n) {
+      size_t src;
+      if constexpr (ROWS) {
+        src = (size_t)(row0 + i) * a.ld + (size_t)h * D + l * 4;
+      } else {
+        int64_t tok = a.perm ? a.perm[row0 + i] : row0 + i;
+        if (tok < 0 || tok >= a.seqlen) tok = 0;  // out-of-range token: read token 0 rather than fault
+        src = ((size_t)h * a.seqlen + tok) * D + l * 4;
+      }
+      rq[u] = *reinterpret_cast<const uint2*>(a.q + src);
+      rk[u] = *reinterpret_cast<const uint2*>(a.k + src);
+      rv[u] = *reinterpret_cast<const uint2*>(a.v + src);
+      if constexpr (ROWS) {
+        const int64_t r = row0 + i;
+        s1v[u] = a.s1[r];
+      }
     }
   }
+  // ---- per-row arithmetic
 #pragma unroll
   for (int u = 0; u < RPW; ++u) {
     const int i = w + u * NWARP;
     if (i >= n) break;  // warp-uniform
-    size_t src;
-    if constexpr (ROWS) {
-      src = (size_t)(row0 + i) * a.ld + (size_t)h * D + l * 4;
-    } else {
-      int64_t tok = a.perm ? a.perm[row0 + i] : row0 + i;
-      if (tok < 0 || tok >= a.seqlen) tok = 0;  // out-of-range token: read token 0 rather than fault
-      src = ((size_t)h * a.seqlen + tok) * D + l * 4;
-    }
     float qf[4], kf[4], vf[4];
-    {
-      const uint2 u0 = *reinterpret_cast<const uint2*>(a.q + src), u1 = *reinterpret_cast<const uint2*>(a.k + src),
-                  u2 = *reinterpret_cast<const uint2*>(a.v + src);
-      const __nv_bfloat162* b0 = reinterpret_cast<const __nv_bfloat162*>(&u0);
-      const __nv_bfloat162* b1 = reinterpret_cast<const __nv_bfloat162*>(&u1);
-      const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&u2);
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        float2 t = __bfloat1622float2(b0[j]);
-        qf[2 * j] = t.x;
-        qf[2 * j + 1] = t.y;
-        t = __bfloat1622float2(b1[j]);
-        kf[2 * j] = t.x;
-        kf[2 * j + 1] = t.y;
-        t = __bfloat1622float2(b2[j]);
-        vf[2 * j] = t.x;
-        vf[2 * j + 1] = t.y;
-      }
-    }
+    unpack4(rq[u], qf);
+    unpack4(rk[u], kf);
+    unpack4(rv[u], vf);
     float qo[4], ko[4];
     if constexpr (ROWS) {
-      const int64_t r = row0 + i;
-      const float s = a.s1[r];
+      const float s = s1v[u];
       float sumq = 0.f, sumk = 0.f;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -128,27 +141,17 @@ __global__ void __launch_bounds__(NWARP * 32) prologue_kernel(const ProArgs a) {
         sumq += __shfl_xor_sync(0xffffffffu, sumq, o);
         sumk += __shfl_xor_sync(0xffffffffu, sumk, o);
       }
-      const float rq = rsqrtf(sumq / D + a.eps), rk = rsqrtf(sumk / D + a.eps);
+      const float rq_ = rsqrtf(sumq / D + a.eps), rk_ = rsqrtf(sumk / D + a.eps);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        qf[j] *= rq * wqv[j];
-        kf[j] *= rk * wkv[j];
+        qf[j] *= rq_ * wqv[j];
+        kf[j] *= rk_ * wkv[j];
       }
       float c[4] = {1.f, 1.f, 1.f, 1.f}, sn[4] = {0.f, 0.f, 0.f, 0.f};
       if (rot) {
-        const uint2 uc = *reinterpret_cast<const uint2*>(a.cosb + r * ROT + l * 4);
-        const uint2 us = *reinterpret_cast<const uint2*>(a.sinb + r * ROT + l * 4);
-        const __nv_bfloat162* bc = reinterpret_cast<const __nv_bfloat162*>(&uc);
-        const __nv_bfloat162* bs = reinterpret_cast<const __nv_bfloat162*>(&us);
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          float2 t = __bfloat1622float2(bc[j]);
-          c[2 * j] = t.x;
-          c[2 * j + 1] = t.y;
-          t = __bfloat1622float2(bs[j]);
-          sn[2 * j] = t.x;
-          sn[2 * j + 1] = t.y;
-        }
+        const int64_t r = row0 + i;
+        unpack4(*reinterpret_cast<const uint2*>(a.cosb + r * ROT + l * 4), c);
+        unpack4(*reinterpret_cast<const uint2*>(a.sinb + r * ROT + l * 4), sn);
       }
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -172,10 +175,10 @@ __global__ void __launch_bounds__(NWARP * 32) prologue_kernel(const ProArgs a) {
       qmax = fmaxf(qmax, fabsf(qo[j]));
       kmax = fmaxf(kmax, fabsf(ko[j]));
       vmax = fmaxf(vmax, fabsf(vf[j]));
-      qs[u][j] = qo[j];
-      ks[u][j] = ko[j];
-      vs[u][j] = vf[j];
     }
+    rq[u] = pack4(qo);
+    rk[u] = pack4(ko);
+    rv[u] = pack4(vf);
   }
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -208,12 +211,13 @@ __global__ void __launch_bounds__(NWARP * 32) prologue_kernel(const ProArgs a) {
     const int i = w + u * NWARP;
     if (i >= n) break;
     const size_t dst = (plane + i) * D + l * 4;
-    *reinterpret_cast<uint32_t*>(a.qb + dst) =
-        e4m3x4(qs[u][0] * inv_q, qs[u][1] * inv_q, qs[u][2] * inv_q, qs[u][3] * inv_q);
-    *reinterpret_cast<uint32_t*>(a.kb + dst) =
-        e4m3x4(ks[u][0] * inv_k, ks[u][1] * inv_k, ks[u][2] * inv_k, ks[u][3] * inv_k);
-    *reinterpret_cast<uint32_t*>(a.vb + dst) =
-        e4m3x4(vs[u][0] * inv_v, vs[u][1] * inv_v, vs[u][2] * inv_v, vs[u][3] * inv_v);
+    float qv[4], kv[4], vv[4];
+    unpack4(rq[u], qv);
+    unpack4(rk[u], kv);
+    unpack4(rv[u], vv);
+    *reinterpret_cast<uint32_t*>(a.qb + dst) = e4m3x4(qv[0] * inv_q, qv[1] * inv_q, qv[2] * inv_q, qv[3] * inv_q);
+    *reinterpret_cast<uint32_t*>(a.kb + dst) = e4m3x4(kv[0] * inv_k, kv[1] * inv_k, kv[2] * inv_k, kv[3] * inv_k);
+    *reinterpret_cast<uint32_t*>(a.vb + dst) = e4m3x4(vv[0] * inv_v, vv[1] * inv_v, vv[2] * inv_v, vv[3] * inv_v);
   }
   const float inv = 1.f / (float)n;
   for (int e = threadIdx.x; e < 3 * D; e += NWARP * 32) {
@@ -274,5 +278,115 @@ extern "C" int h3b_vsa_tile_quant(const void* q, const void* k, const void* v, i
             rows_pad, n_tiles, n_ext, 0.f};
   prologue_kernel<false, true><<<n_tiles * heads, NWARP * 32, 0, stream>>>(a);
   H3B_LAUNCH_CHECK("vsa_tile_quant");
+  return H3B_OK;
+}
+
+// ------------------------------------------------------------------------------------------- one-tensor tile quant
+// The prologue's per-tile E4M3 quantization for a single tensor (cross-attention queries, text keys and values), with
+// the same work split and expression order: x * s1[row] (optional), per-head RMSNorm with weight (optional), bf16
+// rounding, scale max(amax/448, 1e-30) per (head, tile), folded into xs_head with an atomic max (optional).
+namespace h3b {
+namespace {
+struct HtqArgs {
+  const bf16* x;
+  int64_t ld;
+  const float* s1;
+  const int32_t* tile_row0;
+  const int32_t* vbs;
+  const bf16* w;
+  uint8_t* xb;
+  float* xs_blk;
+  float* xs_head;
+  int heads;
+  int64_t rows_pad;
+  int n_ext;
+  float eps;
+};
+
+__global__ void __launch_bounds__(NWARP * 32) head_tile_quant_kernel(const HtqArgs a) {
+  __shared__ float red[32];
+  const int h = blockIdx.x % a.heads, ti = blockIdx.x / a.heads;
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  const int row0 = a.tile_row0[ti], n = a.vbs[ti];
+  float xs[RPW][4];
+  float xmax = 0.f;
+  float wv[4] = {1.f, 1.f, 1.f, 1.f};
+  if (a.w) {
+    const uint2 uw = *reinterpret_cast<const uint2*>(a.w + l * 4);
+    const __nv_bfloat162* hw = reinterpret_cast<const __nv_bfloat162*>(&uw);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const float2 t = __bfloat1622float2(hw[j]);
+      wv[2 * j] = t.x;
+      wv[2 * j + 1] = t.y;
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < RPW; ++u) {
+    const int i = w + u * NWARP;
+    if (i >= n) break;  // warp-uniform
+    const int64_t r = row0 + i;
+    const uint2 u0 = *reinterpret_cast<const uint2*>(a.x + (size_t)r * a.ld + (size_t)h * D + l * 4);
+    const __nv_bfloat162* b0 = reinterpret_cast<const __nv_bfloat162*>(&u0);
+    float f[4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const float2 t = __bfloat1622float2(b0[j]);
+      f[2 * j] = t.x;
+      f[2 * j + 1] = t.y;
+    }
+    const float s = a.s1 ? a.s1[r] : 1.f;
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      f[j] *= s;
+      sum += f[j] * f[j];
+    }
+    if (a.w) {
+#pragma unroll
+      for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      const float rr = rsqrtf(sum / D + a.eps);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) f[j] *= rr * wv[j];
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      xs[u][j] = to_bf16_and_back(f[j]);
+      xmax = fmaxf(xmax, fabsf(xs[u][j]));
+    }
+  }
+  xmax = block_allreduce<NWARP, true>(xmax, red);
+  const float sb = fmaxf(xmax / kFp8Max, 1e-30f);
+  if (threadIdx.x == 0) {
+    a.xs_blk[(size_t)h * a.n_ext + ti] = sb;
+    if (a.xs_head) atomicMax(reinterpret_cast<int*>(a.xs_head + h), __float_as_int(sb));
+  }
+  const float inv = 1.f / sb;
+  const size_t plane = (size_t)h * a.rows_pad + (size_t)ti * TILE;
+#pragma unroll
+  for (int u = 0; u < RPW; ++u) {
+    const int i = w + u * NWARP;
+    if (i >= n) break;
+    *reinterpret_cast<uint32_t*>(a.xb + (plane + i) * D + l * 4) =
+        e4m3x4(xs[u][0] * inv, xs[u][1] * inv, xs[u][2] * inv, xs[u][3] * inv);
+  }
+}
+}  // namespace
+}  // namespace h3b
+
+extern "C" int h3b_head_tile_quant(const void* x, int64_t ld, const float* s1, const int32_t* tile_row0,
+                                   const int32_t* vbs, const void* w, void* xb, float* xs_blk, float* xs_head,
+                                   int heads, int64_t rows_pad, int n_tiles, int n_ext, float eps,
+                                   cudaStream_t stream) {
+  clear_error();
+  H3B_REQUIRE(x && tile_row0 && vbs && xb && xs_blk, "head_tile_quant: null pointer");
+  H3B_REQUIRE(heads > 0 && n_tiles > 0 && n_ext >= n_tiles && rows_pad >= (int64_t)n_ext * TILE,
+              "head_tile_quant: bad heads / tiles / padding");
+  H3B_REQUIRE(ld % 4 == 0 && ld >= (int64_t)heads * D && aligned(x, 8), "head_tile_quant: 8-byte aligned rows");
+  H3B_REQUIRE(!w || aligned(w, 8), "head_tile_quant: norm weight 8-byte aligned");
+  HtqArgs a{static_cast<const bf16*>(x), ld, s1, tile_row0, vbs, static_cast<const bf16*>(w),
+            static_cast<uint8_t*>(xb), xs_blk, xs_head, heads, rows_pad, n_ext, eps};
+  head_tile_quant_kernel<<<n_tiles * heads, NWARP * 32, 0, stream>>>(a);
+  H3B_LAUNCH_CHECK("head_tile_quant");
   return H3B_OK;
 }

@@ -17,26 +17,75 @@ namespace {
 constexpr int D = 128;
 
 // ------------------------------------------------------------------------------------------------ scores
-// Block = 16x16 outputs of one head, 256 threads, one output per thread; q/k tile means staged in shared memory.
+// Block = 128x128 outputs of one head, 256 threads, an 8x8 register tile per thread; the q and k tile means are staged
+// in shared memory 32 dimensions at a time, transposed ([d][row], rows padded by 4 floats against bank conflicts).
+// Each output still accumulates d = 0..127 in order with separately rounded products and sums.
+constexpr int SB = 128, SCH = 32, SPAD = SB + 4;
+
 __global__ void __launch_bounds__(256) scores_kernel(const float* __restrict__ qp, const float* __restrict__ kp,
                                                      int n, float scale, float* __restrict__ sc) {
-  __shared__ float sq[16][D + 1];
-  __shared__ float sk[16][D + 1];
+  __shared__ __align__(16) float sq[SCH][SPAD];
+  __shared__ __align__(16) float sk[SCH][SPAD];
   const int h = blockIdx.z;
-  const int i0 = blockIdx.y * 16, j0 = blockIdx.x * 16;
+  const int i0 = blockIdx.y * SB, j0 = blockIdx.x * SB;
   const float* qh = qp + (size_t)h * n * D;
   const float* kh = kp + (size_t)h * n * D;
-  for (int e = threadIdx.x; e < 16 * D; e += 256) {
-    const int r = e / D, d = e % D;
-    sq[r][d] = (i0 + r < n) ? qh[(size_t)(i0 + r) * D + d] : 0.f;
-    sk[r][d] = (j0 + r < n) ? kh[(size_t)(j0 + r) * D + d] : 0.f;
+  const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
+  float acc[8][8];
+#pragma unroll
+  for (int a = 0; a < 8; ++a)
+#pragma unroll
+    for (int b = 0; b < 8; ++b) acc[a][b] = 0.f;
+  for (int dc = 0; dc < D; dc += SCH) {
+    for (int e = threadIdx.x; e < SB * SCH / 4; e += 256) {
+      const int r = e / (SCH / 4), d4 = (e % (SCH / 4)) * 4;
+      const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 vq = i0 + r < n ? *reinterpret_cast<const float4*>(qh + (size_t)(i0 + r) * D + dc + d4) : zero;
+      const float4 vk = j0 + r < n ? *reinterpret_cast<const float4*>(kh + (size_t)(j0 + r) * D + dc + d4) : zero;
+      sq[d4 + 0][r] = vq.x;
+      sq[d4 + 1][r] = vq.y;
+      sq[d4 + 2][r] = vq.z;
+      sq[d4 + 3][r] = vq.w;
+      sk[d4 + 0][r] = vk.x;
+      sk[d4 + 1][r] = vk.y;
+      sk[d4 + 2][r] = vk.z;
+      sk[d4 + 3][r] = vk.w;
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int d = 0; d < SCH; ++d) {
+      const float4 a0 = *reinterpret_cast<const float4*>(&sq[d][ty * 8]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&sq[d][ty * 8 + 4]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&sk[d][tx * 8]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&sk[d][tx * 8 + 4]);
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int a = 0; a < 8; ++a)
+#pragma unroll
+        for (int b = 0; b < 8; ++b) acc[a][b] = __fadd_rn(acc[a][b], __fmul_rn(av[a], bv[b]));
+    }
+    __syncthreads();
   }
-  __syncthreads();
-  const int ti = threadIdx.x / 16, tj = threadIdx.x % 16;
-  float acc = 0.f;
-#pragma unroll 8
-  for (int d = 0; d < D; ++d) acc = __fadd_rn(acc, __fmul_rn(sq[ti][d], sk[tj][d]));
-  if (i0 + ti < n && j0 + tj < n) sc[((size_t)h * n + i0 + ti) * n + j0 + tj] = __fmul_rn(acc, scale);
+  const int jb = j0 + tx * 8;
+#pragma unroll
+  for (int a = 0; a < 8; ++a) {
+    const int i = i0 + ty * 8 + a;
+    if (i >= n) break;
+    float* dst = sc + ((size_t)h * n + i) * n;
+    if (jb + 8 <= n && (n & 3) == 0) {
+      *reinterpret_cast<float4*>(dst + jb) = make_float4(__fmul_rn(acc[a][0], scale), __fmul_rn(acc[a][1], scale),
+                                                         __fmul_rn(acc[a][2], scale), __fmul_rn(acc[a][3], scale));
+      *reinterpret_cast<float4*>(dst + jb + 4) = make_float4(__fmul_rn(acc[a][4], scale),
+                                                             __fmul_rn(acc[a][5], scale),
+                                                             __fmul_rn(acc[a][6], scale),
+                                                             __fmul_rn(acc[a][7], scale));
+    } else {
+#pragma unroll
+      for (int b = 0; b < 8; ++b)
+        if (jb + b < n) dst[jb + b] = __fmul_rn(acc[a][b], scale);
+    }
+  }
 }
 
 // ------------------------------------------------------------------------------------------------ top-k
@@ -153,7 +202,8 @@ extern "C" int h3b_tile_scores(const float* qp, const float* kp, int heads, int 
   clear_error();
   H3B_REQUIRE(heads > 0 && n > 0, "tile_scores: heads and n must be positive");
   H3B_REQUIRE(qp && kp && sc, "tile_scores: null pointer");
-  const dim3 grid((n + 15) / 16, (n + 15) / 16, heads);
+  H3B_REQUIRE(aligned(qp, 16) && aligned(kp, 16) && aligned(sc, 16), "tile_scores: 16-byte aligned buffers");
+  const dim3 grid((n + SB - 1) / SB, (n + SB - 1) / SB, heads);
   scores_kernel<<<grid, 256, 0, stream>>>(qp, kp, n, scale, sc);
   H3B_LAUNCH_CHECK("tile_scores");
   return H3B_OK;

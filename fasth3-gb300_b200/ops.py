@@ -221,6 +221,13 @@ def vsa_tile_quant(q, k, v, perm, tile_row0, vbs, qb, kb, vb, qs_blk, ks_blk, vs
          vs_blk.shape[-1], _stream(q))
 
 
+def head_tile_quant(x, s1, tile_row0, vbs, w, xb, xs_blk, xs_head, heads, n_tiles, eps=1e-6) -> None:
+    """One tensor of the prologue's per-tile E4M3 form (cross-attention q, text k and v): optional row scale s1,
+    optional per-head RMSNorm weight w, no RoPE. xb [heads, rows_pad, 128], xs_blk [heads, n_ext]."""
+    call("h3b_head_tile_quant", _p(x), x.stride(0), _p(s1), _p(tile_row0), _p(vbs), _p(w), _p(xb), _p(xs_blk),
+         _p(xs_head), int(heads), xb.shape[-2], int(n_tiles), xs_blk.shape[-1], float(eps), _stream(x))
+
+
 def vsa_fp8(q8, k8, v8, q2k_idx, q2k_num, vbs, qk_coef, v_scale_blk, v_scale_head, lse=None, q_scale_blk=None,
             k_scale_blk=None, out=None):
     """FP8 block-sparse attention over the selected 64-key tiles, the reference op's arguments

@@ -1,0 +1,546 @@
+"""H3FastRunner: the quantized DiT block loop on the h3b kernels, with sequence parallelism.
+
+The reference's runner (fastvideo/models/dits/h3fast/__init__.py:406-553) permutes the packed tokens into compact
+tile order, runs ``resid_norm_quant`` once, then per block: q/k/v GEMMs, ``qkv_prologue8``, tile scores, ``topk_rows``,
+the FP8 VSA kernel, ``attn_gate_quant``, the out-projection, ``resid_norm_quant`` (gated residual + norm2 + modulate
++ quant), fc_in, the activation quantizer, fc_out and the next block's ``resid_norm_quant``. This runner keeps that
+order and the buffers-owned-by-a-layout design, for BASELINE's architecture (which adds cross-attention to text and
+uses GELU-tanh), and differs where the B200 kernels allow more fusion:
+
+* the gated residuals (out-projection, cross-attention output, fc_out) and GELU-tanh are GEMM epilogues
+  (``x <- x + gate * (row_scale * col_scale * acc)``), so no bf16 ``y`` round trip;
+* q/k/v are one GEMM over the block's row-packed q/k/v weights (per-column global scales);
+* Q/K E4M3 scales are per (head, tile) like V's (no per-layer static scales from the norm weights);
+* the token dimension is sharded over ranks by whole tiles (``sp.SeqParallel``); the E4M3 Q/K/V tiles and the tile
+  statistics cross ranks in one head all-to-all before attention and the bf16 attention output in one after
+  (Ulysses-style, the exchange FastVideo's stock SP path makes, patches/fastvideo-a01c50a.patch:12-13). The reference
+  runner itself is single-GPU (patch:644-645).
+
+Every GEMM, norm, quantizer, prologue, selection and attention step is an h3b kernel; torch supplies the buffers,
+the all-to-all (NCCL), the timestep MLP and the token permutation.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+import torch.distributed as dist
+
+from . import ops
+from .layout import TILE, TileLayout, rope_3d, tile_layout
+from .model import DiTModel, QuantLinear
+from .sp import SeqParallel
+
+LOG2E = 1.4426950408889634
+
+
+@dataclass
+class VsaMeta:
+    """The VSA metadata the runner needs (the reference reads FastVideo's VideoSparseAttentionMetadata:
+    video_tile_spans, span_sparsities, num_prefix_tiles, tile_elems; __init__.py:171, 440-445)."""
+    grid: tuple[int, int, int]
+    topk: int = 32
+    tile_elems: int = 64
+    exempt: bool = True
+    pad_tokens: int = 0
+
+
+class VirtualSeqParallel:
+    """``world`` ranks run in one process, one after another per stage, on one GPU: the sharded block's data flow and
+    exchange layouts without a second GPU (tests, and to check that the sharded result equals the single-rank one)."""
+
+    def __init__(self, world: int):
+        self.world = world
+
+    def tiles(self, n_tiles: int, rank: int) -> tuple[int, int]:
+        if n_tiles % (2 * self.world):
+            raise ValueError(f"{n_tiles} tiles do not split into an even count per rank over {self.world} ranks")
+        per = n_tiles // self.world
+        return rank * per, (rank + 1) * per
+
+
+class _Exchange:
+    """The list-of-ranks form of the head all-to-all: one entry per rank this process hosts."""
+
+    def __init__(self, sp):
+        self.sp = sp
+        self.world = sp.world
+        self.virtual = isinstance(sp, VirtualSeqParallel)
+        self.ranks = list(range(sp.world)) if self.virtual else [sp.rank]
+
+    def tiles(self, n_tiles: int, rank: int) -> tuple[int, int]:
+        return self.sp.tiles(n_tiles, rank) if self.virtual else self.sp.tiles(n_tiles)
+
+    def seq_to_heads(self, xs: list[torch.Tensor], outs: list[torch.Tensor]) -> None:
+        """[H, R, ...] per rank -> [P, Hl, R, ...] per rank, written into ``outs``."""
+        P = self.world
+        if not self.virtual:
+            if P == 1:
+                outs[0].copy_(xs[0].view(outs[0].shape)) if outs[0].data_ptr() != xs[0].data_ptr() else None
+                return
+            dist.all_to_all_single(outs[0], xs[0], group=self.sp.group)
+            return
+        Hl = xs[0].shape[0] // P
+        for r in range(P):
+            for p in range(P):
+                outs[r][p].copy_(xs[p][r * Hl:(r + 1) * Hl])
+
+    def heads_to_seq(self, ys: list[torch.Tensor], outs: list[torch.Tensor]) -> None:
+        """[P, Hl, R, ...] per rank -> [H, R, ...] per rank."""
+        P = self.world
+        if not self.virtual:
+            if P == 1:
+                if outs[0].data_ptr() != ys[0].data_ptr():
+                    outs[0].copy_(ys[0].view(outs[0].shape))
+                return
+            dist.all_to_all_single(outs[0], ys[0], group=self.sp.group)
+            return
+        Hl = ys[0].shape[1]
+        for r in range(P):
+            for p in range(P):
+                outs[r][p * Hl:(p + 1) * Hl].copy_(ys[p][r])
+
+    def all_gather_rows(self, xs: list[torch.Tensor], rows: list[int]) -> torch.Tensor:
+        """Concatenation over ranks (in rank order) of each rank's [rows_r, C] block."""
+        if self.virtual:
+            return torch.cat([x[:r] for x, r in zip(xs, rows)])
+        if self.world == 1:
+            return xs[0][:rows[0]]
+        m = max(rows)
+        x = xs[0]
+        buf = torch.empty(m, x.shape[1], device=x.device, dtype=x.dtype)
+        buf[:x.shape[0]].copy_(x)
+        out = torch.empty(self.world * m, x.shape[1], device=x.device, dtype=x.dtype)
+        dist.all_gather_into_tensor(out, buf, group=self.sp.group)
+        return torch.cat([out[p * m:p * m + rows[p]] for p in range(self.world)])
+
+
+@dataclass
+class _RankState:
+    """One rank's shard layout and buffers (the reference's _Layout.buffers, __init__.py:207-252)."""
+    rank: int
+    lay: TileLayout        # this rank's tiles, rows renumbered from 0
+    first: int
+    rows: int
+    rows_pad: int
+    n_local: int
+    tok_index: torch.Tensor  # int64 [rows] global token of each local row
+    b: dict = field(default_factory=dict)
+
+
+def _fused_rows(lins: list[QuantLinear]) -> dict:
+    """The packed operand of several row-packed linears as one GEMM B operand, plus per-column global scales."""
+    fmt = lins[0].fmt
+    if fmt == "nvfp4":
+        ws = [lin._nvfp4_weight for lin in lins]
+        sfs = [lin._nvfp4_weight_scale for lin in lins]
+    else:
+        ws = [lin._fp8_weight for lin in lins]
+        sfs = None
+    adjacent = all(ws[i + 1].data_ptr() == ws[i].data_ptr() + ws[i].numel() * ws[i].element_size()
+                   for i in range(len(ws) - 1)) and all(w.is_contiguous() for w in ws)
+    N = sum(w.shape[0] for w in ws)
+    if adjacent:
+        w = ws[0].as_strided((N, ws[0].shape[1]), ws[0].stride())
+        sf = None if sfs is None else sfs[0].as_strided((N, sfs[0].shape[1]), sfs[0].stride())
+    else:
+        w = torch.cat(ws)
+        sf = None if sfs is None else torch.cat(sfs)
+    if fmt == "nvfp4":
+        col = torch.cat([lin._nvfp4_alpha.float().reshape(1).expand(lin.out_features) for lin in lins]).contiguous()
+    else:
+        col = torch.cat([lin._fp8_weight_scale.float().reshape(-1).expand(lin.out_features) for lin in lins])
+    return {"w": w, "sf": sf, "col": col.contiguous(), "fmt": fmt, "N": N}
+
+
+class H3FastRunner:
+    """All blocks of a DiTModel on the h3b kernels. ``sp``: a SeqParallel (one rank per process; NCCL on GPUs), a
+    VirtualSeqParallel (all ranks in this process), or None (one GPU)."""
+
+    def __init__(self, model: DiTModel, sp: SeqParallel | VirtualSeqParallel | None = None):
+        self.model = model
+        self.blocks = list(model.transformer_blocks)
+        cfg = model.config
+        self.cfg = cfg
+        self.heads, self.head_dim, self.hidden, self.ffn = cfg.heads, cfg.head_dim, cfg.hidden, cfg.ffn
+        if self.head_dim != 128:
+            raise ValueError("head_dim 128 only")
+        self.fp4 = cfg.fmt == "nvfp4"
+        self.ex = _Exchange(sp if sp is not None else SeqParallel())
+        if self.heads % self.ex.world:
+            raise ValueError(f"{self.heads} heads do not split over {self.ex.world} ranks")
+        self.layouts: dict[tuple, list[_RankState]] = {}
+        self.fused = []
+        for blk in self.blocks:
+            a, c = blk.attn, blk.attn2
+            self.fused.append({
+                "qkv": _fused_rows([a.to_q, a.to_k, a.to_v]), "o": _fused_rows([a.to_out]),
+                "cq": _fused_rows([c.to_q]), "ckv": _fused_rows([c.to_k, c.to_v]), "co": _fused_rows([c.to_out]),
+                "fc_in": _fused_rows([blk.ff.fc_in]), "fc_out": _fused_rows([blk.ff.fc_out])})
+        dev = self.blocks[0].scale_shift_table.device
+        self.dev = dev
+        self.ones_c = torch.ones(self.hidden, device=dev, dtype=torch.bfloat16)
+        self.text_cache: dict = {}
+        # trace(block, stage, rank, {name: tensor}) after each stage when set (tests and debugging); the tensors are the
+        # live buffers, so a tracer that keeps them must copy them
+        self.trace = None
+
+    @staticmethod
+    def supported(model: DiTModel, meta: VsaMeta) -> bool:
+        """The reference's gate (__init__.py:164-171): packed FP8 or NVFP4 linears, exempt metadata, 64-token tiles."""
+        blk = model.transformer_blocks[0]
+        lins = (blk.attn.to_q, blk.attn.to_k, blk.attn.to_v, blk.attn.to_out, blk.ff.fc_in, blk.ff.fc_out)
+        fp4 = all(getattr(lin, "_nvfp4_weight", None) is not None for lin in lins)
+        fp8 = all(getattr(lin, "_fp8_weight", None) is not None for lin in lins)
+        return (fp4 or fp8) and meta is not None and meta.exempt and not meta.pad_tokens and meta.tile_elems == 64
+
+    # ------------------------------------------------------------------------------------------------- GEMM
+    def _gemm(self, a, a_sf, fused, out, *, row_scale=None, act=None, residual=None, gate=None, cols=None):
+        w, sf, col = fused["w"], fused["sf"], fused["col"]
+        if cols is not None:
+            w, col = w[cols], col[cols]
+            sf = None if sf is None else sf[cols]
+        if fused["fmt"] == "nvfp4":
+            ops.gemm_nvfp4(a, a_sf, w, sf, out, scale_a=row_scale, scale_b=col, act=act, residual=residual,
+                           gate=gate)
+        else:
+            ops.gemm_fp8(a, w, out, scale_a=row_scale, scale_b=col, act=act, residual=residual, gate=gate)
+
+    # ------------------------------------------------------------------------------------------------- layout
+    def _layouts(self, meta: VsaMeta, rotary) -> tuple[TileLayout, list[_RankState]]:
+        key = (tuple(meta.grid), self.ex.world, tuple(self.ex.ranks))
+        hit = self.layouts.get(key)
+        if hit is not None:
+            return hit
+        P = self.ex.world
+        full = tile_layout(*meta.grid, pad_to=2 * P)
+        if full.n_ext != full.n_tiles:
+            raise ValueError(f"{full.n_tiles} tiles do not split into an even count per rank over {P} ranks")
+        if rotary is None:
+            cos, sin = rope_3d(full)
+        else:
+            cos, sin = (t.reshape(-1, t.shape[-1])[full.perm] for t in rotary)
+        H, D, C, F = self.heads, self.head_dim, self.hidden, self.ffn
+        Hl = H // P
+        n_all = full.n_tiles
+        dev = self.dev
+        u8, bf, f32, i32 = torch.uint8, torch.bfloat16, torch.float32, torch.int32
+        states = []
+        for r in self.ex.ranks:
+            first, last = self.ex.tiles(n_all, r)
+            lay = full.shard(first, last)
+            R, n_local = lay.rows, lay.n_ext
+            rows_pad = n_local * TILE
+            r0 = int(full.tile_row0[first])
+            st = _RankState(r, lay, first, R, rows_pad, n_local, full.perm[r0:r0 + R].to(dev))
+            hb = C // 2 if self.fp4 else C
+            fb = F // 2 if self.fp4 else F
+            b = st.b
+            b["tile_row0"], b["vbs"] = lay.tile_row0.to(dev), lay.vbs.to(dev)
+            b["slot"] = lay.slot.to(dev)
+            b["cos"], b["sin"] = cos[r0:r0 + R].contiguous().to(dev), sin[r0:r0 + R].contiguous().to(dev)
+            b["x"] = torch.empty(R, C, device=dev, dtype=bf)
+            b["h"] = torch.empty(R, hb, device=dev, dtype=u8)
+            b["h_sf"] = torch.zeros(ops.sf_rows(R), C // 16, device=dev, dtype=u8) if self.fp4 else None
+            b["hs"] = torch.empty(R, device=dev, dtype=f32)
+            b["qkv"] = torch.empty(R, 3 * C, device=dev, dtype=bf)
+            for nm in ("qb", "kb", "vb"):
+                b[nm] = torch.zeros(H, rows_pad, D, device=dev, dtype=u8)
+                b[nm + "_x"] = torch.zeros(P, Hl, rows_pad, D, device=dev, dtype=u8) if P > 1 else \
+                    b[nm].view(1, H, rows_pad, D)
+            # per (head, tile) E4M3 scales and tile means, local tiles; their exchange buffers; all tiles
+            for nm, tail in (("qs", ()), ("ks", ()), ("vs", ()), ("qp", (D,)), ("kp", (D,))):
+                b[nm] = torch.zeros(H, n_local, *tail, device=dev, dtype=f32)
+                if P > 1:
+                    b[nm + "_x"] = torch.zeros(P, Hl, n_local, *tail, device=dev, dtype=f32)
+                    b[nm + "_all"] = torch.zeros(Hl, n_all, *tail, device=dev, dtype=f32)
+                else:
+                    b[nm + "_x"] = b[nm].view(1, H, n_local, *tail)
+                    b[nm + "_all"] = b[nm]
+            b["vp"] = torch.empty(H, n_local, D, device=dev, dtype=f32)
+            b["vs_head"] = torch.empty(Hl, device=dev, dtype=f32)
+            b["sc"] = torch.empty(Hl, n_all, n_all, device=dev, dtype=f32)
+            b["idx"] = torch.empty(Hl, n_all, n_all, device=dev, dtype=i32)
+            b["num"] = torch.zeros(Hl, n_all, device=dev, dtype=i32)
+            b["vbs_all"] = full.vbs.to(dev)
+            b["ob"] = torch.zeros(H, rows_pad, D, device=dev, dtype=bf)
+            b["ob_x"] = torch.zeros(P, Hl, rows_pad, D, device=dev, dtype=bf) if P > 1 else \
+                b["ob"].view(1, H, rows_pad, D)
+            b["a"] = torch.empty(R, hb, device=dev, dtype=u8)
+            b["a_sf"] = torch.zeros(ops.sf_rows(R), C // 16, device=dev, dtype=u8) if self.fp4 else None
+            b["as"] = torch.empty(R, device=dev, dtype=f32)
+            # cross-attention: queries of this rank's rows, every head; all text tiles selected
+            b["cq"] = torch.empty(R, C, device=dev, dtype=bf)
+            b["cqb"] = torch.zeros(H, rows_pad, D, device=dev, dtype=u8)
+            b["cqs"] = torch.zeros(H, n_local, device=dev, dtype=f32)
+            b["cob"] = torch.zeros(H, rows_pad, D, device=dev, dtype=bf)
+            n_txt = self.cfg.text_len // TILE
+            b["cidx"] = torch.arange(n_txt, device=dev, dtype=i32).repeat(H, n_local, 1).contiguous()
+            b["cnum"] = torch.full((H, n_local), n_txt, device=dev, dtype=i32)
+            b["u"] = torch.empty(R, F, device=dev, dtype=bf)
+            b["f"] = torch.empty(R, fb, device=dev, dtype=u8)
+            b["f_sf"] = torch.zeros(ops.sf_rows(R), F // 16, device=dev, dtype=u8) if self.fp4 else None
+            b["fs"] = torch.empty(R, device=dev, dtype=f32)
+            states.append(st)
+        self.layouts[key] = (full, states)
+        return full, states
+
+    # ------------------------------------------------------------------------------------------------- text K/V
+    def _text_kv(self, context: torch.Tensor) -> dict:
+        """Per block: E4M3 text keys (RMSNorm) and values [H, L, 128] with per-(head, tile) scales; cached for the
+        last context tensor (the text embedding is fixed over the denoising steps)."""
+        key = (context.data_ptr(), context._version, tuple(context.shape))
+        if self.text_cache.get("key") == key:
+            return self.text_cache
+        cfg = self.cfg
+        L = context.shape[-2]
+        if L % TILE:
+            raise ValueError("text length must be a multiple of 64")
+        ctx = context.reshape(L, -1).contiguous()
+        H, D, C, dev = self.heads, self.head_dim, self.hidden, self.dev
+        n_txt = L // TILE
+        tq = torch.empty(L, ctx.shape[1] // 2 if self.fp4 else ctx.shape[1], device=dev, dtype=torch.uint8)
+        tsf = torch.zeros(ops.sf_rows(L), ctx.shape[1] // 16, device=dev, dtype=torch.uint8) if self.fp4 else None
+        ts = torch.empty(L, device=dev, dtype=torch.float32)
+        if self.fp4:
+            ops.quant_nvfp4_rows(ctx, tq, tsf, ts)
+        else:
+            ops.quant_fp8_rows(ctx, tq.view(ops.FP8), ts)
+        kv = torch.empty(L, 2 * C, device=dev, dtype=torch.bfloat16)
+        row0 = torch.arange(n_txt, device=dev, dtype=torch.int32) * TILE
+        vbs = torch.full((n_txt,), TILE, device=dev, dtype=torch.int32)
+        kb = torch.zeros(len(self.blocks), H, L, D, device=dev, dtype=torch.uint8)
+        vb = torch.zeros_like(kb)
+        ks = torch.zeros(len(self.blocks), H, n_txt, device=dev, dtype=torch.float32)
+        vs = torch.zeros_like(ks)
+        vs_head = torch.zeros(len(self.blocks), H, device=dev, dtype=torch.float32)
+        for i, blk in enumerate(self.blocks):
+            self._gemm(tq if self.fp4 else tq.view(ops.FP8), tsf, self.fused[i]["ckv"], kv)
+            ops.head_tile_quant(kv[:, :C], ts, row0, vbs, blk.attn2.norm_k.weight, kb[i], ks[i], None, H, n_txt,
+                                blk.attn2.norm_k.eps)
+            ops.head_tile_quant(kv[:, C:], ts, row0, vbs, None, vb[i], vs[i], vs_head[i], H, n_txt)
+            if self.trace is not None:
+                self.trace(i, "text", self.ex.ranks[0], {"tq": tq, "tsf": tsf, "ts": ts, "kv": kv, "kb": kb[i],
+                                                          "vb": vb[i], "ks": ks[i], "vs": vs[i]})
+        self.text_cache = {"key": key, "kb": kb, "vb": vb, "ks": ks, "vs": vs, "vs_head": vs_head, "n": n_txt,
+                           "vbs": vbs, "L": L}
+        return self.text_cache
+
+    # ------------------------------------------------------------------------------------------------- forward
+    def forward(self, packed: torch.Tensor, temb: torch.Tensor, adaln_indices: torch.Tensor | None,
+                rotary: tuple[torch.Tensor, torch.Tensor] | None, meta: VsaMeta,
+                context: torch.Tensor | None = None) -> torch.Tensor:
+        """All blocks; ``packed`` [1, S, C] bf16 in token order (the full sequence on every rank), ``temb`` [1, C]
+        timestep embedding, ``adaln_indices`` [S] int (table row per token; None: one row), ``rotary`` (cos, sin)
+        [S, 96] in token order (None: 3D RoPE from meta.grid), ``context`` [1, L, 4096] text. Returns [1, S, C] in
+        token order, identical on every rank (the shards are gathered at the end)."""
+        if context is None:
+            raise ValueError("the cross-attention needs context")
+        full, states = self._layouts(meta, rotary)
+        S = packed.shape[-2]
+        if S != full.rows:
+            raise ValueError(f"packed has {S} tokens, the grid {meta.grid} has {full.rows}")
+        if temb.reshape(-1, self.hidden).shape[0] != 1:
+            raise ValueError("one timestep per forward: the gates are GEMM-epilogue column vectors")
+        if adaln_indices is not None and bool((adaln_indices != 0).any()):
+            raise ValueError("adaln_indices must select table row 0 (one timestep)")
+        tabs = self.model.adaln_tables(temb.reshape(1, -1))  # [blocks, 6, C]
+        txt = self._text_kv(context)
+        x_in = packed.reshape(S, -1)
+        for st in states:
+            torch.index_select(x_in, 0, st.tok_index, out=st.b["x"])
+            st.b["adaln"] = None
+        for st in states:
+            self._norm(st, self.blocks[0].eps, tabs[0, 0:1], tabs[0, 1:2], 0)
+        for i, blk in enumerate(self.blocks):
+            self._block(i, blk, full, states, tabs, txt, meta)
+        out = self.ex.all_gather_rows([st.b["x"] for st in states], [st.rows for st in states])  # global tile order
+        inv = torch.empty_like(full.perm)
+        inv[full.perm] = torch.arange(full.rows)
+        return out.index_select(0, inv.to(out.device)).unsqueeze(0)
+
+    def _norm(self, st: _RankState, eps: float, shift: torch.Tensor, scale: torch.Tensor, i: int,
+              stage: str = "norm1") -> None:
+        b = st.b
+        ops.resid_norm_quant(b["x"], None, None, None, b["adaln"], None, shift, scale, b["x"], b["h"], b["h_sf"],
+                             b["hs"], eps, norm="layer")
+        self._t(i, stage, st, x=b["x"], h=b["h"], h_sf=b["h_sf"], hs=b["hs"])
+
+    def _block(self, i: int, blk, full: TileLayout, states: list[_RankState], tabs: torch.Tensor, txt: dict,
+               meta: VsaMeta) -> None:
+        H, D, C = self.heads, self.head_dim, self.hidden
+        P = self.ex.world
+        Hl = H // P
+        n_all = full.n_tiles
+        fz = self.fused[i]
+        tab = tabs[i]  # [6, C]: shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp
+        sm_scale = 1.0 / math.sqrt(D)
+        # ---- q/k/v GEMM (row scale deferred to the prologue) and the prologue, on each rank's rows
+        for st in states:
+            b = st.b
+            self._gemm(b["h"], b["h_sf"], fz["qkv"], b["qkv"])
+            self._t(i, "qkv", st, qkv=b["qkv"])
+            self._prologue(st, blk)
+            self._t(i, "prologue", st, qb=b["qb"], kb=b["kb"], vb=b["vb"], qs=b["qs"], ks=b["ks"], vs=b["vs"],
+                    qp=b["qp"], kp=b["kp"])
+        # ---- sequence -> heads
+        self.ex.seq_to_heads([st.b["qb"] for st in states], [st.b["qb_x"] for st in states])
+        self.ex.seq_to_heads([st.b["kb"] for st in states], [st.b["kb_x"] for st in states])
+        self.ex.seq_to_heads([st.b["vb"] for st in states], [st.b["vb_x"] for st in states])
+        for nm in ("qs", "ks", "vs", "qp", "kp"):
+            self.ex.seq_to_heads([st.b[nm] for st in states], [st.b[nm + "_x"] for st in states])
+        # ---- coarse step and sparse attention over this rank's heads, every rank's rows
+        for st in states:
+            b = st.b
+            if P > 1:  # [P, Hl, n_local, ...] -> [Hl, n_all, ...] in global tile order
+                for nm in ("qs", "ks", "vs", "qp", "kp"):
+                    src = b[nm + "_x"]
+                    b[nm + "_all"].copy_(src.transpose(0, 1).reshape(b[nm + "_all"].shape))
+            torch.amax(b["vs_all"], dim=1, out=b["vs_head"])
+            ops.tile_scores(b["qp_all"], b["kp_all"], b["sc"], sm_scale)
+            k = min(meta.topk, n_all)
+            ops.topk_rows(b["sc"], n_all, n_all, 0, [0], [n_all], [k], b["idx"], b["num"], False)
+            self._t(i, "select", st, qb_x=b["qb_x"], kb_x=b["kb_x"], vb_x=b["vb_x"], qs_all=b["qs_all"],
+                    ks_all=b["ks_all"], vs_all=b["vs_all"], qp_all=b["qp_all"], kp_all=b["kp_all"],
+                    vs_head=b["vs_head"], sc=b["sc"], idx=b["idx"], num=b["num"])
+            ops.vsa_fp8_ex(b["qb_x"], b["kb_x"], b["vb_x"], b["ob_x"], b["idx"], b["num"], b["vbs_all"],
+                           b["vbs_all"], b["vs_all"], b["vs_head"], sm_scale * LOG2E, Hl, n_all, n_all, st.rows_pad,
+                           st.rows_pad, chunks_q=P, chunks_kv=P, qs=b["qs_all"], ks=b["ks_all"], idx_ld=n_all,
+                           q_scale_ld=n_all, kv_scale_ld=n_all)
+            self._t(i, "attn", st, ob_x=b["ob_x"])
+        # ---- heads -> sequence
+        self.ex.heads_to_seq([st.b["ob_x"] for st in states], [st.b["ob"] for st in states])
+        for st in states:
+            b = st.b
+            R = st.rows
+            # attention output -> compact rows, quantized; out-projection with the gated residual in the epilogue
+            ops.attn_gate_quant(b["ob"], None, None, None, b["slot"], st.n_local, TILE, self._q(b["a"]),
+                                b["a_sf"], b["as"], R)
+            self._t(i, "gate", st, ob=b["ob"], a=b["a"], a_sf=b["a_sf"], sa=b["as"])
+            self._gemm(self._q(b["a"]), b["a_sf"], fz["o"], b["x"], row_scale=b["as"], residual=b["x"],
+                       gate=tab[2])
+            self._t(i, "out_proj", st, x=b["x"])
+            # cross-attention: norm3 (affine LayerNorm as a table), q GEMM, per-tile E4M3 q, attention to the text
+            ops.resid_norm_quant(b["x"], None, None, None, None, None, blk.norm3.shift, blk.norm3.scale, b["x"],
+                                 self._q(b["h"]), b["h_sf"], b["hs"], blk.norm3.eps, norm="layer")
+            self._t(i, "norm3", st, h=b["h"], h_sf=b["h_sf"], hs=b["hs"])
+            self._gemm(self._q(b["h"]), b["h_sf"], fz["cq"], b["cq"])
+            ops.head_tile_quant(b["cq"], b["hs"], b["tile_row0"], b["vbs"], blk.attn2.norm_q.weight, b["cqb"],
+                                b["cqs"], None, H, st.n_local, blk.attn2.norm_q.eps)
+            self._t(i, "cross_q", st, cq=b["cq"], cqb=b["cqb"], cqs=b["cqs"])
+            ops.vsa_fp8_ex(b["cqb"], txt["kb"][i], txt["vb"][i], b["cob"], b["cidx"], b["cnum"], b["vbs"],
+                           txt["vbs"], txt["vs"][i], txt["vs_head"][i], sm_scale * LOG2E, H, st.n_local, txt["n"],
+                           st.rows_pad, txt["L"], qs=b["cqs"], ks=txt["ks"][i], idx_ld=txt["n"],
+                           q_scale_ld=st.n_local, kv_scale_ld=txt["n"])
+            ops.attn_gate_quant(b["cob"], None, None, None, b["slot"], st.n_local, TILE, self._q(b["a"]),
+                                b["a_sf"], b["as"], R)
+            self._t(i, "cross_attn", st, cob=b["cob"], a=b["a"], a_sf=b["a_sf"], sa=b["as"])
+            self._gemm(self._q(b["a"]), b["a_sf"], fz["co"], b["x"], row_scale=b["as"], residual=b["x"],
+                       gate=self.ones_c)
+            self._t(i, "cross_out", st, x=b["x"])
+            # FFN: norm2 + modulate + quant, fc_in with GELU-tanh, row quant, fc_out with the gated residual
+            self._norm(st, blk.eps, tab[3:4], tab[4:5], i, "norm2")
+            self._gemm(self._q(b["h"]), b["h_sf"], fz["fc_in"], b["u"], row_scale=b["hs"], act="gelu_tanh")
+            if self.fp4:
+                ops.quant_nvfp4_rows(b["u"], b["f"], b["f_sf"], b["fs"])
+            else:
+                ops.quant_fp8_rows(b["u"], b["f"].view(ops.FP8), b["fs"])
+            self._t(i, "ffn_mid", st, u=b["u"], f=b["f"], f_sf=b["f_sf"], fs=b["fs"])
+            self._gemm(self._q(b["f"]), b["f_sf"], fz["fc_out"], b["x"], row_scale=b["fs"], residual=b["x"],
+                       gate=tab[5])
+            self._t(i, "fc_out", st, x=b["x"])
+            # the next block's norm1 + modulate + quant
+            if i + 1 < len(self.blocks):
+                self._norm(st, self.blocks[i + 1].eps, tabs[i + 1, 0:1], tabs[i + 1, 1:2], i + 1)
+
+    def _t(self, i: int, stage: str, st: _RankState, **tensors) -> None:
+        if self.trace is not None:
+            self.trace(i, stage, st.rank, tensors)
+
+    def _q(self, t: torch.Tensor) -> torch.Tensor:
+        return t if self.fp4 else t.view(ops.FP8)
+
+    def _prologue(self, st: _RankState, blk) -> None:
+        b = st.b
+        C = self.hidden
+        qkv = b["qkv"]
+        ops.qkv_prologue8(qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:], b["hs"], b["tile_row0"], b["vbs"],
+                          blk.attn.norm_q.weight, blk.attn.norm_k.weight, b["cos"], b["sin"], 1.0, 1.0, b["qb"],
+                          b["kb"], b["vb"], b["vs"], None, b["qp"], b["kp"], b["vp"], self.heads, st.n_local, TILE,
+                          blk.attn.norm_q.eps, qs_blk=b["qs"], ks_blk=b["ks"])
+
+
+class Fp8BlockChain:
+    """the FP8 DiT block MLP/projection chain without attention, on the same kernels as the block
+    loop. LayerNorm (no affine) + modulate + per-token FP8 -> QKV 5120->15360 -> per-token FP8 of the V third ->
+    out-projection 5120->5120 with the gated residual -> LayerNorm + modulate + FP8 -> fc_in 5120->13824 with GELU-tanh
+    -> per-token FP8 -> fc_out 13824->5120 with the gated residual. Weights FP8 per output channel."""
+
+    def __init__(self, qkv: list[QuantLinear], o: QuantLinear, fc_in: QuantLinear, fc_out: QuantLinear,
+                 eps: float = 1e-6):
+        self.qkv, self.o = _fused_rows(qkv), _fused_rows([o])
+        self.fc_in, self.fc_out = _fused_rows([fc_in]), _fused_rows([fc_out])
+        self.eps = eps
+        self.C = o.out_features
+        self.F = fc_in.out_features
+        self.bufs: dict = {}
+        self.trace = None
+
+    @staticmethod
+    def random(device="cuda", seed: int = 0, hidden: int = 5120, ffn: int = 13824) -> "Fp8BlockChain":
+        g = torch.Generator(device=device)
+
+        def randn(*shape, s):
+            g.manual_seed(seed * 1_000_003 + s)
+            return (torch.randn(*shape, device=device, generator=g) * 0.02).bfloat16()
+
+        qkv = QuantLinear.pack_rows([randn(hidden, hidden, s=j) for j in range(3)], "fp8")
+        (o,) = QuantLinear.pack_rows([randn(hidden, hidden, s=3)], "fp8")
+        (f1,) = QuantLinear.pack_rows([randn(ffn, hidden, s=4)], "fp8")
+        (f2,) = QuantLinear.pack_rows([randn(hidden, ffn, s=5)], "fp8")
+        return Fp8BlockChain(qkv, o, f1, f2)
+
+    def flop(self, rows: int) -> float:
+        C, F = self.C, self.F
+        return 2.0 * rows * (3 * C * C + C * C + 2 * C * F)
+
+    def _buffers(self, rows: int, dev) -> dict:
+        b = self.bufs.get(rows)
+        if b is None:
+            C, F = self.C, self.F
+            b = self.bufs[rows] = {
+                "h": torch.empty(rows, C, device=dev, dtype=ops.FP8), "hs": torch.empty(rows, device=dev),
+                "qkv": torch.empty(rows, 3 * C, device=dev, dtype=torch.bfloat16),
+                "a": torch.empty(rows, C, device=dev, dtype=ops.FP8), "as": torch.empty(rows, device=dev),
+                "u": torch.empty(rows, F, device=dev, dtype=torch.bfloat16),
+                "f": torch.empty(rows, F, device=dev, dtype=ops.FP8), "fs": torch.empty(rows, device=dev)}
+        return b
+
+    def _t(self, stage, **tensors):
+        if self.trace is not None:
+            self.trace(stage, tensors)
+
+    def __call__(self, x: torch.Tensor, tabs: torch.Tensor) -> torch.Tensor:
+        """x bf16 [rows, 5120] updated in place; tabs bf16 [6, 5120] = shift, scale, gate (attention half), shift,
+        scale, gate (MLP half)."""
+        rows, C = x.shape
+        b = self._buffers(rows, x.device)
+        ops.resid_norm_quant(x, None, None, None, None, None, tabs[0:1], tabs[1:2], x, b["h"], None, b["hs"],
+                             self.eps, norm="layer")
+        self._t("norm1", x=x, h=b["h"], hs=b["hs"])
+        ops.gemm_fp8(b["h"], self.qkv["w"], b["qkv"], scale_a=b["hs"], scale_b=self.qkv["col"])
+        ops.quant_fp8_rows(b["qkv"][:, 2 * C:], b["a"], b["as"])
+        self._t("qkv", qkv=b["qkv"], a=b["a"], sa=b["as"])
+        ops.gemm_fp8(b["a"], self.o["w"], x, scale_a=b["as"], scale_b=self.o["col"], residual=x, gate=tabs[2])
+        self._t("out_proj", x=x)
+        ops.resid_norm_quant(x, None, None, None, None, None, tabs[3:4], tabs[4:5], x, b["h"], None, b["hs"],
+                             self.eps, norm="layer")
+        self._t("norm2", h=b["h"], hs=b["hs"])
+        ops.gemm_fp8(b["h"], self.fc_in["w"], b["u"], scale_a=b["hs"], scale_b=self.fc_in["col"], act="gelu_tanh")
+        ops.quant_fp8_rows(b["u"], b["f"], b["fs"])
+        self._t("ffn_mid", u=b["u"], f=b["f"], fs=b["fs"])
+        ops.gemm_fp8(b["f"], self.fc_out["w"], x, scale_a=b["fs"], scale_b=self.fc_out["col"], residual=x,
+                     gate=tabs[5])
+        self._t("fc_out", x=x)
+        return x

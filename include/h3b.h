@@ -178,6 +178,15 @@ int h3b_vsa_tile_quant(const void* q, const void* k, const void* v, int heads, i
                        float* ks_blk, float* vs_blk, float* vs_head, float* qp, float* kp, float* vp, int64_t rows_pad,
                        int n_tiles, int n_ext, cudaStream_t stream);
 
+/* One tensor of h3b_qkv_prologue8's per-tile E4M3 form (no reference counterpart; the cross-attention queries, text
+ * keys and text values of the DiT block): x bf16 rows [rows, heads*128] with row stride ld in tile order; optional
+ * deferred row scale s1 [rows]; optional per-head RMSNorm weight w bf16 [128] (NULL: no norm); no RoPE. Writes xb e4m3
+ * [heads, rows_pad, 128], xs_blk [heads, n_ext] = max(amax/448, 1e-30) per (head, tile), and folds the per-head
+ * maximum into xs_head [heads] with an atomic max (caller zeroes; may be NULL). */
+int h3b_head_tile_quant(const void* x, int64_t ld, const float* s1, const int32_t* tile_row0, const int32_t* vbs,
+                        const void* w, void* xb, float* xs_blk, float* xs_head, int heads, int64_t rows_pad,
+                        int n_tiles, int n_ext, float eps, cudaStream_t stream);
+
 /* FP8 block-sparse VSA attention, fine step (replaces vsa_fp8_op, fastvideo/models/dits/h3fast/h3attn8.cu:1-42 and
  * vsa_fp8.cuh:782-871). qb/kb/vb e4m3 [heads, rows_pad, 128] (rows_pad = n_ext*64, tile order);
  * idx/num from h3b_topk_rows ([heads, n_ext, n], [heads, n_ext], padding tiles num 0); vbs [n_ext] valid rows per

@@ -67,10 +67,14 @@ def sf_atom_offset(row, col, sf_cols):
             + (col & 3))
 
 
-def _ambiguous(u: np.ndarray, encode) -> np.ndarray:
+def _ambiguous(u: np.ndarray, encode, mag: np.ndarray | None = None) -> np.ndarray:
+    """Codes that a relative error of DELTA could flip. ``mag`` (same shape as u, in u's units) is the magnitude the
+    error is relative to when u comes out of a cancellation (x * (1 + scale) + shift near zero): the window is then
+    DELTA * (|u| + mag) instead of DELTA * |u|."""
     u = np.asarray(u, dtype=np.float64)
-    lo = encode((u * (1 - DELTA)).astype(np.float32))
-    hi = encode((u * (1 + DELTA)).astype(np.float32))
+    err = np.abs(u) * DELTA if mag is None else (np.abs(u) + np.abs(np.asarray(mag, dtype=np.float64))) * DELTA
+    lo = encode((u - err).astype(np.float32))
+    hi = encode((u + err).astype(np.float32))
     return lo != hi
 
 
@@ -115,18 +119,21 @@ def block_sum_sq(v: np.ndarray) -> np.ndarray:
     return butterfly_sum(stage)
 
 
-def fp8_rows_from_values(v: np.ndarray):
-    """FP8 row quantization of float32 rows (h3fast.cu:256-262): returns (codes, scale, ambiguity)."""
+def fp8_rows_from_values(v: np.ndarray, mag: np.ndarray | None = None):
+    """FP8 row quantization of float32 rows (h3fast.cu:256-262): returns (codes, scale, ambiguity). ``mag``: the
+    pre-cancellation magnitude of v for the ambiguity window (see _ambiguous)."""
     am = np.abs(v).max(axis=1).astype(np.float32)
     s = np.maximum((am / FP8_MAX).astype(np.float32), FP8_MIN_SCALE).astype(np.float32)
     inv = (np.float32(1.0) / s).astype(np.float32)
     u = (v * inv[:, None]).astype(np.float32)
-    return e4m3_encode(u), s, _ambiguous(u, e4m3_encode)
+    m = None if mag is None else np.abs(mag) * inv[:, None]
+    return e4m3_encode(u), s, _ambiguous(u, e4m3_encode, m)
 
 
-def nvfp4_blocks(v: np.ndarray, gs: np.ndarray):
+def nvfp4_blocks(v: np.ndarray, gs: np.ndarray, mag: np.ndarray | None = None):
     """NVFP4 block math of h3fast.cu:99-119 for rows ``v`` [rows, K] with global factor ``gs`` [rows] (row mode) or
-    scalar (tensor mode). Returns (codes [rows, K] 0..15, sf bytes [rows, K/16], nibble ambiguity, sf ambiguity)."""
+    scalar (tensor mode). Returns (codes [rows, K] 0..15, sf bytes [rows, K/16], nibble ambiguity, sf ambiguity).
+    ``mag``: the pre-cancellation magnitude of v for the ambiguity window (see _ambiguous)."""
     rows, K = v.shape
     gs = np.broadcast_to(np.asarray(gs, dtype=np.float32).reshape(-1, 1), (rows, 1)).astype(np.float32)
     blk = v.reshape(rows, K // 16, 16).astype(np.float32)
@@ -139,7 +146,8 @@ def nvfp4_blocks(v: np.ndarray, gs: np.ndarray):
         m = np.where((vmax != 0) & (sf != 0), (gs / sf).astype(np.float32), np.float32(0)).astype(np.float32)
     u = (blk * m[:, :, None]).astype(np.float32)
     codes = e2m1_encode(u)
-    amb = _ambiguous(u, e2m1_encode) | sf_amb[:, :, None]
+    mu = None if mag is None else np.abs(np.asarray(mag, dtype=np.float32).reshape(rows, K // 16, 16)) * m[:, :, None]
+    amb = _ambiguous(u, e2m1_encode, mu) | sf_amb[:, :, None]
     return codes.reshape(rows, K), bits, amb.reshape(rows, K), sf_amb
 
 
@@ -215,15 +223,16 @@ def resid_norm_quant(x, y=None, sy=None, gate=None, idx=None, nw=None, shift=Non
     else:
         raise ValueError(norm)
     out["m"] = m
+    mag = np.abs(p.astype(np.float64) * one_sc).astype(np.float32)  # the shift can cancel the normalized term
     if fp4:
         am = np.abs(m).max(axis=1).astype(np.float32)
         s = np.maximum((am / FP4_RANGE).astype(np.float32), FP4_MIN_SCALE).astype(np.float32)
         gs = (np.float32(1.0) / s).astype(np.float32)
-        codes, bits, amb, sf_amb = nvfp4_blocks(m, gs)
+        codes, bits, amb, sf_amb = nvfp4_blocks(m, gs, mag)
         out.update(h=pack_nibbles(codes), codes=codes, hs=s, hsf=swizzle_sf(bits), sf_bits=bits, amb=amb,
                    sf_amb=sf_amb)
     else:
-        codes, s, amb = fp8_rows_from_values(m)
+        codes, s, amb = fp8_rows_from_values(m, mag)
         out.update(h=codes, hs=s, amb=amb)
     return out
 

@@ -1,0 +1,344 @@
+"""The composed DiT block loop (H3FastRunner) on the GPU.
+
+1. Sequence parallelism is exact: the block loop sharded over P ranks (emulated in one process, the same stages, buffers
+   and all-to-all layouts as the NCCL path) gives bit-identical output to one rank, for P = 2 and 4, with full and
+   48-row tiles. Every step is row-, tile- or (head, tile)-local, so nothing may change.
+2. Each stage of a block is checked against the oracle on the stage's own GPU inputs (teacher forcing): quantized bytes
+   against the restated quantizers (codes within the oracle's ambiguity windows), GEMMs against dequantize-then-matmul
+   in fp32, tile scores and top-k selection bit-exact, FP8 attention within rel-Frobenius 2e-2 of exact attention over
+   the same quantized operands.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import quant as oq
+from oracle import vsa as ov
+from test_oracle import assert_codes
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def rel(a: torch.Tensor, b: torch.Tensor) -> float:
+    a, b = a.double(), b.double()
+    return float((a - b).norm() / b.norm().clamp_min(1e-30))
+
+
+def deq_nvfp4(q: torch.Tensor, sf: torch.Tensor, rows: int, K: int) -> torch.Tensor:
+    """NVFP4 codes x block scales (no global scale) -> fp32 [rows, K], plain torch on the GPU (test-side only)."""
+    lut = torch.tensor(oq.E2M1_VALUES, device=q.device)
+    codes = torch.stack([q[:rows] & 15, q[:rows] >> 4], -1).reshape(rows, K)
+    vals = lut[codes.long()].view(rows, K // 16, 16)
+    r = torch.arange(rows, device=q.device)[:, None]
+    c = torch.arange(K // 16, device=q.device)[None, :]
+    off = (r >> 7) * (K // 64) * 512 + (c >> 2) * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4 + (c & 3)
+    s = sf.reshape(-1)[off].view(torch.float8_e4m3fn).float()
+    return (vals * s[..., None]).reshape(rows, K)
+
+
+def weight_fp32(fused: dict) -> torch.Tensor:
+    """Dense fp32 [N, K] of a fused packed operand, global scales applied per column."""
+    w = fused["w"]
+    if fused["fmt"] == "nvfp4":
+        d = deq_nvfp4(w, fused["sf"], w.shape[0], w.shape[1] * 2)
+    else:
+        d = w.float()
+    return d * fused["col"][:, None]
+
+
+def codes_of(h: torch.Tensor, K: int) -> np.ndarray:
+    q = h.cpu().numpy()
+    return np.stack([q & 15, q >> 4], -1).reshape(q.shape[0], K)
+
+
+@pytest.fixture(scope="module")
+def pkg(h3b):
+    from fasth3_b200 import model, runner
+    return model, runner
+
+
+def make(pkg, blocks, fmt="nvfp4", grid=(7, 16, 16), seed=0):
+    model, runner = pkg
+    cfg = model.DiTConfig(blocks=blocks, fmt=fmt)
+    m = model.DiTModel.random(cfg, device=DEV, seed=seed)
+    T, Hh, Ww = grid
+    g = torch.Generator(device=DEV).manual_seed(1000 + seed)
+    x = torch.randn(1, T * Hh * Ww, cfg.hidden, device=DEV, generator=g).bfloat16()
+    ctx = torch.randn(1, cfg.text_len, cfg.text_dim, device=DEV, generator=g).bfloat16()
+    temb = m.timestep_embedding(0.5)
+    meta = runner.VsaMeta(grid=grid, topk=8)
+    return m, x, ctx, temb, meta
+
+
+@pytest.mark.parametrize("grid", [(8, 16, 16), (7, 16, 16)])
+def test_sharded_block_loop_equals_single_rank(pkg, grid):
+    _, runner = pkg
+    m, x, ctx, temb, meta = make(pkg, blocks=2, grid=grid)
+    ref = runner.H3FastRunner(m).forward(x, temb, None, None, meta, context=ctx)
+    torch.cuda.synchronize()
+    assert torch.isfinite(ref.float()).all()
+    assert rel(ref.float(), x.float()) > 1e-2  # the blocks did change the stream
+    for P in (2, 4):
+        got = runner.H3FastRunner(m, runner.VirtualSeqParallel(P)).forward(x, temb, None, None, meta, context=ctx)
+        torch.cuda.synchronize()
+        assert torch.equal(got.view(torch.int16), ref.view(torch.int16)), P
+
+
+def test_fp8_block_loop_runs_and_shards_exactly(pkg):
+    _, runner = pkg
+    m, x, ctx, temb, meta = make(pkg, blocks=1, fmt="fp8", grid=(8, 16, 16))
+    ref = runner.H3FastRunner(m).forward(x, temb, None, None, meta, context=ctx)
+    got = runner.H3FastRunner(m, runner.VirtualSeqParallel(2)).forward(x, temb, None, None, meta, context=ctx)
+    torch.cuda.synchronize()
+    assert torch.isfinite(ref.float()).all()
+    assert torch.equal(got.view(torch.int16), ref.view(torch.int16))
+
+
+# ------------------------------------------------------------------------------------------------ stage parity
+@pytest.fixture(scope="module")
+def traced(pkg):
+    _, runner = pkg
+    m, x, ctx, temb, meta = make(pkg, blocks=1, grid=(7, 16, 16), seed=3)
+    r = runner.H3FastRunner(m)
+    rec = {}
+
+    def trace(i, stage, rank, tensors):
+        rec[(i, stage)] = {k: (v.clone() if v is not None else None) for k, v in tensors.items()}
+
+    r.trace = trace
+    out = r.forward(x, temb, None, None, meta, context=ctx)
+    torch.cuda.synchronize()
+    full, states = r._layouts(meta, None)
+    return {"rec": rec, "runner": r, "model": m, "tabs": m.adaln_tables(temb), "st": states[0], "full": full,
+            "out": out, "ctx": ctx}
+
+
+def _check_norm_fp4(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, h, h_sf, hs, eps, what):
+    want = oq.resid_norm_quant(x.float().cpu().numpy(), shift=shift.float().cpu().numpy(),
+                               scale=scale.float().cpu().numpy(), eps=eps, norm="layer", fp4=True)
+    C = x.shape[1]
+    assert_codes(codes_of(h, C), want["codes"], want["amb"], what)
+    np.testing.assert_allclose(hs.cpu().numpy(), want["hs"], rtol=1e-6, err_msg=what)
+
+
+def test_stage_norms(traced):
+    rec, tabs, blk = traced["rec"], traced["tabs"], traced["model"].transformer_blocks[0]
+    n1 = rec[(0, "norm1")]
+    _check_norm_fp4(n1["x"], tabs[0, 0:1], tabs[0, 1:2], n1["h"], n1["h_sf"], n1["hs"], blk.eps, "norm1")
+    n3 = rec[(0, "norm3")]
+    _check_norm_fp4(rec[(0, "out_proj")]["x"], blk.norm3.shift, blk.norm3.scale, n3["h"], n3["h_sf"], n3["hs"],
+                    blk.norm3.eps, "norm3")
+    n2 = rec[(0, "norm2")]
+    _check_norm_fp4(rec[(0, "cross_out")]["x"], tabs[0, 3:4], tabs[0, 4:5], n2["h"], n2["h_sf"], n2["hs"], blk.eps,
+                    "norm2")
+
+
+def upd_tol(x: torch.Tensor, upd: torch.Tensor) -> float:
+    """Tolerance on a residual update read back as (x_new - x_old): 1e-2 plus the bf16 rounding of x_new (RMS relative
+    error 2^-9/sqrt(3) of |x_new|) measured against |update|."""
+    return 1e-2 + 2 * 1.2e-3 * float(x.norm() / upd.norm())
+
+
+def test_stage_gemms(traced):
+    rec, r, st, tabs = traced["rec"], traced["runner"], traced["st"], traced["tabs"]
+    fz = r.fused[0]
+    R, C, F = st.rows, r.hidden, r.ffn
+
+    def a_of(stage, name="h", sf="h_sf"):
+        return deq_nvfp4(rec[stage][name], rec[stage][sf], R, rec[stage][name].shape[1] * 2)
+
+    # q/k/v: row scale deferred to the prologue
+    want = a_of((0, "norm1")) @ weight_fp32(fz["qkv"]).t()
+    assert rel(rec[(0, "qkv")]["qkv"].float(), want) < 3e-3
+    # out-projection, gated residual in the epilogue
+    g = rec[(0, "gate")]
+    upd = tabs[0, 2].float() * (g["sa"][:, None] * (a_of((0, "gate"), "a", "a_sf") @ weight_fp32(fz["o"]).t()))
+    x0 = rec[(0, "norm1")]["x"].float()
+    x1 = rec[(0, "out_proj")]["x"].float()
+    assert rel(x1, (x0 + upd).bfloat16().float()) < 1e-3
+    assert rel(x1 - x0, upd) < upd_tol(x1, upd)
+    # cross-attention query
+    want = a_of((0, "norm3")) @ weight_fp32(fz["cq"]).t()
+    assert rel(rec[(0, "cross_q")]["cq"].float(), want) < 3e-3
+    # cross-attention output projection (ungated residual)
+    ca = rec[(0, "cross_attn")]
+    upd = ca["sa"][:, None] * (a_of((0, "cross_attn"), "a", "a_sf") @ weight_fp32(fz["co"]).t())
+    x2 = rec[(0, "cross_out")]["x"].float()
+    assert rel(x2, (x1 + upd).bfloat16().float()) < 1e-3
+    # fc_in with GELU-tanh, then fc_out with the gated residual
+    n2 = rec[(0, "norm2")]
+    pre = n2["hs"][:, None] * (a_of((0, "norm2")) @ weight_fp32(fz["fc_in"]).t())
+    want = torch.nn.functional.gelu(pre, approximate="tanh")
+    mid = rec[(0, "ffn_mid")]
+    assert rel(mid["u"].float(), want) < 3e-3
+    upd = tabs[0, 5].float() * (mid["fs"][:, None] * (deq_nvfp4(mid["f"], mid["f_sf"], R, F) @
+                                                      weight_fp32(fz["fc_out"]).t()))
+    x3 = rec[(0, "fc_out")]["x"].float()
+    assert rel(x3, (x2 + upd).bfloat16().float()) < 1e-3
+    assert rel(x3 - x2, upd) < upd_tol(x3, upd)
+
+
+def test_stage_ffn_requant(traced):
+    mid = traced["rec"][(0, "ffn_mid")]
+    u = mid["u"].float().cpu().numpy()
+    am = np.abs(u).max(axis=1).astype(np.float32)
+    s = np.maximum((am / oq.FP4_RANGE).astype(np.float32), oq.FP4_MIN_SCALE).astype(np.float32)
+    codes, bits, amb, sf_amb = oq.nvfp4_blocks(u, (np.float32(1.0) / s).astype(np.float32))
+    assert_codes(codes_of(mid["f"], u.shape[1]), codes, amb, "ffn requant")
+    np.testing.assert_allclose(mid["fs"].cpu().numpy(), s, rtol=1e-6)
+
+
+def test_stage_prologue_and_selection(traced):
+    rec, r, st, blk = traced["rec"], traced["runner"], traced["st"], traced["model"].transformer_blocks[0]
+    H, C = r.heads, r.hidden
+    b = st.b
+    qkv = rec[(0, "qkv")]["qkv"].float().cpu().numpy()
+    hs = rec[(0, "norm1")]["hs"].cpu().numpy()
+    f = lambda t: t.float().cpu().numpy()  # noqa: E731
+    want = ov.qkv_prologue8(qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:], hs, b["tile_row0"].cpu().numpy(),
+                            b["vbs"].cpu().numpy(), f(blk.attn.norm_q.weight), f(blk.attn.norm_k.weight), f(b["cos"]),
+                            f(b["sin"]), H, 1.0, 1.0, eps=blk.attn.norm_q.eps)
+    p = rec[(0, "prologue")]
+    vbs = b["vbs"].cpu().numpy()
+    row0 = b["tile_row0"].cpu().numpy()
+    for name, vals, sname in (("qb", want["q"], "qs"), ("kb", want["k"], "ks"), ("vb", want["v"], "vs")):
+        got_s = p[sname].cpu().numpy()
+        got_b = p[name].cpu().numpy()
+        ok = total = 0
+        for t in range(st.n_local):
+            rows = vals[row0[t]:row0[t] + vbs[t]]  # [n, H, 128]
+            am = np.abs(rows).max(axis=(0, 2)).astype(np.float32)
+            np.testing.assert_allclose(got_s[:, t], np.maximum(am / 448.0, 1e-30), rtol=1e-2, err_msg=name)
+            for h in range(H):
+                w = oq.e4m3_decode(oq.e4m3_encode(rows[:, h] / got_s[h, t]))
+                g = oq.e4m3_decode(got_b[h, t * 64:t * 64 + vbs[t]])
+                close = np.abs(g - w) <= np.maximum(np.abs(w), 2 ** -6) * 0.126
+                ok += int(close.sum())
+                total += close.size
+        assert ok / total > 0.999, (name, ok / total)
+    # tile means of the bf16 values
+    for name, vals in (("qp", want["q"]), ("kp", want["k"])):
+        got = p[name].cpu().numpy()
+        for t in range(st.n_local):
+            m = vals[row0[t]:row0[t] + vbs[t]].mean(axis=0)  # [H, 128]
+            np.testing.assert_allclose(got[:, t], m, rtol=5e-2, atol=2e-2, err_msg=name)
+    # scores bit-exact, selection bit-exact (ties to the lowest column)
+    s = rec[(0, "select")]
+    n = st.n_local
+    sc = ov.tile_scores(s["qp_all"].cpu().numpy(), s["kp_all"].cpu().numpy(), 1.0 / math.sqrt(128))
+    np.testing.assert_array_equal(s["sc"].cpu().numpy(), sc)
+    idx, num = ov.topk_rows(sc, n, n, 0, [(0, n, 8)], False)
+    num_g = s["num"].cpu().numpy()
+    np.testing.assert_array_equal(num_g, num)
+    idx_g = s["idx"].cpu().numpy()
+    for h in range(H):
+        for t in range(n):
+            np.testing.assert_array_equal(idx_g[h, t, :num[h, t]], idx[h, t, :num[h, t]])
+    np.testing.assert_array_equal(s["vs_head"].cpu().numpy(), s["vs_all"].cpu().numpy().max(axis=1))
+
+
+def _deq_tiles(codes: torch.Tensor, scales: torch.Tensor) -> np.ndarray:
+    """E4M3 [H, n*64, 128] with per-(head, tile) scales [H, n] -> float32."""
+    H, rows_pad, D = codes.shape
+    v = oq.e4m3_decode(codes.cpu().numpy()).reshape(H, rows_pad // 64, 64, D)
+    return (v * scales.cpu().numpy()[:, :, None, None]).reshape(H, rows_pad, D)
+
+
+def test_stage_self_attention(traced):
+    rec, st = traced["rec"], traced["st"]
+    s, a = rec[(0, "select")], rec[(0, "attn")]
+    q = _deq_tiles(s["qb_x"][0], s["qs_all"])
+    k = _deq_tiles(s["kb_x"][0], s["ks_all"])
+    v = _deq_tiles(s["vb_x"][0], s["vs_all"])
+    vbs = st.b["vbs"].cpu().numpy()
+    want = ov.vsa_fine(q, k, v, s["idx"].cpu().numpy(), s["num"].cpu().numpy(), vbs, 1.0 / math.sqrt(128))
+    got = a["ob_x"][0].float().cpu().numpy()
+    mask = (np.arange(got.shape[1]) % 64)[None, :] < np.repeat(vbs, 64)[None, :]
+    g, w = got[:, mask[0]], want[:, mask[0]]
+    err = np.linalg.norm(g - w) / np.linalg.norm(w)
+    assert err < 2e-2, err
+    # attention output -> compact rows, NVFP4 row quantization
+    gt = rec[(0, "gate")]
+    ref = ov.attn_gate_quant(gt["ob"].float().cpu().numpy(), st.b["slot"].cpu().numpy(), st.rows, fp4=True)
+    assert_codes(codes_of(gt["a"], ref["codes"].shape[1]), ref["codes"], ref["amb"], "attn out quant")
+    np.testing.assert_allclose(gt["sa"].cpu().numpy(), ref["s"], rtol=1e-6)
+
+
+def test_stage_cross_attention(traced):
+    rec, r, st, blk = traced["rec"], traced["runner"], traced["st"], traced["model"].transformer_blocks[0]
+    H, C = r.heads, r.hidden
+    txt = rec[(0, "text")]
+    fz = r.fused[0]
+    L = txt["kv"].shape[0]
+    # text K/V projection (row scale deferred), per-head RMSNorm for K, per-tile E4M3
+    a = deq_nvfp4(txt["tq"], txt["tsf"], L, txt["tq"].shape[1] * 2)
+    want = a @ weight_fp32(fz["ckv"]).t()
+    assert rel(txt["kv"].float(), want) < 3e-3
+    kv = txt["kv"].float() * txt["ts"][:, None]
+    kf = kv[:, :C].view(L, H, 128)
+    kf = kf * torch.rsqrt(kf.pow(2).mean(-1, keepdim=True) + blk.attn2.norm_k.eps) * blk.attn2.norm_k.weight.float()
+    vf = kv[:, C:].view(L, H, 128)
+    k_deq = torch.from_numpy(_deq_tiles(txt["kb"], txt["ks"])).to(DEV)
+    v_deq = torch.from_numpy(_deq_tiles(txt["vb"], txt["vs"])).to(DEV)
+    assert rel(k_deq, kf.permute(1, 0, 2)) < 4e-2
+    assert rel(v_deq, vf.permute(1, 0, 2)) < 4e-2
+    # cross queries: RMSNorm of (cq * hs), per-tile E4M3
+    cq = rec[(0, "cross_q")]
+    hs = rec[(0, "norm3")]["hs"]
+    qf = (cq["cq"].float() * hs[:, None]).view(st.rows, H, 128)
+    qf = qf * torch.rsqrt(qf.pow(2).mean(-1, keepdim=True) + blk.attn2.norm_q.eps) * blk.attn2.norm_q.weight.float()
+    q_deq = torch.from_numpy(_deq_tiles(cq["cqb"], cq["cqs"])).to(DEV)
+    slot = st.b["slot"].long()
+    assert rel(q_deq[:, slot], qf.permute(1, 0, 2)) < 4e-2
+    # dense attention over the 512 text keys with the same quantized operands
+    p = torch.softmax((q_deq.double() @ k_deq.double().transpose(1, 2)) / math.sqrt(128), -1)
+    want = (p @ v_deq.double()).float()
+    got = rec[(0, "cross_attn")]["cob"].float()
+    assert rel(got[:, slot], want[:, slot]) < 2e-2
+
+
+# ------------------------------------------------------------------------------------------------ config 3 chain
+def test_fp8_block_chain_stages(pkg):
+    """BASELINE config 3's chain at 1000 rows, each stage against the oracle on its own GPU inputs."""
+    _, runner = pkg
+    chain = runner.Fp8BlockChain.random(DEV, seed=5)
+    g = torch.Generator(device=DEV).manual_seed(9)
+    x = torch.randn(1000, 5120, device=DEV, generator=g).bfloat16()
+    tabs = (torch.randn(6, 5120, device=DEV, generator=g) * 0.1).bfloat16()
+    rec = {}
+    chain.trace = lambda stage, t: rec.__setitem__(stage, {k: v.clone() for k, v in t.items()})
+    x0 = x.clone()
+    chain(x, tabs)
+    torch.cuda.synchronize()
+    f = lambda t: t.float().cpu().numpy()  # noqa: E731
+    # LayerNorm + modulate + FP8 (attention half)
+    want = oq.resid_norm_quant(f(x0), shift=f(tabs[0:1]), scale=f(tabs[1:2]), eps=1e-6, norm="layer")
+    assert_codes(rec["norm1"]["h"].view(torch.uint8).cpu().numpy(), want["h"], want["amb"], "chain norm1")
+    # QKV GEMM with row and channel scales, then FP8 of the V third
+    h = rec["norm1"]["h"].float() * rec["norm1"]["hs"][:, None]
+    qkv_ref = h @ weight_fp32(chain.qkv).t()
+    assert rel(rec["qkv"]["qkv"].float(), qkv_ref) < 3e-3
+    codes, s, amb = oq.quant_fp8_rows(f(rec["qkv"]["qkv"][:, 2 * 5120:]))
+    assert_codes(rec["qkv"]["a"].view(torch.uint8).cpu().numpy(), codes, amb, "chain V quant")
+    # out-projection with the gated residual
+    a = rec["qkv"]["a"].float() * rec["qkv"]["sa"][:, None]
+    upd = tabs[2].float() * (a @ weight_fp32(chain.o).t())
+    x1 = rec["out_proj"]["x"].float()
+    assert rel(x1, (x0.float() + upd).bfloat16().float()) < 1e-3
+    # second norm, fc_in with GELU-tanh, FP8 of the intermediate, fc_out with the gated residual
+    want = oq.resid_norm_quant(f(rec["out_proj"]["x"]), shift=f(tabs[3:4]), scale=f(tabs[4:5]), eps=1e-6,
+                               norm="layer")
+    assert_codes(rec["norm2"]["h"].view(torch.uint8).cpu().numpy(), want["h"], want["amb"], "chain norm2")
+    h2 = rec["norm2"]["h"].float() * rec["norm2"]["hs"][:, None]
+    u_ref = torch.nn.functional.gelu(h2 @ weight_fp32(chain.fc_in).t(), approximate="tanh")
+    assert rel(rec["ffn_mid"]["u"].float(), u_ref) < 3e-3
+    codes, s, amb = oq.quant_fp8_rows(f(rec["ffn_mid"]["u"]))
+    assert_codes(rec["ffn_mid"]["f"].view(torch.uint8).cpu().numpy(), codes, amb, "chain FFN quant")
+    fq = rec["ffn_mid"]["f"].float() * rec["ffn_mid"]["fs"][:, None]
+    upd = tabs[5].float() * (fq @ weight_fp32(chain.fc_out).t())
+    assert rel(rec["fc_out"]["x"].float(), (x1 + upd).bfloat16().float()) < 1e-3
