@@ -1,5 +1,5 @@
 // Thin inline-PTX wrappers for the sm_100a instructions the kernels use: mbarriers with bounded waits, TMA / bulk
-// copies (never with cluster multicast), and tcgen05 (TMEM alloc, MMA, SMEM->TMEM copy, TMEM loads, commit).
+// copies (each CTA loads only into its own shared memory), and tcgen05 (TMEM alloc, MMA, SMEM->TMEM copy, TMEM loads, commit).
 // Descriptor bit layouts follow the PTX ISA "tcgen05 matrix descriptors" and "instruction descriptor" tables.
 #pragma once
 
@@ -73,7 +73,7 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
 }
 
-// 2D tiled TMA load into this CTA's shared memory (no multicast), completing on `bar`.
+// 2D tiled TMA load into this CTA's own shared memory, completing on `bar`.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(

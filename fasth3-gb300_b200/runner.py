@@ -102,7 +102,8 @@ class _Exchange:
                 outs[r][p * Hl:(p + 1) * Hl].copy_(ys[p][r])
 
     def all_gather_rows(self, xs: list[torch.Tensor], rows: list[int]) -> torch.Tensor:
-        """Concatenation over ranks (in rank order) of each rank's [rows_r, C] block."""
+        """Concatenation over ranks (in rank order) of each rank's [rows_r, C] block; ``rows`` holds every rank's
+        row count."""
         if self.virtual:
             return torch.cat([x[:r] for x, r in zip(xs, rows)])
         if self.world == 1:
@@ -355,7 +356,9 @@ class H3FastRunner:
             self._norm(st, self.blocks[0].eps, tabs[0, 0:1], tabs[0, 1:2], 0)
         for i, blk in enumerate(self.blocks):
             self._block(i, blk, full, states, tabs, txt, meta)
-        out = self.ex.all_gather_rows([st.b["x"] for st in states], [st.rows for st in states])  # global tile order
+        per = full.n_tiles // self.ex.world
+        rows_all = [int(full.vbs[p * per:(p + 1) * per].sum()) for p in range(self.ex.world)]
+        out = self.ex.all_gather_rows([st.b["x"] for st in states], rows_all)  # global tile order
         inv = torch.empty_like(full.perm)
         inv[full.perm] = torch.arange(full.rows)
         return out.index_select(0, inv.to(out.device)).unsqueeze(0)

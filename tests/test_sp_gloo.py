@@ -94,6 +94,25 @@ def body_layout(rank, world, pkg):
     assert (part.vbs <= 64).all() and part.rows == int(part.vbs.sum())
 
 
+def body_runner_exchange(rank, world, pkg):
+    """The runner's exchange object over real ranks: the all-to-all layouts and the final gather with unequal rows."""
+    from fasth3_b200.runner import _Exchange
+    from fasth3_b200.sp import SeqParallel
+    ex = _Exchange(SeqParallel())
+    H, R, D = 4, 6, 3
+    full = torch.arange(H * world * R * D, dtype=torch.float32).view(H, world * R, D)
+    mine = full[:, rank * R:(rank + 1) * R].contiguous()
+    got = torch.empty(world, H // world, R, D)
+    ex.seq_to_heads([mine], [got])
+    back = torch.empty_like(mine)
+    ex.heads_to_seq([got], [back])
+    assert torch.equal(back, mine)
+    rows = [5 + p for p in range(world)]  # unequal row counts per rank
+    x = torch.full((rows[rank], 2), float(rank))
+    out = ex.all_gather_rows([x], rows)
+    assert torch.equal(out, torch.cat([torch.full((r, 2), float(p)) for p, r in enumerate(rows)]))
+
+
 def body_peer_dies(rank, world, pkg):
     from fasth3_b200.sp import SeqParallel
     sp = SeqParallel()
@@ -111,6 +130,11 @@ def test_head_all_to_all_layouts():
 
 def test_tile_sharding_covers_the_latent():
     res = _run("body_layout")
+    assert all(v == "ok" for v in res.values()), res
+
+
+def test_runner_exchange_over_real_ranks():
+    res = _run("body_runner_exchange")
     assert all(v == "ok" for v in res.values()), res
 
 
