@@ -194,18 +194,18 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t idesc = FP4 ? idesc_nvf4(BN) : idesc_e4m3(BN);
       int stage = 0;
       uint32_t phase = 0;
-      uint32_t acc_phase[2] = {0, 0};
+      uint32_t acc_phase = 0;
       int j = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++j) {
         int mb, nb;
         tile_coords(tile, p, mb, nb);
         const int buf = j & 1;
-        if (!mbar_wait_bounded(&acc_empty[buf], acc_phase[buf] ^ 1, abort_flag, kWaitLimitNs)) {
+        if (!mbar_wait_bounded(&acc_empty[buf], (((acc_phase >> buf) & 1u) ^ 1u), abort_flag, kWaitLimitNs)) {
           fail();
           break;
         }
-        acc_phase[buf] ^= 1;
+        acc_phase ^= 1u << buf;
         tc_fence_after();
         const uint32_t d = tmem + buf * C::kAccCols;
         // NVFP4 B tiles of 192 rows start mid-atom on odd n-blocks: the first 64 rows sit in columns 2-3 of the atom
@@ -256,18 +256,18 @@ __global__ void __launch_bounds__(192, 1)
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const float alpha = e.alpha * (e.alpha_dev ? *e.alpha_dev : 1.f);
-    uint32_t acc_phase[2] = {0, 0};
+    uint32_t acc_phase = 0;
     int j = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++j) {
       int mb, nb;
       tile_coords(tile, p, mb, nb);
       const int buf = j & 1;
-      const bool got = mbar_wait_bounded(&acc_full[buf], acc_phase[buf], abort_flag, kWaitLimitNs);
+      const bool got = mbar_wait_bounded(&acc_full[buf], ((acc_phase >> buf) & 1u), abort_flag, kWaitLimitNs);
       if (!__all_sync(0xffffffffu, got)) {
         if (lane == 0) fail();
         break;
       }
-      acc_phase[buf] ^= 1;
+      acc_phase ^= 1u << buf;
       __syncwarp();
       tc_fence_after();
       const int m = mb * BM + q * 32 + lane;

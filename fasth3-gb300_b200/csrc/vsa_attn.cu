@@ -1,13 +1,18 @@
-// FP8 block-sparse VSA attention (fine step) for sm_100a: tcgen05 MMAs on E4M3 Q/K/V with TMEM accumulators, TMA
-// staging, one persistent CTA per SM.
+// FP8 block-sparse VSA attention (fine step) for sm_100a: tcgen05 MMAs with TMEM accumulators, TMA staging, one
+// persistent CTA per SM.
 //
 // Semantics (BASELINE config 4 and fastvideo/models/dits/h3fast/vsa_fp8.cuh:10-15, 716-764): for each (head, query
 // tile) softmax attention of its rows over the keys of its selected 64-key tiles (keys past vbs_kv[b] masked), scores
-// scaled by the softmax scale and the Q/K scales, fp32 online softmax, bf16 output, optional log2-domain LSE. P is
-// E4M3 with the V tile scale folded in: P' = 2^(x - m + 6) * (sv_b / sv_head) (<= 2^8 < 448 under the lazy-rescale
-// bound 2^2), the row sum carries the same 2^6, so O = (sum P' V8) * sv_head / l. P' is split into two E4M3 terms,
-// hi = e4m3(P') and lo = e4m3(P' - hi), both multiplied with V into the same accumulator: one term leaves ~3% relative
-// noise on O when V is noise-like (BASELINE config 4's N(0,1) data), two leave ~2^-8.
+// scaled by the softmax scale and the Q/K scales, fp32 online softmax with a lazy rescale (the running maximum moves
+// only when a tile's maximum exceeds it by more than 2^4), bf16 output, optional log2-domain LSE.
+//
+// Arithmetic: S = Q8 K8^T on E4M3 operands (kind::f8f6f4). P = 2^(S*coef - m) is evaluated in f16x2 (one
+// ex2.approx.f16x2 per two keys; the exponent argument is at most 4 in magnitude for every key that matters, where f16
+// resolves it to 2^-9) and multiplied with V in f16 (kind::f16). V is stored E4M3 with one scale per (head, tile); each
+// V tile is converted once per use into f16 in shared memory with the tile's scale ratio sv_b / sv_head folded in, so
+// O = (sum P V') * sv_head / l and the row sum l = sum P needs no per-tile correction. The conversion is shared by the
+// 128 query rows of a work item. (The reference's kernel quantizes P to E4M3 instead; f16 P keeps the attention
+// output within ~2^-9 of exact attention over the same E4M3 Q/K/V.)
 //
 // Operand layout: Q/out and K/V are each [chunks * heads, rows_chunk, 128] ("planes" of rows_chunk rows). Query tile t
 // of head h lives in plane (t / tiles_per_chunk) * heads + h at row (t % tiles_per_chunk) * 64. With one chunk this is
@@ -18,12 +23,11 @@
 // Work item = (head, pair of query tiles t0 = 2p, t1 = 2p+1): the 128 query rows form one M=128 MMA operand and the
 // pair walks the ascending union of its two selection lists; a row whose tile did not select a key tile gets P = 0
 // there. CTA = 10 warps:
-//   warp 0    union list (bitmaps + warp prefix sums); TMA loads of the Q pair (per item) and K/V tiles (ring)
-//   warp 1    TMEM allocation, MMA issue: S_j = Q K_j^T (4 x K32, one of two S buffers), O += P_j V_j (2 x K32 per
-//             P term, P from TMEM, V as an MN-major operand); S runs one key tile ahead of PV
-//   warps 2-9 softmax: warps w and w+4 share TMEM lanes 32*(w%4).. (one query row per lane) and split the 64 keys of
-//             a tile (and the 128 output columns) in halves; row maxima and row sums are combined in shared memory
-//             behind per-pair mbarriers (bounded waits, so a pair never blocks forever on a partner that left)
+//   warp 0     union list (bitmaps + warp prefix sums); TMA loads of the Q pair (per item) and K/V tiles (ring)
+//   warp 1     TMEM allocation, MMA issue: S_j = Q K_j^T (E4M3, 4 x K32, two S buffers, one key tile ahead of PV),
+//              O += P_j V'_j (f16, 4 x K16, P from TMEM, V' from shared memory as an MN-major operand)
+//   warps 2-5  V converters: E4M3 V tile -> f16 V' (scale ratio folded in), 128-byte-swizzled MN-major layout
+//   warps 6-9  softmax + epilogue: one query row per thread (TMEM lane), the 64 scores of a key tile in registers
 // Every wait is bounded (2 s) and records H3B_ETIMEOUT in a device status word.
 #include "common.cuh"
 #include "sm100.cuh"
@@ -40,15 +44,16 @@ using namespace sm100;
 
 constexpr int D = 128;
 constexpr int TILE = 64;
-constexpr int KV_STAGES = 6;
+constexpr int KV_STAGES = 4;  // E4M3 K/V tiles
+constexpr int VF_STAGES = 3;  // f16 V' tiles
 constexpr int N_MAX = 4096;   // key tiles (bitmap words: 128)
 constexpr int U_MAX = N_MAX;  // the union of two subsets of N_MAX tiles
-constexpr int SOFT_WARPS = 8;
-constexpr int THREADS = (2 + SOFT_WARPS) * 32;
-constexpr float P_SHIFT = 6.f;
-constexpr float RESCALE_LOG2 = 2.f;
+constexpr int CONV_WARPS = 4;
+constexpr int SOFT_WARPS = 4;
+constexpr int THREADS = (2 + CONV_WARPS + SOFT_WARPS) * 32;
+constexpr float RESCALE_LOG2 = 4.f;
 constexpr uint64_t kLimitNs = 2000000000ull;
-// TMEM columns: O [0,128), S buffers [128,192) [192,256), P buffer b: hi [256+32b, +16), lo [+16, +32)
+// TMEM columns: O [0,128), S buffers [128,192) [192,256), P buffers (f16, 64 keys = 32 columns) [256,288) [288,320)
 constexpr uint32_t COL_O = 0, COL_S = 128, COL_P = 256;
 
 struct AttnArgs {
@@ -73,17 +78,16 @@ struct AttnArgs {
 struct __align__(1024) Smem {
   uint8_t q[2][2 * TILE * D];
   uint8_t kv[KV_STAGES][2][TILE * D];
+  uint8_t vf[VF_STAGES][2][TILE * 128];  // [half of d][key][64 d] f16, 128-byte rows, 128-byte swizzle
   uint32_t ulist[2][U_MAX];
   uint32_t bm[2][N_MAX / 32];
-  float pmax[2][2][2 * TILE];  // [tile parity][half][row]: partial row maxima exchanged between warp pairs
-  float lsum[2][2][2 * TILE];  // [item parity][half][row]: partial row sums at the end of an item
   int ucount[2];
   uint64_t q_full[2], q_empty[2];
   uint64_t kv_full[KV_STAGES], kv_empty[KV_STAGES];
+  uint64_t vf_full[VF_STAGES], vf_empty[VF_STAGES];
   uint64_t list_full[2], list_empty[2];
   uint64_t s_full[2], s_free[2], p_full[2];
   uint64_t pv_done, o_full, o_empty, drain;
-  uint64_t pair_bar[4][3];  // per warp pair: row-max exchange (two parities), row-sum exchange
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -97,20 +101,15 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
-__device__ __forceinline__ void mma_e4m3_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
-                                            uint32_t acc) {
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                           uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
 }
 
-__device__ __forceinline__ void tmem_st_8cols(uint32_t taddr, const uint32_t (&r)[8]) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr), "r"(r[0]),
-               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
-               : "memory");
-}
 __device__ __forceinline__ void tmem_st_32cols(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
@@ -129,27 +128,53 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// Two fp32 -> two E4M3 terms each (hi, lo; hi + lo matches the value to ~2^-8): element a in the low byte.
-__device__ __forceinline__ void split_e4m3x2(float a, float b, uint32_t& hi, uint32_t& lo) {
-  uint32_t h, back, r;
-  uint16_t h8, l8;
-  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(b), "f"(a));
-  asm("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;" : "=h"(h8) : "r"(h));
-  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(back) : "h"(h8));
-  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(h), "r"(back));
-  asm("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;" : "=h"(l8) : "r"(r));
-  hi = h8;
-  lo = l8;
+// 2^x for two keys: x0 (low half) and x1 rounded to f16, exponentiated in f16x2
+__device__ __forceinline__ uint32_t ex2_f16x2(float x0, float x1) {
+  uint32_t h, e;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(x1), "f"(x0));
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(e) : "r"(h));
+  return e;
 }
 
-
-__device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t saddr) {
-  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) |
-         ((uint64_t)2 << 61);
+__device__ __forceinline__ uint32_t hadd2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
 }
 
-__host__ __device__ constexpr uint32_t idesc_e4m3_mn(int n, bool b_mn) {
+// two E4M3 bytes (low byte first) -> f16x2 scaled by an f16x2 factor
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2_scaled(uint16_t v, uint32_t scale2) {
+  uint32_t h, d;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"(v));
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(h), "r"(scale2));
+  return d;
+}
+
+// K-major e4m3 tiles use desc_k_sw128; V' is MN-major: 64 f16 of d (128 bytes) per row, rows = keys, 8-row groups
+// 1024 bytes apart (SBO), the two 64-column halves of d `lbo` bytes apart (LBO), 128-byte swizzle.
+__device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t saddr, uint32_t lbo) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+         ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// fp32 accumulate, A and B of the same 8/16-bit type (E4M3 under kind::f8f6f4, f16 under kind::f16), A K-major,
+// B K-major or MN-major, M = 128
+__host__ __device__ constexpr uint32_t idesc_mn(int n, bool b_mn) {
   return (1u << 4) | (b_mn ? (1u << 16) : 0u) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+
+__device__ __forceinline__ void fail_cta(volatile int* abort_flag) {
+  *abort_flag = 1;
+  atomicExch(&g_attn_status, H3B_ETIMEOUT);
+}
+
+// a wait every lane of the warp takes; false (and the CTA marked aborted) if it gave up
+__device__ __forceinline__ bool warp_wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                  int lane) {
+  const bool got = mbar_wait_bounded(bar, parity, abort_flag, kLimitNs);
+  if (__all_sync(0xffffffffu, got)) return true;
+  if (lane == 0) fail_cta(abort_flag);
+  return false;
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -165,21 +190,23 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&sm.q_full[i], 1);
       mbar_init(&sm.q_empty[i], 1);
       mbar_init(&sm.list_full[i], 1);
-      mbar_init(&sm.list_empty[i], 1 + SOFT_WARPS);
+      mbar_init(&sm.list_empty[i], 1 + CONV_WARPS + SOFT_WARPS);
       mbar_init(&sm.s_full[i], 1);
       mbar_init(&sm.s_free[i], SOFT_WARPS);
       mbar_init(&sm.p_full[i], SOFT_WARPS);
     }
     for (int s = 0; s < KV_STAGES; ++s) {
       mbar_init(&sm.kv_full[s], 1);
-      mbar_init(&sm.kv_empty[s], 1);
+      mbar_init(&sm.kv_empty[s], 1 + CONV_WARPS);  // K read by the S MMA, V read by the converters
+    }
+    for (int s = 0; s < VF_STAGES; ++s) {
+      mbar_init(&sm.vf_full[s], CONV_WARPS);
+      mbar_init(&sm.vf_empty[s], 1);
     }
     mbar_init(&sm.pv_done, 1);
     mbar_init(&sm.o_full, 1);
     mbar_init(&sm.o_empty, SOFT_WARPS);
     mbar_init(&sm.drain, 1);
-    for (int q = 0; q < 4; ++q)
-      for (int k = 0; k < 3; ++k) mbar_init(&sm.pair_bar[q][k], 2);
     sm.abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tmQ);
@@ -194,15 +221,13 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
-  auto fail = [&]() {
-    *abort_flag = 1;
-    atomicExch(&g_attn_status, H3B_ETIMEOUT);
-  };
+#define fail() fail_cta(abort_flag)
+#define warp_wait(bar, parity) warp_wait_bounded((bar), (parity), abort_flag, lane)
   const int pairs = a.n_q_ext / 2;
 
   if (warp == 0) {
     // -------------------------------------------------------------- union lists + TMA producer
-    uint32_t list_phase[2] = {0, 0}, q_phase[2] = {0, 0};
+    uint32_t list_phase = 0, q_phase = 0;
     int stage = 0;
     uint32_t kv_phase = 0;
     bool ok = true;
@@ -212,12 +237,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int buf = it & 1;
       const int h = item / pairs, p = item - h * pairs;
       const int t0 = 2 * p, t1 = 2 * p + 1;
-      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&sm.list_empty[buf], list_phase[buf] ^ 1, abort_flag, kLimitNs))) {
-        if (lane == 0) fail();
-        ok = false;
-        break;
-      }
-      list_phase[buf] ^= 1;
+      if (!warp_wait(&sm.list_empty[buf], (((list_phase >> buf) & 1u) ^ 1u))) break;
+      list_phase ^= 1u << buf;
       for (int w = lane; w < words; w += 32) {
         sm.bm[0][w] = 0u;
         sm.bm[1][w] = 0u;
@@ -263,11 +284,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       const int U = base;
       if (lane == 0) {
-        if (!mbar_wait_bounded(&sm.q_empty[buf], q_phase[buf] ^ 1, abort_flag, kLimitNs)) {
+        if (!mbar_wait_bounded(&sm.q_empty[buf], (((q_phase >> buf) & 1u) ^ 1u), abort_flag, kLimitNs)) {
           fail();
           ok = false;
         } else {
-          q_phase[buf] ^= 1;
+          q_phase ^= 1u << buf;
           mbar_arrive_expect_tx(&sm.q_full[buf], 2 * TILE * D);
           for (int s = 0; s < 2; ++s) {
             const int t = s ? t1 : t0;
@@ -297,67 +318,68 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == 1) {
     // -------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      const uint32_t idesc_s = idesc_e4m3_mn(TILE, false);
-      const uint32_t idesc_pv = idesc_e4m3_mn(D, true);
-      uint32_t list_phase[2] = {0, 0}, q_phase[2] = {0, 0}, s_phase[2] = {0, 0}, p_phase[2] = {0, 0};
+      const uint32_t idesc_s = idesc_mn(TILE, false);
+      const uint32_t idesc_pv = idesc_mn(D, true);
+      uint32_t list_phase = 0, q_phase = 0, s_phase = 0, p_phase = 0;
       uint32_t o_phase = 0;
-      int stage = 0;
-      uint32_t kv_phase = 0;
+      int s_stage = 0, vstage = 0;
+      uint32_t s_kvphase = 0, vf_phase = 0;
       int sbuf_next = 0, pbuf = 0;
       bool ok = true;
       int it = 0;
       for (int item = blockIdx.x; item < a.items && ok; item += gridDim.x, ++it) {
         const int buf = it & 1;
-        if (!mbar_wait_bounded(&sm.list_full[buf], list_phase[buf], abort_flag, kLimitNs)) { fail(); break; }
-        list_phase[buf] ^= 1;
+        if (!mbar_wait_bounded(&sm.list_full[buf], ((list_phase >> buf) & 1u), abort_flag, kLimitNs)) { fail(); break; }
+        list_phase ^= 1u << buf;
         const int U = sm.ucount[buf];
-        if (!mbar_wait_bounded(&sm.q_full[buf], q_phase[buf], abort_flag, kLimitNs)) { fail(); break; }
-        q_phase[buf] ^= 1;
+        if (!mbar_wait_bounded(&sm.q_full[buf], ((q_phase >> buf) & 1u), abort_flag, kLimitNs)) { fail(); break; }
+        q_phase ^= 1u << buf;
         tc_fence_after();
         const uint64_t dq = desc_k_sw128(smem_addr(&sm.q[buf][0]));
-        int s_stage = stage;
-        uint32_t s_kvphase = kv_phase;
-        auto issue_s = [&]() -> bool {
-          const int sb = sbuf_next;
-          if (!mbar_wait_bounded(&sm.kv_full[s_stage], s_kvphase, abort_flag, kLimitNs)) return false;
-          if (!mbar_wait_bounded(&sm.s_free[sb], s_phase[sb] ^ 1, abort_flag, kLimitNs)) return false;
-          s_phase[sb] ^= 1;
-          tc_fence_after();
-          const uint64_t dk = desc_k_sw128(smem_addr(&sm.kv[s_stage][0][0]));
+        // j = -1 issues S(0) only; step j issues S(j+1) (one key tile ahead) and then PV(j)
+        for (int j = -1; j < U; ++j) {
+          if (j + 1 < U) {
+            const int sb = sbuf_next;
+            if (!mbar_wait_bounded(&sm.kv_full[s_stage], s_kvphase, abort_flag, kLimitNs) ||
+                !mbar_wait_bounded(&sm.s_free[sb], (((s_phase >> sb) & 1u) ^ 1u), abort_flag, kLimitNs)) {
+              fail();
+              ok = false;
+              break;
+            }
+            s_phase ^= 1u << sb;
+            tc_fence_after();
+            const uint64_t dk = desc_k_sw128(smem_addr(&sm.kv[s_stage][0][0]));
 #pragma unroll
-          for (int i = 0; i < 4; ++i) mma_e4m3(tmem + COL_S + sb * TILE, dq + 2 * i, dk + 2 * i, idesc_s, i != 0);
-          tc_commit(&sm.s_full[sb]);
-          sbuf_next ^= 1;
-          if (++s_stage == KV_STAGES) {
-            s_stage = 0;
-            s_kvphase ^= 1;
+            for (int i = 0; i < 4; ++i) mma_e4m3(tmem + COL_S + sb * TILE, dq + 2 * i, dk + 2 * i, idesc_s, i != 0);
+            tc_commit(&sm.s_full[sb]);
+            tc_commit(&sm.kv_empty[s_stage]);  // the K half of the stage is consumed
+            sbuf_next ^= 1;
+            if (++s_stage == KV_STAGES) {
+              s_stage = 0;
+              s_kvphase ^= 1;
+            }
           }
-          return true;
-        };
-        if (U > 0 && !issue_s()) { fail(); break; }
-        for (int j = 0; j < U; ++j) {
-          if (j + 1 < U && !issue_s()) { fail(); ok = false; break; }
+          if (j < 0) continue;
           if (j == U - 1) tc_commit(&sm.q_empty[buf]);
           if (j == 0) {
             if (!mbar_wait_bounded(&sm.o_empty, o_phase ^ 1, abort_flag, kLimitNs)) { fail(); ok = false; break; }
             o_phase ^= 1;
           }
-          if (!mbar_wait_bounded(&sm.p_full[pbuf], p_phase[pbuf], abort_flag, kLimitNs)) { fail(); ok = false; break; }
-          p_phase[pbuf] ^= 1;
+          if (!mbar_wait_bounded(&sm.p_full[pbuf], ((p_phase >> pbuf) & 1u), abort_flag, kLimitNs)) { fail(); ok = false; break; }
+          p_phase ^= 1u << pbuf;
+          if (!mbar_wait_bounded(&sm.vf_full[vstage], vf_phase, abort_flag, kLimitNs)) { fail(); ok = false; break; }
           tc_fence_after();
-          const uint64_t dv = desc_mn_sw128(smem_addr(&sm.kv[stage][1][0]));
+          const uint64_t dv = desc_mn_sw128(smem_addr(&sm.vf[vstage][0][0]), TILE * 128);
 #pragma unroll
-          for (int t = 0; t < 2; ++t)
-#pragma unroll
-            for (int i = 0; i < 2; ++i)
-              mma_e4m3_ts(tmem + COL_O, tmem + COL_P + pbuf * 32 + t * 16 + 8 * i,
-                          dv + (uint64_t)((i * 32 * D) >> 4), idesc_pv, (j | i | t) != 0);
-          tc_commit(&sm.kv_empty[stage]);
+          for (int i = 0; i < 4; ++i)  // K = 16 keys per MMA: 8 TMEM columns of P, 16 rows (2048 bytes) of V'
+            mma_f16_ts(tmem + COL_O, tmem + COL_P + pbuf * 32 + 8 * i, dv + (uint64_t)((i * 16 * 128) >> 4),
+                       idesc_pv, (j | i) != 0);
+          tc_commit(&sm.vf_empty[vstage]);
           tc_commit(&sm.pv_done);
           pbuf ^= 1;
-          if (++stage == KV_STAGES) {
-            stage = 0;
-            kv_phase ^= 1;
+          if (++vstage == VF_STAGES) {
+            vstage = 0;
+            vf_phase ^= 1;
           }
         }
         if (!ok) break;
@@ -373,26 +395,76 @@ __global__ void __launch_bounds__(THREADS, 1)
       volatile int no_abort = 0;
       if (!mbar_wait_bounded(&sm.drain, 0, &no_abort, kLimitNs)) fail();
     }
-  } else {
-    // -------------------------------------------------------------- softmax + epilogue (warps 2..9)
-    const int q4 = warp & 3;
-    const int half = (warp - 2) >> 2;  // warps 2-5: keys 0-31 and O columns 0-63; warps 6-9: the other halves
-    const int r = q4 * 32 + lane;
-    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
-    const uint32_t my_bit = r < TILE ? 1u : 2u;
-    uint32_t pair_phase[3] = {0, 0, 0};
-    // both warps of the pair have published their shared-memory values for this exchange
-    auto pair_exchange = [&](int k) -> bool {
+  } else if (warp < 2 + CONV_WARPS) {
+    // -------------------------------------------------------------- V converters: E4M3 -> f16 V' = v * sv_b/sv_head
+    const int ct = (warp - 2) * 32 + lane;
+    uint32_t list_phase = 0;
+    int stage = 0, vstage = 0;
+    uint32_t kv_phase = 0, vf_phase = 0;
+    bool ok = true;
+    int it = 0;
+    for (int item = blockIdx.x; item < a.items && ok; item += gridDim.x, ++it) {
+      const int buf = it & 1;
+      const int h = item / pairs;
+      if (!warp_wait(&sm.list_full[buf], ((list_phase >> buf) & 1u))) break;
+      list_phase ^= 1u << buf;
+      const int U = sm.ucount[buf];
+      const float inv_vhead = 1.f / a.vs_head[h];
+      float vs_next = U > 0 ? a.vs[(size_t)h * a.kv_scale_ld + (sm.ulist[buf][0] & 0xFFFFu)] : 0.f;
+      for (int j = 0; j < U; ++j) {
+        const __half2 r2 = __float2half2_rn(vs_next * inv_vhead);
+        const uint32_t scale2 = *reinterpret_cast<const uint32_t*>(&r2);
+        if (j + 1 < U) vs_next = a.vs[(size_t)h * a.kv_scale_ld + (sm.ulist[buf][j + 1] & 0xFFFFu)];
+        if (!warp_wait(&sm.kv_full[stage], kv_phase)) { ok = false; break; }
+        if (!warp_wait(&sm.vf_empty[vstage], vf_phase ^ 1)) { ok = false; break; }
+        const uint8_t* src = &sm.kv[stage][1][0];
+        uint8_t* dst = &sm.vf[vstage][0][0];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int u = ct + 128 * i;
+          const int key = u >> 3, c = u & 7;  // 16 E4M3 values: d = 16c .. 16c+15
+          const uint4 raw = *reinterpret_cast<const uint4*>(src + key * 128 + ((c ^ (key & 7)) << 4));
+          const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+          uint32_t f[8];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            f[2 * q] = e4m3x2_to_f16x2_scaled((uint16_t)(w[q] & 0xFFFFu), scale2);
+            f[2 * q + 1] = e4m3x2_to_f16x2_scaled((uint16_t)(w[q] >> 16), scale2);
+          }
+          uint8_t* half_base = dst + (c >> 2) * (TILE * 128) + key * 128;
+          const int dc0 = (c & 3) * 2;
+          *reinterpret_cast<uint4*>(half_base + ((dc0 ^ (key & 7)) << 4)) = make_uint4(f[0], f[1], f[2], f[3]);
+          *reinterpret_cast<uint4*>(half_base + (((dc0 + 1) ^ (key & 7)) << 4)) = make_uint4(f[4], f[5], f[6], f[7]);
+        }
+        fence_proxy_async_smem();  // the generic-proxy stores become visible to the tensor core
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&sm.vf_full[vstage]);
+          mbar_arrive(&sm.kv_empty[stage]);
+        }
+        if (++stage == KV_STAGES) {
+          stage = 0;
+          kv_phase ^= 1;
+        }
+        if (++vstage == VF_STAGES) {
+          vstage = 0;
+          vf_phase ^= 1;
+        }
+      }
+      if (!ok) break;
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.pair_bar[q4][k]);
-      const bool done = mbar_wait_bounded(&sm.pair_bar[q4][k], pair_phase[k], abort_flag, kLimitNs);
-      pair_phase[k] ^= 1;
-      return __all_sync(0xffffffffu, done);
-    };
-    uint32_t list_phase[2] = {0, 0}, s_phase[2] = {0, 0};
+      if (lane == 0) mbar_arrive(&sm.list_empty[buf]);
+    }
+  } else {
+    // -------------------------------------------------------------- softmax + epilogue (warps 6..9)
+    const int q4 = warp & 3;       // a warp reaches only the TMEM lanes 32*(warp%4) .. +31
+    const int r = q4 * 32 + lane;  // query row of the item = TMEM lane
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const uint32_t my_bit = r < TILE ? 1u : 2u;  // warp-uniform
+    uint32_t list_phase = 0, s_phase = 0;
     uint32_t o_phase = 0;
     uint32_t pv_count = 0;
-    int sbuf = 0, pbuf_g = 0, par = 0;
+    int sbuf = 0, pbuf = 0;
     int it = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < a.items && ok; item += gridDim.x, ++it) {
@@ -400,62 +472,68 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int h = item / pairs, p = item - h * pairs;
       const int tq = r < TILE ? 2 * p : 2 * p + 1;
       const int rr = r & (TILE - 1);
-      bool got = mbar_wait_bounded(&sm.list_full[buf], list_phase[buf], abort_flag, kLimitNs);
-      if (!__all_sync(0xffffffffu, got)) { if (lane == 0) fail(); ok = false; break; }
-      list_phase[buf] ^= 1;
+      if (!warp_wait(&sm.list_full[buf], ((list_phase >> buf) & 1u))) break;
+      list_phase ^= 1u << buf;
       const int U = sm.ucount[buf];
-      const float qscale = a.qs ? a.qs[(size_t)h * a.q_scale_ld + tq] : 1.f;
-      const float vhead = a.vs_head[h];
-      const float inv_vhead = 1.f / vhead;
+      const float qcoef = a.coef * (a.qs ? a.qs[(size_t)h * a.q_scale_ld + tq] : 1.f);
       float m_ref = -INFINITY, l = 0.f;
+      // per-tile scalars of key tile j+1 are loaded while tile j is processed (global loads off the critical path)
+      int vbs_next = 0;
+      float ks_next = 1.f;
+      if (U > 0) {
+        const int b0 = (int)(sm.ulist[buf][0] & 0xFFFFu);
+        vbs_next = a.vbs_kv[b0];
+        if (a.ks) ks_next = a.ks[(size_t)h * a.kv_scale_ld + b0];
+      }
       for (int j = 0; j < U; ++j) {
         const uint32_t e = sm.ulist[buf][j];
-        const int b = (int)(e & 0xFFFFu);
         const bool member = (e >> 16) & my_bit;
-        got = mbar_wait_bounded(&sm.s_full[sbuf], s_phase[sbuf], abort_flag, kLimitNs);
-        if (!__all_sync(0xffffffffu, got)) { if (lane == 0) fail(); ok = false; break; }
-        s_phase[sbuf] ^= 1;
-        __syncwarp();
+        const int vbs_j = vbs_next;
+        const float ks_j = ks_next;
+        if (j + 1 < U) {
+          const int bn = (int)(sm.ulist[buf][j + 1] & 0xFFFFu);
+          vbs_next = a.vbs_kv[bn];
+          if (a.ks) ks_next = a.ks[(size_t)h * a.kv_scale_ld + bn];
+        }
+        if (!warp_wait(&sm.s_full[sbuf], ((s_phase >> sbuf) & 1u))) { ok = false; break; }
+        s_phase ^= 1u << sbuf;
         tc_fence_after();
-        uint32_t sr[32];
-        tmem_ld_32cols(tmem + lane_off + COL_S + sbuf * TILE + half * 32, sr);
+        uint32_t sr[64];
+        tmem_ld_32cols(tmem + lane_off + COL_S + sbuf * TILE, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+        tmem_ld_32cols(tmem + lane_off + COL_S + sbuf * TILE + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
         tmem_ld_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.s_free[sbuf]);
         sbuf ^= 1;
-        const int kv_valid = member ? a.vbs_kv[b] - half * 32 : 0;  // keys of this half that count
-        const float coef = a.coef * qscale * (a.ks ? a.ks[(size_t)h * a.kv_scale_ld + b] : 1.f);
-        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        const int kv_valid = member ? vbs_j : 0;
+        if (kv_valid < TILE) {
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float s = c < kv_valid ? __uint_as_float(sr[c]) : -INFINITY;
-          sr[c] = __float_as_uint(s);
-          m4[c & 3] = fmaxf(m4[c & 3], s);
+          for (int c = 0; c < 64; ++c)
+            if (c >= kv_valid) sr[c] = __float_as_uint(-INFINITY);
         }
-        const float mraw = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
-        sm.pmax[par][half][r] = mraw;
-        if (!pair_exchange(par)) { if (lane == 0) fail(); ok = false; break; }
-        const float mx = fmaxf(mraw, sm.pmax[par][half ^ 1][r]) * coef;  // coef > 0
-        par ^= 1;
-        // lazy rescale. The decision depends only on the running max, which both halves of the row share (their
-        // partial sums differ: a half whose keys were all masked has l = 0 but its O columns still carry the row's mass)
+        const float coef = qcoef * ks_j;
+        float m8[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) m8[c] = __uint_as_float(sr[c]);
+#pragma unroll
+        for (int c = 8; c < 64; ++c) m8[c & 7] = fmaxf(m8[c & 7], __uint_as_float(sr[c]));
+        const float mraw = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                                 fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        const float mx = mraw * coef;  // coef > 0
+        // lazy rescale: the running maximum moves only when this tile's maximum exceeds it by more than 2^4
         const bool grow = mx > m_ref + RESCALE_LOG2;
         const bool had_mass = m_ref != -INFINITY;
-        const bool need_o = grow && had_mass;
         float alpha = 1.f;
         if (grow) {
           alpha = had_mass ? ex2(m_ref - mx) : 1.f;
           m_ref = mx;
         }
-        if (__any_sync(0xffffffffu, need_o)) {
-          if (j > 0) {
-            got = mbar_wait_bounded(&sm.pv_done, (pv_count - 1) & 1, abort_flag, kLimitNs);
-            if (!__all_sync(0xffffffffu, got)) { if (lane == 0) fail(); ok = false; break; }
-          }
+        if (__any_sync(0xffffffffu, grow && had_mass)) {
+          if (j > 0 && !warp_wait(&sm.pv_done, (pv_count - 1) & 1)) { ok = false; break; }
           tc_fence_after();
 #pragma unroll 1
-          for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
+          for (int c0 = 0; c0 < D; c0 += 32) {
             uint32_t o[32];
             tmem_ld_32cols(tmem + lane_off + COL_O + c0, o);
             tmem_ld_wait();
@@ -466,58 +544,47 @@ __global__ void __launch_bounds__(THREADS, 1)
           tmem_st_wait();
         }
         l *= alpha;
-        uint32_t pw[8], pl[8];
+        uint32_t pw[32];
         if (m_ref == -INFINITY) {
 #pragma unroll
-          for (int c = 0; c < 8; ++c) pw[c] = pl[c] = 0u;
+          for (int c = 0; c < 32; ++c) pw[c] = 0u;
         } else {
-          const float base = P_SHIFT - m_ref;
-          const float vratio = a.vs[(size_t)h * a.kv_scale_ld + b] * inv_vhead;
-          float l4[4] = {0.f, 0.f, 0.f, 0.f};
+          const float nb = -m_ref;
+          uint32_t acc[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-          for (int c = 0; c < 32; c += 4) {
-            float ev[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              ev[u] = ex2(fmaf(__uint_as_float(sr[c + u]), coef, base));
-              l4[u] += ev[u];
-              ev[u] *= vratio;
-            }
-            uint32_t h0, l0, h1, l1;
-            split_e4m3x2(ev[0], ev[1], h0, l0);
-            split_e4m3x2(ev[2], ev[3], h1, l1);
-            pw[c >> 2] = h0 | (h1 << 16);
-            pl[c >> 2] = l0 | (l1 << 16);
+          for (int c = 0; c < 32; ++c) {
+            pw[c] = ex2_f16x2(fmaf(__uint_as_float(sr[2 * c]), coef, nb),
+                              fmaf(__uint_as_float(sr[2 * c + 1]), coef, nb));
+            acc[c & 3] = hadd2(acc[c & 3], pw[c]);
           }
-          l += (l4[0] + l4[1]) + (l4[2] + l4[3]);
+          const float2 s0 = __half22float2(*reinterpret_cast<const __half2*>(&acc[0]));
+          const float2 s1 = __half22float2(*reinterpret_cast<const __half2*>(&acc[1]));
+          const float2 s2 = __half22float2(*reinterpret_cast<const __half2*>(&acc[2]));
+          const float2 s3 = __half22float2(*reinterpret_cast<const __half2*>(&acc[3]));
+          l += ((s0.x + s0.y) + (s1.x + s1.y)) + ((s2.x + s2.y) + (s3.x + s3.y));
         }
-        tmem_st_8cols(tmem + lane_off + COL_P + pbuf_g * 32 + half * 8, pw);
-        tmem_st_8cols(tmem + lane_off + COL_P + pbuf_g * 32 + 16 + half * 8, pl);
+        tmem_st_32cols(tmem + lane_off + COL_P + pbuf * 32, pw);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.p_full[pbuf_g]);
-        pbuf_g ^= 1;
+        if (lane == 0) mbar_arrive(&sm.p_full[pbuf]);
+        pbuf ^= 1;
         ++pv_count;
       }
       if (!ok) break;
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.list_empty[buf]);
-      sm.lsum[buf][half][r] = l;
-      if (!pair_exchange(2)) { if (lane == 0) fail(); ok = false; break; }
-      const float lt = l + sm.lsum[buf][half ^ 1][r];
-      got = mbar_wait_bounded(&sm.o_full, o_phase, abort_flag, kLimitNs);
-      if (!__all_sync(0xffffffffu, got)) { if (lane == 0) fail(); ok = false; break; }
+      if (!warp_wait(&sm.o_full, o_phase)) break;
       o_phase ^= 1;
-      __syncwarp();
       tc_fence_after();
-      const float oscale = lt > 0.f ? vhead / lt : 0.f;
+      const float vhead = a.vs_head[h];
+      const float oscale = l > 0.f ? vhead / l : 0.f;
       const bool row_ok = rr < a.vbs_q[tq];
       const size_t orow =
           (size_t)((tq / a.tpc_q) * a.heads + h) * (size_t)a.rows_chunk_q + (size_t)(tq % a.tpc_q) * TILE + rr;
       bf16* dst = a.out + orow * D;
 #pragma unroll 1
-      for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
+      for (int c0 = 0; c0 < D; c0 += 32) {
         uint32_t o[32];
         tmem_ld_32cols(tmem + lane_off + COL_O + c0, o);
         tmem_ld_wait();
@@ -526,16 +593,15 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int c = 0; c < 32; c += 8) {
             float f[8];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) f[u] = lt > 0.f ? __uint_as_float(o[c + u]) * oscale : 0.f;
+            for (int u = 0; u < 8; ++u) f[u] = l > 0.f ? __uint_as_float(o[c + u]) * oscale : 0.f;
             store8(dst + c0 + c, f);
           }
         }
       }
-      if (a.lse && row_ok && half == 0) a.lse[orow] = lt > 0.f ? m_ref + __log2f(lt) - P_SHIFT : -INFINITY;
+      if (a.lse && row_ok) a.lse[orow] = l > 0.f ? m_ref + __log2f(l) : -INFINITY;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.o_empty);
-      // lsum[buf] is rewritten two items later, after the partner's next row-sum exchange (so after its read)
     }
   }
 
@@ -547,6 +613,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     tmem_dealloc(tmem, 512);
   }
 }
+#undef fail
+#undef warp_wait
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
