@@ -49,18 +49,28 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that may suspend the thread for up to `hint_ns` (it resumes as soon as the phase completes), so a waiting
+// warp does not spin on issue slots its sub-partition neighbours need
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Waits for the phase with the given parity to complete. Gives up after `limit_ns` of wall time, or as soon as
 // *abort is set by another thread of the CTA; returns false then.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort,
                                                   uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
-  for (uint32_t it = 0;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63) == 63) {
-      if (*abort) return false;
-      if (globaltimer_ns() - t0 > limit_ns) return false;
-    }
+  for (;;) {
+    if (mbar_try_wait_suspend(bar, parity, 20000u)) return true;
+    if (*abort) return false;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
   }
 }
 

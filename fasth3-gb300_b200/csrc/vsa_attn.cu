@@ -8,11 +8,10 @@
 //
 // Arithmetic: S = Q8 K8^T on E4M3 operands (kind::f8f6f4). P = 2^(S*coef - m) is evaluated in f16x2 (one
 // ex2.approx.f16x2 per two keys; the exponent argument is at most 4 in magnitude for every key that matters, where f16
-// resolves it to 2^-9) and multiplied with V in f16 (kind::f16). V is stored E4M3 with one scale per (head, tile); each
-// V tile is converted once per use into f16 in shared memory with the tile's scale ratio sv_b / sv_head folded in, so
-// O = (sum P V') * sv_head / l and the row sum l = sum P needs no per-tile correction. The conversion is shared by the
-// 128 query rows of a work item. (The reference's kernel quantizes P to E4M3 instead; f16 P keeps the attention
-// output within ~2^-9 of exact attention over the same E4M3 Q/K/V.)
+// resolves it to 2^-9), multiplied by the key tile's V-scale ratio sv_b / sv_head (P') after the row sum l = sum P is
+// taken, and multiplied with V in f16 (kind::f16): V is stored E4M3 with one scale per (head, tile) and each V tile is
+// converted exactly into f16 in shared memory once per use, so O = (sum P' V8) * sv_head / l. (The reference's kernel
+// quantizes P to E4M3 instead; f16 P keeps the output within ~2^-9 of exact attention over the same E4M3 Q/K/V.)
 //
 // Operand layout: Q/out and K/V are each [chunks * heads, rows_chunk, 128] ("planes" of rows_chunk rows). Query tile t
 // of head h lives in plane (t / tiles_per_chunk) * heads + h at row (t % tiles_per_chunk) * 64. With one chunk this is
@@ -20,14 +19,21 @@
 // delivers ([source rank][local head][rows]), so sequence-parallel callers attend in place without a permute copy.
 // K/V may be a different tensor with its own tile count (cross-attention to text tokens).
 //
-// Work item = (head, pair of query tiles t0 = 2p, t1 = 2p+1): the 128 query rows form one M=128 MMA operand and the
-// pair walks the ascending union of its two selection lists; a row whose tile did not select a key tile gets P = 0
-// there. CTA = 10 warps:
-//   warp 0     union list (bitmaps + warp prefix sums); TMA loads of the Q pair (per item) and K/V tiles (ring)
-//   warp 1     TMEM allocation, MMA issue: S_j = Q K_j^T (E4M3, 4 x K32, two S buffers, one key tile ahead of PV),
-//              O += P_j V'_j (f16, 4 x K16, P from TMEM, V' from shared memory as an MN-major operand)
-//   warps 2-5  V converters: E4M3 V tile -> f16 V' (scale ratio folded in), 128-byte-swizzled MN-major layout
-//   warps 6-9  softmax + epilogue: one query row per thread (TMEM lane), the 64 scores of a key tile in registers
+// Work item = (head, query tiles t0 = 2p and t1 = 2p+1), each with its own list of selected key tiles. The two tiles
+// run as two M=64 MMA streams in the two half-subpartitions of TMEM (tile t0 in lanes 0-15 of each 32-lane quarter,
+// t1 in lanes 16-31), so one 32-lane warp holds 16 rows of each tile and no MMA row computes a key tile its query tile
+// did not select. Step j processes key tile j of both lists. Steps alternate between two softmax warpgroups (split-KV
+// inside the CTA): each keeps its own running maximum, row sum and O accumulator, and the two partial results are
+// merged in the epilogue. CTA = 11 warps:
+//   warp 0      key-tile lists (from the top-k output) and TMA loads: the Q pair per item, K tiles and V tiles (two
+//               rings: K is released by the S MMA, V only after the softmax converted it)
+//   warps 1, 2  MMA issue for the even / odd steps (warp 1 also allocates TMEM): S_j = Q K_j^T (E4M3, M=64 N=64,
+//               4 x K32 per tile) as soon as the warpgroup has read S_{j-2}, O_{j%2} += P_j V'_j (f16, M=64 N=128,
+//               4 x K16 per tile, P from TMEM, V' from shared memory as an MN-major operand)
+//   warps 3-6   steps of even index, warps 7-10 steps of odd index: the softmax with one query row per thread (TMEM
+//               lane) and the 64 scores of a key tile in registers, then the step's E4M3 V tiles into f16 V'
+//               (128-byte-swizzled MN-major layout); the epilogue merges the two warpgroups' partial results (each
+//               writes half of the columns)
 // Every wait is bounded (2 s) and records H3B_ETIMEOUT in a device status word.
 #include "common.cuh"
 #include "sm100.cuh"
@@ -44,17 +50,18 @@ using namespace sm100;
 
 constexpr int D = 128;
 constexpr int TILE = 64;
-constexpr int KV_STAGES = 4;  // E4M3 K/V tiles
-constexpr int VF_STAGES = 3;  // f16 V' tiles
-constexpr int N_MAX = 4096;   // key tiles (bitmap words: 128)
-constexpr int U_MAX = N_MAX;  // the union of two subsets of N_MAX tiles
-constexpr int CONV_WARPS = 4;
-constexpr int SOFT_WARPS = 4;
-constexpr int THREADS = (2 + CONV_WARPS + SOFT_WARPS) * 32;
+constexpr int K_STAGES = 4;   // E4M3 K tiles of both query tiles (consumed by the S MMAs)
+constexpr int V_STAGES = 4;   // E4M3 V tiles of both query tiles (consumed by the conversion after the softmax)
+constexpr int N_MAX = 2048;   // key tiles
+constexpr int L_MAX = 1024;   // longest selection list (more selected key tiles set H3B_EINVAL in the status word)
+constexpr int SOFT_WARPS = 8;  // two warpgroups
+constexpr int THREADS = (3 + SOFT_WARPS) * 32;  // producer, two MMA issuers, two softmax warpgroups
 constexpr float RESCALE_LOG2 = 4.f;
 constexpr uint64_t kLimitNs = 2000000000ull;
-// TMEM columns: O [0,128), S buffers [128,192) [192,256), P buffers (f16, 64 keys = 32 columns) [256,288) [288,320)
-constexpr uint32_t COL_O = 0, COL_S = 128, COL_P = 256;
+// TMEM columns: O of even / odd steps [0,128) [128,256), S of even / odd steps [256,320) [320,384), P (f16, 64 keys =
+// 32 columns) of even / odd steps [384,416) [416,448). Query tile t1 uses the same columns at lane offset 16.
+constexpr uint32_t COL_O = 0, COL_S = 256, COL_P = 384;
+constexpr uint32_t LANE_B = 16u << 16;
 
 struct AttnArgs {
   const int32_t* idx;
@@ -76,18 +83,19 @@ struct AttnArgs {
 };
 
 struct __align__(1024) Smem {
-  uint8_t q[2][2 * TILE * D];
-  uint8_t kv[KV_STAGES][2][TILE * D];
-  uint8_t vf[VF_STAGES][2][TILE * 128];  // [half of d][key][64 d] f16, 128-byte rows, 128-byte swizzle
-  uint32_t ulist[2][U_MAX];
-  uint32_t bm[2][N_MAX / 32];
-  int ucount[2];
-  uint64_t q_full[2], q_empty[2];
-  uint64_t kv_full[KV_STAGES], kv_empty[KV_STAGES];
-  uint64_t vf_full[VF_STAGES], vf_empty[VF_STAGES];
+  uint8_t q[2][TILE * D];                    // [query tile] E4M3, 128-byte swizzle
+  uint8_t k[K_STAGES][2][TILE * D];          // [stage][query tile]
+  uint8_t v[V_STAGES][2][TILE * D];          // [stage][query tile]
+  uint8_t vf[2][2][2][TILE * 128];           // [warpgroup][query tile][half of d]: 64 keys x 64 f16, 128-byte rows
+  uint16_t list[2][2][L_MAX];                // [buffer][query tile] selected key tiles
+  float ml[2][2][2][128];                    // [item parity][max, sum][warpgroup][TMEM lane]
+  int cnt[2][2];                             // [buffer][query tile] list lengths
+  uint64_t q_full, q_empty;
+  uint64_t k_full[K_STAGES], k_empty[K_STAGES];
+  uint64_t v_full[V_STAGES], v_empty[V_STAGES];
   uint64_t list_full[2], list_empty[2];
-  uint64_t s_full[2], s_free[2], p_full[2];
-  uint64_t pv_done, o_full, o_empty, drain;
+  uint64_t s_full[2], s_free[2], p_full[2], pv_done[2];
+  uint64_t ml_bar, o_full, o_empty, drain[2];
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -142,12 +150,17 @@ __device__ __forceinline__ uint32_t hadd2(uint32_t a, uint32_t b) {
   return d;
 }
 
-// two E4M3 bytes (low byte first) -> f16x2 scaled by an f16x2 factor
-__device__ __forceinline__ uint32_t e4m3x2_to_f16x2_scaled(uint16_t v, uint32_t scale2) {
-  uint32_t h, d;
-  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"(v));
-  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(h), "r"(scale2));
+__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
   return d;
+}
+
+// two E4M3 bytes (low byte first) -> f16x2 (exact)
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint16_t v) {
+  uint32_t h;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"(v));
+  return h;
 }
 
 // K-major e4m3 tiles use desc_k_sw128; V' is MN-major: 64 f16 of d (128 bytes) per row, rows = keys, 8-row groups
@@ -158,9 +171,9 @@ __device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t saddr, uint32_t lbo) 
 }
 
 // fp32 accumulate, A and B of the same 8/16-bit type (E4M3 under kind::f8f6f4, f16 under kind::f16), A K-major,
-// B K-major or MN-major, M = 128
-__host__ __device__ constexpr uint32_t idesc_mn(int n, bool b_mn) {
-  return (1u << 4) | (b_mn ? (1u << 16) : 0u) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+// B K-major or MN-major
+__host__ __device__ constexpr uint32_t idesc_mn(int m, int n, bool b_mn) {
+  return (1u << 4) | (b_mn ? (1u << 16) : 0u) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
 __device__ __forceinline__ void fail_cta(volatile int* abort_flag) {
@@ -186,27 +199,29 @@ __global__ void __launch_bounds__(THREADS, 1)
   volatile int* abort_flag = &sm.abort_flag;
 
   if (threadIdx.x == 0) {
+    mbar_init(&sm.q_full, 1);
+    mbar_init(&sm.q_empty, 2);  // the last S MMA of each issuer
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&sm.q_full[i], 1);
-      mbar_init(&sm.q_empty[i], 1);
       mbar_init(&sm.list_full[i], 1);
-      mbar_init(&sm.list_empty[i], 1 + CONV_WARPS + SOFT_WARPS);
+      mbar_init(&sm.list_empty[i], 2 + SOFT_WARPS);
       mbar_init(&sm.s_full[i], 1);
-      mbar_init(&sm.s_free[i], SOFT_WARPS);
-      mbar_init(&sm.p_full[i], SOFT_WARPS);
+      mbar_init(&sm.s_free[i], SOFT_WARPS / 2);
+      mbar_init(&sm.p_full[i], SOFT_WARPS / 2);
+      mbar_init(&sm.pv_done[i], 1);
     }
-    for (int s = 0; s < KV_STAGES; ++s) {
-      mbar_init(&sm.kv_full[s], 1);
-      mbar_init(&sm.kv_empty[s], 1 + CONV_WARPS);  // K read by the S MMA, V read by the converters
+    for (int s = 0; s < K_STAGES; ++s) {
+      mbar_init(&sm.k_full[s], 1);
+      mbar_init(&sm.k_empty[s], 1);  // the S MMAs of the step have read the K tiles
     }
-    for (int s = 0; s < VF_STAGES; ++s) {
-      mbar_init(&sm.vf_full[s], CONV_WARPS);
-      mbar_init(&sm.vf_empty[s], 1);
+    for (int s = 0; s < V_STAGES; ++s) {
+      mbar_init(&sm.v_full[s], 1);
+      mbar_init(&sm.v_empty[s], SOFT_WARPS / 2);  // the step's warpgroup has converted the V tiles
     }
-    mbar_init(&sm.pv_done, 1);
-    mbar_init(&sm.o_full, 1);
+    mbar_init(&sm.ml_bar, SOFT_WARPS);
+    mbar_init(&sm.o_full, 2);  // the last PV MMA of each issuer
     mbar_init(&sm.o_empty, SOFT_WARPS);
-    mbar_init(&sm.drain, 1);
+    mbar_init(&sm.drain[0], 1);
+    mbar_init(&sm.drain[1], 1);
     sm.abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tmQ);
@@ -226,291 +241,240 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int pairs = a.n_q_ext / 2;
 
   if (warp == 0) {
-    // -------------------------------------------------------------- union lists + TMA producer
-    uint32_t list_phase = 0, q_phase = 0;
-    int stage = 0;
-    uint32_t kv_phase = 0;
+    // -------------------------------------------------------------- key-tile lists + TMA producer
+    uint32_t list_phase = 0, q_phase = 0, k_phase = 0, v_phase = 0;
+    int kst = 0, vst = 0;
     bool ok = true;
     int it = 0;
-    const int words = (a.n_kv + 31) / 32;
     for (int item = blockIdx.x; item < a.items && ok; item += gridDim.x, ++it) {
       const int buf = it & 1;
       const int h = item / pairs, p = item - h * pairs;
       const int t0 = 2 * p, t1 = 2 * p + 1;
-      if (!warp_wait(&sm.list_empty[buf], (((list_phase >> buf) & 1u) ^ 1u))) break;
+      if (!warp_wait(&sm.list_empty[buf], ((list_phase >> buf) & 1u) ^ 1u)) break;
       list_phase ^= 1u << buf;
-      for (int w = lane; w < words; w += 32) {
-        sm.bm[0][w] = 0u;
-        sm.bm[1][w] = 0u;
-      }
-      __syncwarp();
-      const int n0 = a.num[(size_t)h * a.n_q_ext + t0], n1 = a.num[(size_t)h * a.n_q_ext + t1];
-      const int32_t* l0 = a.idx + ((size_t)h * a.n_q_ext + t0) * a.idx_ld;
-      const int32_t* l1 = a.idx + ((size_t)h * a.n_q_ext + t1) * a.idx_ld;
-      for (int i = lane; i < n0 && i < a.idx_ld; i += 32) {
-        const int b = l0[i];
-        if (b >= 0 && b < a.n_kv) atomicOr(&sm.bm[0][b >> 5], 1u << (b & 31));
-      }
-      for (int i = lane; i < n1 && i < a.idx_ld; i += 32) {
-        const int b = l1[i];
-        if (b >= 0 && b < a.n_kv) atomicOr(&sm.bm[1][b >> 5], 1u << (b & 31));
-      }
-      __syncwarp();
-      int base = 0;
-      for (int w0 = 0; w0 < words; w0 += 32) {
-        const int w = w0 + lane;
-        const uint32_t b0 = w < words ? sm.bm[0][w] : 0u, b1 = w < words ? sm.bm[1][w] : 0u;
-        uint32_t u = b0 | b1;
-        const int c = __popc(u);
-        int incl = c;
+      int n[2];
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const int y = __shfl_up_sync(0xffffffffu, incl, o);
-          if (lane >= o) incl += y;
-        }
-        int pos = base + incl - c;
-        while (u) {
-          const int bit = __ffs(u) - 1;
-          u &= u - 1;
-          const uint32_t m = ((b0 >> bit) & 1u) | (((b1 >> bit) & 1u) << 1);
-          sm.ulist[buf][pos++] = (uint32_t)(w * 32 + bit) | (m << 16);
-        }
-        base += __shfl_sync(0xffffffffu, incl, 31);
+      for (int s = 0; s < 2; ++s) {
+        const int t = s ? t1 : t0;
+        const int want = min(max(a.num[(size_t)h * a.n_q_ext + t], 0), a.idx_ld);
+        n[s] = min(want, L_MAX);
+        if (want > L_MAX && lane == 0) atomicExch(&g_attn_status, H3B_EINVAL);
+        const int32_t* src = a.idx + ((size_t)h * a.n_q_ext + t) * a.idx_ld;
+        for (int i = lane; i < n[s]; i += 32) sm.list[buf][s][i] = (uint16_t)min(max(src[i], 0), a.n_kv - 1);
       }
+      __syncwarp();
       if (lane == 0) {
-        sm.ucount[buf] = base;
+        sm.cnt[buf][0] = n[0];
+        sm.cnt[buf][1] = n[1];
         mbar_arrive(&sm.list_full[buf]);
       }
       __syncwarp();
-      const int U = base;
+      const int U = max(n[0], n[1]);
       if (lane == 0) {
-        if (!mbar_wait_bounded(&sm.q_empty[buf], (((q_phase >> buf) & 1u) ^ 1u), abort_flag, kLimitNs)) {
+        if (!mbar_wait_bounded(&sm.q_empty, q_phase ^ 1, abort_flag, kLimitNs)) {
           fail();
           ok = false;
         } else {
-          q_phase ^= 1u << buf;
-          mbar_arrive_expect_tx(&sm.q_full[buf], 2 * TILE * D);
+          q_phase ^= 1;
+          mbar_arrive_expect_tx(&sm.q_full, 2 * TILE * D);
           for (int s = 0; s < 2; ++s) {
             const int t = s ? t1 : t0;
-            tma_load_3d(&sm.q[buf][s * TILE * D], &tmQ, 0, (t % a.tpc_q) * TILE, (t / a.tpc_q) * a.heads + h,
-                        &sm.q_full[buf]);
+            tma_load_3d(&sm.q[s][0], &tmQ, 0, (t % a.tpc_q) * TILE, (t / a.tpc_q) * a.heads + h, &sm.q_full);
           }
           for (int j = 0; j < U && ok; ++j) {
-            const int b = (int)(sm.ulist[buf][j] & 0xFFFFu);
-            if (!mbar_wait_bounded(&sm.kv_empty[stage], kv_phase ^ 1, abort_flag, kLimitNs)) {
+            const bool has0 = j < n[0], has1 = j < n[1];
+            const uint32_t bytes = (has0 ? TILE * D : 0) + (has1 ? TILE * D : 0);
+            if (!mbar_wait_bounded(&sm.k_empty[kst], ((k_phase >> kst) & 1u) ^ 1u, abort_flag, kLimitNs)) {
               fail();
               ok = false;
               break;
             }
-            const int y = (b % a.tpc_kv) * TILE, z = (b / a.tpc_kv) * a.heads + h;
-            mbar_arrive_expect_tx(&sm.kv_full[stage], 2 * TILE * D);
-            tma_load_3d(&sm.kv[stage][0][0], &tmK, 0, y, z, &sm.kv_full[stage]);
-            tma_load_3d(&sm.kv[stage][1][0], &tmV, 0, y, z, &sm.kv_full[stage]);
-            if (++stage == KV_STAGES) {
-              stage = 0;
-              kv_phase ^= 1;
+            k_phase ^= 1u << kst;
+            mbar_arrive_expect_tx(&sm.k_full[kst], bytes);
+#pragma unroll
+            for (int s = 0; s < 2; ++s) {
+              if (s ? !has1 : !has0) continue;
+              const int b = sm.list[buf][s][j];
+              tma_load_3d(&sm.k[kst][s][0], &tmK, 0, (b % a.tpc_kv) * TILE, (b / a.tpc_kv) * a.heads + h,
+                          &sm.k_full[kst]);
             }
+            if (++kst == K_STAGES) kst = 0;
+            if (!mbar_wait_bounded(&sm.v_empty[vst], ((v_phase >> vst) & 1u) ^ 1u, abort_flag, kLimitNs)) {
+              fail();
+              ok = false;
+              break;
+            }
+            v_phase ^= 1u << vst;
+            mbar_arrive_expect_tx(&sm.v_full[vst], bytes);
+#pragma unroll
+            for (int s = 0; s < 2; ++s) {
+              if (s ? !has1 : !has0) continue;
+              const int b = sm.list[buf][s][j];
+              tma_load_3d(&sm.v[vst][s][0], &tmV, 0, (b % a.tpc_kv) * TILE, (b / a.tpc_kv) * a.heads + h,
+                          &sm.v_full[vst]);
+            }
+            if (++vst == V_STAGES) vst = 0;
           }
         }
       }
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
     }
-  } else if (warp == 1) {
-    // -------------------------------------------------------------- MMA issuer
+  } else if (warp == 1 || warp == 2) {
+    // -------------------------------------------------------------- MMA issuers: warp 1 even steps, warp 2 odd steps
     if (lane == 0) {
-      const uint32_t idesc_s = idesc_mn(TILE, false);
-      const uint32_t idesc_pv = idesc_mn(D, true);
-      uint32_t list_phase = 0, q_phase = 0, s_phase = 0, p_phase = 0;
-      uint32_t o_phase = 0;
-      int s_stage = 0, vstage = 0;
-      uint32_t s_kvphase = 0, vf_phase = 0;
-      int sbuf_next = 0, pbuf = 0;
+      const int w = warp - 1;
+      const uint32_t idesc_s = idesc_mn(TILE, TILE, false);
+      const uint32_t idesc_pv = idesc_mn(TILE, D, true);
+      uint32_t list_phase = 0, q_phase = 0, s_phase = 0, p_phase = 0, o_phase = 0;
+      uint32_t gbase = 0;  // steps of all earlier items: step j is K-ring use gbase + j
       bool ok = true;
       int it = 0;
       for (int item = blockIdx.x; item < a.items && ok; item += gridDim.x, ++it) {
         const int buf = it & 1;
-        if (!mbar_wait_bounded(&sm.list_full[buf], ((list_phase >> buf) & 1u), abort_flag, kLimitNs)) { fail(); break; }
+        if (!mbar_wait_bounded(&sm.list_full[buf], (list_phase >> buf) & 1u, abort_flag, kLimitNs)) { fail(); break; }
         list_phase ^= 1u << buf;
-        const int U = sm.ucount[buf];
-        if (!mbar_wait_bounded(&sm.q_full[buf], ((q_phase >> buf) & 1u), abort_flag, kLimitNs)) { fail(); break; }
-        q_phase ^= 1u << buf;
+        const int n0 = sm.cnt[buf][0], n1 = sm.cnt[buf][1];
+        const int U = max(n0, n1);
+        if (!mbar_wait_bounded(&sm.q_full, q_phase, abort_flag, kLimitNs)) { fail(); break; }
+        q_phase ^= 1;
         tc_fence_after();
-        const uint64_t dq = desc_k_sw128(smem_addr(&sm.q[buf][0]));
-        // j = -1 issues S(0) only; step j issues S(j+1) (one key tile ahead) and then PV(j)
-        for (int j = -1; j < U; ++j) {
-          if (j + 1 < U) {
-            const int sb = sbuf_next;
-            if (!mbar_wait_bounded(&sm.kv_full[s_stage], s_kvphase, abort_flag, kLimitNs) ||
-                !mbar_wait_bounded(&sm.s_free[sb], (((s_phase >> sb) & 1u) ^ 1u), abort_flag, kLimitNs)) {
+        const uint64_t dq0 = desc_k_sw128(smem_addr(&sm.q[0][0]));
+        const uint64_t dq1 = desc_k_sw128(smem_addr(&sm.q[1][0]));
+        uint32_t started = 0;  // bit s: O of this issuer's parity, query tile s, has been written this item
+        const int last_s = U > w ? w + ((U - 1 - w) / 2) * 2 : -1;  // this issuer's last step
+        if (last_s < 0) tc_commit(&sm.q_empty);
+        // j = w - 2 issues S(w) only; step j issues S(j+2) (into S buffer w, once warpgroup w has read S(j)) and then
+        // PV(j)
+        for (int j = w - 2; j < U; j += 2) {
+          const int js = j + 2;
+          if (js < U) {
+            const uint32_t g = gbase + (uint32_t)js;
+            const int kst = (int)(g % K_STAGES);
+            if (!mbar_wait_bounded(&sm.s_free[w], (s_phase & 1u) ^ 1u, abort_flag, kLimitNs) ||
+                !mbar_wait_bounded(&sm.k_full[kst], (g / K_STAGES) & 1u, abort_flag, kLimitNs)) {
               fail();
               ok = false;
               break;
             }
-            s_phase ^= 1u << sb;
+            s_phase ^= 1;
             tc_fence_after();
-            const uint64_t dk = desc_k_sw128(smem_addr(&sm.kv[s_stage][0][0]));
 #pragma unroll
-            for (int i = 0; i < 4; ++i) mma_e4m3(tmem + COL_S + sb * TILE, dq + 2 * i, dk + 2 * i, idesc_s, i != 0);
-            tc_commit(&sm.s_full[sb]);
-            tc_commit(&sm.kv_empty[s_stage]);  // the K half of the stage is consumed
-            sbuf_next ^= 1;
-            if (++s_stage == KV_STAGES) {
-              s_stage = 0;
-              s_kvphase ^= 1;
+            for (int s = 0; s < 2; ++s) {
+              if (js >= (s ? n1 : n0)) continue;
+              const uint32_t lo = s ? LANE_B : 0u;
+              const uint64_t dk = desc_k_sw128(smem_addr(&sm.k[kst][s][0]));
+              const uint64_t dq = s ? dq1 : dq0;
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                mma_e4m3(tmem + lo + COL_S + 64 * w, dq + 2 * i, dk + 2 * i, idesc_s, i != 0);
             }
+            tc_commit(&sm.s_full[w]);
+            tc_commit(&sm.k_empty[kst]);  // the K tiles of the stage are consumed
+            if (js == last_s) tc_commit(&sm.q_empty);
           }
-          if (j < 0) continue;
-          if (j == U - 1) tc_commit(&sm.q_empty[buf]);
-          if (j == 0) {
+          if (j < w) continue;
+          if (j == w) {
             if (!mbar_wait_bounded(&sm.o_empty, o_phase ^ 1, abort_flag, kLimitNs)) { fail(); ok = false; break; }
             o_phase ^= 1;
           }
-          if (!mbar_wait_bounded(&sm.p_full[pbuf], ((p_phase >> pbuf) & 1u), abort_flag, kLimitNs)) { fail(); ok = false; break; }
-          p_phase ^= 1u << pbuf;
-          if (!mbar_wait_bounded(&sm.vf_full[vstage], vf_phase, abort_flag, kLimitNs)) { fail(); ok = false; break; }
-          tc_fence_after();
-          const uint64_t dv = desc_mn_sw128(smem_addr(&sm.vf[vstage][0][0]), TILE * 128);
-#pragma unroll
-          for (int i = 0; i < 4; ++i)  // K = 16 keys per MMA: 8 TMEM columns of P, 16 rows (2048 bytes) of V'
-            mma_f16_ts(tmem + COL_O, tmem + COL_P + pbuf * 32 + 8 * i, dv + (uint64_t)((i * 16 * 128) >> 4),
-                       idesc_pv, (j | i) != 0);
-          tc_commit(&sm.vf_empty[vstage]);
-          tc_commit(&sm.pv_done);
-          pbuf ^= 1;
-          if (++vstage == VF_STAGES) {
-            vstage = 0;
-            vf_phase ^= 1;
+          if (!mbar_wait_bounded(&sm.p_full[w], p_phase & 1u, abort_flag, kLimitNs)) {  // P and V' of step j ready
+            fail();
+            ok = false;
+            break;
           }
+          p_phase ^= 1;
+          tc_fence_after();
+#pragma unroll
+          for (int s = 0; s < 2; ++s) {
+            if (j >= (s ? n1 : n0)) continue;
+            const uint32_t lo = s ? LANE_B : 0u;
+            const uint64_t dv = desc_mn_sw128(smem_addr(&sm.vf[w][s][0][0]), TILE * 128);
+            const uint32_t bit = 1u << s;
+#pragma unroll
+            for (int i = 0; i < 4; ++i)  // K = 16 keys per MMA: 8 TMEM columns of P, 16 rows (2048 bytes) of V'
+              mma_f16_ts(tmem + lo + COL_O + 128 * w, tmem + lo + COL_P + 32 * w + 8 * i,
+                         dv + (uint64_t)((i * 16 * 128) >> 4), idesc_pv, ((started & bit) || i) ? 1u : 0u);
+            started |= bit;
+          }
+          tc_commit(&sm.pv_done[w]);
         }
         if (!ok) break;
-        if (U == 0) {
-          tc_commit(&sm.q_empty[buf]);
+        if (U <= w) {  // no step of this parity: O of this parity is not used, but the epilogue waits for both
           if (!mbar_wait_bounded(&sm.o_empty, o_phase ^ 1, abort_flag, kLimitNs)) { fail(); break; }
           o_phase ^= 1;
         }
+        gbase += (uint32_t)U;
         tc_commit(&sm.o_full);
         mbar_arrive(&sm.list_empty[buf]);
       }
-      tc_commit(&sm.drain);
+      tc_commit(&sm.drain[w]);
       volatile int no_abort = 0;
-      if (!mbar_wait_bounded(&sm.drain, 0, &no_abort, kLimitNs)) fail();
-    }
-  } else if (warp < 2 + CONV_WARPS) {
-    // -------------------------------------------------------------- V converters: E4M3 -> f16 V' = v * sv_b/sv_head
-    const int ct = (warp - 2) * 32 + lane;
-    uint32_t list_phase = 0;
-    int stage = 0, vstage = 0;
-    uint32_t kv_phase = 0, vf_phase = 0;
-    bool ok = true;
-    int it = 0;
-    for (int item = blockIdx.x; item < a.items && ok; item += gridDim.x, ++it) {
-      const int buf = it & 1;
-      const int h = item / pairs;
-      if (!warp_wait(&sm.list_full[buf], ((list_phase >> buf) & 1u))) break;
-      list_phase ^= 1u << buf;
-      const int U = sm.ucount[buf];
-      const float inv_vhead = 1.f / a.vs_head[h];
-      float vs_next = U > 0 ? a.vs[(size_t)h * a.kv_scale_ld + (sm.ulist[buf][0] & 0xFFFFu)] : 0.f;
-      for (int j = 0; j < U; ++j) {
-        const __half2 r2 = __float2half2_rn(vs_next * inv_vhead);
-        const uint32_t scale2 = *reinterpret_cast<const uint32_t*>(&r2);
-        if (j + 1 < U) vs_next = a.vs[(size_t)h * a.kv_scale_ld + (sm.ulist[buf][j + 1] & 0xFFFFu)];
-        if (!warp_wait(&sm.kv_full[stage], kv_phase)) { ok = false; break; }
-        if (!warp_wait(&sm.vf_empty[vstage], vf_phase ^ 1)) { ok = false; break; }
-        const uint8_t* src = &sm.kv[stage][1][0];
-        uint8_t* dst = &sm.vf[vstage][0][0];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int u = ct + 128 * i;
-          const int key = u >> 3, c = u & 7;  // 16 E4M3 values: d = 16c .. 16c+15
-          const uint4 raw = *reinterpret_cast<const uint4*>(src + key * 128 + ((c ^ (key & 7)) << 4));
-          const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-          uint32_t f[8];
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            f[2 * q] = e4m3x2_to_f16x2_scaled((uint16_t)(w[q] & 0xFFFFu), scale2);
-            f[2 * q + 1] = e4m3x2_to_f16x2_scaled((uint16_t)(w[q] >> 16), scale2);
-          }
-          uint8_t* half_base = dst + (c >> 2) * (TILE * 128) + key * 128;
-          const int dc0 = (c & 3) * 2;
-          *reinterpret_cast<uint4*>(half_base + ((dc0 ^ (key & 7)) << 4)) = make_uint4(f[0], f[1], f[2], f[3]);
-          *reinterpret_cast<uint4*>(half_base + (((dc0 + 1) ^ (key & 7)) << 4)) = make_uint4(f[4], f[5], f[6], f[7]);
-        }
-        fence_proxy_async_smem();  // the generic-proxy stores become visible to the tensor core
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&sm.vf_full[vstage]);
-          mbar_arrive(&sm.kv_empty[stage]);
-        }
-        if (++stage == KV_STAGES) {
-          stage = 0;
-          kv_phase ^= 1;
-        }
-        if (++vstage == VF_STAGES) {
-          vstage = 0;
-          vf_phase ^= 1;
-        }
-      }
-      if (!ok) break;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.list_empty[buf]);
+      if (!mbar_wait_bounded(&sm.drain[w], 0, &no_abort, kLimitNs)) fail();
     }
   } else {
-    // -------------------------------------------------------------- softmax + epilogue (warps 6..9)
-    const int q4 = warp & 3;       // a warp reaches only the TMEM lanes 32*(warp%4) .. +31
-    const int r = q4 * 32 + lane;  // query row of the item = TMEM lane
+    // -------------------------------------------------------------- softmax (steps of parity w) + epilogue
+    const int w = (warp - 3) >> 2;               // warpgroup: 0 = even steps, 1 = odd steps
+    const int q4 = warp & 3;                     // TMEM lane quarter this warp may access
+    const int tsel = lane >> 4;                  // 0: query tile t0 (lanes 0-15), 1: t1 (lanes 16-31)
+    const int rt = 16 * q4 + (lane & 15);        // row within the query tile
+    const int tl = q4 * 32 + lane;               // TMEM lane
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
-    const uint32_t my_bit = r < TILE ? 1u : 2u;  // warp-uniform
-    uint32_t list_phase = 0, s_phase = 0;
-    uint32_t o_phase = 0;
-    uint32_t pv_count = 0;
-    int sbuf = 0, pbuf = 0;
+    uint32_t list_phase = 0, s_phase = 0, ml_phase = 0, o_phase = 0;
+    uint32_t pv_count = 0;  // PV MMAs of this warpgroup's parity issued so far (all items)
+    uint32_t gbase = 0;     // steps of all earlier items: step j of this item is ring use gbase + j
     int it = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < a.items && ok; item += gridDim.x, ++it) {
       const int buf = it & 1;
       const int h = item / pairs, p = item - h * pairs;
-      const int tq = r < TILE ? 2 * p : 2 * p + 1;
-      const int rr = r & (TILE - 1);
-      if (!warp_wait(&sm.list_full[buf], ((list_phase >> buf) & 1u))) break;
+      const int tq = 2 * p + tsel;
+      if (!warp_wait(&sm.list_full[buf], (list_phase >> buf) & 1u)) break;
       list_phase ^= 1u << buf;
-      const int U = sm.ucount[buf];
+      const int n_me = sm.cnt[buf][tsel];
+      const int U = max(sm.cnt[buf][0], sm.cnt[buf][1]);
       const float qcoef = a.coef * (a.qs ? a.qs[(size_t)h * a.q_scale_ld + tq] : 1.f);
+      const float* ksh = a.ks ? a.ks + (size_t)h * a.kv_scale_ld : nullptr;
+      const float* vsh = a.vs + (size_t)h * a.kv_scale_ld;
+      const int n0 = sm.cnt[buf][0], n1 = sm.cnt[buf][1];
+      const float inv_vhead = 1.f / a.vs_head[h];
       float m_ref = -INFINITY, l = 0.f;
-      // per-tile scalars of key tile j+1 are loaded while tile j is processed (global loads off the critical path)
+      // per-tile scalars of this warpgroup's next key tile are loaded one step ahead (global loads off the critical
+      // path; their values are only used in the next iteration)
       int vbs_next = 0;
-      float ks_next = 1.f;
-      if (U > 0) {
-        const int b0 = (int)(sm.ulist[buf][0] & 0xFFFFu);
+      float ks_next = 1.f, vs_next = 0.f;
+      if (w < n_me) {
+        const int b0 = sm.list[buf][tsel][w];
         vbs_next = a.vbs_kv[b0];
-        if (a.ks) ks_next = a.ks[(size_t)h * a.kv_scale_ld + b0];
+        vs_next = vsh[b0];
+        if (ksh) ks_next = ksh[b0];
       }
-      for (int j = 0; j < U; ++j) {
-        const uint32_t e = sm.ulist[buf][j];
-        const bool member = (e >> 16) & my_bit;
-        const int vbs_j = vbs_next;
-        const float ks_j = ks_next;
-        if (j + 1 < U) {
-          const int bn = (int)(sm.ulist[buf][j + 1] & 0xFFFFu);
+      for (int j = w; j < U; j += 2) {
+        const bool valid = j < n_me;
+        const int vbs_j = valid ? vbs_next : 0;
+        const float ks_j = ks_next, vs_j = vs_next;
+        if (j + 2 < n_me) {
+          const int bn = sm.list[buf][tsel][j + 2];
           vbs_next = a.vbs_kv[bn];
-          if (a.ks) ks_next = a.ks[(size_t)h * a.kv_scale_ld + bn];
+          vs_next = vsh[bn];
+          if (ksh) ks_next = ksh[bn];
         }
-        if (!warp_wait(&sm.s_full[sbuf], ((s_phase >> sbuf) & 1u))) { ok = false; break; }
-        s_phase ^= 1u << sbuf;
+        const uint32_t g = gbase + (uint32_t)j;
+        const int stage = (int)(g % V_STAGES);
+        // ---- softmax of step j
+        if (!warp_wait(&sm.s_full[w], (s_phase >> w) & 1u)) { ok = false; break; }
+        s_phase ^= 1u << w;
         tc_fence_after();
         uint32_t sr[64];
-        tmem_ld_32cols(tmem + lane_off + COL_S + sbuf * TILE, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-        tmem_ld_32cols(tmem + lane_off + COL_S + sbuf * TILE + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+        tmem_ld_32cols(tmem + lane_off + COL_S + 64 * w, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+        tmem_ld_32cols(tmem + lane_off + COL_S + 64 * w + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
         tmem_ld_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.s_free[sbuf]);
-        sbuf ^= 1;
-        const int kv_valid = member ? vbs_j : 0;
-        if (kv_valid < TILE) {
+        if (lane == 0) mbar_arrive(&sm.s_free[w]);
+        if (__any_sync(0xffffffffu, vbs_j < TILE)) {
 #pragma unroll
           for (int c = 0; c < 64; ++c)
-            if (c >= kv_valid) sr[c] = __float_as_uint(-INFINITY);
+            if (c >= vbs_j) sr[c] = __float_as_uint(-INFINITY);
         }
         const float coef = qcoef * ks_j;
         float m8[8];
@@ -520,8 +484,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int c = 8; c < 64; ++c) m8[c & 7] = fmaxf(m8[c & 7], __uint_as_float(sr[c]));
         const float mraw = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
                                  fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
-        const float mx = mraw * coef;  // coef > 0
-        // lazy rescale: the running maximum moves only when this tile's maximum exceeds it by more than 2^4
+        const float mx = mraw == -INFINITY ? -INFINITY : mraw * coef;  // coef > 0
         const bool grow = mx > m_ref + RESCALE_LOG2;
         const bool had_mass = m_ref != -INFINITY;
         float alpha = 1.f;
@@ -530,16 +493,17 @@ __global__ void __launch_bounds__(THREADS, 1)
           m_ref = mx;
         }
         if (__any_sync(0xffffffffu, grow && had_mass)) {
-          if (j > 0 && !warp_wait(&sm.pv_done, (pv_count - 1) & 1)) { ok = false; break; }
+          // the previous PV of this parity must have landed in O before O is rescaled
+          if (pv_count > 0 && !warp_wait(&sm.pv_done[w], (pv_count - 1) & 1u)) { ok = false; break; }
           tc_fence_after();
 #pragma unroll 1
           for (int c0 = 0; c0 < D; c0 += 32) {
             uint32_t o[32];
-            tmem_ld_32cols(tmem + lane_off + COL_O + c0, o);
+            tmem_ld_32cols(tmem + lane_off + COL_O + 128 * w + c0, o);
             tmem_ld_wait();
 #pragma unroll
             for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-            tmem_st_32cols(tmem + lane_off + COL_O + c0, o);
+            tmem_st_32cols(tmem + lane_off + COL_O + 128 * w + c0, o);
           }
           tmem_st_wait();
         }
@@ -551,11 +515,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         } else {
           const float nb = -m_ref;
           uint32_t acc[4] = {0u, 0u, 0u, 0u};
+          const __half2 vr2 = __float2half2_rn(vs_j * inv_vhead);  // P' = P * sv_b / sv_head: V' is V8 itself
+          const uint32_t vr = *reinterpret_cast<const uint32_t*>(&vr2);
 #pragma unroll
           for (int c = 0; c < 32; ++c) {
-            pw[c] = ex2_f16x2(fmaf(__uint_as_float(sr[2 * c]), coef, nb),
-                              fmaf(__uint_as_float(sr[2 * c + 1]), coef, nb));
-            acc[c & 3] = hadd2(acc[c & 3], pw[c]);
+            const uint32_t e = ex2_f16x2(fmaf(__uint_as_float(sr[2 * c]), coef, nb),
+                                         fmaf(__uint_as_float(sr[2 * c + 1]), coef, nb));
+            acc[c & 3] = hadd2(acc[c & 3], e);
+            pw[c] = hmul2(e, vr);
           }
           const float2 s0 = __half22float2(*reinterpret_cast<const __half2*>(&acc[0]));
           const float2 s1 = __half22float2(*reinterpret_cast<const __half2*>(&acc[1]));
@@ -563,42 +530,97 @@ __global__ void __launch_bounds__(THREADS, 1)
           const float2 s3 = __half22float2(*reinterpret_cast<const __half2*>(&acc[3]));
           l += ((s0.x + s0.y) + (s1.x + s1.y)) + ((s2.x + s2.y) + (s3.x + s3.y));
         }
-        tmem_st_32cols(tmem + lane_off + COL_P + pbuf * 32, pw);
+        // this warpgroup's previous PV (step j-2) reads the P and V' buffers this step overwrites: it was issued when
+        // that step ended and has normally completed while P was computed
+        if (pv_count > 0 && !warp_wait(&sm.pv_done[w], (pv_count - 1) & 1u)) { ok = false; break; }
+        tmem_st_32cols(tmem + lane_off + COL_P + 32 * w, pw);
+        // ---- V' of this step
+        if (!warp_wait(&sm.v_full[stage], (g / V_STAGES) & 1u)) { ok = false; break; }
+#pragma unroll
+        for (int s = 0; s < 2; ++s) {
+          if (j >= (s ? n1 : n0)) continue;  // warpgroup-uniform
+          const uint8_t* src = &sm.v[stage][s][0];
+          uint8_t* dst = &sm.vf[w][s][0][0];
+#pragma unroll
+          for (int i = 0; i < (TILE * 8) / 128; ++i) {
+            // 16 E4M3 values (d = 16c .. 16c+15) of one key per thread; a warp covers 8 consecutive keys x 4 chunks,
+            // so its 16-byte loads and stores each touch every bank group four times (no bank conflicts)
+            const int key = (lane & 7) + 8 * (q4 + 4 * (i & 1)), c = (lane >> 3) + 4 * (i >> 1);
+            const uint4 raw = *reinterpret_cast<const uint4*>(src + key * 128 + ((c ^ (key & 7)) << 4));
+            const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
+            uint32_t f[8];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              f[2 * q] = e4m3x2_to_f16x2((uint16_t)(wv[q] & 0xFFFFu));
+              f[2 * q + 1] = e4m3x2_to_f16x2((uint16_t)(wv[q] >> 16));
+            }
+            uint8_t* half_base = dst + (c >> 2) * (TILE * 128) + key * 128;
+            const int dc0 = (c & 3) * 2;
+            *reinterpret_cast<uint4*>(half_base + ((dc0 ^ (key & 7)) << 4)) = make_uint4(f[0], f[1], f[2], f[3]);
+            *reinterpret_cast<uint4*>(half_base + (((dc0 + 1) ^ (key & 7)) << 4)) =
+                make_uint4(f[4], f[5], f[6], f[7]);
+          }
+        }
+        fence_proxy_async_smem();  // the generic-proxy stores become visible to the tensor core
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.p_full[pbuf]);
-        pbuf ^= 1;
+        if (lane == 0) {
+          mbar_arrive(&sm.v_empty[stage]);  // the V tiles are consumed
+          mbar_arrive(&sm.p_full[w]);        // P of step j in TMEM and V' of step j in shared memory
+        }
         ++pv_count;
       }
       if (!ok) break;
+      gbase += (uint32_t)U;
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.list_empty[buf]);
+      // merge the two warpgroups' partial results: exchange (max, sum) per row through shared memory
+      const int par = it & 1;
+      sm.ml[par][0][w][tl] = m_ref;
+      sm.ml[par][1][w][tl] = l;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.ml_bar);
+      if (!warp_wait(&sm.ml_bar, ml_phase)) break;
+      ml_phase ^= 1;
+      float mw[2], lw[2];
+      mw[w] = m_ref;
+      lw[w] = l;
+      mw[w ^ 1] = sm.ml[par][0][w ^ 1][tl];
+      lw[w ^ 1] = sm.ml[par][1][w ^ 1][tl];
+      const float M = fmaxf(mw[0], mw[1]);
+      const float f0 = (M == -INFINITY || mw[0] == -INFINITY) ? 0.f : ex2(mw[0] - M);
+      const float f1 = (M == -INFINITY || mw[1] == -INFINITY) ? 0.f : ex2(mw[1] - M);
+      const float L = lw[0] * f0 + lw[1] * f1;
       if (!warp_wait(&sm.o_full, o_phase)) break;
       o_phase ^= 1;
       tc_fence_after();
       const float vhead = a.vs_head[h];
-      const float oscale = l > 0.f ? vhead / l : 0.f;
-      const bool row_ok = rr < a.vbs_q[tq];
+      const float oscale = L > 0.f ? vhead / L : 0.f;
+      const bool row_ok = rt < a.vbs_q[tq];
       const size_t orow =
-          (size_t)((tq / a.tpc_q) * a.heads + h) * (size_t)a.rows_chunk_q + (size_t)(tq % a.tpc_q) * TILE + rr;
+          (size_t)((tq / a.tpc_q) * a.heads + h) * (size_t)a.rows_chunk_q + (size_t)(tq % a.tpc_q) * TILE + rt;
       bf16* dst = a.out + orow * D;
+      const float g0 = f0 * oscale, g1 = f1 * oscale;
 #pragma unroll 1
-      for (int c0 = 0; c0 < D; c0 += 32) {
-        uint32_t o[32];
-        tmem_ld_32cols(tmem + lane_off + COL_O + c0, o);
+      for (int c0 = 64 * w; c0 < 64 * w + 64; c0 += 32) {  // warpgroup w writes output columns 64w .. 64w+63
+        uint32_t o0[32], o1[32];
+        tmem_ld_32cols(tmem + lane_off + COL_O + c0, o0);
+        tmem_ld_32cols(tmem + lane_off + COL_O + 128 + c0, o1);
         tmem_ld_wait();
         if (row_ok) {
 #pragma unroll
           for (int c = 0; c < 32; c += 8) {
-            float f[8];
+            float fv[8];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) f[u] = l > 0.f ? __uint_as_float(o[c + u]) * oscale : 0.f;
-            store8(dst + c0 + c, f);
+            for (int u = 0; u < 8; ++u)  // a partial with no mass contributes nothing (its O may be stale)
+              fv[u] = (g0 != 0.f ? __uint_as_float(o0[c + u]) * g0 : 0.f) +
+                      (g1 != 0.f ? __uint_as_float(o1[c + u]) * g1 : 0.f);
+            store8(dst + c0 + c, fv);
           }
         }
       }
-      if (a.lse && row_ok) a.lse[orow] = l > 0.f ? m_ref + __log2f(l) : -INFINITY;
+      if (a.lse && row_ok && w == 0) a.lse[orow] = L > 0.f ? M + __log2f(L) : -INFINITY;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.o_empty);
@@ -612,9 +634,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
-}
 #undef fail
 #undef warp_wait
+}
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
