@@ -41,6 +41,19 @@ constexpr float kFp4Range = 448.f * 6.f;              // largest |x| reachable a
 constexpr float kMinScaleFp4 = 1e-12f;
 
 // Eight bf16 from one 16-byte load, widened to fp32.
+// 8 bf16 as raw bits (a prefetch: nothing waits on the load until unpack8 reads the registers)
+__device__ __forceinline__ uint4 ld8_raw(const bf16* p) { return *reinterpret_cast<const uint4*>(p); }
+
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
 __device__ __forceinline__ void load8(const bf16* p, float (&f)[8]) {
   uint4 u = *reinterpret_cast<const uint4*>(p);
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);

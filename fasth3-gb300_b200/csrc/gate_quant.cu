@@ -32,15 +32,28 @@ struct GateArgs {
   int64_t rows;
 };
 
+// Persistent CTAs: a CTA walks rows r, r + grid, ...; the next row's attention output is loaded (its slot one more row
+// ahead) while the current row is reduced and quantized. The per-row arithmetic is unchanged.
 template <int W, bool GATE, bool FP4, bool MERGE>
-__global__ void __launch_bounds__(W / 8) gate_quant_kernel(const GateArgs p) {
+__global__ void __launch_bounds__(W / 8, 2) gate_quant_kernel(const GateArgs p) {
   constexpr int NW = W / 8 / 32, H = W / D;
   __shared__ float stage[32];
-  const int64_t r = blockIdx.x;
   const int t = threadIdx.x, h = t / (D / 8), d0 = (t % (D / 8)) * 8;
-  const int sl = p.slot[r];
+  int64_t r = blockIdx.x;
+  if (r >= p.rows) return;
+  const int64_t g = gridDim.x;
+  int sl_next = p.slot[r];
+  uint4 on = ld8_raw(p.ob + ((size_t)h * p.rows_pad + sl_next) * D + d0);
+  int sl_next2 = r + g < p.rows ? p.slot[r + g] : 0;
+  for (; r < p.rows; r += g) {
+  const int sl = sl_next;
   float o[8];
-  load8(p.ob + ((size_t)h * p.rows_pad + sl) * D + d0, o);
+  unpack8(on, o);
+  if (r + g < p.rows) {
+    sl_next = sl_next2;
+    on = ld8_raw(p.ob + ((size_t)h * p.rows_pad + sl_next) * D + d0);
+    if (r + 2 * g < p.rows) sl_next2 = p.slot[r + 2 * g];
+  }
   if constexpr (MERGE) {
     float od[8];
     load8(p.o1 + ((size_t)r * H + h) * D + d0, od);
@@ -88,11 +101,16 @@ __global__ void __launch_bounds__(W / 8) gate_quant_kernel(const GateArgs p) {
     *reinterpret_cast<uint2*>(p.a + r * W + t * 8) = u;
     if (t == 0) p.sa[r] = s;
   }
+  }
 }
 
 template <int W>
 int launch(const GateArgs& p, bool gate, bool fp4, bool merge, cudaStream_t st) {
-  const dim3 grid((unsigned)p.rows), block(W / 8);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t resident = (int64_t)sms * 2;  // two resident CTAs per SM (the launch bounds)
+  const dim3 grid((unsigned)(p.rows < resident ? p.rows : resident)), block(W / 8);
 #define H3B_GQ(G, Q, M) gate_quant_kernel<W, G, Q, M><<<grid, block, 0, st>>>(p)
   if (gate) {
     if (fp4) { if (merge) H3B_GQ(true, true, true); else H3B_GQ(true, true, false); }

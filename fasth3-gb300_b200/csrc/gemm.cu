@@ -224,16 +224,16 @@ __global__ void __launch_bounds__(192, 1)
           if constexpr (FP4) {
             const uint32_t sSFA = smem_addr(sB + C::kBBytes);
             const uint32_t sSFB = sSFA + C::kSfaBytes;
+            // each 64-deep K block: its three scale-factor copies, then its MMA (copies and MMAs share the tensor
+            // pipe; the copy cost is set by the bytes written to TMEM, the scale atoms being replicated four times)
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               tmem_cp_32x128_x4(tmem + C::kSfaCol + 4 * i, desc_sf_atom(sSFA + 512 * i));
               tmem_cp_32x128_x4(tmem + C::kSfbCol + 8 * i, desc_sf_atom(sSFB + 512 * i));
               tmem_cp_32x128_x4(tmem + C::kSfbCol + 8 * i + 4, desc_sf_atom(sSFB + 2048 + 512 * i));
-            }
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
               mma_nvf4(d, da + 2 * i, db + 2 * i, idesc, (kb | i) != 0, tmem + C::kSfaCol + 4 * i,
                        tmem + C::kSfbCol + 8 * i + sfb_shift);
+            }
           } else {
 #pragma unroll
             for (int i = 0; i < 4; ++i) mma_e4m3(d, da + 2 * i, db + 2 * i, idesc, (kb | i) != 0);

@@ -31,94 +31,223 @@ struct RowArgs {
   int64_t rows;
 };
 
-// One CTA per row, C/8 threads, thread t owns elements [8t, 8t+8).
+// Persistent CTAs of C/8 threads, thread t owns elements [8t, 8t+8) of a row; a CTA walks rows r, r + grid, ... and
+// loads the next row while it reduces and quantizes the current one (the per-row arithmetic is unchanged).
 template <int C, bool BRANCH, int NORM, bool FP4>
-__global__ void __launch_bounds__(C / 8) resid_norm_quant_kernel(const RowArgs a) {
+__global__ void __launch_bounds__(C / 8, 2) resid_norm_quant_kernel(const RowArgs a) {
   constexpr int NW = C / 8 / 32;
   __shared__ float stage[32];
   const int t = threadIdx.x;
-  const int64_t r = blockIdx.x;
-  const int64_t tab = a.idx ? (int64_t)a.idx[r] : 0;
-  float v[8];
-  load8(a.x + r * C + t * 8, v);
-  if constexpr (BRANCH) {
-    float b[8], g[8];
-    load8(a.y + r * C + t * 8, b);
-    load8(a.gate + tab * a.gate_ld + t * 8, g);
-    const float s = a.sy[r];
+  int64_t r = blockIdx.x;
+  if (r >= a.rows) return;
+  uint4 vn = ld8_raw(a.x + r * C + t * 8), bn = make_uint4(0u, 0u, 0u, 0u);
+  if constexpr (BRANCH) bn = ld8_raw(a.y + r * C + t * 8);
+  for (; r < a.rows; r += gridDim.x) {
+    const int64_t tab = a.idx ? (int64_t)a.idx[r] : 0;
+    float v[8], b[8];
+    unpack8(vn, v);
+    if constexpr (BRANCH) unpack8(bn, b);
+    const int64_t rn = r + gridDim.x;
+    if (rn < a.rows) {
+      vn = ld8_raw(a.x + rn * C + t * 8);
+      if constexpr (BRANCH) bn = ld8_raw(a.y + rn * C + t * 8);
+    }
+    if constexpr (BRANCH) {
+      float g[8];
+      load8(a.gate + tab * a.gate_ld + t * 8, g);
+      const float s = a.sy[r];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = to_bf16_and_back(v[i] + g[i] * (s * b[i]));
-    store8(a.xo + r * C + t * 8, v);
-  }
-  if constexpr (NORM == H3B_NORM_NONE) {
-    return;
-  } else {
-    float sc[8], sf[8];
-    load8(a.scale + tab * a.tab_ld + t * 8, sc);
-    load8(a.shift + tab * a.tab_ld + t * 8, sf);
-    float am = 0.f;
-    if constexpr (NORM == H3B_NORM_RMS) {
-      float wv[8];
-      load8(a.nw + t * 8, wv);
-      float ss = 0.f;
+      for (int i = 0; i < 8; ++i) v[i] = to_bf16_and_back(v[i] + g[i] * (s * b[i]));
+      store8(a.xo + r * C + t * 8, v);
+    }
+    if constexpr (NORM != H3B_NORM_NONE) {
+      float sc[8], sf[8];
+      load8(a.scale + tab * a.tab_ld + t * 8, sc);
+      load8(a.shift + tab * a.tab_ld + t * 8, sf);
+      float am = 0.f;
+      if constexpr (NORM == H3B_NORM_RMS) {
+        float wv[8];
+        load8(a.nw + t * 8, wv);
+        float ss = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
-      ss = block_allreduce<NW, false>(ss, stage);
-      const float rs = rsqrtf(ss / C + a.eps);
+        for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
+        ss = block_allreduce<NW, false>(ss, stage);
+        const float rs = rsqrtf(ss / C + a.eps);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        v[i] = v[i] * rs * wv[i] * (1.f + sc[i]) + sf[i];
-        am = fmaxf(am, fabsf(v[i]));
+        for (int i = 0; i < 8; ++i) {
+          v[i] = v[i] * rs * wv[i] * (1.f + sc[i]) + sf[i];
+          am = fmaxf(am, fabsf(v[i]));
+        }
+      } else {  // LayerNorm without affine parameters, two passes over the registers
+        float s1 = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) s1 += v[i];
+        const float mean = block_allreduce<NW, false>(s1, stage) / C;
+        float s2 = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          v[i] -= mean;
+          s2 += v[i] * v[i];
+        }
+        const float rs = rsqrtf(block_allreduce<NW, false>(s2, stage) / C + a.eps);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          v[i] = v[i] * rs * (1.f + sc[i]) + sf[i];
+          am = fmaxf(am, fabsf(v[i]));
+        }
       }
-    } else {  // LayerNorm without affine parameters, two passes over the registers
-      float s1 = 0.f;
+      am = block_allreduce<NW, true>(am, stage);
+      if constexpr (FP4) {
+        const float s = fmaxf(am / kFp4Range, kMinScaleFp4);
+        const float gs = 1.f / s;
+        // a 16-element block spans lanes t and t^1
+        float vmax = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) vmax = fmaxf(vmax, fabsf(v[i]));
+        vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
+        uint32_t bits;
+        const float m = nvfp4_block_scale(vmax, gs, &bits);
+        const uint32_t lo = e2m1x4(v[0] * m, v[1] * m, v[2] * m, v[3] * m);
+        const uint32_t hi = e2m1x4(v[4] * m, v[5] * m, v[6] * m, v[7] * m);
+        *reinterpret_cast<uint32_t*>(a.h + r * (C / 2) + t * 4) = lo | (hi << 16);
+        if ((t & 1) == 0) a.hsf[sf_atom_offset(r, t >> 1, C / 16)] = (uint8_t)bits;
+        if (t == 0) a.hs[r] = s;
+      } else {
+        const float s = fmaxf(am / kFp8Max, kMinScaleFp8);
+        const float inv = 1.f / s;
+        uint2 o;
+        o.x = e4m3x4(v[0] * inv, v[1] * inv, v[2] * inv, v[3] * inv);
+        o.y = e4m3x4(v[4] * inv, v[5] * inv, v[6] * inv, v[7] * inv);
+        *reinterpret_cast<uint2*>(a.h + r * C + t * 8) = o;
+        if (t == 0) a.hs[r] = s;
+      }
+    }
+  }
+}
+
+// LayerNorm variant (no reference counterpart; BASELINE's norm1/norm2 and the affine norm3 given as a table): one
+// warp per row, lane l owns the 8-element chunks l, l+32, l+64, ... (coalesced); the row is staged in shared memory
+// (bf16) by asynchronous copies. Row sums are a sequential float32 sum over a lane's chunks (chunk-major, elements in
+// order) followed by the warp butterfly: no block barriers, so many rows are in flight per SM.
+constexpr int LN_WARPS = 8;
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
+               "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+template <int C, bool BRANCH, bool FP4>
+__global__ void __launch_bounds__(LN_WARPS * 32) layer_norm_quant_warp_kernel(const RowArgs a) {
+  constexpr int J = C / 256;  // chunks per lane
+  extern __shared__ __align__(16) uint8_t ln_smem[];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  bf16* row = reinterpret_cast<bf16*>(ln_smem) + (size_t)wid * C;
+  const int64_t warps = (int64_t)gridDim.x * LN_WARPS;
+  for (int64_t r = (int64_t)blockIdx.x * LN_WARPS + wid; r < a.rows; r += warps) {
+    const int64_t tab = a.idx ? (int64_t)a.idx[r] : 0;
+    __syncwarp();  // the previous row's reads of the buffer are done
+#pragma unroll 4
+    for (int j = 0; j < J; ++j) cp_async16(row + (lane + 32 * j) * 8, a.x + r * C + (lane + 32 * j) * 8);
+    cp_async_wait_all();
+    __syncwarp();
+    if constexpr (BRANCH) {
+      const float sy = a.sy[r];
+#pragma unroll 2
+      for (int j = 0; j < J; ++j) {
+        const int c = (lane + 32 * j) * 8;
+        float v[8], b[8], g[8];
+        unpack8(*reinterpret_cast<const uint4*>(row + c), v);
+        load8(a.y + r * C + c, b);
+        load8(a.gate + tab * a.gate_ld + c, g);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = to_bf16_and_back(v[i] + g[i] * (sy * b[i]));
+        store8(a.xo + r * C + c, v);
+        store8(row + c, v);  // v is bf16-exact
+      }
+    }
+    float s1 = 0.f;
+#pragma unroll 4
+    for (int j = 0; j < J; ++j) {
+      float v[8];
+      unpack8(*reinterpret_cast<const uint4*>(row + (lane + 32 * j) * 8), v);
 #pragma unroll
       for (int i = 0; i < 8; ++i) s1 += v[i];
-      const float mean = block_allreduce<NW, false>(s1, stage) / C;
-      float s2 = 0.f;
+    }
+    const float mean = warp_allreduce<false>(s1) / C;
+    float s2 = 0.f;
+#pragma unroll 4
+    for (int j = 0; j < J; ++j) {
+      float v[8];
+      unpack8(*reinterpret_cast<const uint4*>(row + (lane + 32 * j) * 8), v);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         v[i] -= mean;
         s2 += v[i] * v[i];
       }
-      const float rs = rsqrtf(block_allreduce<NW, false>(s2, stage) / C + a.eps);
+    }
+    const float rs = rsqrtf(warp_allreduce<false>(s2) / C + a.eps);
+    float am = 0.f;
+#pragma unroll 2
+    for (int j = 0; j < J; ++j) {
+      const int c = (lane + 32 * j) * 8;
+      float v[8], sc[8], sf[8];
+      unpack8(*reinterpret_cast<const uint4*>(row + c), v);
+      load8(a.scale + tab * a.tab_ld + c, sc);
+      load8(a.shift + tab * a.tab_ld + c, sf);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
+        v[i] -= mean;
         v[i] = v[i] * rs * (1.f + sc[i]) + sf[i];
         am = fmaxf(am, fabsf(v[i]));
       }
     }
-    am = block_allreduce<NW, true>(am, stage);
-    if constexpr (FP4) {
-      const float s = fmaxf(am / kFp4Range, kMinScaleFp4);
-      const float gs = 1.f / s;
-      // a 16-element block spans lanes t and t^1
-      float vmax = 0.f;
+    am = warp_allreduce<true>(am);
+    const float s = FP4 ? fmaxf(am / kFp4Range, kMinScaleFp4) : fmaxf(am / kFp8Max, kMinScaleFp8);
+    const float inv = 1.f / s;
+#pragma unroll 2
+    for (int j = 0; j < J; ++j) {
+      const int chunk = lane + 32 * j, c = chunk * 8;
+      float v[8], sc[8], sf[8];
+      unpack8(*reinterpret_cast<const uint4*>(row + c), v);
+      load8(a.scale + tab * a.tab_ld + c, sc);
+      load8(a.shift + tab * a.tab_ld + c, sf);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) vmax = fmaxf(vmax, fabsf(v[i]));
-      vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
-      uint32_t bits;
-      const float m = nvfp4_block_scale(vmax, gs, &bits);
-      const uint32_t lo = e2m1x4(v[0] * m, v[1] * m, v[2] * m, v[3] * m);
-      const uint32_t hi = e2m1x4(v[4] * m, v[5] * m, v[6] * m, v[7] * m);
-      *reinterpret_cast<uint32_t*>(a.h + r * (C / 2) + t * 4) = lo | (hi << 16);
-      if ((t & 1) == 0) a.hsf[sf_atom_offset(r, t >> 1, C / 16)] = (uint8_t)bits;
-      if (t == 0) a.hs[r] = s;
-    } else {
-      const float s = fmaxf(am / kFp8Max, kMinScaleFp8);
-      const float inv = 1.f / s;
-      uint2 o;
-      o.x = e4m3x4(v[0] * inv, v[1] * inv, v[2] * inv, v[3] * inv);
-      o.y = e4m3x4(v[4] * inv, v[5] * inv, v[6] * inv, v[7] * inv);
-      *reinterpret_cast<uint2*>(a.h + r * C + t * 8) = o;
-      if (t == 0) a.hs[r] = s;
+      for (int i = 0; i < 8; ++i) {
+        v[i] -= mean;
+        v[i] = v[i] * rs * (1.f + sc[i]) + sf[i];
+      }
+      if constexpr (FP4) {
+        // a 16-element block spans chunks 2m and 2m+1: lanes l and l^1 of the same j
+        float vmax = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) vmax = fmaxf(vmax, fabsf(v[i]));
+        vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
+        uint32_t bits;
+        const float m = nvfp4_block_scale(vmax, inv, &bits);
+        const uint32_t lo = e2m1x4(v[0] * m, v[1] * m, v[2] * m, v[3] * m);
+        const uint32_t hi = e2m1x4(v[4] * m, v[5] * m, v[6] * m, v[7] * m);
+        *reinterpret_cast<uint32_t*>(a.h + r * (C / 2) + chunk * 4) = lo | (hi << 16);
+        if ((lane & 1) == 0) a.hsf[sf_atom_offset(r, chunk >> 1, C / 16)] = (uint8_t)bits;
+      } else {
+        uint2 o;
+        o.x = e4m3x4(v[0] * inv, v[1] * inv, v[2] * inv, v[3] * inv);
+        o.y = e4m3x4(v[4] * inv, v[5] * inv, v[6] * inv, v[7] * inv);
+        *reinterpret_cast<uint2*>(a.h + r * C + c) = o;
+      }
     }
+    if (lane == 0) a.hs[r] = s;
   }
 }
 
 template <int C>
 int launch_resid_norm_quant(const RowArgs& a, bool branch, int norm, bool fp4, cudaStream_t st) {
-  const dim3 grid((unsigned)a.rows), block(C / 8);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t resident = (int64_t)sms * 2;  // two resident CTAs per SM (the launch bounds)
+  const dim3 grid((unsigned)(a.rows < resident ? a.rows : resident)), block(C / 8);
 #define H3B_RNQ(B, N, Q) resid_norm_quant_kernel<C, B, N, Q><<<grid, block, 0, st>>>(a)
   if (norm == H3B_NORM_NONE) {
     H3B_RNQ(true, H3B_NORM_NONE, false);
@@ -129,11 +258,22 @@ int launch_resid_norm_quant(const RowArgs& a, bool branch, int norm, bool fp4, c
       if (fp4) H3B_RNQ(false, H3B_NORM_RMS, true); else H3B_RNQ(false, H3B_NORM_RMS, false);
     }
   } else {
+    const int64_t blocks = (a.rows + LN_WARPS - 1) / LN_WARPS, cap = (int64_t)sms * 2;
+    const dim3 g2((unsigned)(blocks < cap ? blocks : cap)), b2(256);
+    const int lsm = LN_WARPS * C * 2;
+#define H3B_LNQ(B, Q)                                                                                  \
+  do {                                                                                                 \
+    if (cudaFuncSetAttribute(layer_norm_quant_warp_kernel<C, B, Q>,                                    \
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, lsm) != cudaSuccess)         \
+      return set_error(H3B_ECUDA, "resid_norm_quant: cannot reserve %d bytes of shared memory", lsm); \
+    layer_norm_quant_warp_kernel<C, B, Q><<<g2, b2, lsm, st>>>(a);                                     \
+  } while (0)
     if (branch) {
-      if (fp4) H3B_RNQ(true, H3B_NORM_LAYER, true); else H3B_RNQ(true, H3B_NORM_LAYER, false);
+      if (fp4) H3B_LNQ(true, true); else H3B_LNQ(true, false);
     } else {
-      if (fp4) H3B_RNQ(false, H3B_NORM_LAYER, true); else H3B_RNQ(false, H3B_NORM_LAYER, false);
+      if (fp4) H3B_LNQ(false, true); else H3B_LNQ(false, false);
     }
+#undef H3B_LNQ
   }
 #undef H3B_RNQ
   H3B_LAUNCH_CHECK("resid_norm_quant");

@@ -321,21 +321,26 @@ __global__ void __launch_bounds__(NWARP * 32) head_tile_quant_kernel(const HtqAr
       wv[2 * j + 1] = t.y;
     }
   }
+  uint2 raw[RPW];
+  float s1v[RPW];
+#pragma unroll
+  for (int u = 0; u < RPW; ++u) {  // all of a warp's rows are loaded before any arithmetic
+    const int i = w + u * NWARP;
+    raw[u] = make_uint2(0u, 0u);
+    s1v[u] = 1.f;
+    if (i < n) {
+      const int64_t r = row0 + i;
+      raw[u] = *reinterpret_cast<const uint2*>(a.x + (size_t)r * a.ld + (size_t)h * D + l * 4);
+      if (a.s1) s1v[u] = a.s1[r];
+    }
+  }
 #pragma unroll
   for (int u = 0; u < RPW; ++u) {
     const int i = w + u * NWARP;
     if (i >= n) break;  // warp-uniform
-    const int64_t r = row0 + i;
-    const uint2 u0 = *reinterpret_cast<const uint2*>(a.x + (size_t)r * a.ld + (size_t)h * D + l * 4);
-    const __nv_bfloat162* b0 = reinterpret_cast<const __nv_bfloat162*>(&u0);
     float f[4];
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const float2 t = __bfloat1622float2(b0[j]);
-      f[2 * j] = t.x;
-      f[2 * j + 1] = t.y;
-    }
-    const float s = a.s1 ? a.s1[r] : 1.f;
+    unpack4(raw[u], f);
+    const float s = s1v[u];
     float sum = 0.f;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {

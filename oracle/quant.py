@@ -119,6 +119,25 @@ def block_sum_sq(v: np.ndarray) -> np.ndarray:
     return butterfly_sum(stage)
 
 
+def warp_row_sum(v: np.ndarray, squares: bool = False) -> np.ndarray:
+    """Row sum in the order of the warp-per-row LayerNorm quantizer (fasth3-gb300_b200/csrc/quant.cu,
+    layer_norm_quant_warp_kernel): lane l owns the 8-element chunks l, l+32, ... and adds them chunk by chunk, elements
+    in order, in float32 (``squares``: v*v accumulated with one fused multiply-add per element); the 32 lane sums are
+    then butterflied."""
+    rows, C = v.shape
+    t = v.reshape(rows, C // 256, 32, 8)  # [row, j, lane, element]: chunk index lane + 32 j
+    acc = np.zeros((rows, 32), dtype=np.float32)
+    for j in range(C // 256):
+        for i in range(8):
+            x = t[:, j, :, i]
+            if squares:
+                x64 = x.astype(np.float64)
+                acc = (acc.astype(np.float64) + x64 * x64).astype(np.float32)
+            else:
+                acc = (acc + x).astype(np.float32)
+    return butterfly_sum(acc)
+
+
 def fp8_rows_from_values(v: np.ndarray, mag: np.ndarray | None = None):
     """FP8 row quantization of float32 rows (h3fast.cu:256-262): returns (codes, scale, ambiguity). ``mag``: the
     pre-cancellation magnitude of v for the ambiguity window (see _ambiguous)."""
@@ -213,10 +232,10 @@ def resid_norm_quant(x, y=None, sy=None, gate=None, idx=None, nw=None, shift=Non
         w = np.asarray(nw, dtype=np.float32)
         p = ((v * rs[:, None]).astype(np.float32) * w[None, :]).astype(np.float32)
         m = (p.astype(np.float64) * one_sc + sf).astype(np.float32)
-    elif norm == "layer":
-        mean = (block_sum(v) / np.float32(C)).astype(np.float32)
+    elif norm == "layer":  # the LayerNorm variant reduces one row per warp (warp_row_sum)
+        mean = (warp_row_sum(v) / np.float32(C)).astype(np.float32)
         d = (v - mean[:, None]).astype(np.float32)
-        var = (block_sum_sq(d) / np.float32(C)).astype(np.float32)
+        var = (warp_row_sum(d, squares=True) / np.float32(C)).astype(np.float32)
         rs = (1.0 / np.sqrt((var + np.float32(eps)).astype(np.float64))).astype(np.float32)
         p = (d * rs[:, None]).astype(np.float32)
         m = (p.astype(np.float64) * one_sc + sf).astype(np.float32)
