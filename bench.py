@@ -225,7 +225,7 @@ def vsa_config4_secondary(ops, dev, stream, args) -> dict:
     import math
 
     import torch
-    H, T, Hh, Ww, D, k = 40, 8, 64, 64, 128, 32
+    H, T, Hh, Ww, D, k = args.vsa_heads, 8, 64, 64, 128, 32
     S = T * Hh * Ww
     n = S // 64
     g = torch.Generator(device=dev).manual_seed(11)
@@ -313,7 +313,7 @@ def dit_step_secondary(pkg, dev, stream, args, ws) -> dict:
     this job (head all-to-all over NCCL). Timed with CUDA events, max over ranks (strong scaling: fixed tokens)."""
     import torch
     import torch.distributed as dist
-    cfg = pkg.model.DiTConfig(blocks=50, fmt="nvfp4")
+    cfg = pkg.model.DiTConfig(blocks=args.dit_blocks, fmt="nvfp4")
     m = pkg.model.DiTModel.random(cfg, device=dev, seed=0)
     grid = (31, 48, 84)
     S = grid[0] * grid[1] * grid[2]
@@ -350,6 +350,31 @@ def dit_step_secondary(pkg, dev, stream, args, ws) -> dict:
     return {"grid": list(grid), "tokens": S, "blocks": cfg.blocks, "topk": 32, "n_gpus": ws, "ms_per_step": ms,
             "steps": reps, "linear_tflop_per_step": lin / 1e12, "linear_share_tflops": lin / (ms * 1e-3) / 1e12,
             "output_finite": finite, "scaling": "strong", "parallelism": f"sp{ws}"}
+
+
+def run_only(args) -> None:
+    """One secondary measurement alone (for profiling captures): prints its JSON object."""
+    import torch
+    import torch.distributed as dist
+
+    import __graft_entry__
+    ws, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    pkg = __graft_entry__.load_package()
+    stream = torch.cuda.current_stream(dev)
+    fn = {"fp8": lambda: fp8_linear_secondary(pkg.ops, dev, stream, args),
+          "chain": lambda: fp8_chain_secondary(pkg, dev, stream, args),
+          "vsa": lambda: vsa_config4_secondary(pkg.ops, dev, stream, args),
+          "dit": lambda: dit_step_secondary(pkg, dev, stream, args, ws)}[args.only]
+    res = fn()
+    if rank == 0:
+        print(json.dumps({"only": args.only, "n_gpus": ws, "result": res}), flush=True)
+    if ws > 1:
+        dist.destroy_process_group()
 
 
 def run_ours(args) -> None:
@@ -505,11 +530,17 @@ def main() -> None:
     ap.add_argument("--no-fp8", action="store_true", help="skip the secondary FP8 linear measurement")
     ap.add_argument("--no-vsa", action="store_true", help="skip the secondary VSA (config 4) measurement")
     ap.add_argument("--no-dit", action="store_true", help="skip the secondary 50-block DiT step (config 5)")
+    ap.add_argument("--only", choices=["fp8", "chain", "vsa", "dit"], default=None,
+                    help="run one secondary measurement alone (profiling captures); no headline line")
+    ap.add_argument("--vsa-heads", type=int, default=40, help="heads of the config-4 VSA measurement (40)")
+    ap.add_argument("--dit-blocks", type=int, default=50, help="blocks of the config-5 step (50)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.only:
+        run_only(args)
     else:
         run_ours(args)
 
