@@ -2,10 +2,14 @@
 // (kind::mxf4nvf4 block16, e2m1 x e2m1 with ue4m3 scales per 16 K-elements), fp32 accumulators in tensor memory,
 // and a fused epilogue (scales, bias, GELU-tanh, gated residual, bf16 store).
 //
-// CTA = 6 warps, one CTA per SM (the shared-memory footprint forbids two):
+// CTA = 6 warps (FP8) or 10 warps (NVFP4), one CTA per SM (the shared-memory footprint forbids two):
 //   warp 0   TMA producer: A/B tiles (128-byte swizzle) and, for NVFP4, the scale-factor atoms (bulk copies)
-//   warp 1   TMEM allocator + MMA issuer (one thread): SMEM->TMEM scale copies, 4 MMAs per 128-byte K block
+//   warp 1   TMEM allocator + MMA issuer (one thread): 4 MMAs per 128-byte K block
 //   warps 2-5 epilogue: TMEM -> registers -> epilogue math -> global (warp w reads TMEM lanes 32*(w%4)..+31)
+//   warps 6-9 (NVFP4) scale factors: each warp writes the stage's scale atoms into its own 32 TMEM lanes with
+//            tcgen05.st (the same replicated image a 32x128b.warpx4 tcgen05.cp would produce), into a two-slot
+//            ring of TMEM columns, so the tensor pipe runs MMAs only (a tcgen05.cp per atom costs tensor-pipe time
+//            in proportion to the bytes it writes)
 // Two accumulator buffers in TMEM let the epilogue of tile j overlap the main loop of tile j+1.
 // Every mbarrier wait is bounded (2 s); on expiry the CTA records H3B_ETIMEOUT in a device status word, the other
 // roles abandon their loops, in-flight copies and MMAs are drained (again bounded) and TMEM is freed.
@@ -36,13 +40,17 @@ struct Cfg {
   static constexpr int kSfbBytes = FP4 ? 4096 : 0;  // 2 row groups x 4 atoms
   static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
   static constexpr int kAccCols = BN;
-  static constexpr int kSfaCol = 2 * BN;        // TMEM column of the A scales (16 columns)
-  static constexpr int kSfbCol = 2 * BN + 16;   // TMEM column of the B scales (32 columns)
+  // TMEM columns of scale slot s: A scales (16 columns: 4 K blocks x 4) at kSfCol + 48 s, B scales (32 columns:
+  // 4 K blocks x 2 row groups x 4) 16 columns further
+  static constexpr int kSfCol = 2 * BN;
+  static constexpr int kSfSlots = 2;
+  static constexpr int kThreads = FP4 ? 320 : 192;
   static constexpr int kTmemCols = 512;
   static constexpr int kElemsPerKB = FP4 ? 256 : 128;
   // barriers + bookkeeping after the stages
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256;
-  static_assert(2 * BN + (FP4 ? 48 : 0) <= kTmemCols, "TMEM budget");
+  static_assert(2 * BN + (FP4 ? 48 * kSfSlots : 0) <= kTmemCols, "TMEM budget");
+  static_assert(kSfCol % 16 == 0, "scale slots must start 16-column aligned");
   static_assert(kStageBytes % 1024 == 0, "stages must keep 1024-byte alignment");
 };
 
@@ -88,7 +96,7 @@ __device__ __forceinline__ float gelu_tanh(float v) {
 }
 
 template <bool FP4, int BN>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(Cfg<FP4, BN>::kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Problem p,
                 const Epi e) {
   using C = Cfg<FP4, BN>;
@@ -99,7 +107,9 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* acc_full = empty + C::kStages;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
-  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* sf_full = drain + 1;             // [slot] the four scale warps have written the slot
+  uint64_t* sf_empty = sf_full + C::kSfSlots;  // [slot] the MMAs reading the slot have completed
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(sf_empty + C::kSfSlots);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -114,6 +124,10 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&acc_empty[b], 4);
     }
     mbar_init(drain, 1);
+    for (int s = 0; s < C::kSfSlots; ++s) {
+      mbar_init(&sf_full[s], 4);
+      mbar_init(&sf_empty[s], 1);
+    }
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tmA);
@@ -195,6 +209,7 @@ __global__ void __launch_bounds__(192, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t acc_phase = 0;
+      uint32_t sf_n = 0;  // scale slots consumed so far: slot sf_n % kSfSlots, parity (sf_n / kSfSlots) & 1
       int j = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++j) {
@@ -222,18 +237,19 @@ __global__ void __launch_bounds__(192, 1)
           const uint64_t da = desc_k_sw128(smem_addr(sA));
           const uint64_t db = desc_k_sw128(smem_addr(sB));
           if constexpr (FP4) {
-            const uint32_t sSFA = smem_addr(sB + C::kBBytes);
-            const uint32_t sSFB = sSFA + C::kSfaBytes;
-            // each 64-deep K block: its three scale-factor copies, then its MMA (copies and MMAs share the tensor
-            // pipe; the copy cost is set by the bytes written to TMEM, the scale atoms being replicated four times)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              tmem_cp_32x128_x4(tmem + C::kSfaCol + 4 * i, desc_sf_atom(sSFA + 512 * i));
-              tmem_cp_32x128_x4(tmem + C::kSfbCol + 8 * i, desc_sf_atom(sSFB + 512 * i));
-              tmem_cp_32x128_x4(tmem + C::kSfbCol + 8 * i + 4, desc_sf_atom(sSFB + 2048 + 512 * i));
-              mma_nvf4(d, da + 2 * i, db + 2 * i, idesc, (kb | i) != 0, tmem + C::kSfaCol + 4 * i,
-                       tmem + C::kSfbCol + 8 * i + sfb_shift);
+            const int slot = (int)(sf_n % C::kSfSlots);
+            if (!mbar_wait_bounded(&sf_full[slot], (sf_n / C::kSfSlots) & 1u, abort_flag, kWaitLimitNs)) {
+              fail();
+              ok = false;
+              break;
             }
+            tc_fence_after();
+            const uint32_t sfa = tmem + C::kSfCol + 48 * slot, sfb = sfa + 16;
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              mma_nvf4(d, da + 2 * i, db + 2 * i, idesc, (kb | i) != 0, sfa + 4 * i, sfb + 8 * i + sfb_shift);
+            tc_commit(&sf_empty[slot]);
+            ++sf_n;
           } else {
 #pragma unroll
             for (int i = 0; i < 4; ++i) mma_e4m3(d, da + 2 * i, db + 2 * i, idesc, (kb | i) != 0);
@@ -251,6 +267,58 @@ __global__ void __launch_bounds__(192, 1)
       tc_commit(drain);
       volatile int no_abort = 0;
       if (!mbar_wait_bounded(drain, 0, &no_abort, kWaitLimitNs)) fail();
+    }
+  } else if (warp >= 6) {
+    // ------------------------------------------------------------------ scale factors (NVFP4)
+    if constexpr (FP4) {
+      // lane r of every 32-lane quarter receives row r of each 512-byte atom (16 bytes: the scales of rows r, r+32,
+      // r+64, r+96 for four 16-element K groups) in the atom's four columns
+      const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+      int stage = 0;
+      uint32_t phase = 0, sf_n = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          const int slot = (int)(sf_n % C::kSfSlots);
+          const bool got =
+              (sf_n < C::kSfSlots ||
+               mbar_wait_bounded(&sf_empty[slot], ((sf_n / C::kSfSlots) & 1u) ^ 1u, abort_flag, kWaitLimitNs)) &&
+              mbar_wait_bounded(&full[stage], phase, abort_flag, kWaitLimitNs);
+          if (!__all_sync(0xffffffffu, got)) {
+            if (lane == 0) fail();
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint8_t* sSFA = smem + stage * C::kStageBytes + C::kABytes + C::kBBytes;
+          const uint8_t* sSFB = sSFA + C::kSfaBytes;
+          uint32_t a[16], b0[16], b1[16];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint4 x = *reinterpret_cast<const uint4*>(sSFA + 512 * i + 16 * lane);
+            const uint4 y = *reinterpret_cast<const uint4*>(sSFB + 512 * i + 16 * lane);
+            const uint4 z = *reinterpret_cast<const uint4*>(sSFB + 2048 + 512 * i + 16 * lane);
+            uint32_t* bb = i < 2 ? b0 : b1;  // B columns 8i .. 8i+7: group 0 atom, then group 1 atom
+            const int o = 8 * (i & 1);
+            a[4 * i] = x.x, a[4 * i + 1] = x.y, a[4 * i + 2] = x.z, a[4 * i + 3] = x.w;
+            bb[o] = y.x, bb[o + 1] = y.y, bb[o + 2] = y.z, bb[o + 3] = y.w;
+            bb[o + 4] = z.x, bb[o + 5] = z.y, bb[o + 6] = z.z, bb[o + 7] = z.w;
+          }
+          const uint32_t sfa = tmem + lane_off + C::kSfCol + 48 * slot;
+          tmem_st_16cols(sfa, a);
+          tmem_st_16cols(sfa + 16, b0);
+          tmem_st_16cols(sfa + 32, b1);
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sf_full[slot]);
+          ++sf_n;
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
     }
   } else {
     // ------------------------------------------------------------------ epilogue
@@ -406,7 +474,7 @@ int run_gemm(const void* A, const uint8_t* sfa, const void* B, const uint8_t* sf
     attr_set = true;
   }
   const int grid = std::min(p.num_tiles, num_sms());
-  kern<<<grid, 192, C::kSmemBytes, stream>>>(ta, tb, p, e);
+  kern<<<grid, C::kThreads, C::kSmemBytes, stream>>>(ta, tb, p, e);
   H3B_LAUNCH_CHECK("gemm");
   return H3B_OK;
 }

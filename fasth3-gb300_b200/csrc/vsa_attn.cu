@@ -118,17 +118,6 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
       : "memory");
 }
 
-__device__ __forceinline__ void tmem_st_32cols(uint32_t taddr, const uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
-      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
-      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
-      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
-      : "memory");
-}
-__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -536,29 +525,40 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_st_32cols(tmem + lane_off + COL_P + 32 * w, pw);
         // ---- V' of this step
         if (!warp_wait(&sm.v_full[stage], (g / V_STAGES) & 1u)) { ok = false; break; }
+        {
+          // 16 E4M3 values (d = 16c .. 16c+15) of one key per thread and chunk; a warp covers 8 consecutive keys x 4
+          // chunks per load, so its 16-byte loads and stores each touch every bank group four times (no bank
+          // conflicts). All eight loads (both query tiles) are issued before the conversions.
+          uint4 raw[2][4];
 #pragma unroll
-        for (int s = 0; s < 2; ++s) {
-          if (j >= (s ? n1 : n0)) continue;  // warpgroup-uniform
-          const uint8_t* src = &sm.v[stage][s][0];
-          uint8_t* dst = &sm.vf[w][s][0][0];
+          for (int s = 0; s < 2; ++s) {
+            if (j >= (s ? n1 : n0)) continue;  // warpgroup-uniform
 #pragma unroll
-          for (int i = 0; i < (TILE * 8) / 128; ++i) {
-            // 16 E4M3 values (d = 16c .. 16c+15) of one key per thread; a warp covers 8 consecutive keys x 4 chunks,
-            // so its 16-byte loads and stores each touch every bank group four times (no bank conflicts)
-            const int key = (lane & 7) + 8 * (q4 + 4 * (i & 1)), c = (lane >> 3) + 4 * (i >> 1);
-            const uint4 raw = *reinterpret_cast<const uint4*>(src + key * 128 + ((c ^ (key & 7)) << 4));
-            const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
-            uint32_t f[8];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              f[2 * q] = e4m3x2_to_f16x2((uint16_t)(wv[q] & 0xFFFFu));
-              f[2 * q + 1] = e4m3x2_to_f16x2((uint16_t)(wv[q] >> 16));
+            for (int i = 0; i < 4; ++i) {
+              const int key = (lane & 7) + 8 * (q4 + 4 * (i & 1)), c = (lane >> 3) + 4 * (i >> 1);
+              raw[s][i] = *reinterpret_cast<const uint4*>(&sm.v[stage][s][0] + key * 128 + ((c ^ (key & 7)) << 4));
             }
-            uint8_t* half_base = dst + (c >> 2) * (TILE * 128) + key * 128;
-            const int dc0 = (c & 3) * 2;
-            *reinterpret_cast<uint4*>(half_base + ((dc0 ^ (key & 7)) << 4)) = make_uint4(f[0], f[1], f[2], f[3]);
-            *reinterpret_cast<uint4*>(half_base + (((dc0 + 1) ^ (key & 7)) << 4)) =
-                make_uint4(f[4], f[5], f[6], f[7]);
+          }
+#pragma unroll
+          for (int s = 0; s < 2; ++s) {
+            if (j >= (s ? n1 : n0)) continue;
+            uint8_t* dst = &sm.vf[w][s][0][0];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int key = (lane & 7) + 8 * (q4 + 4 * (i & 1)), c = (lane >> 3) + 4 * (i >> 1);
+              const uint32_t wv[4] = {raw[s][i].x, raw[s][i].y, raw[s][i].z, raw[s][i].w};
+              uint32_t f[8];
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                f[2 * q] = e4m3x2_to_f16x2((uint16_t)(wv[q] & 0xFFFFu));
+                f[2 * q + 1] = e4m3x2_to_f16x2((uint16_t)(wv[q] >> 16));
+              }
+              uint8_t* half_base = dst + (c >> 2) * (TILE * 128) + key * 128;
+              const int dc0 = (c & 3) * 2;
+              *reinterpret_cast<uint4*>(half_base + ((dc0 ^ (key & 7)) << 4)) = make_uint4(f[0], f[1], f[2], f[3]);
+              *reinterpret_cast<uint4*>(half_base + (((dc0 + 1) ^ (key & 7)) << 4)) =
+                  make_uint4(f[4], f[5], f[6], f[7]);
+            }
           }
         }
         fence_proxy_async_smem();  // the generic-proxy stores become visible to the tensor core
@@ -583,15 +583,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (lane == 0) mbar_arrive(&sm.ml_bar);
       if (!warp_wait(&sm.ml_bar, ml_phase)) break;
       ml_phase ^= 1;
-      float mw[2], lw[2];
-      mw[w] = m_ref;
-      lw[w] = l;
-      mw[w ^ 1] = sm.ml[par][0][w ^ 1][tl];
-      lw[w ^ 1] = sm.ml[par][1][w ^ 1][tl];
-      const float M = fmaxf(mw[0], mw[1]);
-      const float f0 = (M == -INFINITY || mw[0] == -INFINITY) ? 0.f : ex2(mw[0] - M);
-      const float f1 = (M == -INFINITY || mw[1] == -INFINITY) ? 0.f : ex2(mw[1] - M);
-      const float L = lw[0] * f0 + lw[1] * f1;
+      const float m_other = sm.ml[par][0][w ^ 1][tl], l_other = sm.ml[par][1][w ^ 1][tl];
+      const float m0 = w ? m_other : m_ref, m1 = w ? m_ref : m_other;  // selects, not a runtime-indexed array
+      const float l0 = w ? l_other : l, l1 = w ? l : l_other;
+      const float M = fmaxf(m0, m1);
+      const float f0 = (M == -INFINITY || m0 == -INFINITY) ? 0.f : ex2(m0 - M);
+      const float f1 = (M == -INFINITY || m1 == -INFINITY) ? 0.f : ex2(m1 - M);
+      const float L = l0 * f0 + l1 * f1;
       if (!warp_wait(&sm.o_full, o_phase)) break;
       o_phase ^= 1;
       tc_fence_after();
