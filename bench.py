@@ -492,7 +492,7 @@ def run_ours(args) -> None:
                        "l2": "inputs larger than L2 (X 335 MB read, Y 906 MB written per step); no flush"},
             "roofline": {"bound": "tensor", "achieved": gemm_tflops, "peak": fp4_peak, "unit": "TFLOP/s",
                          "frac": gemm_tflops / fp4_peak, "traffic": traffic,
-                         "kernel": "gemm_kernel<FP4=true,BN=192> (tcgen05 mxf4nvf4 block16)",
+                         "kernel": "gemm_nvfp4_pair_kernel (CTA pair, 256x192 tiles, tcgen05 mxf4nvf4 block16)",
                          "peak_source": f"4 x {peaks['source']} dense bf16 ({peaks['bf16']} TFLOP/s)",
                          "nominal_peak": 9000.0},
             "kernels_ms": {"nvfp4_quant_incl_amax": quant_ms, "gemm": gemm_ms,

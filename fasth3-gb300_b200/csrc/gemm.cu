@@ -95,6 +95,55 @@ __device__ __forceinline__ float gelu_tanh(float v) {
   return 0.5f * v * (1.f + t);
 }
 
+// Epilogue of one accumulator row: this thread's TMEM lane (tbase = lane address + accumulator column) holds output
+// row m, columns nb*BN .. nb*BN+BN-1.
+template <int BN>
+__device__ __forceinline__ void store_rows(const Problem& p, const Epi& e, float alpha, uint32_t tbase, int m, int nb) {
+  const bool row_ok = m < p.M;
+  const float rs = alpha * ((e.row_scale && row_ok) ? e.row_scale[m] : 1.f);
+#pragma unroll 1
+  for (int c0 = 0; c0 < BN; c0 += 32) {
+    uint32_t r[32];
+    tmem_ld_32cols(tbase + c0, r);
+    tmem_ld_wait();
+    const int n0 = nb * BN + c0;
+    if (!row_ok || n0 >= p.N) continue;
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int n = min(n0 + i, p.N - 1);
+      float x = __uint_as_float(r[i]) * rs;
+      if (e.col_scale) x *= e.col_scale[e.col_scalar ? 0 : n];
+      if (e.bias) x += __bfloat162float(e.bias[n]);
+      if (e.act == H3B_ACT_GELU_TANH) x = gelu_tanh(x);
+      v[i] = x;
+    }
+    if (e.residual) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        const int n = n0 + i;
+        if (n < p.N) {
+          float res[8], g[8];
+          load8(e.residual + (int64_t)m * e.ldr + n, res);
+          load8(e.gate + n, g);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) v[i + u] = res[u] + g[u] * v[i + u];
+        }
+      }
+    }
+    bf16* dst = e.D + (int64_t)m * e.ldd + n0;
+#pragma unroll
+    for (int i = 0; i < 32; i += 8) {
+      if (n0 + i < p.N) {
+        float w[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) w[u] = v[i + u];
+        store8(dst + i, w);
+      }
+    }
+  }
+}
+
 template <bool FP4, int BN>
 __global__ void __launch_bounds__(Cfg<FP4, BN>::kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Problem p,
@@ -338,51 +387,8 @@ __global__ void __launch_bounds__(Cfg<FP4, BN>::kThreads, 1)
       acc_phase ^= 1u << buf;
       __syncwarp();
       tc_fence_after();
-      const int m = mb * BM + q * 32 + lane;
-      const bool row_ok = m < p.M;
-      const float rs = alpha * ((e.row_scale && row_ok) ? e.row_scale[m] : 1.f);
-      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + buf * C::kAccCols;
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld_32cols(tbase + c0, r);
-        tmem_ld_wait();
-        const int n0 = nb * BN + c0;
-        if (!row_ok || n0 >= p.N) continue;
-        float v[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int n = min(n0 + i, p.N - 1);
-          float x = __uint_as_float(r[i]) * rs;
-          if (e.col_scale) x *= e.col_scale[e.col_scalar ? 0 : n];
-          if (e.bias) x += __bfloat162float(e.bias[n]);
-          if (e.act == H3B_ACT_GELU_TANH) x = gelu_tanh(x);
-          v[i] = x;
-        }
-        if (e.residual) {
-#pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            const int n = n0 + i;
-            if (n < p.N) {
-              float res[8], g[8];
-              load8(e.residual + (int64_t)m * e.ldr + n, res);
-              load8(e.gate + n, g);
-#pragma unroll
-              for (int u = 0; u < 8; ++u) v[i + u] = res[u] + g[u] * v[i + u];
-            }
-          }
-        }
-        bf16* dst = e.D + (int64_t)m * e.ldd + n0;
-#pragma unroll
-        for (int i = 0; i < 32; i += 8) {
-          if (n0 + i < p.N) {
-            float w[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) w[u] = v[i + u];
-            store8(dst + i, w);
-          }
-        }
-      }
+      store_rows<BN>(p, e, alpha, tmem + ((uint32_t)(q * 32) << 16) + buf * C::kAccCols, mb * BM + q * 32 + lane,
+                     nb);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
@@ -395,6 +401,307 @@ __global__ void __launch_bounds__(Cfg<FP4, BN>::kThreads, 1)
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+
+// ------------------------------------------------------------------------------------------------ NVFP4, CTA pairs
+// 256 x 192 output tiles on a cluster of two CTAs (two SMs) with cta_group::2 MMAs: CTA r of the pair loads rows
+// 128r .. 128r+127 of the A tile and rows 96r .. 96r+95 of the B tile, and holds output rows 128r .. 128r+127 in its
+// TMEM; the even CTA issues every MMA (M = 256, N = 192) over both CTAs' shared memory. Per SM this halves the B
+// bytes per MMA against the single-CTA 128 x 192 tile, and the smaller stage leaves room for six of them.
+// Warp roles in each CTA as in gemm_kernel<true, 192>. Barriers the even CTA's MMA thread waits on (the A/B stage,
+// the scale slots of both CTAs, the accumulator drained by both epilogues) live in the even CTA; the odd CTA's
+// producer, scale warps and epilogue reach them through shared::cluster addresses. MMA completion is committed to
+// the barrier of the same name in each CTA.
+struct PairCfg {
+  static constexpr int BN = 192;         // N of one MMA / output tile
+  static constexpr int kBRows = BN / 2;  // B rows each CTA loads
+  static constexpr int kStages = 6;
+  static constexpr int kABytes = BM * KB_BYTES;
+  static constexpr int kBBytes = kBRows * KB_BYTES;
+  static constexpr int kSfaBytes = 2048;
+  static constexpr int kSfbBytes = 4096;
+  static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
+  // scale slots in TMEM after the two accumulators: A scales in 16 columns (4 K blocks x 4), then the B scales of
+  // the tile's 192 rows in 24 (4 K blocks x 6, row 32c + r of the tile in column c, lane r)
+  static constexpr int kSfCol = 2 * BN;
+  static constexpr int kSfSlotCols = 40;
+  static constexpr int kSfSlots = 3;
+  static constexpr int kThreads = 320;
+  static constexpr int kTmemCols = 512;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 512;
+  static_assert(2 * BN + kSfSlotCols * kSfSlots <= kTmemCols, "TMEM budget");
+  static_assert(kSfCol % 8 == 0 && kSfSlotCols % 8 == 0, "scale slots are written 8 columns at a time");
+  static_assert(kStageBytes % 1024 == 0, "stages must keep 1024-byte alignment");
+};
+
+__global__ void __launch_bounds__(PairCfg::kThreads, 1)
+    gemm_nvfp4_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                           const Problem p, const Epi e) {
+  using C = PairCfg;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);  // [stage] even CTA: A/B landed
+  // [stage] the MMAs reading the stage have completed: one commit per stage into the even CTA's barrier; an even-CTA
+  // scale warp relays each completion to the odd CTA's barrier
+  uint64_t* empty = full + C::kStages;
+  uint64_t* sf_loaded = empty + C::kStages;         // [stage] this CTA's scale atoms landed
+  uint64_t* acc_full = sf_loaded + C::kStages;      // [buffer] the tile's MMAs have completed
+  uint64_t* acc_empty = acc_full + 2;               // [buffer] even CTA: both epilogues drained the accumulator
+  uint64_t* sf_full = acc_empty + 2;                // [slot] even CTA: both CTAs' scale warps wrote the slot
+  uint64_t* drain = sf_full + C::kSfSlots;
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int cluster = blockIdx.x >> 1, clusters = gridDim.x >> 1;
+  // shared::cluster address of a barrier of this CTA's layout, in CTA r of the pair
+  auto in_cta = [&](uint64_t* bar, uint32_t r) { return map_to_cta(smem_addr(bar), r); };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&sf_loaded[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 8);  // 4 epilogue warps x 2 CTAs
+    }
+    for (int s = 0; s < C::kSfSlots; ++s) mbar_init(&sf_full[s], 8);  // 4 scale warps x 2 CTAs
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_base_slot, C::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers are initialised before either CTA signals into the other
+  tc_fence_after();
+  const uint32_t tmem = *tmem_base_slot;
+
+  auto fail = [&]() {
+    *abort_flag = 1;
+    atomicExch(&g_gemm_status, H3B_ETIMEOUT);
+  };
+  const int m_blocks2 = (p.m_blocks + 1) >> 1;
+  Problem pp = p;  // tile raster over 256-row blocks
+  pp.m_blocks = m_blocks2;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer (each CTA loads its halves)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      const size_t kstride = (size_t)(p.K / 64) * 512;  // scale bytes per 128-row group
+      for (int tile = cluster; tile < p.num_tiles && ok; tile += clusters) {
+        int mb2, nb;
+        tile_coords(tile, pp, mb2, nb);
+        const int mblk = 2 * mb2 + (int)rank;
+        const int n0 = nb * C::BN;
+        const uint8_t* sfa_src = p.sfa + (size_t)min(mblk, p.m_blocks - 1) * kstride;
+        const int g0 = n0 >> 7;
+        const int g1 = min(g0 + 1, p.sfb_groups - 1);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag, kWaitLimitNs)) {
+            fail();
+            ok = false;
+            break;
+          }
+          uint8_t* sA = smem + stage * C::kStageBytes;
+          uint8_t* sB = sA + C::kABytes;
+          uint8_t* sSFA = sB + C::kBBytes;
+          uint8_t* sSFB = sSFA + C::kSfaBytes;
+          const uint32_t full0 = in_cta(&full[stage], 0);
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (C::kABytes + C::kBBytes));
+          tma_load_2d_pair(sA, &tmA, kb * KB_BYTES, mblk * BM, full0);
+          tma_load_2d_pair(sB, &tmB, kb * KB_BYTES, n0 + (int)rank * C::kBRows, full0);
+          mbar_arrive_expect_tx(&sf_loaded[stage], C::kSfaBytes + C::kSfbBytes);
+          bulk_load(sSFA, sfa_src + (size_t)kb * 2048, 2048, &sf_loaded[stage]);
+          bulk_load(sSFB, p.sfb + (size_t)g0 * kstride + (size_t)kb * 2048, 2048, &sf_loaded[stage]);
+          bulk_load(sSFB + 2048, p.sfb + (size_t)g1 * kstride + (size_t)kb * 2048, 2048, &sf_loaded[stage]);
+          issued = min(issued + 1, C::kStages);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // drain this CTA's scale copies (its A/B copies complete on the even CTA's barrier, drained there)
+        for (int i = 0; i < C::kStages; ++i) {
+          int s = stage - 1 - i;
+          uint32_t ph = phase;
+          if (s < 0) {
+            s += C::kStages;
+            ph ^= 1;
+          }
+          if (i < issued) {
+            volatile int no_abort = 0;
+            mbar_wait_bounded(&sf_loaded[s], ph, &no_abort, kWaitLimitNs / 4);
+            if (rank == 0) mbar_wait_bounded(&full[s], ph, &no_abort, kWaitLimitNs / 4);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer (even CTA, one thread)
+    if (lane == 0 && rank == 0) {
+      const uint32_t idesc = idesc_nvf4_m256(C::BN);
+      int stage = 0;
+      uint32_t phase = 0, acc_phase = 0, sf_n = 0;
+      int j = 0;
+      bool ok = true;
+      for (int tile = cluster; tile < p.num_tiles && ok; tile += clusters, ++j) {
+        int mb2, nb;
+        tile_coords(tile, pp, mb2, nb);
+        const int buf = j & 1;
+        if (!mbar_wait_spin(&acc_empty[buf], (((acc_phase >> buf) & 1u) ^ 1u), abort_flag, kWaitLimitNs)) {
+          fail();
+          break;
+        }
+        acc_phase ^= 1u << buf;
+        tc_fence_after();
+        const uint32_t d = tmem + buf * C::BN;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          const int slot = (int)(sf_n % C::kSfSlots);
+          if (!mbar_wait_spin(&full[stage], phase, abort_flag, kWaitLimitNs) ||
+              !mbar_wait_spin(&sf_full[slot], (sf_n / C::kSfSlots) & 1u, abort_flag, kWaitLimitNs)) {
+            fail();
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint8_t* sA = smem + stage * C::kStageBytes;
+          const uint64_t da = desc_k_sw128(smem_addr(sA));
+          const uint64_t db = desc_k_sw128(smem_addr(sA + C::kABytes));
+          const uint32_t sfa = tmem + C::kSfCol + C::kSfSlotCols * slot, sfb = sfa + 16;
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            mma_nvf4_pair(d, da + 2 * i, db + 2 * i, idesc, (kb | i) != 0, sfa + 4 * i, sfb + 6 * i);
+          tc_commit_pair(smem_addr(&empty[stage]));  // one commit per stage: each extra one costs tensor-pipe time
+          ++sf_n;
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit_pair(in_cta(&acc_full[buf], 0));
+        tc_commit_pair(in_cta(&acc_full[buf], 1));
+      }
+      tc_commit_pair(in_cta(drain, 0));
+      volatile int no_abort = 0;
+      if (!mbar_wait_spin(drain, 0, &no_abort, kWaitLimitNs)) fail();
+    }
+  } else if (warp >= 6) {
+    // ------------------------------------------------------------------ scale factors into this CTA's TMEM
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    int stage = 0;
+    uint32_t phase = 0, sf_n = 0;
+    bool ok = true;
+    for (int tile = cluster; tile < p.num_tiles && ok; tile += clusters) {
+      int mb2, nb;
+      tile_coords(tile, pp, mb2, nb);
+      // the tile's 192 B rows start at word 0 or 2 (rows 0 or 64 of a 128-row group) of the first group's atoms
+      const bool mid = ((nb * C::BN) & 127) != 0;
+      for (int kb = 0; kb < p.k_blocks; ++kb) {
+        const int slot = (int)(sf_n % C::kSfSlots);
+        // the stage's atoms are read into registers first, so the slot wait (MMA completion) is followed only by
+        // the TMEM stores
+        if (!__all_sync(0xffffffffu, mbar_wait_spin(&sf_loaded[stage], phase, abort_flag, kWaitLimitNs))) {
+          if (lane == 0) fail();
+          ok = false;
+          break;
+        }
+        const uint8_t* sSFA = smem + stage * C::kStageBytes + C::kABytes + C::kBBytes;
+        const uint8_t* sSFB = sSFA + C::kSfaBytes;
+        uint32_t a[16], b[24];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint4 x = *reinterpret_cast<const uint4*>(sSFA + 512 * i + 16 * lane);
+          const uint4 y = *reinterpret_cast<const uint4*>(sSFB + 512 * i + 16 * lane);
+          const uint4 z = *reinterpret_cast<const uint4*>(sSFB + 2048 + 512 * i + 16 * lane);
+          a[4 * i] = x.x, a[4 * i + 1] = x.y, a[4 * i + 2] = x.z, a[4 * i + 3] = x.w;
+          // words w0 .. w0+5 of (first group's atom, second group's atom)
+          b[6 * i] = mid ? y.z : y.x;
+          b[6 * i + 1] = mid ? y.w : y.y;
+          b[6 * i + 2] = mid ? z.x : y.z;
+          b[6 * i + 3] = mid ? z.y : y.w;
+          b[6 * i + 4] = mid ? z.z : z.x;
+          b[6 * i + 5] = mid ? z.w : z.y;
+        }
+        // the slot was last read by the MMAs of stage sf_n - kSfSlots: wait for their completion (and, in the even
+        // CTA, pass it on to the odd CTA's barrier of that stage for its producer and scale warps)
+        if (sf_n >= C::kSfSlots) {
+          const uint32_t prev = sf_n - C::kSfSlots;
+          const int ps = (int)(prev % C::kStages);
+          if (!__all_sync(0xffffffffu,
+                          mbar_wait_spin(&empty[ps], (prev / C::kStages) & 1u, abort_flag, kWaitLimitNs))) {
+            if (lane == 0) fail();
+            ok = false;
+            break;
+          }
+          if (rank == 0 && warp == 6 && lane == 0) mbar_arrive_cluster(in_cta(&empty[ps], 1));
+        }
+        tc_fence_after();
+        const uint32_t sfa = tmem + lane_off + C::kSfCol + C::kSfSlotCols * slot;
+        tmem_st_8cols(sfa, a);
+        tmem_st_8cols(sfa + 8, a + 8);
+        tmem_st_8cols(sfa + 16, b);
+        tmem_st_8cols(sfa + 24, b + 8);
+        tmem_st_8cols(sfa + 32, b + 16);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(in_cta(&sf_full[slot], 0));
+        ++sf_n;
+        if (++stage == C::kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (this CTA's 128 rows)
+    const int q = warp & 3;
+    const float alpha = e.alpha * (e.alpha_dev ? *e.alpha_dev : 1.f);
+    uint32_t acc_phase = 0;
+    int j = 0;
+    for (int tile = cluster; tile < p.num_tiles; tile += clusters, ++j) {
+      int mb2, nb;
+      tile_coords(tile, pp, mb2, nb);
+      const int buf = j & 1;
+      const bool got = mbar_wait_bounded(&acc_full[buf], ((acc_phase >> buf) & 1u), abort_flag, kWaitLimitNs);
+      if (!__all_sync(0xffffffffu, got)) {
+        if (lane == 0) fail();
+        break;
+      }
+      acc_phase ^= 1u << buf;
+      __syncwarp();
+      tc_fence_after();
+      store_rows<C::BN>(p, e, alpha, tmem + ((uint32_t)(q * 32) << 16) + buf * C::BN,
+                        (2 * mb2 + (int)rank) * BM + q * 32 + lane, nb);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(in_cta(&acc_empty[buf], 0));
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync_all();  // nothing signals into either CTA after this point
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, C::kTmemCols);
   }
 }
 
@@ -479,6 +786,69 @@ int run_gemm(const void* A, const uint8_t* sfa, const void* B, const uint8_t* sf
   return H3B_OK;
 }
 
+int run_gemm_nvfp4_pair(const void* A, const uint8_t* sfa, const void* B, const uint8_t* sfb, int64_t M, int64_t N,
+                        int64_t K, const h3b_epilogue* epi, cudaStream_t stream) {
+  using C = PairCfg;
+  CUtensorMap ta, tb;
+  int rc = make_tmap(&ta, A, M, K / 2, BM);
+  if (rc) return rc;
+  rc = make_tmap(&tb, B, N, K / 2, C::kBRows);
+  if (rc) return rc;
+  Problem p;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.m_blocks = (int)((M + BM - 1) / BM);
+  p.n_blocks = (int)((N + C::BN - 1) / C::BN);
+  p.k_blocks = (int)(K / 256);
+  p.num_tiles = ((p.m_blocks + 1) / 2) * p.n_blocks;  // 256-row x 192-column tiles
+  p.sfa = sfa;
+  p.sfb = sfb;
+  p.sfb_groups = (int)((N + 127) / 128);
+  Epi e{epi->alpha,
+        epi->alpha_dev,
+        epi->row_scale,
+        epi->col_scale,
+        epi->col_scale_scalar,
+        static_cast<const bf16*>(epi->bias),
+        epi->act,
+        static_cast<const bf16*>(epi->residual),
+        epi->ldr,
+        static_cast<const bf16*>(epi->gate),
+        static_cast<bf16*>(epi->D),
+        epi->ldd};
+  auto kern = gemm_nvfp4_pair_kernel;
+  static int max_clusters = 0;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (!max_clusters) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) != cudaSuccess)
+      return set_error(H3B_ECUDA, "gemm: cannot reserve %d bytes of shared memory", C::kSmemBytes);
+    cfg.gridDim = dim3(2 * (num_sms() / 2));
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0)
+      return set_error(H3B_ECUDA, "gemm: no CTA pair of %d bytes of shared memory fits", C::kSmemBytes);
+    max_clusters = n;
+  }
+  cfg.gridDim = dim3(2 * std::min(p.num_tiles, max_clusters));
+  const cudaError_t le = cudaLaunchKernelEx(&cfg, kern, ta, tb, p, e);
+  if (le != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(H3B_ECUDA, "gemm: CTA-pair launch failed: %s", cudaGetErrorString(le));
+  }
+  H3B_LAUNCH_CHECK("gemm");
+  return H3B_OK;
+}
+
 int check_epilogue(const h3b_epilogue* epi, int64_t N) {
   H3B_REQUIRE(epi && epi->D, "gemm: epilogue and its output D are required");
   H3B_REQUIRE(epi->ldd >= N && epi->ldd % 8 == 0 && aligned(epi->D, 16), "gemm: ldd >= N, multiple of 8, D 16-byte aligned");
@@ -516,7 +886,7 @@ extern "C" int h3b_gemm_nvfp4(const void* A, const uint8_t* sfa, const void* B, 
               "gemm_nvfp4: operands and scales must be 16-byte aligned");
   if (int rc = check_epilogue(epi, N)) return rc;
   if (M == 0) return H3B_OK;
-  return run_gemm<true, 192>(A, sfa, B, sfb, M, N, K, epi, stream);
+  return run_gemm_nvfp4_pair(A, sfa, B, sfb, M, N, K, epi, stream);
 }
 
 extern "C" int h3b_device_status(int* status) {
