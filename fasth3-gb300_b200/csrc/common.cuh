@@ -84,6 +84,12 @@ __device__ __forceinline__ void store8(bf16* p, const float (&f)[8]) {
   *reinterpret_cast<uint4*>(p) = u;
 }
 
+// two fp32 -> bf16x2 (round to nearest even), a in the low half
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
 __device__ __forceinline__ float to_bf16_and_back(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
 // Two fp32 -> two saturating round-to-nearest-even e4m3 bytes (first argument in the low byte).

@@ -144,6 +144,72 @@ __device__ __forceinline__ void store_rows(const Problem& p, const Epi& e, float
   }
 }
 
+// Epilogue of one warp's 32 accumulator rows (TMEM lanes 32q .. 32q+31 at column tcol) through shared memory and
+// TMA stores: per 32-column chunk each lane converts its row to bf16 into a 32 x 64-byte staging box (64-byte
+// swizzle, so the 16-byte writes of a quarter-warp hit distinct banks), and lane 0 stores the box with one
+// cp.async.bulk.tensor (full 32-byte sectors; rows >= M and columns >= N are clipped by the tensor map). Two staging
+// boxes per warp alternate; `chunk` counts this warp's boxes across tiles.
+template <int BN>
+__device__ __forceinline__ void store_rows_tma(const Problem& p, const Epi& e, const CUtensorMap* tmD, float alpha,
+                                               uint32_t tbase, int m0, int nb, uint8_t* stage_box, uint32_t& chunk) {
+  const int lane = threadIdx.x & 31;
+  const int m = m0 + lane;
+  const bool row_ok = m < p.M;
+  const float rs = alpha * ((e.row_scale && row_ok) ? e.row_scale[m] : 1.f);
+#pragma unroll 1
+  for (int c0 = 0; c0 < BN; c0 += 32) {
+    uint32_t r[32];
+    tmem_ld_32cols(tbase + c0, r);
+    tmem_ld_wait();
+    const int n0 = nb * BN + c0;
+    if (m0 >= p.M || n0 >= p.N) continue;  // warp-uniform: nothing of this box is inside the output
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int n = min(n0 + i, p.N - 1);
+      float x = __uint_as_float(r[i]) * rs;
+      if (e.col_scale) x *= e.col_scale[e.col_scalar ? 0 : n];
+      if (e.bias) x += __bfloat162float(e.bias[n]);
+      if (e.act == H3B_ACT_GELU_TANH) x = gelu_tanh(x);
+      v[i] = x;
+    }
+    if (e.residual && row_ok) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        const int n = n0 + i;
+        if (n < p.N) {
+          float res[8], g[8];
+          load8(e.residual + (int64_t)m * e.ldr + n, res);
+          load8(e.gate + n, g);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) v[i + u] = res[u] + g[u] * v[i + u];
+        }
+      }
+    }
+    uint8_t* box = stage_box + (chunk & 1) * 2048;
+    if (lane == 0) bulk_wait_read<1>();  // the store issued from this box two chunks ago has read it
+    __syncwarp();
+    uint8_t* row = box + lane * 64;
+    const int sw = (lane >> 1) & 3;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 w;
+      w.x = pack_bf16x2(v[8 * j], v[8 * j + 1]);
+      w.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+      w.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+      w.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+      *reinterpret_cast<uint4*>(row + ((j ^ sw) << 4)) = w;
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(tmD, n0, m0, box);
+      bulk_commit_group();
+    }
+    ++chunk;
+  }
+}
+
 template <bool FP4, int BN>
 __global__ void __launch_bounds__(Cfg<FP4, BN>::kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Problem p,
@@ -430,7 +496,8 @@ struct PairCfg {
   static constexpr int kSfSlots = 3;
   static constexpr int kThreads = 320;
   static constexpr int kTmemCols = 512;
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 512;
+  static constexpr int kEpiBytes = 4 * 2 * 2048;  // per epilogue warp two 32 x 64-byte output staging boxes
+  static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + 1024 /*align*/ + 512;
   static_assert(2 * BN + kSfSlotCols * kSfSlots <= kTmemCols, "TMEM budget");
   static_assert(kSfCol % 8 == 0 && kSfSlotCols % 8 == 0, "scale slots are written 8 columns at a time");
   static_assert(kStageBytes % 1024 == 0, "stages must keep 1024-byte alignment");
@@ -438,11 +505,12 @@ struct PairCfg {
 
 __global__ void __launch_bounds__(PairCfg::kThreads, 1)
     gemm_nvfp4_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                           const Problem p, const Epi e) {
+                           const __grid_constant__ CUtensorMap tmD, const Problem p, const Epi e) {
   using C = PairCfg;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);  // [stage] even CTA: A/B landed
+  uint8_t* epi_boxes = smem + C::kStages * C::kStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_boxes + C::kEpiBytes);  // [stage] even CTA: A/B landed
   // [stage] the MMAs reading the stage have completed: one commit per stage into the even CTA's barrier; an even-CTA
   // scale warp relays each completion to the odd CTA's barrier
   uint64_t* empty = full + C::kStages;
@@ -476,6 +544,7 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
     fence_mbar_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    prefetch_tmap(&tmD);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_base_slot, C::kTmemCols);
@@ -674,7 +743,8 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
     // ------------------------------------------------------------------ epilogue (this CTA's 128 rows)
     const int q = warp & 3;
     const float alpha = e.alpha * (e.alpha_dev ? *e.alpha_dev : 1.f);
-    uint32_t acc_phase = 0;
+    uint8_t* boxes = epi_boxes + (warp - 2) * 4096;
+    uint32_t acc_phase = 0, chunk = 0;
     int j = 0;
     for (int tile = cluster; tile < p.num_tiles; tile += clusters, ++j) {
       int mb2, nb;
@@ -688,12 +758,13 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
       acc_phase ^= 1u << buf;
       __syncwarp();
       tc_fence_after();
-      store_rows<C::BN>(p, e, alpha, tmem + ((uint32_t)(q * 32) << 16) + buf * C::BN,
-                        (2 * mb2 + (int)rank) * BM + q * 32 + lane, nb);
+      store_rows_tma<C::BN>(p, e, &tmD, alpha, tmem + ((uint32_t)(q * 32) << 16) + buf * C::BN,
+                            (2 * mb2 + (int)rank) * BM + q * 32, nb, boxes, chunk);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(in_cta(&acc_empty[buf], 0));
     }
+    if (lane == 0) bulk_wait_all();  // the output stores have completed before the CTA exits
   }
 
   tc_fence_before();
@@ -730,6 +801,22 @@ int make_tmap(CUtensorMap* m, const void* base, int64_t rows, int64_t cols_bytes
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(H3B_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return H3B_OK;
+}
+
+// Output matrix bf16 [rows, cols] with row stride ld elements as a 2D tensor map with a 32 x 32 box (64-byte rows,
+// 64-byte swizzle): the epilogue's staging box.
+int make_tmap_out(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(H3B_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(H3B_ECUDA, "cuTensorMapEncodeTiled (output) failed (%d)", (int)r);
   return H3B_OK;
 }
 
@@ -794,6 +881,9 @@ int run_gemm_nvfp4_pair(const void* A, const uint8_t* sfa, const void* B, const 
   if (rc) return rc;
   rc = make_tmap(&tb, B, N, K / 2, C::kBRows);
   if (rc) return rc;
+  CUtensorMap td;
+  rc = make_tmap_out(&td, epi->D, M, N, epi->ldd);
+  if (rc) return rc;
   Problem p;
   p.M = (int)M;
   p.N = (int)N;
@@ -840,7 +930,7 @@ int run_gemm_nvfp4_pair(const void* A, const uint8_t* sfa, const void* B, const 
     max_clusters = n;
   }
   cfg.gridDim = dim3(2 * std::min(p.num_tiles, max_clusters));
-  const cudaError_t le = cudaLaunchKernelEx(&cfg, kern, ta, tb, p, e);
+  const cudaError_t le = cudaLaunchKernelEx(&cfg, kern, ta, tb, td, p, e);
   if (le != cudaSuccess) {
     cudaGetLastError();
     return set_error(H3B_ECUDA, "gemm: CTA-pair launch failed: %s", cudaGetErrorString(le));
