@@ -144,25 +144,42 @@ __device__ __forceinline__ void store_rows(const Problem& p, const Epi& e, float
   }
 }
 
-// Epilogue of one warp's 32 accumulator rows (TMEM lanes 32q .. 32q+31 at column tcol) through shared memory and
-// TMA stores: per 32-column chunk each lane converts its row to bf16 into a 32 x 64-byte staging box (64-byte
-// swizzle, so the 16-byte writes of a quarter-warp hit distinct banks), and lane 0 stores the box with one
-// cp.async.bulk.tensor (full 32-byte sectors; rows >= M and columns >= N are clipped by the tensor map). Two staging
-// boxes per warp alternate; `chunk` counts this warp's boxes across tiles.
+// Epilogue of one warp's 32 accumulator rows (TMEM lanes 32q .. 32q+31) through shared memory and TMA: per 32-column
+// chunk each lane turns its row into bf16 inside a 32 x 64-byte staging box (64-byte swizzle, so the 16-byte accesses
+// of a quarter-warp hit distinct banks) and lane 0 writes the box with one tensor store (full sectors; rows >= M and
+// columns >= N are clipped by the tensor map). With a gated residual the box is first filled with the residual's
+// 32 x 32 block by a TMA load (issued one chunk ahead, completing on the box's mbarrier), so the residual is read
+// with full-sector loads off the critical path and updated in place. Two boxes per warp alternate; `chunk` counts
+// this warp's boxes and `lphase` holds the parity of each box's load barrier.
 template <int BN>
-__device__ __forceinline__ void store_rows_tma(const Problem& p, const Epi& e, const CUtensorMap* tmD, float alpha,
-                                               uint32_t tbase, int m0, int nb, uint8_t* stage_box, uint32_t& chunk) {
+__device__ __forceinline__ void store_rows_tma(const Problem& p, const Epi& e, const CUtensorMap* tmD,
+                                               const CUtensorMap* tmR, float alpha, uint32_t tbase, int m0, int nb,
+                                               uint8_t* boxes, uint64_t* box_bar, uint32_t& chunk, uint32_t& lphase,
+                                               volatile int* abort_flag, bool& ok) {
   const int lane = threadIdx.x & 31;
   const int m = m0 + lane;
   const bool row_ok = m < p.M;
   const float rs = alpha * ((e.row_scale && row_ok) ? e.row_scale[m] : 1.f);
+  const bool res = e.residual != nullptr;
+  const int sw = (lane >> 1) & 3;
+  // lane 0: residual block of chunk c into box b, once the store that last read the box has finished reading it
+  auto load_residual = [&](int c, uint32_t b) {
+    bulk_wait_read<0>();
+    mbar_arrive_expect_tx(&box_bar[b], 2048);
+    tma_load_2d(boxes + b * 2048, tmR, nb * BN + 32 * c, m0, &box_bar[b]);
+  };
 #pragma unroll 1
-  for (int c0 = 0; c0 < BN; c0 += 32) {
+  for (int c = 0; c < BN / 32; ++c) {
+    const int n0 = nb * BN + 32 * c;
+    if (m0 >= p.M || n0 >= p.N) break;  // warp-uniform: this and later chunks lie outside the output
+    const uint32_t b = chunk & 1;
+    if (res && lane == 0) {
+      if (c == 0) load_residual(c, b);
+      if (c + 1 < BN / 32 && n0 + 32 < p.N) load_residual(c + 1, b ^ 1);
+    }
     uint32_t r[32];
-    tmem_ld_32cols(tbase + c0, r);
+    tmem_ld_32cols(tbase + 32 * c, r);
     tmem_ld_wait();
-    const int n0 = nb * BN + c0;
-    if (m0 >= p.M || n0 >= p.N) continue;  // warp-uniform: nothing of this box is inside the output
     float v[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
@@ -173,24 +190,32 @@ __device__ __forceinline__ void store_rows_tma(const Problem& p, const Epi& e, c
       if (e.act == H3B_ACT_GELU_TANH) x = gelu_tanh(x);
       v[i] = x;
     }
-    if (e.residual && row_ok) {
-#pragma unroll
-      for (int i = 0; i < 32; i += 8) {
-        const int n = n0 + i;
-        if (n < p.N) {
-          float res[8], g[8];
-          load8(e.residual + (int64_t)m * e.ldr + n, res);
-          load8(e.gate + n, g);
-#pragma unroll
-          for (int u = 0; u < 8; ++u) v[i + u] = res[u] + g[u] * v[i + u];
-        }
+    uint8_t* row = boxes + b * 2048 + lane * 64;
+    if (res) {
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&box_bar[b], (lphase >> b) & 1u, abort_flag, kWaitLimitNs))) {
+        ok = false;
+        return;
       }
+      lphase ^= 1u << b;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4 w = *reinterpret_cast<const uint4*>(row + ((j ^ sw) << 4));
+        float rv[8], g[8];
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float2 t = __bfloat1622float2(h[u]);
+          rv[2 * u] = t.x;
+          rv[2 * u + 1] = t.y;
+        }
+        load8(e.gate + min(n0 + 8 * j, p.N - 8), g);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[8 * j + u] = rv[u] + g[u] * v[8 * j + u];
+      }
+    } else {
+      if (lane == 0) bulk_wait_read<1>();  // the store issued from this box two chunks ago has read it
+      __syncwarp();
     }
-    uint8_t* box = stage_box + (chunk & 1) * 2048;
-    if (lane == 0) bulk_wait_read<1>();  // the store issued from this box two chunks ago has read it
-    __syncwarp();
-    uint8_t* row = box + lane * 64;
-    const int sw = (lane >> 1) & 3;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       uint4 w;
@@ -203,7 +228,7 @@ __device__ __forceinline__ void store_rows_tma(const Problem& p, const Epi& e, c
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
-      tma_store_2d(tmD, n0, m0, box);
+      tma_store_2d(tmD, n0, m0, boxes + b * 2048);
       bulk_commit_group();
     }
     ++chunk;
@@ -505,7 +530,8 @@ struct PairCfg {
 
 __global__ void __launch_bounds__(PairCfg::kThreads, 1)
     gemm_nvfp4_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                           const __grid_constant__ CUtensorMap tmD, const Problem p, const Epi e) {
+                           const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmR,
+                           const Problem p, const Epi e) {
   using C = PairCfg;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -519,7 +545,8 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
   uint64_t* acc_empty = acc_full + 2;               // [buffer] even CTA: both epilogues drained the accumulator
   uint64_t* sf_full = acc_empty + 2;                // [slot] even CTA: both CTAs' scale warps wrote the slot
   uint64_t* drain = sf_full + C::kSfSlots;
-  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* box_bar = drain + 1;                    // [epilogue warp][box] residual block landed in the box
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(box_bar + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -540,11 +567,13 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
     }
     for (int s = 0; s < C::kSfSlots; ++s) mbar_init(&sf_full[s], 8);  // 4 scale warps x 2 CTAs
     mbar_init(drain, 1);
+    for (int i = 0; i < 8; ++i) mbar_init(&box_bar[i], 1);
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
     prefetch_tmap(&tmD);
+    if (e.residual) prefetch_tmap(&tmR);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_base_slot, C::kTmemCols);
@@ -744,7 +773,8 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
     const int q = warp & 3;
     const float alpha = e.alpha * (e.alpha_dev ? *e.alpha_dev : 1.f);
     uint8_t* boxes = epi_boxes + (warp - 2) * 4096;
-    uint32_t acc_phase = 0, chunk = 0;
+    uint32_t acc_phase = 0, chunk = 0, lphase = 0;
+    bool ok = true;
     int j = 0;
     for (int tile = cluster; tile < p.num_tiles; tile += clusters, ++j) {
       int mb2, nb;
@@ -758,8 +788,13 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
       acc_phase ^= 1u << buf;
       __syncwarp();
       tc_fence_after();
-      store_rows_tma<C::BN>(p, e, &tmD, alpha, tmem + ((uint32_t)(q * 32) << 16) + buf * C::BN,
-                            (2 * mb2 + (int)rank) * BM + q * 32, nb, boxes, chunk);
+      store_rows_tma<C::BN>(p, e, &tmD, &tmR, alpha, tmem + ((uint32_t)(q * 32) << 16) + buf * C::BN,
+                            (2 * mb2 + (int)rank) * BM + q * 32, nb, boxes, box_bar + 2 * (warp - 2), chunk, lphase,
+                            abort_flag, ok);
+      if (!ok) {
+        if (lane == 0) fail();
+        break;
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(in_cta(&acc_empty[buf], 0));
@@ -881,8 +916,10 @@ int run_gemm_nvfp4_pair(const void* A, const uint8_t* sfa, const void* B, const 
   if (rc) return rc;
   rc = make_tmap(&tb, B, N, K / 2, C::kBRows);
   if (rc) return rc;
-  CUtensorMap td;
+  CUtensorMap td, tr;
   rc = make_tmap_out(&td, epi->D, M, N, epi->ldd);
+  if (rc) return rc;
+  rc = epi->residual ? make_tmap_out(&tr, epi->residual, M, N, epi->ldr) : make_tmap_out(&tr, epi->D, M, N, epi->ldd);
   if (rc) return rc;
   Problem p;
   p.M = (int)M;
@@ -930,7 +967,7 @@ int run_gemm_nvfp4_pair(const void* A, const uint8_t* sfa, const void* B, const 
     max_clusters = n;
   }
   cfg.gridDim = dim3(2 * std::min(p.num_tiles, max_clusters));
-  const cudaError_t le = cudaLaunchKernelEx(&cfg, kern, ta, tb, td, p, e);
+  const cudaError_t le = cudaLaunchKernelEx(&cfg, kern, ta, tb, td, tr, p, e);
   if (le != cudaSuccess) {
     cudaGetLastError();
     return set_error(H3B_ECUDA, "gemm: CTA-pair launch failed: %s", cudaGetErrorString(le));
