@@ -9,6 +9,8 @@
 // warp butterfly, warp partials butterflied again), so its rounding is the same too.
 #include "common.cuh"
 
+#include <algorithm>
+
 namespace h3b {
 namespace {
 
@@ -310,91 +312,118 @@ __global__ void __launch_bounds__(256) quant_fp8_rows_kernel(const bf16* __restr
 }
 
 // ------------------------------------------------------------------------------------------- per-tensor amax
-__global__ void __launch_bounds__(256) amax_kernel(const bf16* __restrict__ x, int64_t ld, int64_t rows, int K,
-                                                   float* __restrict__ amax) {
+// One warp per row at a time, eight 512-byte row segments in flight per warp (every load instruction reads 512
+// contiguous bytes).
+__global__ void __launch_bounds__(256, 4) amax_kernel(const bf16* __restrict__ x, int64_t ld, int64_t rows, int K,
+                                                      float* __restrict__ amax) {
   __shared__ float stage[32];
-  const int chunks = K / 8;
-  const int64_t total = rows * chunks;
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = (int64_t)gridDim.x * 8;
   float am = 0.f;
-  for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < total; i += (int64_t)gridDim.x * 256) {
-    const int64_t r = i / chunks;
-    const int c = (int)(i - r * chunks);
-    float f[8];
-    load8_nc(x + r * ld + c * 8, f);
+  for (int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); r < rows; r += nwarps) {
+    const bf16* src = x + r * ld;
+    for (int c0 = 0; c0 < K; c0 += 8 * 256) {
+      uint4 raw[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) am = fmaxf(am, fabsf(f[j]));
+      for (int u = 0; u < 8; ++u) {
+        const int col = c0 + u * 256 + 8 * lane;
+        raw[u] = col < K ? __ldg(reinterpret_cast<const uint4*>(src + col)) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        float f[8];
+        unpack8(raw[u], f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) am = fmaxf(am, fabsf(f[j]));
+      }
+    }
   }
   am = block_allreduce<8, true>(am, stage);
   if (threadIdx.x == 0 && am > 0.f) atomicMax(reinterpret_cast<int*>(amax), __float_as_int(am));
 }
 
 // ------------------------------------------------------------------------------------------- per-tensor NVFP4
-// Thread i owns 64 consecutive elements (four 16-element blocks) of one row: row = i / (K/64), group = i % (K/64),
-// so a warp reads 4 KB of one row contiguously and writes its four block scales as one 32-bit word.
-__global__ void __launch_bounds__(256) quant_nvfp4_tensor_kernel(const bf16* __restrict__ x, int64_t ld, int64_t rows,
-                                                                 int K, const float* __restrict__ amax,
-                                                                 uint8_t* __restrict__ q, uint8_t* __restrict__ sf,
-                                                                 float* __restrict__ s_out) {
+// Warp-cooperative, one warp per row at a time: a unit is 256 consecutive elements of the row, lane l holding
+// elements 8l .. 8l+7, so every load instruction reads 512 contiguous bytes and every code store writes 128. A
+// 16-element block spans lanes 2k and 2k+1 (one shuffle for its maximum); lanes 8j gather the four scales of blocks
+// 4j .. 4j+3 (adjacent bytes of one atom row) and write them as one word. A warp keeps 8 units' loads in flight;
+// rows past `rows` up to the next multiple of 128 get zero scales (the atom layout's padding).
+constexpr int kQuantUnits = 8;
+
+__global__ void __launch_bounds__(256, 4) quant_nvfp4_tensor_kernel(const bf16* __restrict__ x, int64_t ld, int64_t rows,
+                                                                    int K, const float* __restrict__ amax,
+                                                                    uint8_t* __restrict__ q, uint8_t* __restrict__ sf,
+                                                                    float* __restrict__ s_out) {
   const float s = fmaxf(*amax / kFp4Range, kMinScaleFp4);
   const float gs = 1.f / s;
-  const int groups = K / 64;
+  const int lane = threadIdx.x & 31;
   const int64_t rows_pad = (rows + 127) / 128 * 128;
-  const int64_t total = rows_pad * groups;
   const int64_t sf_cols = K / 16;
   if (blockIdx.x == 0 && threadIdx.x == 0) s_out[0] = s;
-  for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < total; i += (int64_t)gridDim.x * 256) {
-    const int64_t r = i / groups;
-    const int g = (int)(i - r * groups);
-    uint32_t sfw = 0;
-    if (r < rows) {
-      const bf16* src = x + r * ld + g * 64;
-      uint32_t codes[8];
+  const int64_t nwarps = (int64_t)gridDim.x * 8;
+  for (int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); r < rows_pad; r += nwarps) {
+    const bf16* src = x + r * ld;
+    const bool row_live = r < rows;
+    for (int c0 = 0; c0 < K; c0 += kQuantUnits * 256) {
+      uint4 raw[kQuantUnits];
 #pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        float f[8], e[8];
-        load8_nc(src + b * 16, f);
-        load8_nc(src + b * 16 + 8, e);
+      for (int t = 0; t < kQuantUnits; ++t) {
+        const int col = c0 + t * 256 + 8 * lane;
+        raw[t] = (row_live && col < K) ? __ldg(reinterpret_cast<const uint4*>(src + col)) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int t = 0; t < kQuantUnits; ++t) {
+        const int ucol = c0 + t * 256;
+        if (ucol >= K) break;  // warp-uniform
+        const int col = ucol + 8 * lane;
+        float f[8];
+        unpack8(raw[t], f);
         float vmax = 0.f;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) vmax = fmaxf(vmax, fmaxf(fabsf(f[j]), fabsf(e[j])));
+        for (int j = 0; j < 8; ++j) vmax = fmaxf(vmax, fabsf(f[j]));
+        vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
         uint32_t bits;
         const float m = nvfp4_block_scale(vmax, gs, &bits);
-        codes[2 * b] = e2m1x4(f[0] * m, f[1] * m, f[2] * m, f[3] * m) |
-                       (e2m1x4(f[4] * m, f[5] * m, f[6] * m, f[7] * m) << 16);
-        codes[2 * b + 1] = e2m1x4(e[0] * m, e[1] * m, e[2] * m, e[3] * m) |
-                           (e2m1x4(e[4] * m, e[5] * m, e[6] * m, e[7] * m) << 16);
-        sfw |= bits << (8 * b);
+        if (row_live && col < K)
+          *reinterpret_cast<uint32_t*>(q + r * (K / 2) + col / 2) =
+              e2m1x4(f[0] * m, f[1] * m, f[2] * m, f[3] * m) | (e2m1x4(f[4] * m, f[5] * m, f[6] * m, f[7] * m) << 16);
+        // the scales of blocks 4j .. 4j+3 sit on lanes 8j, 8j+2, 8j+4, 8j+6
+        const uint32_t b1 = __shfl_down_sync(0xffffffffu, bits, 2);
+        const uint32_t b2 = __shfl_down_sync(0xffffffffu, bits, 4);
+        const uint32_t b3 = __shfl_down_sync(0xffffffffu, bits, 6);
+        if ((lane & 7) == 0 && col < K) {
+          const uint32_t w = row_live ? (bits | (b1 << 8) | (b2 << 16) | (b3 << 24)) : 0u;
+          *reinterpret_cast<uint32_t*>(sf + sf_atom_offset(r, col / 16, sf_cols)) = w;
+        }
       }
-      uint4* dst = reinterpret_cast<uint4*>(q + r * (K / 2) + g * 32);
-      dst[0] = make_uint4(codes[0], codes[1], codes[2], codes[3]);
-      dst[1] = make_uint4(codes[4], codes[5], codes[6], codes[7]);
     }
-    // the four scale columns 4g..4g+3 of row r are adjacent bytes of one atom row
-    *reinterpret_cast<uint32_t*>(sf + sf_atom_offset(r, (int64_t)g * 4, sf_cols)) = sfw;
   }
 }
 
-int grid_for(int64_t work, int per_block) {
-  int dev = 0, sms = 148;
+// Grid of a grid-stride kernel: as many CTAs as are resident at once (no partial last wave), at most `need`.
+template <typename Kern>
+int resident_grid(Kern kern, int threads, int64_t need) {
+  int dev = 0, sms = 148, per_sm = 1;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t need = (work + per_block - 1) / per_block;
-  const int64_t cap = (int64_t)sms * 8;  // 8 resident 256-thread CTAs per SM
-  return (int)(need < cap ? (need > 0 ? need : 1) : cap);
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, 0) != cudaSuccess || per_sm < 1) per_sm = 1;
+  const int64_t cap = (int64_t)sms * per_sm;
+  return (int)std::max<int64_t>(1, std::min<int64_t>(cap, need));
 }
 
 }  // namespace
 
 int quant_nvfp4_tensor_launch(const bf16* x, int64_t ld, int64_t rows, int K, const float* amax, uint8_t* q,
                               uint8_t* sf, float* s_out, cudaStream_t st) {
-  const int64_t work = (rows + 127) / 128 * 128 * (K / 64);
-  quant_nvfp4_tensor_kernel<<<grid_for(work, 256), 256, 0, st>>>(x, ld, rows, K, amax, q, sf, s_out);
+  const int64_t rows_pad = (rows + 127) / 128 * 128;
+  quant_nvfp4_tensor_kernel<<<resident_grid(quant_nvfp4_tensor_kernel, 256, (rows_pad + 7) / 8), 256, 0, st>>>(
+      x, ld, rows, K, amax, q, sf, s_out);
   H3B_LAUNCH_CHECK("quant_nvfp4_tensor");
   return H3B_OK;
 }
 
 int amax_launch(const bf16* x, int64_t ld, int64_t rows, int K, float* amax, cudaStream_t st) {
-  amax_kernel<<<grid_for(rows * (K / 8), 256), 256, 0, st>>>(x, ld, rows, K, amax);
+  amax_kernel<<<resident_grid(amax_kernel, 256, (rows + 7) / 8), 256, 0, st>>>(x, ld, rows, K, amax);
   H3B_LAUNCH_CHECK("amax");
   return H3B_OK;
 }
