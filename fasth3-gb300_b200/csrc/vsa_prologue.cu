@@ -13,6 +13,8 @@
 // the reference kernel's.
 #include "common.cuh"
 
+#include <algorithm>
+
 namespace h3b {
 namespace {
 
@@ -69,165 +71,266 @@ __device__ __forceinline__ uint2 pack4(const float (&f)[4]) {
   return u;
 }
 
-// Rows are loaded for all of a warp's rows before any arithmetic (eight rows x three 8-byte loads in flight per lane),
-// and the rounded bf16 values are kept packed until the quantization pass; the arithmetic per element and the order of
-// every float32 sum are those of the reference kernel.
+__device__ __forceinline__ void cp_async8(void* smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)), "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_prev() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+// Persistent: each CTA walks work units (tile, 8 consecutive heads) with a grid stride and the items (tile, head) of
+// a unit in head order. The q/k/v rows of the next item are copied into shared memory (cp.async, two buffers) while the
+// current item is computed, so the loads' latency is off the critical path; each thread copies exactly the 8-byte
+// pieces it later reads (rows w, w+8, ... of its warp, dims 4l .. 4l+3), so the copies need no block barrier. The
+// tile's per-row data (the deferred GEMM scale and the RoPE cos/sin) is read once per unit. The arithmetic per
+// element and the order of every float32 sum are those of the reference kernel.
+constexpr int HG = 8;                                         // heads per work unit
+constexpr int kProBufBytes = 3 * TILE * D * (int)sizeof(bf16);  // one item's q/k/v rows
+constexpr int kProSmem = 2 * kProBufBytes;
+
+struct UnitInfo {
+  int ti, h0, row0, n;
+  int32_t tok[RPW];  // HEAD_MAJOR: token of each of this thread's rows
+};
+
 template <bool ROWS, bool TILE_QK>
 __global__ void __launch_bounds__(NWARP * 32, 2) prologue_kernel(const ProArgs a) {
+  extern __shared__ __align__(16) uint8_t pro_smem[];
   __shared__ float sp[3][NWARP][D];
   __shared__ float red[32];
-  const int h = blockIdx.x % a.heads, ti = blockIdx.x / a.heads;
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  const int row0 = a.tile_row0[ti], n = a.vbs[ti];
-  float pq[4] = {0.f, 0.f, 0.f, 0.f}, pk[4] = {0.f, 0.f, 0.f, 0.f}, pv[4] = {0.f, 0.f, 0.f, 0.f};
-  uint2 rq[RPW], rk[RPW], rv[RPW];
-  float s1v[RPW];
-  float qmax = 0.f, kmax = 0.f, vmax = 0.f;
-  float wqv[4], wkv[4];
+  const int hgroups = (a.heads + HG - 1) / HG;
+  const int units = a.n_tiles * hgroups;
   const int partner = l < HALF_LANES ? l + HALF_LANES : (l < 2 * HALF_LANES ? l - HALF_LANES : l);
   const float sign = l < HALF_LANES ? -1.f : 1.f;
   const bool rot = l < 2 * HALF_LANES && a.cosb != nullptr;
+  float wqv[4], wkv[4];
   if constexpr (ROWS) {
     unpack4(*reinterpret_cast<const uint2*>(a.wq + l * 4), wqv);
     unpack4(*reinterpret_cast<const uint2*>(a.wk + l * 4), wkv);
   }
-  // ---- loads
+  auto unit_info = [&](int unit, UnitInfo& ui) {
+    ui.ti = unit / hgroups;
+    ui.h0 = (unit - ui.ti * hgroups) * HG;
+    ui.row0 = a.tile_row0[ui.ti];
+    ui.n = a.vbs[ui.ti];
+    if constexpr (!ROWS) {
 #pragma unroll
-  for (int u = 0; u < RPW; ++u) {
-    const int i = w + u * NWARP;
-    rq[u] = rk[u] = rv[u] = make_uint2(0u, 0u);
-    s1v[u] = 0.f;
-    if (i < n) {
-      size_t src;
+      for (int u = 0; u < RPW; ++u) {
+        const int i = w + u * NWARP;
+        int32_t tok = 0;
+        if (i < ui.n) {
+          tok = a.perm ? a.perm[ui.row0 + i] : ui.row0 + i;
+          if (tok < 0 || tok >= a.seqlen) tok = 0;  // out-of-range token: read token 0 rather than fault
+        }
+        ui.tok[u] = tok;
+      }
+    }
+  };
+  // this thread's pieces of item (ui's tile, head h) into buffer b
+  auto issue = [&](const UnitInfo& ui, int h, int b) {
+    bf16* dst = reinterpret_cast<bf16*>(pro_smem + b * kProBufBytes);
+#pragma unroll
+    for (int u = 0; u < RPW; ++u) {
+      const int i = w + u * NWARP;
+      if (i < ui.n) {
+        size_t src;
+        if constexpr (ROWS) src = (size_t)(ui.row0 + i) * a.ld + (size_t)h * D + l * 4;
+        else src = ((size_t)h * a.seqlen + (size_t)ui.tok[u]) * D + l * 4;
+        cp_async8(dst + (0 * TILE + i) * D + l * 4, a.q + src);
+        cp_async8(dst + (1 * TILE + i) * D + l * 4, a.k + src);
+        cp_async8(dst + (2 * TILE + i) * D + l * 4, a.v + src);
+      }
+    }
+  };
+
+  int unit = blockIdx.x;
+  if (unit >= units) return;  // CTA-uniform
+  UnitInfo cur, nxt;
+  unit_info(unit, cur);
+  bool more = unit + (int)gridDim.x < units;
+  if (more) unit_info(unit + gridDim.x, nxt);
+  int b = 0;
+  issue(cur, cur.h0, 0);
+  cp_async_commit();
+  for (;;) {
+    const int ti = cur.ti, row0 = cur.row0, n = cur.n;
+    // the tile's per-row data, once per unit
+    float s1v[RPW];
+    uint2 cr[RPW], sr[RPW];
+#pragma unroll
+    for (int u = 0; u < RPW; ++u) {
+      const int i = w + u * NWARP;
+      s1v[u] = 0.f;
+      cr[u] = sr[u] = make_uint2(0u, 0u);
       if constexpr (ROWS) {
-        src = (size_t)(row0 + i) * a.ld + (size_t)h * D + l * 4;
-      } else {
-        int64_t tok = a.perm ? a.perm[row0 + i] : row0 + i;
-        if (tok < 0 || tok >= a.seqlen) tok = 0;  // out-of-range token: read token 0 rather than fault
-        src = ((size_t)h * a.seqlen + tok) * D + l * 4;
-      }
-      rq[u] = *reinterpret_cast<const uint2*>(a.q + src);
-      rk[u] = *reinterpret_cast<const uint2*>(a.k + src);
-      rv[u] = *reinterpret_cast<const uint2*>(a.v + src);
-      if constexpr (ROWS) {
-        const int64_t r = row0 + i;
-        s1v[u] = a.s1[r];
+        if (i < n) {
+          const int64_t r = row0 + i;
+          s1v[u] = a.s1[r];
+          if (rot) {
+            cr[u] = *reinterpret_cast<const uint2*>(a.cosb + r * ROT + l * 4);
+            sr[u] = *reinterpret_cast<const uint2*>(a.sinb + r * ROT + l * 4);
+          }
+        }
       }
     }
-  }
-  // ---- per-row arithmetic
+    const int hend = min(cur.h0 + HG, a.heads);
+    for (int h = cur.h0; h < hend; ++h) {
+      // the next item's rows go in flight before this one is computed
+      if (h + 1 < hend) issue(cur, h + 1, b ^ 1);
+      else if (more) issue(nxt, nxt.h0, b ^ 1);
+      cp_async_commit();
+      cp_async_wait_prev();
+      // the rounded bf16 values go back into this thread's own pieces of the buffer for the quantization pass
+      bf16* buf = reinterpret_cast<bf16*>(pro_smem + b * kProBufBytes);
+      float pq[4] = {0.f, 0.f, 0.f, 0.f}, pk[4] = {0.f, 0.f, 0.f, 0.f}, pv[4] = {0.f, 0.f, 0.f, 0.f};
+      float qmax = 0.f, kmax = 0.f, vmax = 0.f;
+      // ---- per-row arithmetic
 #pragma unroll
-  for (int u = 0; u < RPW; ++u) {
-    const int i = w + u * NWARP;
-    if (i >= n) break;  // warp-uniform
-    float qf[4], kf[4], vf[4];
-    unpack4(rq[u], qf);
-    unpack4(rk[u], kf);
-    unpack4(rv[u], vf);
-    float qo[4], ko[4];
-    if constexpr (ROWS) {
-      const float s = s1v[u];
-      float sumq = 0.f, sumk = 0.f;
+      for (int u = 0; u < RPW; ++u) {
+        // rows past the tile's length are computed as zeros (branch-free, so the rows' shuffle chains overlap);
+        // zeros leave every sum and maximum unchanged and are not stored
+        const int i = w + u * NWARP;
+        const bool valid = i < n;
+        float qf[4], kf[4], vf[4];
+        const uint2 zero = make_uint2(0u, 0u);
+        unpack4(valid ? *reinterpret_cast<const uint2*>(buf + (0 * TILE + i) * D + l * 4) : zero, qf);
+        unpack4(valid ? *reinterpret_cast<const uint2*>(buf + (1 * TILE + i) * D + l * 4) : zero, kf);
+        unpack4(valid ? *reinterpret_cast<const uint2*>(buf + (2 * TILE + i) * D + l * 4) : zero, vf);
+        float qo[4], ko[4];
+        if constexpr (ROWS) {
+          const float s = s1v[u];
+          float sumq = 0.f, sumk = 0.f;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            qf[j] *= s;
+            kf[j] *= s;
+            vf[j] *= s;
+            sumq += qf[j] * qf[j];
+            sumk += kf[j] * kf[j];
+          }
+#pragma unroll
+          for (int o = 16; o; o >>= 1) {
+            sumq += __shfl_xor_sync(0xffffffffu, sumq, o);
+            sumk += __shfl_xor_sync(0xffffffffu, sumk, o);
+          }
+          const float rq_ = rsqrtf(sumq / D + a.eps), rk_ = rsqrtf(sumk / D + a.eps);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            qf[j] *= rq_ * wqv[j];
+            kf[j] *= rk_ * wkv[j];
+          }
+          float c[4] = {1.f, 1.f, 1.f, 1.f}, sn[4] = {0.f, 0.f, 0.f, 0.f};
+          if (rot) {
+            unpack4(cr[u], c);
+            unpack4(sr[u], sn);
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float qr = __shfl_sync(0xffffffffu, qf[j], partner), kr = __shfl_sync(0xffffffffu, kf[j], partner);
+            qo[j] = to_bf16_and_back(qf[j] * c[j] + sign * qr * sn[j]);
+            ko[j] = to_bf16_and_back(kf[j] * c[j] + sign * kr * sn[j]);
+            vf[j] = to_bf16_and_back(vf[j]);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            qo[j] = qf[j];
+            ko[j] = kf[j];
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          pq[j] += qo[j];
+          pk[j] += ko[j];
+          pv[j] += vf[j];
+          qmax = fmaxf(qmax, fabsf(qo[j]));
+          kmax = fmaxf(kmax, fabsf(ko[j]));
+          vmax = fmaxf(vmax, fabsf(vf[j]));
+        }
+        if (valid) {
+          *reinterpret_cast<uint2*>(buf + (0 * TILE + i) * D + l * 4) = pack4(qo);
+          *reinterpret_cast<uint2*>(buf + (1 * TILE + i) * D + l * 4) = pack4(ko);
+          *reinterpret_cast<uint2*>(buf + (2 * TILE + i) * D + l * 4) = pack4(vf);
+        }
+      }
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        qf[j] *= s;
-        kf[j] *= s;
-        vf[j] *= s;
-        sumq += qf[j] * qf[j];
-        sumk += kf[j] * kf[j];
+        sp[0][w][l * 4 + j] = pq[j];
+        sp[1][w][l * 4 + j] = pk[j];
+        sp[2][w][l * 4 + j] = pv[j];
       }
+      vmax = block_allreduce<NWARP, true>(vmax, red);
+      const float svb = fmaxf(vmax / kFp8Max, 1e-30f);
+      float inv_q = a.inv_sq, inv_k = a.inv_sk;
+      if constexpr (TILE_QK) {
+        qmax = block_allreduce<NWARP, true>(qmax, red);
+        kmax = block_allreduce<NWARP, true>(kmax, red);
+        const float sqb = fmaxf(qmax / kFp8Max, 1e-30f), skb = fmaxf(kmax / kFp8Max, 1e-30f);
+        inv_q = 1.f / sqb;
+        inv_k = 1.f / skb;
+        if (threadIdx.x == 0) {
+          a.qs_blk[(size_t)h * a.n_ext + ti] = sqb;
+          a.ks_blk[(size_t)h * a.n_ext + ti] = skb;
+        }
+      }
+      if (threadIdx.x == 0) {
+        a.vs_blk[(size_t)h * a.n_ext + ti] = svb;
+        if (a.vs_head) atomicMax(reinterpret_cast<int*>(a.vs_head + h), __float_as_int(svb));
+      }
+      const float inv_v = 1.f / svb;
+      const size_t plane = (size_t)h * a.rows_pad + (size_t)ti * TILE;
 #pragma unroll
-      for (int o = 16; o; o >>= 1) {
-        sumq += __shfl_xor_sync(0xffffffffu, sumq, o);
-        sumk += __shfl_xor_sync(0xffffffffu, sumk, o);
+      for (int u = 0; u < RPW; ++u) {
+        const int i = w + u * NWARP;
+        if (i >= n) break;
+        const size_t dst = (plane + i) * D + l * 4;
+        float qv[4], kv[4], vv[4];
+        unpack4(*reinterpret_cast<const uint2*>(buf + (0 * TILE + i) * D + l * 4), qv);
+        unpack4(*reinterpret_cast<const uint2*>(buf + (1 * TILE + i) * D + l * 4), kv);
+        unpack4(*reinterpret_cast<const uint2*>(buf + (2 * TILE + i) * D + l * 4), vv);
+        *reinterpret_cast<uint32_t*>(a.qb + dst) = e4m3x4(qv[0] * inv_q, qv[1] * inv_q, qv[2] * inv_q, qv[3] * inv_q);
+        *reinterpret_cast<uint32_t*>(a.kb + dst) = e4m3x4(kv[0] * inv_k, kv[1] * inv_k, kv[2] * inv_k, kv[3] * inv_k);
+        *reinterpret_cast<uint32_t*>(a.vb + dst) = e4m3x4(vv[0] * inv_v, vv[1] * inv_v, vv[2] * inv_v, vv[3] * inv_v);
       }
-      const float rq_ = rsqrtf(sumq / D + a.eps), rk_ = rsqrtf(sumk / D + a.eps);
+      const float inv = 1.f / (float)n;
+      for (int e = threadIdx.x; e < 3 * D; e += NWARP * 32) {
+        const int which = e / D, d = e % D;
+        float acc = 0.f;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        qf[j] *= rq_ * wqv[j];
-        kf[j] *= rk_ * wkv[j];
+        for (int ww = 0; ww < NWARP; ++ww) acc += sp[which][ww][d];
+        float* dst = which == 0 ? a.qp : (which == 1 ? a.kp : a.vp);
+        dst[((size_t)h * a.n_tiles + ti) * D + d] = acc * inv;
       }
-      float c[4] = {1.f, 1.f, 1.f, 1.f}, sn[4] = {0.f, 0.f, 0.f, 0.f};
-      if (rot) {
-        const int64_t r = row0 + i;
-        unpack4(*reinterpret_cast<const uint2*>(a.cosb + r * ROT + l * 4), c);
-        unpack4(*reinterpret_cast<const uint2*>(a.sinb + r * ROT + l * 4), sn);
-      }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float qr = __shfl_sync(0xffffffffu, qf[j], partner), kr = __shfl_sync(0xffffffffu, kf[j], partner);
-        qo[j] = to_bf16_and_back(qf[j] * c[j] + sign * qr * sn[j]);
-        ko[j] = to_bf16_and_back(kf[j] * c[j] + sign * kr * sn[j]);
-        vf[j] = to_bf16_and_back(vf[j]);
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        qo[j] = qf[j];
-        ko[j] = kf[j];
-      }
+      __syncthreads();  // sp is rewritten by the next item
+      b ^= 1;
     }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      pq[j] += qo[j];
-      pk[j] += ko[j];
-      pv[j] += vf[j];
-      qmax = fmaxf(qmax, fabsf(qo[j]));
-      kmax = fmaxf(kmax, fabsf(ko[j]));
-      vmax = fmaxf(vmax, fabsf(vf[j]));
-    }
-    rq[u] = pack4(qo);
-    rk[u] = pack4(ko);
-    rv[u] = pack4(vf);
+    if (!more) break;
+    unit += gridDim.x;
+    cur = nxt;
+    more = unit + (int)gridDim.x < units;
+    if (more) unit_info(unit + gridDim.x, nxt);
   }
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    sp[0][w][l * 4 + j] = pq[j];
-    sp[1][w][l * 4 + j] = pk[j];
-    sp[2][w][l * 4 + j] = pv[j];
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+template <bool ROWS, bool TILE_QK>
+int launch_prologue(const ProArgs& a, cudaStream_t stream) {
+  auto kern = prologue_kernel<ROWS, TILE_QK>;
+  static int grid = 0;
+  if (!grid) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kProSmem) != cudaSuccess)
+      return set_error(H3B_ECUDA, "prologue: cannot reserve %d bytes of shared memory", kProSmem);
+    int dev = 0, sms = 148, per_sm = 1;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, NWARP * 32, kProSmem) != cudaSuccess || per_sm < 1)
+      per_sm = 1;
+    grid = sms * per_sm;
   }
-  vmax = block_allreduce<NWARP, true>(vmax, red);
-  const float svb = fmaxf(vmax / kFp8Max, 1e-30f);
-  float inv_q = a.inv_sq, inv_k = a.inv_sk;
-  if constexpr (TILE_QK) {
-    qmax = block_allreduce<NWARP, true>(qmax, red);
-    kmax = block_allreduce<NWARP, true>(kmax, red);
-    const float sqb = fmaxf(qmax / kFp8Max, 1e-30f), skb = fmaxf(kmax / kFp8Max, 1e-30f);
-    inv_q = 1.f / sqb;
-    inv_k = 1.f / skb;
-    if (threadIdx.x == 0) {
-      a.qs_blk[(size_t)h * a.n_ext + ti] = sqb;
-      a.ks_blk[(size_t)h * a.n_ext + ti] = skb;
-    }
-  }
-  if (threadIdx.x == 0) {
-    a.vs_blk[(size_t)h * a.n_ext + ti] = svb;
-    if (a.vs_head) atomicMax(reinterpret_cast<int*>(a.vs_head + h), __float_as_int(svb));
-  }
-  const float inv_v = 1.f / svb;
-  const size_t plane = (size_t)h * a.rows_pad + (size_t)ti * TILE;
-#pragma unroll
-  for (int u = 0; u < RPW; ++u) {
-    const int i = w + u * NWARP;
-    if (i >= n) break;
-    const size_t dst = (plane + i) * D + l * 4;
-    float qv[4], kv[4], vv[4];
-    unpack4(rq[u], qv);
-    unpack4(rk[u], kv);
-    unpack4(rv[u], vv);
-    *reinterpret_cast<uint32_t*>(a.qb + dst) = e4m3x4(qv[0] * inv_q, qv[1] * inv_q, qv[2] * inv_q, qv[3] * inv_q);
-    *reinterpret_cast<uint32_t*>(a.kb + dst) = e4m3x4(kv[0] * inv_k, kv[1] * inv_k, kv[2] * inv_k, kv[3] * inv_k);
-    *reinterpret_cast<uint32_t*>(a.vb + dst) = e4m3x4(vv[0] * inv_v, vv[1] * inv_v, vv[2] * inv_v, vv[3] * inv_v);
-  }
-  const float inv = 1.f / (float)n;
-  for (int e = threadIdx.x; e < 3 * D; e += NWARP * 32) {
-    const int which = e / D, d = e % D;
-    float acc = 0.f;
-#pragma unroll
-    for (int ww = 0; ww < NWARP; ++ww) acc += sp[which][ww][d];
-    float* dst = which == 0 ? a.qp : (which == 1 ? a.kp : a.vp);
-    dst[((size_t)h * a.n_tiles + ti) * D + d] = acc * inv;
-  }
+  const int units = a.n_tiles * ((a.heads + HG - 1) / HG);
+  kern<<<std::min(grid, units), NWARP * 32, kProSmem, stream>>>(a);
+  return H3B_OK;
 }
 
 }  // namespace
@@ -255,8 +358,8 @@ extern "C" int h3b_qkv_prologue8(const void* q, const void* k, const void* v, in
             static_cast<const bf16*>(cosb), static_cast<const bf16*>(sinb), inv_sq, inv_sk,
             static_cast<uint8_t*>(qb), static_cast<uint8_t*>(kb), static_cast<uint8_t*>(vb), qs_blk, ks_blk, vs_blk,
             vs_head, qp, kp, vp, heads, rows_pad, n_tiles, n_ext, eps};
-  if (tile_qk) prologue_kernel<true, true><<<n_tiles * heads, NWARP * 32, 0, stream>>>(a);
-  else prologue_kernel<true, false><<<n_tiles * heads, NWARP * 32, 0, stream>>>(a);
+  const int rc = tile_qk ? launch_prologue<true, true>(a, stream) : launch_prologue<true, false>(a, stream);
+  if (rc) return rc;
   H3B_LAUNCH_CHECK("qkv_prologue8");
   return H3B_OK;
 }
@@ -276,7 +379,7 @@ extern "C" int h3b_vsa_tile_quant(const void* q, const void* k, const void* v, i
             nullptr, tile_row0, vbs, nullptr, nullptr, nullptr, nullptr, 0.f, 0.f, static_cast<uint8_t*>(qb),
             static_cast<uint8_t*>(kb), static_cast<uint8_t*>(vb), qs_blk, ks_blk, vs_blk, vs_head, qp, kp, vp, heads,
             rows_pad, n_tiles, n_ext, 0.f};
-  prologue_kernel<false, true><<<n_tiles * heads, NWARP * 32, 0, stream>>>(a);
+  if (const int rc = launch_prologue<false, true>(a, stream)) return rc;
   H3B_LAUNCH_CHECK("vsa_tile_quant");
   return H3B_OK;
 }
@@ -335,9 +438,7 @@ __global__ void __launch_bounds__(NWARP * 32) head_tile_quant_kernel(const HtqAr
     }
   }
 #pragma unroll
-  for (int u = 0; u < RPW; ++u) {
-    const int i = w + u * NWARP;
-    if (i >= n) break;  // warp-uniform
+  for (int u = 0; u < RPW; ++u) {  // rows past the tile's length hold zeros: computed branch-free, not stored
     float f[4];
     unpack4(raw[u], f);
     const float s = s1v[u];
