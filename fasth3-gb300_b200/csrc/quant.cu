@@ -130,8 +130,10 @@ __global__ void __launch_bounds__(C / 8, 2) resid_norm_quant_kernel(const RowArg
 // LayerNorm variant (no reference counterpart; BASELINE's norm1/norm2 and the affine norm3 given as a table): one
 // warp per row, lane l owns the 8-element chunks l, l+32, l+64, ... (coalesced); the row is staged in shared memory
 // (bf16) by asynchronous copies. Row sums are a sequential float32 sum over a lane's chunks (chunk-major, elements in
-// order) followed by the warp butterfly: no block barriers, so many rows are in flight per SM.
-constexpr int LN_WARPS = 8;
+// order) followed by the warp butterfly: no block barriers, so many rows are in flight per SM. With one adaLN table
+// row for all tokens (idx NULL) the CTA first converts it to float32 (1 + scale, shift) in shared memory, so the two
+// modulate passes read four floats per load instead of converting bf16 per element.
+constexpr int LN_WARPS = 16;  // one 512-thread CTA per SM (the row buffers and tables fill its shared memory)
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
@@ -141,11 +143,42 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 template <int C, bool BRANCH, bool FP4>
-__global__ void __launch_bounds__(LN_WARPS * 32) layer_norm_quant_warp_kernel(const RowArgs a) {
+__global__ void __launch_bounds__(LN_WARPS * 32, 1) layer_norm_quant_warp_kernel(const RowArgs a) {
   constexpr int J = C / 256;  // chunks per lane
   extern __shared__ __align__(16) uint8_t ln_smem[];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   bf16* row = reinterpret_cast<bf16*>(ln_smem) + (size_t)wid * C;
+  float* t_scale1 = reinterpret_cast<float*>(ln_smem + (size_t)LN_WARPS * C * sizeof(bf16));  // 1 + scale
+  float* t_shift = t_scale1 + C;
+  const bool tab_smem = a.idx == nullptr;
+  if (tab_smem) {
+    for (int c = threadIdx.x * 8; c < C; c += LN_WARPS * 32 * 8) {
+      float sc[8], sf[8];
+      load8(a.scale + c, sc);
+      load8(a.shift + c, sf);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        t_scale1[c + i] = 1.f + sc[i];
+        t_shift[c + i] = sf[i];
+      }
+    }
+    __syncthreads();
+  }
+  // the modulate factors of the 8 columns at c: (1 + scale) and shift, from shared memory or from table row tab
+  auto modulate_factors = [&](int64_t tab, int c, float (&a1)[8], float (&sf)[8]) {
+    if (tab_smem) {
+      const float4 p0 = *reinterpret_cast<const float4*>(t_scale1 + c), p1 = *reinterpret_cast<const float4*>(t_scale1 + c + 4);
+      const float4 q0 = *reinterpret_cast<const float4*>(t_shift + c), q1 = *reinterpret_cast<const float4*>(t_shift + c + 4);
+      a1[0] = p0.x, a1[1] = p0.y, a1[2] = p0.z, a1[3] = p0.w, a1[4] = p1.x, a1[5] = p1.y, a1[6] = p1.z, a1[7] = p1.w;
+      sf[0] = q0.x, sf[1] = q0.y, sf[2] = q0.z, sf[3] = q0.w, sf[4] = q1.x, sf[5] = q1.y, sf[6] = q1.z, sf[7] = q1.w;
+    } else {
+      float sc[8];
+      load8(a.scale + tab * a.tab_ld + c, sc);
+      load8(a.shift + tab * a.tab_ld + c, sf);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) a1[i] = 1.f + sc[i];
+    }
+  };
   const int64_t warps = (int64_t)gridDim.x * LN_WARPS;
   for (int64_t r = (int64_t)blockIdx.x * LN_WARPS + wid; r < a.rows; r += warps) {
     const int64_t tab = a.idx ? (int64_t)a.idx[r] : 0;
@@ -194,14 +227,13 @@ __global__ void __launch_bounds__(LN_WARPS * 32) layer_norm_quant_warp_kernel(co
 #pragma unroll 2
     for (int j = 0; j < J; ++j) {
       const int c = (lane + 32 * j) * 8;
-      float v[8], sc[8], sf[8];
+      float v[8], a1[8], sf[8];
       unpack8(*reinterpret_cast<const uint4*>(row + c), v);
-      load8(a.scale + tab * a.tab_ld + c, sc);
-      load8(a.shift + tab * a.tab_ld + c, sf);
+      modulate_factors(tab, c, a1, sf);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         v[i] -= mean;
-        v[i] = v[i] * rs * (1.f + sc[i]) + sf[i];
+        v[i] = v[i] * rs * a1[i] + sf[i];
         am = fmaxf(am, fabsf(v[i]));
       }
     }
@@ -211,14 +243,13 @@ __global__ void __launch_bounds__(LN_WARPS * 32) layer_norm_quant_warp_kernel(co
 #pragma unroll 2
     for (int j = 0; j < J; ++j) {
       const int chunk = lane + 32 * j, c = chunk * 8;
-      float v[8], sc[8], sf[8];
+      float v[8], a1[8], sf[8];
       unpack8(*reinterpret_cast<const uint4*>(row + c), v);
-      load8(a.scale + tab * a.tab_ld + c, sc);
-      load8(a.shift + tab * a.tab_ld + c, sf);
+      modulate_factors(tab, c, a1, sf);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         v[i] -= mean;
-        v[i] = v[i] * rs * (1.f + sc[i]) + sf[i];
+        v[i] = v[i] * rs * a1[i] + sf[i];
       }
       if constexpr (FP4) {
         // a 16-element block spans chunks 2m and 2m+1: lanes l and l^1 of the same j
@@ -260,9 +291,9 @@ int launch_resid_norm_quant(const RowArgs& a, bool branch, int norm, bool fp4, c
       if (fp4) H3B_RNQ(false, H3B_NORM_RMS, true); else H3B_RNQ(false, H3B_NORM_RMS, false);
     }
   } else {
-    const int64_t blocks = (a.rows + LN_WARPS - 1) / LN_WARPS, cap = (int64_t)sms * 2;
-    const dim3 g2((unsigned)(blocks < cap ? blocks : cap)), b2(256);
-    const int lsm = LN_WARPS * C * 2;
+    const int64_t blocks = (a.rows + LN_WARPS - 1) / LN_WARPS, cap = (int64_t)sms;
+    const dim3 g2((unsigned)(blocks < cap ? blocks : cap)), b2(LN_WARPS * 32);
+    const int lsm = LN_WARPS * C * 2 + 2 * C * 4;  // row buffers + float32 table
 #define H3B_LNQ(B, Q)                                                                                  \
   do {                                                                                                 \
     if (cudaFuncSetAttribute(layer_norm_quant_warp_kernel<C, B, Q>,                                    \
