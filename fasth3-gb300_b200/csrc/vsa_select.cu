@@ -19,7 +19,7 @@ constexpr int D = 128;
 // ------------------------------------------------------------------------------------------------ scores
 // Block = 128x128 outputs of one head, 256 threads, an 8x8 register tile per thread; the q and k tile means are staged
 // in shared memory 32 dimensions at a time, transposed ([d][row], rows padded by 4 floats against bank conflicts).
-// Each output still accumulates d = 0..127 in order with separately rounded products and sums.
+// Each output accumulates d = 0..127 in order, one fused multiply-add per d (the order the CPU oracle restates).
 constexpr int SB = 128, SCH = 32, SPAD = SB + 4;
 
 __global__ void __launch_bounds__(256) scores_kernel(const float* __restrict__ qp, const float* __restrict__ kp,
@@ -63,7 +63,7 @@ __global__ void __launch_bounds__(256) scores_kernel(const float* __restrict__ q
 #pragma unroll
       for (int a = 0; a < 8; ++a)
 #pragma unroll
-        for (int b = 0; b < 8; ++b) acc[a][b] = __fadd_rn(acc[a][b], __fmul_rn(av[a], bv[b]));
+        for (int b = 0; b < 8; ++b) acc[a][b] = __fmaf_rn(av[a], bv[b], acc[a][b]);
     }
     __syncthreads();
   }

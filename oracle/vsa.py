@@ -51,13 +51,38 @@ def topk_rows(scores: np.ndarray, n: int, n_ext: int, prefix: int, spans, split:
     return idx, num
 
 
+def fma32(a, b, c) -> np.ndarray:
+    """Correctly rounded float32 fused multiply-add, round_f32(a*b + c) with ties to even (IEEE 754 fusedMultiplyAdd),
+    for float32 arrays. The product of two float32 values is exact in float64; TwoSum (Knuth) gives the float64 sum s and
+    its exact error e (a*b + c = s + e). Rounding s to float32 gives the correctly rounded result except when s lies
+    exactly halfway between two float32 neighbours (float64 rounding can land on a float32 midpoint, never cross one);
+    there the sign of e decides."""
+    a = np.asarray(a, dtype=np.float32).astype(np.float64)
+    b = np.asarray(b, dtype=np.float32).astype(np.float64)
+    c = np.asarray(c, dtype=np.float32).astype(np.float64)
+    p = a * b
+    s = p + c
+    bb = s - p
+    e = (p - (s - bb)) + (c - bb)
+    t = s.astype(np.float32)
+    td = t.astype(np.float64)
+    d = s - td  # exact (Sterbenz)
+    nb = np.nextafter(t, np.where(d > 0, np.float32(np.inf), np.float32(-np.inf)).astype(np.float32))
+    mid = (d != 0) & ((td + nb.astype(np.float64)) * 0.5 == s)
+    fix = mid & (e != 0) & (np.sign(e) == np.sign(d))
+    return np.where(fix, nb, t).astype(np.float32)
+
+
 def tile_scores(qp: np.ndarray, kp: np.ndarray, scale: float) -> np.ndarray:
-    """sc[h,i,j] = scale * sum_d qp[h,i,d] kp[h,j,d], d ascending, every product and sum rounded to float32."""
+    """sc[h,i,j] = scale * sum_d qp[h,i,d] kp[h,j,d]: one float32 fused multiply-add per d, d ascending, then the scale
+    multiply rounded to float32. The reference scores the tile means with torch.baddbmm (__init__.py:499-500, cuBLAS
+    in TF32 by default or float32), whose internal order is not specified; this fixed order is the one the CUDA kernel
+    implements, so scores and selection compare bit for bit."""
     qp = np.asarray(qp, dtype=np.float32)
     kp = np.asarray(kp, dtype=np.float32)
     acc = np.zeros((qp.shape[0], qp.shape[1], kp.shape[1]), dtype=np.float32)
     for d in range(qp.shape[2]):
-        acc = (acc + (qp[:, :, d, None] * kp[:, None, :, d]).astype(np.float32)).astype(np.float32)
+        acc = fma32(qp[:, :, d, None], kp[:, None, :, d], acc)
     return (acc * np.float32(scale)).astype(np.float32)
 
 

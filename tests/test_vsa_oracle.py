@@ -73,3 +73,58 @@ def test_gate_oracle_matches_reference(name):
         assert_codes(oq.unswizzle_sf(gold["asf"], rows, p["heads"] * 8), ref["sf_bits"], ref["sf_amb"], "gate sf")
     else:
         assert_codes(gold["a"], ref["codes"], ref["amb"], "gate fp8")
+
+
+def _round_f32_exact(x) -> np.float32:
+    """Round an exact rational to float32, ties to even, by comparing the two float32 neighbours exactly."""
+    from fractions import Fraction
+    t = np.float32(float(x))  # within one float32 ulp of x
+    best = None
+    for cand in (np.nextafter(t, np.float32(-np.inf)), t, np.nextafter(t, np.float32(np.inf))):
+        err = abs(Fraction(float(cand)) - x)
+        even = (int(np.asarray(cand).view(np.uint32)) & 1) == 0
+        if best is None or err < best[0] or (err == best[0] and even):
+            best = (err, cand)
+    return np.float32(best[1])
+
+
+def test_fma32_is_correctly_rounded():
+    """The oracle's float32 fused multiply-add (the tile scores' accumulation step) against exact rational
+    arithmetic: random operands over a wide exponent range, plus constructed cases where the float64 sum lands exactly
+    on a float32 midpoint and only the rounding error decides the direction."""
+    from fractions import Fraction
+    rng = np.random.default_rng(7)
+    n = 4000
+    a = (rng.standard_normal(n) * np.exp2(rng.integers(-20, 20, n))).astype(np.float32)
+    b = (rng.standard_normal(n) * np.exp2(rng.integers(-20, 20, n))).astype(np.float32)
+    c = (rng.standard_normal(n) * np.exp2(rng.integers(-40, 40, n))).astype(np.float32)
+    # midpoint cases: a*b = +-half_ulp * (1 - 2^-36) exactly, so c + a*b lies 2^-36 half-ulps inside a float32
+    # midpoint: float64 rounds the sum onto the midpoint itself and only the TwoSum error gives the direction
+    m = 600
+    base = rng.standard_normal(m).astype(np.float32)
+    half_ulp = np.abs(np.spacing(base).astype(np.float64)) / 2
+    a2 = np.full(m, 1.0 + 2.0 ** -18, dtype=np.float32)
+    b2 = (half_ulp * (1.0 - 2.0 ** -18) * rng.choice([-1.0, 1.0], m)).astype(np.float32)
+    c2 = base
+    a = np.concatenate([a, a2])
+    b = np.concatenate([b, b2])
+    c = np.concatenate([c, c2])
+    got = ov.fma32(a, b, c)
+    for i in range(a.size):
+        x = Fraction(float(a[i])) * Fraction(float(b[i])) + Fraction(float(c[i]))
+        want = _round_f32_exact(x)
+        assert got[i].view(np.uint32) == want.view(np.uint32), (i, a[i], b[i], c[i], got[i], want)
+
+
+def test_tile_scores_fixed_order():
+    """tile scores = one fused multiply-add per dimension, d ascending, then the scale: a direct scalar loop."""
+    rng = np.random.default_rng(3)
+    qp = rng.standard_normal((2, 5, 128)).astype(np.float32) * np.float32(0.1)
+    kp = rng.standard_normal((2, 7, 128)).astype(np.float32) * np.float32(0.1)
+    scale = 1.0 / math.sqrt(128)
+    got = ov.tile_scores(qp, kp, scale)
+    for h, i, j in [(0, 0, 0), (1, 4, 6), (0, 3, 2)]:
+        acc = np.float32(0)
+        for d in range(128):
+            acc = ov.fma32(qp[h, i, d], kp[h, j, d], acc)
+        assert got[h, i, j].view(np.uint32) == np.float32(acc * np.float32(scale)).view(np.uint32)
