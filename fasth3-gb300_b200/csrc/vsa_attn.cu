@@ -109,6 +109,14 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// 3D tiled TMA store from this CTA's shared memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_3d(const void* src, const CUtensorMap* map, int32_t x, int32_t y, int32_t z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(z), "r"(smem_addr(src))
+               : "memory");
+}
+
 __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
                                            uint32_t acc) {
   asm volatile(
@@ -181,7 +189,7 @@ __device__ __forceinline__ bool warp_wait_bounded(uint64_t* bar, uint32_t parity
 
 __global__ void __launch_bounds__(THREADS, 1)
     vsa_fp8_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                   const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
+                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, const AttnArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -216,6 +224,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     prefetch_tmap(&tmQ);
     prefetch_tmap(&tmK);
     prefetch_tmap(&tmV);
+    prefetch_tmap(&tmO);
   }
   if (warp == 1) {
     tmem_alloc(&sm.tmem_base, 512);
@@ -598,30 +607,53 @@ __global__ void __launch_bounds__(THREADS, 1)
       const bool row_ok = rt < a.vbs_q[tq];
       const size_t orow =
           (size_t)((tq / a.tpc_q) * a.heads + h) * (size_t)a.rows_chunk_q + (size_t)(tq % a.tpc_q) * TILE + rt;
-      bf16* dst = a.out + orow * D;
       const float g0 = f0 * oscale, g1 = f1 * oscale;
-#pragma unroll 1
-      for (int c0 = 64 * w; c0 < 64 * w + 64; c0 += 32) {  // warpgroup w writes output columns 64w .. 64w+63
+      // warpgroup w writes output columns 64w .. 64w+63 of both query tiles: each row (TMEM lane) is staged as 128
+      // bytes of bf16 in a 64-row box per query tile (128-byte swizzle; the V' buffer of this warpgroup is idle here:
+      // every PV of the item has completed), then one thread stores both boxes with TMA. Rows past the tile's length
+      // are written as zeros (padding rows of the tile's 64-row slot).
+      uint8_t* box = &sm.vf[w][tsel][0][0];
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c0 = 64 * w + 32 * cc;
         uint32_t o0[32], o1[32];
         tmem_ld_32cols(tmem + lane_off + COL_O + c0, o0);
         tmem_ld_32cols(tmem + lane_off + COL_O + 128 + c0, o1);
         tmem_ld_wait();
-        if (row_ok) {
+        if (cc == 1) {  // both accumulators read: the next item's PV MMAs may overwrite them
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.o_empty);
+        }
 #pragma unroll
-          for (int c = 0; c < 32; c += 8) {
-            float fv[8];
+        for (int j = 0; j < 4; ++j) {
+          uint32_t pk[4];
 #pragma unroll
-            for (int u = 0; u < 8; ++u)  // a partial with no mass contributes nothing (its O may be stale)
-              fv[u] = (g0 != 0.f ? __uint_as_float(o0[c + u]) * g0 : 0.f) +
-                      (g1 != 0.f ? __uint_as_float(o1[c + u]) * g1 : 0.f);
-            store8(dst + c0 + c, fv);
+          for (int u = 0; u < 4; ++u) {
+            const int c = 8 * j + 2 * u;
+            // a partial with no mass contributes nothing (its O may be stale)
+            const float x0 = (g0 != 0.f ? __uint_as_float(o0[c]) * g0 : 0.f) + (g1 != 0.f ? __uint_as_float(o1[c]) * g1 : 0.f);
+            const float x1 =
+                (g0 != 0.f ? __uint_as_float(o0[c + 1]) * g0 : 0.f) + (g1 != 0.f ? __uint_as_float(o1[c + 1]) * g1 : 0.f);
+            pk[u] = row_ok ? pack_bf16x2(x0, x1) : 0u;
           }
+          const int chunk = 4 * cc + j;  // 16-byte chunk of the 128-byte box row
+          *reinterpret_cast<uint4*>(box + rt * 128 + ((chunk ^ (rt & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
       }
+      fence_proxy_async_smem();
+      asm volatile("bar.sync %0, 128;" ::"r"(1 + w) : "memory");  // the warpgroup's rows are staged
+      if (warp == 3 + 4 * w && lane == 0) {
+#pragma unroll
+        for (int s2 = 0; s2 < 2; ++s2) {
+          const int t = 2 * p + s2;
+          tma_store_3d(&sm.vf[w][s2][0][0], &tmO, 64 * w, (t % a.tpc_q) * TILE, (t / a.tpc_q) * a.heads + h);
+        }
+        bulk_commit_group();
+        bulk_wait_read<0>();  // the boxes are read before the next conversion overwrites the V' buffer
+      }
+      asm volatile("bar.sync %0, 128;" ::"r"(1 + w) : "memory");
       if (a.lse && row_ok && w == 0) a.lse[orow] = L > 0.f ? M + __log2f(L) : -INFINITY;
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.o_empty);
     }
   }
 
@@ -649,6 +681,21 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // [planes, rows, 128] e4m3 as a 3D tensor map with a {128 B, 64 rows, 1 plane} box, 128-byte swizzle
+// bf16 output [planes, rows, 128] with a {64 columns, 64 rows, 1 plane} box (128-byte rows, 128-byte swizzle)
+int make_out_map(CUtensorMap* m, const void* base, int64_t planes, int64_t rows) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(H3B_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)rows, (cuuint64_t)planes};
+  cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)rows * D * 2};
+  cuuint32_t box[3] = {64, (cuuint32_t)TILE, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(H3B_ECUDA, "cuTensorMapEncodeTiled (output) failed (%d)", (int)r);
+  return H3B_OK;
+}
+
 int make_map(CUtensorMap* m, const void* base, int64_t planes, int64_t rows) {
   auto fn = encode_fn();
   if (!fn) return set_error(H3B_ECUDA, "cuTensorMapEncodeTiled is unavailable");
@@ -686,10 +733,11 @@ extern "C" int h3b_vsa_fp8_ex(const h3b_vsa_args* x, cudaStream_t stream) {
               "vsa_fp8: chunks do not cover the tiles");
   H3B_REQUIRE(aligned(x->q, 16) && aligned(x->k, 16) && aligned(x->v, 16) && aligned(x->out, 16),
               "vsa_fp8: 16-byte aligned operands");
-  CUtensorMap mq, mk, mv;
+  CUtensorMap mq, mk, mv, mo;
   if (int rc = make_map(&mq, x->q, (int64_t)x->chunks_q * x->heads, x->rows_chunk_q)) return rc;
   if (int rc = make_map(&mk, x->k, (int64_t)x->chunks_kv * x->heads, x->rows_chunk_kv)) return rc;
   if (int rc = make_map(&mv, x->v, (int64_t)x->chunks_kv * x->heads, x->rows_chunk_kv)) return rc;
+  if (int rc = make_out_map(&mo, x->out, (int64_t)x->chunks_q * x->heads, x->rows_chunk_q)) return rc;
   AttnArgs a{x->idx, x->num, x->vbs_q, x->vbs_kv, x->qs, x->ks, x->vs, x->vs_head, x->qk_coef,
              static_cast<bf16*>(x->out), x->lse, x->heads, x->n_q_ext, x->n_kv, x->idx_ld, x->q_scale_ld,
              x->kv_scale_ld, tpc_q, tpc_kv, x->rows_chunk_q, x->heads * (x->n_q_ext / 2)};
@@ -704,7 +752,7 @@ extern "C" int h3b_vsa_fp8_ex(const h3b_vsa_args* x, cudaStream_t stream) {
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int grid = a.items < sms ? a.items : sms;
-  vsa_fp8_kernel<<<grid, THREADS, smem, stream>>>(mq, mk, mv, a);
+  vsa_fp8_kernel<<<grid, THREADS, smem, stream>>>(mq, mk, mv, mo, a);
   H3B_LAUNCH_CHECK("vsa_fp8");
   return H3B_OK;
 }
