@@ -168,10 +168,18 @@ __device__ __forceinline__ void store_rows_tma(const Problem& p, const Epi& e, c
     mbar_arrive_expect_tx(&box_bar[b], 2048);
     tma_load_2d(boxes + b * 2048, tmR, nb * BN + 32 * c, m0, &box_bar[b]);
   };
-  // the rest of chunk c once its accumulator columns are in r
-  auto finish = [&](int c, const uint32_t (&r)[32]) -> bool {
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
     const int n0 = nb * BN + 32 * c;
+    if (m0 >= p.M || n0 >= p.N) break;  // warp-uniform: this and later chunks lie outside the output
     const uint32_t b = chunk & 1;
+    if (res && lane == 0) {
+      if (c == 0) load_residual(c, b);
+      if (c + 1 < BN / 32 && n0 + 32 < p.N) load_residual(c + 1, b ^ 1);
+    }
+    uint32_t r[32];
+    tmem_ld_32cols(tbase + 32 * c, r);
+    tmem_ld_wait();
     float v[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
@@ -184,8 +192,10 @@ __device__ __forceinline__ void store_rows_tma(const Problem& p, const Epi& e, c
     }
     uint8_t* row = boxes + b * 2048 + lane * 64;
     if (res) {
-      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&box_bar[b], (lphase >> b) & 1u, abort_flag, kWaitLimitNs)))
-        return false;
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&box_bar[b], (lphase >> b) & 1u, abort_flag, kWaitLimitNs))) {
+        ok = false;
+        return;
+      }
       lphase ^= 1u << b;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -222,34 +232,6 @@ __device__ __forceinline__ void store_rows_tma(const Problem& p, const Epi& e, c
       bulk_commit_group();
     }
     ++chunk;
-    return true;
-  };
-  // chunks in pairs: both TMEM loads are issued before one wait
-#pragma unroll 1
-  for (int c = 0; c < BN / 32; c += 2) {
-    const int n0 = nb * BN + 32 * c;
-    if (m0 >= p.M || n0 >= p.N) break;  // warp-uniform: this and later chunks lie outside the output
-    const bool second = c + 1 < BN / 32 && n0 + 32 < p.N;
-    if (res && lane == 0) {
-      const uint32_t b = chunk & 1;
-      if (c == 0) load_residual(c, b);
-      if (second) load_residual(c + 1, b ^ 1);
-    }
-    uint32_t r0[32], r1[32];
-    tmem_ld_32cols(tbase + 32 * c, r0);
-    if (second) tmem_ld_32cols(tbase + 32 * c + 32, r1);
-    tmem_ld_wait();
-    if (!finish(c, r0)) {
-      ok = false;
-      return;
-    }
-    if (!second) break;
-    // the residual of the pair's next chunk (c + 2) goes into the box chunk c has just handed to its store
-    if (res && lane == 0 && c + 2 < BN / 32 && n0 + 64 < p.N) load_residual(c + 2, (chunk + 1) & 1);
-    if (!finish(c + 1, r1)) {
-      ok = false;
-      return;
-    }
   }
 }
 
