@@ -172,6 +172,21 @@ def test_nvfp4_gemm_epilogue_gelu_residual(ops):
     assert rel(out.cpu().float(), ref) < TOL
 
 
+@pytest.mark.parametrize("M,N,K", [(300, 400, 512), (1000, 5120, 1024)])
+def test_nvfp4_gemm_residual_in_place(ops, M, N, K):
+    """x <- x + gate * (A W^T) with the output over its own residual (the block's update): the epilogue reads each
+    residual block by TMA before the same block is stored; ragged M and N exercise the clipped edge boxes."""
+    (qa, sfa, sa, qw, sfw, sw), a_deq, w_deq, _, _ = nvfp4_operands(ops, M, N, K, seed=M + N)
+    g = torch.Generator().manual_seed(23)
+    res = torch.randn(M, N, generator=g).bfloat16()
+    gate = torch.randn(N, generator=g).bfloat16()
+    x = res.to(DEV).clone()
+    ops.gemm_nvfp4(qa, sfa, qw, sfw, x, alpha_dev=sa, scale_b=sw, residual=x, gate=gate.to(DEV))
+    torch.cuda.synchronize()
+    ref = epilogue_ref(a_deq @ w_deq.T, alpha=sa.item() * sw.item(), residual=res, gate=gate)
+    assert rel(x.cpu().float(), ref) < TOL
+
+
 def test_nvfp4_config2_full_size_sampled_rows(ops):
     """BASELINE config 2 at full size (32768 x 13824 x 5120): the whole GEMM runs on the GPU; 64 sampled rows are
     checked against the dequantize-then-matmul oracle, plus a checksum of every row against the oracle's row sums."""

@@ -72,6 +72,28 @@ def test_tensor_nvfp4_bit_exact_vs_reference_golden(ops, name):
     np.testing.assert_array_equal(s.cpu().numpy().view(np.uint32), gold["s"].view(np.uint32))
 
 
+@pytest.mark.parametrize("rows,K", [(37, 320), (130, 3072), (129, 13824)])
+def test_tensor_nvfp4_widths_vs_oracle(ops, rows, K):
+    """Per-tensor NVFP4 at widths that are not multiples of the quantizer's 256-element warp unit (K = 320: a
+    64-element tail unit), BASELINE's 3072 and the FFN width 13824, and row counts that leave scale padding rows."""
+    x = outlier_matrix(rows, K, 300 + K, 0.005, 30.0)
+    xd = x.to(DEV)
+    q = torch.empty(rows, K // 2, device=DEV, dtype=torch.uint8)
+    sf = torch.full((ops.sf_rows(rows), K // 16), 0xAB, device=DEV, dtype=torch.uint8)  # padding must be rewritten
+    s = torch.empty(1, device=DEV)
+    ops.quant_nvfp4(xd, q, sf, s, torch.empty(ops.workspace_bytes(), device=DEV, dtype=torch.uint8))
+    torch.cuda.synchronize()
+    rq, rsf, rs, amb, sf_amb = oq.quant_nvfp4_tensor(x.float().numpy())
+    np.testing.assert_allclose(s.cpu().numpy(), np.float32(rs).reshape(1), rtol=4e-7)  # fast-math division
+    assert_codes(oq.unpack_nibbles(_u8(q)), oq.unpack_nibbles(rq), amb, "tensor nvfp4 nibbles")
+    got_bits = oq.unswizzle_sf(_u8(sf), rows, K // 16)
+    want_bits = oq.unswizzle_sf(rsf, rows, K // 16)
+    assert_codes(got_bits, want_bits, sf_amb, "tensor nvfp4 scales")
+    pad = _u8(sf).reshape(-1)[oq.sf_atom_offset(np.arange(rows, ops.sf_rows(rows))[:, None],
+                                                 np.arange(K // 16)[None, :], K // 16).reshape(-1)]
+    assert (pad == 0).all()
+
+
 def _ref():
     from oracle.ref_build.build_ref import load
     mod, cdll = load()
