@@ -1,15 +1,13 @@
-// Persistent, warp-specialized tcgen05 GEMMs for the DiT linears: FP8 (kind::f8f6f4, e4m3 x e4m3) and NVFP4
-// (kind::mxf4nvf4 block16, e2m1 x e2m1 with ue4m3 scales per 16 K-elements), fp32 accumulators in tensor memory,
-// and a fused epilogue (scales, bias, GELU-tanh, gated residual, bf16 store).
+// Persistent, warp-specialized tcgen05 GEMMs for the DiT linears, fp32 accumulators in tensor memory and a fused
+// epilogue (scales, bias, GELU-tanh, gated residual, bf16 store):
+//   gemm_fp8_kernel        FP8 (kind::f8f6f4, e4m3 x e4m3), one CTA per SM, 128x256 tiles
+//   gemm_nvfp4_pair_kernel NVFP4 (kind::mxf4nvf4 block16, e2m1 x e2m1 with ue4m3 scales per 16 K-elements) on CTA
+//                          pairs (cta_group::2), 256x192 tiles; described where it is defined
 //
-// CTA = 6 warps (FP8) or 10 warps (NVFP4), one CTA per SM (the shared-memory footprint forbids two):
-//   warp 0   TMA producer: A/B tiles (128-byte swizzle) and, for NVFP4, the scale-factor atoms (bulk copies)
+// gemm_fp8_kernel: CTA = 6 warps, one CTA per SM (the shared-memory footprint forbids two):
+//   warp 0   TMA producer: A/B tiles (128-byte swizzle)
 //   warp 1   TMEM allocator + MMA issuer (one thread): 4 MMAs per 128-byte K block
 //   warps 2-5 epilogue: TMEM -> registers -> epilogue math -> global (warp w reads TMEM lanes 32*(w%4)..+31)
-//   warps 6-9 (NVFP4) scale factors: each warp writes the stage's scale atoms into its own 32 TMEM lanes with
-//            tcgen05.st (the same replicated image a 32x128b.warpx4 tcgen05.cp would produce), into a two-slot
-//            ring of TMEM columns, so the tensor pipe runs MMAs only (a tcgen05.cp per atom costs tensor-pipe time
-//            in proportion to the bytes it writes)
 // Two accumulator buffers in TMEM let the epilogue of tile j overlap the main loop of tile j+1.
 // Every mbarrier wait is bounded (2 s); on expiry the CTA records H3B_ETIMEOUT in a device status word, the other
 // roles abandon their loops, in-flight copies and MMAs are drained (again bounded) and TMEM is freed.
@@ -31,26 +29,19 @@ constexpr int BM = 128;
 constexpr int KB_BYTES = 128;  // one swizzle atom of K per stage
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
-template <bool FP4, int BN>
-struct Cfg {
-  static constexpr int kStages = FP4 ? 4 : 4;
+template <int BN>
+struct Cfg8 {
+  static constexpr int kStages = 4;
   static constexpr int kABytes = BM * KB_BYTES;
   static constexpr int kBBytes = BN * KB_BYTES;
-  static constexpr int kSfaBytes = FP4 ? 2048 : 0;  // 4 atoms: 128 rows x 16 scales
-  static constexpr int kSfbBytes = FP4 ? 4096 : 0;  // 2 row groups x 4 atoms
-  static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
+  static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kAccCols = BN;
-  // TMEM columns of scale slot s: A scales (16 columns: 4 K blocks x 4) at kSfCol + 48 s, B scales (32 columns:
-  // 4 K blocks x 2 row groups x 4) 16 columns further
-  static constexpr int kSfCol = 2 * BN;
-  static constexpr int kSfSlots = 2;
-  static constexpr int kThreads = FP4 ? 320 : 192;
+  static constexpr int kThreads = 192;
   static constexpr int kTmemCols = 512;
-  static constexpr int kElemsPerKB = FP4 ? 256 : 128;
+  static constexpr int kElemsPerKB = 128;
   // barriers + bookkeeping after the stages
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256;
-  static_assert(2 * BN + (FP4 ? 48 * kSfSlots : 0) <= kTmemCols, "TMEM budget");
-  static_assert(kSfCol % 16 == 0, "scale slots must start 16-column aligned");
+  static_assert(2 * BN <= kTmemCols, "TMEM budget");
   static_assert(kStageBytes % 1024 == 0, "stages must keep 1024-byte alignment");
 };
 
@@ -235,11 +226,11 @@ __device__ __forceinline__ void store_rows_tma(const Problem& p, const Epi& e, c
   }
 }
 
-template <bool FP4, int BN>
-__global__ void __launch_bounds__(Cfg<FP4, BN>::kThreads, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Problem p,
+template <int BN>
+__global__ void __launch_bounds__(Cfg8<BN>::kThreads, 1)
+    gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Problem p,
                 const Epi e) {
-  using C = Cfg<FP4, BN>;
+  using C = Cfg8<BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
@@ -247,9 +238,7 @@ __global__ void __launch_bounds__(Cfg<FP4, BN>::kThreads, 1)
   uint64_t* acc_full = empty + C::kStages;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
-  uint64_t* sf_full = drain + 1;             // [slot] the four scale warps have written the slot
-  uint64_t* sf_empty = sf_full + C::kSfSlots;  // [slot] the MMAs reading the slot have completed
-  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(sf_empty + C::kSfSlots);
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -264,10 +253,6 @@ __global__ void __launch_bounds__(Cfg<FP4, BN>::kThreads, 1)
       mbar_init(&acc_empty[b], 4);
     }
     mbar_init(drain, 1);
-    for (int s = 0; s < C::kSfSlots; ++s) {
-      mbar_init(&sf_full[s], 4);
-      mbar_init(&sf_empty[s], 1);
-    }
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tmA);
@@ -309,16 +294,6 @@ __global__ void __launch_bounds__(Cfg<FP4, BN>::kThreads, 1)
           mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
           tma_load_2d(sA, &tmA, kb * KB_BYTES, m0, &full[stage]);
           tma_load_2d(sB, &tmB, kb * KB_BYTES, n0, &full[stage]);
-          if constexpr (FP4) {
-            uint8_t* sSFA = sB + C::kBBytes;
-            uint8_t* sSFB = sSFA + C::kSfaBytes;
-            const size_t kstride = (size_t)(p.K / 64) * 512;  // bytes per 128-row group
-            bulk_load(sSFA, p.sfa + (size_t)mb * kstride + (size_t)kb * 2048, 2048, &full[stage]);
-            const int g0 = n0 >> 7;
-            const int g1 = min(g0 + 1, p.sfb_groups - 1);
-            bulk_load(sSFB, p.sfb + (size_t)g0 * kstride + (size_t)kb * 2048, 2048, &full[stage]);
-            bulk_load(sSFB + 2048, p.sfb + (size_t)g1 * kstride + (size_t)kb * 2048, 2048, &full[stage]);
-          }
           issued = min(issued + 1, C::kStages);
           if (++stage == C::kStages) {
             stage = 0;
@@ -345,11 +320,10 @@ __global__ void __launch_bounds__(Cfg<FP4, BN>::kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = FP4 ? idesc_nvf4(BN) : idesc_e4m3(BN);
+      const uint32_t idesc = idesc_e4m3(BN);
       int stage = 0;
       uint32_t phase = 0;
       uint32_t acc_phase = 0;
-      uint32_t sf_n = 0;  // scale slots consumed so far: slot sf_n % kSfSlots, parity (sf_n / kSfSlots) & 1
       int j = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++j) {
@@ -363,8 +337,6 @@ __global__ void __launch_bounds__(Cfg<FP4, BN>::kThreads, 1)
         acc_phase ^= 1u << buf;
         tc_fence_after();
         const uint32_t d = tmem + buf * C::kAccCols;
-        // NVFP4 B tiles of 192 rows start mid-atom on odd n-blocks: the first 64 rows sit in columns 2-3 of the atom
-        const uint32_t sfb_shift = (FP4 && (BN % 128) != 0) ? (uint32_t)(((nb * BN) & 127) >> 5) : 0u;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!mbar_wait_bounded(&full[stage], phase, abort_flag, kWaitLimitNs)) {
             fail();
@@ -376,24 +348,8 @@ __global__ void __launch_bounds__(Cfg<FP4, BN>::kThreads, 1)
           uint8_t* sB = sA + C::kABytes;
           const uint64_t da = desc_k_sw128(smem_addr(sA));
           const uint64_t db = desc_k_sw128(smem_addr(sB));
-          if constexpr (FP4) {
-            const int slot = (int)(sf_n % C::kSfSlots);
-            if (!mbar_wait_bounded(&sf_full[slot], (sf_n / C::kSfSlots) & 1u, abort_flag, kWaitLimitNs)) {
-              fail();
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t sfa = tmem + C::kSfCol + 48 * slot, sfb = sfa + 16;
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-              mma_nvf4(d, da + 2 * i, db + 2 * i, idesc, (kb | i) != 0, sfa + 4 * i, sfb + 8 * i + sfb_shift);
-            tc_commit(&sf_empty[slot]);
-            ++sf_n;
-          } else {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) mma_e4m3(d, da + 2 * i, db + 2 * i, idesc, (kb | i) != 0);
-          }
+          for (int i = 0; i < 4; ++i) mma_e4m3(d, da + 2 * i, db + 2 * i, idesc, (kb | i) != 0);
           tc_commit(&empty[stage]);
           if (++stage == C::kStages) {
             stage = 0;
@@ -407,58 +363,6 @@ __global__ void __launch_bounds__(Cfg<FP4, BN>::kThreads, 1)
       tc_commit(drain);
       volatile int no_abort = 0;
       if (!mbar_wait_bounded(drain, 0, &no_abort, kWaitLimitNs)) fail();
-    }
-  } else if (warp >= 6) {
-    // ------------------------------------------------------------------ scale factors (NVFP4)
-    if constexpr (FP4) {
-      // lane r of every 32-lane quarter receives row r of each 512-byte atom (16 bytes: the scales of rows r, r+32,
-      // r+64, r+96 for four 16-element K groups) in the atom's four columns
-      const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-      int stage = 0;
-      uint32_t phase = 0, sf_n = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
-          const int slot = (int)(sf_n % C::kSfSlots);
-          const bool got =
-              (sf_n < C::kSfSlots ||
-               mbar_wait_bounded(&sf_empty[slot], ((sf_n / C::kSfSlots) & 1u) ^ 1u, abort_flag, kWaitLimitNs)) &&
-              mbar_wait_bounded(&full[stage], phase, abort_flag, kWaitLimitNs);
-          if (!__all_sync(0xffffffffu, got)) {
-            if (lane == 0) fail();
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint8_t* sSFA = smem + stage * C::kStageBytes + C::kABytes + C::kBBytes;
-          const uint8_t* sSFB = sSFA + C::kSfaBytes;
-          uint32_t a[16], b0[16], b1[16];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const uint4 x = *reinterpret_cast<const uint4*>(sSFA + 512 * i + 16 * lane);
-            const uint4 y = *reinterpret_cast<const uint4*>(sSFB + 512 * i + 16 * lane);
-            const uint4 z = *reinterpret_cast<const uint4*>(sSFB + 2048 + 512 * i + 16 * lane);
-            uint32_t* bb = i < 2 ? b0 : b1;  // B columns 8i .. 8i+7: group 0 atom, then group 1 atom
-            const int o = 8 * (i & 1);
-            a[4 * i] = x.x, a[4 * i + 1] = x.y, a[4 * i + 2] = x.z, a[4 * i + 3] = x.w;
-            bb[o] = y.x, bb[o + 1] = y.y, bb[o + 2] = y.z, bb[o + 3] = y.w;
-            bb[o + 4] = z.x, bb[o + 5] = z.y, bb[o + 6] = z.z, bb[o + 7] = z.w;
-          }
-          const uint32_t sfa = tmem + lane_off + C::kSfCol + 48 * slot;
-          tmem_st_16cols(sfa, a);
-          tmem_st_16cols(sfa + 16, b0);
-          tmem_st_16cols(sfa + 32, b1);
-          tmem_st_wait();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&sf_full[slot]);
-          ++sf_n;
-          if (++stage == C::kStages) {
-            stage = 0;
-            phase ^= 1;
-          }
-        }
-      }
     }
   } else {
     // ------------------------------------------------------------------ epilogue
@@ -500,11 +404,18 @@ __global__ void __launch_bounds__(Cfg<FP4, BN>::kThreads, 1)
 // 256 x 192 output tiles on a cluster of two CTAs (two SMs) with cta_group::2 MMAs: CTA r of the pair loads rows
 // 128r .. 128r+127 of the A tile and rows 96r .. 96r+95 of the B tile, and holds output rows 128r .. 128r+127 in its
 // TMEM; the even CTA issues every MMA (M = 256, N = 192) over both CTAs' shared memory. Per SM this halves the B
-// bytes per MMA against the single-CTA 128 x 192 tile, and the smaller stage leaves room for six of them.
-// Warp roles in each CTA as in gemm_kernel<true, 192>. Barriers the even CTA's MMA thread waits on (the A/B stage,
-// the scale slots of both CTAs, the accumulator drained by both epilogues) live in the even CTA; the odd CTA's
-// producer, scale warps and epilogue reach them through shared::cluster addresses. MMA completion is committed to
-// the barrier of the same name in each CTA.
+// bytes per MMA against a single-CTA 128 x 192 tile, and the smaller stage leaves room for six of them.
+// Warps of each CTA (10):
+//   warp 0    TMA producer: its A and B halves (cta_group::2 loads completing on the even CTA's stage barrier) and its
+//             scale atoms (bulk copies completing on its own barrier)
+//   warp 1    TMEM allocation (both CTAs); in the even CTA, lane 0 issues the MMAs
+//   warps 2-5 epilogue of this CTA's 128 rows (warp w reads TMEM lanes 32*(w%4) .. +31)
+//   warps 6-9 scale factors: each warp writes the stage's scale atoms into its own 32 TMEM lanes with tcgen05.st (the
+//             replicated image a 32x128b.warpx4 tcgen05.cp would produce) in a ring of TMEM slots, so the tensor
+//             pipe runs MMAs only (a tcgen05.cp costs tensor-pipe time in proportion to the bytes it writes)
+// Barriers the even CTA's MMA thread waits on (the A/B stage, the scale slots of both CTAs, the accumulator drained
+// by both epilogues) live in the even CTA; the odd CTA's producer, scale warps and epilogue reach them through
+// shared::cluster addresses.
 struct PairCfg {
   static constexpr int BN = 192;         // N of one MMA / output tile
   static constexpr int kBRows = BN / 2;  // B rows each CTA loads
@@ -862,11 +773,11 @@ int num_sms() {
   return sms;
 }
 
-template <bool FP4, int BN>
-int run_gemm(const void* A, const uint8_t* sfa, const void* B, const uint8_t* sfb, int64_t M, int64_t N, int64_t K,
-             const h3b_epilogue* epi, cudaStream_t stream) {
-  using C = Cfg<FP4, BN>;
-  const int64_t kbytes = FP4 ? K / 2 : K;
+template <int BN>
+int run_gemm_fp8(const void* A, const void* B, int64_t M, int64_t N, int64_t K, const h3b_epilogue* epi,
+                 cudaStream_t stream) {
+  using C = Cfg8<BN>;
+  const int64_t kbytes = K;
   CUtensorMap ta, tb;
   int rc = make_tmap(&ta, A, M, kbytes, BM);
   if (rc) return rc;
@@ -880,9 +791,9 @@ int run_gemm(const void* A, const uint8_t* sfa, const void* B, const uint8_t* sf
   p.n_blocks = (int)((N + BN - 1) / BN);
   p.k_blocks = (int)(K / C::kElemsPerKB);
   p.num_tiles = p.m_blocks * p.n_blocks;
-  p.sfa = sfa;
-  p.sfb = sfb;
-  p.sfb_groups = (int)((N + 127) / 128);
+  p.sfa = nullptr;
+  p.sfb = nullptr;
+  p.sfb_groups = 0;
   Epi e{epi->alpha,
         epi->alpha_dev,
         epi->row_scale,
@@ -895,7 +806,7 @@ int run_gemm(const void* A, const uint8_t* sfa, const void* B, const uint8_t* sf
         static_cast<const bf16*>(epi->gate),
         static_cast<bf16*>(epi->D),
         epi->ldd};
-  auto kern = gemm_kernel<FP4, BN>;
+  auto kern = gemm_fp8_kernel<BN>;
   static bool attr_set = false;
   if (!attr_set) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) != cudaSuccess)
@@ -1000,7 +911,7 @@ extern "C" int h3b_gemm_fp8(const void* A, const void* B, int64_t M, int64_t N, 
   H3B_REQUIRE(aligned(A, 16) && aligned(B, 16), "gemm_fp8: A and B must be 16-byte aligned");
   if (int rc = check_epilogue(epi, N)) return rc;
   if (M == 0) return H3B_OK;
-  return run_gemm<false, 256>(A, nullptr, B, nullptr, M, N, K, epi, stream);
+  return run_gemm_fp8<256>(A, B, M, N, K, epi, stream);
 }
 
 extern "C" int h3b_gemm_nvfp4(const void* A, const uint8_t* sfa, const void* B, const uint8_t* sfb, int64_t M,

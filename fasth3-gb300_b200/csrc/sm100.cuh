@@ -1,5 +1,6 @@
 // Thin inline-PTX wrappers for the sm_100a instructions the kernels use: mbarriers with bounded waits, TMA / bulk
-// copies (each CTA loads only into its own shared memory), and tcgen05 (TMEM alloc, MMA, SMEM->TMEM copy, TMEM loads, commit).
+// copies (each CTA loads only into its own shared memory), and tcgen05 (TMEM alloc, MMA, TMEM loads and stores,
+// commit), in single-CTA and CTA-pair forms.
 // Descriptor bit layouts follow the PTX ISA "tcgen05 matrix descriptors" and "instruction descriptor" tables.
 #pragma once
 
@@ -225,24 +226,13 @@ __device__ __forceinline__ uint64_t desc_k_sw128(uint32_t saddr) {
          ((uint64_t)2 << 61);
 }
 
-// Descriptor of a 32-row x 16-byte block stored densely (rows 16 bytes apart, no swizzle): the source of
-// tcgen05.cp.32x128b (one 512-byte scale-factor atom).
-__device__ __forceinline__ uint64_t desc_sf_atom(uint32_t saddr) {
-  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(128 >> 4) << 32) | ((uint64_t)1 << 46);
-}
-
 // Instruction descriptors, M = 128, both operands K-major.
 // kind::f8f6f4 with e4m3 x e4m3 -> f32: D format f32 (bits 4-5 = 1), A/B format e4m3 (0), N>>3 at 17, M>>4 at 24.
 __host__ __device__ constexpr uint32_t idesc_e4m3(int n) {
   return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
-// kind::mxf4nvf4 block16 with e2m1 x e2m1, ue4m3 scales: A/B format e2m1 (1) at bits 7 and 10, scale format bit 23 = 0,
-// scale-factor ids 0, K = 64.
-__host__ __device__ constexpr uint32_t idesc_nvf4(int n) {
-  return (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-}
-
-// kind::mxf4nvf4 block16 as above with M = 256 (a cta_group::2 MMA: 128 rows in each CTA of the pair).
+// kind::mxf4nvf4 block16 with e2m1 x e2m1, ue4m3 scales, M = 256 (a cta_group::2 MMA: 128 rows in each CTA of the
+// pair): A/B format e2m1 (1) at bits 7 and 10, scale format bit 23 = 0, scale-factor ids 0, K = 64.
 __host__ __device__ constexpr uint32_t idesc_nvf4_m256(int n) {
   return (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
 }
@@ -253,21 +243,6 @@ __device__ __forceinline__ void mma_e4m3(uint32_t d_tmem, uint64_t a, uint64_t b
       "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
-}
-
-__device__ __forceinline__ void mma_nvf4(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc,
-                                         uint32_t sfa_tmem, uint32_t sfb_tmem) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
-          d_tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(sfa_tmem), "r"(sfb_tmem)
-      : "memory");
-}
-
-// 32 rows x 128 bits from shared memory into TMEM, replicated into all four 32-lane sub-partitions.
-__device__ __forceinline__ void tmem_cp_32x128_x4(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
 }
 
 // This thread's TMEM lane, 32 consecutive 32-bit columns starting at taddr.
