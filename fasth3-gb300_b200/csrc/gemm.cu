@@ -135,39 +135,38 @@ __device__ __forceinline__ void store_rows(const Problem& p, const Epi& e, float
   }
 }
 
-// Epilogue of one warp's 32 accumulator rows (TMEM lanes 32q .. 32q+31) through shared memory and TMA: per 32-column
-// chunk each lane turns its row into bf16 inside a 32 x 64-byte staging box (64-byte swizzle, so the 16-byte accesses
-// of a quarter-warp hit distinct banks) and lane 0 writes the box with one tensor store (full sectors; rows >= M and
-// columns >= N are clipped by the tensor map). With a gated residual the box is first filled with the residual's
-// 32 x 32 block by a TMA load (issued one chunk ahead, completing on the box's mbarrier), so the residual is read
-// with full-sector loads off the critical path and updated in place. Two boxes per warp alternate; `chunk` counts
-// this warp's boxes and `lphase` holds the parity of each box's load barrier.
+// Epilogue of one warp's 32 accumulator rows (TMEM lanes 32q .. 32q+31), chunks c_begin .. c_end-1 of 32 columns,
+// through shared memory and TMA: per chunk each lane turns its row into bf16 inside a 32 x 64-byte staging box
+// (64-byte swizzle, so the 16-byte accesses of a quarter-warp hit distinct banks) and lane 0 writes the box with one
+// tensor store (full sectors; rows >= M and columns >= N are clipped by the tensor map). With a gated residual the box
+// is first filled with the residual's 32 x 32 block by a TMA load issued at the start of the chunk (completing on the
+// box's mbarrier while the accumulator is read and scaled), so the residual is read with full-sector loads and updated
+// in place. One box per warp: before it is refilled, the store that last read it has finished reading. `lphase` holds
+// the parity of the box's load barrier.
 template <int BN>
 __device__ __forceinline__ void store_rows_tma(const Problem& p, const Epi& e, const CUtensorMap* tmD,
                                                const CUtensorMap* tmR, float alpha, uint32_t tbase, int m0, int nb,
-                                               uint8_t* boxes, uint64_t* box_bar, uint32_t& chunk, uint32_t& lphase,
-                                               volatile int* abort_flag, bool& ok) {
+                                               int c_begin, int c_end, uint8_t* box, uint64_t* box_bar,
+                                               uint32_t& lphase, volatile int* abort_flag, bool& ok) {
   const int lane = threadIdx.x & 31;
   const int m = m0 + lane;
   const bool row_ok = m < p.M;
   const float rs = alpha * ((e.row_scale && row_ok) ? e.row_scale[m] : 1.f);
   const bool res = e.residual != nullptr;
   const int sw = (lane >> 1) & 3;
-  // lane 0: residual block of chunk c into box b, once the store that last read the box has finished reading it
-  auto load_residual = [&](int c, uint32_t b) {
-    bulk_wait_read<0>();
-    mbar_arrive_expect_tx(&box_bar[b], 2048);
-    tma_load_2d(boxes + b * 2048, tmR, nb * BN + 32 * c, m0, &box_bar[b]);
-  };
+  uint8_t* row = box + lane * 64;
 #pragma unroll 1
-  for (int c = 0; c < BN / 32; ++c) {
+  for (int c = c_begin; c < c_end; ++c) {
     const int n0 = nb * BN + 32 * c;
     if (m0 >= p.M || n0 >= p.N) break;  // warp-uniform: this and later chunks lie outside the output
-    const uint32_t b = chunk & 1;
-    if (res && lane == 0) {
-      if (c == 0) load_residual(c, b);
-      if (c + 1 < BN / 32 && n0 + 32 < p.N) load_residual(c + 1, b ^ 1);
+    if (lane == 0) {
+      bulk_wait_read<0>();  // the previous store from the box has read it
+      if (res) {
+        mbar_arrive_expect_tx(box_bar, 2048);
+        tma_load_2d(box, tmR, n0, m0, box_bar);
+      }
     }
+    __syncwarp();
     uint32_t r[32];
     tmem_ld_32cols(tbase + 32 * c, r);
     tmem_ld_wait();
@@ -181,13 +180,12 @@ __device__ __forceinline__ void store_rows_tma(const Problem& p, const Epi& e, c
       if (e.act == H3B_ACT_GELU_TANH) x = gelu_tanh(x);
       v[i] = x;
     }
-    uint8_t* row = boxes + b * 2048 + lane * 64;
     if (res) {
-      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&box_bar[b], (lphase >> b) & 1u, abort_flag, kWaitLimitNs))) {
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(box_bar, lphase & 1u, abort_flag, kWaitLimitNs))) {
         ok = false;
         return;
       }
-      lphase ^= 1u << b;
+      lphase ^= 1u;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const uint4 w = *reinterpret_cast<const uint4*>(row + ((j ^ sw) << 4));
@@ -203,9 +201,6 @@ __device__ __forceinline__ void store_rows_tma(const Problem& p, const Epi& e, c
 #pragma unroll
         for (int u = 0; u < 8; ++u) v[8 * j + u] = rv[u] + g[u] * v[8 * j + u];
       }
-    } else {
-      if (lane == 0) bulk_wait_read<1>();  // the store issued from this box two chunks ago has read it
-      __syncwarp();
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -219,10 +214,9 @@ __device__ __forceinline__ void store_rows_tma(const Problem& p, const Epi& e, c
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
-      tma_store_2d(tmD, n0, m0, boxes + b * 2048);
+      tma_store_2d(tmD, n0, m0, box);
       bulk_commit_group();
     }
-    ++chunk;
   }
 }
 
@@ -405,11 +399,12 @@ __global__ void __launch_bounds__(Cfg8<BN>::kThreads, 1)
 // 128r .. 128r+127 of the A tile and rows 96r .. 96r+95 of the B tile, and holds output rows 128r .. 128r+127 in its
 // TMEM; the even CTA issues every MMA (M = 256, N = 192) over both CTAs' shared memory. Per SM this halves the B
 // bytes per MMA against a single-CTA 128 x 192 tile, and the smaller stage leaves room for six of them.
-// Warps of each CTA (10):
+// Warps of each CTA (14):
 //   warp 0    TMA producer: its A and B halves (cta_group::2 loads completing on the even CTA's stage barrier) and its
 //             scale atoms (bulk copies completing on its own barrier)
 //   warp 1    TMEM allocation (both CTAs); in the even CTA, lane 0 issues the MMAs
-//   warps 2-5 epilogue of this CTA's 128 rows (warp w reads TMEM lanes 32*(w%4) .. +31)
+//   warps 2-5, 10-13 epilogue of this CTA's 128 rows (warp w reads TMEM lanes 32*(w%4) .. +31; warps 2-5 take
+//             columns 0-95 of the tile, warps 10-13 columns 96-191), so a tile drains within the next tile's main loop
 //   warps 6-9 scale factors: each warp writes the stage's scale atoms into its own 32 TMEM lanes with tcgen05.st (the
 //             replicated image a 32x128b.warpx4 tcgen05.cp would produce) in a ring of TMEM slots, so the tensor
 //             pipe runs MMAs only (a tcgen05.cp costs tensor-pipe time in proportion to the bytes it writes)
@@ -430,9 +425,10 @@ struct PairCfg {
   static constexpr int kSfCol = 2 * BN;
   static constexpr int kSfSlotCols = 40;
   static constexpr int kSfSlots = 3;
-  static constexpr int kThreads = 320;
+  static constexpr int kThreads = 448;
   static constexpr int kTmemCols = 512;
-  static constexpr int kEpiBytes = 4 * 2 * 2048;  // per epilogue warp two 32 x 64-byte output staging boxes
+  static constexpr int kEpiWarps = 8;                 // two per TMEM lane quarter, each on half of the columns
+  static constexpr int kEpiBytes = kEpiWarps * 2048;  // per epilogue warp one 32 x 64-byte output staging box
   static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + 1024 /*align*/ + 512;
   static_assert(2 * BN + kSfSlotCols * kSfSlots <= kTmemCols, "TMEM budget");
   static_assert(kSfCol % 8 == 0 && kSfSlotCols % 8 == 0, "scale slots are written 8 columns at a time");
@@ -456,7 +452,7 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
   uint64_t* acc_empty = acc_full + 2;               // [buffer] even CTA: both epilogues drained the accumulator
   uint64_t* sf_full = acc_empty + 2;                // [slot] even CTA: both CTAs' scale warps wrote the slot
   uint64_t* drain = sf_full + C::kSfSlots;
-  uint64_t* box_bar = drain + 1;                    // [epilogue warp][box] residual block landed in the box
+  uint64_t* box_bar = drain + 1;                    // [epilogue warp] residual block landed in its box
   uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(box_bar + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
 
@@ -474,7 +470,7 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 8);  // 4 epilogue warps x 2 CTAs
+      mbar_init(&acc_empty[b], 2 * C::kEpiWarps);  // epilogue warps of both CTAs
     }
     for (int s = 0; s < C::kSfSlots; ++s) mbar_init(&sf_full[s], 8);  // 4 scale warps x 2 CTAs
     mbar_init(drain, 1);
@@ -611,7 +607,7 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
       volatile int no_abort = 0;
       if (!mbar_wait_spin(drain, 0, &no_abort, kWaitLimitNs)) fail();
     }
-  } else if (warp >= 6) {
+  } else if (warp >= 6 && warp < 10) {
     // ------------------------------------------------------------------ scale factors into this CTA's TMEM
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     int stage = 0;
@@ -683,8 +679,10 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
     // ------------------------------------------------------------------ epilogue (this CTA's 128 rows)
     const int q = warp & 3;
     const float alpha = e.alpha * (e.alpha_dev ? *e.alpha_dev : 1.f);
-    uint8_t* boxes = epi_boxes + (warp - 2) * 4096;
-    uint32_t acc_phase = 0, chunk = 0, lphase = 0;
+    const int ew = warp < 6 ? warp - 2 : warp - 6;  // epilogue warp 0..7
+    const int half = warp < 6 ? 0 : 1;              // columns 0-95 or 96-191 of the tile
+    uint8_t* box = epi_boxes + ew * 2048;
+    uint32_t acc_phase = 0, lphase = 0;
     bool ok = true;
     int j = 0;
     for (int tile = cluster; tile < p.num_tiles; tile += clusters, ++j) {
@@ -700,8 +698,8 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
       __syncwarp();
       tc_fence_after();
       store_rows_tma<C::BN>(p, e, &tmD, &tmR, alpha, tmem + ((uint32_t)(q * 32) << 16) + buf * C::BN,
-                            (2 * mb2 + (int)rank) * BM + q * 32, nb, boxes, box_bar + 2 * (warp - 2), chunk, lphase,
-                            abort_flag, ok);
+                            (2 * mb2 + (int)rank) * BM + q * 32, nb, 3 * half, 3 * half + 3, box, box_bar + ew,
+                            lphase, abort_flag, ok);
       if (!ok) {
         if (lane == 0) fail();
         break;
