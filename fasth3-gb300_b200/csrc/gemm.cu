@@ -4,10 +4,11 @@
 //   gemm_nvfp4_pair_kernel NVFP4 (kind::mxf4nvf4 block16, e2m1 x e2m1 with ue4m3 scales per 16 K-elements) on CTA
 //                          pairs (cta_group::2), 256x192 tiles; described where it is defined
 //
-// gemm_fp8_kernel: CTA = 6 warps, one CTA per SM (the shared-memory footprint forbids two):
+// gemm_fp8_kernel: CTA = 10 warps, one CTA per SM (the shared-memory footprint forbids two):
 //   warp 0   TMA producer: A/B tiles (128-byte swizzle)
 //   warp 1   TMEM allocator + MMA issuer (one thread): 4 MMAs per 128-byte K block
-//   warps 2-5 epilogue: TMEM -> registers -> epilogue math -> global (warp w reads TMEM lanes 32*(w%4)..+31)
+//   warps 2-9 epilogue: TMEM -> registers -> epilogue math -> global (warp w reads TMEM lanes 32*(w%4)..+31; warps
+//            2-5 take the first half of the tile's columns, warps 6-9 the second)
 // Two accumulator buffers in TMEM let the epilogue of tile j overlap the main loop of tile j+1.
 // Every mbarrier wait is bounded (2 s); on expiry the CTA records H3B_ETIMEOUT in a device status word, the other
 // roles abandon their loops, in-flight copies and MMAs are drained (again bounded) and TMEM is freed.
@@ -36,7 +37,7 @@ struct Cfg8 {
   static constexpr int kBBytes = BN * KB_BYTES;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kAccCols = BN;
-  static constexpr int kThreads = 192;
+  static constexpr int kThreads = 320;  // 2 + 8 epilogue warps (two per TMEM lane quarter, half the columns each)
   static constexpr int kTmemCols = 512;
   static constexpr int kElemsPerKB = 128;
   // barriers + bookkeeping after the stages
@@ -87,13 +88,14 @@ __device__ __forceinline__ float gelu_tanh(float v) {
 }
 
 // Epilogue of one accumulator row: this thread's TMEM lane (tbase = lane address + accumulator column) holds output
-// row m, columns nb*BN .. nb*BN+BN-1.
+// row m, columns nb*BN .. nb*BN+BN-1; this call stores tile columns c_lo .. c_hi-1.
 template <int BN>
-__device__ __forceinline__ void store_rows(const Problem& p, const Epi& e, float alpha, uint32_t tbase, int m, int nb) {
+__device__ __forceinline__ void store_rows(const Problem& p, const Epi& e, float alpha, uint32_t tbase, int m, int nb,
+                                           int c_lo, int c_hi) {
   const bool row_ok = m < p.M;
   const float rs = alpha * ((e.row_scale && row_ok) ? e.row_scale[m] : 1.f);
 #pragma unroll 1
-  for (int c0 = 0; c0 < BN; c0 += 32) {
+  for (int c0 = c_lo; c0 < c_hi; c0 += 32) {
     uint32_t r[32];
     tmem_ld_32cols(tbase + c0, r);
     tmem_ld_wait();
@@ -244,7 +246,7 @@ __global__ void __launch_bounds__(Cfg8<BN>::kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);
+      mbar_init(&acc_empty[b], 8);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -360,7 +362,8 @@ __global__ void __launch_bounds__(Cfg8<BN>::kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------------ epilogue
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int q = warp & 3;         // TMEM lane quarter this warp may access
+    const int half = warp < 6 ? 0 : 1;  // warps 2-5: tile columns 0 .. BN/2-1, warps 6-9: the rest
     const float alpha = e.alpha * (e.alpha_dev ? *e.alpha_dev : 1.f);
     uint32_t acc_phase = 0;
     int j = 0;
@@ -377,7 +380,7 @@ __global__ void __launch_bounds__(Cfg8<BN>::kThreads, 1)
       __syncwarp();
       tc_fence_after();
       store_rows<BN>(p, e, alpha, tmem + ((uint32_t)(q * 32) << 16) + buf * C::kAccCols, mb * BM + q * 32 + lane,
-                     nb);
+                     nb, half * (BN / 2), half * (BN / 2) + BN / 2);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
