@@ -411,9 +411,11 @@ __global__ void __launch_bounds__(Cfg8<BN>::kThreads, 1)
 //   warps 6-9 scale factors: each warp writes the stage's scale atoms into its own 32 TMEM lanes with tcgen05.st (the
 //             replicated image a 32x128b.warpx4 tcgen05.cp would produce) in a ring of TMEM slots, so the tensor
 //             pipe runs MMAs only (a tcgen05.cp costs tensor-pipe time in proportion to the bytes it writes)
-// Barriers the even CTA's MMA thread waits on (the A/B stage, the scale slots of both CTAs, the accumulator drained
-// by both epilogues) live in the even CTA; the odd CTA's producer, scale warps and epilogue reach them through
-// shared::cluster addresses.
+// Barriers the even CTA's MMA thread waits on live in the even CTA: one per stage, which completes when both CTAs'
+// A/B halves have landed and the eight scale warps of the pair have written the stage's scale slot (one wait per
+// stage keeps the issuing thread's gaps between MMAs short), and one per accumulator, drained by both epilogues. The
+// odd CTA's producer, scale warps and epilogue reach them through shared::cluster addresses. Each producer issues its
+// scale copies before its A/B copies, so the scale warps' TMEM writes are not queued behind 28 KB of operand tiles.
 struct PairCfg {
   static constexpr int BN = 192;         // N of one MMA / output tile
   static constexpr int kBRows = BN / 2;  // B rows each CTA loads
@@ -446,15 +448,15 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* epi_boxes = smem + C::kStages * C::kStageBytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(epi_boxes + C::kEpiBytes);  // [stage] even CTA: A/B landed
+  // [stage] even CTA: A/B halves landed (transaction bytes) and the eight scale warps wrote the stage's slot
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_boxes + C::kEpiBytes);
   // [stage] the MMAs reading the stage have completed: one commit per stage into the even CTA's barrier; an even-CTA
   // scale warp relays each completion to the odd CTA's barrier
   uint64_t* empty = full + C::kStages;
   uint64_t* sf_loaded = empty + C::kStages;         // [stage] this CTA's scale atoms landed
   uint64_t* acc_full = sf_loaded + C::kStages;      // [buffer] the tile's MMAs have completed
   uint64_t* acc_empty = acc_full + 2;               // [buffer] even CTA: both epilogues drained the accumulator
-  uint64_t* sf_full = acc_empty + 2;                // [slot] even CTA: both CTAs' scale warps wrote the slot
-  uint64_t* drain = sf_full + C::kSfSlots;
+  uint64_t* drain = acc_empty + 2;
   uint64_t* box_bar = drain + 1;                    // [epilogue warp] residual block landed in its box
   uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(box_bar + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
@@ -467,7 +469,7 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], 1 + 8);  // the even producer's arrive.expect_tx + 4 scale warps x 2 CTAs
       mbar_init(&empty[s], 1);
       mbar_init(&sf_loaded[s], 1);
     }
@@ -475,7 +477,6 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 2 * C::kEpiWarps);  // epilogue warps of both CTAs
     }
-    for (int s = 0; s < C::kSfSlots; ++s) mbar_init(&sf_full[s], 8);  // 4 scale warps x 2 CTAs
     mbar_init(drain, 1);
     for (int i = 0; i < 8; ++i) mbar_init(&box_bar[i], 1);
     *abort_flag = 0;
@@ -529,13 +530,13 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
           uint8_t* sSFA = sB + C::kBBytes;
           uint8_t* sSFB = sSFA + C::kSfaBytes;
           const uint32_t full0 = in_cta(&full[stage], 0);
-          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (C::kABytes + C::kBBytes));
-          tma_load_2d_pair(sA, &tmA, kb * KB_BYTES, mblk * BM, full0);
-          tma_load_2d_pair(sB, &tmB, kb * KB_BYTES, n0 + (int)rank * C::kBRows, full0);
           mbar_arrive_expect_tx(&sf_loaded[stage], C::kSfaBytes + C::kSfbBytes);
           bulk_load(sSFA, sfa_src + (size_t)kb * 2048, 2048, &sf_loaded[stage]);
           bulk_load(sSFB, p.sfb + (size_t)g0 * kstride + (size_t)kb * 2048, 2048, &sf_loaded[stage]);
           bulk_load(sSFB + 2048, p.sfb + (size_t)g1 * kstride + (size_t)kb * 2048, 2048, &sf_loaded[stage]);
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (C::kABytes + C::kBBytes));
+          tma_load_2d_pair(sA, &tmA, kb * KB_BYTES, mblk * BM, full0);
+          tma_load_2d_pair(sB, &tmB, kb * KB_BYTES, n0 + (int)rank * C::kBRows, full0);
           issued = min(issued + 1, C::kStages);
           if (++stage == C::kStages) {
             stage = 0;
@@ -555,7 +556,9 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
           if (i < issued) {
             volatile int no_abort = 0;
             mbar_wait_bounded(&sf_loaded[s], ph, &no_abort, kWaitLimitNs / 4);
-            if (rank == 0) mbar_wait_bounded(&full[s], ph, &no_abort, kWaitLimitNs / 4);
+            // the stage barrier also counts scale-warp arrivals that an aborting pair may never make; its bound (far
+            // above the latency of a copy) ends the wait then
+            if (rank == 0) mbar_wait_bounded(&full[s], ph, &no_abort, kWaitLimitNs / 64);
           }
         }
       }
@@ -581,8 +584,7 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
         const uint32_t d = tmem + buf * C::BN;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           const int slot = (int)(sf_n % C::kSfSlots);
-          if (!mbar_wait_spin(&full[stage], phase, abort_flag, kWaitLimitNs) ||
-              !mbar_wait_spin(&sf_full[slot], (sf_n / C::kSfSlots) & 1u, abort_flag, kWaitLimitNs)) {
+          if (!mbar_wait_spin(&full[stage], phase, abort_flag, kWaitLimitNs)) {
             fail();
             ok = false;
             break;
@@ -670,7 +672,7 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(in_cta(&sf_full[slot], 0));
+        if (lane == 0) mbar_arrive_cluster(in_cta(&full[stage], 0));
         ++sf_n;
         if (++stage == C::kStages) {
           stage = 0;
