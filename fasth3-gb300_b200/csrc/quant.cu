@@ -131,9 +131,18 @@ __global__ void __launch_bounds__(C / 8, 2) resid_norm_quant_kernel(const RowArg
 // warp per row, lane l owns the 8-element chunks l, l+32, l+64, ... (coalesced); the row is staged in shared memory
 // (bf16) by asynchronous copies. Row sums are a sequential float32 sum over a lane's chunks (chunk-major, elements in
 // order) followed by the warp butterfly: no block barriers, so many rows are in flight per SM. With one adaLN table
-// row for all tokens (idx NULL) the CTA first converts it to float32 (1 + scale, shift) in shared memory, so the two
-// modulate passes read four floats per load instead of converting bf16 per element.
-constexpr int LN_WARPS = 16;  // one 512-thread CTA per SM (the row buffers and tables fill its shared memory)
+// row for all tokens (idx NULL) the CTA first copies it into shared memory (bf16: half the bytes the two modulate
+// passes read per row against a float32 copy; 1 + scale is formed per element as in the idx path, so the values are
+// the same). One CTA per SM with as many row buffers as fit beside the table (20 warps at C = 5120).
+constexpr int kLnSmemBudget = 227 * 1024;
+template <int C>
+constexpr int ln_warps() {
+  return (kLnSmemBudget - 4 * C) / (2 * C) < 20 ? (kLnSmemBudget - 4 * C) / (2 * C) : 20;
+}
+template <int C>
+constexpr int ln_smem_bytes() {
+  return ln_warps<C>() * C * 2 + 2 * C * 2;  // row buffers + bf16 table (scale, shift)
+}
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
@@ -143,34 +152,30 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 template <int C, bool BRANCH, bool FP4>
-__global__ void __launch_bounds__(LN_WARPS * 32, 1) layer_norm_quant_warp_kernel(const RowArgs a) {
+__global__ void __launch_bounds__(ln_warps<C>() * 32, 1) layer_norm_quant_warp_kernel(const RowArgs a) {
+  constexpr int LN_WARPS = ln_warps<C>();
   constexpr int J = C / 256;  // chunks per lane
   extern __shared__ __align__(16) uint8_t ln_smem[];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   bf16* row = reinterpret_cast<bf16*>(ln_smem) + (size_t)wid * C;
-  float* t_scale1 = reinterpret_cast<float*>(ln_smem + (size_t)LN_WARPS * C * sizeof(bf16));  // 1 + scale
-  float* t_shift = t_scale1 + C;
+  bf16* tb_scale = reinterpret_cast<bf16*>(ln_smem + (size_t)LN_WARPS * C * sizeof(bf16));
+  bf16* tb_shift = tb_scale + C;
   const bool tab_smem = a.idx == nullptr;
   if (tab_smem) {
     for (int c = threadIdx.x * 8; c < C; c += LN_WARPS * 32 * 8) {
-      float sc[8], sf[8];
-      load8(a.scale + c, sc);
-      load8(a.shift + c, sf);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        t_scale1[c + i] = 1.f + sc[i];
-        t_shift[c + i] = sf[i];
-      }
+      *reinterpret_cast<uint4*>(tb_scale + c) = *reinterpret_cast<const uint4*>(a.scale + c);
+      *reinterpret_cast<uint4*>(tb_shift + c) = *reinterpret_cast<const uint4*>(a.shift + c);
     }
     __syncthreads();
   }
   // the modulate factors of the 8 columns at c: (1 + scale) and shift, from shared memory or from table row tab
   auto modulate_factors = [&](int64_t tab, int c, float (&a1)[8], float (&sf)[8]) {
     if (tab_smem) {
-      const float4 p0 = *reinterpret_cast<const float4*>(t_scale1 + c), p1 = *reinterpret_cast<const float4*>(t_scale1 + c + 4);
-      const float4 q0 = *reinterpret_cast<const float4*>(t_shift + c), q1 = *reinterpret_cast<const float4*>(t_shift + c + 4);
-      a1[0] = p0.x, a1[1] = p0.y, a1[2] = p0.z, a1[3] = p0.w, a1[4] = p1.x, a1[5] = p1.y, a1[6] = p1.z, a1[7] = p1.w;
-      sf[0] = q0.x, sf[1] = q0.y, sf[2] = q0.z, sf[3] = q0.w, sf[4] = q1.x, sf[5] = q1.y, sf[6] = q1.z, sf[7] = q1.w;
+      float sc[8];
+      unpack8(*reinterpret_cast<const uint4*>(tb_scale + c), sc);
+      unpack8(*reinterpret_cast<const uint4*>(tb_shift + c), sf);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) a1[i] = 1.f + sc[i];
     } else {
       float sc[8];
       load8(a.scale + tab * a.tab_ld + c, sc);
@@ -291,9 +296,10 @@ int launch_resid_norm_quant(const RowArgs& a, bool branch, int norm, bool fp4, c
       if (fp4) H3B_RNQ(false, H3B_NORM_RMS, true); else H3B_RNQ(false, H3B_NORM_RMS, false);
     }
   } else {
+    constexpr int LN_WARPS = ln_warps<C>();
     const int64_t blocks = (a.rows + LN_WARPS - 1) / LN_WARPS, cap = (int64_t)sms;
     const dim3 g2((unsigned)(blocks < cap ? blocks : cap)), b2(LN_WARPS * 32);
-    const int lsm = LN_WARPS * C * 2 + 2 * C * 4;  // row buffers + float32 table
+    const int lsm = ln_smem_bytes<C>();
 #define H3B_LNQ(B, Q)                                                                                  \
   do {                                                                                                 \
     if (cudaFuncSetAttribute(layer_norm_quant_warp_kernel<C, B, Q>,                                    \
