@@ -6,6 +6,8 @@
 // (bf16) before the division, the quotient is rounded to bf16, clamped to +-448, then rounded to e4m3.
 #include "common.cuh"
 
+#include <algorithm>
+
 namespace h3b {
 
 int amax_launch(const bf16* x, int64_t ld, int64_t rows, int K, float* amax, cudaStream_t st);
@@ -55,10 +57,87 @@ __global__ void __launch_bounds__(256) pack_fp8_kernel(const bf16* __restrict__ 
   }
 }
 
+// LoRA merge on the base weight's FP8 grid (fastvideo/models/dits/h3fast/__init__.py:82-92, `_on_grid`): the merged
+// fp32 weight keeps the base scale s0 of its row (or tensor) while amax <= 1.05 * 448 * s0 -- evaluated as torch does
+// for a float32 tensor and a Python scalar: fl32(470.4f * s0) -- and otherwise gets its own max(amax / 448, 1e-12);
+// codes are e4m3(clamp(m / s, +-448)) with IEEE division. One CTA per row; `tensor_amax` set selects the tensor form.
+__global__ void __launch_bounds__(256) fp8_on_grid_kernel(const float* __restrict__ m, int K,
+                                                          const float* __restrict__ base, const float* tensor_amax,
+                                                          uint8_t* __restrict__ q, float* __restrict__ scale) {
+  __shared__ float stage[32];
+  const int64_t n = blockIdx.x;
+  const float* row = m + n * K;
+  float am;
+  if (tensor_amax) {
+    am = *tensor_amax;
+  } else {
+    am = 0.f;
+    for (int c = threadIdx.x * 4; c < K; c += 256 * 4) {
+      const float4 f = *reinterpret_cast<const float4*>(row + c);
+      am = fmaxf(am, fmaxf(fmaxf(fabsf(f.x), fabsf(f.y)), fmaxf(fabsf(f.z), fabsf(f.w))));
+    }
+    am = block_allreduce<8, true>(am, stage);
+  }
+  const float s0 = tensor_amax ? base[0] : base[n];
+  const float lim = __fmul_rn(470.4f, s0);
+  const float s = am <= lim ? s0 : fmaxf(__fdiv_rn(am, kFp8Max), 1e-12f);
+  for (int c = threadIdx.x * 4; c < K; c += 256 * 4) {
+    const float4 f = *reinterpret_cast<const float4*>(row + c);
+    const float v[4] = {f.x, f.y, f.z, f.w};
+    uint32_t o = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float x = fminf(fmaxf(__fdiv_rn(v[i], s), -kFp8Max), kFp8Max);
+      o |= (uint32_t)__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3) << (8 * i);
+    }
+    *reinterpret_cast<uint32_t*>(q + n * K + c) = o;
+  }
+  if (threadIdx.x == 0) {
+    if (!tensor_amax) scale[n] = s;
+    else if (n == 0) scale[0] = s;
+  }
+}
+
+// max |x| over an fp32 matrix into *amax (non-negative floats order like their bit patterns as integers).
+__global__ void __launch_bounds__(256) amax_f32_kernel(const float* __restrict__ x, int64_t n, float* amax) {
+  __shared__ float stage[32];
+  float am = 0.f;
+  for (int64_t i = ((int64_t)blockIdx.x * 256 + threadIdx.x) * 4; i < n; i += (int64_t)gridDim.x * 256 * 4) {
+    const float4 f = *reinterpret_cast<const float4*>(x + i);
+    am = fmaxf(am, fmaxf(fmaxf(fabsf(f.x), fabsf(f.y)), fmaxf(fabsf(f.z), fabsf(f.w))));
+  }
+  am = block_allreduce<8, true>(am, stage);
+  if (threadIdx.x == 0 && am > 0.f) atomicMax(reinterpret_cast<int*>(amax), __float_as_int(am));
+}
+
 }  // namespace
 }  // namespace h3b
 
 using namespace h3b;
+
+extern "C" int h3b_quant_fp8_on_grid(const float* merged, int64_t N, int K, const float* base_scale, int per_row,
+                                     void* wq, float* wscale, void* workspace, cudaStream_t stream) {
+  clear_error();
+  H3B_REQUIRE(merged && base_scale && wq && wscale, "quant_fp8_on_grid: null pointer");
+  H3B_REQUIRE(K > 0 && K % 4 == 0 && N >= 0, "quant_fp8_on_grid: K must be a positive multiple of 4");
+  H3B_REQUIRE(aligned(merged, 16) && aligned(wq, 4), "quant_fp8_on_grid: merged 16-byte, wq 4-byte aligned");
+  if (N == 0) return H3B_OK;
+  const float* tam = nullptr;
+  if (!per_row) {
+    H3B_REQUIRE(workspace && aligned(workspace, 256), "quant_fp8_on_grid: tensor mode needs a 256-byte aligned workspace");
+    float* amax = static_cast<float*>(workspace);
+    if (cudaMemsetAsync(amax, 0, sizeof(float), stream) != cudaSuccess)
+      return set_error(H3B_ECUDA, "quant_fp8_on_grid: workspace memset failed");
+    const int64_t n = N * (int64_t)K;
+    const int64_t blocks = std::min<int64_t>((n / 4 + 255) / 256, 148 * 8);
+    amax_f32_kernel<<<(unsigned)blocks, 256, 0, stream>>>(merged, n, amax);
+    H3B_LAUNCH_CHECK("quant_fp8_on_grid (amax)");
+    tam = amax;
+  }
+  fp8_on_grid_kernel<<<(unsigned)N, 256, 0, stream>>>(merged, K, base_scale, tam, static_cast<uint8_t*>(wq), wscale);
+  H3B_LAUNCH_CHECK("quant_fp8_on_grid");
+  return H3B_OK;
+}
 
 extern "C" int h3b_pack_weight_fp8(const void* w, int64_t N, int K, int granularity, void* wq, float* wscale,
                                    void* workspace, cudaStream_t stream) {

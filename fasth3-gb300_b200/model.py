@@ -3,9 +3,10 @@
 40 heads x 128, FFN 13824 with GELU-tanh, adaLN-zero modulation from the timestep, self-attention with per-head
 QK-RMSNorm and 3D RoPE, cross-attention to 512 text tokens of width 4096.
 
-Weights are random-init N(0, 0.02) (no checkpoints), generated on the device from a seed so that every rank of a
-sequence-parallel job holds the same model, and packed once at construction the way FastVideo's quant methods pack a
-checkpoint: NVFP4 (``_nvfp4_weight`` [N, K/2], ``_nvfp4_weight_scale`` 128x4 [pad128(N), K/16], ``_nvfp4_alpha``) or FP8
+Weights come from a dense checkpoint (``weights.load_dit_checkpoint``, names of ``DiTModel.checkpoint_specs``) or are
+random-init N(0, 0.02) (``DiTModel.random``: generated on the device from per-tensor seeds, so that every rank of a
+sequence-parallel job holds the same model); either way they are packed once at construction, block by block, the way
+FastVideo's quant methods pack a checkpoint: NVFP4 (``_nvfp4_weight`` [N, K/2], ``_nvfp4_weight_scale`` 128x4 [pad128(N), K/16], ``_nvfp4_alpha``) or FP8
 per output channel (``_fp8_weight`` [N, K], ``_fp8_weight_scale`` [N]; patches/fastvideo-a01c50a.patch:384-394, 459-460).
 The q/k/v (and cross-attention k/v) linears of a block are packed into one buffer and exposed as row views of it, so
 the runner issues one GEMM for them.
@@ -145,33 +146,88 @@ class DiTModel:
         return torch.stack([blk.scale_shift_table + e0 for blk in self.transformer_blocks])
 
     @staticmethod
-    def random(config: DiTConfig | None = None, device: str | torch.device = "cuda", seed: int = 0) -> "DiTModel":
+    def checkpoint_specs(config: DiTConfig | None = None) -> dict[str, tuple[int, ...]]:
+        """Names and shapes of the dense tensors a checkpoint of this DiT holds (FastVideo-style names: blocks under
+        ``transformer_blocks.{i}``, the self-attention as ``attn``, the cross-attention as ``attn2``)."""
         cfg = config or DiTConfig()
-        C, F, T = cfg.hidden, cfg.ffn, cfg.text_dim
-        g = torch.Generator(device=device)
+        C, F, T, D = cfg.hidden, cfg.ffn, cfg.text_dim, cfg.head_dim
+        specs: dict[str, tuple[int, ...]] = {
+            "time_embedder.linear_1.weight": (C, cfg.freq_dim), "time_embedder.linear_1.bias": (C,),
+            "time_embedder.linear_2.weight": (C, C), "time_embedder.linear_2.bias": (C,),
+            "time_proj.weight": (6 * C, C), "time_proj.bias": (6 * C,)}
+        for i in range(cfg.blocks):
+            p = f"transformer_blocks.{i}."
+            for a, kv in (("attn", C), ("attn2", T)):
+                specs.update({p + f"{a}.to_q.weight": (C, C), p + f"{a}.to_k.weight": (C, kv),
+                              p + f"{a}.to_v.weight": (C, kv), p + f"{a}.to_out.weight": (C, C),
+                              p + f"{a}.norm_q.weight": (D,), p + f"{a}.norm_k.weight": (D,)})
+            specs.update({p + "norm3.weight": (C,), p + "norm3.bias": (C,), p + "ff.fc_in.weight": (F, C),
+                          p + "ff.fc_out.weight": (C, F), p + "scale_shift_table": (6, C)})
+        return specs
 
-        def randn(*shape, std=0.02, s=0):
-            g.manual_seed(seed * 1_000_003 + s)
-            return (torch.randn(*shape, device=device, generator=g, dtype=torch.float32) * std).to(torch.bfloat16)
+    @staticmethod
+    def from_dense(config: DiTConfig, get, device: str | torch.device = "cuda") -> "DiTModel":
+        """Builds the model from dense tensors: ``get(name)`` returns the tensor named in ``checkpoint_specs`` (any
+        device, any float dtype; it is cast to bf16 and moved to ``device``). Linears are packed block by block as
+        they arrive (``config.fmt``), so at most one block's dense weights are on the device at a time."""
+        cfg = config
+        specs = DiTModel.checkpoint_specs(cfg)
+
+        def t(name: str) -> torch.Tensor:
+            x = get(name)
+            if tuple(x.shape) != specs[name]:
+                raise ValueError(f"{name}: shape {tuple(x.shape)}, expected {specs[name]}")
+            return x.to(device=device, dtype=torch.bfloat16).contiguous()
 
         blocks = []
         for i in range(cfg.blocks):
-            base = 100 * (i + 1)
-            q, k, v = QuantLinear.pack_rows([randn(C, C, s=base + j) for j in range(3)], cfg.fmt)
-            (o,) = QuantLinear.pack_rows([randn(C, C, s=base + 3)], cfg.fmt)
-            (cq,) = QuantLinear.pack_rows([randn(C, C, s=base + 4)], cfg.fmt)
-            ck, cv = QuantLinear.pack_rows([randn(C, T, s=base + 5), randn(C, T, s=base + 6)], cfg.fmt)
-            (co,) = QuantLinear.pack_rows([randn(C, C, s=base + 7)], cfg.fmt)
-            (f1,) = QuantLinear.pack_rows([randn(F, C, s=base + 8)], cfg.fmt)
-            (f2,) = QuantLinear.pack_rows([randn(C, F, s=base + 9)], cfg.fmt)
-            ones = lambda s: (1.0 + randn(cfg.head_dim, std=0.1, s=s).float()).to(torch.bfloat16)  # noqa: E731
-            attn = Attention(q, k, v, o, RMSNorm(ones(base + 10), cfg.eps), RMSNorm(ones(base + 11), cfg.eps),
-                             cfg.heads, cfg.head_dim)
-            attn2 = Attention(cq, ck, cv, co, RMSNorm(ones(base + 12), cfg.eps), RMSNorm(ones(base + 13), cfg.eps),
-                              cfg.heads, cfg.head_dim)
-            norm3 = LayerNormAffine(randn(1, C, std=0.1, s=base + 14), randn(1, C, std=0.1, s=base + 15), cfg.eps)
-            table = randn(6, C, std=0.1, s=base + 16)
-            blocks.append(DiTBlock(attn, attn2, norm3, FeedForward(f1, f2), table, cfg.eps))
-        time_mlp = (randn(C, cfg.freq_dim, s=1), randn(C, std=0.0, s=2), randn(C, C, s=3), randn(C, std=0.0, s=4))
-        time_proj = (randn(6 * C, C, s=5), randn(6 * C, std=0.0, s=6))
+            p = f"transformer_blocks.{i}."
+            q, k, v = QuantLinear.pack_rows([t(p + f"attn.to_{n}.weight") for n in "qkv"], cfg.fmt)
+            (o,) = QuantLinear.pack_rows([t(p + "attn.to_out.weight")], cfg.fmt)
+            (cq,) = QuantLinear.pack_rows([t(p + "attn2.to_q.weight")], cfg.fmt)
+            ck, cv = QuantLinear.pack_rows([t(p + "attn2.to_k.weight"), t(p + "attn2.to_v.weight")], cfg.fmt)
+            (co,) = QuantLinear.pack_rows([t(p + "attn2.to_out.weight")], cfg.fmt)
+            (f1,) = QuantLinear.pack_rows([t(p + "ff.fc_in.weight")], cfg.fmt)
+            (f2,) = QuantLinear.pack_rows([t(p + "ff.fc_out.weight")], cfg.fmt)
+            attn = Attention(q, k, v, o, RMSNorm(t(p + "attn.norm_q.weight"), cfg.eps),
+                             RMSNorm(t(p + "attn.norm_k.weight"), cfg.eps), cfg.heads, cfg.head_dim)
+            attn2 = Attention(cq, ck, cv, co, RMSNorm(t(p + "attn2.norm_q.weight"), cfg.eps),
+                              RMSNorm(t(p + "attn2.norm_k.weight"), cfg.eps), cfg.heads, cfg.head_dim)
+            # affine LayerNorm as an adaLN table: shift = bias, scale = weight - 1 (exact in float32, rounded to bf16)
+            w3 = t(p + "norm3.weight").float()
+            norm3 = LayerNormAffine(t(p + "norm3.bias").reshape(1, -1), (w3 - 1.0).to(torch.bfloat16).reshape(1, -1),
+                                    cfg.eps)
+            blocks.append(DiTBlock(attn, attn2, norm3, FeedForward(f1, f2), t(p + "scale_shift_table"), cfg.eps))
+        time_mlp = (t("time_embedder.linear_1.weight"), t("time_embedder.linear_1.bias"),
+                    t("time_embedder.linear_2.weight"), t("time_embedder.linear_2.bias"))
+        time_proj = (t("time_proj.weight"), t("time_proj.bias"))
         return DiTModel(cfg, blocks, time_mlp, time_proj)
+
+    @staticmethod
+    def random_dense(config: DiTConfig | None = None, device: str | torch.device = "cuda", seed: int = 0):
+        """``get(name)`` for ``from_dense``: every tensor N(0, 0.02) (norm weights 1 + N(0, 0.1), adaLN tables and
+        norm3's offsets N(0, 0.1), time biases 0) from its own seed on ``device``, so any subset can be drawn in any
+        order and every rank of a sequence-parallel job draws the same model."""
+        cfg = config or DiTConfig()
+        specs = DiTModel.checkpoint_specs(cfg)
+        names = list(specs)
+        g = torch.Generator(device=device)
+
+        def get(name: str) -> torch.Tensor:
+            g.manual_seed(seed * 1_000_003 + names.index(name))
+            leaf = name.rsplit(".", 1)[-1]
+            if name.startswith("time") and leaf == "bias":
+                return torch.zeros(specs[name], device=device, dtype=torch.bfloat16)
+            std = 0.1 if ("norm" in name or leaf == "scale_shift_table" or leaf == "bias") else 0.02
+            x = torch.randn(*specs[name], device=device, generator=g, dtype=torch.float32) * std
+            if "norm" in name and leaf == "weight":
+                x = 1.0 + x
+            return x.to(torch.bfloat16)
+
+        return get
+
+    @staticmethod
+    def random(config: DiTConfig | None = None, device: str | torch.device = "cuda", seed: int = 0) -> "DiTModel":
+        """Random-init weights (no checkpoints): ``from_dense`` over ``random_dense``."""
+        cfg = config or DiTConfig()
+        return DiTModel.from_dense(cfg, DiTModel.random_dense(cfg, device, seed), device)

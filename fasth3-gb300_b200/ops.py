@@ -132,6 +132,29 @@ def pack_nvfp4_weight(weight: torch.Tensor, workspace: torch.Tensor | None = Non
     return wq, wsf, ws
 
 
+def quant_fp8_on_grid(merged: torch.Tensor, base_scale: torch.Tensor, workspace: torch.Tensor | None = None
+                      ) -> tuple[torch.Tensor, torch.Tensor]:
+    """``_on_grid`` (fastvideo/models/dits/h3fast/__init__.py:82-92): the fp32 ``merged`` weight (a LoRA folded into
+    the dense weight) in E4M3 on the base weight's grid ``base_scale`` (one float32 per output row, or one for the
+    tensor). A row (or the tensor) whose amax exceeds 1.05 x 448 x its grid scale gets its own scale amax / 448.
+    Returns ``(fp8 weight [N, K], float32 scale [N] or [1])``."""
+    _contig(merged, "merged")
+    if merged.dtype != torch.float32:
+        raise RuntimeError("merged must be float32")
+    N, K = merged.shape
+    per_row = base_scale.numel() > 1
+    if per_row and base_scale.numel() != N:
+        raise RuntimeError(f"base_scale has {base_scale.numel()} entries for {N} rows")
+    base = base_scale.reshape(-1).to(torch.float32).contiguous()
+    wq = torch.empty(N, K, device=merged.device, dtype=FP8)
+    ws = torch.empty(N if per_row else 1, device=merged.device, dtype=torch.float32)
+    if workspace is None and not per_row:
+        workspace = torch.empty(256, device=merged.device, dtype=torch.uint8)
+    call("h3b_quant_fp8_on_grid", _p(merged), N, K, _p(base), int(per_row), _p(wq), _p(ws), _p(workspace),
+         _stream(merged))
+    return wq, ws
+
+
 # ------------------------------------------------------------------------------------------------- GEMMs
 def _epilogue(out: torch.Tensor, alpha: float, alpha_dev, row_scale, col_scale, bias, act, residual, gate) -> Epilogue:
     e = Epilogue()

@@ -172,13 +172,7 @@ class H3FastRunner:
         if self.heads % self.ex.world:
             raise ValueError(f"{self.heads} heads do not split over {self.ex.world} ranks")
         self.layouts: dict[tuple, list[_RankState]] = {}
-        self.fused = []
-        for blk in self.blocks:
-            a, c = blk.attn, blk.attn2
-            self.fused.append({
-                "qkv": _fused_rows([a.to_q, a.to_k, a.to_v]), "o": _fused_rows([a.to_out]),
-                "cq": _fused_rows([c.to_q]), "ckv": _fused_rows([c.to_k, c.to_v]), "co": _fused_rows([c.to_out]),
-                "fc_in": _fused_rows([blk.ff.fc_in]), "fc_out": _fused_rows([blk.ff.fc_out])})
+        self.refresh_weights()
         dev = self.blocks[0].scale_shift_table.device
         self.dev = dev
         self.ones_c = torch.ones(self.hidden, device=dev, dtype=torch.bfloat16)
@@ -186,6 +180,20 @@ class H3FastRunner:
         # trace(block, stage, rank, {name: tensor}) after each stage when set (tests and debugging); the tensors are the
         # live buffers, so a tracer that keeps them must copy them
         self.trace = None
+
+    def refresh_weights(self) -> None:
+        """(Re)builds the GEMM B operands of every block from its linears' packed weights: at construction, and after
+        a linear's weights were replaced (a LoRA adapter merged or removed, ``weights.merge_lora_into``). The cached
+        text keys/values are dropped with them."""
+        self.fused = []
+        for blk in self.blocks:
+            a, c = blk.attn, blk.attn2
+            self.fused.append({
+                "qkv": _fused_rows([a.to_q, a.to_k, a.to_v]), "o": _fused_rows([a.to_out]),
+                "cq": _fused_rows([c.to_q]), "ckv": _fused_rows([c.to_k, c.to_v]), "co": _fused_rows([c.to_out]),
+                "fc_in": _fused_rows([blk.ff.fc_in]), "fc_out": _fused_rows([blk.ff.fc_out])})
+        if hasattr(self, "text_cache"):
+            self.text_cache.clear()
 
     @staticmethod
     def supported(model: DiTModel, meta: VsaMeta) -> bool:

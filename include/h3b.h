@@ -34,7 +34,7 @@ const char* h3b_last_error(void);
 const char* h3b_version(void);
 
 /* ---------------------------------------------------------------------------------------------------------------
- * Row quantizers (SURVEY a1, a2, a12).
+ * Row quantizers.
  * Replaces resid_norm_quant_op (fastvideo/models/dits/h3fast/h3fast.cu:831-858; kernel :188-265).
  *
  *   branch  (y != NULL):  x' = bf16(x + gate[idx[r]] * (sy[r] * y)), written to xo (xo may alias x)
@@ -97,7 +97,7 @@ int h3b_quant_nvfp4_noalloc(const void* x, int64_t ld, int64_t rows, int K, void
                             cudaStream_t stream);
 
 /* ---------------------------------------------------------------------------------------------------------------
- * Offline weight packing (SURVEY a3).
+ * Offline weight packing.
  * FP8: replaces quantize_fp8_weight (patches/fastvideo-a01c50a.patch:384-394):
  *   channel: s[n] = max(amax_n/448, FP8_MIN_SCALE); wq = e4m3(clamp(bf16(w / bf16(s[n])), +-448))
  *   tensor:  s[0] = max(amax/448, FP8_MIN_SCALE);   wq = e4m3(clamp(bf16(w / bf16(s[0])), +-448))
@@ -113,8 +113,16 @@ int h3b_pack_weight_fp8(const void* w, int64_t N, int K, int granularity, void* 
 int h3b_pack_weight_nvfp4(const void* w, int64_t N, int K, void* wq, uint8_t* wsf, float* wscale, void* workspace,
                           cudaStream_t stream);
 
+/* LoRA merge on the base weight's FP8 grid: replaces `_on_grid` (fastvideo/models/dits/h3fast/__init__.py:82-92),
+ * which H3FastRunner._merged_fp8 (:354-376) applies to W + scale * B @ A (merged in fp32). merged fp32 [N, K];
+ * base_scale fp32 [N] (per_row = 1) or [1] (per_row = 0). Per row (or for the tensor): amax = max|merged|;
+ * s = base_scale when amax <= fl32(470.4f * base_scale), else max(amax / 448, 1e-12); wq = e4m3(clamp(merged / s,
+ * +-448)) with IEEE division; wscale = s. `workspace` (>= 256 bytes, 256-aligned) is used when per_row = 0. */
+int h3b_quant_fp8_on_grid(const float* merged, int64_t N, int K, const float* base_scale, int per_row, void* wq,
+                          float* wscale, void* workspace, cudaStream_t stream);
+
 /* ---------------------------------------------------------------------------------------------------------------
- * tcgen05 GEMMs with a fused epilogue (SURVEY a4, a5, a11, a12).
+ * tcgen05 GEMMs with a fused epilogue.
  * FP8 replaces torch._scaled_mm(a, w.T, scale_a, scale_b) in H3FastRunner._gemm
  *   (fastvideo/models/dits/h3fast/__init__.py:378-392), NVFP4 replaces FlashInfer mm_fp4 (:393-404).
  *
@@ -151,7 +159,7 @@ int h3b_gemm_nvfp4(const void* A, const uint8_t* sfa, const void* B, const uint8
                    int64_t K, const h3b_epilogue* epi, cudaStream_t stream);
 
 /* ---------------------------------------------------------------------------------------------------------------
- * VSA coarse step and prologue and the attention-output gate (a10).
+ * VSA coarse step and prologue, and the attention-output gate.
  * ------------------------------------------------------------------------------------------------------------- */
 
 /* Replaces qkv_prologue8_op (fastvideo/models/dits/h3fast/h3fast.cu:889-927; kernel :376-510) for 64-token tiles.

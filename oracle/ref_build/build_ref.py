@@ -6,7 +6,8 @@ This is this repository's recipe, not the reference's build system: nvcc is driv
 because the reference TU is a torch extension. The output lands only in ``oracle/_ref/`` (git-ignored; it travels to
 the GPU box with the snapshot, where ``load()`` imports the prebuilt file without the reference sources).
 
-Run: ``python oracle/ref_build/build_ref.py`` (needs the reference at $H3_REFERENCE or /root/reference).
+Run: ``python oracle/ref_build/build_ref.py`` (needs the reference source tree: $H3_REFERENCE, else the default
+of ``reference_root()``).
 """
 from __future__ import annotations
 

@@ -103,3 +103,28 @@ TOPK_CASES = {
 PROLOGUE_CASES = {"prologue8_h2": dict(heads=2, n_tiles=10, seed=24)}
 GATE_CASES = {"gate5120_fp8": dict(heads=40, vbs=[16, 32], seed=25, fp4=False),
               "gate5120_fp4": dict(heads=40, vbs=[16, 32], seed=26, fp4=True)}
+
+
+def lora_inputs(N: int, K: int, rank: int, seed: int, per_row: bool, big_every: int, big: float
+                ) -> dict[str, torch.Tensor]:
+    """A dense weight N(0, 0.02) with its FP8 grid (per-row or per-tensor amax/448) and a LoRA pair (A [rank, K],
+    B [N, rank]) whose product is scaled up by ``big`` on every ``big_every``-th row, so that some rows (or the tensor)
+    outgrow the grid's 5% slack and take their own scale."""
+    g = torch.Generator().manual_seed(seed)
+    w = (torch.randn(N, K, generator=g) * 0.02).bfloat16()
+    A = (torch.randn(rank, K, generator=g) * 0.05).bfloat16()
+    B = (torch.randn(N, rank, generator=g) * 0.01).bfloat16()
+    if big_every:
+        B[::big_every] *= big
+    amax = w.float().abs().amax(dim=1) if per_row else w.float().abs().amax().reshape(1)
+    base = (amax / 448.0).clamp(min=1.0 / (448.0 * 512.0)).float()
+    return {"w": w, "A": A, "B": B, "base_scale": base}
+
+
+LORA_CASES = {
+    "lora_rows": dict(N=128, K=256, rank=16, seed=31, per_row=True, big_every=7, big=40.0, strength=0.8, alpha=32.0),
+    "lora_tensor_own": dict(N=64, K=256, rank=8, seed=32, per_row=False, big_every=5, big=60.0, strength=1.0,
+                            alpha=8.0),
+    "lora_tensor_grid": dict(N=64, K=256, rank=8, seed=33, per_row=False, big_every=0, big=1.0, strength=0.5,
+                             alpha=16.0),
+}

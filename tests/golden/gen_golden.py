@@ -2,7 +2,8 @@
 built from the reference's ``h3fast.cu`` by ``oracle/ref_build/build_ref.py``) on a B200.
 
 Run on a GPU box: ``python tests/golden/gen_golden.py``; it writes ``tests/golden/<case>.npz`` (and a copy under
-``gpurun_out/golden/`` so a remote run can bring them back). Only the reference's outputs are stored.
+the repository's returned-output folder, so a remote run can bring them back). Only the reference's outputs are
+stored.
 """
 from __future__ import annotations
 

@@ -1,4 +1,4 @@
-"""GPU parity of the tcgen05 GEMMs and their fused epilogues (SURVEY rows a4, a5, a11, a12).
+"""GPU parity of the tcgen05 GEMMs and their fused epilogues.
 
 Oracle: the reference's dequantize-then-matmul in fp32 (its CPU torch path), the epilogue applied in fp32, then
 rounded to bf16 like the kernel's output. Tolerance: rel-Frobenius <= 1e-3 for both FP8 and NVFP4 (the north star

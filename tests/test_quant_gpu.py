@@ -1,4 +1,4 @@
-"""GPU parity of the quantizers and weight packing (SURVEY rows a1, a2, a3, a12).
+"""GPU parity of the quantizers and weight packing.
 
 Three references, strongest first:
   1. the golden outputs of the reference's own kernels (tests/golden, bit-exact);

@@ -1,4 +1,4 @@
-"""GPU parity of the VSA coarse step, prologue and attention-output gate (SURVEY rows a6, a7, a8, a10).
+"""GPU parity of the VSA coarse step, prologue and attention-output gate.
 
 Bit-exact against the reference kernels (golden outputs and, where oracle/_ref is present, live runs) for the
 prologue, top-k selection and gate-quant; bit-exact against the CPU oracle for the tile scores and for the indices
