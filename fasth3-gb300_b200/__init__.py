@@ -7,6 +7,6 @@ from __future__ import annotations
 
 from . import ops  # noqa: F401
 from ._lib import LIB_PATH, lib  # noqa: F401
-from . import layout, model, runner, sp, weights  # noqa: F401,E402
+from . import layout, model, reduction, runner, sp, weights  # noqa: F401,E402
 
-__all__ = ["ops", "lib", "LIB_PATH", "layout", "model", "runner", "sp", "weights"]
+__all__ = ["ops", "lib", "LIB_PATH", "layout", "model", "reduction", "runner", "sp", "weights"]

@@ -66,15 +66,19 @@ def rope_3d(layout: TileLayout, rot_dims: int = 96, theta: float = 10000.0) -> t
     (d, d + rot_dims/2) (the reference's RoPE form, tests/test_kernels.py:49-52). The rot_dims/2 frequencies are split
     evenly over the (t, h, w) axes."""
     T, H, W = layout.grid
+    pos = torch.stack([layout.perm // (H * W), (layout.perm // W) % H, layout.perm % W], 1)
+    return rope_positions(pos, rot_dims, theta)
+
+
+def rope_positions(pos: torch.Tensor, rot_dims: int = 96, theta: float = 10000.0) -> tuple[torch.Tensor, torch.Tensor]:
+    """cos/sin [rows, rot_dims] (bf16) of rows at (t, h, w) positions ``pos`` [rows, 3] (integer grid coordinates, or
+    the half-integer mean positions of token pairs), in the form of ``rope_3d``."""
     half = rot_dims // 2
     per_axis = half // 3
-    t = layout.perm // (H * W)
-    h = (layout.perm // W) % H
-    w = layout.perm % W
     ang = []
-    for pos in (t, h, w):
+    for a in range(3):
         freqs = theta ** (-torch.arange(per_axis, dtype=torch.float64) / per_axis)
-        ang.append(pos.double()[:, None] * freqs[None, :])
+        ang.append(pos[:, a].double()[:, None] * freqs[None, :])
     a = torch.cat(ang, 1)
     a = torch.cat([a, torch.zeros(a.shape[0], half - a.shape[1], dtype=torch.float64)], 1)
     cos = torch.cat([a.cos(), a.cos()], 1)

@@ -101,6 +101,36 @@ def quant_nvfp4(x: torch.Tensor, q: torch.Tensor, sf: torch.Tensor, s_out: torch
          _p(workspace), _stream(x))
 
 
+# ------------------------------------------------------------------------------------------------- token reduction
+def pool_pairs(x: torch.Tensor, ia: torch.Tensor, ib: torch.Tensor, out: torch.Tensor,
+               pooled: torch.Tensor | None = None) -> torch.Tensor:
+    """``H3FastRunner._pool`` (fastvideo/models/dits/h3fast/__init__.py:280-285): ``out[r] = (x[ia[r]] + x[ib[r]]) / 2``
+    in float32 for bf16 rows; ``pooled`` (optional) receives the same rows."""
+    _contig(x, "x")
+    _contig(out, "out")
+    C = x.shape[-1]
+    for t, n in ((ia, "ia"), (ib, "ib")):
+        if t.dtype != torch.int32 or t.numel() != out.shape[0]:
+            raise RuntimeError(f"{n} must be int32 with one entry per output row")
+    call("h3b_pool_pairs", _p(x), _p(ia), _p(ib), out.shape[0], C, _p(out), _p(pooled), _stream(x))
+    return out
+
+
+def expand_pairs(x: torch.Tensor, xr: torch.Tensor, pooled: torch.Tensor, par: torch.Tensor, pair: torch.Tensor,
+                 scale: float) -> torch.Tensor:
+    """``H3FastRunner._expand`` (:287-293), in place on ``x``: a paired row becomes ``x + scale * (xr - pooled)`` of
+    its reduced row ``par``, every other row takes ``xr[par]``."""
+    _contig(x, "x")
+    C = x.shape[-1]
+    if par.dtype != torch.int32 or par.numel() != x.shape[0] or pair.numel() != x.shape[0]:
+        raise RuntimeError("par (int32) and pair need one entry per row of x")
+    if pair.dtype not in (torch.bool, torch.uint8) or not pair.is_contiguous():
+        raise RuntimeError("pair must be a contiguous bool or uint8 mask")
+    call("h3b_expand_pairs", _p(x), x.shape[0], _p(xr), _p(pooled), _p(par), _p(pair.view(torch.uint8) if pair.dtype == torch.bool else pair), C,
+         float(scale), _stream(x))
+    return x
+
+
 # ------------------------------------------------------------------------------------------------- weight packing
 def quantize_fp8_weight(weight: torch.Tensor, granularity: str = "tensor",
                         workspace: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:

@@ -21,6 +21,7 @@ the all-to-all (NCCL), the timestep MLP and the token permutation.
 """
 from __future__ import annotations
 
+import dataclasses
 import math
 from dataclasses import dataclass, field
 
@@ -28,8 +29,9 @@ import torch
 import torch.distributed as dist
 
 from . import ops
-from .layout import TILE, TileLayout, rope_3d, tile_layout
+from .layout import TILE, TileLayout, rope_3d, rope_positions, tile_layout
 from .model import DiTModel, QuantLinear
+from .reduction import TokenReduction, pair_maps
 from .sp import SeqParallel
 
 LOG2E = 1.4426950408889634
@@ -217,8 +219,8 @@ class H3FastRunner:
             ops.gemm_fp8(a, w, out, scale_a=row_scale, scale_b=col, act=act, residual=residual, gate=gate)
 
     # ------------------------------------------------------------------------------------------------- layout
-    def _layouts(self, meta: VsaMeta, rotary) -> tuple[TileLayout, list[_RankState]]:
-        key = (tuple(meta.grid), self.ex.world, tuple(self.ex.ranks))
+    def _layouts(self, meta: VsaMeta, rotary, tag: object = None) -> tuple[TileLayout, list[_RankState]]:
+        key = (tuple(meta.grid), self.ex.world, tuple(self.ex.ranks), tag)
         hit = self.layouts.get(key)
         if hit is not None:
             return hit
@@ -339,11 +341,13 @@ class H3FastRunner:
     # ------------------------------------------------------------------------------------------------- forward
     def forward(self, packed: torch.Tensor, temb: torch.Tensor, adaln_indices: torch.Tensor | None,
                 rotary: tuple[torch.Tensor, torch.Tensor] | None, meta: VsaMeta,
-                context: torch.Tensor | None = None) -> torch.Tensor:
+                context: torch.Tensor | None = None, reduction: TokenReduction | None = None) -> torch.Tensor:
         """All blocks; ``packed`` [1, S, C] bf16 in token order (the full sequence on every rank), ``temb`` [1, C]
         timestep embedding, ``adaln_indices`` [S] int (table row per token; None: one row), ``rotary`` (cos, sin)
         [S, 96] in token order (None: 3D RoPE from meta.grid), ``context`` [1, L, 4096] text. Returns [1, S, C] in
-        token order, identical on every rank (the shards are gathered at the end)."""
+        token order, identical on every rank (the shards are gathered at the end). ``reduction`` (one rank only, like
+        the reference runner): blocks [begin, end) run on horizontally paired tokens (``reduction.build_token_reduction``
+        over meta.grid), pooled before block ``begin`` and expanded before block ``end`` (__init__.py:406-430)."""
         if context is None:
             raise ValueError("the cross-attention needs context")
         full, states = self._layouts(meta, rotary)
@@ -362,14 +366,57 @@ class H3FastRunner:
             st.b["adaln"] = None
         for st in states:
             self._norm(st, self.blocks[0].eps, tabs[0, 0:1], tabs[0, 1:2], 0)
+        red = self._reduced(reduction, meta) if reduction is not None else None
+        cur = (full, states, meta)
         for i, blk in enumerate(self.blocks):
-            self._block(i, blk, full, states, tabs, txt, meta)
+            if red is not None and i in (reduction.begin, reduction.end):
+                L, Rst = states[0].b, red["states"][0].b
+                if i == reduction.begin:
+                    ops.pool_pairs(L["x"], red["ia"], red["ib"], Rst["x"], red["pooled"])
+                    cur = (red["full"], red["states"], red["meta"])
+                else:
+                    ops.expand_pairs(L["x"], Rst["x"], red["pooled"], red["par"], red["pair"], reduction.update_scale)
+                    cur = (full, states, meta)
+                # the previous block ended with this block's norm1 on the other layout
+                self._norm(cur[1][0], blk.eps, tabs[i, 0:1], tabs[i, 1:2], i)
+            self._block(i, blk, cur[0], cur[1], tabs, txt, cur[2])
+        if red is not None and reduction.begin < len(self.blocks) <= reduction.end:
+            ops.expand_pairs(states[0].b["x"], red["states"][0].b["x"], red["pooled"], red["par"], red["pair"],
+                             reduction.update_scale)
         per = full.n_tiles // self.ex.world
         rows_all = [int(full.vbs[p * per:(p + 1) * per].sum()) for p in range(self.ex.world)]
         out = self.ex.all_gather_rows([st.b["x"] for st in states], rows_all)  # global tile order
         inv = torch.empty_like(full.perm)
         inv[full.perm] = torch.arange(full.rows)
         return out.index_select(0, inv.to(out.device)).unsqueeze(0)
+
+    def _reduced(self, plan: TokenReduction, meta: VsaMeta) -> dict:
+        """The paired layout of ``plan`` (its grid at half width, RoPE at the pairs' mean positions) and the compact-row
+        maps between it and the full layout (``_pair_maps``, __init__.py:262-278), cached per plan."""
+        if self.ex.world != 1:
+            raise ValueError("token reduction runs on one rank (the reference runner is single-GPU)")
+        if tuple(plan.grid) != tuple(meta.grid) or plan.video_start != 0:
+            raise ValueError(f"the reduction plan's grid {plan.grid} (video_start {plan.video_start}) is not "
+                             f"the sequence's {tuple(meta.grid)}")
+        cache = self.__dict__.setdefault("_red_cache", {})
+        hit = cache.get(id(plan))
+        if hit is not None and hit["plan"] is plan:
+            return hit
+        cache.clear()
+        rmeta = dataclasses.replace(meta, grid=plan.reduced_grid)
+        rotary = rope_positions(plan.positions)
+        rfull, rstates = self._layouts(rmeta, rotary, tag=("pairs", plan.positions.data_ptr()))
+        for st in rstates:
+            st.b["adaln"] = None  # one timestep: every pair takes table row 0, as its first source does
+        full, _ = self._layouts(meta, None)
+        maps = pair_maps(plan, full.perm, rfull.perm)
+        dev = self.dev
+        hit = {"plan": plan, "meta": rmeta, "full": rfull, "states": rstates,
+               "ia": maps["ia"].to(dev), "ib": maps["ib"].to(dev), "par": maps["par"].to(dev),
+               "pair": maps["pair"].to(dev), "pooled": torch.empty(rfull.rows, self.hidden, device=dev,
+                                                                    dtype=torch.bfloat16)}
+        cache[id(plan)] = hit
+        return hit
 
     def _norm(self, st: _RankState, eps: float, shift: torch.Tensor, scale: torch.Tensor, i: int,
               stage: str = "norm1") -> None:

@@ -122,6 +122,19 @@ int h3b_quant_fp8_on_grid(const float* merged, int64_t N, int K, const float* ba
                           float* wscale, void* workspace, cudaStream_t stream);
 
 /* ---------------------------------------------------------------------------------------------------------------
+ * Token reduction around an interval of blocks (horizontal pairs of video tokens): replace H3FastRunner._pool and
+ * _expand (fastvideo/models/dits/h3fast/__init__.py:280-293), whose arithmetic is pool_token_pairs /
+ * expand_token_pairs (fastvideo/models/dits/minimax_h3_token_reduction.py:124-150). Rows are bf16 [*, C], C % 8 == 0,
+ * 16-byte aligned; float32 arithmetic, one bf16 rounding at the store.
+ *   pool:   out[r] = (x[ia[r]] + x[ib[r]]) * 0.5 for r < rows_out (ia == ib copies); pooled (may be NULL) gets the same.
+ *   expand: x[i] = pair[i] ? x[i] + scale * (xr[par[i]] - pooled[par[i]]) : xr[par[i]] for i < rows (in place).
+ * ------------------------------------------------------------------------------------------------------------- */
+int h3b_pool_pairs(const void* x, const int32_t* ia, const int32_t* ib, int64_t rows_out, int C, void* out,
+                   void* pooled, cudaStream_t stream);
+int h3b_expand_pairs(void* x, int64_t rows, const void* xr, const void* pooled, const int32_t* par,
+                     const uint8_t* pair, int C, float scale, cudaStream_t stream);
+
+/* ---------------------------------------------------------------------------------------------------------------
  * tcgen05 GEMMs with a fused epilogue.
  * FP8 replaces torch._scaled_mm(a, w.T, scale_a, scale_b) in H3FastRunner._gemm
  *   (fastvideo/models/dits/h3fast/__init__.py:378-392), NVFP4 replaces FlashInfer mm_fp4 (:393-404).

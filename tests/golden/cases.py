@@ -128,3 +128,25 @@ LORA_CASES = {
     "lora_tensor_grid": dict(N=64, K=256, rank=8, seed=33, per_row=False, big_every=0, big=1.0, strength=0.5,
                              alpha=16.0),
 }
+
+
+REDUCTION_CASES = {
+    "red_odd_prefix": dict(grid=(3, 4, 5), video_start=3, C=64, seed=41, scale=0.7),
+    "red_even": dict(grid=(2, 3, 8), video_start=0, C=128, seed=42, scale=1.0),
+}
+
+
+def reduction_inputs(grid: tuple[int, int, int], video_start: int, C: int, seed: int) -> dict[str, torch.Tensor]:
+    """Hidden states [1, S, C] bf16 N(0, 1), float positions [S, 3] (prefix rows at t = -1), and a per-row update of
+    the reduced rows N(0, 0.25) (what the reduced blocks add to the pooled stream)."""
+    t, h, w = grid
+    S = video_start + t * h * w
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(1, S, C, generator=g).bfloat16()
+    tok = torch.arange(t * h * w)
+    pos = torch.zeros(S, 3, dtype=torch.float32)
+    pos[:video_start, 0] = -1.0
+    pos[video_start:] = torch.stack([tok // (h * w), (tok // w) % h, tok % w], 1).float()
+    R = video_start + t * h * ((w + 1) // 2)
+    delta = (torch.randn(1, R, C, generator=g) * 0.25).bfloat16()
+    return {"x": x, "positions": pos, "delta": delta}
