@@ -345,12 +345,33 @@ def dit_step_secondary(pkg, dev, stream, args, ws) -> dict:
         ms = float(t.item())
         dist.barrier()
     finite = bool(torch.isfinite(out.float()).all())
+    reduced = None
+    if args.dit_reduction and ws == 1:
+        # token reduction (one rank, like the reference runner): blocks [begin, end) on horizontally paired tokens
+        parts = args.dit_reduction.split(":")
+        b, e = int(parts[0]), int(parts[1])
+        scale = float(parts[2]) if len(parts) > 2 else 1.0
+        plan = pkg.reduction.build_token_reduction(grid, b, min(e, cfg.blocks), scale)
+        for _ in range(2):
+            out = r.forward(x, temb, None, None, meta, context=ctx, reduction=plan)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(reps):
+            out = r.forward(x, temb, None, None, meta, context=ctx, reduction=plan)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        reduced = {"blocks": [b, min(e, cfg.blocks)], "update_scale": scale, "reduced_grid": list(plan.reduced_grid),
+                   "ms_per_step": e0.elapsed_time(e1) / reps, "output_finite": bool(torch.isfinite(out.float()).all())}
     lin = 2.0 * S * (6 * cfg.hidden ** 2 + 2 * cfg.hidden * cfg.ffn) * cfg.blocks
     del r, m, x, out
     torch.cuda.empty_cache()
-    return {"grid": list(grid), "tokens": S, "blocks": cfg.blocks, "topk": args.dit_topk, "n_gpus": ws,
-            "ms_per_step": ms, "steps": reps, "linear_tflop_per_step": lin / 1e12, "linear_share_tflops": lin / (ms * 1e-3) / 1e12,
-            "output_finite": finite, "scaling": "strong", "parallelism": f"sp{ws}"}
+    res = {"grid": list(grid), "tokens": S, "blocks": cfg.blocks, "topk": args.dit_topk, "n_gpus": ws,
+           "ms_per_step": ms, "steps": reps, "linear_tflop_per_step": lin / 1e12,
+           "linear_share_tflops": lin / (ms * 1e-3) / 1e12, "output_finite": finite, "scaling": "strong",
+           "parallelism": f"sp{ws}"}
+    if reduced is not None:
+        res["token_reduction"] = reduced
+    return res
 
 
 def run_only(args) -> None:
@@ -555,6 +576,8 @@ def run_ours(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--dit-reduction", default="", metavar="BEGIN:END[:SCALE]",
+                    help="also time the config-5 step with token reduction over blocks [BEGIN, END) (one GPU)")
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
