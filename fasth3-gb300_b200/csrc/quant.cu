@@ -383,11 +383,12 @@ __global__ void __launch_bounds__(256, 4) amax_kernel(const bf16* __restrict__ x
 // Warp-cooperative, one warp per row at a time: a unit is 256 consecutive elements of the row, lane l holding
 // elements 8l .. 8l+7, so every load instruction reads 512 contiguous bytes and every code store writes 128. A
 // 16-element block spans lanes 2k and 2k+1 (one shuffle for its maximum); lanes 8j gather the four scales of blocks
-// 4j .. 4j+3 (adjacent bytes of one atom row) and write them as one word. A warp keeps 8 units' loads in flight;
-// rows past `rows` up to the next multiple of 128 get zero scales (the atom layout's padding).
-constexpr int kQuantUnits = 8;
+// 4j .. 4j+3 (adjacent bytes of one atom row) and write them as one word. A warp converts 5 units while the next 5
+// units' loads are in flight (a 5120-wide row is 4 batches); rows past `rows` up to the next multiple of 128 get zero
+// scales (the atom layout's padding).
+constexpr int kQuantUnits = 5;
 
-__global__ void __launch_bounds__(256, 4) quant_nvfp4_tensor_kernel(const bf16* __restrict__ x, int64_t ld, int64_t rows,
+__global__ void __launch_bounds__(256, 3) quant_nvfp4_tensor_kernel(const bf16* __restrict__ x, int64_t ld, int64_t rows,
                                                                     int K, const float* __restrict__ amax,
                                                                     uint8_t* __restrict__ q, uint8_t* __restrict__ sf,
                                                                     float* __restrict__ s_out) {
@@ -398,42 +399,59 @@ __global__ void __launch_bounds__(256, 4) quant_nvfp4_tensor_kernel(const bf16* 
   const int64_t sf_cols = K / 16;
   if (blockIdx.x == 0 && threadIdx.x == 0) s_out[0] = s;
   const int64_t nwarps = (int64_t)gridDim.x * 8;
-  for (int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); r < rows_pad; r += nwarps) {
+  constexpr int U = kQuantUnits;
+  auto load = [&](int64_t r, int c0, uint4 (&raw)[U]) {
     const bf16* src = x + r * ld;
     const bool row_live = r < rows;
-    for (int c0 = 0; c0 < K; c0 += kQuantUnits * 256) {
-      uint4 raw[kQuantUnits];
 #pragma unroll
-      for (int t = 0; t < kQuantUnits; ++t) {
-        const int col = c0 + t * 256 + 8 * lane;
-        raw[t] = (row_live && col < K) ? __ldg(reinterpret_cast<const uint4*>(src + col)) : make_uint4(0u, 0u, 0u, 0u);
-      }
+    for (int t = 0; t < U; ++t) {
+      const int col = c0 + t * 256 + 8 * lane;
+      raw[t] = (row_live && col < K) ? __ldg(reinterpret_cast<const uint4*>(src + col)) : make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+  // the warp walks its (row, 5-unit batch) positions in order, the next batch's loads in flight while the current
+  // one is converted
+  int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  int c0 = 0;
+  uint4 cur[U], nxt[U];
+  if (r < rows_pad) load(r, c0, cur);
+  while (r < rows_pad) {
+    int c1 = c0 + U * 256;
+    int64_t r1 = r;
+    if (c1 >= K) {
+      c1 = 0;
+      r1 = r + nwarps;
+    }
+    if (r1 < rows_pad) load(r1, c1, nxt);
+    const bool row_live = r < rows;
 #pragma unroll
-      for (int t = 0; t < kQuantUnits; ++t) {
-        const int ucol = c0 + t * 256;
-        if (ucol >= K) break;  // warp-uniform
-        const int col = ucol + 8 * lane;
-        float f[8];
-        unpack8(raw[t], f);
-        float vmax = 0.f;
+    for (int t = 0; t < U; ++t) {
+      const int ucol = c0 + t * 256;
+      if (ucol >= K) break;  // warp-uniform
+      const int col = ucol + 8 * lane;
+      float f[8];
+      unpack8(cur[t], f);
+      float vmax = 0.f;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) vmax = fmaxf(vmax, fabsf(f[j]));
-        vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
-        uint32_t bits;
-        const float m = nvfp4_block_scale(vmax, gs, &bits);
-        if (row_live && col < K)
-          *reinterpret_cast<uint32_t*>(q + r * (K / 2) + col / 2) =
-              e2m1x4(f[0] * m, f[1] * m, f[2] * m, f[3] * m) | (e2m1x4(f[4] * m, f[5] * m, f[6] * m, f[7] * m) << 16);
-        // the scales of blocks 4j .. 4j+3 sit on lanes 8j, 8j+2, 8j+4, 8j+6
-        const uint32_t b1 = __shfl_down_sync(0xffffffffu, bits, 2);
-        const uint32_t b2 = __shfl_down_sync(0xffffffffu, bits, 4);
-        const uint32_t b3 = __shfl_down_sync(0xffffffffu, bits, 6);
-        if ((lane & 7) == 0 && col < K) {
-          const uint32_t w = row_live ? (bits | (b1 << 8) | (b2 << 16) | (b3 << 24)) : 0u;
-          *reinterpret_cast<uint32_t*>(sf + sf_atom_offset(r, col / 16, sf_cols)) = w;
-        }
+      for (int j = 0; j < 8; ++j) vmax = fmaxf(vmax, fabsf(f[j]));
+      vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
+      uint32_t bits;
+      const float m = nvfp4_block_scale(vmax, gs, &bits);
+      if (row_live && col < K)
+        *reinterpret_cast<uint32_t*>(q + r * (K / 2) + col / 2) =
+            e2m1x4(f[0] * m, f[1] * m, f[2] * m, f[3] * m) | (e2m1x4(f[4] * m, f[5] * m, f[6] * m, f[7] * m) << 16);
+      const uint32_t b1 = __shfl_down_sync(0xffffffffu, bits, 2);
+      const uint32_t b2 = __shfl_down_sync(0xffffffffu, bits, 4);
+      const uint32_t b3 = __shfl_down_sync(0xffffffffu, bits, 6);
+      if ((lane & 7) == 0 && col < K) {
+        const uint32_t w = row_live ? (bits | (b1 << 8) | (b2 << 16) | (b3 << 24)) : 0u;
+        *reinterpret_cast<uint32_t*>(sf + sf_atom_offset(r, col / 16, sf_cols)) = w;
       }
     }
+#pragma unroll
+    for (int t = 0; t < U; ++t) cur[t] = nxt[t];
+    r = r1;
+    c0 = c1;
   }
 }
 
