@@ -33,6 +33,9 @@ class DiTConfig:
     freq_dim: int = 256
     eps: float = 1e-6
     fmt: str = "nvfp4"  # "nvfp4" | "fp8"
+    # self-attention gate-compress branch (VSA's compressed branch gated per channel, FastVideo's to_gate_compress);
+    # BASELINE's DiT has none
+    gate_compress: bool = False
 
 
 class QuantLinear:
@@ -163,6 +166,8 @@ class DiTModel:
                               p + f"{a}.norm_q.weight": (D,), p + f"{a}.norm_k.weight": (D,)})
             specs.update({p + "norm3.weight": (C,), p + "norm3.bias": (C,), p + "ff.fc_in.weight": (F, C),
                           p + "ff.fc_out.weight": (C, F), p + "scale_shift_table": (6, C)})
+            if cfg.gate_compress:
+                specs[p + "attn.to_gate_compress.weight"] = (C, C)
         return specs
 
     @staticmethod
@@ -191,6 +196,8 @@ class DiTModel:
             (f2,) = QuantLinear.pack_rows([t(p + "ff.fc_out.weight")], cfg.fmt)
             attn = Attention(q, k, v, o, RMSNorm(t(p + "attn.norm_q.weight"), cfg.eps),
                              RMSNorm(t(p + "attn.norm_k.weight"), cfg.eps), cfg.heads, cfg.head_dim)
+            if cfg.gate_compress:
+                (attn.to_gate_compress,) = QuantLinear.pack_rows([t(p + "attn.to_gate_compress.weight")], cfg.fmt)
             attn2 = Attention(cq, ck, cv, co, RMSNorm(t(p + "attn2.norm_q.weight"), cfg.eps),
                               RMSNorm(t(p + "attn2.norm_k.weight"), cfg.eps), cfg.heads, cfg.head_dim)
             # affine LayerNorm as an adaLN table: shift = bias, scale = weight - 1 (exact in float32, rounded to bf16)

@@ -179,6 +179,9 @@ class H3FastRunner:
         self.dev = dev
         self.ones_c = torch.ones(self.hidden, device=dev, dtype=torch.bfloat16)
         self.text_cache: dict = {}
+        # the gate-compress branch (gate GEMM, compressed attention) runs on this stream beside the sparse attention
+        # (the reference's side stream, __init__.py:465-535)
+        self.side = torch.cuda.Stream(dev) if any(f["gate"] is not None for f in self.fused) else None
         # trace(block, stage, rank, {name: tensor}) after each stage when set (tests and debugging); the tensors are the
         # live buffers, so a tracer that keeps them must copy them
         self.trace = None
@@ -193,7 +196,8 @@ class H3FastRunner:
             self.fused.append({
                 "qkv": _fused_rows([a.to_q, a.to_k, a.to_v]), "o": _fused_rows([a.to_out]),
                 "cq": _fused_rows([c.to_q]), "ckv": _fused_rows([c.to_k, c.to_v]), "co": _fused_rows([c.to_out]),
-                "fc_in": _fused_rows([blk.ff.fc_in]), "fc_out": _fused_rows([blk.ff.fc_out])})
+                "fc_in": _fused_rows([blk.ff.fc_in]), "fc_out": _fused_rows([blk.ff.fc_out]),
+                "gate": _fused_rows([a.to_gate_compress]) if a.to_gate_compress is not None else None})
         if hasattr(self, "text_cache"):
             self.text_cache.clear()
 
@@ -270,6 +274,17 @@ class H3FastRunner:
                     b[nm + "_x"] = b[nm].view(1, H, n_local, *tail)
                     b[nm + "_all"] = b[nm]
             b["vp"] = torch.empty(H, n_local, D, device=dev, dtype=f32)
+            if self.side is not None:  # gate-compress branch
+                b["g"] = torch.empty(R, C, device=dev, dtype=bf)
+                b["oc"] = torch.zeros(H, n_local, D, device=dev, dtype=bf)
+                if P > 1:
+                    b["vp_x"] = torch.zeros(P, Hl, n_local, D, device=dev, dtype=f32)
+                    b["vp_all"] = torch.zeros(Hl, n_all, D, device=dev, dtype=f32)
+                    b["oc_all"] = torch.zeros(Hl, n_all, D, device=dev, dtype=bf)
+                    b["oc_x"] = torch.zeros(P, Hl, n_local, D, device=dev, dtype=bf)
+                else:
+                    b["vp_x"], b["vp_all"] = b["vp"].view(1, H, n_local, D), b["vp"]
+                    b["oc_all"], b["oc_x"] = b["oc"], b["oc"].view(1, H, n_local, D)
             b["vs_head"] = torch.empty(Hl, device=dev, dtype=f32)
             b["sc"] = torch.empty(Hl, n_all, n_all, device=dev, dtype=f32)
             b["idx"] = torch.empty(Hl, n_all, n_all, device=dev, dtype=i32)
@@ -434,9 +449,15 @@ class H3FastRunner:
         fz = self.fused[i]
         tab = tabs[i]  # [6, C]: shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp
         sm_scale = 1.0 / math.sqrt(D)
+        gate = fz["gate"] is not None
+        main = torch.cuda.current_stream(self.dev)
         # ---- q/k/v GEMM (row scale deferred to the prologue) and the prologue, on each rank's rows
         for st in states:
             b = st.b
+            if gate:  # g = h @ Wg^T on the side stream (h's row scale is applied by the gate quantizer, as sg)
+                self.side.wait_stream(main)
+                with torch.cuda.stream(self.side):
+                    self._gemm(b["h"], b["h_sf"], fz["gate"], b["g"])
             self._gemm(b["h"], b["h_sf"], fz["qkv"], b["qkv"])
             self._t(i, "qkv", st, qkv=b["qkv"])
             self._prologue(st, blk)
@@ -446,22 +467,26 @@ class H3FastRunner:
         self.ex.seq_to_heads([st.b["qb"] for st in states], [st.b["qb_x"] for st in states])
         self.ex.seq_to_heads([st.b["kb"] for st in states], [st.b["kb_x"] for st in states])
         self.ex.seq_to_heads([st.b["vb"] for st in states], [st.b["vb_x"] for st in states])
-        for nm in ("qs", "ks", "vs", "qp", "kp"):
+        for nm in ("qs", "ks", "vs", "qp", "kp") + (("vp",) if gate else ()):
             self.ex.seq_to_heads([st.b[nm] for st in states], [st.b[nm + "_x"] for st in states])
         # ---- coarse step and sparse attention over this rank's heads, every rank's rows
         for st in states:
             b = st.b
             if P > 1:  # [P, Hl, n_local, ...] -> [Hl, n_all, ...] in global tile order
-                for nm in ("qs", "ks", "vs", "qp", "kp"):
+                for nm in ("qs", "ks", "vs", "qp", "kp") + (("vp",) if gate else ()):
                     src = b[nm + "_x"]
                     b[nm + "_all"].copy_(src.transpose(0, 1).reshape(b[nm + "_all"].shape))
             torch.amax(b["vs_all"], dim=1, out=b["vs_head"])
             ops.tile_scores(b["qp_all"], b["kp_all"], b["sc"], sm_scale)
             k = min(meta.topk, n_all)
             ops.topk_rows(b["sc"], n_all, n_all, 0, [0], [n_all], [k], b["idx"], b["num"], False)
+            if gate:  # compressed branch oc = softmax(sc) @ vp on the side stream, beside the sparse attention
+                self.side.wait_stream(main)
+                with torch.cuda.stream(self.side):
+                    ops.compressed_branch(b["sc"], b["vp_all"], b["oc_all"])
             self._t(i, "select", st, qb_x=b["qb_x"], kb_x=b["kb_x"], vb_x=b["vb_x"], qs_all=b["qs_all"],
                     ks_all=b["ks_all"], vs_all=b["vs_all"], qp_all=b["qp_all"], kp_all=b["kp_all"],
-                    vs_head=b["vs_head"], sc=b["sc"], idx=b["idx"], num=b["num"])
+                    vs_head=b["vs_head"], sc=b["sc"], idx=b["idx"], num=b["num"], vp_all=b.get("vp_all"))
             ops.vsa_fp8_ex(b["qb_x"], b["kb_x"], b["vb_x"], b["ob_x"], b["idx"], b["num"], b["vbs_all"],
                            b["vbs_all"], b["vs_all"], b["vs_head"], sm_scale * LOG2E, Hl, n_all, n_all, st.rows_pad,
                            st.rows_pad, chunks_q=P, chunks_kv=P, qs=b["qs_all"], ks=b["ks_all"], idx_ld=n_all,
@@ -469,13 +494,27 @@ class H3FastRunner:
             self._t(i, "attn", st, ob_x=b["ob_x"])
         # ---- heads -> sequence
         self.ex.heads_to_seq([st.b["ob_x"] for st in states], [st.b["ob"] for st in states])
+        if gate:
+            main.wait_stream(self.side)
+            if P > 1:  # [Hl, n_all, D] -> [P, Hl, n_local, D] -> every head of this rank's tiles
+                for st in states:
+                    b = st.b
+                    b["oc_x"].copy_(b["oc_all"].view(Hl, P, -1, D).transpose(0, 1))
+            self.ex.heads_to_seq([st.b["oc_x"] for st in states], [st.b["oc"] for st in states])
         for st in states:
             b = st.b
             R = st.rows
-            # attention output -> compact rows, quantized; out-projection with the gated residual in the epilogue
-            ops.attn_gate_quant(b["ob"], None, None, None, b["slot"], st.n_local, TILE, self._q(b["a"]),
-                                b["a_sf"], b["as"], R)
-            self._t(i, "gate", st, ob=b["ob"], a=b["a"], a_sf=b["a_sf"], sa=b["as"])
+            # attention output (+ the gated compressed branch) -> compact rows, quantized; out-projection with the
+            # gated residual in the epilogue
+            if gate:
+                ops.attn_gate_quant(b["ob"], b["g"], b["hs"], b["oc"], b["slot"], st.n_local, TILE, self._q(b["a"]),
+                                    b["a_sf"], b["as"], R)
+            else:
+                ops.attn_gate_quant(b["ob"], None, None, None, b["slot"], st.n_local, TILE, self._q(b["a"]),
+                                    b["a_sf"], b["as"], R)
+            self._t(i, "gate", st, ob=b["ob"], a=b["a"], a_sf=b["a_sf"], sa=b["as"], g=b.get("g") if gate else None,
+                    oc=b.get("oc") if gate else None, hs=b["hs"] if gate else None, h=b["h"] if gate else None,
+                    h_sf=b["h_sf"] if gate else None)
             self._gemm(self._q(b["a"]), b["a_sf"], fz["o"], b["x"], row_scale=b["as"], residual=b["x"],
                        gate=tab[2])
             self._t(i, "out_proj", st, x=b["x"])

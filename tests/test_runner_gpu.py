@@ -89,6 +89,53 @@ def test_sharded_block_loop_equals_single_rank(pkg, grid):
         assert torch.equal(got.view(torch.int16), ref.view(torch.int16)), P
 
 
+@pytest.mark.parametrize("fmt", ["nvfp4", "fp8"])
+def test_gate_compress_branch(pkg, fmt):
+    """The optional gate-compress branch (gate GEMM and compressed attention on the side stream, joined in the gate
+    quantizer): sharded equals single rank bit for bit (the compressed outputs take a heads -> sequence exchange), the
+    gate GEMM matches dequantize-then-matmul, the compressed branch matches softmax(sc) @ vp, and the branch changes
+    the block's output."""
+    model, runner = pkg
+    cfg = model.DiTConfig(blocks=1, fmt=fmt, gate_compress=True)
+    m = model.DiTModel.random(cfg, device=DEV, seed=9)
+    grid = (8, 16, 16)
+    g = torch.Generator(device=DEV).manual_seed(77)
+    x = torch.randn(1, grid[0] * grid[1] * grid[2], cfg.hidden, device=DEV, generator=g).bfloat16()
+    ctx = torch.randn(1, cfg.text_len, cfg.text_dim, device=DEV, generator=g).bfloat16()
+    temb = m.timestep_embedding(0.5)
+    meta = runner.VsaMeta(grid=grid, topk=8)
+    r = runner.H3FastRunner(m)
+    rec = {}
+
+    def trace(i, stage, rank, tensors):
+        if stage in ("select", "gate"):
+            rec[stage] = {k: (v.clone() if v is not None else None) for k, v in tensors.items()}
+
+    r.trace = trace
+    ref = r.forward(x, temb, None, None, meta, context=ctx)
+    torch.cuda.synchronize()
+    got = runner.H3FastRunner(m, runner.VirtualSeqParallel(2)).forward(x, temb, None, None, meta, context=ctx)
+    assert torch.equal(got.view(torch.int16), ref.view(torch.int16))
+    # gate GEMM: g = h @ Wg^T without h's row scale (the gate quantizer applies it)
+    t = rec["gate"]
+    K = cfg.hidden
+    rows = t["g"].shape[0]
+    if fmt == "nvfp4":
+        h = deq_nvfp4(t["h"], t["h_sf"], rows, K)
+    else:
+        h = t["h"].view(torch.float8_e4m3fn).float()
+    want = (h.double() @ weight_fp32(r.fused[0]["gate"]).double().t()).bfloat16().double()
+    assert rel(t["g"].double(), want) < 1e-3
+    # compressed branch: oc = softmax(sc) @ vp, bf16
+    sc, vp = rec["select"]["sc"].double(), rec["select"]["vp_all"].double()
+    oc_want = torch.softmax(sc, -1) @ vp
+    assert rel(t["oc"].double(), oc_want) < 4e-3
+    # the branch contributes: the same model without it gives another output
+    m.transformer_blocks[0].attn.to_gate_compress = None
+    plain = runner.H3FastRunner(m).forward(x, temb, None, None, meta, context=ctx)
+    assert not torch.equal(plain, ref)
+
+
 def test_fp8_block_loop_runs_and_shards_exactly(pkg):
     _, runner = pkg
     m, x, ctx, temb, meta = make(pkg, blocks=1, fmt="fp8", grid=(8, 16, 16))
