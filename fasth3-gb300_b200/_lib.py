@@ -24,7 +24,7 @@ class VsaArgs(ctypes.Structure):
         ("q", P), ("k", P), ("v", P), ("out", P), ("lse", P), ("idx", P), ("num", P), ("vbs_q", P), ("vbs_kv", P),
         ("qs", P), ("ks", P), ("vs", P), ("vs_head", P), ("qk_coef", F32), ("heads", I32), ("n_q_ext", I32),
         ("n_kv", I32), ("idx_ld", I32), ("q_scale_ld", I32), ("kv_scale_ld", I32), ("rows_chunk_q", I64),
-        ("rows_chunk_kv", I64), ("chunks_q", I32), ("chunks_kv", I32),
+        ("rows_chunk_kv", I64), ("chunks_q", I32), ("chunks_kv", I32), ("qk_int8", I32),
     ]
 
 
@@ -67,6 +67,8 @@ SIGNATURES: dict[str, list] = {
     "h3b_gemm_nvfp4": [P, P, P, P, I64, I64, I64, ctypes.POINTER(Epilogue), P],
     "h3b_qkv_prologue8": [P, P, P, I64, P, P, P, P, P, P, P, F32, F32, P, P, P, P, P, P, P, P, P, P, I32, I64, I32,
                           I32, F32, P],
+    "h3b_qkv_prologue8_qk_int8": [P, P, P, I64, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, I32, I64, I32, I32,
+                                  F32, P],
     "h3b_vsa_tile_quant": [P, P, P, I32, I64, P, P, P, P, P, P, P, P, P, P, P, P, P, I64, I32, I32, P],
     "h3b_head_tile_quant": [P, I64, P, P, P, P, P, P, P, I32, I64, I32, I32, F32, P],
     "h3b_vsa_fp8": [P, P, P, P, P, P, P, P, P, P, F32, P, P, I32, I32, I32, I64, P],

@@ -6,7 +6,8 @@
 // scaled by the softmax scale and the Q/K scales, fp32 online softmax with a lazy rescale (the running maximum moves
 // only when a tile's maximum exceeds it by more than 2^4), bf16 output, optional log2-domain LSE.
 //
-// Arithmetic: S = Q8 K8^T on E4M3 operands (kind::f8f6f4). P = 2^(S*coef - m) is evaluated in f16x2 (one
+// Arithmetic: S = Q8 K8^T on E4M3 operands (kind::f8f6f4), or on int8 codes (kind::i8, s32 accumulation, exact;
+// h3b_vsa_args.qk_int8) whose integer S is converted to float before the softmax. P = 2^(S*coef - m) is evaluated in f16x2 (one
 // ex2.approx.f16x2 per two keys; the exponent argument is at most 4 in magnitude for every key that matters, where f16
 // resolves it to 2^-9), multiplied by the key tile's V-scale ratio sv_b / sv_head (P') after the row sum l = sum P is
 // taken, and multiplied with V in f16 (kind::f16): V is stored E4M3 with one scale per (head, tile) and each V tile is
@@ -172,6 +173,23 @@ __device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t saddr, uint32_t lbo) 
 __host__ __device__ constexpr uint32_t idesc_mn(int m, int n, bool b_mn) {
   return (1u << 4) | (b_mn ? (1u << 16) : 0u) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
+// kind::i8: signed 8-bit A and B (format 1 in bits 7-9 and 10-12), s32 accumulate (format 2 in bits 4-5), both
+// K-major
+__host__ __device__ constexpr uint32_t idesc_s8(int m, int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+__device__ __forceinline__ void mma_s8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+// an s32 accumulator word -> its float value, exact for |x| < 2^22 (|Q K^T| <= 128 * 127 * 127 < 2^21 here): the
+// integer added to the bit pattern of 1.5 * 2^23 lands in the mantissa of a float of that binade
+__device__ __forceinline__ uint32_t s32_bits_to_f32_bits(uint32_t x) {
+  return __float_as_uint(__fsub_rn(__int_as_float((int)x + 0x4B400000), 12582912.f));
+}
 
 __device__ __forceinline__ void fail_cta(volatile int* abort_flag) {
   *abort_flag = 1;
@@ -187,6 +205,7 @@ __device__ __forceinline__ bool warp_wait_bounded(uint64_t* bar, uint32_t parity
   return false;
 }
 
+template <bool QKI8>
 __global__ void __launch_bounds__(THREADS, 1)
     vsa_fp8_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, const AttnArgs a) {
@@ -321,7 +340,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     // -------------------------------------------------------------- MMA issuers: warp 1 even steps, warp 2 odd steps
     if (lane == 0) {
       const int w = warp - 1;
-      const uint32_t idesc_s = idesc_mn(TILE, TILE, false);
+      const uint32_t idesc_s = QKI8 ? idesc_s8(TILE, TILE) : idesc_mn(TILE, TILE, false);
       const uint32_t idesc_pv = idesc_mn(TILE, D, true);
       uint32_t list_phase = 0, q_phase = 0, s_phase = 0, p_phase = 0, o_phase = 0;
       uint32_t gbase = 0;  // steps of all earlier items: step j is K-ring use gbase + j
@@ -363,8 +382,12 @@ __global__ void __launch_bounds__(THREADS, 1)
               const uint64_t dk = desc_k_sw128(smem_addr(&sm.k[kst][s][0]));
               const uint64_t dq = s ? dq1 : dq0;
 #pragma unroll
-              for (int i = 0; i < 4; ++i)
-                mma_e4m3(tmem + lo + COL_S + 64 * w, dq + 2 * i, dk + 2 * i, idesc_s, i != 0);
+              for (int i = 0; i < 4; ++i) {
+                if constexpr (QKI8)
+                  mma_s8(tmem + lo + COL_S + 64 * w, dq + 2 * i, dk + 2 * i, idesc_s, i != 0);
+                else
+                  mma_e4m3(tmem + lo + COL_S + 64 * w, dq + 2 * i, dk + 2 * i, idesc_s, i != 0);
+              }
             }
             tc_commit(&sm.s_full[w]);
             tc_commit(&sm.k_empty[kst]);  // the K tiles of the stage are consumed
@@ -466,6 +489,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_ld_32cols(tmem + lane_off + COL_S + 64 * w, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
         tmem_ld_32cols(tmem + lane_off + COL_S + 64 * w + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
         tmem_ld_wait();
+        if constexpr (QKI8) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c) sr[c] = s32_bits_to_f32_bits(sr[c]);
+        }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.s_free[w]);
@@ -742,17 +769,18 @@ extern "C" int h3b_vsa_fp8_ex(const h3b_vsa_args* x, cudaStream_t stream) {
              static_cast<bf16*>(x->out), x->lse, x->heads, x->n_q_ext, x->n_kv, x->idx_ld, x->q_scale_ld,
              x->kv_scale_ld, tpc_q, tpc_kv, x->rows_chunk_q, x->heads * (x->n_q_ext / 2)};
   const int smem = (int)sizeof(Smem) + 1024;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(vsa_fp8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+  auto kern = x->qk_int8 ? vsa_fp8_kernel<true> : vsa_fp8_kernel<false>;
+  static bool attr[2] = {false, false};
+  if (!attr[x->qk_int8 ? 1 : 0]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return set_error(H3B_ECUDA, "vsa_fp8: cannot reserve %d bytes of shared memory", smem);
-    attr = true;
+    attr[x->qk_int8 ? 1 : 0] = true;
   }
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int grid = a.items < sms ? a.items : sms;
-  vsa_fp8_kernel<<<grid, THREADS, smem, stream>>>(mq, mk, mv, mo, a);
+  kern<<<grid, THREADS, smem, stream>>>(mq, mk, mv, mo, a);
   H3B_LAUNCH_CHECK("vsa_fp8");
   return H3B_OK;
 }

@@ -93,7 +93,15 @@ struct UnitInfo {
   int32_t tok[RPW];  // HEAD_MAJOR: token of each of this thread's rows
 };
 
-template <bool ROWS, bool TILE_QK>
+// int8 codes of four floats already scaled into [-127, 127] (round to nearest even), packed low byte first
+__device__ __forceinline__ uint32_t s8x4(float a, float b, float c, float d) {
+  auto one = [](float v) { return (uint32_t)(min(127, max(-127, __float2int_rn(v))) & 0xFF); };
+  return one(a) | (one(b) << 8) | (one(c) << 16) | (one(d) << 24);
+}
+
+// QK_I8: Q and K as symmetric int8 with per-(head, tile) scales max(amax / 127, 1e-30) (for the kind::i8 QK^T of the
+// attention kernel); V stays E4M3.
+template <bool ROWS, bool TILE_QK, bool QK_I8 = false>
 __global__ void __launch_bounds__(NWARP * 32, 2) prologue_kernel(const ProArgs a) {
   extern __shared__ __align__(16) uint8_t pro_smem[];
   __shared__ float sp[3][NWARP][D];
@@ -266,7 +274,8 @@ __global__ void __launch_bounds__(NWARP * 32, 2) prologue_kernel(const ProArgs a
       if constexpr (TILE_QK) {
         qmax = block_allreduce<NWARP, true>(qmax, red);
         kmax = block_allreduce<NWARP, true>(kmax, red);
-        const float sqb = fmaxf(qmax / kFp8Max, 1e-30f), skb = fmaxf(kmax / kFp8Max, 1e-30f);
+        const float qk_max = QK_I8 ? 127.f : kFp8Max;
+        const float sqb = fmaxf(qmax / qk_max, 1e-30f), skb = fmaxf(kmax / qk_max, 1e-30f);
         inv_q = 1.f / sqb;
         inv_k = 1.f / skb;
         if (threadIdx.x == 0) {
@@ -289,8 +298,15 @@ __global__ void __launch_bounds__(NWARP * 32, 2) prologue_kernel(const ProArgs a
         unpack4(*reinterpret_cast<const uint2*>(buf + (0 * TILE + i) * D + l * 4), qv);
         unpack4(*reinterpret_cast<const uint2*>(buf + (1 * TILE + i) * D + l * 4), kv);
         unpack4(*reinterpret_cast<const uint2*>(buf + (2 * TILE + i) * D + l * 4), vv);
-        *reinterpret_cast<uint32_t*>(a.qb + dst) = e4m3x4(qv[0] * inv_q, qv[1] * inv_q, qv[2] * inv_q, qv[3] * inv_q);
-        *reinterpret_cast<uint32_t*>(a.kb + dst) = e4m3x4(kv[0] * inv_k, kv[1] * inv_k, kv[2] * inv_k, kv[3] * inv_k);
+        if constexpr (QK_I8) {
+          *reinterpret_cast<uint32_t*>(a.qb + dst) = s8x4(qv[0] * inv_q, qv[1] * inv_q, qv[2] * inv_q, qv[3] * inv_q);
+          *reinterpret_cast<uint32_t*>(a.kb + dst) = s8x4(kv[0] * inv_k, kv[1] * inv_k, kv[2] * inv_k, kv[3] * inv_k);
+        } else {
+          *reinterpret_cast<uint32_t*>(a.qb + dst) =
+              e4m3x4(qv[0] * inv_q, qv[1] * inv_q, qv[2] * inv_q, qv[3] * inv_q);
+          *reinterpret_cast<uint32_t*>(a.kb + dst) =
+              e4m3x4(kv[0] * inv_k, kv[1] * inv_k, kv[2] * inv_k, kv[3] * inv_k);
+        }
         *reinterpret_cast<uint32_t*>(a.vb + dst) = e4m3x4(vv[0] * inv_v, vv[1] * inv_v, vv[2] * inv_v, vv[3] * inv_v);
       }
       const float inv = 1.f / (float)n;
@@ -314,9 +330,9 @@ __global__ void __launch_bounds__(NWARP * 32, 2) prologue_kernel(const ProArgs a
   asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
-template <bool ROWS, bool TILE_QK>
+template <bool ROWS, bool TILE_QK, bool QK_I8 = false>
 int launch_prologue(const ProArgs& a, cudaStream_t stream) {
-  auto kern = prologue_kernel<ROWS, TILE_QK>;
+  auto kern = prologue_kernel<ROWS, TILE_QK, QK_I8>;
   static int grid = 0;
   if (!grid) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kProSmem) != cudaSuccess)
@@ -361,6 +377,31 @@ extern "C" int h3b_qkv_prologue8(const void* q, const void* k, const void* v, in
   const int rc = tile_qk ? launch_prologue<true, true>(a, stream) : launch_prologue<true, false>(a, stream);
   if (rc) return rc;
   H3B_LAUNCH_CHECK("qkv_prologue8");
+  return H3B_OK;
+}
+
+extern "C" int h3b_qkv_prologue8_qk_int8(const void* q, const void* k, const void* v, int64_t ld, const float* s1,
+                                         const int32_t* tile_row0, const int32_t* vbs, const void* wq, const void* wk,
+                                         const void* cosb, const void* sinb, void* qb, void* kb, void* vb,
+                                         float* qs_blk, float* ks_blk, float* vs_blk, float* vs_head, float* qp,
+                                         float* kp, float* vp, int heads, int64_t rows_pad, int n_tiles, int n_ext,
+                                         float eps, cudaStream_t stream) {
+  clear_error();
+  H3B_REQUIRE(q && k && v && s1 && tile_row0 && vbs && wq && wk && qb && kb && vb && qs_blk && ks_blk && vs_blk && qp &&
+                  kp && vp,
+              "qkv_prologue8_qk_int8: null pointer");
+  H3B_REQUIRE((cosb == nullptr) == (sinb == nullptr), "qkv_prologue8_qk_int8: give both or neither of cosb/sinb");
+  H3B_REQUIRE(heads > 0 && n_tiles > 0 && n_ext >= n_tiles && rows_pad >= (int64_t)n_ext * TILE,
+              "qkv_prologue8_qk_int8: bad heads / tiles / padding");
+  H3B_REQUIRE(ld % 4 == 0 && aligned(q, 8) && aligned(k, 8) && aligned(v, 8),
+              "qkv_prologue8_qk_int8: 8-byte aligned rows");
+  ProArgs a{static_cast<const bf16*>(q), static_cast<const bf16*>(k), static_cast<const bf16*>(v), ld, 0, nullptr, s1,
+            tile_row0, vbs, static_cast<const bf16*>(wq), static_cast<const bf16*>(wk),
+            static_cast<const bf16*>(cosb), static_cast<const bf16*>(sinb), 1.f, 1.f,
+            static_cast<uint8_t*>(qb), static_cast<uint8_t*>(kb), static_cast<uint8_t*>(vb), qs_blk, ks_blk, vs_blk,
+            vs_head, qp, kp, vp, heads, rows_pad, n_tiles, n_ext, eps};
+  if (const int rc = launch_prologue<true, true, true>(a, stream)) return rc;
+  H3B_LAUNCH_CHECK("qkv_prologue8_qk_int8");
   return H3B_OK;
 }
 

@@ -249,16 +249,23 @@ def _i32_array(vals):
 
 
 def qkv_prologue8(q, k, v, s1, tile_row0, vbs, wq, wk, cosb, sinb, inv_sq, inv_sk, qb, kb, vb, vs_blk, vs_head, qp,
-                  kp, vp, heads, n_tiles, tile, eps, qc=None, kc=None, vc=None, qs_blk=None, ks_blk=None) -> None:
+                  kp, vp, heads, n_tiles, tile, eps, qc=None, kc=None, vc=None, qs_blk=None, ks_blk=None,
+                  qk_int8: bool = False) -> None:
     """The reference op's argument order (h3fast.cu:889-927): RMSNorm + RoPE + tile means + E4M3 Q/K/V. 64-token
     tiles only; the compact dense-prefix copies (qc/kc/vc) are not supported. With qs_blk/ks_blk the Q/K scales are
-    per (head, tile) instead of the static inv_sq/inv_sk."""
+    per (head, tile) instead of the static inv_sq/inv_sk; ``qk_int8`` (needs them) writes Q and K as symmetric int8
+    (scale amax/127) for the attention's INT8 QK^T."""
     if tile != 64:
         raise RuntimeError("qkv_prologue8: 64-token tiles only")
     if qc is not None or kc is not None or vc is not None:
         raise RuntimeError("qkv_prologue8: the dense-prefix write-back (qc/kc/vc) is not supported")
     rows_pad = vb.shape[-2]
     n_ext = vs_blk.shape[-1]
+    if qk_int8:
+        call("h3b_qkv_prologue8_qk_int8", _p(q), _p(k), _p(v), q.stride(0), _p(s1), _p(tile_row0), _p(vbs), _p(wq),
+             _p(wk), _p(cosb), _p(sinb), _p(qb), _p(kb), _p(vb), _p(qs_blk), _p(ks_blk), _p(vs_blk), _p(vs_head),
+             _p(qp), _p(kp), _p(vp), int(heads), rows_pad, int(n_tiles), n_ext, float(eps), _stream(q))
+        return
     call("h3b_qkv_prologue8", _p(q), _p(k), _p(v), q.stride(0), _p(s1), _p(tile_row0), _p(vbs), _p(wq), _p(wk),
          _p(cosb), _p(sinb), float(inv_sq), float(inv_sk), _p(qb), _p(kb), _p(vb), _p(qs_blk), _p(ks_blk), _p(vs_blk),
          _p(vs_head), _p(qp), _p(kp), _p(vp), int(heads), rows_pad, int(n_tiles), n_ext, float(eps), _stream(q))
@@ -331,7 +338,7 @@ def attn_gate_quant(ob, g, sg, oc, slot, n_tiles, tile, a, asf, sa, rows, o1=Non
 
 def vsa_fp8_ex(q, k, v, out, idx, num, vbs_q, vbs_kv, vs, vs_head, qk_coef, heads, n_q_ext, n_kv, rows_chunk_q,
                rows_chunk_kv, chunks_q=1, chunks_kv=1, qs=None, ks=None, lse=None, idx_ld=None, q_scale_ld=None,
-               kv_scale_ld=None):
+               kv_scale_ld=None, qk_int8: bool = False):
     """General FP8 block-sparse attention (h3b_vsa_fp8_ex): chunked [chunks * heads, rows_chunk, 128] layouts (the
     all-to-all layout of sequence parallelism) and separate key/value tiles (cross-attention)."""
     import ctypes
@@ -348,5 +355,6 @@ def vsa_fp8_ex(q, k, v, out, idx, num, vbs_q, vbs_kv, vs, vs_head, qk_coef, head
     x.kv_scale_ld = int(kv_scale_ld if kv_scale_ld is not None else n_kv)
     x.rows_chunk_q, x.rows_chunk_kv = int(rows_chunk_q), int(rows_chunk_kv)
     x.chunks_q, x.chunks_kv = int(chunks_q), int(chunks_kv)
+    x.qk_int8 = int(bool(qk_int8))
     call("h3b_vsa_fp8_ex", ctypes.byref(x), _stream(q))
     return out

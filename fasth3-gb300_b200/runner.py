@@ -159,10 +159,12 @@ def _fused_rows(lins: list[QuantLinear]) -> dict:
 
 class H3FastRunner:
     """All blocks of a DiTModel on the h3b kernels. ``sp``: a SeqParallel (one rank per process; NCCL on GPUs), a
-    VirtualSeqParallel (all ranks in this process), or None (one GPU)."""
+    VirtualSeqParallel (all ranks in this process), or None (one GPU). ``qk_int8``: the self-attention's Q and K as
+    per-tile int8 with the QK^T on the tensor cores' integer path (exact scores; E4M3 otherwise)."""
 
-    def __init__(self, model: DiTModel, sp: SeqParallel | VirtualSeqParallel | None = None):
+    def __init__(self, model: DiTModel, sp: SeqParallel | VirtualSeqParallel | None = None, qk_int8: bool = False):
         self.model = model
+        self.qk_int8 = bool(qk_int8)
         self.blocks = list(model.transformer_blocks)
         cfg = model.config
         self.cfg = cfg
@@ -490,7 +492,7 @@ class H3FastRunner:
             ops.vsa_fp8_ex(b["qb_x"], b["kb_x"], b["vb_x"], b["ob_x"], b["idx"], b["num"], b["vbs_all"],
                            b["vbs_all"], b["vs_all"], b["vs_head"], sm_scale * LOG2E, Hl, n_all, n_all, st.rows_pad,
                            st.rows_pad, chunks_q=P, chunks_kv=P, qs=b["qs_all"], ks=b["ks_all"], idx_ld=n_all,
-                           q_scale_ld=n_all, kv_scale_ld=n_all)
+                           q_scale_ld=n_all, kv_scale_ld=n_all, qk_int8=self.qk_int8)
             self._t(i, "attn", st, ob_x=b["ob_x"])
         # ---- heads -> sequence
         self.ex.heads_to_seq([st.b["ob_x"] for st in states], [st.b["ob"] for st in states])
@@ -565,7 +567,7 @@ class H3FastRunner:
         ops.qkv_prologue8(qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:], b["hs"], b["tile_row0"], b["vbs"],
                           blk.attn.norm_q.weight, blk.attn.norm_k.weight, b["cos"], b["sin"], 1.0, 1.0, b["qb"],
                           b["kb"], b["vb"], b["vs"], None, b["qp"], b["kp"], b["vp"], self.heads, st.n_local, TILE,
-                          blk.attn.norm_q.eps, qs_blk=b["qs"], ks_blk=b["ks"])
+                          blk.attn.norm_q.eps, qs_blk=b["qs"], ks_blk=b["ks"], qk_int8=self.qk_int8)
 
 
 class Fp8BlockChain:

@@ -190,6 +190,16 @@ int h3b_qkv_prologue8(const void* q, const void* k, const void* v, int64_t ld, c
                       float* ks_blk, float* vs_blk, float* vs_head, float* qp, float* kp, float* vp, int heads,
                       int64_t rows_pad, int n_tiles, int n_ext, float eps, cudaStream_t stream);
 
+/* h3b_qkv_prologue8 with per-tile scales, Q and K as symmetric int8 for the attention's kind::i8 QK^T (the
+ * INT8 QK^T that sm_100a offers and the reference could not use on sm_103a, fastvideo/models/dits/h3fast/vsa_fp8.cuh:7-9):
+ * qs_blk/ks_blk[h, t] = max(amax / 127, 1e-30) of the tile's rounded bf16 values, codes = clamp(rint(x / s), +-127)
+ * (x times the fast-math reciprocal of s); V, the means and the V scales as h3b_qkv_prologue8. */
+int h3b_qkv_prologue8_qk_int8(const void* q, const void* k, const void* v, int64_t ld, const float* s1,
+                              const int32_t* tile_row0, const int32_t* vbs, const void* wq, const void* wk,
+                              const void* cosb, const void* sinb, void* qb, void* kb, void* vb, float* qs_blk,
+                              float* ks_blk, float* vs_blk, float* vs_head, float* qp, float* kp, float* vp, int heads,
+                              int64_t rows_pad, int n_tiles, int n_ext, float eps, cudaStream_t stream);
+
 /* BASELINE config 4's prologue (no reference counterpart for its layout; the tile and scale math are qkv_prologue8's):
  * q/k/v bf16 [heads, seqlen, 128] in token order; perm [rows] maps tile-ordered rows to tokens (NULL = identity);
  * per-tile E4M3 scales for Q, K and V (max(amax/448, 1e-30)); vs_head [heads] (caller zeroes) takes the per-head
@@ -250,6 +260,8 @@ typedef struct h3b_vsa_args {
   int64_t rows_chunk_kv;
   int chunks_q;
   int chunks_kv;
+  int qk_int8;           /* nonzero: q and k hold int8 codes (symmetric, per-tile scales qs/ks = amax/127) and
+                            S = Q K^T runs as tcgen05 kind::i8 with s32 accumulation (exact), else E4M3 */
 } h3b_vsa_args;
 int h3b_vsa_fp8_ex(const h3b_vsa_args* args, cudaStream_t stream);
 /* Status word of the attention kernel's bounded waits (0 = none); reset != 0 clears it. Synchronizes the device. */
