@@ -362,6 +362,27 @@ def dit_step_secondary(pkg, dev, stream, args, ws) -> dict:
         torch.cuda.synchronize()
         reduced = {"blocks": [b, min(e, cfg.blocks)], "update_scale": scale, "reduced_grid": list(plan.reduced_grid),
                    "ms_per_step": e0.elapsed_time(e1) / reps, "output_finite": bool(torch.isfinite(out.float()).all())}
+    qk8 = None
+    if args.dit_qk_int8:
+        # the same step with INT8 QK^T in the self-attention (tcgen05 kind::i8 scores)
+        r8 = pkg.runner.H3FastRunner(m, sp, qk_int8=True)
+        for _ in range(2):
+            out = r8.forward(x, temb, None, None, meta, context=ctx)
+        torch.cuda.synchronize()
+        if ws > 1:
+            dist.barrier()
+        e0.record(stream)
+        for _ in range(reps):
+            out = r8.forward(x, temb, None, None, meta, context=ctx)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t8 = e0.elapsed_time(e1) / reps
+        if ws > 1:
+            t = torch.tensor([t8], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            t8 = float(t.item())
+        qk8 = {"ms_per_step": t8, "output_finite": bool(torch.isfinite(out.float()).all())}
+        del r8
     lin = 2.0 * S * (6 * cfg.hidden ** 2 + 2 * cfg.hidden * cfg.ffn) * cfg.blocks
     del r, m, x, out
     torch.cuda.empty_cache()
@@ -371,6 +392,8 @@ def dit_step_secondary(pkg, dev, stream, args, ws) -> dict:
            "parallelism": f"sp{ws}"}
     if reduced is not None:
         res["token_reduction"] = reduced
+    if qk8 is not None:
+        res["qk_int8"] = qk8
     return res
 
 
@@ -576,6 +599,8 @@ def run_ours(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--dit-qk-int8", action="store_true",
+                    help="also time the config-5 step with INT8 QK^T in the self-attention")
     ap.add_argument("--dit-reduction", default="", metavar="BEGIN:END[:SCALE]",
                     help="also time the config-5 step with token reduction over blocks [BEGIN, END) (one GPU)")
     ap.add_argument("--steps", type=int, default=100)
