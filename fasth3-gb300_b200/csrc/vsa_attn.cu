@@ -185,11 +185,13 @@ __device__ __forceinline__ void mma_s8(uint32_t d_tmem, uint64_t a, uint64_t b, 
       "l"(a), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
 }
-// an s32 accumulator word -> its float value, exact for |x| < 2^22 (|Q K^T| <= 128 * 127 * 127 < 2^21 here): the
-// integer added to the bit pattern of 1.5 * 2^23 lands in the mantissa of a float of that binade
-__device__ __forceinline__ uint32_t s32_bits_to_f32_bits(uint32_t x) {
-  return __float_as_uint(__fsub_rn(__int_as_float((int)x + 0x4B400000), 12582912.f));
-}
+// an s32 accumulator word x -> the float x + 1.5 * 2^23, exact for |x| < 2^22 (|Q K^T| <= 128 * 127 * 127 < 2^21
+// here): the integer added to the bit pattern of 1.5 * 2^23 lands in the mantissa of a float of that binade. The
+// softmax keeps this biased value (order-preserving); the bias leaves the row maximum exactly and enters the
+// exponent's constant term, fl(nb - 1.5 * 2^23 * coef), whose one rounding shifts every exponent of the step by at
+// most 0.75 * coef (less than one integer unit of S).
+constexpr float kS32Bias = 12582912.f;
+__device__ __forceinline__ uint32_t s32_bits_to_biased_f32_bits(uint32_t x) { return (uint32_t)((int)x + 0x4B400000); }
 
 __device__ __forceinline__ void fail_cta(volatile int* abort_flag) {
   *abort_flag = 1;
@@ -489,13 +491,13 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_ld_32cols(tmem + lane_off + COL_S + 64 * w, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
         tmem_ld_32cols(tmem + lane_off + COL_S + 64 * w + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
         tmem_ld_wait();
-        if constexpr (QKI8) {
-#pragma unroll
-          for (int c = 0; c < 64; ++c) sr[c] = s32_bits_to_f32_bits(sr[c]);
-        }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.s_free[w]);
+        if constexpr (QKI8) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c) sr[c] = s32_bits_to_biased_f32_bits(sr[c]);
+        }
         if (__any_sync(0xffffffffu, vbs_j < TILE)) {
 #pragma unroll
           for (int c = 0; c < 64; ++c)
@@ -507,8 +509,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int c = 0; c < 8; ++c) m8[c] = __uint_as_float(sr[c]);
 #pragma unroll
         for (int c = 8; c < 64; ++c) m8[c & 7] = fmaxf(m8[c & 7], __uint_as_float(sr[c]));
-        const float mraw = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                                 fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        float mraw = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                           fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        if constexpr (QKI8) {
+          if (mraw != -INFINITY) mraw = __fsub_rn(mraw, kS32Bias);  // exact
+        }
         const float mx = mraw == -INFINITY ? -INFINITY : mraw * coef;  // coef > 0
         const bool grow = mx > m_ref + RESCALE_LOG2;
         const bool had_mass = m_ref != -INFINITY;
@@ -538,7 +543,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
           for (int c = 0; c < 32; ++c) pw[c] = 0u;
         } else {
-          const float nb = -m_ref;
+          const float nb = QKI8 ? fmaf(-kS32Bias, coef, -m_ref) : -m_ref;
           uint32_t acc[4] = {0u, 0u, 0u, 0u};
           const __half2 vr2 = __float2half2_rn(vs_j * inv_vhead);  // P' = P * sv_b / sv_head: V' is V8 itself
           const uint32_t vr = *reinterpret_cast<const uint32_t*>(&vr2);
