@@ -76,6 +76,7 @@ SIGNATURES: dict[str, list] = {
     "h3b_vsa_fp8_ex": [ctypes.POINTER(VsaArgs), P],
     "h3b_tile_scores": [P, P, I32, I32, F32, P, P],
     "h3b_topk_rows": [P, I32, I32, I32, I32, I32, P, P, P, P, P, I32, P],
+    "h3b_topk_pairs": [P, I32, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P],
     "h3b_compressed_branch": [P, P, I32, I32, P, P],
     "h3b_attn_gate_quant": [P, P, P, P, P, I64, I32, I32, P, P, P, I64, I32, P, P, P, I32, P, P],
     "h3b_device_status": [ctypes.POINTER(I32)],

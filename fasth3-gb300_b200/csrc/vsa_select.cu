@@ -192,6 +192,51 @@ __global__ void __launch_bounds__(128) compressed_kernel(const float* __restrict
   oc[((size_t)h * n + i) * D + threadIdx.x] = __float2bfloat16_rn(acc * inv);
 }
 
+// The union of two adjacent query tiles' selections, ascending, with a membership byte per entry (bit 0: tile 2p,
+// bit 1: tile 2p+1): topk_pairs' output format (fastvideo/models/dits/h3fast/h3fast.cu:590-686) built from topk_rows'
+// lists. One warp per (head, pair); a byte per key column in shared memory marks the members, then a ballot
+// compaction writes the columns in ascending order. Tiles past n (padding) select nothing.
+constexpr int kUnionWarps = 4;
+__global__ void __launch_bounds__(kUnionWarps * 32) union_pairs_kernel(const int* __restrict__ idx,
+                                                                       const int* __restrict__ num, int n, int n_ext,
+                                                                       int pairs_total, int* __restrict__ u_idx,
+                                                                       uint8_t* __restrict__ u_mem,
+                                                                       int* __restrict__ u_num) {
+  extern __shared__ uint8_t umem[];
+  const int wid = threadIdx.x >> 5, l = threadIdx.x & 31;
+  const int gp = blockIdx.x * kUnionWarps + wid;
+  if (gp >= pairs_total) return;  // warp-uniform
+  uint8_t* m = umem + (size_t)wid * n;
+  const int n_pairs = n_ext / 2;
+  const int hh = gp / n_pairs, pr = gp % n_pairs;
+  for (int c = l; c < n; c += 32) m[c] = 0;
+  __syncwarp();
+  for (int t = 0; t < 2; ++t) {
+    const int r = 2 * pr + t;
+    if (r >= n) break;
+    const int cnt = num[(size_t)hh * n_ext + r];
+    const int* list = idx + ((size_t)hh * n_ext + r) * n;
+    for (int j = l; j < cnt; j += 32) m[list[j]] |= (uint8_t)(1 << t);  // a list holds each column once
+    __syncwarp();
+  }
+  const uint32_t lt = (1u << l) - 1u;
+  int total = 0;
+  int* oi = u_idx + (size_t)gp * n;
+  uint8_t* om = u_mem + (size_t)gp * n;
+  for (int c0 = 0; c0 < n; c0 += 32) {
+    const int c = c0 + l;
+    const uint8_t b = c < n ? m[c] : 0;
+    const uint32_t any = __ballot_sync(0xffffffffu, b != 0);
+    if (b) {
+      const int pos = total + __popc(any & lt);
+      oi[pos] = c;
+      om[pos] = b;
+    }
+    total += __popc(any);
+  }
+  if (l == 0) u_num[gp] = total;
+}
+
 }  // namespace
 }  // namespace h3b
 
@@ -246,5 +291,32 @@ extern "C" int h3b_compressed_branch(const float* sc, const float* vp, int heads
   H3B_REQUIRE((size_t)n * sizeof(float) <= 48 * 1024, "compressed_branch: n = %d tiles exceeds 12288", n);
   compressed_kernel<<<dim3(n, heads), 128, n * sizeof(float), stream>>>(sc, vp, n, static_cast<bf16*>(oc));
   H3B_LAUNCH_CHECK("compressed_branch");
+  return H3B_OK;
+}
+
+extern "C" int h3b_topk_pairs(const float* scores, int heads, int n, int n_ext, int prefix, int n_spans,
+                              const int* starts, const int* ends, const int* ks, int* idx, int* num, int* u_idx,
+                              uint8_t* u_mem, int* u_num, cudaStream_t stream) {
+  clear_error();
+  H3B_REQUIRE(idx && num && u_idx && u_mem && u_num, "topk_pairs: null pointer");
+  H3B_REQUIRE(n_ext % 2 == 0, "topk_pairs: n_ext must be even");
+  // a dense (prefix) query tile selects the prefix plus every span here and every column in topk_rows: the two agree
+  // when the spans tile [prefix, n)
+  int covered = prefix;
+  for (int s = 0; s < n_spans; ++s) {
+    H3B_REQUIRE(starts && ends && starts[s] == covered, "topk_pairs: the spans must tile [prefix, n) in order");
+    covered = ends[s];
+  }
+  H3B_REQUIRE(covered == n, "topk_pairs: the spans must tile [prefix, n) in order");
+  if (cudaMemsetAsync(num, 0, sizeof(int) * (size_t)heads * n_ext, stream) != cudaSuccess)
+    return set_error(H3B_ECUDA, "topk_pairs: memset failed");
+  if (const int rc = h3b_topk_rows(scores, heads, n, n_ext, prefix, n_spans, starts, ends, ks, idx, num, 0, stream))
+    return rc;
+  const int pairs = heads * (n_ext / 2);
+  const size_t smem = (size_t)kUnionWarps * n;
+  H3B_REQUIRE(smem <= 48 * 1024, "topk_pairs: n = %d tiles exceeds 12288", n);
+  union_pairs_kernel<<<(pairs + kUnionWarps - 1) / kUnionWarps, kUnionWarps * 32, smem, stream>>>(
+      idx, num, n, n_ext, pairs, u_idx, u_mem, u_num);
+  H3B_LAUNCH_CHECK("topk_pairs");
   return H3B_OK;
 }

@@ -322,6 +322,18 @@ def topk_rows(scores, n, n_ext, prefix, starts, ends, ks, idx, num, split) -> No
          _i32_array(ends), _i32_array(ks), _p(idx), _p(num), int(bool(split)), _stream(scores))
 
 
+def topk_pairs(scores, n, n_ext, prefix, starts, ends, ks, u_idx, u_mem, u_num, idx=None, num=None) -> None:
+    """The reference op's arguments (h3fast.cu:959-987): per (head, pair of adjacent query tiles) the ascending union of
+    both tiles' selections with membership bytes. ``idx``/``num``: optional topk_rows-shaped scratch."""
+    heads = scores.numel() // (n * n)
+    if idx is None:
+        idx = torch.empty(heads, n_ext, n, device=scores.device, dtype=torch.int32)
+    if num is None:
+        num = torch.empty(heads, n_ext, device=scores.device, dtype=torch.int32)
+    call("h3b_topk_pairs", _p(scores), heads, int(n), int(n_ext), int(prefix), len(starts), _i32_array(starts),
+         _i32_array(ends), _i32_array(ks), _p(idx), _p(num), _p(u_idx), _p(u_mem), _p(u_num), _stream(scores))
+
+
 def compressed_branch(sc: torch.Tensor, vp: torch.Tensor, oc: torch.Tensor) -> None:
     heads, n = vp.shape[0], vp.shape[1]
     call("h3b_compressed_branch", _p(sc), _p(vp), heads, n, _p(oc), _stream(sc))

@@ -278,6 +278,15 @@ int h3b_tile_scores(const float* qp, const float* kp, int heads, int n, float sc
 int h3b_topk_rows(const float* scores, int heads, int n, int n_ext, int prefix, int n_spans, const int* starts,
                   const int* ends, const int* ks, int* idx, int* num, int split, cudaStream_t stream);
 
+/* Replaces topk_pairs_op (fastvideo/models/dits/h3fast/h3fast.cu:959-987; kernel :590-686): per (head, pair of
+ * adjacent query tiles 2p, 2p+1) the ascending union of both tiles' topk_rows selections with a membership byte per
+ * entry (bit 0: tile 2p selected it, bit 1: tile 2p+1), u_idx/u_mem [heads * n_ext/2, n], u_num [heads * n_ext/2].
+ * Pad tiles (>= n) select nothing; prefix query tiles are dense. The spans must tile [prefix, n) in order. idx/num:
+ * scratch of topk_rows' shape ([heads, n_ext, n], [heads, n_ext]). */
+int h3b_topk_pairs(const float* scores, int heads, int n, int n_ext, int prefix, int n_spans, const int* starts,
+                   const int* ends, const int* ks, int* idx, int* num, int* u_idx, uint8_t* u_mem, int* u_num,
+                   cudaStream_t stream);
+
 /* The compressed (mean-pooled) attention branch: oc[h,i,:] = softmax_j(sc[h,i,:]) @ vp[h,:,:], stored bf16
  * [heads, n, 128] (fastvideo/models/dits/h3fast/__init__.py:505-511). */
 int h3b_compressed_branch(const float* sc, const float* vp, int heads, int n, void* oc, cudaStream_t stream);

@@ -51,6 +51,31 @@ def topk_rows(scores: np.ndarray, n: int, n_ext: int, prefix: int, spans, split:
     return idx, num
 
 
+def topk_pairs(scores: np.ndarray, n: int, n_ext: int, prefix: int, spans):
+    """topk_pairs (h3fast.cu:590-686): per (head, pair 2p, 2p+1 of query tiles) the ascending union of both tiles'
+    topk_rows selections, with membership bits (1: tile 2p, 2: tile 2p+1); pad tiles (>= n) select nothing.
+    Returns (u_idx [H * n_ext/2, n] with -1 past u_num, u_mem, u_num)."""
+    idx, num = topk_rows(scores, n, n_ext, prefix, spans, False)
+    H = idx.shape[0]
+    P = n_ext // 2
+    u_idx = np.full((H * P, n), -1, dtype=np.int32)
+    u_mem = np.zeros((H * P, n), dtype=np.uint8)
+    u_num = np.zeros(H * P, dtype=np.int32)
+    for h in range(H):
+        for p in range(P):
+            mem = np.zeros(n, dtype=np.uint8)
+            for t in range(2):
+                r = 2 * p + t
+                if r < n:
+                    mem[idx[h, r, :num[h, r]]] |= np.uint8(1 << t)
+            cols = np.nonzero(mem)[0]
+            g = h * P + p
+            u_idx[g, :cols.size] = cols
+            u_mem[g, :cols.size] = mem[cols]
+            u_num[g] = cols.size
+    return u_idx, u_mem, u_num
+
+
 def fma32(a, b, c) -> np.ndarray:
     """Correctly rounded float32 fused multiply-add, round_f32(a*b + c) with ties to even (IEEE 754 fusedMultiplyAdd),
     for float32 arrays. The product of two float32 values is exact in float64; TwoSum (Knuth) gives the float64 sum s and

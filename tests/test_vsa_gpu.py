@@ -71,6 +71,38 @@ def test_topk_vs_oracle_and_live_reference(ops, n, k, quantize):
     np.testing.assert_array_equal(idx[:, :, :k], ridx.cpu().numpy()[0][:, :, :k])
 
 
+@pytest.mark.parametrize("n,prefix,spans", [(37, 0, [(0, 37, 6)]), (64, 3, [(3, 40, 5), (40, 64, 4)])])
+def test_topk_pairs_vs_oracle_and_live_reference(ops, n, prefix, spans):
+    heads = 3
+    n_ext = n + n % 2
+    sc = topk_inputs(heads, n, 200 + n, 64.0)
+    P = heads * n_ext // 2
+    u_idx = torch.full((P, n), -1, device=DEV, dtype=torch.int32)
+    u_mem = torch.zeros(P, n, device=DEV, dtype=torch.uint8)
+    u_num = torch.zeros(P, device=DEV, dtype=torch.int32)
+    st, en, ks = ([s[i] for s in spans] for i in range(3))
+    ops.topk_pairs(sc.to(DEV), n, n_ext, prefix, st, en, ks, u_idx, u_mem, u_num)
+    torch.cuda.synchronize()
+    oi, om, on = ov.topk_pairs(sc.numpy(), n, n_ext, prefix, spans)
+    got_num = u_num.cpu().numpy()
+    np.testing.assert_array_equal(got_num, on)
+    gi, gm = u_idx.cpu().numpy(), u_mem.cpu().numpy()
+    for g in range(P):
+        np.testing.assert_array_equal(gi[g, :on[g]], oi[g, :on[g]])
+        np.testing.assert_array_equal(gm[g, :on[g]], om[g, :on[g]])
+    mod = _ref()[0]
+    ri = torch.full((P, n), -1, device=DEV, dtype=torch.int32)
+    rm = torch.zeros(P, n, device=DEV, dtype=torch.uint8)
+    rn = torch.zeros(P, device=DEV, dtype=torch.int32)
+    mod.topk_pairs(sc.to(DEV), n, n_ext, prefix, st, en, ks, ri, rm, rn)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(got_num, rn.cpu().numpy())
+    ri, rm = ri.cpu().numpy(), rm.cpu().numpy()
+    for g in range(P):
+        np.testing.assert_array_equal(gi[g, :on[g]], ri[g, :on[g]])
+        np.testing.assert_array_equal(gm[g, :on[g]], rm[g, :on[g]])
+
+
 # ------------------------------------------------------------------------------------------------ scores
 def test_tile_scores_bit_exact_and_selection_end_to_end(ops):
     """C4's coarse step on a reduced head count: tile means -> scores (bit-exact) -> top-32 of 512 (bit-exact)."""

@@ -128,3 +128,19 @@ def test_tile_scores_fixed_order():
         for d in range(128):
             acc = ov.fma32(qp[h, i, d], kp[h, j, d], acc)
         assert got[h, i, j].view(np.uint32) == np.float32(acc * np.float32(scale)).view(np.uint32)
+
+
+def test_topk_pairs_union_by_hand():
+    """Two query tiles' selections merged: ascending union, membership bits, a pad tile selecting nothing."""
+    n, n_ext = 5, 6
+    sc = np.zeros((1, n, n), dtype=np.float32)
+    sc[0, 0] = [5, 4, 3, 2, 1]   # tile 0 keeps 0, 1
+    sc[0, 1] = [1, 2, 3, 4, 5]   # tile 1 keeps 3, 4
+    sc[0, 2] = [1, 9, 1, 9, 1]   # tile 2 keeps 1, 3
+    sc[0, 3] = [9, 1, 1, 1, 9]   # tile 3 keeps 0, 4
+    sc[0, 4] = [2, 2, 2, 2, 2]   # tile 4 keeps 0, 1 (ties to the lowest column); tile 5 is padding
+    u_idx, u_mem, u_num = ov.topk_pairs(sc, n, n_ext, 0, [(0, n, 2)])
+    assert u_num.tolist() == [4, 4, 2]
+    assert u_idx[0, :4].tolist() == [0, 1, 3, 4] and u_mem[0, :4].tolist() == [1, 1, 2, 2]
+    assert u_idx[1, :4].tolist() == [0, 1, 3, 4] and u_mem[1, :4].tolist() == [2, 1, 1, 2]
+    assert u_idx[2, :2].tolist() == [0, 1] and u_mem[2, :2].tolist() == [1, 1]
