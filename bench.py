@@ -362,6 +362,20 @@ def dit_step_secondary(pkg, dev, stream, args, ws) -> dict:
         torch.cuda.synchronize()
         reduced = {"blocks": [b, min(e, cfg.blocks)], "update_scale": scale, "reduced_grid": list(plan.reduced_grid),
                    "ms_per_step": e0.elapsed_time(e1) / reps, "output_finite": bool(torch.isfinite(out.float()).all())}
+    graphed = None
+    if args.dit_graph and ws == 1:
+        # the same step replayed from one CUDA graph (every launch of the 50 blocks captured once)
+        gf = pkg.runner.GraphedForward(r, x, temb, meta, ctx)
+        for _ in range(2):
+            out = gf(x, temb)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(reps):
+            out = gf(x, temb)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        graphed = {"ms_per_step": e0.elapsed_time(e1) / reps, "output_finite": bool(torch.isfinite(out.float()).all())}
+        del gf
     qk8 = None
     if args.dit_qk_int8:
         # the same step with INT8 QK^T in the self-attention (tcgen05 kind::i8 scores)
@@ -394,6 +408,8 @@ def dit_step_secondary(pkg, dev, stream, args, ws) -> dict:
         res["token_reduction"] = reduced
     if qk8 is not None:
         res["qk_int8"] = qk8
+    if graphed is not None:
+        res["cuda_graph"] = graphed
     return res
 
 
@@ -599,6 +615,8 @@ def run_ours(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--dit-graph", action="store_true",
+                    help="also time the config-5 step replayed from one CUDA graph (one GPU)")
     ap.add_argument("--dit-qk-int8", action="store_true",
                     help="also time the config-5 step with INT8 QK^T in the self-attention")
     ap.add_argument("--dit-reduction", default="", metavar="BEGIN:END[:SCALE]",

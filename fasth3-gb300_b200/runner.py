@@ -403,9 +403,12 @@ class H3FastRunner:
         per = full.n_tiles // self.ex.world
         rows_all = [int(full.vbs[p * per:(p + 1) * per].sum()) for p in range(self.ex.world)]
         out = self.ex.all_gather_rows([st.b["x"] for st in states], rows_all)  # global tile order
-        inv = torch.empty_like(full.perm)
-        inv[full.perm] = torch.arange(full.rows)
-        return out.index_select(0, inv.to(out.device)).unsqueeze(0)
+        inv = self.__dict__.setdefault("_inv_cache", {}).get(id(full))
+        if inv is None or inv[0] is not full:
+            t = torch.empty_like(full.perm)
+            t[full.perm] = torch.arange(full.rows)
+            inv = self._inv_cache[id(full)] = (full, t.to(out.device))
+        return out.index_select(0, inv[1]).unsqueeze(0)
 
     def _reduced(self, plan: TokenReduction, meta: VsaMeta) -> dict:
         """The paired layout of ``plan`` (its grid at half width, RoPE at the pairs' mean positions) and the compact-row
@@ -643,3 +646,37 @@ class Fp8BlockChain:
                      gate=tabs[5])
         self._t("fc_out", x=x)
         return x
+
+
+class GraphedForward:
+    """``H3FastRunner.forward`` captured once into a CUDA graph and replayed (one rank): every launch of the 50-block
+    step -- kernels, the side-stream branch, the torch glue -- is one graph launch, with no per-launch host work.
+
+    The graph reads its inputs from static buffers: ``__call__(packed, temb)`` copies the new latent and timestep
+    embedding in and replays. The text context, the metadata, rotary tables and the reduction plan are fixed at
+    capture (the text keys/values are projected before the capture and cached; a new context needs a new
+    ``GraphedForward``). Returns the static output tensor, overwritten by the next replay."""
+
+    def __init__(self, runner: H3FastRunner, packed: torch.Tensor, temb: torch.Tensor, meta: VsaMeta,
+                 context: torch.Tensor, rotary=None, reduction: TokenReduction | None = None):
+        if runner.ex.world != 1:
+            raise ValueError("GraphedForward captures one rank")
+        self.runner = runner
+        self.packed = packed.clone()
+        self.temb = temb.clone()
+        self.context = context
+        args = (None, rotary, meta)
+        kw = {"context": context, "reduction": reduction}
+        runner.forward(self.packed, self.temb, *args, **kw)  # layouts, text cache, kernel attributes: outside capture
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = runner.forward(self.packed, self.temb, *args, **kw)
+        torch.cuda.synchronize()
+
+    def __call__(self, packed: torch.Tensor, temb: torch.Tensor | None = None) -> torch.Tensor:
+        self.packed.copy_(packed)
+        if temb is not None:
+            self.temb.copy_(temb)
+        self.graph.replay()
+        return self.out

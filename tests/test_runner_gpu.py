@@ -389,3 +389,26 @@ def test_fp8_block_chain_stages(pkg):
     fq = rec["ffn_mid"]["f"].float() * rec["ffn_mid"]["fs"][:, None]
     upd = tabs[5].float() * (fq @ weight_fp32(chain.fc_out).t())
     assert rel(rec["fc_out"]["x"].float(), (x1 + upd).bfloat16().float()) < 1e-3
+
+
+@pytest.mark.parametrize("gate", [False, True])
+def test_graphed_forward_replays_the_eager_result(pkg, gate):
+    """The CUDA-graph replay of the block loop gives the eager forward's bytes, for new inputs copied into the graph
+    (and with the side-stream gate-compress branch inside the graph)."""
+    model, runner = pkg
+    cfg = model.DiTConfig(blocks=2, gate_compress=gate)
+    m = model.DiTModel.random(cfg, device=DEV, seed=14)
+    grid = (8, 16, 16)
+    g = torch.Generator(device=DEV).manual_seed(90)
+    S = grid[0] * grid[1] * grid[2]
+    xs = [torch.randn(1, S, cfg.hidden, device=DEV, generator=g).bfloat16() for _ in range(2)]
+    ctx = torch.randn(1, cfg.text_len, cfg.text_dim, device=DEV, generator=g).bfloat16()
+    temb = m.timestep_embedding(0.5)
+    meta = runner.VsaMeta(grid=grid, topk=8)
+    r = runner.H3FastRunner(m)
+    gf = runner.GraphedForward(r, xs[0], temb, meta, ctx)
+    for x in (xs[1], xs[0]):
+        got = gf(x, temb).clone()
+        want = runner.H3FastRunner(m).forward(x, temb, None, None, meta, context=ctx)
+        torch.cuda.synchronize()
+        assert torch.equal(got.view(torch.int16), want.view(torch.int16))
