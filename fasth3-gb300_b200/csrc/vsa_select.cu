@@ -1,9 +1,9 @@
 // VSA coarse step: tile scores from the tile means, top-k key-tile selection per query tile, and the compressed
 // (mean-pooled) attention branch.
 //
-// Scores are defined bit-exactly: sc[h,i,j] = fmul(sum_d, scale) with sum_d accumulated over d = 0..127 in order with
-// separately rounded products and sums (no fused multiply-add), so a float32 CPU restatement reproduces every bit and
-// the selected tile indices are reproducible. The reference scores with cuBLAS (TF32 by default,
+// Scores are defined bit-exactly: sc[h,i,j] = fmul(sum_d, scale) with sum_d accumulated over d = 0..127 in order, one
+// correctly rounded fused multiply-add per d, so a float32 CPU restatement (an exact product added with one rounding)
+// reproduces every bit and the selected tile indices are reproducible. The reference scores with cuBLAS (TF32 by default,
 // fastvideo/models/dits/h3fast/__init__.py:146-149, 498-500), which no other implementation can reproduce bit for bit.
 //
 // Selection follows topk_rows (fastvideo/models/dits/h3fast/h3fast.cu:524-588): prefix tiles kept, per span the k

@@ -267,8 +267,8 @@ int h3b_vsa_fp8_ex(const h3b_vsa_args* args, cudaStream_t stream);
 /* Status word of the attention kernel's bounded waits (0 = none); reset != 0 clears it. Synchronizes the device. */
 int h3b_vsa_status(int* status, int reset);
 
-/* Tile scores sc[h, i, j] = scale * sum_d qp[h,i,d] kp[h,j,d] in fp32 with a fixed order (d ascending, products and
- * sums rounded separately), replacing the runner's torch.baddbmm (fastvideo/models/dits/h3fast/__init__.py:498-500,
+/* Tile scores sc[h, i, j] = scale * sum_d qp[h,i,d] kp[h,j,d] in fp32 with a fixed order (d ascending, one fused
+ * multiply-add per d), replacing the runner's torch.baddbmm (fastvideo/models/dits/h3fast/__init__.py:498-500,
  * TF32 there) with a bit-reproducible definition. qp/kp [heads, n, 128], sc [heads, n, n]. */
 int h3b_tile_scores(const float* qp, const float* kp, int heads, int n, float scale, float* sc, cudaStream_t stream);
 
