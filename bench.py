@@ -466,6 +466,60 @@ def weight_pack_secondary(ops, w, dev) -> dict:
             "note": "amax pass + pack; the amax pass reads W a second time (not counted)"}
 
 
+def e2e_pipelined(ops, x_host, qw, sfw, sw, dev, args, barrier) -> tuple[float, int]:
+    """End to end through the public ops with the host copies overlapped: step i's input copy (host -> device, its own
+    stream), step i-1's quantize + GEMM and step i-2's result copy (device -> host, its own stream) run at once on
+    double-buffered device and pinned host buffers; PCIe carries both directions at the same time. Every step still
+    moves its own 335 MB in and 906 MB out. Device-timed from the first input copy to the last result copy."""
+    import torch
+    bf = torch.bfloat16
+    xs = [torch.empty(M, K, device=dev, dtype=bf) for _ in range(2)]
+    ys = [torch.empty(M, N, device=dev, dtype=bf) for _ in range(2)]
+    y_hosts = [torch.empty(M, N, dtype=bf).pin_memory() for _ in range(2)]
+    qa = torch.empty(M, K // 2, device=dev, dtype=torch.uint8)
+    sfa = torch.empty(ops.sf_rows(M), K // 16, device=dev, dtype=torch.uint8)
+    sa = torch.empty(1, device=dev)
+    wsp = torch.empty(ops.workspace_bytes(), device=dev, dtype=torch.uint8)
+    comp = torch.cuda.current_stream(dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in, ev_comp, ev_out = ([torch.cuda.Event() for _ in range(2)] for _ in range(3))
+
+    def one(i: int) -> None:
+        b = i % 2
+        with torch.cuda.stream(s_in):
+            if i >= 2:
+                s_in.wait_event(ev_comp[b])  # step i-2 has read xs[b]
+            xs[b].copy_(x_host, non_blocking=True)
+            ev_in[b].record(s_in)
+        comp.wait_event(ev_in[b])
+        if i >= 2:
+            comp.wait_event(ev_out[b])  # step i-2's result has left ys[b]
+        ops.quant_nvfp4(xs[b], qa, sfa, sa, wsp)
+        ops.gemm_nvfp4(qa, sfa, qw, sfw, ys[b], alpha_dev=sa, scale_b=sw)
+        ev_comp[b].record(comp)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_comp[b])
+            y_hosts[b].copy_(ys[b], non_blocking=True)
+            ev_out[b].record(s_out)
+
+    for i in range(2):
+        one(i)
+    torch.cuda.synchronize()
+    barrier()
+    steps = max(4, min(args.steps, 8))
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(s_in)
+    for i in range(steps):
+        one(2 + i)
+    t1.record(s_out)
+    torch.cuda.synchronize()
+    barrier()
+    ms = t0.elapsed_time(t1) / steps
+    del xs, ys, y_hosts
+    torch.cuda.empty_cache()
+    return ms, steps
+
+
 def run_ours(args) -> None:
     import torch
     import torch.distributed as dist
@@ -547,7 +601,8 @@ def run_ours(args) -> None:
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()
-    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    e2e_serial_ms = e0.elapsed_time(e1) / e2e_steps
+    e2e_ms, e2e_steps_p = e2e_pipelined(ops, x_host, qw, sfw, sw, dev, args, barrier)
 
     pkg = __graft_entry__.load_package()
     fp8 = fp8_linear_secondary(ops, dev, stream, args) if not args.no_fp8 else None
@@ -558,9 +613,9 @@ def run_ours(args) -> None:
     dit = dit_step_secondary(pkg, dev, stream, args, ws) if not args.no_dit else None
 
     if ws > 1:
-        t = torch.tensor([total_ms, e2e_ms, gemm_ms, quant_ms], device=dev, dtype=torch.float64)
+        t = torch.tensor([total_ms, e2e_ms, gemm_ms, quant_ms, e2e_serial_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms, e2e_ms, gemm_ms, quant_ms = t.tolist()
+        total_ms, e2e_ms, gemm_ms, quant_ms, e2e_serial_ms = t.tolist()
     ms_per_step = total_ms / args.steps
     value = ws * FLOP / (ms_per_step * 1e-3) / 1e12
 
@@ -588,7 +643,10 @@ def run_ours(args) -> None:
             "kernels_ms": {"nvfp4_quant_incl_amax": quant_ms, "gemm": gemm_ms,
                            "quant_gbs": QUANT_BYTES / (quant_ms * 1e-3) / 1e9, "hbm_peak_gbs": peaks["hbm"]},
             "e2e": {"value": ws * FLOP / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-                    "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2, "ms_per_step": e2e_ms},
+                    "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2, "ms_per_step": e2e_ms,
+                    "steps": e2e_steps_p, "copies": "overlapped: input copy, compute and result copy of consecutive "
+                    "steps on three streams, double-buffered",
+                    "serial_ms_per_step": e2e_serial_ms},
             "clocks": clocks.summary(),
             "gpu_launches": launches_per_step * args.steps,
         }
