@@ -930,6 +930,32 @@ extern "C" int h3b_gemm_nvfp4(const void* A, const uint8_t* sfa, const void* B, 
   return run_gemm_nvfp4_pair(A, sfa, B, sfb, M, N, K, epi, stream);
 }
 
+namespace h3b {
+namespace {
+// Self-test of the bounded-wait path: one warp waits on an mbarrier that nothing arrives on, with the wait helper the
+// kernels use; when the limit expires it records H3B_ETIMEOUT in the device status word and returns.
+__global__ void selftest_wait_kernel(uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  volatile int no_abort = 0;
+  const bool got = mbar_wait_bounded(&bar, 0, &no_abort, limit_ns);
+  if (!__all_sync(0xffffffffu, got) && threadIdx.x == 0) atomicExch(&g_gemm_status, H3B_ETIMEOUT);
+}
+}  // namespace
+}  // namespace h3b
+
+extern "C" int h3b_selftest_wait_timeout(uint64_t limit_ns, cudaStream_t stream) {
+  clear_error();
+  H3B_REQUIRE(limit_ns > 0 && limit_ns <= 2000000000ull, "selftest_wait_timeout: limit must be in (0, 2 s]");
+  selftest_wait_kernel<<<1, 32, 0, stream>>>(limit_ns);
+  H3B_LAUNCH_CHECK("selftest_wait_timeout");
+  return H3B_OK;
+}
+
 extern "C" int h3b_device_status(int* status) {
   clear_error();
   H3B_REQUIRE(status, "device_status: null pointer");

@@ -241,6 +241,15 @@ def device_status() -> int:
     return int(v.value)
 
 
+def reset_device_status() -> None:
+    call("h3b_reset_device_status")
+
+
+def selftest_wait_timeout(limit_ns: int, device: torch.device | str = "cuda") -> None:
+    """Launches the bounded-wait self-test (a wait that nothing completes, given up after ``limit_ns``)."""
+    call("h3b_selftest_wait_timeout", int(limit_ns), torch.cuda.current_stream(device).cuda_stream)
+
+
 # ------------------------------------------------------------------------------------------------- VSA coarse step
 def _i32_array(vals):
     import ctypes

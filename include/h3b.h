@@ -305,6 +305,9 @@ int h3b_attn_gate_quant(const void* ob, const void* g, const float* sg, const vo
  * h3b_reset_device_status. Both synchronize the current device. */
 int h3b_device_status(int* status);
 int h3b_reset_device_status(void);
+/* Exercises the bounded-wait path without a fault: one warp waits on an mbarrier nothing arrives on, with the kernels'
+ * wait helper, gives up after limit_ns (<= 2 s) and sets the status word to H3B_ETIMEOUT; the context stays usable. */
+int h3b_selftest_wait_timeout(uint64_t limit_ns, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

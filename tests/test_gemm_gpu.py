@@ -232,3 +232,28 @@ def _dequant_gpu(q: torch.Tensor, sf: torch.Tensor, rows: int, K: int) -> torch.
     off = (r >> 7) * (K // 64) * 512 + (c >> 2) * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4 + (c & 3)
     s = sf.reshape(-1)[off].view(torch.float8_e4m3fn).float()
     return (vals * s[..., None]).reshape(rows, K)
+
+
+def test_bounded_wait_expires_with_status_and_context_survives(ops):
+    """A wait that nothing completes gives up after its limit and reports H3B_ETIMEOUT through the status word, with
+    no fault: the same context then runs a GEMM correctly and the status reads clean after a reset."""
+    import time
+
+    ops.reset_device_status()
+    t0 = time.time()
+    ops.selftest_wait_timeout(50_000_000)  # 50 ms
+    torch.cuda.synchronize()
+    waited = time.time() - t0
+    assert ops.device_status() == 3  # H3B_ETIMEOUT
+    assert 0.04 < waited < 5.0
+    ops.reset_device_status()
+    assert ops.device_status() == 0
+    g = torch.Generator().manual_seed(123)
+    a = (torch.randn(256, 512, generator=g) * 4).to(torch.float8_e4m3fn).to(DEV)
+    w = (torch.randn(384, 512, generator=g) * 4).to(torch.float8_e4m3fn).to(DEV)
+    y = torch.empty(256, 384, device=DEV, dtype=torch.bfloat16)
+    ops.gemm_fp8(a, w, y)
+    torch.cuda.synchronize()
+    ref = (a.float() @ w.float().t()).bfloat16().float()
+    assert rel(y.float().cpu(), ref.cpu()) < TOL
+    assert ops.device_status() == 0
