@@ -2,9 +2,9 @@
 of a module tree, and LoRA adapters merged on the base weight's FP8 grid.
 
 - ``load_dit_checkpoint`` / ``save_dit_checkpoint``: the on-disk boundary of ``DiTModel`` (names and shapes of
-  ``DiTModel.checkpoint_specs``). Tensors are read one at a time (``safetensors.safe_open``), staged through one
-  page-locked host buffer, and packed on the device block by block by the h3b packing kernels, so neither the whole
-  dense model nor a second host copy of it is ever resident.
+  ``DiTModel.checkpoint_specs``). Tensors are read one at a time (``safetensors.safe_open``), staged through two
+  page-locked host buffers and copied on their own stream, and packed on the device block by block by the h3b packing
+  kernels, so neither the whole dense model nor a second host copy of it is ever resident.
 - ``convert_model_to_fp8``: ``convert_model_to_fp8`` of patches/fastvideo-a01c50a.patch:397-471 for a torch module
   tree -- every FP8-tagged linear gets ``_fp8_weight`` / ``_fp8_weight_scale`` (``quantize_fp8_weight``, :384-394) and
   loses its dense ``weight``; with ``keep_sources`` the dense weights are kept in one page-locked host slab per dtype
@@ -42,21 +42,37 @@ def save_dit_checkpoint(tensors: Mapping[str, torch.Tensor], path: str | Path,
 
 
 class _PinnedStage:
-    """One page-locked staging buffer, grown to the largest tensor, for host -> device copies of checkpoint tensors."""
+    """Two page-locked staging buffers (each grown to the largest tensor) and a copy stream for host -> device copies
+    of checkpoint tensors: the file read and host copy of tensor i+1 overlap the device copy of tensor i, and the
+    packing kernels on the current stream wait for their tensor's copy on the device, not on the host."""
 
-    def __init__(self) -> None:
-        self.buf: torch.Tensor | None = None
+    def __init__(self, device: torch.device) -> None:
+        self.bufs: list[torch.Tensor | None] = [None, None]
+        self.events: list[torch.cuda.Event | None] = [None, None]
+        self.i = 0
+        self.stream = torch.cuda.Stream(device)
 
     def to_device(self, t: torch.Tensor, device: torch.device) -> torch.Tensor:
+        slot = self.i % 2
+        self.i += 1
+        if self.events[slot] is not None:
+            self.events[slot].synchronize()  # the device copy that last read this buffer has finished
         nbytes = t.numel() * t.element_size()
-        if self.buf is None or self.buf.numel() < nbytes:
-            self.buf = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
-        staged = self.buf[:nbytes].view(t.dtype).view(t.shape)
+        if self.bufs[slot] is None or self.bufs[slot].numel() < nbytes:
+            self.bufs[slot] = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+        staged = self.bufs[slot][:nbytes].view(t.dtype).view(t.shape)
         staged.copy_(t)
-        out = torch.empty(t.shape, dtype=t.dtype, device=device)
-        out.copy_(staged, non_blocking=True)
-        # the staging buffer is reused by the next tensor: its copy must have left the host buffer
-        torch.cuda.current_stream(device).synchronize()
+        cur = torch.cuda.current_stream(device)
+        with torch.cuda.stream(self.stream):
+            # allocated on the copy stream (its memory is reused in that stream's order), recorded on the current
+            # stream (not reused before the packing kernels there have read it)
+            out = torch.empty(t.shape, dtype=t.dtype, device=device)
+            out.copy_(staged, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(self.stream)
+        self.events[slot] = ev
+        cur.wait_event(ev)
+        out.record_stream(cur)
         return out
 
 
@@ -70,7 +86,7 @@ def load_dit_checkpoint(path: str | Path, config: DiTConfig | None = None,
 
     cfg = config or DiTConfig()
     dev = torch.device(device)
-    stage = _PinnedStage()
+    stage = _PinnedStage(dev)
     with safe_open(str(path), framework="pt", device="cpu") as f:
         have = set(f.keys())
         missing = sorted(set(DiTModel.checkpoint_specs(cfg)) - have)
@@ -80,7 +96,9 @@ def load_dit_checkpoint(path: str | Path, config: DiTConfig | None = None,
         def get(name: str) -> torch.Tensor:
             return stage.to_device(f.get_tensor(name), dev)
 
-        return DiTModel.from_dense(cfg, get, dev)
+        model = DiTModel.from_dense(cfg, get, dev)
+    torch.cuda.current_stream(dev).synchronize()  # the staging buffers are released after every copy has landed
+    return model
 
 
 # --------------------------------------------------------------------------------------------- FP8 module conversion
