@@ -166,6 +166,33 @@ def test_layernorm_variant_vs_oracle(ops):
             assert_codes(_u8(h), out["h"], out["amb"], "ln fp8")
 
 
+@pytest.mark.parametrize("C", [3072, 4096, 5120, 5376])
+def test_layernorm_shared_table_every_width(ops, C):
+    """The runner's LayerNorm form: one adaLN table row for all tokens (idx NULL, the table kept in shared memory), at
+    every supported width (the CTA's row-buffer count depends on C), FP8 and NVFP4, against the oracle."""
+    rows = 131
+    d = rnq_inputs(C, rows, seed=40 + C % 97)
+    f = lambda t: t.float().numpy()  # noqa: E731
+    shift, scale = d["shift"][0:1].contiguous(), d["scale"][0:1].contiguous()
+    for fp4 in (False, True):
+        x = d["x"].to(DEV)
+        xo = torch.empty_like(x)
+        h = torch.zeros(rows, C // 2 if fp4 else C, device=DEV, dtype=torch.uint8)
+        hsf = torch.zeros(ops.sf_rows(rows), C // 16, device=DEV, dtype=torch.uint8) if fp4 else None
+        hs = torch.zeros(rows, device=DEV)
+        ops.resid_norm_quant(x, None, None, None, None, None, shift.to(DEV), scale.to(DEV), xo, h, hsf, hs, 1e-6,
+                             norm="layer")
+        torch.cuda.synchronize()
+        out = oq.resid_norm_quant(f(d["x"]), None, None, None, np.zeros(rows, dtype=np.int32), None, f(shift),
+                                  f(scale), 1e-6, norm="layer", fp4=fp4)
+        assert_scales(hs.cpu().numpy(), out["hs"], f"layernorm row scales C={C}", rtol=2e-6)
+        if fp4:
+            assert_codes(oq.unswizzle_sf(_u8(hsf), rows, C // 16), out["sf_bits"], out["sf_amb"], f"ln sf C={C}")
+            assert_codes(oq.unpack_nibbles(_u8(h)), out["codes"], out["amb"], f"ln nibbles C={C}")
+        else:
+            assert_codes(_u8(h), out["h"], out["amb"], f"ln fp8 C={C}")
+
+
 def test_fp8_rows_vs_oracle_config1(ops):
     # BASELINE config 1 activations: [2048 x 3072] N(0,1) with 1% of columns x20
     x = outlier_matrix(2048, 3072, 0, 0.01, 20.0)
