@@ -161,14 +161,13 @@ __device__ __forceinline__ void store_rows_tma(const Problem& p, const Epi& e, c
   for (int c = c_begin; c < c_end; ++c) {
     const int n0 = nb * BN + 32 * c;
     if (m0 >= p.M || n0 >= p.N) break;  // warp-uniform: this and later chunks lie outside the output
-    if (lane == 0) {
-      bulk_wait_read<0>();  // the previous store from the box has read it
-      if (res) {
-        mbar_arrive_expect_tx(box_bar, 2048);
-        tma_load_2d(box, tmR, n0, m0, box_bar);
-      }
+    if (res && lane == 0) {
+      // the residual block goes in flight at once (it lands while the accumulator is read and scaled), into a box
+      // the previous store has finished reading
+      bulk_wait_read<0>();
+      mbar_arrive_expect_tx(box_bar, 2048);
+      tma_load_2d(box, tmR, n0, m0, box_bar);
     }
-    __syncwarp();
     uint32_t r[32];
     tmem_ld_32cols(tbase + 32 * c, r);
     tmem_ld_wait();
@@ -203,6 +202,11 @@ __device__ __forceinline__ void store_rows_tma(const Problem& p, const Epi& e, c
 #pragma unroll
         for (int u = 0; u < 8; ++u) v[8 * j + u] = rv[u] + g[u] * v[8 * j + u];
       }
+    }
+    if (!res) {
+      // without a residual the box is first needed here: the previous store's read overlapped the TMEM load above
+      if (lane == 0) bulk_wait_read<0>();
+      __syncwarp();
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
