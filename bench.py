@@ -9,6 +9,9 @@ X bf16 [32768 x 5120] (N(0,1), 0.5% of columns x30) -> per-tensor NVFP4 quantiza
 
 N > 1 runs under torchrun, one rank per GPU; each rank processes its own 32768-token shard (weak scaling, no data
 collective: the linear is row-independent). Rank 0 prints one JSON line.
+Secondary lines beside the headline: the FP8 linear and block chain (config 3), the VSA step (config 4), offline
+weight packing, and the 50-block DiT step (config 5), on one GPU also with token reduction over blocks 4..29 and with
+INT8 QK^T (``--no-dit-extras`` skips those two).
 ``--impl reference`` times the reference's CPU path of the same linear (its torch restatement in ``oracle/``:
 quantize, dequantize, fp32 matmul) on the host cores, on a bounded sample of rows per step.
 """
@@ -346,22 +349,29 @@ def dit_step_secondary(pkg, dev, stream, args, ws) -> dict:
         dist.barrier()
     finite = bool(torch.isfinite(out.float()).all())
     reduced = None
+    if args.dit_extras and ws == 1 and not args.dit_reduction:
+        args.dit_reduction = "4:30"  # the reference schedule's default interval (blocks 4..29)
     if args.dit_reduction and ws == 1:
-        # token reduction (one rank, like the reference runner): blocks [begin, end) on horizontally paired tokens
-        parts = args.dit_reduction.split(":")
-        b, e = int(parts[0]), int(parts[1])
-        scale = float(parts[2]) if len(parts) > 2 else 1.0
-        plan = pkg.reduction.build_token_reduction(grid, b, min(e, cfg.blocks), scale)
-        for _ in range(2):
-            out = r.forward(x, temb, None, None, meta, context=ctx, reduction=plan)
-        torch.cuda.synchronize()
-        e0.record(stream)
-        for _ in range(reps):
-            out = r.forward(x, temb, None, None, meta, context=ctx, reduction=plan)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        reduced = {"blocks": [b, min(e, cfg.blocks)], "update_scale": scale, "reduced_grid": list(plan.reduced_grid),
-                   "ms_per_step": e0.elapsed_time(e1) / reps, "output_finite": bool(torch.isfinite(out.float()).all())}
+        try:
+            # token reduction (one rank, like the reference runner): blocks [begin, end) on horizontally paired tokens
+            parts = args.dit_reduction.split(":")
+            b, e = int(parts[0]), int(parts[1])
+            scale = float(parts[2]) if len(parts) > 2 else 1.0
+            plan = pkg.reduction.build_token_reduction(grid, b, min(e, cfg.blocks), scale)
+            for _ in range(2):
+                out = r.forward(x, temb, None, None, meta, context=ctx, reduction=plan)
+            torch.cuda.synchronize()
+            e0.record(stream)
+            for _ in range(reps):
+                out = r.forward(x, temb, None, None, meta, context=ctx, reduction=plan)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            reduced = {"blocks": [b, min(e, cfg.blocks)], "update_scale": scale,
+                       "reduced_grid": list(plan.reduced_grid), "ms_per_step": e0.elapsed_time(e1) / reps,
+                       "output_finite": bool(torch.isfinite(out.float()).all())}
+        except Exception as exc:  # an extra timing must not cost the line; its error is reported
+            reduced = {"error": repr(exc)[:300]}
+            torch.cuda.empty_cache()
     graphed = None
     if args.dit_graph and ws == 1:
         # the same step replayed from one CUDA graph (every launch of the 50 blocks captured once)
@@ -377,26 +387,30 @@ def dit_step_secondary(pkg, dev, stream, args, ws) -> dict:
         graphed = {"ms_per_step": e0.elapsed_time(e1) / reps, "output_finite": bool(torch.isfinite(out.float()).all())}
         del gf
     qk8 = None
-    if args.dit_qk_int8:
-        # the same step with INT8 QK^T in the self-attention (tcgen05 kind::i8 scores)
-        r8 = pkg.runner.H3FastRunner(m, sp, qk_int8=True)
-        for _ in range(2):
-            out = r8.forward(x, temb, None, None, meta, context=ctx)
-        torch.cuda.synchronize()
-        if ws > 1:
-            dist.barrier()
-        e0.record(stream)
-        for _ in range(reps):
-            out = r8.forward(x, temb, None, None, meta, context=ctx)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        t8 = e0.elapsed_time(e1) / reps
-        if ws > 1:
-            t = torch.tensor([t8], device=dev, dtype=torch.float64)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            t8 = float(t.item())
-        qk8 = {"ms_per_step": t8, "output_finite": bool(torch.isfinite(out.float()).all())}
-        del r8
+    if args.dit_qk_int8 or (args.dit_extras and ws == 1):
+        try:
+            # the same step with INT8 QK^T in the self-attention (tcgen05 kind::i8 scores)
+            r8 = pkg.runner.H3FastRunner(m, sp, qk_int8=True)
+            for _ in range(2):
+                out = r8.forward(x, temb, None, None, meta, context=ctx)
+            torch.cuda.synchronize()
+            if ws > 1:
+                dist.barrier()
+            e0.record(stream)
+            for _ in range(reps):
+                out = r8.forward(x, temb, None, None, meta, context=ctx)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            t8 = e0.elapsed_time(e1) / reps
+            if ws > 1:
+                t = torch.tensor([t8], device=dev, dtype=torch.float64)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                t8 = float(t.item())
+            qk8 = {"ms_per_step": t8, "output_finite": bool(torch.isfinite(out.float()).all())}
+            del r8
+        except Exception as exc:  # an extra timing must not cost the line; its error is reported
+            qk8 = {"error": repr(exc)[:300]}
+            torch.cuda.empty_cache()
     lin = 2.0 * S * (6 * cfg.hidden ** 2 + 2 * cfg.hidden * cfg.ffn) * cfg.blocks
     del r, m, x, out
     torch.cuda.empty_cache()
@@ -443,8 +457,8 @@ def weight_pack_secondary(ops, w, dev) -> dict:
     5 launches after 2 warm-ups; algorithmic bytes: read W once (bf16), write codes + block scales."""
     import torch
     wsp = torch.empty(256, device=dev, dtype=torch.uint8)
-    outs = [torch.empty(N, K // 2, device=dev, dtype=torch.uint8), torch.empty(N, K // 16, device=dev, dtype=torch.uint8),
-            torch.empty(1, device=dev)]
+    outs = [torch.empty(N, K // 2, device=dev, dtype=torch.uint8),
+            torch.empty(N, K // 16, device=dev, dtype=torch.uint8), torch.empty(1, device=dev)]
     lib_call = ops.call
     stream = torch.cuda.current_stream(dev)
 
@@ -675,6 +689,9 @@ def main() -> None:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--dit-graph", action="store_true",
                     help="also time the config-5 step replayed from one CUDA graph (one GPU)")
+    ap.add_argument("--no-dit-extras", dest="dit_extras", action="store_false",
+                    help="skip the one-GPU extra config-5 timings run by default: token reduction over blocks 4..29 "
+                         "and INT8 QK^T")
     ap.add_argument("--dit-qk-int8", action="store_true",
                     help="also time the config-5 step with INT8 QK^T in the self-attention")
     ap.add_argument("--dit-reduction", default="", metavar="BEGIN:END[:SCALE]",
