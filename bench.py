@@ -299,15 +299,44 @@ def fp8_chain_secondary(pkg, dev, stream, args) -> dict:
     for i in range(n):
         x.copy_(x0)  # every pass starts from the same stream (the copy is outside the timed interval)
         ev[2 * i].record(stream)
-        chain(x, tabs)
+        chain(x, tabs, check=False)
         ev[2 * i + 1].record(stream)
     torch.cuda.synchronize()
+    pkg.ops.check_status(dev)  # once after the timed passes
     ms = sum(ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(n)) / n
     flop = chain.flop(rows)
     del chain, x, x0
     torch.cuda.empty_cache()
     return {"rows": rows, "ms": ms, "tflops": flop / (ms * 1e-3) / 1e12, "gemm_tflop": flop / 1e12,
             "launches_per_pass": 8}
+
+
+def sp_bitexact_check(pkg, dev, ws) -> dict:
+    """Two blocks on the (7, 16, 16) latent (32 tiles, 1792 tokens) sequence-parallel over every rank of this job (the
+    NCCL all-to-alls of the runner), compared bit for bit with one rank's runner on the same input, which every rank
+    also runs on its own GPU. Every step of the sharded block is row-, tile- or (head, tile)-local, so the two must
+    agree exactly; the result is the minimum over ranks. Also counts the ranks that answer one NCCL all-reduce."""
+    import torch
+    import torch.distributed as dist
+    cfg = pkg.model.DiTConfig(blocks=2, fmt="nvfp4")
+    m = pkg.model.DiTModel.random(cfg, device=dev, seed=0)
+    grid = (7, 16, 16)
+    g = torch.Generator(device=dev).manual_seed(1000)
+    x = torch.randn(1, grid[0] * grid[1] * grid[2], cfg.hidden, device=dev, generator=g).bfloat16()
+    ctx = torch.randn(1, cfg.text_len, cfg.text_dim, device=dev, generator=g).bfloat16()
+    temb = m.timestep_embedding(0.5)
+    meta = pkg.runner.VsaMeta(grid=grid, topk=8)
+    ref = pkg.runner.H3FastRunner(m).forward(x, temb, None, None, meta, context=ctx)
+    got = pkg.runner.H3FastRunner(m, pkg.sp.SeqParallel()).forward(x, temb, None, None, meta, context=ctx)
+    same = torch.tensor([1 if torch.equal(got.view(torch.int16), ref.view(torch.int16)) else 0], device=dev)
+    seen = torch.ones(1, device=dev, dtype=torch.int32)
+    if ws > 1:
+        dist.all_reduce(same, op=dist.ReduceOp.MIN)
+        dist.all_reduce(seen)
+    del m, x, ctx, ref, got
+    torch.cuda.empty_cache()
+    return {"sp_bitexact": bool(same.item()), "grid": list(grid), "blocks": 2, "ranks_in_nccl_allreduce": int(seen.item()),
+            "backend": dist.get_backend() if ws > 1 else None}
 
 
 def dit_step_secondary(pkg, dev, stream, args, ws) -> dict:
@@ -326,13 +355,31 @@ def dit_step_secondary(pkg, dev, stream, args, ws) -> dict:
     ctx = torch.randn(1, cfg.text_len, cfg.text_dim, device=dev, generator=g).bfloat16()
     temb = m.timestep_embedding(0.5)
     meta = pkg.runner.VsaMeta(grid=grid, topk=args.dit_topk)
+    reps = max(2, min(args.steps, 3))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    one_gpu = None
+    if ws > 1:
+        # the denominator of the strong-scaling ratio, in the same job: rank 0 alone runs the step on one GPU (the
+        # other ranks wait at the barrier)
+        if dist.get_rank() == 0:
+            r1 = pkg.runner.H3FastRunner(m)
+            for _ in range(2):
+                out = r1.forward(x, temb, None, None, meta, context=ctx)
+            torch.cuda.synchronize()
+            e0.record(stream)
+            for _ in range(reps):
+                out = r1.forward(x, temb, None, None, meta, context=ctx)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            one_gpu = e0.elapsed_time(e1) / reps
+            del r1, out
+            torch.cuda.empty_cache()
+        dist.barrier()
     sp = pkg.sp.SeqParallel() if ws > 1 else None
     r = pkg.runner.H3FastRunner(m, sp)
     for _ in range(2):
         out = r.forward(x, temb, None, None, meta, context=ctx)
     torch.cuda.synchronize()
-    reps = max(2, min(args.steps, 3))
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if ws > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -342,10 +389,26 @@ def dit_step_secondary(pkg, dev, stream, args, ws) -> dict:
     e1.record(stream)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps
+    exchange = None
     if ws > 1:
         t = torch.tensor([ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
+        dist.barrier()
+        # one more step with device events around every all-to-all: per-exchange time per step (max over ranks)
+        r.ex.timing = []
+        out = r.forward(x, temb, None, None, meta, context=ctx)
+        torch.cuda.synchronize()
+        names = ["qkv_e4m3", "tile_stats", "attn_out_bf16"]
+        per = {nm: 0.0 for nm in names}
+        for nm, a, b in r.ex.timing:
+            per[nm] += a.elapsed_time(b)
+        r.ex.timing = None
+        t = torch.tensor([per[nm] for nm in names], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        exchange = {"ms_per_step": dict(zip(names, t.tolist())),
+                    "note": "device time of each kind of all-to-all summed over the 50 blocks of one step (max over "
+                            "ranks); each exchange includes waiting for the slowest rank to reach it"}
         dist.barrier()
     finite = bool(torch.isfinite(out.float()).all())
     reduced = None
@@ -387,6 +450,7 @@ def dit_step_secondary(pkg, dev, stream, args, ws) -> dict:
         graphed = {"ms_per_step": e0.elapsed_time(e1) / reps, "output_finite": bool(torch.isfinite(out.float()).all())}
         del gf
     qk8 = None
+    r8 = None
     if args.dit_qk_int8 or (args.dit_extras and ws == 1):
         try:
             # the same step with INT8 QK^T in the self-attention (tcgen05 kind::i8 scores)
@@ -407,9 +471,14 @@ def dit_step_secondary(pkg, dev, stream, args, ws) -> dict:
                 dist.all_reduce(t, op=dist.ReduceOp.MAX)
                 t8 = float(t.item())
             qk8 = {"ms_per_step": t8, "output_finite": bool(torch.isfinite(out.float()).all())}
-            del r8
         except Exception as exc:  # an extra timing must not cost the line; its error is reported
             qk8 = {"error": repr(exc)[:300]}
+            try:
+                torch.cuda.synchronize()
+            except Exception:  # noqa: BLE001  a sticky CUDA error: every later GPU line would fail for this reason
+                qk8["context_lost"] = True
+        finally:
+            r8 = None
             torch.cuda.empty_cache()
     lin = 2.0 * S * (6 * cfg.hidden ** 2 + 2 * cfg.hidden * cfg.ffn) * cfg.blocks
     del r, m, x, out
@@ -418,6 +487,10 @@ def dit_step_secondary(pkg, dev, stream, args, ws) -> dict:
            "ms_per_step": ms, "steps": reps, "linear_tflop_per_step": lin / 1e12,
            "linear_share_tflops": lin / (ms * 1e-3) / 1e12, "output_finite": finite, "scaling": "strong",
            "parallelism": f"sp{ws}"}
+    if one_gpu is not None:
+        res["one_gpu_ms_per_step_same_job"] = one_gpu
+    if exchange is not None:
+        res["exchanges"] = exchange
     if reduced is not None:
         res["token_reduction"] = reduced
     if qk8 is not None:
@@ -547,6 +620,9 @@ def run_ours(args) -> None:
     dev = torch.device("cuda", local)
     if ws > 1:
         from datetime import timedelta
+        # NCCL's own communicator set-up log (rank count, transports) on stderr, so the ranks NCCL saw are on record
+        if "NCCL_DEBUG" not in os.environ:
+            os.environ.update(NCCL_DEBUG="INFO", NCCL_DEBUG_SUBSYS="INIT", NCCL_DEBUG_FILE="/dev/stderr")
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
     ops = __graft_entry__.load_package().ops
 
@@ -594,6 +670,7 @@ def run_ours(args) -> None:
         t_end.record(stream)
         torch.cuda.synchronize()
     barrier()
+    ops.check_status(dev)  # a GEMM whose bounded wait expired during the timed steps fails the run
     total_ms = t_start.elapsed_time(t_end)
     quant_ms = sum(e[0].elapsed_time(e[1]) for e in evs) / args.steps
     gemm_ms = sum(e[1].elapsed_time(e[2]) for e in evs) / args.steps
@@ -624,6 +701,7 @@ def run_ours(args) -> None:
     vsa = vsa_config4_secondary(ops, dev, stream, args) if not args.no_vsa else None
     del x, y, qa, sfa
     torch.cuda.empty_cache()
+    sp_check = sp_bitexact_check(pkg, dev, ws) if ws > 1 else None
     dit = dit_step_secondary(pkg, dev, stream, args, ws) if not args.no_dit else None
 
     if ws > 1:
@@ -675,6 +753,8 @@ def run_ours(args) -> None:
         if chain is not None:
             chain["frac_of_2x_bf16"] = chain["tflops"] / (2.0 * peaks["bf16"])
             line["fp8_block_chain_config3"] = chain
+        if sp_check is not None:
+            line["sp_check"] = sp_check
         if dit is not None:
             line["dit_step_config5"] = dit
         if cpu is not None:

@@ -81,6 +81,7 @@ SIGNATURES: dict[str, list] = {
     "h3b_attn_gate_quant": [P, P, P, P, P, I64, I32, I32, P, P, P, I64, I32, P, P, P, I32, P, P],
     "h3b_device_status": [ctypes.POINTER(I32)],
     "h3b_reset_device_status": [],
+    "h3b_status_async": [P, I32, P],
     "h3b_selftest_wait_timeout": [ctypes.c_uint64, P],
 }
 _RESTYPES = {"h3b_last_error": ctypes.c_char_p, "h3b_version": ctypes.c_char_p,

@@ -10,6 +10,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstdarg>
+#include <mutex>
 
 #include "../../include/h3b.h"
 
@@ -33,6 +34,39 @@ void clear_error();
   } while (0)
 
 inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+// A launch setting computed once per device (cudaFuncSetAttribute and occupancy queries apply to the current device:
+// a host that drives several GPUs from one process needs them on each). Thread-safe; an init that fails (nonzero
+// return) is not cached, so the next call retries.
+constexpr int kMaxDevices = 64;
+struct PerDevice {
+  std::mutex m;
+  int value[kMaxDevices] = {};
+  bool ready[kMaxDevices] = {};
+
+  template <class Init>
+  int get(Init&& init, int* out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+      return set_error(H3B_ECUDA, "no usable current device (at most %d)", kMaxDevices);
+    std::lock_guard<std::mutex> lock(m);
+    if (!ready[dev]) {
+      int v = 0;
+      if (const int rc = init(&v)) return rc;
+      value[dev] = v;
+      ready[dev] = true;
+    }
+    *out = value[dev];
+    return H3B_OK;
+  }
+};
+
+inline int current_sms() {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
 
 // ------------------------------------------------------------------------------------------------ device helpers
 constexpr float kFp8Max = 448.f;

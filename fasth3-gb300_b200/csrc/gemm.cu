@@ -168,6 +168,7 @@ __device__ __forceinline__ void store_rows_tma(const Problem& p, const Epi& e, c
       mbar_arrive_expect_tx(box_bar, 2048);
       tma_load_2d(box, tmR, n0, m0, box_bar);
     }
+    __syncwarp();  // tcgen05.ld below is warp-collective: reconverge after the lane-0 branch
     uint32_t r[32];
     tmem_ld_32cols(tbase + 32 * c, r);
     tmem_ld_wait();
@@ -814,13 +815,16 @@ int run_gemm_fp8(const void* A, const void* B, int64_t M, int64_t N, int64_t K, 
         static_cast<bf16*>(epi->D),
         epi->ldd};
   auto kern = gemm_fp8_kernel<BN>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) != cudaSuccess)
-      return set_error(H3B_ECUDA, "gemm: cannot reserve %d bytes of shared memory", C::kSmemBytes);
-    attr_set = true;
-  }
-  const int grid = std::min(p.num_tiles, num_sms());
+  static PerDevice setup;  // the shared-memory reservation, per device; the value is the SM count
+  int sms = 0;
+  if (int rc = setup.get([&](int* v) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) != cudaSuccess)
+          return set_error(H3B_ECUDA, "gemm: cannot reserve %d bytes of shared memory", C::kSmemBytes);
+        *v = num_sms();
+        return H3B_OK;
+      }, &sms))
+    return rc;
+  const int grid = std::min(p.num_tiles, sms);
   kern<<<grid, C::kThreads, C::kSmemBytes, stream>>>(ta, tb, p, e);
   H3B_LAUNCH_CHECK("gemm");
   return H3B_OK;
@@ -863,7 +867,7 @@ int run_gemm_nvfp4_pair(const void* A, const uint8_t* sfa, const void* B, const 
         static_cast<bf16*>(epi->D),
         epi->ldd};
   auto kern = gemm_nvfp4_pair_kernel;
-  static int max_clusters = 0;
+  static PerDevice setup;  // the shared-memory reservation and the resident CTA pairs, per device
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -875,15 +879,16 @@ int run_gemm_nvfp4_pair(const void* A, const uint8_t* sfa, const void* B, const 
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (!max_clusters) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) != cudaSuccess)
-      return set_error(H3B_ECUDA, "gemm: cannot reserve %d bytes of shared memory", C::kSmemBytes);
-    cfg.gridDim = dim3(2 * (num_sms() / 2));
-    int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0)
-      return set_error(H3B_ECUDA, "gemm: no CTA pair of %d bytes of shared memory fits", C::kSmemBytes);
-    max_clusters = n;
-  }
+  int max_clusters = 0;
+  if (int rc = setup.get([&](int* v) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) != cudaSuccess)
+          return set_error(H3B_ECUDA, "gemm: cannot reserve %d bytes of shared memory", C::kSmemBytes);
+        cfg.gridDim = dim3(2 * (num_sms() / 2));
+        if (cudaOccupancyMaxActiveClusters(v, kern, &cfg) != cudaSuccess || *v <= 0)
+          return set_error(H3B_ECUDA, "gemm: no CTA pair of %d bytes of shared memory fits", C::kSmemBytes);
+        return H3B_OK;
+      }, &max_clusters))
+    return rc;
   cfg.gridDim = dim3(2 * std::min(p.num_tiles, max_clusters));
   const cudaError_t le = cudaLaunchKernelEx(&cfg, kern, ta, tb, td, tr, p, e);
   if (le != cudaSuccess) {
@@ -959,6 +964,19 @@ extern "C" int h3b_selftest_wait_timeout(uint64_t limit_ns, cudaStream_t stream)
   H3B_LAUNCH_CHECK("selftest_wait_timeout");
   return H3B_OK;
 }
+
+namespace h3b {
+int gemm_status_async(int* dst, int clear, cudaStream_t stream) {
+  if (cudaMemcpyFromSymbolAsync(dst, g_gemm_status, sizeof(int), 0, cudaMemcpyDefault, stream) != cudaSuccess)
+    return set_error(H3B_ECUDA, "status: reading the GEMM status word failed");
+  if (clear) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_gemm_status) != cudaSuccess || cudaMemsetAsync(p, 0, sizeof(int), stream) != cudaSuccess)
+      return set_error(H3B_ECUDA, "status: clearing the GEMM status word failed");
+  }
+  return H3B_OK;
+}
+}  // namespace h3b
 
 extern "C" int h3b_device_status(int* status) {
   clear_error();

@@ -9,6 +9,7 @@
 // exits. The entry point calls no cudaMalloc, cudaFree or allocating library routine.
 #include "common.cuh"
 
+#include <cuda.h>
 #include <mutex>
 
 namespace h3b {
@@ -24,25 +25,49 @@ namespace {
 constexpr size_t kScratchBytes = 256;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
-constexpr int kMaxDevices = 64;
-std::once_flag g_once[kMaxDevices];
+std::mutex g_mutex;  // kMaxDevices: common.cuh
 void* g_scratch_addr[kMaxDevices] = {nullptr};
-cudaError_t g_setup_err[kMaxDevices] = {cudaSuccess};
+CUcontext g_scratch_ctx[kMaxDevices] = {nullptr};
 
-// Resolves the array's device address on the current device, once per device.
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  }
+  return fn;
+}
+
+// Resolves the array's device address on the current device. The lookup runs on the first call on a device and again
+// whenever the thread's current context on that device is not the one the cached address belongs to (after
+// cudaDeviceReset, or under a context the caller created); a failed lookup is not cached, the next call retries.
 int scratch_for_current_device(void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return set_error(H3B_ECUDA, "quant_nvfp4_noalloc: cudaGetDevice failed");
   if (dev < 0 || dev >= kMaxDevices)
     return set_error(H3B_EINVAL, "quant_nvfp4_noalloc: device %d is beyond the %d devices supported", dev, kMaxDevices);
-  std::call_once(g_once[dev], [dev]() {
+  const CtxGetCurrentFn get = ctx_get_current();
+  if (!get) return set_error(H3B_ECUDA, "quant_nvfp4_noalloc: cuCtxGetCurrent is unavailable");
+  CUcontext ctx = nullptr;
+  if (get(&ctx) != CUDA_SUCCESS) return set_error(H3B_ECUDA, "quant_nvfp4_noalloc: cannot read the current context");
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (g_scratch_addr[dev] == nullptr || ctx == nullptr || g_scratch_ctx[dev] != ctx) {
     void* p = nullptr;
-    g_setup_err[dev] = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);  // binds the runtime's context if none is
+    if (e != cudaSuccess || p == nullptr) {
+      g_scratch_addr[dev] = nullptr;
+      return set_error(H3B_ECUDA, "quant_nvfp4_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
+                       cudaGetErrorString(e));
+    }
+    if (get(&ctx) != CUDA_SUCCESS) ctx = nullptr;  // a null context key makes the next call look up again
     g_scratch_addr[dev] = p;
-  });
-  if (g_setup_err[dev] != cudaSuccess || g_scratch_addr[dev] == nullptr)
-    return set_error(H3B_ECUDA, "quant_nvfp4_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
-                     cudaGetErrorString(g_setup_err[dev]));
+    g_scratch_ctx[dev] = ctx;
+  }
   *out = g_scratch_addr[dev];
   return H3B_OK;
 }

@@ -300,17 +300,20 @@ int launch_resid_norm_quant(const RowArgs& a, bool branch, int norm, bool fp4, c
     const int64_t blocks = (a.rows + LN_WARPS - 1) / LN_WARPS, cap = (int64_t)sms;
     const dim3 g2((unsigned)(blocks < cap ? blocks : cap)), b2(LN_WARPS * 32);
     const int lsm = ln_smem_bytes<C>();
-    // the shared-memory attribute is set on each instantiation's first launch only (later launches may be inside a
-    // CUDA-graph capture)
+    // the shared-memory attribute is set on each instantiation's first launch on a device only (later launches may
+    // be inside a CUDA-graph capture)
 #define H3B_LNQ(B, Q)                                                                                    \
   do {                                                                                                   \
-    static bool attr_set = false;                                                                        \
-    if (!attr_set) {                                                                                     \
-      if (cudaFuncSetAttribute(layer_norm_quant_warp_kernel<C, B, Q>,                                    \
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, lsm) != cudaSuccess)         \
-        return set_error(H3B_ECUDA, "resid_norm_quant: cannot reserve %d bytes of shared memory", lsm); \
-      attr_set = true;                                                                                   \
-    }                                                                                                    \
+    static PerDevice setup;                                                                              \
+    int done_ = 0;                                                                                       \
+    if (int rc_ = setup.get([&](int* v) {                                                                \
+          if (cudaFuncSetAttribute(layer_norm_quant_warp_kernel<C, B, Q>,                                \
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, lsm) != cudaSuccess)     \
+            return set_error(H3B_ECUDA, "resid_norm_quant: cannot reserve %d bytes of shared memory", lsm); \
+          *v = 1;                                                                                        \
+          return H3B_OK;                                                                                 \
+        }, &done_))                                                                                      \
+      return rc_;                                                                                        \
     layer_norm_quant_warp_kernel<C, B, Q><<<g2, b2, lsm, st>>>(a);                                       \
   } while (0)
     if (branch) {

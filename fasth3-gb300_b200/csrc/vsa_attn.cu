@@ -775,15 +775,15 @@ extern "C" int h3b_vsa_fp8_ex(const h3b_vsa_args* x, cudaStream_t stream) {
              x->kv_scale_ld, tpc_q, tpc_kv, x->rows_chunk_q, x->heads * (x->n_q_ext / 2)};
   const int smem = (int)sizeof(Smem) + 1024;
   auto kern = x->qk_int8 ? vsa_fp8_kernel<true> : vsa_fp8_kernel<false>;
-  static bool attr[2] = {false, false};
-  if (!attr[x->qk_int8 ? 1 : 0]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-      return set_error(H3B_ECUDA, "vsa_fp8: cannot reserve %d bytes of shared memory", smem);
-    attr[x->qk_int8 ? 1 : 0] = true;
-  }
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  static PerDevice setup[2];  // the shared-memory reservation per instantiation and device; the value is the SM count
+  int sms = 0;
+  if (int rc = setup[x->qk_int8 ? 1 : 0].get([&](int* v) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+          return set_error(H3B_ECUDA, "vsa_fp8: cannot reserve %d bytes of shared memory", smem);
+        *v = current_sms();
+        return H3B_OK;
+      }, &sms))
+    return rc;
   const int grid = a.items < sms ? a.items : sms;
   kern<<<grid, THREADS, smem, stream>>>(mq, mk, mv, mo, a);
   H3B_LAUNCH_CHECK("vsa_fp8");
@@ -823,6 +823,19 @@ extern "C" int h3b_vsa_fp8(const void* qb, const void* kb, const void* vb, const
   x.chunks_kv = 1;
   return h3b_vsa_fp8_ex(&x, stream);
 }
+
+namespace h3b {
+int attn_status_async(int* dst, int clear, cudaStream_t stream) {
+  if (cudaMemcpyFromSymbolAsync(dst, g_attn_status, sizeof(int), 0, cudaMemcpyDefault, stream) != cudaSuccess)
+    return set_error(H3B_ECUDA, "status: reading the attention status word failed");
+  if (clear) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_attn_status) != cudaSuccess || cudaMemsetAsync(p, 0, sizeof(int), stream) != cudaSuccess)
+      return set_error(H3B_ECUDA, "status: clearing the attention status word failed");
+  }
+  return H3B_OK;
+}
+}  // namespace h3b
 
 extern "C" int h3b_vsa_status(int* status, int reset) {
   clear_error();

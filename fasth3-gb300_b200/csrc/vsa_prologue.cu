@@ -333,17 +333,19 @@ __global__ void __launch_bounds__(NWARP * 32, 2) prologue_kernel(const ProArgs a
 template <bool ROWS, bool TILE_QK, bool QK_I8 = false>
 int launch_prologue(const ProArgs& a, cudaStream_t stream) {
   auto kern = prologue_kernel<ROWS, TILE_QK, QK_I8>;
-  static int grid = 0;
-  if (!grid) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kProSmem) != cudaSuccess)
-      return set_error(H3B_ECUDA, "prologue: cannot reserve %d bytes of shared memory", kProSmem);
-    int dev = 0, sms = 148, per_sm = 1;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, NWARP * 32, kProSmem) != cudaSuccess || per_sm < 1)
-      per_sm = 1;
-    grid = sms * per_sm;
-  }
+  static PerDevice setup;  // the shared-memory reservation and the resident CTAs, per device
+  int grid = 0;
+  if (int rc = setup.get([&](int* v) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kProSmem) != cudaSuccess)
+          return set_error(H3B_ECUDA, "prologue: cannot reserve %d bytes of shared memory", kProSmem);
+        int per_sm = 1;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, NWARP * 32, kProSmem) != cudaSuccess ||
+            per_sm < 1)
+          per_sm = 1;
+        *v = current_sms() * per_sm;
+        return H3B_OK;
+      }, &grid))
+    return rc;
   const int units = a.n_tiles * ((a.heads + HG - 1) / HG);
   kern<<<std::min(grid, units), NWARP * 32, kProSmem, stream>>>(a);
   return H3B_OK;

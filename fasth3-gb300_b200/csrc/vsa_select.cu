@@ -89,6 +89,30 @@ __global__ void __launch_bounds__(256) scores_kernel(const float* __restrict__ q
 }
 
 // ------------------------------------------------------------------------------------------------ top-k
+// Selection semantics (the interface of topk_rows, fastvideo/models/dits/h3fast/h3fast.cu:524-588): query tiles below
+// `prefix` are dense (every column, or nothing in split mode); any other row keeps the prefix columns (unless split),
+// then per span the k largest scores under the order-preserving map of the float bits to uint32 (so -0.0 < +0.0 and
+// NaNs sort by their bits), ties going to the lowest column, the kept columns written in ascending order.
+//
+// Algorithm (one warp per row and span; the span's keys -- the order-preserving uint32 map of the float bits -- in
+// registers, PER per lane at column p * 32 + lane):
+//   1. one read of the span, tracking each lane's smallest and largest key;
+//   2. a lower bound L with at least k keys >= L, and a candidate list of the keys >= L with their columns, gathered
+//      into shared memory in ascending column order (ballot compaction):
+//        k <= 32: L = the smallest of the 32 lanes' largest keys (32 distinct keys are >= L); for N(0, 1)-like scores
+//                 about 5% of a 2016-column span survive;
+//        k > 32:  a 256-bucket histogram of the values over the span's finite range, bucket = min(255,
+//                 uint(fma(v, 256 / (hi - lo), -lo * 256 / (hi - lo)))), non-decreasing in v (a span with a NaN puts
+//                 everything in bucket 0); the list holds the buckets from the one containing the k-th largest up;
+//   3. exact selection on the list by most-significant-digit radix levels over a key interval [lo, hi]: each level
+//      histograms the list keys inside the interval by (key - lo) >> shift (256 buckets spanning the interval), finds
+//      the bucket holding the `need`-th largest, drops the keys above it from `need` and narrows the interval to that
+//      bucket. Every level removes at least 8 bits of the interval's width, so at most four levels leave a single key:
+//      the threshold t, the k-th largest key of the span. The list entries equal to t are kept up to the `need`-th
+//      in column order;
+//   4. the list is written out in order: keys above t, and keys equal to t up to the last kept column.
+// A span whose list would exceed 512 entries (heavy ties at the bound, or k > 32 with a wide boundary bucket) runs the
+// same radix levels over the keys in registers instead, and writes its output from the registers.
 struct Spans {
   int n;
   int start[4];
@@ -96,25 +120,296 @@ struct Spans {
   int k[4];
 };
 
-__device__ __forceinline__ uint32_t order_key(float f) {
-  const uint32_t u = __float_as_uint(f);
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+constexpr int kSelWarps = 4;     // rows per CTA
+constexpr int kBuckets = 256;
+constexpr int kListCap = 512;    // candidate list entries per warp
+constexpr int kLaneBoundK = 32;  // k up to which the lane-maximum bound is used
+
+__device__ __forceinline__ uint32_t order_key(uint32_t u) {
+  return u ^ ((uint32_t)((int32_t)u >> 31) | 0x80000000u);
+}
+__device__ __forceinline__ float key_value(uint32_t key) {  // the inverse map
+  return __uint_as_float(key ^ ((key & 0x80000000u) ? 0x80000000u : 0xffffffffu));
 }
 
-// One warp per (head, query tile). PER = keys per lane (span length <= 32 * PER).
-template <int PER>
-__global__ void __launch_bounds__(128) topk_kernel(const float* __restrict__ scores, int n, int n_ext, int prefix,
-                                                   Spans sp, int rows, int* __restrict__ idx, int* __restrict__ num,
-                                                   int split) {
-  const int row = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-  if (row >= rows) return;
+__device__ __forceinline__ uint32_t value_bucket(uint32_t key, float sc, float off) {
+  return min(__float2uint_rz(__fmaf_rn(key_value(key), sc, off)), (uint32_t)(kBuckets - 1));
+}
+
+// The bucket holding the need-th largest entry of the histogram (counted from the top bucket down) and the number of
+// entries in the buckets above it. Lane l sums buckets 8l .. 8l+7; suffix sums across lanes locate the lane.
+__device__ __forceinline__ void boundary_bucket(const int* hist, int need, int& b, int& above) {
+  const int lane = threadIdx.x & 31;
+  const int4 h0 = *reinterpret_cast<const int4*>(hist + 8 * lane);
+  const int4 h1 = *reinterpret_cast<const int4*>(hist + 8 * lane + 4);
+  const int hb[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+  int own = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) own += hb[j];
+  int suffix = own;  // entries in buckets >= 8 * lane
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_down_sync(0xffffffffu, suffix, o);
+    if (lane + o < 32) suffix += t;
+  }
+  const uint32_t reach = __ballot_sync(0xffffffffu, suffix >= need);  // lanes 0 .. L (suffix does not increase)
+  const int L = 31 - __clz(reach);
+  int higher = __shfl_down_sync(0xffffffffu, suffix, 1);  // entries in buckets >= 8 * (lane + 1)
+  if (lane == 31) higher = 0;
+  int bb = 0, ab = 0;
+  if (lane == L) {
+    int acc = higher;
+#pragma unroll
+    for (int j = 7; j >= 0; --j) {
+      if (acc + hb[j] >= need) {
+        bb = 8 * lane + j;
+        ab = acc;
+        break;
+      }
+      acc += hb[j];
+    }
+  }
+  b = __shfl_sync(0xffffffffu, bb, L);
+  above = __shfl_sync(0xffffffffu, ab, L);
+}
+
+// One radix level: `hist` holds the counts of the active keys (those in [lo, hi]) by (key - lo) >> shift. Narrows
+// [lo, hi] to the bucket holding the need-th largest active key and takes the keys above it off `need`.
+__device__ __forceinline__ void narrow(const int* hist, int shift, int& need, uint32_t& lo, uint32_t& hi) {
+  int b, above;
+  boundary_bucket(hist, need, b, above);
+  need -= above;
+  const uint32_t nlo = lo + ((uint32_t)b << shift);
+  const uint32_t width = (1u << shift) - 1u;
+  hi = (hi - nlo > width) ? nlo + width : hi;
+  lo = nlo;
+}
+
+// Digits of one level: 256 buckets cover [lo, hi].
+__device__ __forceinline__ int level_shift(uint32_t lo, uint32_t hi) {
+  const int bits = 32 - __clz(hi - lo);
+  return bits > 8 ? bits - 8 : 0;
+}
+
+// Selects the k largest of scores[start, start + len) and appends their columns (ascending) at out[cnt..]. FULL: the
+// span is exactly 32 * PER long (every register slot holds a key; no per-slot bounds checks).
+template <int PER, bool FULL>
+__device__ __forceinline__ void select_span(const float* __restrict__ srow, int start, int len, int k,
+                                            int* __restrict__ out, int& cnt, int* hist, uint32_t* lkey, int* lcol) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t below = (1u << lane) - 1u;
+  if (k <= 0 || len <= 0) return;
+  if (k >= len) {
+    for (int c = lane; c < len; c += 32) out[cnt + c] = start + c;
+    cnt += len;
+    return;
+  }
+  // 1. the span's keys: every load is issued before the first is used
+  auto valid = [&](int p) { return FULL || p * 32 + lane < len; };
+  auto live = [&](int p) { return FULL || p * 32 < len; };  // warp-uniform: slot p holds keys in some lane
+  uint32_t key[PER];
+#pragma unroll
+  for (int p = 0; p < PER; ++p) key[p] = valid(p) ? __float_as_uint(srow[start + p * 32 + lane]) : 0u;
+  uint32_t kmin = 0xffffffffu, kmax = 0u;
+#pragma unroll
+  for (int p = 0; p < PER; ++p) {
+    if (valid(p)) {
+      key[p] = order_key(key[p]);
+      kmin = min(kmin, key[p]);
+      kmax = max(kmax, key[p]);
+    }
+  }
+  // 2. lower bound and candidate list; [lo, hi] = the key interval still undecided, `need` = keys wanted from it
+  int need = k, n_list = 0;
+  uint32_t lo, hi;
+  bool listed = false;
+  if (k <= kLaneBoundK) {
+    const uint32_t bound = __reduce_min_sync(0xffffffffu, len >= 32 ? kmax : 0u);
+    lo = bound;
+    hi = __reduce_max_sync(0xffffffffu, kmax);
+#pragma unroll
+    for (int p = 0; p < PER; ++p) {
+      if (!live(p)) break;
+      const int c = p * 32 + lane;
+      const bool in = valid(p) && key[p] >= bound;
+      const uint32_t m = __ballot_sync(0xffffffffu, in);
+      const int pos = n_list + __popc(m & below);
+      if (in && pos < kListCap) {
+        lkey[pos] = key[p];
+        lcol[pos] = c;
+      }
+      n_list += __popc(m);
+    }
+    listed = n_list <= kListCap;
+  } else {
+    float vlo = INFINITY, vhi = -INFINITY;
+    bool nan = false;
+#pragma unroll
+    for (int p = 0; p < PER; ++p) {
+      if (!live(p)) break;
+      if (valid(p)) {
+        const float v = key_value(key[p]);
+        if (fabsf(v) < INFINITY) {
+          vlo = fminf(vlo, v);
+          vhi = fmaxf(vhi, v);
+        }
+        nan |= v != v;
+      }
+    }
+    vlo = -warp_allreduce<true>(-vlo);
+    vhi = warp_allreduce<true>(vhi);
+    nan = __any_sync(0xffffffffu, nan);
+    float sc = 0.f, off = 0.f;
+    if (!nan && vhi > vlo && vhi - vlo < INFINITY) {
+      sc = 256.f / (vhi - vlo);
+      off = -vlo * sc;
+      if (!(sc < INFINITY)) sc = 0.f, off = 0.f;
+    }
+    for (int i = lane; i < kBuckets; i += 32) hist[i] = 0;
+    __syncwarp();
+#pragma unroll
+    for (int p = 0; p < PER; ++p) {
+      if (!live(p)) break;
+      if (valid(p)) atomicAdd(&hist[value_bucket(key[p], sc, off)], 1);
+    }
+    __syncwarp();
+    int b, above;
+    boundary_bucket(hist, k, b, above);
+    const int total = above + hist[b];
+    __syncwarp();  // hist is reused by the radix levels
+    if (total <= kListCap) {
+      uint32_t blo = 0xffffffffu, bhi = 0u;
+#pragma unroll
+      for (int p = 0; p < PER; ++p) {
+        if (!live(p)) break;
+        const int c = p * 32 + lane;
+        const uint32_t vb = valid(p) ? value_bucket(key[p], sc, off) : 0u;
+        const bool in = valid(p) && vb >= (uint32_t)b;
+        const uint32_t m = __ballot_sync(0xffffffffu, in);
+        if (in) {
+          const int pos = n_list + __popc(m & below);
+          lkey[pos] = key[p];
+          lcol[pos] = c;
+          if (vb == (uint32_t)b) {
+            blo = min(blo, key[p]);
+            bhi = max(bhi, key[p]);
+          }
+        }
+        n_list += __popc(m);
+      }
+      lo = __reduce_min_sync(0xffffffffu, blo);
+      hi = __reduce_max_sync(0xffffffffu, bhi);
+      need = k - above;  // every key of a higher bucket exceeds every key of bucket b
+      listed = true;
+    }
+  }
+  // 3. radix levels down to one key t; tie_last = the last column kept among the keys equal to t
+  uint32_t t;
+  int tie_last = -1;
+  if (listed) {
+    __syncwarp();
+#pragma unroll 1
+    for (int level = 0; level < 5 && lo != hi; ++level) {
+      const int shift = level_shift(lo, hi);
+      for (int i = lane; i < kBuckets; i += 32) hist[i] = 0;
+      __syncwarp();
+      for (int i = lane; i < n_list; i += 32) {
+        const uint32_t kk = lkey[i];
+        if (kk >= lo && kk <= hi) atomicAdd(&hist[(kk - lo) >> shift], 1);
+      }
+      __syncwarp();
+      narrow(hist, shift, need, lo, hi);
+      __syncwarp();
+    }
+    t = lo;
+    int seen = 0;
+    for (int base = 0; base < n_list; base += 32) {
+      const int i = base + lane;
+      const bool eq = i < n_list && lkey[i] == t;
+      const uint32_t m = __ballot_sync(0xffffffffu, eq);
+      const uint32_t hit = __ballot_sync(0xffffffffu, eq && seen + __popc(m & below) + 1 == need);
+      if (hit) {
+        tie_last = lcol[base + __ffs(hit) - 1];
+        break;
+      }
+      seen += __popc(m);
+    }
+    // 4. the kept list entries, in column order
+    for (int base = 0; base < n_list; base += 32) {
+      const int i = base + lane;
+      bool keep = false;
+      int c = 0;
+      if (i < n_list) {
+        const uint32_t kk = lkey[i];
+        c = lcol[i];
+        keep = kk > t || (kk == t && c <= tie_last);
+      }
+      const uint32_t m = __ballot_sync(0xffffffffu, keep);
+      if (keep) out[cnt + __popc(m & below)] = start + c;
+      cnt += __popc(m);
+    }
+    __syncwarp();  // the list is reused by the next span
+    return;
+  }
+  // the same levels over the keys in registers
+  lo = __reduce_min_sync(0xffffffffu, kmin);
+  hi = __reduce_max_sync(0xffffffffu, kmax);
+  need = k;
+#pragma unroll 1
+  for (int level = 0; level < 5 && lo != hi; ++level) {
+    const int shift = level_shift(lo, hi);
+    for (int i = lane; i < kBuckets; i += 32) hist[i] = 0;
+    __syncwarp();
+#pragma unroll
+    for (int p = 0; p < PER; ++p) {
+      if (!live(p)) break;
+      if (valid(p) && key[p] >= lo && key[p] <= hi) atomicAdd(&hist[(key[p] - lo) >> shift], 1);
+    }
+    __syncwarp();
+    narrow(hist, shift, need, lo, hi);
+    __syncwarp();
+  }
+  t = lo;
+  int seen = 0;
+#pragma unroll
+  for (int p = 0; p < PER; ++p) {
+    if (!live(p) || tie_last >= 0) break;
+    const int c = p * 32 + lane;
+    const bool eq = valid(p) && key[p] == t;
+    const uint32_t m = __ballot_sync(0xffffffffu, eq);
+    const uint32_t hit = __ballot_sync(0xffffffffu, eq && seen + __popc(m & below) + 1 == need);
+    if (hit) tie_last = p * 32 + __ffs(hit) - 1;
+    seen += __popc(m);
+  }
+#pragma unroll
+  for (int p = 0; p < PER; ++p) {
+    if (!live(p)) break;
+    const int c = p * 32 + lane;
+    const bool keep = valid(p) && (key[p] > t || (key[p] == t && c <= tie_last));
+    const uint32_t m = __ballot_sync(0xffffffffu, keep);
+    if (keep) out[cnt + __popc(m & below)] = start + c;
+    cnt += __popc(m);
+  }
+}
+
+// One warp per (head, query tile) row; PER = keys per lane (span length <= 32 * PER).
+template <int PER, bool FULL>
+__global__ void __launch_bounds__(kSelWarps * 32, PER <= 32 ? 4 : (PER <= 64 ? 3 : 1)) select_kernel(const float* __restrict__ scores, int n, int n_ext,
+                                                                int prefix, Spans sp, int rows, int* __restrict__ idx,
+                                                                int* __restrict__ num, int split) {
+  __shared__ __align__(16) int hist[kSelWarps][kBuckets];
+  __shared__ uint32_t lkey[kSelWarps][kListCap];
+  __shared__ int lcol[kSelWarps][kListCap];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kSelWarps + w;
+  if (row >= rows) return;  // warp-uniform; the CTA's warps never synchronise with each other
   const int hh = row / n, q = row - hh * n;
   int* out = idx + ((size_t)hh * n_ext + q) * n;
-  const float* srow = scores + (size_t)row * n;
-  if (q < prefix) {
+  int* count = num + (size_t)hh * n_ext + q;
+  if (q < prefix) {  // a dense query tile
     if (!split)
       for (int c = lane; c < n; c += 32) out[c] = c;
-    if (lane == 0) num[(size_t)hh * n_ext + q] = split ? 0 : n;
+    if (lane == 0) *count = split ? 0 : n;
     return;
   }
   int cnt = 0;
@@ -122,49 +417,10 @@ __global__ void __launch_bounds__(128) topk_kernel(const float* __restrict__ sco
     for (int c = lane; c < prefix; c += 32) out[c] = c;
     cnt = prefix;
   }
-  const uint32_t below = (1u << lane) - 1u;
-  for (int s = 0; s < sp.n; ++s) {
-    const int start = sp.start[s], len = sp.end[s] - start, k = sp.k[s];
-    if (k >= len) {
-      for (int c = lane; c < len; c += 32) out[cnt + c] = start + c;
-      cnt += len;
-      continue;
-    }
-    uint32_t key[PER];
-#pragma unroll
-    for (int p = 0; p < PER; ++p) {
-      const int c = p * 32 + lane;
-      key[p] = c < len ? order_key(srow[start + c]) : 0u;
-    }
-    // the largest threshold t with count(key >= t) >= k, found bit by bit from the top
-    uint32_t t = 0;
-#pragma unroll 1
-    for (int b = 31; b >= 0; --b) {
-      const uint32_t cand = t | (1u << b);
-      int c = 0;
-#pragma unroll
-      for (int p = 0; p < PER; ++p) c += key[p] >= cand ? 1 : 0;
-      if (__reduce_add_sync(0xffffffffu, c) >= k) t = cand;
-    }
-    int above = 0;
-#pragma unroll
-    for (int p = 0; p < PER; ++p) above += key[p] > t ? 1 : 0;
-    const int ties_needed = k - __reduce_add_sync(0xffffffffu, above);
-    int ties_seen = 0;
-#pragma unroll
-    for (int p = 0; p < PER; ++p) {
-      const int c = p * 32 + lane;
-      const bool valid = c < len;
-      const bool eq = valid && key[p] == t;
-      const uint32_t eq_mask = __ballot_sync(0xffffffffu, eq);
-      const bool keep = (valid && key[p] > t) || (eq && ties_seen + __popc(eq_mask & below) < ties_needed);
-      ties_seen += __popc(eq_mask);
-      const uint32_t keep_mask = __ballot_sync(0xffffffffu, keep);
-      if (keep) out[cnt + __popc(keep_mask & below)] = start + c;
-      cnt += __popc(keep_mask);
-    }
-  }
-  if (lane == 0) num[(size_t)hh * n_ext + q] = cnt;
+  const float* srow = scores + (size_t)row * n;
+  for (int s = 0; s < sp.n; ++s)
+    select_span<PER, FULL>(srow, sp.start[s], sp.end[s] - sp.start[s], sp.k[s], out, cnt, hist[w], lkey[w], lcol[w]);
+  if (lane == 0) *count = cnt;
 }
 
 // ------------------------------------------------------------------------------------------------ compressed branch
@@ -272,14 +528,20 @@ extern "C" int h3b_topk_rows(const float* scores, int heads, int n, int n_ext, i
     longest = longest > ends[s] - starts[s] ? longest : ends[s] - starts[s];
   }
   const int rows = heads * n;
-  const int grid = (rows + 3) / 4;
-#define H3B_TOPK(P) topk_kernel<P><<<grid, 128, 0, stream>>>(scores, n, n_ext, prefix, sp, rows, idx, num, split)
-  if (longest <= 16 * 32) H3B_TOPK(16);
-  else if (longest <= 32 * 32) H3B_TOPK(32);
-  else if (longest <= 64 * 32) H3B_TOPK(64);
-  else if (longest <= 160 * 32) H3B_TOPK(160);
+  const int grid = (rows + kSelWarps - 1) / kSelWarps;
+#define H3B_SELECT(P, F) \
+  select_kernel<P, F><<<grid, kSelWarps * 32, 0, stream>>>(scores, n, n_ext, prefix, sp, rows, idx, num, split)
+  // one span of exactly 32 * PER columns (BASELINE's 512- and 2016-tile layouts): the check-free instantiation
+  const bool one = n_spans == 1;
+  if (one && longest == 16 * 32) H3B_SELECT(16, true);
+  else if (one && longest == 63 * 32) H3B_SELECT(63, true);
+  else if (one && longest == 64 * 32) H3B_SELECT(64, true);
+  else if (longest <= 16 * 32) H3B_SELECT(16, false);
+  else if (longest <= 32 * 32) H3B_SELECT(32, false);
+  else if (longest <= 64 * 32) H3B_SELECT(64, false);
+  else if (longest <= 160 * 32) H3B_SELECT(160, false);
   else return set_error(H3B_EINVAL, "topk_rows: span of %d tiles is too long (max 5120)", longest);
-#undef H3B_TOPK
+#undef H3B_SELECT
   H3B_LAUNCH_CHECK("topk_rows");
   return H3B_OK;
 }

@@ -70,25 +70,38 @@ class _Exchange:
         self.world = sp.world
         self.virtual = isinstance(sp, VirtualSeqParallel)
         self.ranks = list(range(sp.world)) if self.virtual else [sp.rank]
+        # when a list: (name, start event, end event) of every NCCL exchange is appended to it (device timing of the
+        # collectives, read after the step; recording events does not synchronize)
+        self.timing = None
+
+    def _a2a(self, name: str, out: torch.Tensor, x: torch.Tensor) -> None:
+        if self.timing is None:
+            dist.all_to_all_single(out, x, group=self.sp.group)
+            return
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        dist.all_to_all_single(out, x, group=self.sp.group)
+        e1.record()
+        self.timing.append((name, e0, e1))
 
     def tiles(self, n_tiles: int, rank: int) -> tuple[int, int]:
         return self.sp.tiles(n_tiles, rank) if self.virtual else self.sp.tiles(n_tiles)
 
-    def seq_to_heads(self, xs: list[torch.Tensor], outs: list[torch.Tensor]) -> None:
+    def seq_to_heads(self, xs: list[torch.Tensor], outs: list[torch.Tensor], name: str = "seq_to_heads") -> None:
         """[H, R, ...] per rank -> [P, Hl, R, ...] per rank, written into ``outs``."""
         P = self.world
         if not self.virtual:
             if P == 1:
                 outs[0].copy_(xs[0].view(outs[0].shape)) if outs[0].data_ptr() != xs[0].data_ptr() else None
                 return
-            dist.all_to_all_single(outs[0], xs[0], group=self.sp.group)
+            self._a2a(name, outs[0], xs[0])
             return
         Hl = xs[0].shape[0] // P
         for r in range(P):
             for p in range(P):
                 outs[r][p].copy_(xs[p][r * Hl:(r + 1) * Hl])
 
-    def heads_to_seq(self, ys: list[torch.Tensor], outs: list[torch.Tensor]) -> None:
+    def heads_to_seq(self, ys: list[torch.Tensor], outs: list[torch.Tensor], name: str = "heads_to_seq") -> None:
         """[P, Hl, R, ...] per rank -> [H, R, ...] per rank."""
         P = self.world
         if not self.virtual:
@@ -96,7 +109,7 @@ class _Exchange:
                 if outs[0].data_ptr() != ys[0].data_ptr():
                     outs[0].copy_(ys[0].view(outs[0].shape))
                 return
-            dist.all_to_all_single(outs[0], ys[0], group=self.sp.group)
+            self._a2a(name, outs[0], ys[0])
             return
         Hl = ys[0].shape[1]
         for r in range(P):
@@ -187,6 +200,9 @@ class H3FastRunner:
         # trace(block, stage, rank, {name: tensor}) after each stage when set (tests and debugging); the tensors are the
         # live buffers, so a tracer that keeps them must copy them
         self.trace = None
+        # read the kernels' device status words after each forward's last kernel and raise on a failure (a bounded
+        # wait that expired, a selection list longer than the attention kernel holds); costs one host sync per step
+        self.check_status = True
 
     def refresh_weights(self) -> None:
         """(Re)builds the GEMM B operands of every block from its linears' packed weights: at construction, and after
@@ -408,7 +424,10 @@ class H3FastRunner:
             t = torch.empty_like(full.perm)
             t[full.perm] = torch.arange(full.rows)
             inv = self._inv_cache[id(full)] = (full, t.to(out.device))
-        return out.index_select(0, inv[1]).unsqueeze(0)
+        result = out.index_select(0, inv[1]).unsqueeze(0)
+        if self.check_status and not torch.cuda.is_current_stream_capturing():
+            ops.check_status(self.dev)
+        return result
 
     def _reduced(self, plan: TokenReduction, meta: VsaMeta) -> dict:
         """The paired layout of ``plan`` (its grid at half width, RoPE at the pairs' mean positions) and the compact-row
@@ -469,11 +488,10 @@ class H3FastRunner:
             self._t(i, "prologue", st, qb=b["qb"], kb=b["kb"], vb=b["vb"], qs=b["qs"], ks=b["ks"], vs=b["vs"],
                     qp=b["qp"], kp=b["kp"])
         # ---- sequence -> heads
-        self.ex.seq_to_heads([st.b["qb"] for st in states], [st.b["qb_x"] for st in states])
-        self.ex.seq_to_heads([st.b["kb"] for st in states], [st.b["kb_x"] for st in states])
-        self.ex.seq_to_heads([st.b["vb"] for st in states], [st.b["vb_x"] for st in states])
+        for nm in ("qb", "kb", "vb"):
+            self.ex.seq_to_heads([st.b[nm] for st in states], [st.b[nm + "_x"] for st in states], "qkv_e4m3")
         for nm in ("qs", "ks", "vs", "qp", "kp") + (("vp",) if gate else ()):
-            self.ex.seq_to_heads([st.b[nm] for st in states], [st.b[nm + "_x"] for st in states])
+            self.ex.seq_to_heads([st.b[nm] for st in states], [st.b[nm + "_x"] for st in states], "tile_stats")
         # ---- coarse step and sparse attention over this rank's heads, every rank's rows
         for st in states:
             b = st.b
@@ -498,7 +516,7 @@ class H3FastRunner:
                            q_scale_ld=n_all, kv_scale_ld=n_all, qk_int8=self.qk_int8)
             self._t(i, "attn", st, ob_x=b["ob_x"])
         # ---- heads -> sequence
-        self.ex.heads_to_seq([st.b["ob_x"] for st in states], [st.b["ob"] for st in states])
+        self.ex.heads_to_seq([st.b["ob_x"] for st in states], [st.b["ob"] for st in states], "attn_out_bf16")
         if gate:
             main.wait_stream(self.side)
             if P > 1:  # [Hl, n_all, D] -> [P, Hl, n_local, D] -> every head of this rank's tiles
@@ -623,9 +641,10 @@ class Fp8BlockChain:
         if self.trace is not None:
             self.trace(stage, tensors)
 
-    def __call__(self, x: torch.Tensor, tabs: torch.Tensor) -> torch.Tensor:
+    def __call__(self, x: torch.Tensor, tabs: torch.Tensor, check: bool = True) -> torch.Tensor:
         """x bf16 [rows, 5120] updated in place; tabs bf16 [6, 5120] = shift, scale, gate (attention half), shift,
-        scale, gate (MLP half)."""
+        scale, gate (MLP half). ``check``: read the GEMMs' device status word after the last GEMM (one host sync) and
+        raise on a failure."""
         rows, C = x.shape
         b = self._buffers(rows, x.device)
         ops.resid_norm_quant(x, None, None, None, None, None, tabs[0:1], tabs[1:2], x, b["h"], None, b["hs"],
@@ -645,6 +664,8 @@ class Fp8BlockChain:
         ops.gemm_fp8(b["f"], self.fc_out["w"], x, scale_a=b["fs"], scale_b=self.fc_out["col"], residual=x,
                      gate=tabs[5])
         self._t("fc_out", x=x)
+        if check and not torch.cuda.is_current_stream_capturing():
+            ops.check_status(x.device)
         return x
 
 
@@ -679,4 +700,6 @@ class GraphedForward:
         if temb is not None:
             self.temb.copy_(temb)
         self.graph.replay()
+        if self.runner.check_status:
+            ops.check_status(self.runner.dev)
         return self.out

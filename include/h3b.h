@@ -89,8 +89,9 @@ int h3b_quant_nvfp4(const void* x, int64_t ld, int64_t rows, int K, void* q, uin
  * only hands the library the tensors it owns -- a plugin running inside an engine whose device memory is planned up
  * front, or a foreign-language host with a fixed buffer set -- cannot call cudaMalloc for a workspace mid-run. This
  * variant keeps its scratch in a 256-byte static device array (present on every GPU that loads the library until the
- * process exits) and allocates nothing. The first call on each device looks up the array's device address; make that
- * first call before any stream capture. Every call on a device shares the array and zeroes it first, so calls that
+ * process exits) and allocates nothing. The first call on each device looks up the array's device address (and so
+ * does the first call after the thread's context on that device changed, e.g. after cudaDeviceReset); make that first
+ * call before any stream capture. Every call on a device shares the array and zeroes it first, so calls that
  * overlap on the GPU (e.g. on two streams) race and must be serialized by the caller. Same arguments and results as
  * h3b_quant_nvfp4 without the workspace; a build whose scratch need exceeds the array is rejected with H3B_EINVAL. */
 int h3b_quant_nvfp4_noalloc(const void* x, int64_t ld, int64_t rows, int K, void* q, uint8_t* sf, float* s_out,
@@ -305,6 +306,12 @@ int h3b_attn_gate_quant(const void* ob, const void* g, const float* sg, const vo
  * h3b_reset_device_status. Both synchronize the current device. */
 int h3b_device_status(int* status);
 int h3b_reset_device_status(void);
+/* The kernels' device status words, read in stream order (no counterpart in the reference, whose kernels have no
+ * bounded waits): dst[0] = the GEMMs' word (H3B_ETIMEOUT when a bounded wait expired), dst[1] = the attention's
+ * (H3B_ETIMEOUT, or H3B_EINVAL when a selection list exceeded the 1024 key tiles the kernel holds). dst is device
+ * memory or page-locked host memory for two ints; with `clear` both words are reset after the read. A step that
+ * enqueues this after its last kernel and checks dst once the stream reaches it learns of any failure in the step. */
+int h3b_status_async(int* dst, int clear, cudaStream_t stream);
 /* Exercises the bounded-wait path without a fault: one warp waits on an mbarrier nothing arrives on, with the kernels'
  * wait helper, gives up after limit_ns (<= 2 s) and sets the status word to H3B_ETIMEOUT; the context stays usable. */
 int h3b_selftest_wait_timeout(uint64_t limit_ns, cudaStream_t stream);

@@ -150,3 +150,20 @@ def reduction_inputs(grid: tuple[int, int, int], video_start: int, C: int, seed:
     R = video_start + t * h * ((w + 1) // 2)
     delta = (torch.randn(1, R, C, generator=g) * 0.25).bfloat16()
     return {"x": x, "positions": pos, "delta": delta}
+
+
+def fp8_pack_weight(N: int, K: int, seed: int, std: float, big_rows: int, zero_rows: int) -> torch.Tensor:
+    """A dense bf16 weight [N, K] ~ N(0, std) with ``big_rows`` rows scaled x300 (values past the E4M3 range of the
+    tensor scale's neighbours) and ``zero_rows`` all-zero rows (the scale floor)."""
+    g = torch.Generator().manual_seed(seed)
+    w = torch.randn(N, K, generator=g) * std
+    rows = torch.randperm(N, generator=g)
+    w[rows[:big_rows]] *= 300.0
+    w[rows[big_rows:big_rows + zero_rows]] = 0.0
+    return w.bfloat16()
+
+
+FP8_PACK_CASES = {
+    "fp8pack_small": dict(N=128, K=512, seed=51, std=0.02, big_rows=3, zero_rows=2),
+    "fp8pack_3072": dict(N=32, K=3072, seed=52, std=0.02, big_rows=1, zero_rows=1),
+}

@@ -133,7 +133,13 @@ def main() -> None:
     mod, cdll = load()
     if mod is None:
         raise SystemExit("oracle/_ref/h3ref.so is missing: run oracle/ref_build/build_ref.py where the reference is")
-    outdirs = [HERE, ROOT / "gpurun_out" / "golden"]
+    args = sys.argv[1:]
+    extra = []
+    if "--also-to" in args:  # a second copy of every fixture (e.g. a folder a remote run sends back)
+        i = args.index("--also-to")
+        extra = [Path(args[i + 1])]
+        del args[i:i + 2]
+    outdirs = [HERE, *extra]
     for dd in outdirs:
         dd.mkdir(parents=True, exist_ok=True)
     jobs = [(name, (lambda p=p, kind=kind: run_rnq(mod, cdll, **p) if kind == "rnq" else run_nvfp4(cdll, **p)))
@@ -141,7 +147,7 @@ def main() -> None:
     jobs += [(name, (lambda p=p: run_topk(mod, **p))) for name, p in TOPK_CASES.items()]
     jobs += [(name, (lambda p=p: run_prologue(mod, **p))) for name, p in PROLOGUE_CASES.items()]
     jobs += [(name, (lambda p=p: run_gate(cdll, **p))) for name, p in GATE_CASES.items()]
-    only = set(sys.argv[1:])
+    only = set(args)
     for name, job in jobs:
         if only and name not in only:
             continue

@@ -257,3 +257,14 @@ def test_bounded_wait_expires_with_status_and_context_survives(ops):
     ref = (a.float() @ w.float().t()).bfloat16().float()
     assert rel(y.float().cpu(), ref.cpu()) < TOL
     assert ops.device_status() == 0
+
+
+def test_check_status_raises_after_an_expired_wait(ops):
+    """ops.check_status (what the runner calls after each step) turns an expired wait into a RuntimeError, clears the
+    word, and passes on the next check."""
+    ops.check_status()
+    ops.selftest_wait_timeout(20_000_000)  # 20 ms
+    with pytest.raises(RuntimeError, match="ETIMEOUT"):
+        ops.check_status()
+    ops.check_status()
+    assert ops.device_status() == 0

@@ -9,6 +9,8 @@ Three references, strongest first:
 """
 from __future__ import annotations
 
+from pathlib import Path
+
 import numpy as np
 import pytest
 import torch
@@ -239,3 +241,17 @@ def test_nvfp4_weight_packing(ops):
     assert_scales(ws.cpu().numpy(), np.array([s]), "weight tensor scale")
     assert_codes(oq.unswizzle_sf(_u8(wsf), N, K // 16), oq.unswizzle_sf(sf, N, K // 16), sf_amb, "weight sf")
     assert_codes(oq.unpack_nibbles(_u8(wq)), oq.unpack_nibbles(q), amb, "weight nibbles")
+
+
+@pytest.mark.parametrize("case", ["fp8pack_small", "fp8pack_3072"])
+@pytest.mark.parametrize("gran", ["channel", "tensor"])
+def test_fp8_weight_packing_vs_reference_run(ops, case, gran):
+    """h3b_pack_weight_fp8 against the reference's own quantize_fp8_weight (patch:384-394) run on the same seeded
+    weights (golden fixture from tests/golden/gen_fp8_pack_golden.py): codes and scales bit for bit."""
+    from cases import FP8_PACK_CASES, fp8_pack_weight
+    gold = np.load(Path(__file__).resolve().parent / "golden" / "fp8_weight_pack.npz")
+    w = fp8_pack_weight(**FP8_PACK_CASES[case]).to(DEV)
+    q, s = ops.quantize_fp8_weight(w, gran)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(q.view(torch.uint8).cpu().numpy(), gold[f"{case}.{gran}.q"])
+    np.testing.assert_array_equal(s.cpu().numpy().view(np.uint32), gold[f"{case}.{gran}.s"].view(np.uint32))

@@ -89,6 +89,21 @@ def test_sharded_block_loop_equals_single_rank(pkg, grid):
         assert torch.equal(got.view(torch.int16), ref.view(torch.int16)), P
 
 
+def test_forward_raises_on_an_overlong_selection(pkg):
+    """The attention kernel holds at most 1024 selected key tiles per query tile. A longer list is not a fault: the
+    kernel clamps it and records H3B_EINVAL in its status word, and forward raises instead of returning the truncated
+    attention. The read clears the word, so the next valid step returns normally."""
+    _, runner = pkg
+    m, x, ctx, temb, meta = make(pkg, blocks=1, grid=(4, 64, 288))  # 1152 tiles of 64 tokens
+    r = runner.H3FastRunner(m)
+    meta.topk = 1100
+    with pytest.raises(RuntimeError, match="EINVAL"):
+        r.forward(x, temb, None, None, meta, context=ctx)
+    meta.topk = 32
+    out = r.forward(x, temb, None, None, meta, context=ctx)
+    assert torch.isfinite(out.float()).all()
+
+
 @pytest.mark.parametrize("fmt", ["nvfp4", "fp8"])
 def test_gate_compress_branch(pkg, fmt):
     """The optional gate-compress branch (gate GEMM and compressed attention on the side stream, joined in the gate

@@ -54,6 +54,20 @@ def test_noalloc_matches_workspace_version_on_two_calls(h3b):
         assert torch.equal(sf0, sf1)
 
 
+def test_noalloc_zero_rows_leaves_outputs(h3b):
+    """rows == 0 is a valid call that writes nothing."""
+    lib = h3b.lib()
+    x = torch.zeros(1, 128, device=DEV, dtype=torch.bfloat16)
+    q = torch.full((1, 64), 0x5A, device=DEV, dtype=torch.uint8)
+    sf = torch.full((128, 8), 0xA5, device=DEV, dtype=torch.uint8)
+    s = torch.full((1,), -1.0, device=DEV)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    rc = lib.h3b_quant_nvfp4_noalloc(x.data_ptr(), 128, 0, 128, q.data_ptr(), sf.data_ptr(), s.data_ptr(), stream)
+    torch.cuda.synchronize()
+    assert rc == 0, lib.h3b_last_error().decode()
+    assert (q == 0x5A).all() and (sf == 0xA5).all() and s.item() == -1.0
+
+
 def test_noalloc_rejects_bad_arguments(h3b):
     lib = h3b.lib()
     x = torch.zeros(4, 100, device=DEV, dtype=torch.bfloat16)  # K not a multiple of 64
