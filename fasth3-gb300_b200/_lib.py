@@ -74,6 +74,7 @@ SIGNATURES: dict[str, list] = {
     "h3b_vsa_fp8": [P, P, P, P, P, P, P, P, P, P, F32, P, P, I32, I32, I32, I64, P],
     "h3b_vsa_status": [ctypes.POINTER(I32), I32],
     "h3b_vsa_fp8_ex": [ctypes.POINTER(VsaArgs), P],
+    "h3b_vsa_pair": [ctypes.POINTER(VsaArgs), P, P],
     "h3b_tile_scores": [P, P, I32, I32, F32, P, P],
     "h3b_topk_rows": [P, I32, I32, I32, I32, I32, P, P, P, P, P, I32, P],
     "h3b_topk_pairs": [P, I32, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P],

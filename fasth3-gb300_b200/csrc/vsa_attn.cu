@@ -81,6 +81,9 @@ struct AttnArgs {
   int tpc_q, tpc_kv;  // tiles per chunk
   int64_t rows_chunk_q;
   int items;
+  // pair mode (topk_pairs' format): idx / num hold one union list per (head, pair of query tiles) and u_mem a
+  // membership byte per union entry (bit 0: tile 2p selected it, bit 1: tile 2p+1); NULL: one list per query tile
+  const uint8_t* u_mem;
 };
 
 struct __align__(1024) Smem {
@@ -272,14 +275,43 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!warp_wait(&sm.list_empty[buf], ((list_phase >> buf) & 1u) ^ 1u)) break;
       list_phase ^= 1u << buf;
       int n[2];
+      if (a.u_mem) {
+        // the pair's union list, ascending, split by membership into each query tile's own list (ballot
+        // compaction keeps the ascending order)
+        const size_t urow = (size_t)h * pairs + p;
+        const int u = min(max(a.num[urow], 0), a.idx_ld);
+        const int32_t* src = a.idx + urow * a.idx_ld;
+        const uint8_t* mem = a.u_mem + urow * a.idx_ld;
+        const uint32_t below = (1u << lane) - 1u;
+        int c[2] = {0, 0};
+        for (int base = 0; base < u; base += 32) {
+          const int i = base + lane;
+          const uint32_t mb = i < u ? mem[i] : 0u;
+          const uint16_t col = i < u ? (uint16_t)min(max(src[i], 0), a.n_kv - 1) : (uint16_t)0;
 #pragma unroll
-      for (int s = 0; s < 2; ++s) {
-        const int t = s ? t1 : t0;
-        const int want = min(max(a.num[(size_t)h * a.n_q_ext + t], 0), a.idx_ld);
-        n[s] = min(want, L_MAX);
-        if (want > L_MAX && lane == 0) atomicExch(&g_attn_status, H3B_EINVAL);
-        const int32_t* src = a.idx + ((size_t)h * a.n_q_ext + t) * a.idx_ld;
-        for (int i = lane; i < n[s]; i += 32) sm.list[buf][s][i] = (uint16_t)min(max(src[i], 0), a.n_kv - 1);
+          for (int s = 0; s < 2; ++s) {
+            const bool in = (mb >> s) & 1u;
+            const uint32_t m = __ballot_sync(0xffffffffu, in);
+            const int pos = c[s] + __popc(m & below);
+            if (in && pos < L_MAX) sm.list[buf][s][pos] = col;
+            c[s] += __popc(m);
+          }
+        }
+#pragma unroll
+        for (int s = 0; s < 2; ++s) {
+          n[s] = min(c[s], L_MAX);
+          if (c[s] > L_MAX && lane == 0) atomicExch(&g_attn_status, H3B_EINVAL);
+        }
+      } else {
+#pragma unroll
+        for (int s = 0; s < 2; ++s) {
+          const int t = s ? t1 : t0;
+          const int want = min(max(a.num[(size_t)h * a.n_q_ext + t], 0), a.idx_ld);
+          n[s] = min(want, L_MAX);
+          if (want > L_MAX && lane == 0) atomicExch(&g_attn_status, H3B_EINVAL);
+          const int32_t* src = a.idx + ((size_t)h * a.n_q_ext + t) * a.idx_ld;
+          for (int i = lane; i < n[s]; i += 32) sm.list[buf][s][i] = (uint16_t)min(max(src[i], 0), a.n_kv - 1);
+        }
       }
       __syncwarp();
       if (lane == 0) {
@@ -747,8 +779,26 @@ int make_map(CUtensorMap* m, const void* base, int64_t planes, int64_t rows) {
 
 using namespace h3b;
 
+namespace h3b {
+namespace {
+int vsa_launch(const h3b_vsa_args* x, const uint8_t* u_mem, cudaStream_t stream);
+}  // namespace
+}  // namespace h3b
+
 extern "C" int h3b_vsa_fp8_ex(const h3b_vsa_args* x, cudaStream_t stream) {
   clear_error();
+  return h3b::vsa_launch(x, nullptr, stream);
+}
+
+extern "C" int h3b_vsa_pair(const h3b_vsa_args* x, const uint8_t* u_mem, cudaStream_t stream) {
+  clear_error();
+  H3B_REQUIRE(u_mem, "vsa_pair: null membership bytes");
+  return h3b::vsa_launch(x, u_mem, stream);
+}
+
+namespace h3b {
+namespace {
+int vsa_launch(const h3b_vsa_args* x, const uint8_t* u_mem, cudaStream_t stream) {
   H3B_REQUIRE(x, "vsa_fp8: null argument block");
   H3B_REQUIRE(x->q && x->k && x->v && x->idx && x->num && x->vbs_q && x->vbs_kv && x->vs && x->vs_head && x->out,
               "vsa_fp8: null pointer");
@@ -772,7 +822,7 @@ extern "C" int h3b_vsa_fp8_ex(const h3b_vsa_args* x, cudaStream_t stream) {
   if (int rc = make_out_map(&mo, x->out, (int64_t)x->chunks_q * x->heads, x->rows_chunk_q)) return rc;
   AttnArgs a{x->idx, x->num, x->vbs_q, x->vbs_kv, x->qs, x->ks, x->vs, x->vs_head, x->qk_coef,
              static_cast<bf16*>(x->out), x->lse, x->heads, x->n_q_ext, x->n_kv, x->idx_ld, x->q_scale_ld,
-             x->kv_scale_ld, tpc_q, tpc_kv, x->rows_chunk_q, x->heads * (x->n_q_ext / 2)};
+             x->kv_scale_ld, tpc_q, tpc_kv, x->rows_chunk_q, x->heads * (x->n_q_ext / 2), u_mem};
   const int smem = (int)sizeof(Smem) + 1024;
   auto kern = x->qk_int8 ? vsa_fp8_kernel<true> : vsa_fp8_kernel<false>;
   static PerDevice setup[2];  // the shared-memory reservation per instantiation and device; the value is the SM count
@@ -789,6 +839,8 @@ extern "C" int h3b_vsa_fp8_ex(const h3b_vsa_args* x, cudaStream_t stream) {
   H3B_LAUNCH_CHECK("vsa_fp8");
   return H3B_OK;
 }
+}  // namespace
+}  // namespace h3b
 
 extern "C" int h3b_vsa_fp8(const void* qb, const void* kb, const void* vb, const int32_t* idx, const int32_t* num,
                            const int32_t* vbs, const float* qs_blk, const float* ks_blk, const float* vs_blk,

@@ -1,5 +1,7 @@
 """Token layout of the DiT latent for the VSA path: the compact tile order of FastH3's runner (_get_layout,
-fastvideo/models/dits/h3fast/__init__.py:183-260), built here from the latent grid directly.
+fastvideo/models/dits/h3fast/__init__.py:183-260), built from the latent grid (``tile_layout``) or, as the reference
+does, from FastVideo's VSA metadata (``tile_layout_from_metadata``: ``untile_combined_index`` and
+``variable_block_sizes``, with any prefix tiles -- text, audio, references -- ahead of the video tiles).
 
 Tokens of a T x H x W latent are grouped into 4 x 4 x 4 cubes (64-token tiles; cubes on the far edges are smaller,
 e.g. 48 tokens when the last time slab has 3 frames). Tiles are ordered (t, h, w); tokens inside a tile (t, h, w).
@@ -19,7 +21,7 @@ TILE = 64
 
 @dataclass
 class TileLayout:
-    grid: tuple[int, int, int]
+    grid: tuple[int, int, int] | None  # None for a layout built from metadata
     perm: torch.Tensor       # int64 [rows]: tile-ordered row -> token
     vbs: torch.Tensor        # int32 [n_ext]
     tile_row0: torch.Tensor  # int32 [n_ext]
@@ -84,3 +86,63 @@ def rope_positions(pos: torch.Tensor, rot_dims: int = 96, theta: float = 10000.0
     cos = torch.cat([a.cos(), a.cos()], 1)
     sin = torch.cat([a.sin(), a.sin()], 1)
     return cos.to(torch.bfloat16), sin.to(torch.bfloat16)
+
+
+def tile_layout_from_metadata(untile_combined_index: torch.Tensor, variable_block_sizes: torch.Tensor,
+                              pad_to: int = 2) -> TileLayout:
+    """The layout the reference's ``_get_layout`` derives from FastVideo's metadata (__init__.py:194-202):
+    ``perm = argsort(untile)`` (compact row -> packed row), ``slot = untile[perm]`` (compact row -> padded slot),
+    ``tile_row0 = cumsum(vbs) - vbs``; the tile list padded with empty tiles to a multiple of ``pad_to`` (the
+    reference pads to an even count). ``untile[packed row]`` is the token's slot ``tile * 64 + offset``; the offsets of
+    a tile's tokens must be 0 .. vbs-1 (the slots the prologue writes and the gate quantizer reads)."""
+    untile = untile_combined_index.reshape(-1).to(torch.int64).cpu()
+    vbs = variable_block_sizes.reshape(-1).to(torch.int32).cpu()
+    rows = untile.numel()
+    if int(vbs.sum()) != rows:
+        raise ValueError(f"variable_block_sizes sum to {int(vbs.sum())}, the index has {rows} tokens")
+    if bool((vbs > TILE).any()) or bool((vbs < 0).any()):
+        raise ValueError(f"variable_block_sizes must lie in [0, {TILE}]")
+    perm = torch.argsort(untile)
+    slot = untile[perm]
+    n = vbs.numel()
+    n_ext = (n + pad_to - 1) // pad_to * pad_to
+    vbs_ext = torch.cat([vbs, torch.zeros(n_ext - n, dtype=torch.int32)])
+    row0 = (vbs_ext.cumsum(0) - vbs_ext).to(torch.int32)
+    want = torch.cat([torch.arange(int(v)) + i * TILE for i, v in enumerate(vbs.tolist())]) if rows else slot
+    if not torch.equal(slot, want.to(slot.dtype)):
+        raise ValueError("untile_combined_index: each tile's tokens must take the slots tile * 64 + 0 .. vbs - 1")
+    return TileLayout(None, perm, vbs_ext, row0, slot.to(torch.int32), n, n_ext, rows)
+
+
+def vsa_metadata(grid: tuple[int, int, int], prefix_tokens: int = 0, cube=(4, 4, 4)) -> dict:
+    """FastVideo-style VSA metadata of a sequence of ``prefix_tokens`` exempt tokens (text, audio, references) followed
+    by a T x H x W video latent in raster order: the prefix cut into 64-token tiles (the last one partial), the latent
+    into 4 x 4 x 4 cubes (smaller on the far edges), tiles ordered prefix first, then (t, h, w).
+    Returns ``untile_combined_index`` (int64 [S]: the slot tile * 64 + offset of packed token i),
+    ``variable_block_sizes`` (int32 [n_tiles]), ``num_prefix_tiles`` and ``video_tile_spans`` ([(first video tile,
+    n_tiles)])."""
+    T, H, W = grid
+    ct, ch, cw = cube
+    nt, nh, nw = math.ceil(T / ct), math.ceil(H / ch), math.ceil(W / cw)
+    n_pre = (prefix_tokens + TILE - 1) // TILE
+    vbs = [min(TILE, prefix_tokens - TILE * i) for i in range(n_pre)]
+    untile = torch.empty(prefix_tokens + T * H * W, dtype=torch.int64)
+    untile[:prefix_tokens] = torch.arange(prefix_tokens)  # prefix tile i holds packed tokens 64i .. 64i + vbs - 1
+    tok = torch.arange(T * H * W).view(T, H, W) + prefix_tokens
+    tile = n_pre
+    for a in range(nt):
+        for b in range(nh):
+            for c in range(nw):
+                block = tok[a * ct:(a + 1) * ct, b * ch:(b + 1) * ch, c * cw:(c + 1) * cw].reshape(-1)
+                untile[block] = tile * TILE + torch.arange(block.numel())
+                vbs.append(block.numel())
+                tile += 1
+    return {"untile_combined_index": untile, "variable_block_sizes": torch.tensor(vbs, dtype=torch.int32),
+            "num_prefix_tiles": n_pre, "video_tile_spans": [(n_pre, tile)]}
+
+
+def compute_topk(sparsity: float, n_tiles: int) -> int:
+    """Key tiles kept per query tile in a span of ``n_tiles`` at ``sparsity`` (the reference calls FastVideo's
+    ``compute_topk`` here, __init__.py:443; FastVideo is not vendored, so its rounding is restated as
+    ceil((1 - sparsity) * n), at least 1)."""
+    return max(1, min(n_tiles, math.ceil((1.0 - float(sparsity)) * n_tiles - 1e-9)))

@@ -381,9 +381,28 @@ def attn_gate_quant(ob, g, sg, oc, slot, n_tiles, tile, a, asf, sa, rows, o1=Non
          _p(a), _p(asf), _p(sa), int(rows), W, _p(o1), _p(lse1a), _p(lse1b), n1, _p(lse2), _stream(ob))
 
 
+def vsa_pair(q8, k8, v8, u_idx, u_mem, u_num, vbs, qk_coef, v_scale_blk, v_scale_head, lse=None, q_scale_blk=None,
+             k_scale_blk=None, out=None):
+    """The pair form of the FP8 attention (vsa_pair_op, h3attn8.cu:44-77): per (head, pair of adjacent query tiles)
+    the union list ``u_idx`` [heads * n_ext/2, max_u] of length ``u_num`` with membership bytes ``u_mem`` (bit 0:
+    tile 2p, bit 1: tile 2p+1), as h3b_topk_pairs writes them. Q/K/V are the E4M3 [heads, rows_pad, 128] codes of
+    vsa_fp8; returns ``out`` bf16 [1, heads, rows_pad, 128]."""
+    heads, rows_pad = q8.shape[-3], q8.shape[-2]
+    n_ext = rows_pad // 64
+    if out is None:
+        out = torch.zeros(1, heads, rows_pad, 128, device=q8.device, dtype=torch.bfloat16)
+    if u_mem.dtype != torch.uint8 or u_mem.shape[-1] != u_idx.shape[-1]:
+        raise RuntimeError("u_mem: uint8 with the shape of u_idx")
+    return vsa_fp8_ex(q8, k8, v8, out, u_idx, u_num, vbs, vbs, v_scale_blk, v_scale_head, qk_coef, heads, n_ext,
+                      vbs.numel(), rows_pad, rows_pad, qs=q_scale_blk, ks=k_scale_blk, lse=lse,
+                      idx_ld=u_idx.shape[-1],
+                      q_scale_ld=q_scale_blk.shape[-1] if q_scale_blk is not None else n_ext,
+                      kv_scale_ld=v_scale_blk.shape[-1], _u_mem=u_mem)
+
+
 def vsa_fp8_ex(q, k, v, out, idx, num, vbs_q, vbs_kv, vs, vs_head, qk_coef, heads, n_q_ext, n_kv, rows_chunk_q,
                rows_chunk_kv, chunks_q=1, chunks_kv=1, qs=None, ks=None, lse=None, idx_ld=None, q_scale_ld=None,
-               kv_scale_ld=None, qk_int8: bool = False):
+               kv_scale_ld=None, qk_int8: bool = False, _u_mem=None):
     """General FP8 block-sparse attention (h3b_vsa_fp8_ex): chunked [chunks * heads, rows_chunk, 128] layouts (the
     all-to-all layout of sequence parallelism) and separate key/value tiles (cross-attention)."""
     import ctypes
@@ -401,5 +420,8 @@ def vsa_fp8_ex(q, k, v, out, idx, num, vbs_q, vbs_kv, vs, vs_head, qk_coef, head
     x.rows_chunk_q, x.rows_chunk_kv = int(rows_chunk_q), int(rows_chunk_kv)
     x.chunks_q, x.chunks_kv = int(chunks_q), int(chunks_kv)
     x.qk_int8 = int(bool(qk_int8))
-    call("h3b_vsa_fp8_ex", ctypes.byref(x), _stream(q))
+    if _u_mem is not None:
+        call("h3b_vsa_pair", ctypes.byref(x), _p(_u_mem), _stream(q))
+    else:
+        call("h3b_vsa_fp8_ex", ctypes.byref(x), _stream(q))
     return out

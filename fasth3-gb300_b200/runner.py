@@ -29,7 +29,7 @@ import torch
 import torch.distributed as dist
 
 from . import ops
-from .layout import TILE, TileLayout, rope_3d, rope_positions, tile_layout
+from .layout import TILE, TileLayout, compute_topk, rope_3d, rope_positions, tile_layout, tile_layout_from_metadata
 from .model import DiTModel, QuantLinear
 from .reduction import TokenReduction, pair_maps
 from .sp import SeqParallel
@@ -39,13 +39,53 @@ LOG2E = 1.4426950408889634
 
 @dataclass
 class VsaMeta:
-    """The VSA metadata the runner needs (the reference reads FastVideo's VideoSparseAttentionMetadata:
-    video_tile_spans, span_sparsities, num_prefix_tiles, tile_elems; __init__.py:171, 440-445)."""
-    grid: tuple[int, int, int]
+    """The VSA metadata the runner needs: the fields the reference reads from FastVideo's
+    VideoSparseAttentionMetadata (__init__.py:171, 187-204, 440-445, 501-503) plus this runner's defaults.
+
+    * ``grid``: the video latent (T, H, W); with no ``untile_combined_index`` the layout is built from it, the whole
+      sequence is video and every query tile keeps ``topk`` key tiles.
+    * ``untile_combined_index`` [S] / ``variable_block_sizes`` [n_tiles]: FastVideo's token -> slot map and tile
+      sizes; the layout is then built from them (``layout.tile_layout_from_metadata``), prefix tiles first.
+    * ``num_prefix_tiles``: exempt tiles (text, audio, references) every query tile attends to; their query tiles
+      attend to every key tile.
+    * ``video_tile_spans`` [(start, end)] with ``span_sparsities``: per span, compute_topk(sparsity, end - start) key
+      tiles per query tile (the reference's sparse_ks); ``dense_layers``: blocks whose query tiles keep every tile of
+      every span (dense_ks).
+    * ``dense_prefix``: the reference's FASTVIDEO_H3_DENSE_PREFIX (one rank): the prefix queries against every key,
+      and the other queries against the prefix keys, run as a separate dense pass (here this library's attention
+      kernel with every such tile selected), and the sparse pass keeps the span tiles only; the gate quantizer merges
+      the two by log-sum-exp (h3fast.cu:689-719)."""
+    grid: tuple[int, int, int] | None = None
     topk: int = 32
     tile_elems: int = 64
     exempt: bool = True
     pad_tokens: int = 0
+    untile_combined_index: torch.Tensor | None = None
+    variable_block_sizes: torch.Tensor | None = None
+    num_prefix_tiles: int = 0
+    video_tile_spans: list | None = None
+    span_sparsities: list | None = None
+    dense_layers: tuple = ()
+    dense_prefix: bool = False
+
+    def selection(self, n_tiles: int, block: int) -> dict:
+        """topk_rows' arguments for one block (the reference's _attn_cfg, __init__.py:440-445, and the dense-layer
+        switch at :501-503)."""
+        if self.video_tile_spans is None:
+            if self.num_prefix_tiles:
+                raise ValueError("num_prefix_tiles needs video_tile_spans")
+            k = min(self.topk, n_tiles)
+            return {"prefix": 0, "starts": [0], "ends": [n_tiles], "ks": [k], "split": False}
+        spans = [(int(a), int(b)) for a, b in self.video_tile_spans]
+        sparsities = self.span_sparsities if self.span_sparsities is not None else [None] * len(spans)
+        if len(sparsities) != len(spans):
+            raise ValueError("one sparsity per video tile span")
+        if block in tuple(self.dense_layers):
+            ks = [b - a for a, b in spans]
+        else:
+            ks = [min(self.topk, b - a) if sp is None else compute_topk(sp, b - a) for (a, b), sp in zip(spans, sparsities)]
+        return {"prefix": int(self.num_prefix_tiles), "starts": [a for a, _ in spans], "ends": [b for _, b in spans],
+                "ks": ks, "split": bool(self.dense_prefix and self.num_prefix_tiles > 0)}
 
 
 class VirtualSeqParallel:
@@ -172,7 +212,8 @@ def _fused_rows(lins: list[QuantLinear]) -> dict:
 
 class H3FastRunner:
     """All blocks of a DiTModel on the h3b kernels. ``sp``: a SeqParallel (one rank per process; NCCL on GPUs), a
-    VirtualSeqParallel (all ranks in this process), or None (one GPU). ``qk_int8``: the self-attention's Q and K as
+    VirtualSeqParallel (all ranks in this process), or None (this GPU alone, even inside an initialized process
+    group). ``qk_int8``: the self-attention's Q and K as
     per-tile int8 with the QK^T on the tensor cores' integer path (exact scores; E4M3 otherwise)."""
 
     def __init__(self, model: DiTModel, sp: SeqParallel | VirtualSeqParallel | None = None, qk_int8: bool = False):
@@ -185,7 +226,7 @@ class H3FastRunner:
         if self.head_dim != 128:
             raise ValueError("head_dim 128 only")
         self.fp4 = cfg.fmt == "nvfp4"
-        self.ex = _Exchange(sp if sp is not None else SeqParallel())
+        self.ex = _Exchange(sp if sp is not None else SeqParallel.local())
         if self.heads % self.ex.world:
             raise ValueError(f"{self.heads} heads do not split over {self.ex.world} ranks")
         self.layouts: dict[tuple, list[_RankState]] = {}
@@ -242,15 +283,25 @@ class H3FastRunner:
 
     # ------------------------------------------------------------------------------------------------- layout
     def _layouts(self, meta: VsaMeta, rotary, tag: object = None) -> tuple[TileLayout, list[_RankState]]:
-        key = (tuple(meta.grid), self.ex.world, tuple(self.ex.ranks), tag)
+        by_meta = meta.untile_combined_index is not None
+        src = (meta.untile_combined_index.data_ptr(), meta.untile_combined_index.numel()) if by_meta else \
+            tuple(meta.grid)
+        key = (src, self.ex.world, tuple(self.ex.ranks), tag, None if rotary is None else rotary[0].data_ptr())
         hit = self.layouts.get(key)
         if hit is not None:
             return hit
         P = self.ex.world
-        full = tile_layout(*meta.grid, pad_to=2 * P)
+        if by_meta:
+            if meta.variable_block_sizes is None:
+                raise ValueError("untile_combined_index needs variable_block_sizes")
+            full = tile_layout_from_metadata(meta.untile_combined_index, meta.variable_block_sizes, pad_to=2 * P)
+        else:
+            full = tile_layout(*meta.grid, pad_to=2 * P)
         if full.n_ext != full.n_tiles:
             raise ValueError(f"{full.n_tiles} tiles do not split into an even count per rank over {P} ranks")
         if rotary is None:
+            if full.grid is None:
+                raise ValueError("a layout from metadata needs the rotary tables (cos, sin) of its tokens")
             cos, sin = rope_3d(full)
         else:
             cos, sin = (t.reshape(-1, t.shape[-1])[full.perm] for t in rotary)
@@ -386,7 +437,9 @@ class H3FastRunner:
         full, states = self._layouts(meta, rotary)
         S = packed.shape[-2]
         if S != full.rows:
-            raise ValueError(f"packed has {S} tokens, the grid {meta.grid} has {full.rows}")
+            raise ValueError(f"packed has {S} tokens, the layout has {full.rows}")
+        if meta.dense_prefix and meta.num_prefix_tiles and self.ex.world != 1:
+            raise ValueError("the dense-prefix pass runs on one rank (like the reference runner)")
         if temb.reshape(-1, self.hidden).shape[0] != 1:
             raise ValueError("one timestep per forward: the gates are GEMM-epilogue column vectors")
         if adaln_indices is not None and bool((adaln_indices != 0).any()):
@@ -501,8 +554,9 @@ class H3FastRunner:
                     b[nm + "_all"].copy_(src.transpose(0, 1).reshape(b[nm + "_all"].shape))
             torch.amax(b["vs_all"], dim=1, out=b["vs_head"])
             ops.tile_scores(b["qp_all"], b["kp_all"], b["sc"], sm_scale)
-            k = min(meta.topk, n_all)
-            ops.topk_rows(b["sc"], n_all, n_all, 0, [0], [n_all], [k], b["idx"], b["num"], False)
+            sel = meta.selection(n_all, i)
+            ops.topk_rows(b["sc"], n_all, n_all, sel["prefix"], sel["starts"], sel["ends"], sel["ks"], b["idx"],
+                          b["num"], sel["split"])
             if gate:  # compressed branch oc = softmax(sc) @ vp on the side stream, beside the sparse attention
                 self.side.wait_stream(main)
                 with torch.cuda.stream(self.side):
@@ -510,10 +564,15 @@ class H3FastRunner:
             self._t(i, "select", st, qb_x=b["qb_x"], kb_x=b["kb_x"], vb_x=b["vb_x"], qs_all=b["qs_all"],
                     ks_all=b["ks_all"], vs_all=b["vs_all"], qp_all=b["qp_all"], kp_all=b["kp_all"],
                     vs_head=b["vs_head"], sc=b["sc"], idx=b["idx"], num=b["num"], vp_all=b.get("vp_all"))
+            lse2 = self._buf(b, "lse2", (Hl, st.rows_pad), torch.float32) if sel["split"] else None
             ops.vsa_fp8_ex(b["qb_x"], b["kb_x"], b["vb_x"], b["ob_x"], b["idx"], b["num"], b["vbs_all"],
                            b["vbs_all"], b["vs_all"], b["vs_head"], sm_scale * LOG2E, Hl, n_all, n_all, st.rows_pad,
-                           st.rows_pad, chunks_q=P, chunks_kv=P, qs=b["qs_all"], ks=b["ks_all"], idx_ld=n_all,
-                           q_scale_ld=n_all, kv_scale_ld=n_all, qk_int8=self.qk_int8)
+                           st.rows_pad, chunks_q=P, chunks_kv=P, qs=b["qs_all"], ks=b["ks_all"], lse=lse2,
+                           idx_ld=n_all, q_scale_ld=n_all, kv_scale_ld=n_all, qk_int8=self.qk_int8)
+            if sel["split"]:
+                self._dense_prefix(st, sel["prefix"], n_all, sm_scale)
+                self._t(i, "dense_prefix", st, o1=b["o1"], lse1a=b["lse1a"], lse1b=b["lse1b"], lse2=b["lse2"],
+                        ob_x=b["ob_x"])
             self._t(i, "attn", st, ob_x=b["ob_x"])
         # ---- heads -> sequence
         self.ex.heads_to_seq([st.b["ob_x"] for st in states], [st.b["ob"] for st in states], "attn_out_bf16")
@@ -529,12 +588,15 @@ class H3FastRunner:
             R = st.rows
             # attention output (+ the gated compressed branch) -> compact rows, quantized; out-projection with the
             # gated residual in the epilogue
+            merge = {}
+            if "o1" in b and meta.selection(n_all, i)["split"]:  # the dense-prefix pass, merged by log-sum-exp
+                merge = {"o1": b["o1"], "lse1a": b["lse1a"], "lse1b": b["lse1b"], "lse2": b["lse2"]}
             if gate:
                 ops.attn_gate_quant(b["ob"], b["g"], b["hs"], b["oc"], b["slot"], st.n_local, TILE, self._q(b["a"]),
-                                    b["a_sf"], b["as"], R)
+                                    b["a_sf"], b["as"], R, **merge)
             else:
                 ops.attn_gate_quant(b["ob"], None, None, None, b["slot"], st.n_local, TILE, self._q(b["a"]),
-                                    b["a_sf"], b["as"], R)
+                                    b["a_sf"], b["as"], R, **merge)
             self._t(i, "gate", st, ob=b["ob"], a=b["a"], a_sf=b["a_sf"], sa=b["as"], g=b.get("g") if gate else None,
                     oc=b.get("oc") if gate else None, hs=b["hs"] if gate else None, h=b["h"] if gate else None,
                     h_sf=b["h_sf"] if gate else None)
@@ -573,6 +635,69 @@ class H3FastRunner:
             # the next block's norm1 + modulate + quant
             if i + 1 < len(self.blocks):
                 self._norm(st, self.blocks[i + 1].eps, tabs[i + 1, 0:1], tabs[i + 1, 1:2], i + 1)
+
+    @staticmethod
+    def _buf(b: dict, name: str, shape: tuple, dtype, fill=None) -> torch.Tensor:
+        """A layout buffer created on first use (the dense-prefix buffers exist only for layouts that need them)."""
+        t = b.get(name)
+        if t is None or tuple(t.shape) != tuple(shape) or t.dtype != dtype:
+            dev = b["x"].device
+            t = b[name] = torch.empty(shape, device=dev, dtype=dtype) if fill is None else \
+                torch.full(shape, fill, device=dev, dtype=dtype)
+        return t
+
+    def _dense_prefix(self, st: _RankState, n_pre_tiles: int, n_all: int, sm_scale: float) -> None:
+        """The dense-prefix pass of one rank (the reference runs it on FlashAttention, __init__.py:304-324; here it
+        is this library's attention kernel with every such key tile selected, over the same E4M3 operands): (a) the
+        prefix query tiles against every key tile, in chunks of at most 1024 key tiles merged by log-sum-exp, and
+        (b) every other query tile against the prefix key tiles. Writes ``o1`` [rows, H, 128] bf16 (compact rows) and
+        the natural-log LSEs ``lse1a`` [H, prefix rows] / ``lse1b`` [H, other rows] that attn_gate_quant merges with
+        the sparse pass (h3fast.cu:689-719)."""
+        b = st.b
+        H = self.heads
+        L_MAX = 1024
+        if n_pre_tiles > L_MAX:
+            raise ValueError(f"{n_pre_tiles} prefix tiles: the attention kernel holds at most {L_MAX} per list")
+        dev, i32 = self.dev, torch.int32
+        rows_pad, R = st.rows_pad, st.rows
+        n_pre_rows = int(st.lay.tile_row0[n_pre_tiles]) if n_pre_tiles < st.lay.n_ext else R
+        n_q_a = n_pre_tiles + n_pre_tiles % 2
+        coef = sm_scale * LOG2E
+        args = dict(qs=b["qs_all"], ks=b["ks_all"], q_scale_ld=n_all, kv_scale_ld=n_all, qk_int8=self.qk_int8)
+        # (a) prefix queries x every key tile, key chunks of <= L_MAX tiles
+        outs = []
+        for c0 in range(0, n_all, L_MAX):
+            c1 = min(n_all, c0 + L_MAX)
+            idx = torch.arange(c0, c1, device=dev, dtype=i32).repeat(H, n_q_a, 1).contiguous()
+            num = torch.zeros(H, n_q_a, device=dev, dtype=i32)
+            num[:, :n_pre_tiles] = c1 - c0
+            out = torch.zeros(H, rows_pad, 128, device=dev, dtype=torch.bfloat16)
+            lse = torch.full((H, rows_pad), -float("inf"), device=dev, dtype=torch.float32)
+            ops.vsa_fp8_ex(b["qb_x"], b["kb_x"], b["vb_x"], out, idx, num, b["vbs_all"], b["vbs_all"], b["vs_all"],
+                           b["vs_head"], coef, H, n_q_a, n_all, rows_pad, rows_pad, lse=lse, idx_ld=c1 - c0, **args)
+            outs.append((out[:, :n_pre_tiles * TILE].float(), lse[:, :n_pre_tiles * TILE]))
+        lses = torch.stack([lse for _, lse in outs])
+        m = lses.amax(0)
+        m = torch.where(torch.isfinite(m), m, torch.zeros_like(m))
+        w = torch.exp2(lses - m)
+        den = w.sum(0)
+        out_a = sum(wc[..., None] * o for wc, (o, _) in zip(w, outs)) / den.clamp_min(1e-30)[..., None]
+        lse_a = torch.where(den > 0, m + torch.log2(den), torch.full_like(den, -float("inf")))
+        # (b) every other query tile x the prefix key tiles
+        idx = torch.arange(n_pre_tiles, device=dev, dtype=i32).repeat(H, n_all, 1).contiguous()
+        num = torch.full((H, n_all), n_pre_tiles, device=dev, dtype=i32)
+        num[:, :n_pre_tiles] = 0
+        out_b = torch.zeros(H, rows_pad, 128, device=dev, dtype=torch.bfloat16)
+        lse_b = torch.full((H, rows_pad), -float("inf"), device=dev, dtype=torch.float32)
+        ops.vsa_fp8_ex(b["qb_x"], b["kb_x"], b["vb_x"], out_b, idx, num, b["vbs_all"], b["vbs_all"], b["vs_all"],
+                       b["vs_head"], coef, H, n_all, n_all, rows_pad, rows_pad, lse=lse_b, idx_ld=n_pre_tiles, **args)
+        out_b[:, :n_pre_tiles * TILE] = out_a.to(torch.bfloat16)
+        lse_b[:, :n_pre_tiles * TILE] = lse_a
+        slot = b["slot"].long()
+        self._buf(b, "o1", (R, H, 128), torch.bfloat16).copy_(out_b[:, slot].transpose(0, 1))
+        lse_rows = lse_b[:, slot] * math.log(2.0)  # log2 -> natural log
+        self._buf(b, "lse1a", (H, n_pre_rows), torch.float32).copy_(lse_rows[:, :n_pre_rows])
+        self._buf(b, "lse1b", (H, R - n_pre_rows), torch.float32).copy_(lse_rows[:, n_pre_rows:])
 
     def _t(self, i: int, stage: str, st: _RankState, **tensors) -> None:
         if self.trace is not None:

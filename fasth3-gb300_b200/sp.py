@@ -23,6 +23,13 @@ class SeqParallel:
         self.world = dist.get_world_size(group) if (group is not None or dist.is_initialized()) else 1
         self.rank = dist.get_rank(group) if (group is not None or dist.is_initialized()) else 0
 
+    @classmethod
+    def local(cls) -> "SeqParallel":
+        """One rank with no exchange, whether or not a process group is initialized."""
+        sp = cls.__new__(cls)
+        sp.group, sp.world, sp.rank = None, 1, 0
+        return sp
+
     def tiles(self, n_tiles: int) -> tuple[int, int]:
         """[first, last) tile of this rank; n_tiles must split into an even count per rank."""
         if n_tiles % (2 * self.world):

@@ -265,6 +265,14 @@ typedef struct h3b_vsa_args {
                             S = Q K^T runs as tcgen05 kind::i8 with s32 accumulation (exact), else E4M3 */
 } h3b_vsa_args;
 int h3b_vsa_fp8_ex(const h3b_vsa_args* args, cudaStream_t stream);
+/* Replaces vsa_pair_op (fastvideo/models/dits/h3fast/h3attn8.cu:44-77; kernel vsa_pair.cuh:140-770): the same
+ * attention driven by topk_pairs' output (h3b_topk_pairs) -- per (head, pair of adjacent 64-token query tiles) the
+ * ascending union of both tiles' selections in args->idx [heads * n_q_ext/2, idx_ld] with its length in args->num
+ * [heads * n_q_ext/2], and u_mem [heads * n_q_ext/2, idx_ld] one membership byte per union entry (bit 0: tile 2p
+ * selected the key tile, bit 1: tile 2p+1). Every query row attends exactly its own tile's selection. A 128-token
+ * tile is run as a pair whose 128-key blocks appear as two 64-key blocks selected by both halves (byte 3). The other
+ * fields as h3b_vsa_fp8_ex; each tile's list holds at most 1024 key tiles (H3B_EINVAL in the status word beyond). */
+int h3b_vsa_pair(const h3b_vsa_args* args, const uint8_t* u_mem, cudaStream_t stream);
 /* Status word of the attention kernel's bounded waits (0 = none); reset != 0 clears it. Synchronizes the device. */
 int h3b_vsa_status(int* status, int reset);
 

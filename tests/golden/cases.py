@@ -167,3 +167,11 @@ FP8_PACK_CASES = {
     "fp8pack_small": dict(N=128, K=512, seed=51, std=0.02, big_rows=3, zero_rows=2),
     "fp8pack_3072": dict(N=32, K=3072, seed=52, std=0.02, big_rows=1, zero_rows=1),
 }
+
+
+# latent grids with exempt prefixes (text / audio / reference tokens ahead of the video tiles)
+LAYOUT_CASES = {
+    "layout_video_only": dict(grid=(3, 8, 8), prefix=0),
+    "layout_partial_prefix": dict(grid=(5, 8, 12), prefix=100),
+    "layout_prefix_512": dict(grid=(7, 16, 16), prefix=512),
+}

@@ -89,6 +89,113 @@ def test_sharded_block_loop_equals_single_rank(pkg, grid):
         assert torch.equal(got.view(torch.int16), ref.view(torch.int16)), P
 
 
+def make_prefixed(pkg, blocks, prefix=100, grid=(7, 16, 16), seed=3, **meta_kw):
+    """A sequence of ``prefix`` exempt tokens ahead of a video latent, described by FastVideo-style metadata (the layout
+    is built from untile_combined_index / variable_block_sizes), with RoPE tables in packed token order."""
+    model, runner = pkg
+    from fasth3_b200 import layout
+    cfg = model.DiTConfig(blocks=blocks, fmt="nvfp4")
+    m = model.DiTModel.random(cfg, device=DEV, seed=seed)
+    md = layout.vsa_metadata(grid, prefix)
+    S = md["untile_combined_index"].numel()
+    T, Hh, Ww = grid
+    tok = torch.arange(T * Hh * Ww)
+    pos = torch.zeros(S, 3)
+    pos[:prefix, 0] = torch.arange(prefix).float() * 0.25  # any fixed positions for the exempt tokens
+    pos[prefix:] = torch.stack([tok // (Hh * Ww), (tok // Ww) % Hh, tok % Ww], 1).float()
+    cos, sin = layout.rope_positions(pos)
+    g = torch.Generator(device=DEV).manual_seed(2000 + seed)
+    x = torch.randn(1, S, cfg.hidden, device=DEV, generator=g).bfloat16()
+    ctx = torch.randn(1, cfg.text_len, cfg.text_dim, device=DEV, generator=g).bfloat16()
+    temb = m.timestep_embedding(0.5)
+    meta = runner.VsaMeta(grid=None, untile_combined_index=md["untile_combined_index"],
+                          variable_block_sizes=md["variable_block_sizes"], num_prefix_tiles=md["num_prefix_tiles"],
+                          video_tile_spans=md["video_tile_spans"], **meta_kw)
+    return m, x, ctx, temb, meta, (cos.to(DEV), sin.to(DEV))
+
+
+def test_prefix_spans_and_dense_layers_drive_the_selection(pkg):
+    """With prefix tiles, a video span at sparsity 0.75 and block 1 dense: every video query tile keeps the prefix
+    tiles plus compute_topk(0.75, video tiles) of the span in sparse blocks and every tile in the dense block; prefix
+    query tiles keep every tile. The sharded loop (layout from metadata) equals one rank bit for bit."""
+    _, runner = pkg
+    from fasth3_b200 import layout
+    # 200 prefix tokens (4 tiles, the last one of 8 tokens) + 32 video tiles: 36 tiles, an even count per rank at P=2
+    m, x, ctx, temb, meta, rot = make_prefixed(pkg, blocks=2, prefix=200, span_sparsities=[0.75], dense_layers=(1,))
+    nums = {}
+    r = runner.H3FastRunner(m)
+    r.trace = lambda i, stage, rank, t: nums.__setitem__(i, t["num"].clone()) if stage == "select" else None
+    ref = r.forward(x, temb, None, rot, meta, context=ctx)
+    torch.cuda.synchronize()
+    assert torch.isfinite(ref.float()).all()
+    n_pre = meta.num_prefix_tiles
+    a, b = meta.video_tile_spans[0]
+    k = layout.compute_topk(0.75, b - a)
+    sparse, dense = nums[0].cpu(), nums[1].cpu()
+    assert (sparse[:, :n_pre] == b).all() and (sparse[:, n_pre:b] == n_pre + k).all()
+    assert (dense[:, :b] == b).all()
+    got = runner.H3FastRunner(m, runner.VirtualSeqParallel(2)).forward(x, temb, None, rot, meta, context=ctx)
+    torch.cuda.synchronize()
+    assert torch.equal(got.view(torch.int16), ref.view(torch.int16))
+
+
+@pytest.mark.parametrize("prefix", [100, 128])
+def test_dense_prefix_pass_merged_by_lse_equals_one_pass(pkg, prefix):
+    """The dense-prefix mode (prefix queries x every key and other queries x prefix keys as a separate dense pass of
+    this library's attention kernel, the sparse pass on the span tiles only, joined by the log-sum-exp merge in the
+    gate quantizer) against the same block with the prefix tiles inside every selection list: the same attention up
+    to accumulation order. The merged attention is restated from the traced pieces and compared before quantization
+    (5e-3); the NVFP4 attention codes agree within one quantization step (6e-2)."""
+    _, runner = pkg
+    m, x, ctx, temb, meta, rot = make_prefixed(pkg, blocks=1, prefix=prefix, span_sparsities=[0.75])
+    cap = {}
+
+    def tracer(tag):
+        def t(i, stage, rank, ts):
+            if stage == "gate":
+                cap[(tag, i)] = (ts["a"].clone(), ts["a_sf"].clone(), ts["sa"].clone(), ts["ob"].clone())
+            if stage == "dense_prefix":
+                cap[("dense", i)] = {k: v.clone() for k, v in ts.items()}
+        return t
+
+    r1 = runner.H3FastRunner(m)
+    r1.trace = tracer("one")
+    out1 = r1.forward(x, temb, None, rot, meta, context=ctx)
+    meta2 = runner.VsaMeta(**{**meta.__dict__, "dense_prefix": True})
+    r2 = runner.H3FastRunner(m)
+    r2.trace = tracer("split")
+    out2 = r2.forward(x, temb, None, rot, meta2, context=ctx)
+    torch.cuda.synchronize()
+    rows = x.shape[1]
+    slot = r2.layouts[next(iter(r2.layouts))][1][0].b["slot"].long()
+    # one block: both runs see the same input (in deeper stacks the residual streams drift apart by the NVFP4
+    # re-quantization of each block's attention output, and near-tie selections then differ)
+    for i in range(1):
+        a1, sf1, s1, ob1 = cap[("one", i)]
+        a2, sf2, s2, _ = cap[("split", i)]
+        # the merge the gate quantizer performs, restated in float64 from the traced pieces: the dense pass (o1,
+        # natural-log LSEs) and the sparse pass (its output and log2 LSE; prefix rows take the dense pass alone)
+        d = cap[("dense", i)]
+        ob2 = d["ob_x"][0].double()[:, slot].transpose(0, 1)  # [rows, H, 128]
+        l1 = torch.cat([d["lse1a"], d["lse1b"]], 1).double().t() / math.log(2.0)  # [rows, H], log2
+        l2 = d["lse2"].double()[:, slot].t()
+        n1 = d["lse1a"].shape[1]
+        l2[:n1] = -float("inf")
+        m = torch.maximum(l1, l2)
+        w1 = torch.where(torch.isfinite(m), torch.exp2(l1 - m), torch.zeros_like(m))
+        w2 = torch.where(torch.isfinite(m), torch.exp2(l2 - m), torch.zeros_like(m))
+        merged = (w1[..., None] * d["o1"].double() + torch.nan_to_num(w2[..., None] * ob2)) / (w1 + w2)[..., None]
+        one = ob1.double()[:, slot].transpose(0, 1)
+        assert rel(merged, one) < 5e-3, (i, rel(merged, one))
+        # after the NVFP4 re-quantization of either, codes near a rounding boundary may differ by one step
+        d1 = deq_nvfp4(a1, sf1, rows, a1.shape[1] * 2) * s1[:, None]
+        d2 = deq_nvfp4(a2, sf2, rows, a2.shape[1] * 2) * s2[:, None]
+        assert rel(d2, d1) < 6e-2, (i, rel(d2, d1))
+    # the block output carries the re-quantization noise of two more NVFP4 stages (out-projection input, FFN
+    # intermediate): a gross-error bound only; the merged attention above is the precise check
+    assert rel(out2.float(), out1.float()) < 0.1
+
+
 def test_forward_raises_on_an_overlong_selection(pkg):
     """The attention kernel holds at most 1024 selected key tiles per query tile. A longer list is not a fault: the
     kernel clamps it and records H3B_EINVAL in its status word, and forward raises instead of returning the truncated

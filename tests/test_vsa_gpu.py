@@ -545,3 +545,83 @@ def test_vsa_fp8_cross_attention_dense_text(ops):
     err = float((out.cpu().double()[:, :rows] - ref[:, :rows]).norm() / ref[:, :rows].norm())
     assert err < 1e-2
     assert (out.cpu()[:, rows:] == 0).all()  # rows past vbs_q are not written (buffer was zero)
+
+
+# ------------------------------------------------------------------------------------------------ pair form (f3)
+def _pair_operands(ops, heads, T, Hh, Ww, seed):
+    g = torch.Generator().manual_seed(seed)
+    S = T * Hh * Ww
+    perm = tile_permutation(T, Hh, Ww).to(DEV)
+    n = S // 64
+    vbs = torch.full((n,), 64, dtype=torch.int32, device=DEV)
+    row0 = (torch.arange(n, device=DEV) * 64).to(torch.int32)
+    q, kk, v = (torch.randn(heads, S, 128, generator=g).bfloat16().to(DEV) for _ in range(3))
+    qb, kb, vb = (torch.zeros(heads, S, 128, device=DEV, dtype=torch.uint8) for _ in range(3))
+    qs, ks, vs = (torch.ones(heads, n, device=DEV) for _ in range(3))
+    vs_head = torch.zeros(heads, device=DEV)
+    qp, kp, vp = (torch.zeros(heads, n, 128, device=DEV) for _ in range(3))
+    ops.vsa_tile_quant(q, kk, v, perm, row0, vbs, qb, kb, vb, qs, ks, vs, qp, kp, vp, n, vs_head=vs_head)
+    sc = torch.empty(heads, n, n, device=DEV)
+    ops.tile_scores(qp, kp, sc, 1.0 / math.sqrt(128))
+    return dict(qb=qb, kb=kb, vb=vb, qs=qs, ks=ks, vs=vs, vs_head=vs_head, vbs=vbs, sc=sc, n=n)
+
+
+def test_vsa_pair_equals_per_tile_lists(ops):
+    """vsa_pair on topk_pairs' union lists with membership bytes gives the same output bits as vsa_fp8 on topk_rows'
+    per-tile lists (every row attends exactly its own tile's selection), LSE included."""
+    heads, k = 3, 6
+    o = _pair_operands(ops, heads, 8, 16, 16, seed=61)
+    n = o["n"]
+    coef = math.log2(math.e) / math.sqrt(128)
+    idx = torch.full((1, heads, n, n), -1, device=DEV, dtype=torch.int32)
+    num = torch.zeros(1, heads, n, device=DEV, dtype=torch.int32)
+    ops.topk_rows(o["sc"], n, n, 0, [0], [n], [k], idx, num, False)
+    lse1 = torch.zeros(heads, n * 64, device=DEV)
+    out1 = ops.vsa_fp8(o["qb"], o["kb"], o["vb"], idx, num, o["vbs"], coef, o["vs"], o["vs_head"], lse=lse1,
+                       q_scale_blk=o["qs"], k_scale_blk=o["ks"])
+    P = heads * n // 2
+    u_idx = torch.full((P, n), -1, device=DEV, dtype=torch.int32)
+    u_mem = torch.zeros(P, n, device=DEV, dtype=torch.uint8)
+    u_num = torch.zeros(P, device=DEV, dtype=torch.int32)
+    ops.topk_pairs(o["sc"], n, n, 0, [0], [n], [k], u_idx, u_mem, u_num)
+    lse2 = torch.zeros(heads, n * 64, device=DEV)
+    out2 = ops.vsa_pair(o["qb"], o["kb"], o["vb"], u_idx, u_mem, u_num, o["vbs"], coef, o["vs"], o["vs_head"],
+                        lse=lse2, q_scale_blk=o["qs"], k_scale_blk=o["ks"])
+    torch.cuda.synchronize()
+    assert ops.vsa_status(reset=True) == 0
+    assert int(u_num.max()) > k  # the unions are longer than a single list
+    assert torch.equal(out1.view(torch.int16), out2.view(torch.int16))
+    assert torch.equal(lse1, lse2)
+
+
+def test_vsa_pair_runs_128_token_tiles(ops):
+    """128-token VSA through the pair form: each 128-row query tile selects 128-key blocks, handed over as pairs of
+    64-key blocks selected by both halves (membership byte 3). Equals vsa_fp8 with both 64-row halves given the
+    same list of 64-key blocks, and exact attention over the same E4M3 operands within 1e-2."""
+    heads, blocks_kept = 2, 3
+    o = _pair_operands(ops, heads, 8, 16, 16, seed=62)
+    n = o["n"]
+    nb = n // 2  # 128-key blocks
+    g = torch.Generator().manual_seed(63)
+    sel = torch.stack([torch.stack([torch.randperm(nb, generator=g)[:blocks_kept].sort().values
+                                    for _ in range(nb)]) for _ in range(heads)])  # [heads, 128-row tiles, kept]
+    u = torch.stack([2 * sel, 2 * sel + 1], -1).reshape(heads * nb, 2 * blocks_kept).to(torch.int32)
+    u_idx = torch.full((heads * nb, n), -1, dtype=torch.int32)
+    u_idx[:, :2 * blocks_kept] = u
+    u_mem = torch.full((heads * nb, n), 3, dtype=torch.uint8)
+    u_num = torch.full((heads * nb,), 2 * blocks_kept, dtype=torch.int32)
+    coef = math.log2(math.e) / math.sqrt(128)
+    out2 = ops.vsa_pair(o["qb"], o["kb"], o["vb"], u_idx.to(DEV), u_mem.to(DEV), u_num.to(DEV), o["vbs"], coef,
+                        o["vs"], o["vs_head"], q_scale_blk=o["qs"], k_scale_blk=o["ks"])
+    per_tile = u_idx.view(heads, nb, 1, n).expand(heads, nb, 2, n).reshape(1, heads, n, n).contiguous()
+    num = torch.full((1, heads, n), 2 * blocks_kept, dtype=torch.int32)
+    out1 = ops.vsa_fp8(o["qb"], o["kb"], o["vb"], per_tile.to(DEV), num.to(DEV), o["vbs"], coef, o["vs"],
+                       o["vs_head"], q_scale_blk=o["qs"], k_scale_blk=o["ks"])
+    torch.cuda.synchronize()
+    assert ops.vsa_status(reset=True) == 0
+    assert torch.equal(out1.view(torch.int16), out2.view(torch.int16))
+    deq = lambda codes, s: (oq.e4m3_decode(codes.cpu().numpy()).reshape(heads, n, 64, 128)  # noqa: E731
+                            * s.cpu().numpy()[:, :, None, None]).reshape(heads, n * 64, 128)
+    ref = ov.vsa_fine(deq(o["qb"], o["qs"]), deq(o["kb"], o["ks"]), deq(o["vb"], o["vs"]), per_tile.numpy()[0],
+                      num.numpy()[0], o["vbs"].cpu().numpy(), 1.0 / math.sqrt(128))
+    assert _rel(out2.cpu().float().numpy()[0], ref) < 1e-2
