@@ -135,6 +135,14 @@ __device__ __forceinline__ uint32_t e4m3x4(float a, float b, float c, float d) {
   return e4m3x2(a, b) | (e4m3x2(c, d) << 16);
 }
 
+// Four E4M3 codes (low byte first) -> four f16 (exact: every E4M3 value is an f16 value), low code in the low half.
+__device__ __forceinline__ uint2 e4m3x4_to_f16x4(uint32_t codes) {
+  uint2 r;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r.x) : "h"((uint16_t)(codes & 0xFFFFu)));
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r.y) : "h"((uint16_t)(codes >> 16)));
+  return r;
+}
+
 __device__ __forceinline__ float e4m3_to_float(uint32_t byte) {
   __half_raw h = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)byte, __NV_E4M3);
   return __half2float(__half(h));

@@ -52,7 +52,10 @@ using namespace sm100;
 constexpr int D = 128;
 constexpr int TILE = 64;
 constexpr int K_STAGES = 4;   // E4M3 K tiles of both query tiles (consumed by the S MMAs)
-constexpr int V_STAGES = 4;   // E4M3 V tiles of both query tiles (consumed by the conversion after the softmax)
+constexpr int V_STAGES = 4;   // V ring slots (barriers): E4M3 V tiles of both query tiles (consumed by the conversion
+                              // after the softmax), or 3 of f16 V tiles (consumed by the PV MMAs)
+template <bool VF16>
+constexpr int v_stages() { return 4; }
 constexpr int N_MAX = 2048;   // key tiles
 constexpr int L_MAX = 1024;   // longest selection list (more selected key tiles set H3B_EINVAL in the status word)
 constexpr int SOFT_WARPS = 8;  // two warpgroups
@@ -89,8 +92,10 @@ struct AttnArgs {
 struct __align__(1024) Smem {
   uint8_t q[2][TILE * D];                    // [query tile] E4M3, 128-byte swizzle
   uint8_t k[K_STAGES][2][TILE * D];          // [stage][query tile]
-  uint8_t v[V_STAGES][2][TILE * D];          // [stage][query tile]
-  uint8_t vf[2][2][2][TILE * 128];           // [warpgroup][query tile][half of d]: 64 keys x 64 f16, 128-byte rows
+  // V: with E4M3 V, the ring [4 stages][query tile][64 keys x 128 B] then the converted tiles V'
+  // [warpgroup][query tile][half of d][64 keys x 128 B] (also the epilogue's output staging boxes); with f16 V, the
+  // ring [4 stages][query tile][half of d][64 keys x 128 B] (the epilogue stores its rows directly)
+  uint8_t vbuf[128 * 1024];
   uint16_t list[2][2][L_MAX];                // [buffer][query tile] selected key tiles
   float ml[2][2][2][128];                    // [item parity][max, sum][warpgroup][TMEM lane]
   int cnt[2][2];                             // [buffer][query tile] list lengths
@@ -103,6 +108,14 @@ struct __align__(1024) Smem {
   uint32_t tmem_base;
   int abort_flag;
 };
+
+__device__ __forceinline__ uint8_t* v8_slot(Smem& sm, int stage, int s) { return sm.vbuf + (stage * 2 + s) * TILE * D; }
+__device__ __forceinline__ uint8_t* vconv(Smem& sm, int w, int s) {
+  return sm.vbuf + 64 * 1024 + (w * 2 + s) * 2 * TILE * 128;
+}
+__device__ __forceinline__ uint8_t* v16_slot(Smem& sm, int stage, int s) {
+  return sm.vbuf + (stage * 2 + s) * 2 * TILE * 128;
+}
 
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, int32_t z,
                                             uint64_t* bar) {
@@ -135,6 +148,34 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// max of three floats in one instruction (sm_100)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^(s * coef + nb) for two keys: both exponent arguments by one paired fp32 fused multiply-add (sm_100), rounded to
+// f16 (s0 in the low half) and exponentiated in f16x2
+__device__ __forceinline__ uint32_t ex2_pair(uint32_t s0, uint32_t s1, uint64_t coef2, uint64_t nb2) {
+  uint32_t e;
+  asm("{\n\t.reg .b64 s, x;\n\t.reg .f32 x0, x1;\n\t.reg .b32 h;\n\t"
+      "mov.b64 s, {%1, %2};\n\t"
+      "fma.rn.f32x2 x, s, %3, %4;\n\t"
+      "mov.b64 {x0, x1}, x;\n\t"
+      "cvt.rn.f16x2.f32 h, x1, x0;\n\t"
+      "ex2.approx.f16x2 %0, h;\n\t}"
+      : "=r"(e)
+      : "r"(s0), "r"(s1), "l"(coef2), "l"(nb2));
+  return e;
+}
+
+__device__ __forceinline__ uint64_t pack_f32x2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
 }
 
 // 2^x for two keys: x0 (low half) and x1 rounded to f16, exponentiated in f16x2
@@ -210,7 +251,7 @@ __device__ __forceinline__ bool warp_wait_bounded(uint64_t* bar, uint32_t parity
   return false;
 }
 
-template <bool QKI8>
+template <bool QKI8, bool VF16>
 __global__ void __launch_bounds__(THREADS, 1)
     vsa_fp8_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, const AttnArgs a) {
@@ -236,7 +277,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int s = 0; s < V_STAGES; ++s) {
       mbar_init(&sm.v_full[s], 1);
-      mbar_init(&sm.v_empty[s], SOFT_WARPS / 2);  // the step's warpgroup has converted the V tiles
+      // E4M3 V: the step's warpgroup has converted the V tiles; f16 V: the step's PV MMAs have read them
+      mbar_init(&sm.v_empty[s], VF16 ? 1 : SOFT_WARPS / 2);
     }
     mbar_init(&sm.ml_bar, SOFT_WARPS);
     mbar_init(&sm.o_full, 2);  // the last PV MMA of each issuer
@@ -356,15 +398,21 @@ __global__ void __launch_bounds__(THREADS, 1)
               break;
             }
             v_phase ^= 1u << vst;
-            mbar_arrive_expect_tx(&sm.v_full[vst], bytes);
+            mbar_arrive_expect_tx(&sm.v_full[vst], VF16 ? 2 * bytes : bytes);
 #pragma unroll
             for (int s = 0; s < 2; ++s) {
               if (s ? !has1 : !has0) continue;
               const int b = sm.list[buf][s][j];
-              tma_load_3d(&sm.v[vst][s][0], &tmV, 0, (b % a.tpc_kv) * TILE, (b / a.tpc_kv) * a.heads + h,
-                          &sm.v_full[vst]);
+              if constexpr (VF16) {  // 64 keys x 128 f16 as two 128-byte-wide boxes (the halves of d)
+                for (int half = 0; half < 2; ++half)
+                  tma_load_3d(v16_slot(sm, vst, s) + half * TILE * 128, &tmV, 128 * half, (b % a.tpc_kv) * TILE,
+                              (b / a.tpc_kv) * a.heads + h, &sm.v_full[vst]);
+              } else {
+                tma_load_3d(v8_slot(sm, vst, s), &tmV, 0, (b % a.tpc_kv) * TILE, (b / a.tpc_kv) * a.heads + h,
+                            &sm.v_full[vst]);
+              }
             }
-            if (++vst == V_STAGES) vst = 0;
+            if (++vst == v_stages<VF16>()) vst = 0;
           }
         }
       }
@@ -438,12 +486,23 @@ __global__ void __launch_bounds__(THREADS, 1)
             break;
           }
           p_phase ^= 1;
+          const uint32_t gv = gbase + (uint32_t)j;
+          const int vstage = (int)(gv % (uint32_t)v_stages<VF16>());
+          if constexpr (VF16) {  // the f16 V tiles of step j landed
+            if (!mbar_wait_bounded(&sm.v_full[vstage], (gv / (uint32_t)v_stages<VF16>()) & 1u, abort_flag,
+                                   kLimitNs)) {
+              fail();
+              ok = false;
+              break;
+            }
+          }
           tc_fence_after();
 #pragma unroll
           for (int s = 0; s < 2; ++s) {
             if (j >= (s ? n1 : n0)) continue;
             const uint32_t lo = s ? LANE_B : 0u;
-            const uint64_t dv = desc_mn_sw128(smem_addr(&sm.vf[w][s][0][0]), TILE * 128);
+            const uint64_t dv =
+                desc_mn_sw128(smem_addr(VF16 ? v16_slot(sm, vstage, s) : vconv(sm, w, s)), TILE * 128);
             const uint32_t bit = 1u << s;
 #pragma unroll
             for (int i = 0; i < 4; ++i)  // K = 16 keys per MMA: 8 TMEM columns of P, 16 rows (2048 bytes) of V'
@@ -452,6 +511,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             started |= bit;
           }
           tc_commit(&sm.pv_done[w]);
+          if constexpr (VF16) tc_commit(&sm.v_empty[vstage]);  // the V tiles of the stage are consumed
         }
         if (!ok) break;
         if (U <= w) {  // no step of this parity: O of this parity is not used, but the epilogue waits for both
@@ -536,13 +596,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (c >= vbs_j) sr[c] = __float_as_uint(-INFINITY);
         }
         const float coef = qcoef * ks_j;
-        float m8[8];
+        // row maximum: four chains of three-input maxima
+        float m4[4];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) m8[c] = __uint_as_float(sr[c]);
+        for (int c = 0; c < 4; ++c) m4[c] = fmaxf(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1]));
 #pragma unroll
-        for (int c = 8; c < 64; ++c) m8[c & 7] = fmaxf(m8[c & 7], __uint_as_float(sr[c]));
-        float mraw = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                           fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        for (int c = 4; c < 32; ++c)
+          m4[c & 3] = fmax3(m4[c & 3], __uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1]));
+        float mraw = fmax3(m4[0], m4[1], fmaxf(m4[2], m4[3]));
         if constexpr (QKI8) {
           if (mraw != -INFINITY) mraw = __fsub_rn(mraw, kS32Bias);  // exact
         }
@@ -579,10 +640,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           uint32_t acc[4] = {0u, 0u, 0u, 0u};
           const __half2 vr2 = __float2half2_rn(vs_j * inv_vhead);  // P' = P * sv_b / sv_head: V' is V8 itself
           const uint32_t vr = *reinterpret_cast<const uint32_t*>(&vr2);
+          const uint64_t coef2 = pack_f32x2(coef, coef), nb2 = pack_f32x2(nb, nb);
 #pragma unroll
           for (int c = 0; c < 32; ++c) {
-            const uint32_t e = ex2_f16x2(fmaf(__uint_as_float(sr[2 * c]), coef, nb),
-                                         fmaf(__uint_as_float(sr[2 * c + 1]), coef, nb));
+            const uint32_t e = ex2_pair(sr[2 * c], sr[2 * c + 1], coef2, nb2);
             acc[c & 3] = hadd2(acc[c & 3], e);
             pw[c] = hmul2(e, vr);
           }
@@ -596,7 +657,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         // that step ended and has normally completed while P was computed
         if (pv_count > 0 && !warp_wait(&sm.pv_done[w], (pv_count - 1) & 1u)) { ok = false; break; }
         tmem_st_32cols(tmem + lane_off + COL_P + 32 * w, pw);
-        // ---- V' of this step
+        // ---- V' of this step (E4M3 V only: f16 V tiles are read by the PV MMAs as they land)
+        if constexpr (!VF16) {
         if (!warp_wait(&sm.v_full[stage], (g / V_STAGES) & 1u)) { ok = false; break; }
         {
           // 16 E4M3 values (d = 16c .. 16c+15) of one key per thread and chunk; a warp covers 8 consecutive keys x 4
@@ -609,13 +671,13 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const int key = (lane & 7) + 8 * (q4 + 4 * (i & 1)), c = (lane >> 3) + 4 * (i >> 1);
-              raw[s][i] = *reinterpret_cast<const uint4*>(&sm.v[stage][s][0] + key * 128 + ((c ^ (key & 7)) << 4));
+              raw[s][i] = *reinterpret_cast<const uint4*>(v8_slot(sm, stage, s) + key * 128 + ((c ^ (key & 7)) << 4));
             }
           }
 #pragma unroll
           for (int s = 0; s < 2; ++s) {
             if (j >= (s ? n1 : n0)) continue;
-            uint8_t* dst = &sm.vf[w][s][0][0];
+            uint8_t* dst = vconv(sm, w, s);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const int key = (lane & 7) + 8 * (q4 + 4 * (i & 1)), c = (lane >> 3) + 4 * (i >> 1);
@@ -635,12 +697,13 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
         fence_proxy_async_smem();  // the generic-proxy stores become visible to the tensor core
+        }
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&sm.v_empty[stage]);  // the V tiles are consumed
-          mbar_arrive(&sm.p_full[w]);        // P of step j in TMEM and V' of step j in shared memory
+          if constexpr (!VF16) mbar_arrive(&sm.v_empty[stage]);  // the V tiles are consumed
+          mbar_arrive(&sm.p_full[w]);  // P of step j in TMEM (and, E4M3 V, V' of step j in shared memory)
         }
         ++pv_count;
       }
@@ -676,7 +739,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       // bytes of bf16 in a 64-row box per query tile (128-byte swizzle; the V' buffer of this warpgroup is idle here:
       // every PV of the item has completed), then one thread stores both boxes with TMA. Rows past the tile's length
       // are written as zeros (padding rows of the tile's 64-row slot).
-      uint8_t* box = &sm.vf[w][tsel][0][0];
+      uint8_t* box = vconv(sm, w, tsel);
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {
         const int c0 = 64 * w + 32 * cc;
@@ -701,22 +764,29 @@ __global__ void __launch_bounds__(THREADS, 1)
                 (g0 != 0.f ? __uint_as_float(o0[c + 1]) * g0 : 0.f) + (g1 != 0.f ? __uint_as_float(o1[c + 1]) * g1 : 0.f);
             pk[u] = row_ok ? pack_bf16x2(x0, x1) : 0u;
           }
-          const int chunk = 4 * cc + j;  // 16-byte chunk of the 128-byte box row
-          *reinterpret_cast<uint4*>(box + rt * 128 + ((chunk ^ (rt & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          if constexpr (VF16) {  // the row's 128 bytes of this warpgroup's columns, stored directly
+            *reinterpret_cast<uint4*>(a.out + orow * D + c0 + 8 * j) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          } else {
+            const int chunk = 4 * cc + j;  // 16-byte chunk of the 128-byte box row
+            *reinterpret_cast<uint4*>(box + rt * 128 + ((chunk ^ (rt & 7)) << 4)) =
+                make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          }
         }
       }
-      fence_proxy_async_smem();
-      asm volatile("bar.sync %0, 128;" ::"r"(1 + w) : "memory");  // the warpgroup's rows are staged
-      if (warp == 3 + 4 * w && lane == 0) {
+      if constexpr (!VF16) {
+        fence_proxy_async_smem();
+        asm volatile("bar.sync %0, 128;" ::"r"(1 + w) : "memory");  // the warpgroup's rows are staged
+        if (warp == 3 + 4 * w && lane == 0) {
 #pragma unroll
-        for (int s2 = 0; s2 < 2; ++s2) {
-          const int t = 2 * p + s2;
-          tma_store_3d(&sm.vf[w][s2][0][0], &tmO, 64 * w, (t % a.tpc_q) * TILE, (t / a.tpc_q) * a.heads + h);
+          for (int s2 = 0; s2 < 2; ++s2) {
+            const int t = 2 * p + s2;
+            tma_store_3d(vconv(sm, w, s2), &tmO, 64 * w, (t % a.tpc_q) * TILE, (t / a.tpc_q) * a.heads + h);
+          }
+          bulk_commit_group();
+          bulk_wait_read<0>();  // the boxes are read before the next conversion overwrites the V' buffer
         }
-        bulk_commit_group();
-        bulk_wait_read<0>();  // the boxes are read before the next conversion overwrites the V' buffer
+        asm volatile("bar.sync %0, 128;" ::"r"(1 + w) : "memory");
       }
-      asm volatile("bar.sync %0, 128;" ::"r"(1 + w) : "memory");
       if (a.lse && row_ok && w == 0) a.lse[orow] = L > 0.f ? M + __log2f(L) : -INFINITY;
     }
   }
@@ -760,6 +830,21 @@ int make_out_map(CUtensorMap* m, const void* base, int64_t planes, int64_t rows)
   return H3B_OK;
 }
 
+// f16 V [planes, rows, 128] as bytes [planes, rows, 256]: 128-byte-wide boxes of 64 rows (one half of d each)
+int make_map_v16(CUtensorMap* m, const void* base, int64_t planes, int64_t rows) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(H3B_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[3] = {(cuuint64_t)(2 * D), (cuuint64_t)rows, (cuuint64_t)planes};
+  cuuint64_t strides[2] = {(cuuint64_t)(2 * D), (cuuint64_t)rows * 2 * D};
+  cuuint32_t box[3] = {128, (cuuint32_t)TILE, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(H3B_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return H3B_OK;
+}
+
 int make_map(CUtensorMap* m, const void* base, int64_t planes, int64_t rows) {
   auto fn = encode_fn();
   if (!fn) return set_error(H3B_ECUDA, "cuTensorMapEncodeTiled is unavailable");
@@ -781,24 +866,35 @@ using namespace h3b;
 
 namespace h3b {
 namespace {
-int vsa_launch(const h3b_vsa_args* x, const uint8_t* u_mem, cudaStream_t stream);
+int vsa_launch(const h3b_vsa_args* x, const uint8_t* u_mem, bool v16, cudaStream_t stream);
 }  // namespace
 }  // namespace h3b
 
 extern "C" int h3b_vsa_fp8_ex(const h3b_vsa_args* x, cudaStream_t stream) {
   clear_error();
-  return h3b::vsa_launch(x, nullptr, stream);
+  return h3b::vsa_launch(x, nullptr, false, stream);
+}
+
+extern "C" int h3b_vsa_fp8_ex_v16(const h3b_vsa_args* x, cudaStream_t stream) {
+  clear_error();
+  return h3b::vsa_launch(x, nullptr, true, stream);
 }
 
 extern "C" int h3b_vsa_pair(const h3b_vsa_args* x, const uint8_t* u_mem, cudaStream_t stream) {
   clear_error();
   H3B_REQUIRE(u_mem, "vsa_pair: null membership bytes");
-  return h3b::vsa_launch(x, u_mem, stream);
+  return h3b::vsa_launch(x, u_mem, false, stream);
+}
+
+extern "C" int h3b_vsa_pair_v16(const h3b_vsa_args* x, const uint8_t* u_mem, cudaStream_t stream) {
+  clear_error();
+  H3B_REQUIRE(u_mem, "vsa_pair: null membership bytes");
+  return h3b::vsa_launch(x, u_mem, true, stream);
 }
 
 namespace h3b {
 namespace {
-int vsa_launch(const h3b_vsa_args* x, const uint8_t* u_mem, cudaStream_t stream) {
+int vsa_launch(const h3b_vsa_args* x, const uint8_t* u_mem, bool v16, cudaStream_t stream) {
   H3B_REQUIRE(x, "vsa_fp8: null argument block");
   H3B_REQUIRE(x->q && x->k && x->v && x->idx && x->num && x->vbs_q && x->vbs_kv && x->vs && x->vs_head && x->out,
               "vsa_fp8: null pointer");
@@ -818,16 +914,19 @@ int vsa_launch(const h3b_vsa_args* x, const uint8_t* u_mem, cudaStream_t stream)
   CUtensorMap mq, mk, mv, mo;
   if (int rc = make_map(&mq, x->q, (int64_t)x->chunks_q * x->heads, x->rows_chunk_q)) return rc;
   if (int rc = make_map(&mk, x->k, (int64_t)x->chunks_kv * x->heads, x->rows_chunk_kv)) return rc;
-  if (int rc = make_map(&mv, x->v, (int64_t)x->chunks_kv * x->heads, x->rows_chunk_kv)) return rc;
+  if (int rc = v16 ? make_map_v16(&mv, x->v, (int64_t)x->chunks_kv * x->heads, x->rows_chunk_kv)
+                    : make_map(&mv, x->v, (int64_t)x->chunks_kv * x->heads, x->rows_chunk_kv))
+    return rc;
   if (int rc = make_out_map(&mo, x->out, (int64_t)x->chunks_q * x->heads, x->rows_chunk_q)) return rc;
   AttnArgs a{x->idx, x->num, x->vbs_q, x->vbs_kv, x->qs, x->ks, x->vs, x->vs_head, x->qk_coef,
              static_cast<bf16*>(x->out), x->lse, x->heads, x->n_q_ext, x->n_kv, x->idx_ld, x->q_scale_ld,
              x->kv_scale_ld, tpc_q, tpc_kv, x->rows_chunk_q, x->heads * (x->n_q_ext / 2), u_mem};
   const int smem = (int)sizeof(Smem) + 1024;
-  auto kern = x->qk_int8 ? vsa_fp8_kernel<true> : vsa_fp8_kernel<false>;
-  static PerDevice setup[2];  // the shared-memory reservation per instantiation and device; the value is the SM count
+  auto kern = x->qk_int8 ? (v16 ? vsa_fp8_kernel<true, true> : vsa_fp8_kernel<true, false>)
+                         : (v16 ? vsa_fp8_kernel<false, true> : vsa_fp8_kernel<false, false>);
+  static PerDevice setup[4];  // the shared-memory reservation per instantiation and device; the value is the SM count
   int sms = 0;
-  if (int rc = setup[x->qk_int8 ? 1 : 0].get([&](int* v) {
+  if (int rc = setup[(x->qk_int8 ? 1 : 0) + (v16 ? 2 : 0)].get([&](int* v) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
           return set_error(H3B_ECUDA, "vsa_fp8: cannot reserve %d bytes of shared memory", smem);
         *v = current_sms();

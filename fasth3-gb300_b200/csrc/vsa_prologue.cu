@@ -50,6 +50,7 @@ struct ProArgs {
   int n_tiles;
   int n_ext;
   float eps;
+  int v16;  // V written as f16 (the decoded E4M3 values, 2 bytes per element) instead of E4M3 codes
 };
 
 __device__ __forceinline__ void unpack4(uint2 u, float (&f)[4]) {
@@ -307,7 +308,11 @@ __global__ void __launch_bounds__(NWARP * 32, 2) prologue_kernel(const ProArgs a
           *reinterpret_cast<uint32_t*>(a.kb + dst) =
               e4m3x4(kv[0] * inv_k, kv[1] * inv_k, kv[2] * inv_k, kv[3] * inv_k);
         }
-        *reinterpret_cast<uint32_t*>(a.vb + dst) = e4m3x4(vv[0] * inv_v, vv[1] * inv_v, vv[2] * inv_v, vv[3] * inv_v);
+        const uint32_t vcodes = e4m3x4(vv[0] * inv_v, vv[1] * inv_v, vv[2] * inv_v, vv[3] * inv_v);
+        if (a.v16)
+          *reinterpret_cast<uint2*>(a.vb + 2 * dst) = e4m3x4_to_f16x4(vcodes);
+        else
+          *reinterpret_cast<uint32_t*>(a.vb + dst) = vcodes;
       }
       const float inv = 1.f / (float)n;
       for (int e = threadIdx.x; e < 3 * D; e += NWARP * 32) {
@@ -375,7 +380,7 @@ extern "C" int h3b_qkv_prologue8(const void* q, const void* k, const void* v, in
             tile_row0, vbs, static_cast<const bf16*>(wq), static_cast<const bf16*>(wk),
             static_cast<const bf16*>(cosb), static_cast<const bf16*>(sinb), inv_sq, inv_sk,
             static_cast<uint8_t*>(qb), static_cast<uint8_t*>(kb), static_cast<uint8_t*>(vb), qs_blk, ks_blk, vs_blk,
-            vs_head, qp, kp, vp, heads, rows_pad, n_tiles, n_ext, eps};
+            vs_head, qp, kp, vp, heads, rows_pad, n_tiles, n_ext, eps, 0};
   const int rc = tile_qk ? launch_prologue<true, true>(a, stream) : launch_prologue<true, false>(a, stream);
   if (rc) return rc;
   H3B_LAUNCH_CHECK("qkv_prologue8");
@@ -401,7 +406,7 @@ extern "C" int h3b_qkv_prologue8_qk_int8(const void* q, const void* k, const voi
             tile_row0, vbs, static_cast<const bf16*>(wq), static_cast<const bf16*>(wk),
             static_cast<const bf16*>(cosb), static_cast<const bf16*>(sinb), 1.f, 1.f,
             static_cast<uint8_t*>(qb), static_cast<uint8_t*>(kb), static_cast<uint8_t*>(vb), qs_blk, ks_blk, vs_blk,
-            vs_head, qp, kp, vp, heads, rows_pad, n_tiles, n_ext, eps};
+            vs_head, qp, kp, vp, heads, rows_pad, n_tiles, n_ext, eps, 0};
   if (const int rc = launch_prologue<true, true, true>(a, stream)) return rc;
   H3B_LAUNCH_CHECK("qkv_prologue8_qk_int8");
   return H3B_OK;
@@ -421,9 +426,58 @@ extern "C" int h3b_vsa_tile_quant(const void* q, const void* k, const void* v, i
   ProArgs a{static_cast<const bf16*>(q), static_cast<const bf16*>(k), static_cast<const bf16*>(v), 0, seqlen, perm,
             nullptr, tile_row0, vbs, nullptr, nullptr, nullptr, nullptr, 0.f, 0.f, static_cast<uint8_t*>(qb),
             static_cast<uint8_t*>(kb), static_cast<uint8_t*>(vb), qs_blk, ks_blk, vs_blk, vs_head, qp, kp, vp, heads,
-            rows_pad, n_tiles, n_ext, 0.f};
+            rows_pad, n_tiles, n_ext, 0.f, 0};
   if (const int rc = launch_prologue<false, true>(a, stream)) return rc;
   H3B_LAUNCH_CHECK("vsa_tile_quant");
+  return H3B_OK;
+}
+
+extern "C" int h3b_vsa_tile_quant_v16(const void* q, const void* k, const void* v, int heads, int64_t seqlen,
+                                      const int32_t* perm, const int32_t* tile_row0, const int32_t* vbs, void* qb,
+                                      void* kb, void* vh, float* qs_blk, float* ks_blk, float* vs_blk, float* vs_head,
+                                      float* qp, float* kp, float* vp, int64_t rows_pad, int n_tiles, int n_ext,
+                                      cudaStream_t stream) {
+  clear_error();
+  H3B_REQUIRE(q && k && v && tile_row0 && vbs && qb && kb && vh && qs_blk && ks_blk && vs_blk && qp && kp && vp,
+              "vsa_tile_quant_v16: null pointer");
+  H3B_REQUIRE(heads > 0 && n_tiles > 0 && n_ext >= n_tiles && rows_pad >= (int64_t)n_ext * TILE && seqlen > 0,
+              "vsa_tile_quant_v16: bad heads / tiles / padding");
+  H3B_REQUIRE(aligned(q, 8) && aligned(k, 8) && aligned(v, 8) && aligned(vh, 16),
+              "vsa_tile_quant_v16: 8-byte aligned inputs, 16-byte aligned f16 V");
+  ProArgs a{static_cast<const bf16*>(q), static_cast<const bf16*>(k), static_cast<const bf16*>(v), 0, seqlen, perm,
+            nullptr, tile_row0, vbs, nullptr, nullptr, nullptr, nullptr, 0.f, 0.f, static_cast<uint8_t*>(qb),
+            static_cast<uint8_t*>(kb), static_cast<uint8_t*>(vh), qs_blk, ks_blk, vs_blk, vs_head, qp, kp, vp, heads,
+            rows_pad, n_tiles, n_ext, 0.f, 1};
+  if (const int rc = launch_prologue<false, true>(a, stream)) return rc;
+  H3B_LAUNCH_CHECK("vsa_tile_quant_v16");
+  return H3B_OK;
+}
+
+extern "C" int h3b_qkv_prologue8_tiles(const void* q, const void* k, const void* v, int64_t ld, const float* s1,
+                                       const int32_t* tile_row0, const int32_t* vbs, const void* wq, const void* wk,
+                                       const void* cosb, const void* sinb, void* qb, void* kb, void* vb,
+                                       float* qs_blk, float* ks_blk, float* vs_blk, float* vs_head, float* qp,
+                                       float* kp, float* vp, int heads, int64_t rows_pad, int n_tiles, int n_ext,
+                                       float eps, int flags, cudaStream_t stream) {
+  clear_error();
+  H3B_REQUIRE(q && k && v && s1 && tile_row0 && vbs && wq && wk && qb && kb && vb && qs_blk && ks_blk && vs_blk && qp &&
+                  kp && vp,
+              "qkv_prologue8_tiles: null pointer");
+  H3B_REQUIRE((cosb == nullptr) == (sinb == nullptr), "qkv_prologue8_tiles: give both or neither of cosb/sinb");
+  H3B_REQUIRE(heads > 0 && n_tiles > 0 && n_ext >= n_tiles && rows_pad >= (int64_t)n_ext * TILE,
+              "qkv_prologue8_tiles: bad heads / tiles / padding");
+  H3B_REQUIRE(ld % 4 == 0 && aligned(q, 8) && aligned(k, 8) && aligned(v, 8), "qkv_prologue8_tiles: 8-byte aligned rows");
+  H3B_REQUIRE((flags & ~3) == 0, "qkv_prologue8_tiles: unknown flag bits %d", flags);
+  const bool v16 = (flags & H3B_PRO_V_F16) != 0, i8 = (flags & H3B_PRO_QK_INT8) != 0;
+  H3B_REQUIRE(!v16 || aligned(vb, 16), "qkv_prologue8_tiles: 16-byte aligned f16 V");
+  ProArgs a{static_cast<const bf16*>(q), static_cast<const bf16*>(k), static_cast<const bf16*>(v), ld, 0, nullptr, s1,
+            tile_row0, vbs, static_cast<const bf16*>(wq), static_cast<const bf16*>(wk),
+            static_cast<const bf16*>(cosb), static_cast<const bf16*>(sinb), 1.f, 1.f,
+            static_cast<uint8_t*>(qb), static_cast<uint8_t*>(kb), static_cast<uint8_t*>(vb), qs_blk, ks_blk, vs_blk,
+            vs_head, qp, kp, vp, heads, rows_pad, n_tiles, n_ext, eps, v16 ? 1 : 0};
+  const int rc = i8 ? launch_prologue<true, true, true>(a, stream) : launch_prologue<true, true>(a, stream);
+  if (rc) return rc;
+  H3B_LAUNCH_CHECK("qkv_prologue8_tiles");
   return H3B_OK;
 }
 
@@ -447,6 +501,7 @@ struct HtqArgs {
   int64_t rows_pad;
   int n_ext;
   float eps;
+  int v16;  // written as f16 (decoded E4M3 values) instead of E4M3 codes
 };
 
 __global__ void __launch_bounds__(NWARP * 32) head_tile_quant_kernel(const HtqArgs a) {
@@ -516,8 +571,11 @@ __global__ void __launch_bounds__(NWARP * 32) head_tile_quant_kernel(const HtqAr
   for (int u = 0; u < RPW; ++u) {
     const int i = w + u * NWARP;
     if (i >= n) break;
-    *reinterpret_cast<uint32_t*>(a.xb + (plane + i) * D + l * 4) =
-        e4m3x4(xs[u][0] * inv, xs[u][1] * inv, xs[u][2] * inv, xs[u][3] * inv);
+    const uint32_t codes = e4m3x4(xs[u][0] * inv, xs[u][1] * inv, xs[u][2] * inv, xs[u][3] * inv);
+    if (a.v16)
+      *reinterpret_cast<uint2*>(a.xb + 2 * ((plane + i) * D + l * 4)) = e4m3x4_to_f16x4(codes);
+    else
+      *reinterpret_cast<uint32_t*>(a.xb + (plane + i) * D + l * 4) = codes;
   }
 }
 }  // namespace
@@ -534,8 +592,26 @@ extern "C" int h3b_head_tile_quant(const void* x, int64_t ld, const float* s1, c
   H3B_REQUIRE(ld % 4 == 0 && ld >= (int64_t)heads * D && aligned(x, 8), "head_tile_quant: 8-byte aligned rows");
   H3B_REQUIRE(!w || aligned(w, 8), "head_tile_quant: norm weight 8-byte aligned");
   HtqArgs a{static_cast<const bf16*>(x), ld, s1, tile_row0, vbs, static_cast<const bf16*>(w),
-            static_cast<uint8_t*>(xb), xs_blk, xs_head, heads, rows_pad, n_ext, eps};
+            static_cast<uint8_t*>(xb), xs_blk, xs_head, heads, rows_pad, n_ext, eps, 0};
   head_tile_quant_kernel<<<n_tiles * heads, NWARP * 32, 0, stream>>>(a);
   H3B_LAUNCH_CHECK("head_tile_quant");
+  return H3B_OK;
+}
+
+extern "C" int h3b_head_tile_quant_v16(const void* x, int64_t ld, const float* s1, const int32_t* tile_row0,
+                                       const int32_t* vbs, const void* w, void* xh, float* xs_blk, float* xs_head,
+                                       int heads, int64_t rows_pad, int n_tiles, int n_ext, float eps,
+                                       cudaStream_t stream) {
+  clear_error();
+  H3B_REQUIRE(x && tile_row0 && vbs && xh && xs_blk, "head_tile_quant_v16: null pointer");
+  H3B_REQUIRE(heads > 0 && n_tiles > 0 && n_ext >= n_tiles && rows_pad >= (int64_t)n_ext * TILE,
+              "head_tile_quant_v16: bad heads / tiles / padding");
+  H3B_REQUIRE(ld % 4 == 0 && ld >= (int64_t)heads * D && aligned(x, 8) && aligned(xh, 16),
+              "head_tile_quant_v16: 8-byte aligned rows, 16-byte aligned output");
+  H3B_REQUIRE(!w || aligned(w, 8), "head_tile_quant_v16: norm weight 8-byte aligned");
+  HtqArgs a{static_cast<const bf16*>(x), ld, s1, tile_row0, vbs, static_cast<const bf16*>(w),
+            static_cast<uint8_t*>(xh), xs_blk, xs_head, heads, rows_pad, n_ext, eps, 1};
+  head_tile_quant_kernel<<<n_tiles * heads, NWARP * 32, 0, stream>>>(a);
+  H3B_LAUNCH_CHECK("head_tile_quant_v16");
   return H3B_OK;
 }

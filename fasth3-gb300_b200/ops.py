@@ -294,6 +294,14 @@ def qkv_prologue8(q, k, v, s1, tile_row0, vbs, wq, wk, cosb, sinb, inv_sq, inv_s
         raise RuntimeError("qkv_prologue8: the dense-prefix write-back (qc/kc/vc) is not supported")
     rows_pad = vb.shape[-2]
     n_ext = vs_blk.shape[-1]
+    if vb.dtype == torch.float16:  # V as f16 (the decoded E4M3 values) for the f16-V attention
+        if qs_blk is None or ks_blk is None:
+            raise RuntimeError("qkv_prologue8: f16 V needs the per-tile Q/K scales")
+        flags = 2 | (1 if qk_int8 else 0)
+        call("h3b_qkv_prologue8_tiles", _p(q), _p(k), _p(v), q.stride(0), _p(s1), _p(tile_row0), _p(vbs), _p(wq),
+             _p(wk), _p(cosb), _p(sinb), _p(qb), _p(kb), _p(vb), _p(qs_blk), _p(ks_blk), _p(vs_blk), _p(vs_head),
+             _p(qp), _p(kp), _p(vp), int(heads), rows_pad, int(n_tiles), n_ext, float(eps), flags, _stream(q))
+        return
     if qk_int8:
         call("h3b_qkv_prologue8_qk_int8", _p(q), _p(k), _p(v), q.stride(0), _p(s1), _p(tile_row0), _p(vbs), _p(wq),
              _p(wk), _p(cosb), _p(sinb), _p(qb), _p(kb), _p(vb), _p(qs_blk), _p(ks_blk), _p(vs_blk), _p(vs_head),
@@ -309,7 +317,8 @@ def vsa_tile_quant(q, k, v, perm, tile_row0, vbs, qb, kb, vb, qs_blk, ks_blk, vs
     """BASELINE config 4's prologue: head-major q/k/v [heads, S, 128] gathered into 64-token tiles through ``perm``,
     per-tile E4M3 Q/K/V, tile means; ``vs_head`` (zeroed by the caller) receives the per-head max V scale."""
     heads, seqlen = q.shape[-3], q.shape[-2]
-    call("h3b_vsa_tile_quant", _p(q), _p(k), _p(v), heads, seqlen, _p(perm), _p(tile_row0), _p(vbs), _p(qb), _p(kb),
+    name = "h3b_vsa_tile_quant_v16" if vb.dtype == torch.float16 else "h3b_vsa_tile_quant"
+    call(name, _p(q), _p(k), _p(v), heads, seqlen, _p(perm), _p(tile_row0), _p(vbs), _p(qb), _p(kb),
          _p(vb), _p(qs_blk), _p(ks_blk), _p(vs_blk), _p(vs_head), _p(qp), _p(kp), _p(vp), vb.shape[-2], int(n_tiles),
          vs_blk.shape[-1], _stream(q))
 
@@ -317,7 +326,8 @@ def vsa_tile_quant(q, k, v, perm, tile_row0, vbs, qb, kb, vb, qs_blk, ks_blk, vs
 def head_tile_quant(x, s1, tile_row0, vbs, w, xb, xs_blk, xs_head, heads, n_tiles, eps=1e-6) -> None:
     """One tensor of the prologue's per-tile E4M3 form (cross-attention q, text k and v): optional row scale s1,
     optional per-head RMSNorm weight w, no RoPE. xb [heads, rows_pad, 128], xs_blk [heads, n_ext]."""
-    call("h3b_head_tile_quant", _p(x), x.stride(0), _p(s1), _p(tile_row0), _p(vbs), _p(w), _p(xb), _p(xs_blk),
+    name = "h3b_head_tile_quant_v16" if xb.dtype == torch.float16 else "h3b_head_tile_quant"
+    call(name, _p(x), x.stride(0), _p(s1), _p(tile_row0), _p(vbs), _p(w), _p(xb), _p(xs_blk),
          _p(xs_head), int(heads), xb.shape[-2], int(n_tiles), xs_blk.shape[-1], float(eps), _stream(x))
 
 
@@ -331,6 +341,10 @@ def vsa_fp8(q8, k8, v8, q2k_idx, q2k_num, vbs, qk_coef, v_scale_blk, v_scale_hea
     n = q2k_idx.shape[-1]
     if out is None:
         out = torch.zeros(1, heads, rows_pad, 128, device=q8.device, dtype=torch.bfloat16)
+    if v8.dtype == torch.float16:  # V as f16 (the decoded E4M3 values): the same call on the f16-V kernel
+        return vsa_fp8_ex(q8, k8, v8, out, q2k_idx, q2k_num, vbs, vbs, v_scale_blk, v_scale_head, qk_coef, heads,
+                          n_ext, n, rows_pad, rows_pad, qs=q_scale_blk, ks=k_scale_blk, lse=lse, idx_ld=n,
+                          q_scale_ld=n_ext, kv_scale_ld=n_ext)
     call("h3b_vsa_fp8", _p(q8), _p(k8), _p(v8), _p(q2k_idx), _p(q2k_num), _p(vbs), _p(q_scale_blk), _p(k_scale_blk),
          _p(v_scale_blk), _p(v_scale_head), float(qk_coef), _p(out), _p(lse), heads, n, n_ext, rows_pad, _stream(q8))
     return out
@@ -420,8 +434,9 @@ def vsa_fp8_ex(q, k, v, out, idx, num, vbs_q, vbs_kv, vs, vs_head, qk_coef, head
     x.rows_chunk_q, x.rows_chunk_kv = int(rows_chunk_q), int(rows_chunk_kv)
     x.chunks_q, x.chunks_kv = int(chunks_q), int(chunks_kv)
     x.qk_int8 = int(bool(qk_int8))
+    v16 = "_v16" if v.dtype == torch.float16 else ""  # f16 V (decoded E4M3 values) or E4M3 codes
     if _u_mem is not None:
-        call("h3b_vsa_pair", ctypes.byref(x), _p(_u_mem), _stream(q))
+        call("h3b_vsa_pair" + v16, ctypes.byref(x), _p(_u_mem), _stream(q))
     else:
-        call("h3b_vsa_fp8_ex", ctypes.byref(x), _stream(q))
+        call("h3b_vsa_fp8_ex" + v16, ctypes.byref(x), _stream(q))
     return out

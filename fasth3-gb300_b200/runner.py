@@ -213,12 +213,17 @@ def _fused_rows(lins: list[QuantLinear]) -> dict:
 class H3FastRunner:
     """All blocks of a DiTModel on the h3b kernels. ``sp``: a SeqParallel (one rank per process; NCCL on GPUs), a
     VirtualSeqParallel (all ranks in this process), or None (this GPU alone, even inside an initialized process
-    group). ``qk_int8``: the self-attention's Q and K as
-    per-tile int8 with the QK^T on the tensor cores' integer path (exact scores; E4M3 otherwise)."""
+    group). ``qk_int8``: the self-attention's Q and K as per-tile int8 with the QK^T on the tensor cores' integer path
+    (exact scores; E4M3 otherwise). ``v_f16``: V tiles as f16 (see below)."""
 
-    def __init__(self, model: DiTModel, sp: SeqParallel | VirtualSeqParallel | None = None, qk_int8: bool = False):
+    def __init__(self, model: DiTModel, sp: SeqParallel | VirtualSeqParallel | None = None, qk_int8: bool = False,
+                 v_f16: bool = False):
         self.model = model
         self.qk_int8 = bool(qk_int8)
+        # V tiles as E4M3 codes converted by the attention kernel on every use (default: half the bytes in the
+        # prologue's writes and the sequence-parallel exchange), or as f16 holding the E4M3 values (decoded once by
+        # the prologue, loaded by the PV MMAs as is); the results are bit-identical and the attention time equal
+        self.v_dtype = torch.float16 if v_f16 else torch.uint8
         self.blocks = list(model.transformer_blocks)
         cfg = model.config
         self.cfg = cfg
@@ -330,8 +335,9 @@ class H3FastRunner:
             b["hs"] = torch.empty(R, device=dev, dtype=f32)
             b["qkv"] = torch.empty(R, 3 * C, device=dev, dtype=bf)
             for nm in ("qb", "kb", "vb"):
-                b[nm] = torch.zeros(H, rows_pad, D, device=dev, dtype=u8)
-                b[nm + "_x"] = torch.zeros(P, Hl, rows_pad, D, device=dev, dtype=u8) if P > 1 else \
+                dt = self.v_dtype if nm == "vb" else u8
+                b[nm] = torch.zeros(H, rows_pad, D, device=dev, dtype=dt)
+                b[nm + "_x"] = torch.zeros(P, Hl, rows_pad, D, device=dev, dtype=dt) if P > 1 else \
                     b[nm].view(1, H, rows_pad, D)
             # per (head, tile) E4M3 scales and tile means, local tiles; their exchange buffers; all tiles
             for nm, tail in (("qs", ()), ("ks", ()), ("vs", ()), ("qp", (D,)), ("kp", (D,))):
@@ -406,7 +412,7 @@ class H3FastRunner:
         row0 = torch.arange(n_txt, device=dev, dtype=torch.int32) * TILE
         vbs = torch.full((n_txt,), TILE, device=dev, dtype=torch.int32)
         kb = torch.zeros(len(self.blocks), H, L, D, device=dev, dtype=torch.uint8)
-        vb = torch.zeros_like(kb)
+        vb = torch.zeros(len(self.blocks), H, L, D, device=dev, dtype=self.v_dtype)
         ks = torch.zeros(len(self.blocks), H, n_txt, device=dev, dtype=torch.float32)
         vs = torch.zeros_like(ks)
         vs_head = torch.zeros(len(self.blocks), H, device=dev, dtype=torch.float32)

@@ -201,6 +201,18 @@ int h3b_qkv_prologue8_qk_int8(const void* q, const void* k, const void* v, int64
                               float* ks_blk, float* vs_blk, float* vs_head, float* qp, float* kp, float* vp, int heads,
                               int64_t rows_pad, int n_tiles, int n_ext, float eps, cudaStream_t stream);
 
+/* The per-tile form the block runner uses (no reference counterpart; the tile and scale math are qkv_prologue8's):
+ * per-(head, tile) scales for Q, K and V; flags H3B_PRO_QK_INT8 writes Q and K as int8 (as
+ * h3b_qkv_prologue8_qk_int8), H3B_PRO_V_F16 writes V as f16 [heads, rows_pad, 128] -- the decoded E4M3 values, so
+ * the attention kernel's PV operand is loaded as is (h3b_vsa_fp8_ex_v16) instead of converted on every use. */
+#define H3B_PRO_QK_INT8 1
+#define H3B_PRO_V_F16 2
+int h3b_qkv_prologue8_tiles(const void* q, const void* k, const void* v, int64_t ld, const float* s1,
+                            const int32_t* tile_row0, const int32_t* vbs, const void* wq, const void* wk,
+                            const void* cosb, const void* sinb, void* qb, void* kb, void* vb, float* qs_blk,
+                            float* ks_blk, float* vs_blk, float* vs_head, float* qp, float* kp, float* vp, int heads,
+                            int64_t rows_pad, int n_tiles, int n_ext, float eps, int flags, cudaStream_t stream);
+
 /* BASELINE config 4's prologue (no reference counterpart for its layout; the tile and scale math are qkv_prologue8's):
  * q/k/v bf16 [heads, seqlen, 128] in token order; perm [rows] maps tile-ordered rows to tokens (NULL = identity);
  * per-tile E4M3 scales for Q, K and V (max(amax/448, 1e-30)); vs_head [heads] (caller zeroes) takes the per-head
@@ -209,6 +221,11 @@ int h3b_vsa_tile_quant(const void* q, const void* k, const void* v, int heads, i
                        const int32_t* tile_row0, const int32_t* vbs, void* qb, void* kb, void* vb, float* qs_blk,
                        float* ks_blk, float* vs_blk, float* vs_head, float* qp, float* kp, float* vp, int64_t rows_pad,
                        int n_tiles, int n_ext, cudaStream_t stream);
+/* h3b_vsa_tile_quant with V written as f16 [heads, rows_pad, 128] (the decoded E4M3 values) for h3b_vsa_fp8_ex_v16. */
+int h3b_vsa_tile_quant_v16(const void* q, const void* k, const void* v, int heads, int64_t seqlen,
+                           const int32_t* perm, const int32_t* tile_row0, const int32_t* vbs, void* qb, void* kb,
+                           void* vh, float* qs_blk, float* ks_blk, float* vs_blk, float* vs_head, float* qp, float* kp,
+                           float* vp, int64_t rows_pad, int n_tiles, int n_ext, cudaStream_t stream);
 
 /* One tensor of h3b_qkv_prologue8's per-tile E4M3 form (no reference counterpart; the cross-attention queries, text
  * keys and text values of the DiT block): x bf16 rows [rows, heads*128] with row stride ld in tile order; optional
@@ -218,6 +235,11 @@ int h3b_vsa_tile_quant(const void* q, const void* k, const void* v, int heads, i
 int h3b_head_tile_quant(const void* x, int64_t ld, const float* s1, const int32_t* tile_row0, const int32_t* vbs,
                         const void* w, void* xb, float* xs_blk, float* xs_head, int heads, int64_t rows_pad,
                         int n_tiles, int n_ext, float eps, cudaStream_t stream);
+/* h3b_head_tile_quant writing f16 [heads, rows_pad, 128] (the decoded E4M3 values): text values for the f16-V
+ * attention. */
+int h3b_head_tile_quant_v16(const void* x, int64_t ld, const float* s1, const int32_t* tile_row0, const int32_t* vbs,
+                            const void* w, void* xh, float* xs_blk, float* xs_head, int heads, int64_t rows_pad,
+                            int n_tiles, int n_ext, float eps, cudaStream_t stream);
 
 /* FP8 block-sparse VSA attention, fine step (replaces vsa_fp8_op, fastvideo/models/dits/h3fast/h3attn8.cu:1-42 and
  * vsa_fp8.cuh:782-871). qb/kb/vb e4m3 [heads, rows_pad, 128] (rows_pad = n_ext*64, tile order);
@@ -265,6 +287,9 @@ typedef struct h3b_vsa_args {
                             S = Q K^T runs as tcgen05 kind::i8 with s32 accumulation (exact), else E4M3 */
 } h3b_vsa_args;
 int h3b_vsa_fp8_ex(const h3b_vsa_args* args, cudaStream_t stream);
+/* h3b_vsa_fp8_ex with V given as f16 [planes, rows, 128] holding the E4M3 values (h3b_qkv_prologue8_tiles with
+ * H3B_PRO_V_F16): the PV MMAs read the V tiles as the TMA lands them, with no per-use conversion. */
+int h3b_vsa_fp8_ex_v16(const h3b_vsa_args* args, cudaStream_t stream);
 /* Replaces vsa_pair_op (fastvideo/models/dits/h3fast/h3attn8.cu:44-77; kernel vsa_pair.cuh:140-770): the same
  * attention driven by topk_pairs' output (h3b_topk_pairs) -- per (head, pair of adjacent 64-token query tiles) the
  * ascending union of both tiles' selections in args->idx [heads * n_q_ext/2, idx_ld] with its length in args->num
@@ -273,6 +298,8 @@ int h3b_vsa_fp8_ex(const h3b_vsa_args* args, cudaStream_t stream);
  * tile is run as a pair whose 128-key blocks appear as two 64-key blocks selected by both halves (byte 3). The other
  * fields as h3b_vsa_fp8_ex; each tile's list holds at most 1024 key tiles (H3B_EINVAL in the status word beyond). */
 int h3b_vsa_pair(const h3b_vsa_args* args, const uint8_t* u_mem, cudaStream_t stream);
+/* h3b_vsa_pair with f16 V (as h3b_vsa_fp8_ex_v16). */
+int h3b_vsa_pair_v16(const h3b_vsa_args* args, const uint8_t* u_mem, cudaStream_t stream);
 /* Status word of the attention kernel's bounded waits (0 = none); reset != 0 clears it. Synchronizes the device. */
 int h3b_vsa_status(int* status, int reset);
 

@@ -197,7 +197,8 @@ def test_vsa_attention_timing_config4(ops):
     perm = grid.permute(0, 2, 4, 1, 3, 5).reshape(-1).to(torch.int32)
     vbs = torch.full((n,), 64, device=DEV, dtype=torch.int32)
     row0 = (torch.arange(n, device=DEV) * 64).to(torch.int32)
-    qb, kb, vb = (torch.empty(H, S, D, device=DEV, dtype=torch.uint8) for _ in range(3))
+    qb, kb = (torch.empty(H, S, D, device=DEV, dtype=torch.uint8) for _ in range(2))
+    vb = torch.empty(H, S, D, device=DEV, dtype=torch.float16)  # this library's f16-V form
     qs, ks, vs = (torch.empty(H, n, device=DEV) for _ in range(3))
     vs_head = torch.zeros(H, device=DEV)
     qp, kp, vp = (torch.empty(H, n, D, device=DEV) for _ in range(3))

@@ -196,6 +196,21 @@ def test_dense_prefix_pass_merged_by_lse_equals_one_pass(pkg, prefix):
     assert rel(out2.float(), out1.float()) < 0.1
 
 
+def test_f16_v_runner_equals_e4m3_v_runner(pkg):
+    """The runner with V tiles as f16 (decoded once by the prologue) and with E4M3 V tiles (converted by the attention
+    kernel): the same values reach the tensor cores, so the block loop's output is identical bit for bit, sharded
+    too."""
+    _, runner = pkg
+    m, x, ctx, temb, meta = make(pkg, blocks=2, grid=(7, 16, 16))
+    a = runner.H3FastRunner(m, v_f16=True).forward(x, temb, None, None, meta, context=ctx)
+    b = runner.H3FastRunner(m, v_f16=False).forward(x, temb, None, None, meta, context=ctx)
+    c = runner.H3FastRunner(m, runner.VirtualSeqParallel(2), v_f16=True).forward(x, temb, None, None, meta,
+                                                                                  context=ctx)
+    torch.cuda.synchronize()
+    assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+    assert torch.equal(a.view(torch.int16), c.view(torch.int16))
+
+
 def test_forward_raises_on_an_overlong_selection(pkg):
     """The attention kernel holds at most 1024 selected key tiles per query tile. A longer list is not a fault: the
     kernel clamps it and records H3B_EINVAL in its status word, and forward raises instead of returning the truncated
@@ -385,7 +400,7 @@ def test_stage_prologue_and_selection(traced):
             np.testing.assert_allclose(got_s[:, t], np.maximum(am / 448.0, 1e-30), rtol=1e-2, err_msg=name)
             for h in range(H):
                 w = oq.e4m3_decode(oq.e4m3_encode(rows[:, h] / got_s[h, t]))
-                g = oq.e4m3_decode(got_b[h, t * 64:t * 64 + vbs[t]])
+                g = _values(got_b[h, t * 64:t * 64 + vbs[t]])
                 close = np.abs(g - w) <= np.maximum(np.abs(w), 2 ** -6) * 0.126
                 ok += int(close.sum())
                 total += close.size
@@ -411,10 +426,16 @@ def test_stage_prologue_and_selection(traced):
     np.testing.assert_array_equal(s["vs_head"].cpu().numpy(), s["vs_all"].cpu().numpy().max(axis=1))
 
 
+def _values(t) -> np.ndarray:
+    """E4M3 codes (uint8) or the f16 tensors holding their values (the f16-V path) -> float32 values."""
+    t = t.cpu() if isinstance(t, torch.Tensor) else torch.from_numpy(t)
+    return t.float().numpy() if t.dtype == torch.float16 else oq.e4m3_decode(t.numpy())
+
+
 def _deq_tiles(codes: torch.Tensor, scales: torch.Tensor) -> np.ndarray:
-    """E4M3 [H, n*64, 128] with per-(head, tile) scales [H, n] -> float32."""
+    """E4M3 [H, n*64, 128] (codes, or f16 values) with per-(head, tile) scales [H, n] -> float32."""
     H, rows_pad, D = codes.shape
-    v = oq.e4m3_decode(codes.cpu().numpy()).reshape(H, rows_pad // 64, 64, D)
+    v = _values(codes).reshape(H, rows_pad // 64, 64, D)
     return (v * scales.cpu().numpy()[:, :, None, None]).reshape(H, rows_pad, D)
 
 

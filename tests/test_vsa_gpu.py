@@ -625,3 +625,52 @@ def test_vsa_pair_runs_128_token_tiles(ops):
     ref = ov.vsa_fine(deq(o["qb"], o["qs"]), deq(o["kb"], o["ks"]), deq(o["vb"], o["vs"]), per_tile.numpy()[0],
                       num.numpy()[0], o["vbs"].cpu().numpy(), 1.0 / math.sqrt(128))
     assert _rel(out2.cpu().float().numpy()[0], ref) < 1e-2
+
+
+# ------------------------------------------------------------------------------------------------ f16 V
+def test_f16_v_path_is_bit_identical(ops):
+    """V written once as f16 by the tile quantizer (the decoded E4M3 values) and loaded by the attention's PV MMAs
+    as is, against E4M3 V converted inside the kernel: the same operands reach the tensor cores, so the outputs, the
+    LSE and the per-tile scales are identical bit for bit; the pair form too."""
+    heads, T, Hh, Ww, k = 3, 8, 16, 16, 6
+    g = torch.Generator().manual_seed(71)
+    S = T * Hh * Ww
+    n = S // 64
+    perm = tile_permutation(T, Hh, Ww).to(DEV)
+    vbs = torch.full((n,), 64, dtype=torch.int32, device=DEV)
+    vbs[-1] = 40  # a partial last tile (masked keys)
+    S_eff = int(vbs.sum())
+    perm = perm[:S_eff]
+    row0 = (vbs.cumsum(0) - vbs).to(torch.int32)
+    q, kk, v = (torch.randn(heads, S, 128, generator=g).bfloat16().to(DEV) for _ in range(3))
+    outs = {}
+    for vdt in (torch.uint8, torch.float16):
+        qb, kb = (torch.zeros(heads, n * 64, 128, device=DEV, dtype=torch.uint8) for _ in range(2))
+        vb = torch.zeros(heads, n * 64, 128, device=DEV, dtype=vdt)
+        qs, ks, vs = (torch.ones(heads, n, device=DEV) for _ in range(3))
+        vs_head = torch.zeros(heads, device=DEV)
+        qp, kp, vp = (torch.zeros(heads, n, 128, device=DEV) for _ in range(3))
+        ops.vsa_tile_quant(q, kk, v, perm, row0, vbs, qb, kb, vb, qs, ks, vs, qp, kp, vp, n, vs_head=vs_head)
+        sc = torch.empty(heads, n, n, device=DEV)
+        ops.tile_scores(qp, kp, sc, 1.0 / math.sqrt(128))
+        idx = torch.full((1, heads, n, n), -1, device=DEV, dtype=torch.int32)
+        num = torch.zeros(1, heads, n, device=DEV, dtype=torch.int32)
+        ops.topk_rows(sc, n, n, 0, [0], [n], [k], idx, num, False)
+        coef = math.log2(math.e) / math.sqrt(128)
+        lse = torch.zeros(heads, n * 64, device=DEV)
+        out = ops.vsa_fp8(qb, kb, vb, idx, num, vbs, coef, vs, vs_head, lse=lse, q_scale_blk=qs, k_scale_blk=ks)
+        P = heads * n // 2
+        u_idx = torch.full((P, n), -1, device=DEV, dtype=torch.int32)
+        u_mem = torch.zeros(P, n, device=DEV, dtype=torch.uint8)
+        u_num = torch.zeros(P, device=DEV, dtype=torch.int32)
+        ops.topk_pairs(sc, n, n, 0, [0], [n], [k], u_idx, u_mem, u_num)
+        outp = ops.vsa_pair(qb, kb, vb, u_idx, u_mem, u_num, vbs, coef, vs, vs_head, q_scale_blk=qs, k_scale_blk=ks)
+        torch.cuda.synchronize()
+        assert ops.vsa_status(reset=True) == 0
+        outs[vdt] = (vb, vs, out, lse, outp)
+    (v8, vs8, o8, l8, p8), (v16, vs16, o16, l16, p16) = outs[torch.uint8], outs[torch.float16]
+    assert torch.equal(vs8, vs16)
+    assert torch.equal(v16.cpu().float(), torch.from_numpy(oq.e4m3_decode(v8.cpu().numpy())))
+    assert torch.equal(o8.view(torch.int16), o16.view(torch.int16))
+    assert torch.equal(l8, l16)
+    assert torch.equal(p8.view(torch.int16), p16.view(torch.int16))
