@@ -500,6 +500,103 @@ def dit_step_secondary(pkg, dev, stream, args, ws) -> dict:
     return res
 
 
+def memory_kernels_secondary(pkg, dev, args) -> dict:
+    """The memory-bound kernels of the path, each at its BASELINE size (``--mem-rows`` overrides the row counts): the
+    per-tensor NVFP4 quantizer of config 2 (amax pass and quantize pass), the LayerNorm + modulate + NVFP4 quantizer and
+    the q/k/v prologue of the config-5 block (124,992 rows), the per-row NVFP4 quantizer of the FFN intermediate
+    (13824 wide), the attention-output gate quantizer and the tile selection (top-32 of 2016). Median of ``reps``
+    launches (CUDA events) after warm-ups; GB/s are algorithmic bytes (inputs read once, outputs written once) over
+    the launch time, and ``frac`` divides them by the measured HBM copy bandwidth."""
+    import torch
+    ops = pkg.ops
+    reps, warm = (1, 0) if args.mem_once else (10, 3)
+    hbm = _peaks()["hbm"]
+    g = torch.Generator(device=dev).manual_seed(31)
+
+    def tm(fn):
+        for _ in range(warm):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return sorted(ts)[len(ts) // 2]
+
+    out = {}
+
+    def rec(name, ms, nbytes, note):
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"ms": ms, "alg_bytes": nbytes, "gbs": gbs, "frac": gbs / hbm, "what": note}
+
+    M2, K = (args.mem_rows or 32768), 5120
+    x = torch.randn(M2, K, device=dev, generator=g).bfloat16()
+    q = torch.empty(M2, K // 2, device=dev, dtype=torch.uint8)
+    sf = torch.empty(ops.sf_rows(M2), K // 16, device=dev, dtype=torch.uint8)
+    s, am = torch.empty(1, device=dev), torch.zeros(1, device=dev)
+    rec("amax_c2", tm(lambda: ops.amax(x, am)), M2 * K * 2, f"amax pass over X [{M2} x {K}] bf16")
+    rec("quant_nvfp4_tensor_c2", tm(lambda: ops.quant_nvfp4_tensor(x, am, q, sf, s)),
+        M2 * K * 2 + M2 * (K // 2 + K // 16), "quantize pass: read X, write codes + block scales")
+    del x, q, sf
+    R = args.mem_rows or 124992
+    xl = torch.randn(R, K, device=dev, generator=g).bfloat16()
+    tabs = (torch.randn(2, K, device=dev, generator=g) * 0.1).bfloat16()
+    h = torch.empty(R, K // 2, device=dev, dtype=torch.uint8)
+    hsf = torch.zeros(ops.sf_rows(R), K // 16, device=dev, dtype=torch.uint8)
+    hs = torch.empty(R, device=dev)
+    rec("layer_norm_quant_c5", tm(lambda: ops.resid_norm_quant(xl, None, None, None, None, None, tabs[0:1], tabs[1:2],
+                                                                 xl, h, hsf, hs, 1e-6, norm="layer")),
+        R * K * 2 + R * (K // 2 + K // 16 + 4), f"LayerNorm + modulate + NVFP4, {R} x {K}")
+    del xl, h, hsf, hs
+    F = 13824
+    Rf = min(R, 32768)
+    u = torch.randn(Rf, F, device=dev, generator=g).bfloat16()
+    f = torch.empty(Rf, F // 2, device=dev, dtype=torch.uint8)
+    fsf = torch.zeros(ops.sf_rows(Rf), F // 16, device=dev, dtype=torch.uint8)
+    fs = torch.empty(Rf, device=dev)
+    rec("quant_nvfp4_rows_ffn", tm(lambda: ops.quant_nvfp4_rows(u, f, fsf, fs)), Rf * F * 2 + Rf * (F // 2 + F // 16 + 4),
+        f"per-row NVFP4 of the FFN intermediate, {Rf} x {F}")
+    del u, f, fsf
+    H, n = 40, (R // 64) - (R // 64) % 2
+    rows = n * 64
+    qkv = torch.randn(rows, 3 * K, device=dev, generator=g).bfloat16()
+    s1 = torch.rand(rows, device=dev, generator=g) + 0.5
+    wq, wk = (torch.randn(128, device=dev, generator=g).bfloat16() for _ in range(2))
+    ang = torch.rand(rows, 48, device=dev, generator=g) * 6.28
+    cos, sin = torch.cat([ang.cos()] * 2, -1).bfloat16(), torch.cat([ang.sin()] * 2, -1).bfloat16()
+    vbs = torch.full((n,), 64, device=dev, dtype=torch.int32)
+    row0 = torch.arange(n, device=dev, dtype=torch.int32) * 64
+    qb, kb, vb = (torch.zeros(H, rows, 128, device=dev, dtype=torch.uint8) for _ in range(3))
+    qs, ks, vs = (torch.ones(H, n, device=dev) for _ in range(3))
+    qp, kp, vp = (torch.zeros(H, n, 128, device=dev) for _ in range(3))
+    rec("qkv_prologue_c5", tm(lambda: ops.qkv_prologue8(qkv[:, :K], qkv[:, K:2 * K], qkv[:, 2 * K:], s1, row0, vbs, wq, wk,
+                                                        cos, sin, 1.0, 1.0, qb, kb, vb, vs, None, qp, kp, vp, H, n, 64,
+                                                        1e-6, qs_blk=qs, ks_blk=ks)),
+        3 * rows * K * 2 + 3 * rows * K + 3 * H * n * 128 * 4, f"q/k/v prologue, {H} heads x {rows} rows")
+    ob = torch.randn(H, rows, 128, device=dev, generator=g).bfloat16()
+    slot = torch.arange(rows, device=dev, dtype=torch.int32)
+    a = torch.empty(rows, K // 2, device=dev, dtype=torch.uint8)
+    asf = torch.zeros(ops.sf_rows(rows), K // 16, device=dev, dtype=torch.uint8)
+    sa = torch.empty(rows, device=dev)
+    rec("attn_gate_quant_c5", tm(lambda: ops.attn_gate_quant(ob, None, None, None, slot, n, 64, a, asf, sa, rows)),
+        rows * K * 2 + rows * (K // 2 + K // 16 + 4), f"attention output gather + NVFP4, {rows} rows")
+    del qkv, qb, kb, vb, ob, a, asf
+    nt = 2016 if not args.mem_rows else max(64, min(2016, (args.mem_rows // 64) // 2 * 2))
+    sc = torch.randn(H, nt, nt, device=dev, generator=g)
+    idx = torch.empty(1, H, nt, nt, device=dev, dtype=torch.int32)
+    num = torch.zeros(1, H, nt, device=dev, dtype=torch.int32)
+    rec("topk_select_c5", tm(lambda: ops.topk_rows(sc, nt, nt, 0, [0], [nt], [32], idx, num, False)),
+        H * nt * nt * 4 + H * nt * 32 * 4, f"top-32 of {nt} tiles, {H} heads")
+    del sc, idx
+    torch.cuda.empty_cache()
+    out["hbm_peak_gbs"] = hbm
+    return out
+
+
 def run_only(args) -> None:
     """One secondary measurement alone (for profiling captures): prints its JSON object."""
     import torch
@@ -517,7 +614,8 @@ def run_only(args) -> None:
     fn = {"fp8": lambda: fp8_linear_secondary(pkg.ops, dev, stream, args),
           "chain": lambda: fp8_chain_secondary(pkg, dev, stream, args),
           "vsa": lambda: vsa_config4_secondary(pkg.ops, dev, stream, args),
-          "dit": lambda: dit_step_secondary(pkg, dev, stream, args, ws)}[args.only]
+          "dit": lambda: dit_step_secondary(pkg, dev, stream, args, ws),
+          "mem": lambda: memory_kernels_secondary(pkg, dev, args)}[args.only]
     res = fn()
     if rank == 0:
         print(json.dumps({"only": args.only, "n_gpus": ws, "result": res}), flush=True)
@@ -702,6 +800,7 @@ def run_ours(args) -> None:
     del x, y, qa, sfa
     torch.cuda.empty_cache()
     sp_check = sp_bitexact_check(pkg, dev, ws) if ws > 1 else None
+    mem = memory_kernels_secondary(pkg, dev, args) if ws == 1 and not args.no_mem else None
     dit = dit_step_secondary(pkg, dev, stream, args, ws) if not args.no_dit else None
 
     if ws > 1:
@@ -755,6 +854,8 @@ def run_ours(args) -> None:
             line["fp8_block_chain_config3"] = chain
         if sp_check is not None:
             line["sp_check"] = sp_check
+        if mem is not None:
+            line["memory_kernels"] = mem
         if dit is not None:
             line["dit_step_config5"] = dit
         if cpu is not None:
@@ -783,7 +884,12 @@ def main() -> None:
     ap.add_argument("--no-fp8", action="store_true", help="skip the secondary FP8 linear measurement")
     ap.add_argument("--no-vsa", action="store_true", help="skip the secondary VSA (config 4) measurement")
     ap.add_argument("--no-dit", action="store_true", help="skip the secondary 50-block DiT step (config 5)")
-    ap.add_argument("--only", choices=["fp8", "chain", "vsa", "dit"], default=None,
+    ap.add_argument("--no-mem", action="store_true", help="skip the memory-bound kernel measurements")
+    ap.add_argument("--mem-rows", type=int, default=0,
+                    help="row count of the memory-kernel measurements (0: BASELINE sizes; smaller for ncu captures)")
+    ap.add_argument("--mem-once", action="store_true",
+                    help="memory kernels: one launch each, no warm-up (so an ncu capture sees each kernel once)")
+    ap.add_argument("--only", choices=["fp8", "chain", "vsa", "dit", "mem"], default=None,
                     help="run one secondary measurement alone (profiling captures); no headline line")
     ap.add_argument("--vsa-heads", type=int, default=40, help="heads of the config-4 VSA measurement (40)")
     ap.add_argument("--dit-blocks", type=int, default=50, help="blocks of the config-5 step (50)")
