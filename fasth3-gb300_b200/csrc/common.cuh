@@ -176,6 +176,41 @@ __device__ __forceinline__ float nvfp4_block_scale(float vmax, float gs, uint32_
   return (vmax != 0.f && sf != 0.f) ? gs / sf : 0.f;
 }
 
+// Paired fp32 arithmetic (sm_100 f32x2): two independent operations in one instruction, each rounded to nearest and
+// flushed to zero like the scalar instructions of the fast-math build, so the results equal two scalar operations.
+__device__ __forceinline__ void add2(float& a0, float& a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 a, b;\n\tmov.b64 a, {%0, %1};\n\tmov.b64 b, {%2, %3};\n\t"
+      "add.rn.ftz.f32x2 a, a, b;\n\tmov.b64 {%0, %1}, a;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ void sub2(float& a0, float& a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 a, b;\n\tmov.b64 a, {%0, %1};\n\tmov.b64 b, {%2, %3};\n\t"
+      "sub.rn.ftz.f32x2 a, a, b;\n\tmov.b64 {%0, %1}, a;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ void mul2(float& a0, float& a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 a, b;\n\tmov.b64 a, {%0, %1};\n\tmov.b64 b, {%2, %3};\n\t"
+      "mul.rn.ftz.f32x2 a, a, b;\n\tmov.b64 {%0, %1}, a;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(b0), "f"(b1));
+}
+// a = a * b + c
+__device__ __forceinline__ void fma2(float& a0, float& a1, float b0, float b1, float c0, float c1) {
+  asm("{\n\t.reg .b64 a, b, c;\n\tmov.b64 a, {%0, %1};\n\tmov.b64 b, {%2, %3};\n\tmov.b64 c, {%4, %5};\n\t"
+      "fma.rn.ftz.f32x2 a, a, b, c;\n\tmov.b64 {%0, %1}, a;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+// acc += d * d for a pair
+__device__ __forceinline__ void sq_acc2(float& acc0, float& acc1, float d0, float d1) {
+  asm("{\n\t.reg .b64 a, d;\n\tmov.b64 a, {%0, %1};\n\tmov.b64 d, {%2, %3};\n\t"
+      "fma.rn.ftz.f32x2 a, d, d, a;\n\tmov.b64 {%0, %1}, a;\n\t}"
+      : "+f"(acc0), "+f"(acc1)
+      : "f"(d0), "f"(d1));
+}
+
 // Butterfly reductions. Every lane ends with the same value: at each stage lanes l and l^o add the same two operands.
 template <bool MAX>
 __device__ __forceinline__ float warp_allreduce(float v) {

@@ -145,84 +145,129 @@ __device__ __forceinline__ void store_rows(const Problem& p, const Epi& e, float
 // box's mbarrier while the accumulator is read and scaled), so the residual is read with full-sector loads and updated
 // in place. One box per warp: before it is refilled, the store that last read it has finished reading. `lphase` holds
 // the parity of the box's load barrier.
+// Per-chunk pieces of the epilogue. epi_issue_residual: with a gated residual, lane 0 puts the chunk's 32 x 32
+// residual block in flight into the box (which the previous store has finished reading). epi_finish: scale, bias,
+// activation and residual of the chunk's 32 raw accumulator words, bf16 into the box, one tensor store. Returns false
+// when the residual block never arrived.
+__device__ __forceinline__ void epi_issue_residual(const Epi& e, const CUtensorMap* tmR, uint8_t* box,
+                                                   uint64_t* box_bar, int n0, int m0) {
+  const int lane = threadIdx.x & 31;
+  if (e.residual && lane == 0) {
+    bulk_wait_read<0>();
+    mbar_arrive_expect_tx(box_bar, 2048);
+    tma_load_2d(box, tmR, n0, m0, box_bar);
+  }
+  __syncwarp();  // tcgen05.ld after this is warp-collective: reconverge after the lane-0 branch
+}
+
+__device__ __forceinline__ bool epi_finish(const Problem& p, const Epi& e, const CUtensorMap* tmD, float rs,
+                                           const uint32_t (&r)[32], int n0, int m0, uint8_t* box, uint64_t* box_bar,
+                                           uint32_t& lphase, volatile int* abort_flag) {
+  const int lane = threadIdx.x & 31;
+  const bool res = e.residual != nullptr;
+  const int sw = (lane >> 1) & 3;
+  uint8_t* row = box + lane * 64;
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const int n = min(n0 + i, p.N - 1);
+    float x = __uint_as_float(r[i]) * rs;
+    if (e.col_scale) x *= e.col_scale[e.col_scalar ? 0 : n];
+    if (e.bias) x += __bfloat162float(e.bias[n]);
+    if (e.act == H3B_ACT_GELU_TANH) x = gelu_tanh(x);
+    v[i] = x;
+  }
+  if (res) {
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(box_bar, lphase & 1u, abort_flag, kWaitLimitNs))) return false;
+    lphase ^= 1u;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 w = *reinterpret_cast<const uint4*>(row + ((j ^ sw) << 4));
+      float rv[8], g[8];
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float2 t = __bfloat1622float2(h[u]);
+        rv[2 * u] = t.x;
+        rv[2 * u + 1] = t.y;
+      }
+      load8(e.gate + min(n0 + 8 * j, p.N - 8), g);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[8 * j + u] = rv[u] + g[u] * v[8 * j + u];
+    }
+  } else {
+    // without a residual the box is first needed here: the previous store's read overlapped the accumulator read
+    if (lane == 0) bulk_wait_read<0>();
+    __syncwarp();
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 w;
+    w.x = pack_bf16x2(v[8 * j], v[8 * j + 1]);
+    w.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+    w.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+    w.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+    *reinterpret_cast<uint4*>(row + ((j ^ sw) << 4)) = w;
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(tmD, n0, m0, box);
+    bulk_commit_group();
+  }
+  return true;
+}
+
+__device__ __forceinline__ float epi_row_scale(const Problem& p, const Epi& e, float alpha, int m0) {
+  const int m = m0 + (threadIdx.x & 31);
+  return alpha * ((e.row_scale && m < p.M) ? e.row_scale[m] : 1.f);
+}
+
+// Epilogue of one warp's 32 accumulator rows (TMEM lanes 32q .. 32q+31), chunks c_begin .. c_end-1 of 32 columns,
+// through shared memory and TMA: per chunk each lane turns its row into bf16 inside a 32 x 64-byte staging box
+// (64-byte swizzle, so the 16-byte accesses of a quarter-warp hit distinct banks) and lane 0 writes the box with one
+// tensor store (full sectors; rows >= M and columns >= N are clipped by the tensor map). With a gated residual the box
+// is first filled with the residual's 32 x 32 block by a TMA load issued at the start of the chunk (completing on the
+// box's mbarrier while the accumulator is read and scaled), so the residual is read with full-sector loads and updated
+// in place. One box per warp: before it is refilled, the store that last read it has finished reading. `lphase` holds
+// the parity of the box's load barrier.
 template <int BN>
 __device__ __forceinline__ void store_rows_tma(const Problem& p, const Epi& e, const CUtensorMap* tmD,
                                                const CUtensorMap* tmR, float alpha, uint32_t tbase, int m0, int nb,
                                                int c_begin, int c_end, uint8_t* box, uint64_t* box_bar,
                                                uint32_t& lphase, volatile int* abort_flag, bool& ok) {
-  const int lane = threadIdx.x & 31;
-  const int m = m0 + lane;
-  const bool row_ok = m < p.M;
-  const float rs = alpha * ((e.row_scale && row_ok) ? e.row_scale[m] : 1.f);
-  const bool res = e.residual != nullptr;
-  const int sw = (lane >> 1) & 3;
-  uint8_t* row = box + lane * 64;
+  const float rs = epi_row_scale(p, e, alpha, m0);
 #pragma unroll 1
   for (int c = c_begin; c < c_end; ++c) {
     const int n0 = nb * BN + 32 * c;
     if (m0 >= p.M || n0 >= p.N) break;  // warp-uniform: this and later chunks lie outside the output
-    if (res && lane == 0) {
-      // the residual block goes in flight at once (it lands while the accumulator is read and scaled), into a box
-      // the previous store has finished reading
-      bulk_wait_read<0>();
-      mbar_arrive_expect_tx(box_bar, 2048);
-      tma_load_2d(box, tmR, n0, m0, box_bar);
-    }
-    __syncwarp();  // tcgen05.ld below is warp-collective: reconverge after the lane-0 branch
+    epi_issue_residual(e, tmR, box, box_bar, n0, m0);
     uint32_t r[32];
     tmem_ld_32cols(tbase + 32 * c, r);
     tmem_ld_wait();
-    float v[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const int n = min(n0 + i, p.N - 1);
-      float x = __uint_as_float(r[i]) * rs;
-      if (e.col_scale) x *= e.col_scale[e.col_scalar ? 0 : n];
-      if (e.bias) x += __bfloat162float(e.bias[n]);
-      if (e.act == H3B_ACT_GELU_TANH) x = gelu_tanh(x);
-      v[i] = x;
+    if (!epi_finish(p, e, tmD, rs, r, n0, m0, box, box_bar, lphase, abort_flag)) {
+      ok = false;
+      return;
     }
-    if (res) {
-      if (!__all_sync(0xffffffffu, mbar_wait_bounded(box_bar, lphase & 1u, abort_flag, kWaitLimitNs))) {
-        ok = false;
-        return;
-      }
-      lphase ^= 1u;
+  }
+}
+
+// As store_rows_tma for NC chunks whose accumulator words the caller has already read into registers (so it could
+// release the TMEM accumulator before the stores).
+template <int BN, int NC>
+__device__ __forceinline__ void store_rows_regs(const Problem& p, const Epi& e, const CUtensorMap* tmD,
+                                                const CUtensorMap* tmR, float alpha, const uint32_t (&acc)[NC][32],
+                                                int m0, int nb, int c_begin, uint8_t* box, uint64_t* box_bar,
+                                                uint32_t& lphase, volatile int* abort_flag, bool& ok) {
+  const float rs = epi_row_scale(p, e, alpha, m0);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint4 w = *reinterpret_cast<const uint4*>(row + ((j ^ sw) << 4));
-        float rv[8], g[8];
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float2 t = __bfloat1622float2(h[u]);
-          rv[2 * u] = t.x;
-          rv[2 * u + 1] = t.y;
-        }
-        load8(e.gate + min(n0 + 8 * j, p.N - 8), g);
-#pragma unroll
-        for (int u = 0; u < 8; ++u) v[8 * j + u] = rv[u] + g[u] * v[8 * j + u];
-      }
-    }
-    if (!res) {
-      // without a residual the box is first needed here: the previous store's read overlapped the TMEM load above
-      if (lane == 0) bulk_wait_read<0>();
-      __syncwarp();
-    }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      uint4 w;
-      w.x = pack_bf16x2(v[8 * j], v[8 * j + 1]);
-      w.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
-      w.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
-      w.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
-      *reinterpret_cast<uint4*>(row + ((j ^ sw) << 4)) = w;
-    }
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) {
-      tma_store_2d(tmD, n0, m0, box);
-      bulk_commit_group();
+  for (int cc = 0; cc < NC; ++cc) {
+    const int n0 = nb * BN + 32 * (c_begin + cc);
+    if (m0 >= p.M || n0 >= p.N) break;
+    epi_issue_residual(e, tmR, box, box_bar, n0, m0);
+    if (!epi_finish(p, e, tmD, rs, acc[cc], n0, m0, box, box_bar, lphase, abort_flag)) {
+      ok = false;
+      return;
     }
   }
 }
@@ -421,26 +466,41 @@ __global__ void __launch_bounds__(Cfg8<BN>::kThreads, 1)
 // stage keeps the issuing thread's gaps between MMAs short), and one per accumulator, drained by both epilogues. The
 // odd CTA's producer, scale warps and epilogue reach them through shared::cluster addresses. Each producer issues its
 // scale copies before its A/B copies, so the scale warps' TMEM writes are not queued behind 28 KB of operand tiles.
+#ifndef H3B_PAIR_ACC_BUFS
+#define H3B_PAIR_ACC_BUFS 2
+#endif
+#ifndef H3B_PAIR_KSTAGE
+#define H3B_PAIR_KSTAGE 1
+#endif
 struct PairCfg {
   static constexpr int BN = 192;         // N of one MMA / output tile
   static constexpr int kBRows = BN / 2;  // B rows each CTA loads
-  static constexpr int kStages = 6;
-  static constexpr int kABytes = BM * KB_BYTES;
-  static constexpr int kBBytes = kBRows * KB_BYTES;
-  static constexpr int kSfaBytes = 2048;
-  static constexpr int kSfbBytes = 4096;
+  static constexpr int KS = H3B_PAIR_KSTAGE;  // 256-deep K blocks per stage
+  static constexpr int kStages = KS == 1 ? 6 : 3;
+  static constexpr int kAKb = BM * KB_BYTES;          // one K block of A (128 rows x 128 bytes)
+  static constexpr int kBKb = kBRows * KB_BYTES;      // one K block of this CTA's B rows
+  static constexpr int kABytes = KS * kAKb;
+  static constexpr int kBBytes = KS * kBKb;
+  static constexpr int kSfaBytes = KS * 2048;         // four 512-byte atoms per K block
+  static constexpr int kSfbBytes = KS * 4096;         // the same for two 128-row groups of B
   static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
-  // scale slots in TMEM after the two accumulators: A scales in 16 columns (4 K blocks x 4), then the B scales of
-  // the tile's 192 rows in 24 (4 K blocks x 6, row 32c + r of the tile in column c, lane r)
-  static constexpr int kSfCol = 2 * BN;
-  static constexpr int kSfSlotCols = 40;
-  static constexpr int kSfSlots = 3;
+  // Accumulator buffers and scale slots in TMEM. Two accumulators let a tile's epilogue overlap the next tile's
+  // MMAs, but leave room for three scale slots only, so a stage's scales can be written only once the MMAs of the
+  // stage three back have completed; with one accumulator there is a slot per stage (the scale writes then wait
+  // on the same completions as the producer) and the epilogue reads the accumulator into registers and releases it
+  // before its stores. A scales take 16 columns (4 K blocks x 4), the B scales of the tile's 192 rows 24 (4 K blocks
+  // x 6, row 32c + r of the tile in column c, lane r).
+  static constexpr int kAccBufs = H3B_PAIR_ACC_BUFS;
+  static constexpr int kSfCol = kAccBufs * BN;
+  static constexpr int kSfSlotCols = 40 * KS;
+  static constexpr int kSfSlots = kAccBufs == 1 ? kStages : 3;
+  static_assert(KS == 1 || kAccBufs == 1, "two K blocks per stage leave TMEM for one accumulator only");
   static constexpr int kThreads = 448;
   static constexpr int kTmemCols = 512;
   static constexpr int kEpiWarps = 8;                 // two per TMEM lane quarter, each on half of the columns
   static constexpr int kEpiBytes = kEpiWarps * 2048;  // per epilogue warp one 32 x 64-byte output staging box
   static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + 1024 /*align*/ + 512;
-  static_assert(2 * BN + kSfSlotCols * kSfSlots <= kTmemCols, "TMEM budget");
+  static_assert(kAccBufs * BN + kSfSlotCols * kSfSlots <= kTmemCols, "TMEM budget");
   static_assert(kSfCol % 8 == 0 && kSfSlotCols % 8 == 0, "scale slots are written 8 columns at a time");
   static_assert(kStageBytes % 1024 == 0, "stages must keep 1024-byte alignment");
 };
@@ -505,6 +565,7 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
     atomicExch(&g_gemm_status, H3B_ETIMEOUT);
   };
   const int m_blocks2 = (p.m_blocks + 1) >> 1;
+  const int ksteps = (p.k_blocks + C::KS - 1) / C::KS;  // stages per tile
   Problem pp = p;  // tile raster over 256-row blocks
   pp.m_blocks = m_blocks2;
 
@@ -524,24 +585,29 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
         const uint8_t* sfa_src = p.sfa + (size_t)min(mblk, p.m_blocks - 1) * kstride;
         const int g0 = n0 >> 7;
         const int g1 = min(g0 + 1, p.sfb_groups - 1);
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int ks = 0; ks < ksteps; ++ks) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag, kWaitLimitNs)) {
             fail();
             ok = false;
             break;
           }
+          const int kb0 = ks * C::KS, nk = min(C::KS, p.k_blocks - kb0);
           uint8_t* sA = smem + stage * C::kStageBytes;
           uint8_t* sB = sA + C::kABytes;
           uint8_t* sSFA = sB + C::kBBytes;
           uint8_t* sSFB = sSFA + C::kSfaBytes;
           const uint32_t full0 = in_cta(&full[stage], 0);
-          mbar_arrive_expect_tx(&sf_loaded[stage], C::kSfaBytes + C::kSfbBytes);
-          bulk_load(sSFA, sfa_src + (size_t)kb * 2048, 2048, &sf_loaded[stage]);
-          bulk_load(sSFB, p.sfb + (size_t)g0 * kstride + (size_t)kb * 2048, 2048, &sf_loaded[stage]);
-          bulk_load(sSFB + 2048, p.sfb + (size_t)g1 * kstride + (size_t)kb * 2048, 2048, &sf_loaded[stage]);
-          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (C::kABytes + C::kBBytes));
-          tma_load_2d_pair(sA, &tmA, kb * KB_BYTES, mblk * BM, full0);
-          tma_load_2d_pair(sB, &tmB, kb * KB_BYTES, n0 + (int)rank * C::kBRows, full0);
+          const uint32_t sf_bytes = (uint32_t)nk * 2048;
+          mbar_arrive_expect_tx(&sf_loaded[stage], 3 * sf_bytes);
+          bulk_load(sSFA, sfa_src + (size_t)kb0 * 2048, sf_bytes, &sf_loaded[stage]);
+          bulk_load(sSFB, p.sfb + (size_t)g0 * kstride + (size_t)kb0 * 2048, sf_bytes, &sf_loaded[stage]);
+          bulk_load(sSFB + C::kSfbBytes / 2, p.sfb + (size_t)g1 * kstride + (size_t)kb0 * 2048, sf_bytes,
+                    &sf_loaded[stage]);
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * nk * (C::kAKb + C::kBKb));
+          for (int h = 0; h < nk; ++h) {
+            tma_load_2d_pair(sA + h * C::kAKb, &tmA, (kb0 + h) * KB_BYTES, mblk * BM, full0);
+            tma_load_2d_pair(sB + h * C::kBKb, &tmB, (kb0 + h) * KB_BYTES, n0 + (int)rank * C::kBRows, full0);
+          }
           issued = min(issued + 1, C::kStages);
           if (++stage == C::kStages) {
             stage = 0;
@@ -579,7 +645,7 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
       for (int tile = cluster; tile < p.num_tiles && ok; tile += clusters, ++j) {
         int mb2, nb;
         tile_coords(tile, pp, mb2, nb);
-        const int buf = j & 1;
+        const int buf = j % C::kAccBufs;
         if (!mbar_wait_spin(&acc_empty[buf], (((acc_phase >> buf) & 1u) ^ 1u), abort_flag, kWaitLimitNs)) {
           fail();
           break;
@@ -587,8 +653,9 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
         acc_phase ^= 1u << buf;
         tc_fence_after();
         const uint32_t d = tmem + buf * C::BN;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int ks = 0; ks < ksteps; ++ks) {
           const int slot = (int)(sf_n % C::kSfSlots);
+          const int nk = min(C::KS, p.k_blocks - ks * C::KS);
           if (!mbar_wait_spin(&full[stage], phase, abort_flag, kWaitLimitNs)) {
             fail();
             ok = false;
@@ -596,12 +663,18 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
           }
           tc_fence_after();
           uint8_t* sA = smem + stage * C::kStageBytes;
-          const uint64_t da = desc_k_sw128(smem_addr(sA));
-          const uint64_t db = desc_k_sw128(smem_addr(sA + C::kABytes));
-          const uint32_t sfa = tmem + C::kSfCol + C::kSfSlotCols * slot, sfb = sfa + 16;
+          const uint32_t sfa = tmem + C::kSfCol + C::kSfSlotCols * slot, sfb = sfa + 16 * C::KS;
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            mma_nvf4_pair(d, da + 2 * i, db + 2 * i, idesc, (kb | i) != 0, sfa + 4 * i, sfb + 6 * i);
+          for (int h = 0; h < C::KS; ++h) {
+            if (h < nk) {
+              const uint64_t da = desc_k_sw128(smem_addr(sA + h * C::kAKb));
+              const uint64_t db = desc_k_sw128(smem_addr(sA + C::kABytes + h * C::kBKb));
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                mma_nvf4_pair(d, da + 2 * i, db + 2 * i, idesc, (ks | h | i) != 0, sfa + 4 * (4 * h + i),
+                              sfb + 6 * (4 * h + i));
+            }
+          }
           tc_commit_pair(smem_addr(&empty[stage]));  // one commit per stage: each extra one costs tensor-pipe time
           ++sf_n;
           if (++stage == C::kStages) {
@@ -628,7 +701,7 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
       tile_coords(tile, pp, mb2, nb);
       // the tile's 192 B rows start at word 0 or 2 (rows 0 or 64 of a 128-row group) of the first group's atoms
       const bool mid = ((nb * C::BN) & 127) != 0;
-      for (int kb = 0; kb < p.k_blocks; ++kb) {
+      for (int ks = 0; ks < ksteps; ++ks) {
         const int slot = (int)(sf_n % C::kSfSlots);
         // the stage's atoms are read into registers first, so the slot wait (MMA completion) is followed only by
         // the TMEM stores
@@ -639,12 +712,13 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
         }
         const uint8_t* sSFA = smem + stage * C::kStageBytes + C::kABytes + C::kBBytes;
         const uint8_t* sSFB = sSFA + C::kSfaBytes;
-        uint32_t a[16], b[24];
+        // (a tail stage with fewer K blocks writes its unused columns from stale atoms; no MMA reads them)
+        uint32_t a[16 * C::KS], b[24 * C::KS];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < 4 * C::KS; ++i) {
           const uint4 x = *reinterpret_cast<const uint4*>(sSFA + 512 * i + 16 * lane);
           const uint4 y = *reinterpret_cast<const uint4*>(sSFB + 512 * i + 16 * lane);
-          const uint4 z = *reinterpret_cast<const uint4*>(sSFB + 2048 + 512 * i + 16 * lane);
+          const uint4 z = *reinterpret_cast<const uint4*>(sSFB + C::kSfbBytes / 2 + 512 * i + 16 * lane);
           a[4 * i] = x.x, a[4 * i + 1] = x.y, a[4 * i + 2] = x.z, a[4 * i + 3] = x.w;
           // words w0 .. w0+5 of (first group's atom, second group's atom)
           b[6 * i] = mid ? y.z : y.x;
@@ -669,11 +743,10 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
         }
         tc_fence_after();
         const uint32_t sfa = tmem + lane_off + C::kSfCol + C::kSfSlotCols * slot;
-        tmem_st_8cols(sfa, a);
-        tmem_st_8cols(sfa + 8, a + 8);
-        tmem_st_8cols(sfa + 16, b);
-        tmem_st_8cols(sfa + 24, b + 8);
-        tmem_st_8cols(sfa + 32, b + 16);
+#pragma unroll
+        for (int c = 0; c < 2 * C::KS; ++c) tmem_st_8cols(sfa + 8 * c, a + 8 * c);
+#pragma unroll
+        for (int c = 0; c < 3 * C::KS; ++c) tmem_st_8cols(sfa + 16 * C::KS + 8 * c, b + 8 * c);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
@@ -698,7 +771,7 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
     for (int tile = cluster; tile < p.num_tiles; tile += clusters, ++j) {
       int mb2, nb;
       tile_coords(tile, pp, mb2, nb);
-      const int buf = j & 1;
+      const int buf = j % C::kAccBufs;
       const bool got = mbar_wait_bounded(&acc_full[buf], ((acc_phase >> buf) & 1u), abort_flag, kWaitLimitNs);
       if (!__all_sync(0xffffffffu, got)) {
         if (lane == 0) fail();
@@ -707,16 +780,34 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1)
       acc_phase ^= 1u << buf;
       __syncwarp();
       tc_fence_after();
-      store_rows_tma<C::BN>(p, e, &tmD, &tmR, alpha, tmem + ((uint32_t)(q * 32) << 16) + buf * C::BN,
-                            (2 * mb2 + (int)rank) * BM + q * 32, nb, 3 * half, 3 * half + 3, box, box_bar + ew,
-                            lphase, abort_flag, ok);
-      if (!ok) {
-        if (lane == 0) fail();
-        break;
+      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + buf * C::BN;
+      const int m0 = (2 * mb2 + (int)rank) * BM + q * 32;
+      if constexpr (C::kAccBufs == 1) {
+        // read this warp's 96 columns, release the accumulator to the next tile's MMAs, then scale and store
+        uint32_t acc[3][32];
+#pragma unroll
+        for (int cc = 0; cc < 3; ++cc) tmem_ld_32cols(tbase + 32 * (3 * half + cc), acc[cc]);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(in_cta(&acc_empty[buf], 0));
+        store_rows_regs<C::BN, 3>(p, e, &tmD, &tmR, alpha, acc, m0, nb, 3 * half, box, box_bar + ew, lphase,
+                                  abort_flag, ok);
+        if (!ok) {
+          if (lane == 0) fail();
+          break;
+        }
+      } else {
+        store_rows_tma<C::BN>(p, e, &tmD, &tmR, alpha, tbase, m0, nb, 3 * half, 3 * half + 3, box, box_bar + ew,
+                              lphase, abort_flag, ok);
+        if (!ok) {
+          if (lane == 0) fail();
+          break;
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(in_cta(&acc_empty[buf], 0));
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(in_cta(&acc_empty[buf], 0));
     }
     if (lane == 0) bulk_wait_all();  // the output stores have completed before the CTA exits
   }

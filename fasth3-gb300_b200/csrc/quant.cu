@@ -5,9 +5,11 @@
 // per-element expression below is written in the same operand order as the reference kernel
 // (fastvideo/models/dits/h3fast/h3fast.cu:188-265): with the same flags the compiler emits the same approximate
 // reciprocal, rsqrt and contractions, which is what makes the quantized bytes bit-identical to the reference's.
-// The row sum of squares uses the reference's reduction tree (8 contiguous elements per thread summed in order,
-// warp butterfly, warp partials butterflied again), so its rounding is the same too.
+// The RMSNorm row sum of squares uses the reference's reduction tree (8 contiguous elements per thread summed in order,
+// warp butterfly, warp partials butterflied again), so its rounding is the same too. The LayerNorm variant has no
+// reference counterpart; its summation order is defined below and restated by the oracle.
 #include "common.cuh"
+#include "sm100.cuh"
 
 #include <algorithm>
 
@@ -127,10 +129,207 @@ __global__ void __launch_bounds__(C / 8, 2) resid_norm_quant_kernel(const RowArg
   }
 }
 
-// LayerNorm variant (no reference counterpart; BASELINE's norm1/norm2 and the affine norm3 given as a table): one
+// ------------------------------------------------------------------------------------------------ LayerNorm
+// The LayerNorm variant (no reference counterpart: the DiT block's norm1/norm2 with the adaLN modulate, and the affine
+// norm3 given as a table) has one summation order for every kernel below, defined by a thread layout: a row of
+// C = 8 K G elements is shared by G threads (a whole number of warps), thread t owning the 8-element chunks
+// t, t + G, ..., t + (K - 1) G, with K the largest of 5, 4, 3, 2 that gives whole warps (else 1). A thread sums its
+// values with two float32 accumulators (even and odd elements of each chunk, chunk by chunk), adds the two, the warp
+// butterflies the thread sums, and the warp sums are added in warp order. The sum of squares of (x - mean) is formed
+// the same way with one fused multiply-add per element.
+template <int C>
+struct LnRowShape {
+  static constexpr int kChunks = C / 8;
+  static constexpr int pick() {
+    for (int k = 5; k > 1; --k)
+      if (kChunks % k == 0 && (kChunks / k) % 32 == 0) return k;
+    return 1;
+  }
+  static constexpr int K = pick();
+  static constexpr int G = kChunks / K;
+  static constexpr int NW = G / 32;
+  static_assert(G % 32 == 0, "the LayerNorm row layout needs whole warps");
+};
+
+// one thread's share of the row sum from its chunks' values v[8 K]: the pair accumulators, then their sum
+template <int E>
+__device__ __forceinline__ float ln_thread_sum(const float (&v)[E]) {
+  float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < E; i += 2) add2(s0, s1, v[i], v[i + 1]);
+  return s0 + s1;
+}
+template <int E>
+__device__ __forceinline__ float ln_thread_sumsq(const float (&d)[E]) {
+  float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < E; i += 2) sq_acc2(s0, s1, d[i], d[i + 1]);
+  return s0 + s1;
+}
+
+__device__ int g_rows_status = 0;
+constexpr uint64_t kRowWaitLimitNs = 1000000000ull;
+
+// Row-per-CTA LayerNorm quantizer for the common case of one modulation row for all tokens (or a per-token table row
+// given by idx) and no residual branch. G threads per CTA walk rows r, r + grid, ...; thread 0 keeps kLnStages rows
+// in flight as 1D bulk copies into a ring of shared-memory row buffers (mbarrier completion), so the loads need no
+// registers and many rows are in flight per SM. A thread reads its chunks once into registers and keeps them there
+// through both statistics, the modulate and the quantization; the modulate factors (1 + scale, shift) of its columns
+// stay in registers for the whole launch when the table row is shared. Three CTA reductions per row (sum, sum of
+// squares, maximum). Every wait is bounded: on expiry the CTA records H3B_ETIMEOUT in the row kernels' status word,
+// waits (bounded) for its copies in flight and returns.
+constexpr int kLnStages = 4;
+template <int C>
+constexpr int ln_rows_smem_bytes() {
+  return kLnStages * C * 2 + kLnStages * 8 + 3 * 32 * 4;
+}
+
+template <int C, bool FP4, bool IDX>
+__global__ void __launch_bounds__(LnRowShape<C>::G, (LnRowShape<C>::G <= 128 ? 3 : 2))
+    layer_norm_quant_rows_kernel(const RowArgs a) {
+  using Sh = LnRowShape<C>;
+  constexpr int K = Sh::K, G = Sh::G, NW = Sh::NW, E = 8 * K;
+  constexpr uint32_t kRowBytes = C * 2;
+  extern __shared__ __align__(16) uint8_t ln_smem[];
+  bf16* ring = reinterpret_cast<bf16*>(ln_smem);
+  uint64_t* full = reinterpret_cast<uint64_t*>(ln_smem + (size_t)kLnStages * kRowBytes);
+  float* red = reinterpret_cast<float*>(full + kLnStages);  // [3][32]: warp sums, sums of squares, maxima
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  const int64_t step = gridDim.x;
+  if (t == 0) {
+    for (int s = 0; s < kLnStages; ++s) sm100::mbar_init(&full[s], 1);
+    sm100::fence_mbar_init();
+    for (int s = 0; s < kLnStages; ++s) {
+      const int64_t r = blockIdx.x + s * step;
+      if (r < a.rows) {
+        sm100::mbar_arrive_expect_tx(&full[s], kRowBytes);
+        sm100::bulk_load(ring + (size_t)s * C, a.x + r * C, kRowBytes, &full[s]);
+      }
+    }
+  }
+  float a1[E], sh[E];
+  auto factors = [&](int64_t tab) {
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int c = (t + G * k) * 8;
+      float sc[8], sf[8];
+      load8_nc(a.scale + tab * a.tab_ld + c, sc);
+      load8_nc(a.shift + tab * a.tab_ld + c, sf);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        a1[8 * k + i] = 1.f + sc[i];
+        sh[8 * k + i] = sf[i];
+      }
+    }
+  };
+  if constexpr (!IDX) factors(0);
+  __syncthreads();
+  volatile int no_abort = 0;
+  uint32_t it = 0;
+  for (int64_t r = blockIdx.x; r < a.rows; r += step, ++it) {
+    const uint32_t s = it % kLnStages;
+    if constexpr (IDX) factors(a.idx[r]);
+    const bool ok = sm100::mbar_wait_bounded(&full[s], (it / kLnStages) & 1u, &no_abort, kRowWaitLimitNs);
+    float v[E];
+    const bf16* row = ring + (size_t)s * C;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      float f[8];
+      unpack8(*reinterpret_cast<const uint4*>(row + (t + G * k) * 8), f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[8 * k + i] = f[i];
+    }
+    const float ts = warp_allreduce<false>(ln_thread_sum(v));
+    if (lane == 0) red[w] = ts;
+    if (__syncthreads_or(!ok)) {  // a row never arrived: record it, drain this CTA's copies, leave
+      if (t == 0) {
+        atomicExch(&g_rows_status, H3B_ETIMEOUT);
+        for (int j = 0; j < kLnStages; ++j) {
+          if (r + j * step >= a.rows) break;
+          const uint32_t ij = it + j;
+          sm100::mbar_wait_bounded(&full[ij % kLnStages], (ij / kLnStages) & 1u, &no_abort, kRowWaitLimitNs / 8);
+        }
+      }
+      return;
+    }
+    if (t == 0) {  // every thread has read buffer s (before the barrier): refill it with row r + kLnStages * step
+      const int64_t rn = r + kLnStages * step;
+      if (rn < a.rows) {
+        sm100::fence_proxy_async_smem();
+        sm100::mbar_arrive_expect_tx(&full[s], kRowBytes);
+        sm100::bulk_load(ring + (size_t)s * C, a.x + rn * C, kRowBytes, &full[s]);
+      }
+    }
+    float tot = red[0];
+#pragma unroll
+    for (int q = 1; q < NW; ++q) tot += red[q];
+    const float mean = tot / C;
+#pragma unroll
+    for (int i = 0; i < E; i += 2) sub2(v[i], v[i + 1], mean, mean);
+    const float tq = warp_allreduce<false>(ln_thread_sumsq(v));
+    if (lane == 0) red[32 + w] = tq;
+    __syncthreads();
+    float tot2 = red[32];
+#pragma unroll
+    for (int q = 1; q < NW; ++q) tot2 += red[32 + q];
+    const float rs = rsqrtf(tot2 / C + a.eps);
+    float cm[K];
+    float am = 0.f;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+#pragma unroll
+      for (int i = 8 * k; i < 8 * k + 8; i += 2) {
+        mul2(v[i], v[i + 1], rs, rs);
+        fma2(v[i], v[i + 1], a1[i], a1[i + 1], sh[i], sh[i + 1]);
+      }
+      const float* u = v + 8 * k;
+      float m = fmaxf(fabsf(u[0]), fabsf(u[1]));
+#pragma unroll
+      for (int i = 2; i < 8; ++i) m = fmaxf(m, fabsf(u[i]));
+      cm[k] = m;
+      am = fmaxf(am, m);
+    }
+    am = warp_allreduce<true>(am);
+    if (lane == 0) red[64 + w] = am;
+    __syncthreads();
+    am = red[64];
+#pragma unroll
+    for (int q = 1; q < NW; ++q) am = fmaxf(am, red[64 + q]);
+    const float gscale = FP4 ? fmaxf(am / kFp4Range, kMinScaleFp4) : fmaxf(am / kFp8Max, kMinScaleFp8);
+    const float inv = 1.f / gscale;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int chunk = t + G * k;
+      float* u = v + 8 * k;
+      if constexpr (FP4) {
+        // a 16-element block spans chunks 2m and 2m+1: threads t and t^1 of the same k (G is even)
+        const float vmax = fmaxf(cm[k], __shfl_xor_sync(0xffffffffu, cm[k], 1));
+        uint32_t bits;
+        const float mult = nvfp4_block_scale(vmax, inv, &bits);
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) mul2(u[i], u[i + 1], mult, mult);
+        const uint32_t lo = e2m1x4(u[0], u[1], u[2], u[3]);
+        const uint32_t hi = e2m1x4(u[4], u[5], u[6], u[7]);
+        *reinterpret_cast<uint32_t*>(a.h + r * (C / 2) + chunk * 4) = lo | (hi << 16);
+        if ((t & 1) == 0) a.hsf[sf_atom_offset(r, chunk >> 1, C / 16)] = (uint8_t)bits;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) mul2(u[i], u[i + 1], inv, inv);
+        uint2 o;
+        o.x = e4m3x4(u[0], u[1], u[2], u[3]);
+        o.y = e4m3x4(u[4], u[5], u[6], u[7]);
+        *reinterpret_cast<uint2*>(a.h + r * C + chunk * 8) = o;
+      }
+    }
+    if (t == 0) a.hs[r] = gscale;
+  }
+}
+
+// LayerNorm with the gated residual branch in front (x + gate * (sy * y) written to xo, then normalized): one
 // warp per row, lane l owns the 8-element chunks l, l+32, l+64, ... (coalesced); the row is staged in shared memory
-// (bf16) by asynchronous copies. Row sums are a sequential float32 sum over a lane's chunks (chunk-major, elements in
-// order) followed by the warp butterfly: no block barriers, so many rows are in flight per SM. With one adaLN table
+// (bf16) by asynchronous copies. The row statistics follow the LayerNorm order above: lane l plays thread 32q + l of
+// each of the NW warps of the row layout in turn (one butterfly per warp), so the results equal the row-per-CTA
+// kernel's. No block barriers, so many rows are in flight per SM. With one adaLN table
 // row for all tokens (idx NULL) the CTA first copies it into shared memory (bf16: half the bytes the two modulate
 // passes read per row against a float32 copy; 1 + scale is formed per element as in the idx path, so the values are
 // the same). One CTA per SM with as many row buffers as fit beside the table (20 warps at C = 5120).
@@ -207,27 +406,41 @@ __global__ void __launch_bounds__(ln_warps<C>() * 32, 1) layer_norm_quant_warp_k
         store8(row + c, v);  // v is bf16-exact
       }
     }
-    float s1 = 0.f;
-#pragma unroll 4
-    for (int j = 0; j < J; ++j) {
-      float v[8];
-      unpack8(*reinterpret_cast<const uint4*>(row + (lane + 32 * j) * 8), v);
+    // row statistics in the LayerNorm order: lane l plays thread 32 q + l of warp q of the row layout
+    using Sh = LnRowShape<C>;
+    float tot = 0.f;
+#pragma unroll 1
+    for (int q = 0; q < Sh::NW; ++q) {
+      float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) s1 += v[i];
-    }
-    const float mean = warp_allreduce<false>(s1) / C;
-    float s2 = 0.f;
-#pragma unroll 4
-    for (int j = 0; j < J; ++j) {
-      float v[8];
-      unpack8(*reinterpret_cast<const uint4*>(row + (lane + 32 * j) * 8), v);
+      for (int k = 0; k < Sh::K; ++k) {
+        float v[8];
+        unpack8(*reinterpret_cast<const uint4*>(row + (32 * q + lane + Sh::G * k) * 8), v);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        v[i] -= mean;
-        s2 += v[i] * v[i];
+        for (int i = 0; i < 8; i += 2) add2(s0, s1, v[i], v[i + 1]);
       }
+      const float part = warp_allreduce<false>(s0 + s1);
+      tot = q == 0 ? part : tot + part;
     }
-    const float rs = rsqrtf(warp_allreduce<false>(s2) / C + a.eps);
+    const float mean = tot / C;
+    float tot2 = 0.f;
+#pragma unroll 1
+    for (int q = 0; q < Sh::NW; ++q) {
+      float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+      for (int k = 0; k < Sh::K; ++k) {
+        float v[8];
+        unpack8(*reinterpret_cast<const uint4*>(row + (32 * q + lane + Sh::G * k) * 8), v);
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+          sub2(v[i], v[i + 1], mean, mean);
+          sq_acc2(s0, s1, v[i], v[i + 1]);
+        }
+      }
+      const float part = warp_allreduce<false>(s0 + s1);
+      tot2 = q == 0 ? part : tot2 + part;
+    }
+    const float rs = rsqrtf(tot2 / C + a.eps);
     float am = 0.f;
 #pragma unroll 2
     for (int j = 0; j < J; ++j) {
@@ -279,6 +492,28 @@ __global__ void __launch_bounds__(ln_warps<C>() * 32, 1) layer_norm_quant_warp_k
   }
 }
 
+// Row-per-CTA LayerNorm launch: as many CTAs as are resident on the device (occupancy queried once per device).
+template <int C, bool FP4, bool IDX>
+int launch_ln_rows(const RowArgs& a, int sms, cudaStream_t st) {
+  constexpr int lsm = ln_rows_smem_bytes<C>();
+  static_assert(lsm <= 48 * 1024, "the row ring fits the default dynamic shared-memory limit");
+  static PerDevice occupancy;
+  int per_sm = 0;
+  if (int rc = occupancy.get([&](int* v) {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, layer_norm_quant_rows_kernel<C, FP4, IDX>,
+                                                          LnRowShape<C>::G, lsm) != cudaSuccess || n < 1)
+          return set_error(H3B_ECUDA, "resid_norm_quant: occupancy query failed");
+        *v = n;
+        return H3B_OK;
+      }, &per_sm))
+    return rc;
+  const int64_t cap = (int64_t)sms * per_sm;
+  layer_norm_quant_rows_kernel<C, FP4, IDX>
+      <<<(unsigned)(a.rows < cap ? a.rows : cap), LnRowShape<C>::G, lsm, st>>>(a);
+  return H3B_OK;
+}
+
 template <int C>
 int launch_resid_norm_quant(const RowArgs& a, bool branch, int norm, bool fp4, cudaStream_t st) {
   int dev = 0, sms = 148;
@@ -318,8 +553,12 @@ int launch_resid_norm_quant(const RowArgs& a, bool branch, int norm, bool fp4, c
   } while (0)
     if (branch) {
       if (fp4) H3B_LNQ(true, true); else H3B_LNQ(true, false);
+    } else if (a.idx) {
+      if (int rc = fp4 ? launch_ln_rows<C, true, true>(a, sms, st) : launch_ln_rows<C, false, true>(a, sms, st))
+        return rc;
     } else {
-      if (fp4) H3B_LNQ(false, true); else H3B_LNQ(false, false);
+      if (int rc = fp4 ? launch_ln_rows<C, true, false>(a, sms, st) : launch_ln_rows<C, false, false>(a, sms, st))
+        return rc;
     }
 #undef H3B_LNQ
   }
@@ -492,6 +731,20 @@ int amax_launch(const bf16* x, int64_t ld, int64_t rows, int K, float* amax, cud
   return H3B_OK;
 }
 
+}  // namespace h3b
+
+namespace h3b {
+// The row kernels' status word (H3B_ETIMEOUT when a LayerNorm row copy never completed), read in stream order.
+int rows_status_async(int* dst, int clear, cudaStream_t stream) {
+  if (cudaMemcpyFromSymbolAsync(dst, g_rows_status, sizeof(int), 0, cudaMemcpyDefault, stream) != cudaSuccess)
+    return set_error(H3B_ECUDA, "status: reading the row kernels' status word failed");
+  if (clear) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_rows_status) != cudaSuccess || cudaMemsetAsync(p, 0, sizeof(int), stream) != cudaSuccess)
+      return set_error(H3B_ECUDA, "status: clearing the row kernels' status word failed");
+  }
+  return H3B_OK;
+}
 }  // namespace h3b
 
 using namespace h3b;

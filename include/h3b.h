@@ -343,8 +343,9 @@ int h3b_device_status(int* status);
 int h3b_reset_device_status(void);
 /* The kernels' device status words, read in stream order (no counterpart in the reference, whose kernels have no
  * bounded waits): dst[0] = the GEMMs' word (H3B_ETIMEOUT when a bounded wait expired), dst[1] = the attention's
- * (H3B_ETIMEOUT, or H3B_EINVAL when a selection list exceeded the 1024 key tiles the kernel holds). dst is device
- * memory or page-locked host memory for two ints; with `clear` both words are reset after the read. A step that
+ * (H3B_ETIMEOUT, or H3B_EINVAL when a selection list exceeded the 1024 key tiles the kernel holds), dst[2] = the row
+ * kernels' (H3B_ETIMEOUT when a LayerNorm row copy never completed). dst is device memory or page-locked host memory
+ * for three ints; with `clear` the words are reset after the read. A step that
  * enqueues this after its last kernel and checks dst once the stream reaches it learns of any failure in the step. */
 int h3b_status_async(int* dst, int clear, cudaStream_t stream);
 /* Exercises the bounded-wait path without a fault: one warp waits on an mbarrier nothing arrives on, with the kernels'

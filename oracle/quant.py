@@ -119,23 +119,40 @@ def block_sum_sq(v: np.ndarray) -> np.ndarray:
     return butterfly_sum(stage)
 
 
-def warp_row_sum(v: np.ndarray, squares: bool = False) -> np.ndarray:
-    """Row sum in the order of the warp-per-row LayerNorm quantizer (fasth3-gb300_b200/csrc/quant.cu,
-    layer_norm_quant_warp_kernel): lane l owns the 8-element chunks l, l+32, ... and adds them chunk by chunk, elements
-    in order, in float32 (``squares``: v*v accumulated with one fused multiply-add per element); the 32 lane sums are
-    then butterflied."""
+def ln_row_shape(C: int) -> tuple[int, int]:
+    """(K, G) of the LayerNorm row layout (fasth3-gb300_b200/csrc/quant.cu, LnRowShape): G threads per row, thread t
+    owning the 8-element chunks t, t + G, ..., t + (K - 1) G; K the largest of 5, 4, 3, 2 giving whole warps, else 1."""
+    chunks = C // 8
+    for k in (5, 4, 3, 2):
+        if chunks % k == 0 and (chunks // k) % 32 == 0:
+            return k, chunks // k
+    return 1, chunks
+
+
+def ln_row_sum(v: np.ndarray, squares: bool = False) -> np.ndarray:
+    """Row sum in the LayerNorm quantizer's order (fasth3-gb300_b200/csrc/quant.cu, ln_thread_sum and the kernels'
+    reductions): each thread of the row layout (ln_row_shape) keeps two float32 accumulators, one for the even and one
+    for the odd elements of its chunks, advanced chunk by chunk (``squares``: v*v added with one fused multiply-add per
+    element); the thread's sum is the two accumulators added, each warp butterflies its 32 thread sums, and the warp
+    sums are added in warp order."""
     rows, C = v.shape
-    t = v.reshape(rows, C // 256, 32, 8)  # [row, j, lane, element]: chunk index lane + 32 j
-    acc = np.zeros((rows, 32), dtype=np.float32)
-    for j in range(C // 256):
-        for i in range(8):
-            x = t[:, j, :, i]
+    K, G = ln_row_shape(C)
+    t = np.asarray(v, dtype=np.float32).reshape(rows, K, G, 4, 2)  # [row, k, thread, pair, even/odd]
+    acc = np.zeros((rows, G, 2), dtype=np.float32)
+    for k in range(K):
+        for p in range(4):
+            x = t[:, k, :, p, :]
             if squares:
                 x64 = x.astype(np.float64)
                 acc = (acc.astype(np.float64) + x64 * x64).astype(np.float32)
             else:
                 acc = (acc + x).astype(np.float32)
-    return butterfly_sum(acc)
+    th = (acc[..., 0] + acc[..., 1]).astype(np.float32)
+    warp = butterfly_sum(th.reshape(rows, G // 32, 32))
+    tot = warp[:, 0]
+    for q in range(1, G // 32):
+        tot = (tot + warp[:, q]).astype(np.float32)
+    return tot
 
 
 def fp8_rows_from_values(v: np.ndarray, mag: np.ndarray | None = None):
@@ -232,10 +249,10 @@ def resid_norm_quant(x, y=None, sy=None, gate=None, idx=None, nw=None, shift=Non
         w = np.asarray(nw, dtype=np.float32)
         p = ((v * rs[:, None]).astype(np.float32) * w[None, :]).astype(np.float32)
         m = (p.astype(np.float64) * one_sc + sf).astype(np.float32)
-    elif norm == "layer":  # the LayerNorm variant reduces one row per warp (warp_row_sum)
-        mean = (warp_row_sum(v) / np.float32(C)).astype(np.float32)
+    elif norm == "layer":  # the LayerNorm variant's own summation order (ln_row_sum)
+        mean = (ln_row_sum(v) / np.float32(C)).astype(np.float32)
         d = (v - mean[:, None]).astype(np.float32)
-        var = (warp_row_sum(d, squares=True) / np.float32(C)).astype(np.float32)
+        var = (ln_row_sum(d, squares=True) / np.float32(C)).astype(np.float32)
         rs = (1.0 / np.sqrt((var + np.float32(eps)).astype(np.float64))).astype(np.float32)
         p = (d * rs[:, None]).astype(np.float32)
         m = (p.astype(np.float64) * one_sc + sf).astype(np.float32)

@@ -195,6 +195,37 @@ def test_layernorm_shared_table_every_width(ops, C):
             assert_codes(_u8(h), out["h"], out["amb"], f"ln fp8 C={C}")
 
 
+@pytest.mark.parametrize("C,rows,per_token", [(5120, 4999, False), (5376, 3001, True), (3072, 2311, True)])
+def test_layernorm_row_ring_wraps(ops, C, rows, per_token):
+    """Row counts above (resident CTAs x ring stages), so every CTA refills and re-uses its row buffers several times
+    (the mbarrier parity flips), with one shared table row or a per-token table row (idx), NVFP4 and FP8."""
+    d = rnq_inputs(C, rows, seed=7 + C % 89)
+    f = lambda t: t.float().numpy()  # noqa: E731
+    if per_token:
+        idx = d["idx"]
+        shift, scale = d["shift"].contiguous(), d["scale"].contiguous()
+    else:
+        idx = None
+        shift, scale = d["shift"][0:1].contiguous(), d["scale"][0:1].contiguous()
+    oidx = np.zeros(rows, dtype=np.int32) if idx is None else idx.numpy()
+    for fp4 in (True, False):
+        x = d["x"].to(DEV)
+        h = torch.zeros(rows, C // 2 if fp4 else C, device=DEV, dtype=torch.uint8)
+        hsf = torch.zeros(ops.sf_rows(rows), C // 16, device=DEV, dtype=torch.uint8) if fp4 else None
+        hs = torch.zeros(rows, device=DEV)
+        ops.resid_norm_quant(x, None, None, None, None if idx is None else idx.to(DEV), None, shift.to(DEV),
+                             scale.to(DEV), x, h, hsf, hs, 1e-6, norm="layer")
+        ops.check_status()
+        out = oq.resid_norm_quant(f(d["x"]), None, None, None, oidx, None, f(shift), f(scale), 1e-6, norm="layer",
+                                  fp4=fp4)
+        assert_scales(hs.cpu().numpy(), out["hs"], f"ring row scales C={C}", rtol=2e-6)
+        if fp4:
+            assert_codes(oq.unswizzle_sf(_u8(hsf), rows, C // 16), out["sf_bits"], out["sf_amb"], f"ring sf C={C}")
+            assert_codes(oq.unpack_nibbles(_u8(h)), out["codes"], out["amb"], f"ring nibbles C={C}")
+        else:
+            assert_codes(_u8(h), out["h"], out["amb"], f"ring fp8 C={C}")
+
+
 def test_fp8_rows_vs_oracle_config1(ops):
     # BASELINE config 1 activations: [2048 x 3072] N(0,1) with 1% of columns x20
     x = outlier_matrix(2048, 3072, 0, 0.01, 20.0)
