@@ -480,6 +480,38 @@ def dit_step_secondary(pkg, dev, stream, args, ws) -> dict:
         finally:
             r8 = None
             torch.cuda.empty_cache()
+    ffn_static = None
+    if args.dit_ffn_static or (args.dit_extras and ws == 1):
+        try:
+            # the same step with the FFN intermediate re-quantized in fc_in's epilogue under fixed per-block global
+            # scales (recorded by the first forward) instead of the bf16 store + per-row quantization pass
+            rs = pkg.runner.H3FastRunner(m, sp, ffn_requant="static")
+            for _ in range(2):
+                out = rs.forward(x, temb, None, None, meta, context=ctx)
+            torch.cuda.synchronize()
+            if ws > 1:
+                dist.barrier()
+            e0.record(stream)
+            for _ in range(reps):
+                out = rs.forward(x, temb, None, None, meta, context=ctx)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            tf = e0.elapsed_time(e1) / reps
+            if ws > 1:
+                t = torch.tensor([tf], device=dev, dtype=torch.float64)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                tf = float(t.item())
+            ffn_static = {"ms_per_step": tf, "output_finite": bool(torch.isfinite(out.float()).all()),
+                          "headroom": rs.ffn_headroom}
+        except Exception as exc:  # an extra timing must not cost the line; its error is reported
+            ffn_static = {"error": repr(exc)[:300]}
+            try:
+                torch.cuda.synchronize()
+            except Exception:  # noqa: BLE001  a sticky CUDA error: every later GPU line would fail for this reason
+                ffn_static["context_lost"] = True
+        finally:
+            rs = None
+            torch.cuda.empty_cache()
     lin = 2.0 * S * (6 * cfg.hidden ** 2 + 2 * cfg.hidden * cfg.ffn) * cfg.blocks
     del r, m, x, out
     torch.cuda.empty_cache()
@@ -495,6 +527,8 @@ def dit_step_secondary(pkg, dev, stream, args, ws) -> dict:
         res["token_reduction"] = reduced
     if qk8 is not None:
         res["qk_int8"] = qk8
+    if ffn_static is not None:
+        res["ffn_static_requant"] = ffn_static
     if graphed is not None:
         res["cuda_graph"] = graphed
     return res
@@ -871,10 +905,12 @@ def main() -> None:
     ap.add_argument("--dit-graph", action="store_true",
                     help="also time the config-5 step replayed from one CUDA graph (one GPU)")
     ap.add_argument("--no-dit-extras", dest="dit_extras", action="store_false",
-                    help="skip the one-GPU extra config-5 timings run by default: token reduction over blocks 4..29 "
-                         "and INT8 QK^T")
+                    help="skip the one-GPU extra config-5 timings run by default: token reduction over blocks 4..29, "
+                         "INT8 QK^T and the static FFN re-quantization")
     ap.add_argument("--dit-qk-int8", action="store_true",
                     help="also time the config-5 step with INT8 QK^T in the self-attention")
+    ap.add_argument("--dit-ffn-static", action="store_true",
+                    help="also time the config-5 step with the FFN re-quantized in fc_in's epilogue (static scales)")
     ap.add_argument("--dit-reduction", default="", metavar="BEGIN:END[:SCALE]",
                     help="also time the config-5 step with token reduction over blocks [BEGIN, END) (one GPU)")
     ap.add_argument("--steps", type=int, default=100)

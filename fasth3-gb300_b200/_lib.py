@@ -65,6 +65,7 @@ SIGNATURES: dict[str, list] = {
     "h3b_expand_pairs": [P, I64, P, P, P, P, I32, F32, P],
     "h3b_gemm_fp8": [P, P, I64, I64, I64, ctypes.POINTER(Epilogue), P],
     "h3b_gemm_nvfp4": [P, P, P, P, I64, I64, I64, ctypes.POINTER(Epilogue), P],
+    "h3b_gemm_nvfp4_requant": [P, P, P, P, I64, I64, I64, ctypes.POINTER(Epilogue), P, P, P, P],
     "h3b_qkv_prologue8": [P, P, P, I64, P, P, P, P, P, P, P, F32, F32, P, P, P, P, P, P, P, P, P, P, I32, I64, I32,
                           I32, F32, P],
     "h3b_qkv_prologue8_qk_int8": [P, P, P, I64, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, I32, I64, I32, I32,

@@ -59,6 +59,10 @@ struct Epi {
   const bf16* gate;
   bf16* D;
   int64_t ldd;
+  // NVFP4 re-quantization of the output for the next GEMM instead of the bf16 store (NVFP4 pair kernel only)
+  uint8_t* q;              // [M, N/2] packed e2m1, element 2i in the low nibble
+  uint8_t* q_sf;           // [pad128(M), N/16] ue4m3 block scales in 128x4 atoms
+  const float* q_scale;    // device scalar: the fixed global scale s (blocks encoded under gs = 1/s)
 };
 
 struct Problem {
@@ -176,6 +180,34 @@ __device__ __forceinline__ bool epi_finish(const Problem& p, const Epi& e, const
     if (e.bias) x += __bfloat162float(e.bias[n]);
     if (e.act == H3B_ACT_GELU_TANH) x = gelu_tanh(x);
     v[i] = x;
+  }
+  if (e.q) {
+    // NVFP4 of the row's 32 values (two 16-element blocks) from their bf16 roundings -- the values a bf16 output
+    // would hold -- under the fixed global factor gs = 1/s: the block math of the activation quantizers
+    const int m = m0 + lane;
+    const float gs = 1.f / *e.q_scale;
+    uint32_t codes[4], bits[2];
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+      float vmax = 0.f;
+#pragma unroll
+      for (int i = 16 * b; i < 16 * b + 16; ++i) {
+        v[i] = to_bf16_and_back(v[i]);
+        vmax = fmaxf(vmax, fabsf(v[i]));
+      }
+      const float mult = nvfp4_block_scale(vmax, gs, &bits[b]);
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const float* u = v + 16 * b + 8 * j;
+        codes[2 * b + j] = e2m1x4(u[0] * mult, u[1] * mult, u[2] * mult, u[3] * mult) |
+                           (e2m1x4(u[4] * mult, u[5] * mult, u[6] * mult, u[7] * mult) << 16);
+      }
+    }
+    if (m < p.M) {
+      *reinterpret_cast<uint4*>(e.q + (size_t)m * (p.N / 2) + n0 / 2) = make_uint4(codes[0], codes[1], codes[2], codes[3]);
+      *reinterpret_cast<uint16_t*>(e.q_sf + sf_atom_offset(m, n0 / 16, p.N / 16)) = (uint16_t)(bits[0] | (bits[1] << 8));
+    }
+    return true;
   }
   if (res) {
     if (!__all_sync(0xffffffffu, mbar_wait_bounded(box_bar, lphase & 1u, abort_flag, kWaitLimitNs))) return false;
@@ -922,7 +954,8 @@ int run_gemm_fp8(const void* A, const void* B, int64_t M, int64_t N, int64_t K, 
 }
 
 int run_gemm_nvfp4_pair(const void* A, const uint8_t* sfa, const void* B, const uint8_t* sfb, int64_t M, int64_t N,
-                        int64_t K, const h3b_epilogue* epi, cudaStream_t stream) {
+                        int64_t K, const h3b_epilogue* epi, uint8_t* q, uint8_t* q_sf, const float* q_scale,
+                        cudaStream_t stream) {
   using C = PairCfg;
   CUtensorMap ta, tb;
   int rc = make_tmap(&ta, A, M, K / 2, BM);
@@ -930,9 +963,12 @@ int run_gemm_nvfp4_pair(const void* A, const uint8_t* sfa, const void* B, const 
   rc = make_tmap(&tb, B, N, K / 2, C::kBRows);
   if (rc) return rc;
   CUtensorMap td, tr;
-  rc = make_tmap_out(&td, epi->D, M, N, epi->ldd);
+  // with re-quantization the output maps are unused: they are built over the code buffer (as bf16 [M, N/4])
+  void* dbase = q ? static_cast<void*>(q) : epi->D;
+  const int64_t dcols = q ? N / 4 : N, dld = q ? N / 4 : epi->ldd;
+  rc = make_tmap_out(&td, dbase, M, dcols, dld);
   if (rc) return rc;
-  rc = epi->residual ? make_tmap_out(&tr, epi->residual, M, N, epi->ldr) : make_tmap_out(&tr, epi->D, M, N, epi->ldd);
+  rc = epi->residual ? make_tmap_out(&tr, epi->residual, M, N, epi->ldr) : make_tmap_out(&tr, dbase, M, dcols, dld);
   if (rc) return rc;
   Problem p;
   p.M = (int)M;
@@ -956,7 +992,10 @@ int run_gemm_nvfp4_pair(const void* A, const uint8_t* sfa, const void* B, const 
         epi->ldr,
         static_cast<const bf16*>(epi->gate),
         static_cast<bf16*>(epi->D),
-        epi->ldd};
+        epi->ldd,
+        q,
+        q_sf,
+        q_scale};
   auto kern = gemm_nvfp4_pair_kernel;
   static PerDevice setup;  // the shared-memory reservation and the resident CTA pairs, per device
   cudaLaunchConfig_t cfg = {};
@@ -1027,7 +1066,26 @@ extern "C" int h3b_gemm_nvfp4(const void* A, const uint8_t* sfa, const void* B, 
               "gemm_nvfp4: operands and scales must be 16-byte aligned");
   if (int rc = check_epilogue(epi, N)) return rc;
   if (M == 0) return H3B_OK;
-  return run_gemm_nvfp4_pair(A, sfa, B, sfb, M, N, K, epi, stream);
+  return run_gemm_nvfp4_pair(A, sfa, B, sfb, M, N, K, epi, nullptr, nullptr, nullptr, stream);
+}
+
+extern "C" int h3b_gemm_nvfp4_requant(const void* A, const uint8_t* sfa, const void* B, const uint8_t* sfb,
+                                      int64_t M, int64_t N, int64_t K, const h3b_epilogue* epi, uint8_t* q,
+                                      uint8_t* q_sf, const float* q_scale, cudaStream_t stream) {
+  clear_error();
+  H3B_REQUIRE(A && B && sfa && sfb, "gemm_nvfp4_requant: null operand");
+  H3B_REQUIRE(K > 0 && K % 256 == 0, "gemm_nvfp4_requant: K must be a positive multiple of 256 (got %lld)",
+              (long long)K);
+  H3B_REQUIRE(N > 0 && N % 32 == 0 && M >= 0, "gemm_nvfp4_requant: N must be a positive multiple of 32");
+  H3B_REQUIRE(aligned(A, 16) && aligned(B, 16) && aligned(sfa, 16) && aligned(sfb, 16),
+              "gemm_nvfp4_requant: operands and scales must be 16-byte aligned");
+  H3B_REQUIRE(epi && !epi->D && !epi->residual,
+              "gemm_nvfp4_requant: the epilogue writes q/q_sf only (D and residual must be NULL)");
+  H3B_REQUIRE(epi->act == H3B_ACT_NONE || epi->act == H3B_ACT_GELU_TANH, "gemm_nvfp4_requant: act %d", epi->act);
+  H3B_REQUIRE(q && q_sf && q_scale && aligned(q, 16) && aligned(q_sf, 2),
+              "gemm_nvfp4_requant: q (16-byte aligned), q_sf and q_scale are required");
+  if (M == 0) return H3B_OK;
+  return run_gemm_nvfp4_pair(A, sfa, B, sfb, M, N, K, epi, q, q_sf, q_scale, stream);
 }
 
 namespace h3b {

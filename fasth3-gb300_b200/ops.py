@@ -186,7 +186,8 @@ def quant_fp8_on_grid(merged: torch.Tensor, base_scale: torch.Tensor, workspace:
 
 
 # ------------------------------------------------------------------------------------------------- GEMMs
-def _epilogue(out: torch.Tensor, alpha: float, alpha_dev, row_scale, col_scale, bias, act, residual, gate) -> Epilogue:
+def _epilogue(out: torch.Tensor | None, alpha: float, alpha_dev, row_scale, col_scale, bias, act, residual,
+              gate) -> Epilogue:
     e = Epilogue()
     e.alpha = float(alpha)
     e.alpha_dev = _p(alpha_dev)
@@ -199,7 +200,7 @@ def _epilogue(out: torch.Tensor, alpha: float, alpha_dev, row_scale, col_scale, 
     e.ldr = residual.stride(0) if residual is not None else 0
     e.gate = _p(gate)
     e.D = _p(out)
-    e.ldd = out.stride(0)
+    e.ldd = out.stride(0) if out is not None else 0
     return e
 
 
@@ -232,6 +233,31 @@ def gemm_nvfp4(a: torch.Tensor, a_sf: torch.Tensor, w: torch.Tensor, w_sf: torch
     e = _epilogue(out, alpha, alpha_dev, scale_a, scale_b, bias, act, residual, gate)
     call("h3b_gemm_nvfp4", _p(a), _p(a_sf), _p(w), _p(w_sf), M, N, K, e, _stream(a))
     return out
+
+
+def gemm_nvfp4_requant(a: torch.Tensor, a_sf: torch.Tensor, w: torch.Tensor, w_sf: torch.Tensor, q: torch.Tensor,
+                       q_sf: torch.Tensor, q_scale: torch.Tensor, *, alpha: float = 1.0,
+                       alpha_dev: torch.Tensor | None = None, scale_a: torch.Tensor | None = None,
+                       scale_b: torch.Tensor | None = None, bias: torch.Tensor | None = None,
+                       act: str | None = None) -> torch.Tensor:
+    """gemm_nvfp4 whose epilogue writes the output re-quantized for the next NVFP4 GEMM: q [M, N/2] packed e2m1 and
+    q_sf [sf_rows(M), N/16] block scales under the fixed global scale ``q_scale`` (a device float; the next GEMM takes
+    it as its alpha). Replaces the bf16 store plus the separate per-row quantization pass of the reference's FFN
+    (h3fast.cu:781-817) when a static global scale is acceptable."""
+    _contig(a, "a")
+    _contig(w, "w")
+    M, K = a.shape[0], a.shape[1] * 2
+    N = w.shape[0]
+    if q.shape != (M, N // 2) or q.dtype != torch.uint8 or not q.is_contiguous():
+        raise ValueError(f"q must be contiguous uint8 [{M}, {N // 2}]")
+    if q_sf.shape != (sf_rows(M), N // 16) or q_sf.dtype != torch.uint8:
+        raise ValueError(f"q_sf must be uint8 [{sf_rows(M)}, {N // 16}]")
+    if q_scale.numel() != 1 or q_scale.dtype != torch.float32:
+        raise ValueError("q_scale must be one float32 on the device")
+    e = _epilogue(None, alpha, alpha_dev, scale_a, scale_b, bias, act, None, None)
+    call("h3b_gemm_nvfp4_requant", _p(a), _p(a_sf), _p(w), _p(w_sf), M, N, K, e, _p(q), _p(q_sf), _p(q_scale),
+         _stream(a))
+    return q
 
 
 def device_status() -> int:

@@ -217,9 +217,17 @@ class H3FastRunner:
     (exact scores; E4M3 otherwise). ``v_f16``: V tiles as f16 (see below)."""
 
     def __init__(self, model: DiTModel, sp: SeqParallel | VirtualSeqParallel | None = None, qk_int8: bool = False,
-                 v_f16: bool = False):
+                 v_f16: bool = False, ffn_requant: str = "rows"):
         self.model = model
         self.qk_int8 = bool(qk_int8)
+        # FFN re-quantization between fc_in and fc_out: "rows" -- the reference's rule, the bf16 fc_in output
+        # re-quantized per row (global scale amax_row / 2688) by a separate pass; "static" -- fc_in's epilogue writes
+        # NVFP4 directly under a fixed global scale per block, s_i = headroom * max|u_i| / 2688 recorded by the first
+        # forward (which runs the "rows" path; max over ranks) and kept; values above headroom x that maximum saturate
+        if ffn_requant not in ("rows", "static"):
+            raise ValueError(f"ffn_requant must be 'rows' or 'static', not {ffn_requant!r}")
+        self.ffn_requant = ffn_requant
+        self.ffn_headroom = 2.0
         # V tiles as E4M3 codes converted by the attention kernel on every use (default: half the bytes in the
         # prologue's writes and the sequence-parallel exchange), or as f16 holding the E4M3 values (decoded once by
         # the prologue, loaded by the PV MMAs as is); the results are bit-identical and the attention time equal
@@ -231,6 +239,8 @@ class H3FastRunner:
         if self.head_dim != 128:
             raise ValueError("head_dim 128 only")
         self.fp4 = cfg.fmt == "nvfp4"
+        if ffn_requant == "static" and not self.fp4:
+            raise ValueError("ffn_requant='static' needs NVFP4 linears")
         self.ex = _Exchange(sp if sp is not None else SeqParallel.local())
         if self.heads % self.ex.world:
             raise ValueError(f"{self.heads} heads do not split over {self.ex.world} ranks")
@@ -239,6 +249,9 @@ class H3FastRunner:
         dev = self.blocks[0].scale_shift_table.device
         self.dev = dev
         self.ones_c = torch.ones(self.hidden, device=dev, dtype=torch.bfloat16)
+        self.ffn_scales = torch.zeros(len(self.blocks), device=dev)  # "static": s_i once recorded
+        self._ffn_amax = torch.zeros(len(self.blocks), device=dev)
+        self._ffn_state = "unset"  # "unset" -> "recording" (during the first forward) -> "set"
         self.text_cache: dict = {}
         # the gate-compress branch (gate GEMM, compressed attention) runs on this stream beside the sparse attention
         # (the reference's side stream, __init__.py:465-535)
@@ -275,16 +288,23 @@ class H3FastRunner:
         return (fp4 or fp8) and meta is not None and meta.exempt and not meta.pad_tokens and meta.tile_elems == 64
 
     # ------------------------------------------------------------------------------------------------- GEMM
-    def _gemm(self, a, a_sf, fused, out, *, row_scale=None, act=None, residual=None, gate=None, cols=None):
+    def _gemm(self, a, a_sf, fused, out, *, row_scale=None, act=None, residual=None, gate=None, cols=None,
+              alpha_dev=None):
         w, sf, col = fused["w"], fused["sf"], fused["col"]
         if cols is not None:
             w, col = w[cols], col[cols]
             sf = None if sf is None else sf[cols]
         if fused["fmt"] == "nvfp4":
             ops.gemm_nvfp4(a, a_sf, w, sf, out, scale_a=row_scale, scale_b=col, act=act, residual=residual,
-                           gate=gate)
+                           gate=gate, alpha_dev=alpha_dev)
         else:
-            ops.gemm_fp8(a, w, out, scale_a=row_scale, scale_b=col, act=act, residual=residual, gate=gate)
+            ops.gemm_fp8(a, w, out, scale_a=row_scale, scale_b=col, act=act, residual=residual, gate=gate,
+                         alpha_dev=alpha_dev)
+
+    def reset_ffn_scales(self) -> None:
+        """With ffn_requant="static": the next forward records the FFN global scales again (e.g. after new
+        weights)."""
+        self._ffn_state = "unset"
 
     # ------------------------------------------------------------------------------------------------- layout
     def _layouts(self, meta: VsaMeta, rotary, tag: object = None) -> tuple[TileLayout, list[_RankState]]:
@@ -452,6 +472,9 @@ class H3FastRunner:
             raise ValueError("adaln_indices must select table row 0 (one timestep)")
         tabs = self.model.adaln_tables(temb.reshape(1, -1))  # [blocks, 6, C]
         txt = self._text_kv(context)
+        if self.ffn_requant == "static" and self._ffn_state == "unset":
+            self._ffn_amax.zero_()
+            self._ffn_state = "recording"
         x_in = packed.reshape(S, -1)
         for st in states:
             torch.index_select(x_in, 0, st.tok_index, out=st.b["x"])
@@ -475,6 +498,12 @@ class H3FastRunner:
         if red is not None and reduction.begin < len(self.blocks) <= reduction.end:
             ops.expand_pairs(states[0].b["x"], red["states"][0].b["x"], red["pooled"], red["par"], red["pair"],
                              reduction.update_scale)
+        if self._ffn_state == "recording":
+            if not self.ex.virtual and self.ex.world > 1:
+                dist.all_reduce(self._ffn_amax, op=dist.ReduceOp.MAX, group=self.ex.sp.group)
+            torch.mul(self._ffn_amax, self.ffn_headroom / 2688.0, out=self.ffn_scales)
+            self.ffn_scales.clamp_(min=1e-12)
+            self._ffn_state = "set"
         per = full.n_tiles // self.ex.world
         rows_all = [int(full.vbs[p * per:(p + 1) * per].sum()) for p in range(self.ex.world)]
         out = self.ex.all_gather_rows([st.b["x"] for st in states], rows_all)  # global tile order
@@ -629,14 +658,25 @@ class H3FastRunner:
             self._t(i, "cross_out", st, x=b["x"])
             # FFN: norm2 + modulate + quant, fc_in with GELU-tanh, row quant, fc_out with the gated residual
             self._norm(st, blk.eps, tab[3:4], tab[4:5], i, "norm2")
-            self._gemm(self._q(b["h"]), b["h_sf"], fz["fc_in"], b["u"], row_scale=b["hs"], act="gelu_tanh")
-            if self.fp4:
-                ops.quant_nvfp4_rows(b["u"], b["f"], b["f_sf"], b["fs"])
+            if self._ffn_state == "set":
+                # fc_in + GELU-tanh with NVFP4 re-quantization in the epilogue under the block's fixed scale
+                s_i = self.ffn_scales[i:i + 1]
+                fi = fz["fc_in"]
+                ops.gemm_nvfp4_requant(b["h"], b["h_sf"], fi["w"], fi["sf"], b["f"], b["f_sf"], s_i,
+                                       scale_a=b["hs"], scale_b=fi["col"], act="gelu_tanh")
+                self._t(i, "ffn_mid", st, f=b["f"], f_sf=b["f_sf"], fs=s_i)
+                self._gemm(b["f"], b["f_sf"], fz["fc_out"], b["x"], alpha_dev=s_i, residual=b["x"], gate=tab[5])
             else:
-                ops.quant_fp8_rows(b["u"], b["f"].view(ops.FP8), b["fs"])
-            self._t(i, "ffn_mid", st, u=b["u"], f=b["f"], f_sf=b["f_sf"], fs=b["fs"])
-            self._gemm(self._q(b["f"]), b["f_sf"], fz["fc_out"], b["x"], row_scale=b["fs"], residual=b["x"],
-                       gate=tab[5])
+                self._gemm(self._q(b["h"]), b["h_sf"], fz["fc_in"], b["u"], row_scale=b["hs"], act="gelu_tanh")
+                if self.fp4:
+                    ops.quant_nvfp4_rows(b["u"], b["f"], b["f_sf"], b["fs"])
+                else:
+                    ops.quant_fp8_rows(b["u"], b["f"].view(ops.FP8), b["fs"])
+                if self._ffn_state == "recording":
+                    ops.amax(b["u"], self._ffn_amax[i:i + 1])
+                self._t(i, "ffn_mid", st, u=b["u"], f=b["f"], f_sf=b["f_sf"], fs=b["fs"])
+                self._gemm(self._q(b["f"]), b["f_sf"], fz["fc_out"], b["x"], row_scale=b["fs"], residual=b["x"],
+                           gate=tab[5])
             self._t(i, "fc_out", st, x=b["x"])
             # the next block's norm1 + modulate + quant
             if i + 1 < len(self.blocks):

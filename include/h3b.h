@@ -171,6 +171,18 @@ int h3b_gemm_fp8(const void* A, const void* B, int64_t M, int64_t N, int64_t K, 
                  cudaStream_t stream);
 int h3b_gemm_nvfp4(const void* A, const uint8_t* sfa, const void* B, const uint8_t* sfb, int64_t M, int64_t N,
                    int64_t K, const h3b_epilogue* epi, cudaStream_t stream);
+/* NVFP4 GEMM whose epilogue re-quantizes its output for the next NVFP4 GEMM instead of storing bf16 (the reference
+ * writes the fc_in output and re-quantizes it in a separate pass, fastvideo/models/dits/h3fast/h3fast.cu:781-817, with
+ * a per-row global scale that needs the whole row). Each output value (alpha, row/col scales, bias, activation as in
+ * h3b_gemm_nvfp4) is rounded to bf16 -- the value a bf16 output would hold -- and encoded with the activation
+ * quantizers' block math under a FIXED global scale s = *q_scale (device float, e.g. a calibrated per-layer
+ * constant): ue4m3 block scale sat(vmax / 6 / s) per 16 columns, e2m1 codes of v * (1/s) / block scale; magnitudes
+ * above 2688 * s saturate. q: [M, N/2] packed (element 2i in the low nibble); q_sf: [pad128(M), N/16] in 128x4 atoms
+ * (padding rows are not written). epi->D and epi->residual must be NULL; N a multiple of 32. The next GEMM takes
+ * s as its alpha. */
+int h3b_gemm_nvfp4_requant(const void* A, const uint8_t* sfa, const void* B, const uint8_t* sfb, int64_t M, int64_t N,
+                           int64_t K, const h3b_epilogue* epi, uint8_t* q, uint8_t* q_sf, const float* q_scale,
+                           cudaStream_t stream);
 
 /* ---------------------------------------------------------------------------------------------------------------
  * VSA coarse step and prologue, and the attention-output gate.

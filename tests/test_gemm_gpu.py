@@ -187,6 +187,36 @@ def test_nvfp4_gemm_residual_in_place(ops, M, N, K):
     assert rel(x.cpu().float(), ref) < TOL
 
 
+@pytest.mark.parametrize("M,N,K,headroom", [(300, 384, 512, 2.0), (4099, 1536, 1024, 2.0), (1000, 13824, 5120, 2.0),
+                                            (257, 576, 512, 0.25)])
+def test_nvfp4_requant_epilogue_vs_oracle(ops, M, N, K, headroom):
+    """The fc_in form: GEMM + bias + GELU-tanh with the output re-quantized to NVFP4 in the epilogue under a fixed
+    global scale s. The codes and block scales equal the oracle's block math applied to the bf16 output of the same
+    GEMM (h3b_gemm_nvfp4 with the same epilogue) under gs = 1/s; headroom 0.25 puts s below amax/2688, so the largest
+    blocks saturate (scale 448, codes +-6) in both."""
+    (qa, sfa, sa, qw, sfw, sw), _, _, _, _ = nvfp4_operands(ops, M, N, K, seed=M + 3 * N)
+    bias = (torch.randn(N, generator=torch.Generator().manual_seed(M)) * 0.1).bfloat16().to(DEV)
+    u = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    ops.gemm_nvfp4(qa, sfa, qw, sfw, u, alpha_dev=sa, scale_b=sw, bias=bias, act="gelu_tanh")
+    s = (u.float().abs().amax() * headroom / 2688.0).reshape(1).contiguous()
+    q = torch.full((M, N // 2), 0xEE, device=DEV, dtype=torch.uint8)
+    q_sf = torch.zeros(ops.sf_rows(M), N // 16, device=DEV, dtype=torch.uint8)
+    ops.gemm_nvfp4_requant(qa, sfa, qw, sfw, q, q_sf, s, alpha_dev=sa, scale_b=sw, bias=bias, act="gelu_tanh")
+    ops.check_status()
+    uf = u.float().cpu().numpy()
+    gs = np.float32(np.float32(1.0) / np.float32(s.item()))
+    codes, bits, _, _ = oq.nvfp4_blocks(uf, gs)
+    if headroom < 1:
+        assert (bits == 0x7E).any(), "the small global scale should saturate some block scales"
+    # the epilogue divides and multiplies with IEEE rounding (no fast math in the GEMM), like the oracle: bit-exact
+    np.testing.assert_array_equal(oq.unswizzle_sf(q_sf.cpu().numpy(), M, N // 16), bits)
+    np.testing.assert_array_equal(oq.unpack_nibbles(q.cpu().numpy()), codes)
+    # and the next GEMM reading q with alpha = s reproduces u to NVFP4's error level
+    deq = oq.dequant_nvfp4(q.cpu().numpy(), q_sf.cpu().numpy(), M, N, s.item())
+    if headroom >= 1:
+        assert rel(torch.from_numpy(deq), u.float().cpu()) < 0.12
+
+
 def test_nvfp4_config2_full_size_sampled_rows(ops):
     """BASELINE config 2 at full size (32768 x 13824 x 5120): the whole GEMM runs on the GPU; 64 sampled rows are
     checked against the dequantize-then-matmul oracle, plus a checksum of every row against the oracle's row sums."""

@@ -211,6 +211,34 @@ def test_f16_v_runner_equals_e4m3_v_runner(pkg):
     assert torch.equal(a.view(torch.int16), c.view(torch.int16))
 
 
+def test_static_ffn_requant_runner(pkg):
+    """ffn_requant="static": the first forward runs the per-row path (its output equals the default runner's bit for
+    bit) and records each block's fixed FFN global scale; later forwards quantize fc_in's output in its epilogue under
+    that scale. The result stays at the NVFP4 noise level of the per-row rule, and the sharded runner (the scale being
+    the maximum over ranks) equals one rank bit for bit."""
+    _, runner = pkg
+    m, x, ctx, temb, meta = make(pkg, blocks=2, grid=(7, 16, 16))
+    ref = runner.H3FastRunner(m).forward(x, temb, None, None, meta, context=ctx)
+    st = runner.H3FastRunner(m, ffn_requant="static")
+    first = st.forward(x, temb, None, None, meta, context=ctx)
+    torch.cuda.synchronize()
+    assert torch.equal(first.view(torch.int16), ref.view(torch.int16))
+    assert bool((st.ffn_scales > 0).all())
+    second = st.forward(x, temb, None, None, meta, context=ctx)
+    sharded = runner.H3FastRunner(m, runner.VirtualSeqParallel(2), ffn_requant="static")
+    sharded.forward(x, temb, None, None, meta, context=ctx)
+    third = sharded.forward(x, temb, None, None, meta, context=ctx)
+    torch.cuda.synchronize()
+    assert torch.equal(sharded.ffn_scales, st.ffn_scales)
+    assert torch.equal(third.view(torch.int16), second.view(torch.int16))
+    # two NVFP4 quantizations of the FFN intermediate (per-row vs fixed global scale) differ by about sqrt(2) times
+    # e2m1's relative noise (~0.09 each on this data), which is what the blocks' updates show
+    upd_ref, upd = (ref.float() - x.float()), (second.float() - x.float())
+    assert rel(upd, upd_ref) < 0.2, rel(upd, upd_ref)
+    with pytest.raises(ValueError):
+        runner.H3FastRunner(m, ffn_requant="per-tile")
+
+
 def test_forward_raises_on_an_overlong_selection(pkg):
     """The attention kernel holds at most 1024 selected key tiles per query tile. A longer list is not a fault: the
     kernel clamps it and records H3B_EINVAL in its status word, and forward raises instead of returning the truncated
