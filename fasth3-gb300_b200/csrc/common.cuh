@@ -203,6 +203,12 @@ __device__ __forceinline__ void fma2(float& a0, float& a1, float b0, float b1, f
       : "+f"(a0), "+f"(a1)
       : "f"(b0), "f"(b1), "f"(c0), "f"(c1));
 }
+// three-input maximum (sm_100 max.f32 with three sources)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
 // acc += d * d for a pair
 __device__ __forceinline__ void sq_acc2(float& acc0, float& acc1, float d0, float d1) {
   asm("{\n\t.reg .b64 a, d;\n\tmov.b64 a, {%0, %1};\n\tmov.b64 d, {%2, %3};\n\t"

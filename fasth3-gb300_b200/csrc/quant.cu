@@ -325,6 +325,178 @@ __global__ void __launch_bounds__(LnRowShape<C>::G, (LnRowShape<C>::G <= 128 ? 3
   }
 }
 
+// The shared-table form of the row kernel: one CTA per SM holding ln_groups() row groups of G threads, each group
+// working on its own rows with its own ring of kLnGroupStages bulk-copied row buffers and named barriers, so several
+// rows are in flight per SM while the adaLN table row -- the same for all tokens -- sits once in shared memory as
+// float32 pairs (1 + scale, shift), formed once per CTA exactly as the register form forms them. The arithmetic and
+// the summation order are those of layer_norm_quant_rows_kernel.
+template <int C>
+constexpr int ln_groups() {
+  return LnRowShape<C>::G <= 128 ? 6 : 4;
+}
+constexpr int kLnGroupStages = 2;
+template <int C>
+constexpr int ln_group_smem_bytes() {
+  return 2 * C * 4 + ln_groups<C>() * (kLnGroupStages * C * 2 + kLnGroupStages * 8 + 3 * 32 * 4);
+}
+
+__device__ __forceinline__ void bar_group(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+__device__ __forceinline__ bool bar_group_or(int id, int n, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+
+template <int C, bool FP4>
+__global__ void __launch_bounds__(LnRowShape<C>::G * ln_groups<C>(), 1)
+    layer_norm_quant_groups_kernel(const RowArgs a) {
+  using Sh = LnRowShape<C>;
+  constexpr int K = Sh::K, G = Sh::G, NW = Sh::NW, E = 8 * K, RG = ln_groups<C>();
+  constexpr uint32_t kRowBytes = C * 2;
+  extern __shared__ __align__(16) uint8_t ln_smem[];
+  // [4][C/8] float4: for pair p of chunk c, (1 + scale, 1 + scale, shift, shift) of columns 8c+2p, 8c+2p+1 -- a
+  // warp's reads of one pair index are contiguous
+  float4* tb = reinterpret_cast<float4*>(ln_smem);
+  const int grp = threadIdx.x / G, t = threadIdx.x - grp * G, lane = t & 31, w = t >> 5;
+  uint8_t* gbase = ln_smem + 8 * C + (size_t)grp * (kLnGroupStages * C * 2 + kLnGroupStages * 8 + 3 * 32 * 4);
+  bf16* ring = reinterpret_cast<bf16*>(gbase);
+  uint64_t* full = reinterpret_cast<uint64_t*>(gbase + (size_t)kLnGroupStages * kRowBytes);
+  float* red = reinterpret_cast<float*>(full + kLnGroupStages);  // [3][32]
+  const int bar_id = 1 + grp;
+  const int64_t step = (int64_t)gridDim.x * RG;
+  const int64_t first = (int64_t)blockIdx.x * RG + grp;
+  if (t == 0) {
+    for (int s = 0; s < kLnGroupStages; ++s) sm100::mbar_init(&full[s], 1);
+    sm100::fence_mbar_init();
+    for (int s = 0; s < kLnGroupStages; ++s) {
+      const int64_t r = first + s * step;
+      if (r < a.rows) {
+        sm100::mbar_arrive_expect_tx(&full[s], kRowBytes);
+        sm100::bulk_load(ring + (size_t)s * C, a.x + r * C, kRowBytes, &full[s]);
+      }
+    }
+  }
+  for (int c = threadIdx.x; c < C / 8; c += G * RG) {
+    float sc[8], sf[8];
+    load8_nc(a.scale + 8 * c, sc);
+    load8_nc(a.shift + 8 * c, sf);
+#pragma unroll
+    for (int p = 0; p < 4; ++p)
+      tb[p * (C / 8) + c] = make_float4(1.f + sc[2 * p], 1.f + sc[2 * p + 1], sf[2 * p], sf[2 * p + 1]);
+  }
+  // this thread's output offsets: codes / scale-byte columns of its chunks (the row part is added per row)
+  int sf_col[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) sf_col[k] = (int)sf_atom_offset(0, (t + G * k) >> 1, C / 16);
+  __syncthreads();
+  volatile int no_abort = 0;
+  uint32_t it = 0;
+  for (int64_t r = first; r < a.rows; r += step, ++it) {
+    const uint32_t s = it % kLnGroupStages;
+    const bool ok = sm100::mbar_wait_bounded(&full[s], (it / kLnGroupStages) & 1u, &no_abort, kRowWaitLimitNs);
+    float v[E];
+    const bf16* row = ring + (size_t)s * C;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      float f[8];
+      unpack8(*reinterpret_cast<const uint4*>(row + (t + G * k) * 8), f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[8 * k + i] = f[i];
+    }
+    const float ts = warp_allreduce<false>(ln_thread_sum(v));
+    if (lane == 0) red[w] = ts;
+    if (bar_group_or(bar_id, G, !ok)) {  // a row never arrived: record it, drain this group's copies, leave
+      if (t == 0) {
+        atomicExch(&g_rows_status, H3B_ETIMEOUT);
+        for (int j = 0; j < kLnGroupStages; ++j) {
+          if (r + j * step >= a.rows) break;
+          const uint32_t ij = it + j;
+          sm100::mbar_wait_bounded(&full[ij % kLnGroupStages], (ij / kLnGroupStages) & 1u, &no_abort,
+                                   kRowWaitLimitNs / 8);
+        }
+      }
+      return;
+    }
+    if (t == 0) {  // every thread of the group has read buffer s (before the barrier): refill it
+      const int64_t rn = r + kLnGroupStages * step;
+      if (rn < a.rows) {
+        sm100::fence_proxy_async_smem();
+        sm100::mbar_arrive_expect_tx(&full[s], kRowBytes);
+        sm100::bulk_load(ring + (size_t)s * C, a.x + rn * C, kRowBytes, &full[s]);
+      }
+    }
+    float tot = red[0];
+#pragma unroll
+    for (int q = 1; q < NW; ++q) tot += red[q];
+    const float mean = tot / C;
+#pragma unroll
+    for (int i = 0; i < E; i += 2) sub2(v[i], v[i + 1], mean, mean);
+    const float tq = warp_allreduce<false>(ln_thread_sumsq(v));
+    if (lane == 0) red[32 + w] = tq;
+    bar_group(bar_id, G);
+    float tot2 = red[32];
+#pragma unroll
+    for (int q = 1; q < NW; ++q) tot2 += red[32 + q];
+    const float rs = rsqrtf(tot2 / C + a.eps);
+    float cm[K];
+    float am = 0.f;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        const float4 ab = tb[(i / 2) * (C / 8) + t + G * k];
+        mul2(v[8 * k + i], v[8 * k + i + 1], rs, rs);
+        fma2(v[8 * k + i], v[8 * k + i + 1], ab.x, ab.y, ab.z, ab.w);
+      }
+      const float* u = v + 8 * k;
+      float m = fmax3(fabsf(u[0]), fabsf(u[1]), fabsf(u[2]));
+      m = fmax3(m, fabsf(u[3]), fabsf(u[4]));
+      m = fmax3(m, fabsf(u[5]), fabsf(u[6]));
+      m = fmaxf(m, fabsf(u[7]));
+      cm[k] = m;
+      am = fmaxf(am, m);
+    }
+    am = warp_allreduce<true>(am);
+    if (lane == 0) red[64 + w] = am;
+    bar_group(bar_id, G);
+    am = red[64];
+#pragma unroll
+    for (int q = 1; q < NW; ++q) am = fmaxf(am, red[64 + q]);
+    const float gscale = FP4 ? fmaxf(am / kFp4Range, kMinScaleFp4) : fmaxf(am / kFp8Max, kMinScaleFp8);
+    const float inv = 1.f / gscale;
+    uint8_t* hrow = a.h + r * (FP4 ? C / 2 : C);
+    uint8_t* sfrow = FP4 ? a.hsf + sf_atom_offset(r, 0, C / 16) : nullptr;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int chunk = t + G * k;
+      float* u = v + 8 * k;
+      if constexpr (FP4) {
+        const float vmax = fmaxf(cm[k], __shfl_xor_sync(0xffffffffu, cm[k], 1));
+        uint32_t bits;
+        const float mult = nvfp4_block_scale(vmax, inv, &bits);
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) mul2(u[i], u[i + 1], mult, mult);
+        const uint32_t lo = e2m1x4(u[0], u[1], u[2], u[3]);
+        const uint32_t hi = e2m1x4(u[4], u[5], u[6], u[7]);
+        *reinterpret_cast<uint32_t*>(hrow + chunk * 4) = lo | (hi << 16);
+        if ((t & 1) == 0) sfrow[sf_col[k]] = (uint8_t)bits;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) mul2(u[i], u[i + 1], inv, inv);
+        uint2 o;
+        o.x = e4m3x4(u[0], u[1], u[2], u[3]);
+        o.y = e4m3x4(u[4], u[5], u[6], u[7]);
+        *reinterpret_cast<uint2*>(hrow + chunk * 8) = o;
+      }
+    }
+    if (t == 0) a.hs[r] = gscale;
+  }
+}
+
 // LayerNorm with the gated residual branch in front (x + gate * (sy * y) written to xo, then normalized): one
 // warp per row, lane l owns the 8-element chunks l, l+32, l+64, ... (coalesced); the row is staged in shared memory
 // (bf16) by asynchronous copies. The row statistics follow the LayerNorm order above: lane l plays thread 32q + l of
@@ -492,6 +664,27 @@ __global__ void __launch_bounds__(ln_warps<C>() * 32, 1) layer_norm_quant_warp_k
   }
 }
 
+// Shared-table LayerNorm launch: one CTA per SM (fewer when there are fewer row groups' worth of rows).
+template <int C, bool FP4>
+int launch_ln_groups(const RowArgs& a, int sms, cudaStream_t st) {
+  constexpr int lsm = ln_group_smem_bytes<C>();
+  static PerDevice setup;
+  int done = 0;
+  if (int rc = setup.get([&](int* v) {
+        if (cudaFuncSetAttribute(layer_norm_quant_groups_kernel<C, FP4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 lsm) != cudaSuccess)
+          return set_error(H3B_ECUDA, "resid_norm_quant: cannot reserve %d bytes of shared memory", lsm);
+        *v = 1;
+        return H3B_OK;
+      }, &done))
+    return rc;
+  constexpr int RG = ln_groups<C>();
+  const int64_t need = (a.rows + RG - 1) / RG;
+  layer_norm_quant_groups_kernel<C, FP4>
+      <<<(unsigned)(need < sms ? need : sms), LnRowShape<C>::G * RG, lsm, st>>>(a);
+  return H3B_OK;
+}
+
 // Row-per-CTA LayerNorm launch: as many CTAs as are resident on the device (occupancy queried once per device).
 template <int C, bool FP4, bool IDX>
 int launch_ln_rows(const RowArgs& a, int sms, cudaStream_t st) {
@@ -557,8 +750,7 @@ int launch_resid_norm_quant(const RowArgs& a, bool branch, int norm, bool fp4, c
       if (int rc = fp4 ? launch_ln_rows<C, true, true>(a, sms, st) : launch_ln_rows<C, false, true>(a, sms, st))
         return rc;
     } else {
-      if (int rc = fp4 ? launch_ln_rows<C, true, false>(a, sms, st) : launch_ln_rows<C, false, false>(a, sms, st))
-        return rc;
+      if (int rc = fp4 ? launch_ln_groups<C, true>(a, sms, st) : launch_ln_groups<C, false>(a, sms, st)) return rc;
     }
 #undef H3B_LNQ
   }

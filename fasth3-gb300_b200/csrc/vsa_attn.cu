@@ -151,11 +151,6 @@ __device__ __forceinline__ float ex2(float x) {
 }
 
 // max of three floats in one instruction (sm_100)
-__device__ __forceinline__ float fmax3(float a, float b, float c) {
-  float d;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
 
 // 2^(s * coef + nb) for two keys: both exponent arguments by one paired fp32 fused multiply-add (sm_100), rounded to
 // f16 (s0 in the low half) and exponentiated in f16x2
