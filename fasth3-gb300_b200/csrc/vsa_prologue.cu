@@ -207,60 +207,83 @@ __global__ void __launch_bounds__(NWARP * 32, 2) prologue_kernel(const ProArgs a
         unpack4(valid ? *reinterpret_cast<const uint2*>(buf + (1 * TILE + i) * D + l * 4) : zero, kf);
         unpack4(valid ? *reinterpret_cast<const uint2*>(buf + (2 * TILE + i) * D + l * 4) : zero, vf);
         float qo[4], ko[4];
+        uint2 qw, kw, vw;  // the bf16 roundings, packed (what goes back into the buffer)
         if constexpr (ROWS) {
+          // the reference's per-element operations (h3fast.cu:376-510) in the same order, two lanes of work per
+          // paired fp32 instruction: q with k, or neighbouring dims
           const float s = s1v[u];
+#pragma unroll
+          for (int j = 0; j < 4; j += 2) {
+            mul2(qf[j], qf[j + 1], s, s);
+            mul2(kf[j], kf[j + 1], s, s);
+            mul2(vf[j], vf[j + 1], s, s);
+          }
           float sumq = 0.f, sumk = 0.f;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            qf[j] *= s;
-            kf[j] *= s;
-            vf[j] *= s;
-            sumq += qf[j] * qf[j];
-            sumk += kf[j] * kf[j];
-          }
+          for (int j = 0; j < 4; ++j) sq_acc2(sumq, sumk, qf[j], kf[j]);
 #pragma unroll
           for (int o = 16; o; o >>= 1) {
-            sumq += __shfl_xor_sync(0xffffffffu, sumq, o);
-            sumk += __shfl_xor_sync(0xffffffffu, sumk, o);
+            const float tq = __shfl_xor_sync(0xffffffffu, sumq, o), tk = __shfl_xor_sync(0xffffffffu, sumk, o);
+            add2(sumq, sumk, tq, tk);
           }
           const float rq_ = rsqrtf(sumq / D + a.eps), rk_ = rsqrtf(sumk / D + a.eps);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            qf[j] *= rq_ * wqv[j];
-            kf[j] *= rk_ * wkv[j];
+          for (int j = 0; j < 4; j += 2) {
+            float tq0 = rq_, tq1 = rq_, tk0 = rk_, tk1 = rk_;
+            mul2(tq0, tq1, wqv[j], wqv[j + 1]);
+            mul2(tk0, tk1, wkv[j], wkv[j + 1]);
+            mul2(qf[j], qf[j + 1], tq0, tq1);
+            mul2(kf[j], kf[j + 1], tk0, tk1);
           }
+          // rotate-half RoPE: x * cos + sign * partner * sin; sign * sin is exact, so it is applied to the table
           float c[4] = {1.f, 1.f, 1.f, 1.f}, sn[4] = {0.f, 0.f, 0.f, 0.f};
           if (rot) {
             unpack4(cr[u], c);
             unpack4(sr[u], sn);
           }
+          float qr[4], kr[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const float qr = __shfl_sync(0xffffffffu, qf[j], partner), kr = __shfl_sync(0xffffffffu, kf[j], partner);
-            qo[j] = to_bf16_and_back(qf[j] * c[j] + sign * qr * sn[j]);
-            ko[j] = to_bf16_and_back(kf[j] * c[j] + sign * kr * sn[j]);
-            vf[j] = to_bf16_and_back(vf[j]);
+            qr[j] = __shfl_sync(0xffffffffu, qf[j], partner);
+            kr[j] = __shfl_sync(0xffffffffu, kf[j], partner);
+            sn[j] *= sign;
           }
+#pragma unroll
+          for (int j = 0; j < 4; j += 2) {
+            mul2(qr[j], qr[j + 1], sn[j], sn[j + 1]);
+            mul2(kr[j], kr[j + 1], sn[j], sn[j + 1]);
+            fma2(qf[j], qf[j + 1], c[j], c[j + 1], qr[j], qr[j + 1]);
+            fma2(kf[j], kf[j + 1], c[j], c[j + 1], kr[j], kr[j + 1]);
+          }
+          qw = make_uint2(pack_bf16x2(qf[0], qf[1]), pack_bf16x2(qf[2], qf[3]));
+          kw = make_uint2(pack_bf16x2(kf[0], kf[1]), pack_bf16x2(kf[2], kf[3]));
+          vw = make_uint2(pack_bf16x2(vf[0], vf[1]), pack_bf16x2(vf[2], vf[3]));
+          unpack4(qw, qo);
+          unpack4(kw, ko);
+          unpack4(vw, vf);
         } else {
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             qo[j] = qf[j];
             ko[j] = kf[j];
           }
+          qw = pack4(qo);
+          kw = pack4(ko);
+          vw = pack4(vf);
         }
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          pq[j] += qo[j];
-          pk[j] += ko[j];
-          pv[j] += vf[j];
-          qmax = fmaxf(qmax, fabsf(qo[j]));
-          kmax = fmaxf(kmax, fabsf(ko[j]));
-          vmax = fmaxf(vmax, fabsf(vf[j]));
+        for (int j = 0; j < 4; j += 2) {
+          add2(pq[j], pq[j + 1], qo[j], qo[j + 1]);
+          add2(pk[j], pk[j + 1], ko[j], ko[j + 1]);
+          add2(pv[j], pv[j + 1], vf[j], vf[j + 1]);
+          qmax = fmax3(qmax, fabsf(qo[j]), fabsf(qo[j + 1]));
+          kmax = fmax3(kmax, fabsf(ko[j]), fabsf(ko[j + 1]));
+          vmax = fmax3(vmax, fabsf(vf[j]), fabsf(vf[j + 1]));
         }
         if (valid) {
-          *reinterpret_cast<uint2*>(buf + (0 * TILE + i) * D + l * 4) = pack4(qo);
-          *reinterpret_cast<uint2*>(buf + (1 * TILE + i) * D + l * 4) = pack4(ko);
-          *reinterpret_cast<uint2*>(buf + (2 * TILE + i) * D + l * 4) = pack4(vf);
+          *reinterpret_cast<uint2*>(buf + (0 * TILE + i) * D + l * 4) = qw;
+          *reinterpret_cast<uint2*>(buf + (1 * TILE + i) * D + l * 4) = kw;
+          *reinterpret_cast<uint2*>(buf + (2 * TILE + i) * D + l * 4) = vw;
         }
       }
 #pragma unroll
@@ -269,12 +292,31 @@ __global__ void __launch_bounds__(NWARP * 32, 2) prologue_kernel(const ProArgs a
         sp[1][w][l * 4 + j] = pk[j];
         sp[2][w][l * 4 + j] = pv[j];
       }
-      vmax = block_allreduce<NWARP, true>(vmax, red);
+      // the tile maxima (V, and Q/K with per-tile scales): warp butterflies, one staging round
+      vmax = warp_allreduce<true>(vmax);
+      if constexpr (TILE_QK) {
+        qmax = warp_allreduce<true>(qmax);
+        kmax = warp_allreduce<true>(kmax);
+      }
+      if (l == 0) {
+        red[w] = vmax;
+        red[NWARP + w] = qmax;
+        red[2 * NWARP + w] = kmax;
+      }
+      __syncthreads();
+      vmax = red[0];
+#pragma unroll
+      for (int ww = 1; ww < NWARP; ++ww) vmax = fmaxf(vmax, red[ww]);
       const float svb = fmaxf(vmax / kFp8Max, 1e-30f);
       float inv_q = a.inv_sq, inv_k = a.inv_sk;
       if constexpr (TILE_QK) {
-        qmax = block_allreduce<NWARP, true>(qmax, red);
-        kmax = block_allreduce<NWARP, true>(kmax, red);
+        qmax = red[NWARP];
+        kmax = red[2 * NWARP];
+#pragma unroll
+        for (int ww = 1; ww < NWARP; ++ww) {
+          qmax = fmaxf(qmax, red[NWARP + ww]);
+          kmax = fmaxf(kmax, red[2 * NWARP + ww]);
+        }
         const float qk_max = QK_I8 ? 127.f : kFp8Max;
         const float sqb = fmaxf(qmax / qk_max, 1e-30f), skb = fmaxf(kmax / qk_max, 1e-30f);
         inv_q = 1.f / sqb;
@@ -299,16 +341,20 @@ __global__ void __launch_bounds__(NWARP * 32, 2) prologue_kernel(const ProArgs a
         unpack4(*reinterpret_cast<const uint2*>(buf + (0 * TILE + i) * D + l * 4), qv);
         unpack4(*reinterpret_cast<const uint2*>(buf + (1 * TILE + i) * D + l * 4), kv);
         unpack4(*reinterpret_cast<const uint2*>(buf + (2 * TILE + i) * D + l * 4), vv);
-        if constexpr (QK_I8) {
-          *reinterpret_cast<uint32_t*>(a.qb + dst) = s8x4(qv[0] * inv_q, qv[1] * inv_q, qv[2] * inv_q, qv[3] * inv_q);
-          *reinterpret_cast<uint32_t*>(a.kb + dst) = s8x4(kv[0] * inv_k, kv[1] * inv_k, kv[2] * inv_k, kv[3] * inv_k);
-        } else {
-          *reinterpret_cast<uint32_t*>(a.qb + dst) =
-              e4m3x4(qv[0] * inv_q, qv[1] * inv_q, qv[2] * inv_q, qv[3] * inv_q);
-          *reinterpret_cast<uint32_t*>(a.kb + dst) =
-              e4m3x4(kv[0] * inv_k, kv[1] * inv_k, kv[2] * inv_k, kv[3] * inv_k);
+#pragma unroll
+        for (int j = 0; j < 4; j += 2) {
+          mul2(qv[j], qv[j + 1], inv_q, inv_q);
+          mul2(kv[j], kv[j + 1], inv_k, inv_k);
+          mul2(vv[j], vv[j + 1], inv_v, inv_v);
         }
-        const uint32_t vcodes = e4m3x4(vv[0] * inv_v, vv[1] * inv_v, vv[2] * inv_v, vv[3] * inv_v);
+        if constexpr (QK_I8) {
+          *reinterpret_cast<uint32_t*>(a.qb + dst) = s8x4(qv[0], qv[1], qv[2], qv[3]);
+          *reinterpret_cast<uint32_t*>(a.kb + dst) = s8x4(kv[0], kv[1], kv[2], kv[3]);
+        } else {
+          *reinterpret_cast<uint32_t*>(a.qb + dst) = e4m3x4(qv[0], qv[1], qv[2], qv[3]);
+          *reinterpret_cast<uint32_t*>(a.kb + dst) = e4m3x4(kv[0], kv[1], kv[2], kv[3]);
+        }
+        const uint32_t vcodes = e4m3x4(vv[0], vv[1], vv[2], vv[3]);
         if (a.v16)
           *reinterpret_cast<uint2*>(a.vb + 2 * dst) = e4m3x4_to_f16x4(vcodes);
         else
