@@ -246,7 +246,10 @@ __device__ __forceinline__ bool warp_wait_bounded(uint64_t* bar, uint32_t parity
   return false;
 }
 
-template <bool QKI8, bool VF16>
+// SH: the two query tiles of an item share one key list (the list of tile 2p; cross-attention to text, dense
+// layers): each step loads one K and one V tile, and S and PV run as single M = 128 MMAs over both tiles (full
+// datapath; row r of the pair in TMEM lane r, tile 2p in lanes 0-63) instead of two M = 64 streams.
+template <bool QKI8, bool VF16, bool SH = false>
 __global__ void __launch_bounds__(THREADS, 1)
     vsa_fp8_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, const AttnArgs a) {
@@ -342,7 +345,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       } else {
 #pragma unroll
         for (int s = 0; s < 2; ++s) {
-          const int t = s ? t1 : t0;
+          const int t = (s && !SH) ? t1 : t0;
           const int want = min(max(a.num[(size_t)h * a.n_q_ext + t], 0), a.idx_ld);
           n[s] = min(want, L_MAX);
           if (want > L_MAX && lane == 0) atomicExch(&g_attn_status, H3B_EINVAL);
@@ -370,7 +373,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             tma_load_3d(&sm.q[s][0], &tmQ, 0, (t % a.tpc_q) * TILE, (t / a.tpc_q) * a.heads + h, &sm.q_full);
           }
           for (int j = 0; j < U && ok; ++j) {
-            const bool has0 = j < n[0], has1 = j < n[1];
+            const bool has0 = j < n[0], has1 = !SH && j < n[1];  // shared lists: one K and one V tile per step
             const uint32_t bytes = (has0 ? TILE * D : 0) + (has1 ? TILE * D : 0);
             if (!mbar_wait_bounded(&sm.k_empty[kst], ((k_phase >> kst) & 1u) ^ 1u, abort_flag, kLimitNs)) {
               fail();
@@ -417,8 +420,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     // -------------------------------------------------------------- MMA issuers: warp 1 even steps, warp 2 odd steps
     if (lane == 0) {
       const int w = warp - 1;
-      const uint32_t idesc_s = QKI8 ? idesc_s8(TILE, TILE) : idesc_mn(TILE, TILE, false);
-      const uint32_t idesc_pv = idesc_mn(TILE, D, true);
+      constexpr int MQ = SH ? 2 * TILE : TILE;  // query rows per MMA
+      const uint32_t idesc_s = QKI8 ? idesc_s8(MQ, TILE) : idesc_mn(MQ, TILE, false);
+      const uint32_t idesc_pv = idesc_mn(MQ, D, true);
       uint32_t list_phase = 0, q_phase = 0, s_phase = 0, p_phase = 0, o_phase = 0;
       uint32_t gbase = 0;  // steps of all earlier items: step j is K-ring use gbase + j
       bool ok = true;
@@ -454,7 +458,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc_fence_after();
 #pragma unroll
             for (int s = 0; s < 2; ++s) {
-              if (js >= (s ? n1 : n0)) continue;
+              if (js >= (s ? n1 : n0) || (SH && s)) continue;
               const uint32_t lo = s ? LANE_B : 0u;
               const uint64_t dk = desc_k_sw128(smem_addr(&sm.k[kst][s][0]));
               const uint64_t dq = s ? dq1 : dq0;
@@ -494,7 +498,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           tc_fence_after();
 #pragma unroll
           for (int s = 0; s < 2; ++s) {
-            if (j >= (s ? n1 : n0)) continue;
+            if (j >= (s ? n1 : n0) || (SH && s)) continue;
             const uint32_t lo = s ? LANE_B : 0u;
             const uint64_t dv =
                 desc_mn_sw128(smem_addr(VF16 ? v16_slot(sm, vstage, s) : vconv(sm, w, s)), TILE * 128);
@@ -525,8 +529,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     // -------------------------------------------------------------- softmax (steps of parity w) + epilogue
     const int w = (warp - 3) >> 2;               // warpgroup: 0 = even steps, 1 = odd steps
     const int q4 = warp & 3;                     // TMEM lane quarter this warp may access
-    const int tsel = lane >> 4;                  // 0: query tile t0 (lanes 0-15), 1: t1 (lanes 16-31)
-    const int rt = 16 * q4 + (lane & 15);        // row within the query tile
+    // query tile and row of this thread's TMEM lane: M = 64 streams put tile t0 in lanes 0-15 and t1 in lanes 16-31
+    // of each quarter; an M = 128 MMA (shared lists) puts t0 in lanes 0-63 and t1 in lanes 64-127
+    const int tsel = SH ? (q4 >> 1) : (lane >> 4);
+    const int rt = SH ? 32 * (q4 & 1) + lane : 16 * q4 + (lane & 15);
     const int tl = q4 * 32 + lane;               // TMEM lane
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
     uint32_t list_phase = 0, s_phase = 0, ml_phase = 0, o_phase = 0;
@@ -662,7 +668,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           uint4 raw[2][4];
 #pragma unroll
           for (int s = 0; s < 2; ++s) {
-            if (j >= (s ? n1 : n0)) continue;  // warpgroup-uniform
+            if (j >= (s ? n1 : n0) || (SH && s)) continue;  // warpgroup-uniform
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const int key = (lane & 7) + 8 * (q4 + 4 * (i & 1)), c = (lane >> 3) + 4 * (i >> 1);
@@ -671,7 +677,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
 #pragma unroll
           for (int s = 0; s < 2; ++s) {
-            if (j >= (s ? n1 : n0)) continue;
+            if (j >= (s ? n1 : n0) || (SH && s)) continue;
             uint8_t* dst = vconv(sm, w, s);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -861,7 +867,7 @@ using namespace h3b;
 
 namespace h3b {
 namespace {
-int vsa_launch(const h3b_vsa_args* x, const uint8_t* u_mem, bool v16, cudaStream_t stream);
+int vsa_launch(const h3b_vsa_args* x, const uint8_t* u_mem, bool v16, cudaStream_t stream, bool shared = false);
 }  // namespace
 }  // namespace h3b
 
@@ -873,6 +879,16 @@ extern "C" int h3b_vsa_fp8_ex(const h3b_vsa_args* x, cudaStream_t stream) {
 extern "C" int h3b_vsa_fp8_ex_v16(const h3b_vsa_args* x, cudaStream_t stream) {
   clear_error();
   return h3b::vsa_launch(x, nullptr, true, stream);
+}
+
+extern "C" int h3b_vsa_fp8_shared(const h3b_vsa_args* x, cudaStream_t stream) {
+  clear_error();
+  return h3b::vsa_launch(x, nullptr, false, stream, true);
+}
+
+extern "C" int h3b_vsa_fp8_shared_v16(const h3b_vsa_args* x, cudaStream_t stream) {
+  clear_error();
+  return h3b::vsa_launch(x, nullptr, true, stream, true);
 }
 
 extern "C" int h3b_vsa_pair(const h3b_vsa_args* x, const uint8_t* u_mem, cudaStream_t stream) {
@@ -889,8 +905,9 @@ extern "C" int h3b_vsa_pair_v16(const h3b_vsa_args* x, const uint8_t* u_mem, cud
 
 namespace h3b {
 namespace {
-int vsa_launch(const h3b_vsa_args* x, const uint8_t* u_mem, bool v16, cudaStream_t stream) {
+int vsa_launch(const h3b_vsa_args* x, const uint8_t* u_mem, bool v16, cudaStream_t stream, bool shared) {
   H3B_REQUIRE(x, "vsa_fp8: null argument block");
+  H3B_REQUIRE(!shared || !x->qk_int8, "vsa_fp8_shared: E4M3 QK^T only");
   H3B_REQUIRE(x->q && x->k && x->v && x->idx && x->num && x->vbs_q && x->vbs_kv && x->vs && x->vs_head && x->out,
               "vsa_fp8: null pointer");
   H3B_REQUIRE((x->qs == nullptr) == (x->ks == nullptr), "vsa_fp8: give both or neither per-tile Q/K scales");
@@ -917,11 +934,12 @@ int vsa_launch(const h3b_vsa_args* x, const uint8_t* u_mem, bool v16, cudaStream
              static_cast<bf16*>(x->out), x->lse, x->heads, x->n_q_ext, x->n_kv, x->idx_ld, x->q_scale_ld,
              x->kv_scale_ld, tpc_q, tpc_kv, x->rows_chunk_q, x->heads * (x->n_q_ext / 2), u_mem};
   const int smem = (int)sizeof(Smem) + 1024;
-  auto kern = x->qk_int8 ? (v16 ? vsa_fp8_kernel<true, true> : vsa_fp8_kernel<true, false>)
-                         : (v16 ? vsa_fp8_kernel<false, true> : vsa_fp8_kernel<false, false>);
-  static PerDevice setup[4];  // the shared-memory reservation per instantiation and device; the value is the SM count
+  auto kern = shared ? (v16 ? vsa_fp8_kernel<false, true, true> : vsa_fp8_kernel<false, false, true>)
+             : x->qk_int8 ? (v16 ? vsa_fp8_kernel<true, true> : vsa_fp8_kernel<true, false>)
+                          : (v16 ? vsa_fp8_kernel<false, true> : vsa_fp8_kernel<false, false>);
+  static PerDevice setup[6];  // the shared-memory reservation per instantiation and device; the value is the SM count
   int sms = 0;
-  if (int rc = setup[(x->qk_int8 ? 1 : 0) + (v16 ? 2 : 0)].get([&](int* v) {
+  if (int rc = setup[shared ? 4 + (v16 ? 1 : 0) : (x->qk_int8 ? 1 : 0) + (v16 ? 2 : 0)].get([&](int* v) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
           return set_error(H3B_ECUDA, "vsa_fp8: cannot reserve %d bytes of shared memory", smem);
         *v = current_sms();

@@ -442,9 +442,11 @@ def vsa_pair(q8, k8, v8, u_idx, u_mem, u_num, vbs, qk_coef, v_scale_blk, v_scale
 
 def vsa_fp8_ex(q, k, v, out, idx, num, vbs_q, vbs_kv, vs, vs_head, qk_coef, heads, n_q_ext, n_kv, rows_chunk_q,
                rows_chunk_kv, chunks_q=1, chunks_kv=1, qs=None, ks=None, lse=None, idx_ld=None, q_scale_ld=None,
-               kv_scale_ld=None, qk_int8: bool = False, _u_mem=None):
+               kv_scale_ld=None, qk_int8: bool = False, _u_mem=None, shared_lists: bool = False):
     """General FP8 block-sparse attention (h3b_vsa_fp8_ex): chunked [chunks * heads, rows_chunk, 128] layouts (the
-    all-to-all layout of sequence parallelism) and separate key/value tiles (cross-attention)."""
+    all-to-all layout of sequence parallelism) and separate key/value tiles (cross-attention). ``shared_lists``: the
+    list of each even query tile applies to it and the next tile (h3b_vsa_fp8_shared: one M=128 MMA stream per pair;
+    cross-attention, dense layers)."""
     import ctypes
 
     from ._lib import VsaArgs
@@ -463,6 +465,8 @@ def vsa_fp8_ex(q, k, v, out, idx, num, vbs_q, vbs_kv, vs, vs_head, qk_coef, head
     v16 = "_v16" if v.dtype == torch.float16 else ""  # f16 V (decoded E4M3 values) or E4M3 codes
     if _u_mem is not None:
         call("h3b_vsa_pair" + v16, ctypes.byref(x), _p(_u_mem), _stream(q))
+    elif shared_lists:
+        call("h3b_vsa_fp8_shared" + v16, ctypes.byref(x), _stream(q))
     else:
         call("h3b_vsa_fp8_ex" + v16, ctypes.byref(x), _stream(q))
     return out

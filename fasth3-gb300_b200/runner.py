@@ -228,9 +228,10 @@ class H3FastRunner:
             raise ValueError(f"ffn_requant must be 'rows' or 'static', not {ffn_requant!r}")
         self.ffn_requant = ffn_requant
         self.ffn_headroom = 2.0
-        # V tiles as E4M3 codes converted by the attention kernel on every use (default: half the bytes in the
-        # prologue's writes and the sequence-parallel exchange), or as f16 holding the E4M3 values (decoded once by
-        # the prologue, loaded by the PV MMAs as is); the results are bit-identical and the attention time equal
+        # self-attention V tiles as E4M3 codes converted by the attention kernel on every use (default: half the bytes
+        # in the prologue's writes and the sequence-parallel exchange), or as f16 holding the E4M3 values (decoded
+        # once by the prologue, loaded by the PV MMAs as is); the results are bit-identical and the attention time
+        # equal. The cross-attention's text V is always f16.
         self.v_dtype = torch.float16 if v_f16 else torch.uint8
         self.blocks = list(model.transformer_blocks)
         cfg = model.config
@@ -432,7 +433,9 @@ class H3FastRunner:
         row0 = torch.arange(n_txt, device=dev, dtype=torch.int32) * TILE
         vbs = torch.full((n_txt,), TILE, device=dev, dtype=torch.int32)
         kb = torch.zeros(len(self.blocks), H, L, D, device=dev, dtype=torch.uint8)
-        vb = torch.zeros(len(self.blocks), H, L, D, device=dev, dtype=self.v_dtype)
+        # text V always as f16 holding the E4M3 values (bit-identical results; a few MB per block, and the
+        # cross-attention's PV MMAs load it as is instead of converting every use)
+        vb = torch.zeros(len(self.blocks), H, L, D, device=dev, dtype=torch.float16)
         ks = torch.zeros(len(self.blocks), H, n_txt, device=dev, dtype=torch.float32)
         vs = torch.zeros_like(ks)
         vs_head = torch.zeros(len(self.blocks), H, device=dev, dtype=torch.float32)
@@ -649,7 +652,7 @@ class H3FastRunner:
             ops.vsa_fp8_ex(b["cqb"], txt["kb"][i], txt["vb"][i], b["cob"], b["cidx"], b["cnum"], b["vbs"],
                            txt["vbs"], txt["vs"][i], txt["vs_head"][i], sm_scale * LOG2E, H, st.n_local, txt["n"],
                            st.rows_pad, txt["L"], qs=b["cqs"], ks=txt["ks"][i], idx_ld=txt["n"],
-                           q_scale_ld=st.n_local, kv_scale_ld=txt["n"])
+                           q_scale_ld=st.n_local, kv_scale_ld=txt["n"], shared_lists=True)
             ops.attn_gate_quant(b["cob"], None, None, None, b["slot"], st.n_local, TILE, self._q(b["a"]),
                                 b["a_sf"], b["as"], R)
             self._t(i, "cross_attn", st, cob=b["cob"], a=b["a"], a_sf=b["a_sf"], sa=b["as"])

@@ -312,6 +312,13 @@ int h3b_vsa_fp8_ex_v16(const h3b_vsa_args* args, cudaStream_t stream);
 int h3b_vsa_pair(const h3b_vsa_args* args, const uint8_t* u_mem, cudaStream_t stream);
 /* h3b_vsa_pair with f16 V (as h3b_vsa_fp8_ex_v16). */
 int h3b_vsa_pair_v16(const h3b_vsa_args* args, const uint8_t* u_mem, cudaStream_t stream);
+/* h3b_vsa_fp8_ex for key lists shared by each pair of query tiles (no counterpart in the reference, whose
+ * cross-attention is a dense FlashAttention call): the list of query tile 2p (idx/num rows of the even tile) applies
+ * to tiles 2p and 2p+1, as for cross-attention to text tokens or a dense layer. One K and one V tile per step serve
+ * both query tiles, and S = Q K^T and O += P V run as M = 128 MMAs over the pair. Same arguments and outputs as
+ * h3b_vsa_fp8_ex; qk_int8 must be 0. The _v16 form takes f16 V like h3b_vsa_fp8_ex_v16. */
+int h3b_vsa_fp8_shared(const h3b_vsa_args* args, cudaStream_t stream);
+int h3b_vsa_fp8_shared_v16(const h3b_vsa_args* args, cudaStream_t stream);
 /* Status word of the attention kernel's bounded waits (0 = none); reset != 0 clears it. Synchronizes the device. */
 int h3b_vsa_status(int* status, int reset);
 

@@ -511,8 +511,10 @@ def test_vsa_fp8_chunked_layout_matches_plain(ops):
     assert torch.equal(out.permute(1, 0, 2, 3).reshape(heads, rows, 128), plain)
 
 
-def test_vsa_fp8_cross_attention_dense_text(ops):
-    """Cross-attention: 600 query rows (10 tiles) over 512 text keys (8 tiles), every tile selected: dense attention."""
+@pytest.mark.parametrize("shared", [False, True])
+def test_vsa_fp8_cross_attention_dense_text(ops, shared):
+    """Cross-attention: 600 query rows (10 tiles) over 512 text keys (8 tiles), every tile selected: dense attention,
+    as two M=64 streams with per-tile lists or (shared) as one M=128 stream per pair of query tiles."""
     heads, n_q, n_kv = 3, 10, 8
     g = torch.Generator().manual_seed(61)
     q = torch.randn(heads, n_q * 64, 128, generator=g)
@@ -535,8 +537,10 @@ def test_vsa_fp8_cross_attention_dense_text(ops):
     sm = 1.0 / math.sqrt(128)
     dv = lambda t: t.to(DEV)  # noqa: E731
     ops.vsa_fp8_ex(dv(q8), dv(k8), dv(v8), out, dv(idx), dv(num), dv(vbs_q), dv(vbs_kv), dv(vs), dv(vs.amax(1)),
-                   sm * math.log2(math.e), heads, n_q, n_kv, n_q * 64, n_kv * 64, qs=dv(qs), ks=dv(ks))
+                   sm * math.log2(math.e), heads, n_q, n_kv, n_q * 64, n_kv * 64, qs=dv(qs), ks=dv(ks),
+                   shared_lists=shared)
     torch.cuda.synchronize()
+    ops.check_status()
     deq = lambda c, s, n: (c.view(torch.float8_e4m3fn).float().view(heads, n, 64, 128)  # noqa: E731
                            * s[:, :, None, None]).view(heads, n * 64, 128).double()
     qd, kd, vd = deq(q8, qs, n_q), deq(k8, ks, n_kv), deq(v8, vs, n_kv)
@@ -545,6 +549,44 @@ def test_vsa_fp8_cross_attention_dense_text(ops):
     err = float((out.cpu().double()[:, :rows] - ref[:, :rows]).norm() / ref[:, :rows].norm())
     assert err < 1e-2
     assert (out.cpu()[:, rows:] == 0).all()  # rows past vbs_q are not written (buffer was zero)
+
+
+def test_vsa_shared_lists_match_per_tile_streams(ops):
+    """The shared-list kernel (one K/V tile per step, M=128 MMAs over a pair of query tiles) against the per-tile
+    kernel given the same list for both tiles, E4M3 and f16 V, on cross-attention geometry with 40 heads and a sparse
+    shared selection: the same operands reach the tensor cores and every softmax step is the same, so the outputs agree
+    to the accumulation order inside the MMAs (rel 1e-3; equal in practice)."""
+    heads, n_q, n_kv, k = 40, 32, 16, 6
+    g = torch.Generator().manual_seed(71)
+    q8 = torch.randn(heads, n_q * 64, 128, generator=g).mul(40).clamp(-448, 448).to(torch.float8_e4m3fn)
+    k8 = torch.randn(heads, n_kv * 64, 128, generator=g).mul(40).clamp(-448, 448).to(torch.float8_e4m3fn)
+    v8 = torch.randn(heads, n_kv * 64, 128, generator=g).mul(40).clamp(-448, 448).to(torch.float8_e4m3fn)
+    qs = torch.rand(heads, n_q, generator=g) * 0.01 + 0.005
+    ks = torch.rand(heads, n_kv, generator=g) * 0.01 + 0.005
+    vs = torch.rand(heads, n_kv, generator=g) * 0.01 + 0.005
+    # each pair of query tiles shares one ascending random selection of k key tiles
+    sel = torch.stack([torch.randperm(n_kv, generator=g)[:k].sort().values for _ in range(heads * n_q // 2)])
+    idx = sel.view(heads, n_q // 2, 1, k).expand(heads, n_q // 2, 2, k).reshape(heads, n_q, k).int().contiguous()
+    num = torch.full((heads, n_q), k, dtype=torch.int32)
+    vbs_q = torch.full((n_q,), 64, dtype=torch.int32)
+    vbs_kv = torch.full((n_kv,), 64, dtype=torch.int32)
+    vbs_kv[3] = 40  # a partial key tile
+    dv = lambda t: t.to(DEV)  # noqa: E731
+    outs = {}
+    for v16 in (False, True):
+        vv = v8.float().half() if v16 else v8.view(torch.uint8)
+        for shared in (False, True):
+            out = torch.zeros(heads, n_q * 64, 128, device=DEV, dtype=torch.bfloat16)
+            ops.vsa_fp8_ex(dv(q8.view(torch.uint8)), dv(k8.view(torch.uint8)), dv(vv), out, dv(idx), dv(num),
+                           dv(vbs_q), dv(vbs_kv), dv(vs), dv(vs.amax(1)), 0.127, heads, n_q, n_kv, n_q * 64,
+                           n_kv * 64, qs=dv(qs), ks=dv(ks), idx_ld=k, shared_lists=shared)
+            outs[(v16, shared)] = out
+    torch.cuda.synchronize()
+    ops.check_status()
+    for v16 in (False, True):
+        a, b = outs[(v16, False)].double(), outs[(v16, True)].double()
+        assert torch.isfinite(b).all()
+        assert float((a - b).norm() / a.norm()) < 1e-3, v16
 
 
 # ------------------------------------------------------------------------------------------------ pair form (f3)
