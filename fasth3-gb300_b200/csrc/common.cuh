@@ -209,6 +209,13 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
 }
+// acc += x * y for a pair, IEEE rounding without flush to zero (one correctly rounded fused multiply-add per lane)
+__device__ __forceinline__ void fma2_acc_rn(float& acc0, float& acc1, float x0, float x1, float y0, float y1) {
+  asm("{\n\t.reg .b64 a, x, y;\n\tmov.b64 a, {%0, %1};\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\t"
+      "fma.rn.f32x2 a, x, y, a;\n\tmov.b64 {%0, %1}, a;\n\t}"
+      : "+f"(acc0), "+f"(acc1)
+      : "f"(x0), "f"(x1), "f"(y0), "f"(y1));
+}
 // acc += d * d for a pair
 __device__ __forceinline__ void sq_acc2(float& acc0, float& acc1, float d0, float d1) {
   asm("{\n\t.reg .b64 a, d;\n\tmov.b64 a, {%0, %1};\n\tmov.b64 d, {%2, %3};\n\t"

@@ -30,7 +30,10 @@ __global__ void __launch_bounds__(256) scores_kernel(const float* __restrict__ q
   const int i0 = blockIdx.y * SB, j0 = blockIdx.x * SB;
   const float* qh = qp + (size_t)h * n * D;
   const float* kh = kp + (size_t)h * n * D;
-  const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
+  // thread (ty, tx) owns rows 8ty.. and columns 8tx.. of the block; a warp covers 4 values of ty and 8 of tx (a 32 x 64
+  // sub-block), so its shared-memory reads per d touch 32 q and 64 k values (one wavefront each) instead of 16 and 128
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ty = (warp >> 1) * 4 + (lane >> 3), tx = (warp & 1) * 8 + (lane & 7);
   float acc[8][8];
 #pragma unroll
   for (int a = 0; a < 8; ++a)
@@ -63,7 +66,7 @@ __global__ void __launch_bounds__(256) scores_kernel(const float* __restrict__ q
 #pragma unroll
       for (int a = 0; a < 8; ++a)
 #pragma unroll
-        for (int b = 0; b < 8; ++b) acc[a][b] = __fmaf_rn(av[a], bv[b], acc[a][b]);
+        for (int b = 0; b < 8; b += 2) fma2_acc_rn(acc[a][b], acc[a][b + 1], av[a], av[a], bv[b], bv[b + 1]);
     }
     __syncthreads();
   }
