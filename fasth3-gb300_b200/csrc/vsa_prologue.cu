@@ -100,6 +100,65 @@ __device__ __forceinline__ uint32_t s8x4(float a, float b, float c, float d) {
   return one(a) | (one(b) << 8) | (one(c) << 16) | (one(d) << 24);
 }
 
+// One row of the q/k/v row form, per lane 4 dims of q, k and v: the deferred row scale, per-head RMSNorm of q and k
+// with weights (warp butterfly over the 128 dims), rotate-half RoPE on the first 96 dims, bf16 rounding. The
+// reference's per-element operations (h3fast.cu:376-510) in the same order, two lanes of work per paired fp32
+// instruction (q with k, or neighbouring dims); sign * sin is exact, so the sign is applied to the table. Returns
+// the rounded values (qo, ko, vf) and their packed bf16 words. Warp-collective (shuffles).
+__device__ __forceinline__ void rows_arith(float (&qf)[4], float (&kf)[4], float (&vf)[4], float s, uint2 crow,
+                                           uint2 srow, bool rot, int partner, float sign, const float (&wqv)[4],
+                                           const float (&wkv)[4], float eps, float (&qo)[4], float (&ko)[4],
+                                           uint2& qw, uint2& kw, uint2& vw) {
+#pragma unroll
+  for (int j = 0; j < 4; j += 2) {
+    mul2(qf[j], qf[j + 1], s, s);
+    mul2(kf[j], kf[j + 1], s, s);
+    mul2(vf[j], vf[j + 1], s, s);
+  }
+  float sumq = 0.f, sumk = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) sq_acc2(sumq, sumk, qf[j], kf[j]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const float tq = __shfl_xor_sync(0xffffffffu, sumq, o), tk = __shfl_xor_sync(0xffffffffu, sumk, o);
+    add2(sumq, sumk, tq, tk);
+  }
+  const float rq_ = rsqrtf(sumq / D + eps), rk_ = rsqrtf(sumk / D + eps);
+#pragma unroll
+  for (int j = 0; j < 4; j += 2) {
+    float tq0 = rq_, tq1 = rq_, tk0 = rk_, tk1 = rk_;
+    mul2(tq0, tq1, wqv[j], wqv[j + 1]);
+    mul2(tk0, tk1, wkv[j], wkv[j + 1]);
+    mul2(qf[j], qf[j + 1], tq0, tq1);
+    mul2(kf[j], kf[j + 1], tk0, tk1);
+  }
+  float c[4] = {1.f, 1.f, 1.f, 1.f}, sn[4] = {0.f, 0.f, 0.f, 0.f};
+  if (rot) {
+    unpack4(crow, c);
+    unpack4(srow, sn);
+  }
+  float qr[4], kr[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    qr[j] = __shfl_sync(0xffffffffu, qf[j], partner);
+    kr[j] = __shfl_sync(0xffffffffu, kf[j], partner);
+    sn[j] *= sign;
+  }
+#pragma unroll
+  for (int j = 0; j < 4; j += 2) {
+    mul2(qr[j], qr[j + 1], sn[j], sn[j + 1]);
+    mul2(kr[j], kr[j + 1], sn[j], sn[j + 1]);
+    fma2(qf[j], qf[j + 1], c[j], c[j + 1], qr[j], qr[j + 1]);
+    fma2(kf[j], kf[j + 1], c[j], c[j + 1], kr[j], kr[j + 1]);
+  }
+  qw = make_uint2(pack_bf16x2(qf[0], qf[1]), pack_bf16x2(qf[2], qf[3]));
+  kw = make_uint2(pack_bf16x2(kf[0], kf[1]), pack_bf16x2(kf[2], kf[3]));
+  vw = make_uint2(pack_bf16x2(vf[0], vf[1]), pack_bf16x2(vf[2], vf[3]));
+  unpack4(qw, qo);
+  unpack4(kw, ko);
+  unpack4(vw, vf);
+}
+
 // QK_I8: Q and K as symmetric int8 with per-(head, tile) scales max(amax / 127, 1e-30) (for the kind::i8 QK^T of the
 // attention kernel); V stays E4M3.
 template <bool ROWS, bool TILE_QK, bool QK_I8 = false>
@@ -209,58 +268,7 @@ __global__ void __launch_bounds__(NWARP * 32, 2) prologue_kernel(const ProArgs a
         float qo[4], ko[4];
         uint2 qw, kw, vw;  // the bf16 roundings, packed (what goes back into the buffer)
         if constexpr (ROWS) {
-          // the reference's per-element operations (h3fast.cu:376-510) in the same order, two lanes of work per
-          // paired fp32 instruction: q with k, or neighbouring dims
-          const float s = s1v[u];
-#pragma unroll
-          for (int j = 0; j < 4; j += 2) {
-            mul2(qf[j], qf[j + 1], s, s);
-            mul2(kf[j], kf[j + 1], s, s);
-            mul2(vf[j], vf[j + 1], s, s);
-          }
-          float sumq = 0.f, sumk = 0.f;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) sq_acc2(sumq, sumk, qf[j], kf[j]);
-#pragma unroll
-          for (int o = 16; o; o >>= 1) {
-            const float tq = __shfl_xor_sync(0xffffffffu, sumq, o), tk = __shfl_xor_sync(0xffffffffu, sumk, o);
-            add2(sumq, sumk, tq, tk);
-          }
-          const float rq_ = rsqrtf(sumq / D + a.eps), rk_ = rsqrtf(sumk / D + a.eps);
-#pragma unroll
-          for (int j = 0; j < 4; j += 2) {
-            float tq0 = rq_, tq1 = rq_, tk0 = rk_, tk1 = rk_;
-            mul2(tq0, tq1, wqv[j], wqv[j + 1]);
-            mul2(tk0, tk1, wkv[j], wkv[j + 1]);
-            mul2(qf[j], qf[j + 1], tq0, tq1);
-            mul2(kf[j], kf[j + 1], tk0, tk1);
-          }
-          // rotate-half RoPE: x * cos + sign * partner * sin; sign * sin is exact, so it is applied to the table
-          float c[4] = {1.f, 1.f, 1.f, 1.f}, sn[4] = {0.f, 0.f, 0.f, 0.f};
-          if (rot) {
-            unpack4(cr[u], c);
-            unpack4(sr[u], sn);
-          }
-          float qr[4], kr[4];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            qr[j] = __shfl_sync(0xffffffffu, qf[j], partner);
-            kr[j] = __shfl_sync(0xffffffffu, kf[j], partner);
-            sn[j] *= sign;
-          }
-#pragma unroll
-          for (int j = 0; j < 4; j += 2) {
-            mul2(qr[j], qr[j + 1], sn[j], sn[j + 1]);
-            mul2(kr[j], kr[j + 1], sn[j], sn[j + 1]);
-            fma2(qf[j], qf[j + 1], c[j], c[j + 1], qr[j], qr[j + 1]);
-            fma2(kf[j], kf[j + 1], c[j], c[j + 1], kr[j], kr[j + 1]);
-          }
-          qw = make_uint2(pack_bf16x2(qf[0], qf[1]), pack_bf16x2(qf[2], qf[3]));
-          kw = make_uint2(pack_bf16x2(kf[0], kf[1]), pack_bf16x2(kf[2], kf[3]));
-          vw = make_uint2(pack_bf16x2(vf[0], vf[1]), pack_bf16x2(vf[2], vf[3]));
-          unpack4(qw, qo);
-          unpack4(kw, ko);
-          unpack4(vw, vf);
+          rows_arith(qf, kf, vf, s1v[u], cr[u], sr[u], rot, partner, sign, wqv, wkv, a.eps, qo, ko, qw, kw, vw);
         } else {
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
@@ -381,6 +389,177 @@ __global__ void __launch_bounds__(NWARP * 32, 2) prologue_kernel(const ProArgs a
   asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
+// The q/k/v row form with one CTA per (tile, head) item (blockIdx = tile * heads + head, so a tile's heads run side by
+// side and its per-row scale and RoPE rows are read from L2 by all of them). Warp w owns rows w, w + 8, ... and lane l
+// dims 4l .. 4l+3, as in the reference kernel; each warp loads its rows straight into registers one row ahead of the
+// arithmetic, and the item's rounded values are staged in one 48 KB buffer for the quantization pass (the tile's
+// maxima are needed first), so three CTAs share an SM. Arithmetic, rounding and summation orders are those of
+// prologue_kernel (rows_arith; the per-lane row sums in row order, the warp partials in warp order).
+constexpr int kItemSmem = 3 * TILE * D * (int)sizeof(bf16);
+
+template <bool TILE_QK, bool QK_I8>
+__global__ void __launch_bounds__(NWARP * 32, 3) prologue_item_kernel(const ProArgs a) {
+  extern __shared__ __align__(16) uint8_t pro_smem[];
+  __shared__ float sp[3][NWARP][D];
+  __shared__ float red[32];
+  bf16* buf = reinterpret_cast<bf16*>(pro_smem);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  const int h = blockIdx.x % a.heads, ti = blockIdx.x / a.heads;
+  const int row0 = a.tile_row0[ti], n = a.vbs[ti];
+  const int partner = l < HALF_LANES ? l + HALF_LANES : (l < 2 * HALF_LANES ? l - HALF_LANES : l);
+  const float sign = l < HALF_LANES ? -1.f : 1.f;
+  const bool rot = l < 2 * HALF_LANES && a.cosb != nullptr;
+  float wqv[4], wkv[4];
+  unpack4(*reinterpret_cast<const uint2*>(a.wq + l * 4), wqv);
+  unpack4(*reinterpret_cast<const uint2*>(a.wk + l * 4), wkv);
+  float pq[4] = {0.f, 0.f, 0.f, 0.f}, pk[4] = {0.f, 0.f, 0.f, 0.f}, pv[4] = {0.f, 0.f, 0.f, 0.f};
+  float qmax = 0.f, kmax = 0.f, vmax = 0.f;
+  // raw data of row w + 8u (zeros past the tile's length)
+  uint2 nq = make_uint2(0u, 0u), nk = nq, nv = nq, ncr = nq, nsr = nq;
+  float ns = 0.f;
+  auto load_row = [&](int u) {
+    const int i = w + u * NWARP;
+    if (i < n) {
+      const int64_t r = row0 + i;
+      const size_t src = (size_t)r * a.ld + (size_t)h * D + l * 4;
+      nq = __ldg(reinterpret_cast<const uint2*>(a.q + src));
+      nk = __ldg(reinterpret_cast<const uint2*>(a.k + src));
+      nv = __ldg(reinterpret_cast<const uint2*>(a.v + src));
+      ns = __ldg(a.s1 + r);
+      if (rot) {
+        ncr = __ldg(reinterpret_cast<const uint2*>(a.cosb + r * ROT + l * 4));
+        nsr = __ldg(reinterpret_cast<const uint2*>(a.sinb + r * ROT + l * 4));
+      }
+    }
+  };
+  load_row(0);
+#pragma unroll 1
+  for (int u = 0; u < RPW; ++u) {
+    const int i = w + u * NWARP;
+    if (i >= n) break;  // warp-uniform: later rows of this warp are past the tile too (zeros would change nothing)
+    float qf[4], kf[4], vf[4];
+    unpack4(nq, qf);
+    unpack4(nk, kf);
+    unpack4(nv, vf);
+    const float s = ns;
+    const uint2 crow = ncr, srow = nsr;
+    if (u + 1 < RPW) load_row(u + 1);
+    float qo[4], ko[4];
+    uint2 qw, kw, vw;
+    rows_arith(qf, kf, vf, s, crow, srow, rot, partner, sign, wqv, wkv, a.eps, qo, ko, qw, kw, vw);
+#pragma unroll
+    for (int j = 0; j < 4; j += 2) {
+      add2(pq[j], pq[j + 1], qo[j], qo[j + 1]);
+      add2(pk[j], pk[j + 1], ko[j], ko[j + 1]);
+      add2(pv[j], pv[j + 1], vf[j], vf[j + 1]);
+      qmax = fmax3(qmax, fabsf(qo[j]), fabsf(qo[j + 1]));
+      kmax = fmax3(kmax, fabsf(ko[j]), fabsf(ko[j + 1]));
+      vmax = fmax3(vmax, fabsf(vf[j]), fabsf(vf[j + 1]));
+    }
+    *reinterpret_cast<uint2*>(buf + (0 * TILE + i) * D + l * 4) = qw;
+    *reinterpret_cast<uint2*>(buf + (1 * TILE + i) * D + l * 4) = kw;
+    *reinterpret_cast<uint2*>(buf + (2 * TILE + i) * D + l * 4) = vw;
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    sp[0][w][l * 4 + j] = pq[j];
+    sp[1][w][l * 4 + j] = pk[j];
+    sp[2][w][l * 4 + j] = pv[j];
+  }
+  vmax = warp_allreduce<true>(vmax);
+  if constexpr (TILE_QK) {
+    qmax = warp_allreduce<true>(qmax);
+    kmax = warp_allreduce<true>(kmax);
+  }
+  if (l == 0) {
+    red[w] = vmax;
+    red[NWARP + w] = qmax;
+    red[2 * NWARP + w] = kmax;
+  }
+  __syncthreads();
+  vmax = red[0];
+#pragma unroll
+  for (int ww = 1; ww < NWARP; ++ww) vmax = fmaxf(vmax, red[ww]);
+  const float svb = fmaxf(vmax / kFp8Max, 1e-30f);
+  float inv_q = a.inv_sq, inv_k = a.inv_sk;
+  if constexpr (TILE_QK) {
+    qmax = red[NWARP];
+    kmax = red[2 * NWARP];
+#pragma unroll
+    for (int ww = 1; ww < NWARP; ++ww) {
+      qmax = fmaxf(qmax, red[NWARP + ww]);
+      kmax = fmaxf(kmax, red[2 * NWARP + ww]);
+    }
+    const float qk_max = QK_I8 ? 127.f : kFp8Max;
+    const float sqb = fmaxf(qmax / qk_max, 1e-30f), skb = fmaxf(kmax / qk_max, 1e-30f);
+    inv_q = 1.f / sqb;
+    inv_k = 1.f / skb;
+    if (threadIdx.x == 0) {
+      a.qs_blk[(size_t)h * a.n_ext + ti] = sqb;
+      a.ks_blk[(size_t)h * a.n_ext + ti] = skb;
+    }
+  }
+  if (threadIdx.x == 0) {
+    a.vs_blk[(size_t)h * a.n_ext + ti] = svb;
+    if (a.vs_head) atomicMax(reinterpret_cast<int*>(a.vs_head + h), __float_as_int(svb));
+  }
+  const float inv_v = 1.f / svb;
+  const size_t plane = (size_t)h * a.rows_pad + (size_t)ti * TILE;
+#pragma unroll 2
+  for (int u = 0; u < RPW; ++u) {
+    const int i = w + u * NWARP;
+    if (i >= n) break;
+    const size_t dst = (plane + i) * D + l * 4;
+    float qv[4], kv[4], vv[4];
+    unpack4(*reinterpret_cast<const uint2*>(buf + (0 * TILE + i) * D + l * 4), qv);
+    unpack4(*reinterpret_cast<const uint2*>(buf + (1 * TILE + i) * D + l * 4), kv);
+    unpack4(*reinterpret_cast<const uint2*>(buf + (2 * TILE + i) * D + l * 4), vv);
+#pragma unroll
+    for (int j = 0; j < 4; j += 2) {
+      mul2(qv[j], qv[j + 1], inv_q, inv_q);
+      mul2(kv[j], kv[j + 1], inv_k, inv_k);
+      mul2(vv[j], vv[j + 1], inv_v, inv_v);
+    }
+    if constexpr (QK_I8) {
+      *reinterpret_cast<uint32_t*>(a.qb + dst) = s8x4(qv[0], qv[1], qv[2], qv[3]);
+      *reinterpret_cast<uint32_t*>(a.kb + dst) = s8x4(kv[0], kv[1], kv[2], kv[3]);
+    } else {
+      *reinterpret_cast<uint32_t*>(a.qb + dst) = e4m3x4(qv[0], qv[1], qv[2], qv[3]);
+      *reinterpret_cast<uint32_t*>(a.kb + dst) = e4m3x4(kv[0], kv[1], kv[2], kv[3]);
+    }
+    const uint32_t vcodes = e4m3x4(vv[0], vv[1], vv[2], vv[3]);
+    if (a.v16)
+      *reinterpret_cast<uint2*>(a.vb + 2 * dst) = e4m3x4_to_f16x4(vcodes);
+    else
+      *reinterpret_cast<uint32_t*>(a.vb + dst) = vcodes;
+  }
+  const float inv = 1.f / (float)n;
+  for (int e = threadIdx.x; e < 3 * D; e += NWARP * 32) {
+    const int which = e / D, d = e % D;
+    float acc = 0.f;
+#pragma unroll
+    for (int ww = 0; ww < NWARP; ++ww) acc += sp[which][ww][d];
+    float* dst = which == 0 ? a.qp : (which == 1 ? a.kp : a.vp);
+    dst[((size_t)h * a.n_tiles + ti) * D + d] = acc * inv;
+  }
+}
+
+template <bool TILE_QK, bool QK_I8 = false>
+int launch_prologue_item(const ProArgs& a, cudaStream_t stream) {
+  auto kern = prologue_item_kernel<TILE_QK, QK_I8>;
+  static PerDevice setup;  // the shared-memory reservation, per device
+  int done = 0;
+  if (int rc = setup.get([&](int* v) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kItemSmem) != cudaSuccess)
+          return set_error(H3B_ECUDA, "prologue: cannot reserve %d bytes of shared memory", kItemSmem);
+        *v = 1;
+        return H3B_OK;
+      }, &done))
+    return rc;
+  kern<<<(unsigned)((int64_t)a.n_tiles * a.heads), NWARP * 32, kItemSmem, stream>>>(a);
+  return H3B_OK;
+}
+
 template <bool ROWS, bool TILE_QK, bool QK_I8 = false>
 int launch_prologue(const ProArgs& a, cudaStream_t stream) {
   auto kern = prologue_kernel<ROWS, TILE_QK, QK_I8>;
@@ -427,7 +606,7 @@ extern "C" int h3b_qkv_prologue8(const void* q, const void* k, const void* v, in
             static_cast<const bf16*>(cosb), static_cast<const bf16*>(sinb), inv_sq, inv_sk,
             static_cast<uint8_t*>(qb), static_cast<uint8_t*>(kb), static_cast<uint8_t*>(vb), qs_blk, ks_blk, vs_blk,
             vs_head, qp, kp, vp, heads, rows_pad, n_tiles, n_ext, eps, 0};
-  const int rc = tile_qk ? launch_prologue<true, true>(a, stream) : launch_prologue<true, false>(a, stream);
+  const int rc = tile_qk ? launch_prologue_item<true>(a, stream) : launch_prologue_item<false>(a, stream);
   if (rc) return rc;
   H3B_LAUNCH_CHECK("qkv_prologue8");
   return H3B_OK;
@@ -453,7 +632,7 @@ extern "C" int h3b_qkv_prologue8_qk_int8(const void* q, const void* k, const voi
             static_cast<const bf16*>(cosb), static_cast<const bf16*>(sinb), 1.f, 1.f,
             static_cast<uint8_t*>(qb), static_cast<uint8_t*>(kb), static_cast<uint8_t*>(vb), qs_blk, ks_blk, vs_blk,
             vs_head, qp, kp, vp, heads, rows_pad, n_tiles, n_ext, eps, 0};
-  if (const int rc = launch_prologue<true, true, true>(a, stream)) return rc;
+  if (const int rc = launch_prologue_item<true, true>(a, stream)) return rc;
   H3B_LAUNCH_CHECK("qkv_prologue8_qk_int8");
   return H3B_OK;
 }
@@ -521,7 +700,7 @@ extern "C" int h3b_qkv_prologue8_tiles(const void* q, const void* k, const void*
             static_cast<const bf16*>(cosb), static_cast<const bf16*>(sinb), 1.f, 1.f,
             static_cast<uint8_t*>(qb), static_cast<uint8_t*>(kb), static_cast<uint8_t*>(vb), qs_blk, ks_blk, vs_blk,
             vs_head, qp, kp, vp, heads, rows_pad, n_tiles, n_ext, eps, v16 ? 1 : 0};
-  const int rc = i8 ? launch_prologue<true, true, true>(a, stream) : launch_prologue<true, true>(a, stream);
+  const int rc = i8 ? launch_prologue_item<true, true>(a, stream) : launch_prologue_item<true>(a, stream);
   if (rc) return rc;
   H3B_LAUNCH_CHECK("qkv_prologue8_tiles");
   return H3B_OK;
