@@ -27,6 +27,14 @@ import time
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
+
+# Under torchrun (WORLD_SIZE > 1): NCCL's own communicator set-up log (rank count, transports), written per process to
+# a file so stdout keeps the one JSON line; rank 0 quotes its "nRanks" lines in the line. Set before torch is imported:
+# NCCL reads these variables once, at its first call.
+NCCL_LOG = None
+if int(os.environ.get("WORLD_SIZE", "1")) > 1 and "NCCL_DEBUG" not in os.environ:
+    NCCL_LOG = f"/tmp/h3b_bench_nccl.{os.getpid()}.log"
+    os.environ.update(NCCL_DEBUG="INFO", NCCL_DEBUG_SUBSYS="INIT", NCCL_DEBUG_FILE=NCCL_LOG)
 sys.path.insert(0, str(ROOT))
 
 M, N, K = 32768, 13824, 5120
@@ -752,9 +760,6 @@ def run_ours(args) -> None:
     dev = torch.device("cuda", local)
     if ws > 1:
         from datetime import timedelta
-        # NCCL's own communicator set-up log (rank count, transports) on stderr, so the ranks NCCL saw are on record
-        if "NCCL_DEBUG" not in os.environ:
-            os.environ.update(NCCL_DEBUG="INFO", NCCL_DEBUG_SUBSYS="INIT", NCCL_DEBUG_FILE="/dev/stderr")
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
     ops = __graft_entry__.load_package().ops
 
@@ -888,6 +893,13 @@ def run_ours(args) -> None:
             line["fp8_block_chain_config3"] = chain
         if sp_check is not None:
             line["sp_check"] = sp_check
+        if NCCL_LOG is not None:
+            try:
+                with open(NCCL_LOG) as fh:
+                    init = [ln.strip() for ln in fh if "nRanks" in ln or "NCCL version" in ln]
+                line["nccl_init_log"] = {"file": NCCL_LOG, "lines": init[:4]}
+            except OSError as exc:
+                line["nccl_init_log"] = {"file": NCCL_LOG, "error": repr(exc)[:200]}
         if mem is not None:
             line["memory_kernels"] = mem
         if dit is not None:

@@ -104,6 +104,106 @@ __global__ void __launch_bounds__(W / 8, 2) gate_quant_kernel(const GateArgs p) 
   }
 }
 
+// The plain form (no gate branch, no merge: the block's attention output straight into the next GEMM's input) with
+// row groups: a CTA per SM holds RG groups of G threads, each group working on its own rows r, r + step, ...
+// with the next row's attention output in flight in registers; thread t of a group owns the 8-element chunks
+// t, t + G, ... of the row (a warp's 16-byte loads cover two heads' 256-byte segments), and the row maximum is reduced
+// over the group's warps with a named barrier, so many rows are in flight per SM without the 20-warp block reduction
+// of the one-row-per-CTA form. The per-element arithmetic is gate_quant_kernel's (bit-identical bytes).
+template <int W>
+struct GqShape {
+  static constexpr int kChunks = W / 8;
+  static constexpr int pick() {
+    for (int k = 5; k > 1; --k)
+      if (kChunks % k == 0 && (kChunks / k) % 32 == 0) return k;
+    return 1;
+  }
+  static constexpr int K = pick();
+  static constexpr int G = kChunks / K;
+  static constexpr int NW = G / 32;
+  static constexpr int RG = G <= 128 ? 5 : 3;
+  static_assert(G % 32 == 0 && G % 2 == 0, "whole warps, even thread count");
+};
+
+__device__ __forceinline__ void gq_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+
+template <int W, bool FP4>
+__global__ void __launch_bounds__(GqShape<W>::G * GqShape<W>::RG, 1) gate_quant_groups_kernel(const GateArgs p) {
+  using Sh = GqShape<W>;
+  constexpr int K = Sh::K, G = Sh::G, NW = Sh::NW, RG = Sh::RG;
+  __shared__ float red[RG][2][NW];
+  const int grp = threadIdx.x / G, t = threadIdx.x - grp * G, lane = t & 31, w = t >> 5;
+  const int64_t step = (int64_t)gridDim.x * RG;
+  int64_t r = (int64_t)blockIdx.x * RG + grp;
+  if (r >= p.rows) return;  // group-uniform; a group with no rows takes no part in any barrier
+  int hk[K], dk[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const int c = t + G * k;
+    hk[k] = c / (D / 8);
+    dk[k] = (c % (D / 8)) * 8;
+  }
+  uint4 nxt[K];
+  auto load = [&](int64_t row) {
+    const int sl = p.slot[row];
+#pragma unroll
+    for (int k = 0; k < K; ++k) nxt[k] = ld8_raw(p.ob + ((size_t)hk[k] * p.rows_pad + sl) * D + dk[k]);
+  };
+  load(r);
+  int par = 0;
+  for (; r < p.rows; r += step, par ^= 1) {
+    float o[K][8];
+#pragma unroll
+    for (int k = 0; k < K; ++k) unpack8(nxt[k], o[k]);
+    if (r + step < p.rows) load(r + step);
+    float cm[K];
+    float am = 0.f;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      float m = fmax3(fabsf(o[k][0]), fabsf(o[k][1]), fabsf(o[k][2]));
+      m = fmax3(m, fabsf(o[k][3]), fabsf(o[k][4]));
+      m = fmax3(m, fabsf(o[k][5]), fabsf(o[k][6]));
+      cm[k] = fmaxf(m, fabsf(o[k][7]));
+      am = fmaxf(am, cm[k]);
+    }
+    am = warp_allreduce<true>(am);
+    if (lane == 0) red[grp][par][w] = am;
+    gq_bar(1 + grp, G);
+    am = red[grp][par][0];
+#pragma unroll
+    for (int q = 1; q < NW; ++q) am = fmaxf(am, red[grp][par][q]);
+    if constexpr (FP4) {
+      const float s = fmaxf(am / kFp4Range, kMinScaleFp4);
+      const float gs = 1.f / s;
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        const int c = t + G * k;
+        // a 16-element block spans chunks 2m and 2m+1: threads t and t^1 of the same k (G is even)
+        const float vmax = fmaxf(cm[k], __shfl_xor_sync(0xffffffffu, cm[k], 1));
+        uint32_t bits;
+        const float m = nvfp4_block_scale(vmax, gs, &bits);
+        const uint32_t lo = e2m1x4(o[k][0] * m, o[k][1] * m, o[k][2] * m, o[k][3] * m);
+        const uint32_t hi = e2m1x4(o[k][4] * m, o[k][5] * m, o[k][6] * m, o[k][7] * m);
+        *reinterpret_cast<uint32_t*>(p.a + r * (W / 2) + c * 4) = lo | (hi << 16);
+        if ((t & 1) == 0) p.asf[sf_atom_offset(r, c >> 1, W / 16)] = (uint8_t)bits;
+      }
+      if (t == 0) p.sa[r] = s;
+    } else {
+      const float s = fmaxf(am / kFp8Max, kMinScaleFp8);
+      const float inv = 1.f / s;
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        const int c = t + G * k;
+        uint2 u;
+        u.x = e4m3x4(o[k][0] * inv, o[k][1] * inv, o[k][2] * inv, o[k][3] * inv);
+        u.y = e4m3x4(o[k][4] * inv, o[k][5] * inv, o[k][6] * inv, o[k][7] * inv);
+        *reinterpret_cast<uint2*>(p.a + r * W + c * 8) = u;
+      }
+      if (t == 0) p.sa[r] = s;
+    }
+  }
+}
+
 template <int W>
 int launch(const GateArgs& p, bool gate, bool fp4, bool merge, cudaStream_t st) {
   int dev = 0, sms = 148;
@@ -112,7 +212,13 @@ int launch(const GateArgs& p, bool gate, bool fp4, bool merge, cudaStream_t st) 
   const int64_t resident = (int64_t)sms * 2;  // two resident CTAs per SM (the launch bounds)
   const dim3 grid((unsigned)(p.rows < resident ? p.rows : resident)), block(W / 8);
 #define H3B_GQ(G, Q, M) gate_quant_kernel<W, G, Q, M><<<grid, block, 0, st>>>(p)
-  if (gate) {
+  if (!gate && !merge) {  // the plain form: row groups
+    using Sh = GqShape<W>;
+    const int64_t need = (p.rows + Sh::RG - 1) / Sh::RG;
+    const dim3 g2((unsigned)(need < sms ? need : sms)), b2(Sh::G * Sh::RG);
+    if (fp4) gate_quant_groups_kernel<W, true><<<g2, b2, 0, st>>>(p);
+    else gate_quant_groups_kernel<W, false><<<g2, b2, 0, st>>>(p);
+  } else if (gate) {
     if (fp4) { if (merge) H3B_GQ(true, true, true); else H3B_GQ(true, true, false); }
     else { if (merge) H3B_GQ(true, false, true); else H3B_GQ(true, false, false); }
   } else {
