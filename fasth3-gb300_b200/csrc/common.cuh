@@ -161,6 +161,20 @@ __device__ __forceinline__ uint32_t e2m1x4(float a, float b, float c, float d) {
   return r & 0xffffu;
 }
 
+// Eight fp32 -> eight e2m1 nibbles in one word (element 0 in the lowest nibble; the same codes as two e2m1x4).
+__device__ __forceinline__ uint32_t e2m1x8(const float* v) {
+  uint32_t r;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+      "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+      : "=r"(r)
+      : "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]));
+  return r;
+}
+
 // Byte offset of scale (row, col) in the 128x4-atom layout that tcgen05 block-scaled MMA reads (one 512-byte atom per
 // 128 rows x 4 scale columns; inside it row r sits at (r % 32) * 16 + ((r % 128) / 32) * 4).
 __host__ __device__ __forceinline__ size_t sf_atom_offset(int64_t row, int64_t col, int64_t sf_cols) {

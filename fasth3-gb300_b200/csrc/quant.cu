@@ -820,13 +820,13 @@ __global__ void __launch_bounds__(256, 4) amax_kernel(const bf16* __restrict__ x
 }
 
 // ------------------------------------------------------------------------------------------- per-tensor NVFP4
-// Warp-cooperative, one warp per row at a time: a unit is 256 consecutive elements of the row, lane l holding
-// elements 8l .. 8l+7, so every load instruction reads 512 contiguous bytes and every code store writes 128. A
-// 16-element block spans lanes 2k and 2k+1 (one shuffle for its maximum); lanes 8j gather the four scales of blocks
-// 4j .. 4j+3 (adjacent bytes of one atom row) and write them as one word. A warp converts 5 units while the next 5
-// units' loads are in flight (a 5120-wide row is 4 batches); rows past `rows` up to the next multiple of 128 get zero
-// scales (the atom layout's padding).
-constexpr int kQuantUnits = 5;
+// Warp-cooperative, one warp per row at a time: a unit is 512 consecutive elements of the row and lane l holds the
+// 16-element block 16l .. 16l+15 (two 16-byte loads; a warp's loads cover 1 KB of the row), so each lane owns whole
+// blocks: one block scale per lane and block, no shuffles, its 8 code bytes in one store and its scale byte in one
+// byte store. A warp converts 2 units while the next 2 units' loads are in flight; a row's last unit may be partial
+// (K is a multiple of 64; lanes past K are masked). Rows past `rows` up to the next multiple of 128 get zero scales
+// (the atom layout's padding). The per-element arithmetic is the block math of h3fast.cu:99-119.
+constexpr int kQuantUnits = 2;
 
 __global__ void __launch_bounds__(256, 3) quant_nvfp4_tensor_kernel(const bf16* __restrict__ x, int64_t ld, int64_t rows,
                                                                     int K, const float* __restrict__ amax,
@@ -840,23 +840,23 @@ __global__ void __launch_bounds__(256, 3) quant_nvfp4_tensor_kernel(const bf16* 
   if (blockIdx.x == 0 && threadIdx.x == 0) s_out[0] = s;
   const int64_t nwarps = (int64_t)gridDim.x * 8;
   constexpr int U = kQuantUnits;
-  auto load = [&](int64_t r, int c0, uint4 (&raw)[U]) {
+  auto load = [&](int64_t r, int c0, uint4 (&raw)[U][2]) {
     const bf16* src = x + r * ld;
     const bool row_live = r < rows;
 #pragma unroll
     for (int t = 0; t < U; ++t) {
-      const int col = c0 + t * 256 + 8 * lane;
-      raw[t] = (row_live && col < K) ? __ldg(reinterpret_cast<const uint4*>(src + col)) : make_uint4(0u, 0u, 0u, 0u);
+      const int col = c0 + t * 512 + 16 * lane;
+      const bool live = row_live && col < K;
+      raw[t][0] = live ? __ldg(reinterpret_cast<const uint4*>(src + col)) : make_uint4(0u, 0u, 0u, 0u);
+      raw[t][1] = live ? __ldg(reinterpret_cast<const uint4*>(src + col + 8)) : make_uint4(0u, 0u, 0u, 0u);
     }
   };
-  // the warp walks its (row, 5-unit batch) positions in order, the next batch's loads in flight while the current
-  // one is converted
   int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   int c0 = 0;
-  uint4 cur[U], nxt[U];
+  uint4 cur[U][2], nxt[U][2];
   if (r < rows_pad) load(r, c0, cur);
   while (r < rows_pad) {
-    int c1 = c0 + U * 256;
+    int c1 = c0 + U * 512;
     int64_t r1 = r;
     if (c1 >= K) {
       c1 = 0;
@@ -864,32 +864,34 @@ __global__ void __launch_bounds__(256, 3) quant_nvfp4_tensor_kernel(const bf16* 
     }
     if (r1 < rows_pad) load(r1, c1, nxt);
     const bool row_live = r < rows;
+    const size_t sf_row = sf_atom_offset(r, 0, sf_cols);
 #pragma unroll
     for (int t = 0; t < U; ++t) {
-      const int ucol = c0 + t * 256;
-      if (ucol >= K) break;  // warp-uniform
-      const int col = ucol + 8 * lane;
-      float f[8];
-      unpack8(cur[t], f);
-      float vmax = 0.f;
+      const int col = c0 + t * 512 + 16 * lane;
+      if (col < K) {
+        const int c = col >> 4;  // this lane's block
+        uint32_t bits = 0;
+        if (row_live) {
+          float f[16];
+          unpack8(cur[t][0], *reinterpret_cast<float(*)[8]>(&f[0]));
+          unpack8(cur[t][1], *reinterpret_cast<float(*)[8]>(&f[8]));
+          float vmax = fmax3(fabsf(f[0]), fabsf(f[1]), fabsf(f[2]));
 #pragma unroll
-      for (int j = 0; j < 8; ++j) vmax = fmaxf(vmax, fabsf(f[j]));
-      vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
-      uint32_t bits;
-      const float m = nvfp4_block_scale(vmax, gs, &bits);
-      if (row_live && col < K)
-        *reinterpret_cast<uint32_t*>(q + r * (K / 2) + col / 2) =
-            e2m1x4(f[0] * m, f[1] * m, f[2] * m, f[3] * m) | (e2m1x4(f[4] * m, f[5] * m, f[6] * m, f[7] * m) << 16);
-      const uint32_t b1 = __shfl_down_sync(0xffffffffu, bits, 2);
-      const uint32_t b2 = __shfl_down_sync(0xffffffffu, bits, 4);
-      const uint32_t b3 = __shfl_down_sync(0xffffffffu, bits, 6);
-      if ((lane & 7) == 0 && col < K) {
-        const uint32_t w = row_live ? (bits | (b1 << 8) | (b2 << 16) | (b3 << 24)) : 0u;
-        *reinterpret_cast<uint32_t*>(sf + sf_atom_offset(r, col / 16, sf_cols)) = w;
+          for (int i = 3; i < 15; i += 2) vmax = fmax3(vmax, fabsf(f[i]), fabsf(f[i + 1]));
+          vmax = fmaxf(vmax, fabsf(f[15]));
+          const float m = nvfp4_block_scale(vmax, gs, &bits);
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) mul2(f[i], f[i + 1], m, m);
+          *reinterpret_cast<uint2*>(q + r * (K / 2) + col / 2) = make_uint2(e2m1x8(f), e2m1x8(f + 8));
+        }
+        sf[sf_row + (size_t)(c >> 2) * 512 + (c & 3)] = (uint8_t)bits;
       }
     }
 #pragma unroll
-    for (int t = 0; t < U; ++t) cur[t] = nxt[t];
+    for (int t = 0; t < U; ++t) {
+      cur[t][0] = nxt[t][0];
+      cur[t][1] = nxt[t][1];
+    }
     r = r1;
     c0 = c1;
   }
