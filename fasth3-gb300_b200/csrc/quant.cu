@@ -685,6 +685,126 @@ int launch_ln_groups(const RowArgs& a, int sms, cudaStream_t st) {
   return H3B_OK;
 }
 
+// The reference's RMSNorm row form (gated residual, RMSNorm with weights, adaLN modulate, FP8 / NVFP4) with row
+// groups: G threads per row (the LayerNorm layout, thread t owning the 8-element chunks t, t + G, ...), RG groups per
+// CTA, each group on its own rows with the next row in flight in registers. The reference's kernel has a thread per
+// 8-element chunk and reduces the row's sum of squares thread by thread in element order, butterflies each warp and
+// butterflies the warp partials again (zeros past the last warp); here thread t plays the reference's threads
+// t + G k, so each of its warps butterflies once per k (the reference's warp w + (G/32) k), the partials are staged in
+// shared memory and every warp butterflies them the same way: the sum, and so every byte, is the reference's.
+template <int C>
+constexpr int rms_groups() {
+  return LnRowShape<C>::G <= 96 ? 5 : (LnRowShape<C>::G <= 128 ? 3 : 2);
+}
+
+template <int C, bool BRANCH, bool FP4>
+__global__ void __launch_bounds__(LnRowShape<C>::G * rms_groups<C>(), 1) rms_norm_quant_groups_kernel(const RowArgs a) {
+  using Sh = LnRowShape<C>;
+  constexpr int K = Sh::K, G = Sh::G, NW = Sh::NW, RG = rms_groups<C>();
+  constexpr int NWV = C / 8 / 32;  // warps of the reference's row layout
+  static_assert(NWV <= 32, "at most 32 warps in the reference layout");
+  __shared__ float stage[RG][32];
+  __shared__ float red[RG][NW];
+  const int grp = threadIdx.x / G, t = threadIdx.x - grp * G, lane = t & 31, w = t >> 5;
+  const int bar = 1 + grp;
+  const int64_t step = (int64_t)gridDim.x * RG;
+  int64_t r = (int64_t)blockIdx.x * RG + grp;
+  if (r >= a.rows) return;  // group-uniform; a group without rows takes no part in any barrier
+  uint4 xn[K], yn[K];
+  auto load = [&](int64_t row) {
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int c = (t + G * k) * 8;
+      xn[k] = ld8_raw(a.x + row * C + c);
+      if constexpr (BRANCH) yn[k] = ld8_raw(a.y + row * C + c);
+    }
+  };
+  load(r);
+  for (; r < a.rows; r += step) {
+    const int64_t tab = a.idx ? (int64_t)a.idx[r] : 0;
+    float v[K][8];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      unpack8(xn[k], v[k]);
+      if constexpr (BRANCH) {
+        float b[8], g[8];
+        unpack8(yn[k], b);
+        const int c = (t + G * k) * 8;
+        load8(a.gate + tab * a.gate_ld + c, g);
+        const float s = a.sy[r];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[k][i] = to_bf16_and_back(v[k][i] + g[i] * (s * b[i]));
+        store8(a.xo + r * C + c, v[k]);
+      }
+    }
+    if (r + step < a.rows) load(r + step);
+    // the sum of squares in the reference's tree
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += v[k][i] * v[k][i];
+      ss = warp_allreduce<false>(ss);
+      if (lane == 0) stage[grp][w + NW * k] = ss;
+    }
+    asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(G) : "memory");
+    float ss = lane < NWV ? stage[grp][lane] : 0.f;
+    ss = warp_allreduce<false>(ss);
+    const float rs = rsqrtf(ss / C + a.eps);
+    float am = 0.f;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int c = (t + G * k) * 8;
+      float sc[8], sf[8], wv[8];
+      load8(a.scale + tab * a.tab_ld + c, sc);
+      load8(a.shift + tab * a.tab_ld + c, sf);
+      load8(a.nw + c, wv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        v[k][i] = v[k][i] * rs * wv[i] * (1.f + sc[i]) + sf[i];
+        am = fmaxf(am, fabsf(v[k][i]));
+      }
+    }
+    am = warp_allreduce<true>(am);
+    if (lane == 0) red[grp][w] = am;
+    asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(G) : "memory");
+    am = red[grp][0];
+#pragma unroll
+    for (int q = 1; q < NW; ++q) am = fmaxf(am, red[grp][q]);
+    if constexpr (FP4) {
+      const float s = fmaxf(am / kFp4Range, kMinScaleFp4);
+      const float gs = 1.f / s;
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        const int chunk = t + G * k;
+        float vmax = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) vmax = fmaxf(vmax, fabsf(v[k][i]));
+        vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));  // the block's other half: thread t^1, same k
+        uint32_t bits;
+        const float m = nvfp4_block_scale(vmax, gs, &bits);
+        const uint32_t lo = e2m1x4(v[k][0] * m, v[k][1] * m, v[k][2] * m, v[k][3] * m);
+        const uint32_t hi = e2m1x4(v[k][4] * m, v[k][5] * m, v[k][6] * m, v[k][7] * m);
+        *reinterpret_cast<uint32_t*>(a.h + r * (C / 2) + chunk * 4) = lo | (hi << 16);
+        if ((t & 1) == 0) a.hsf[sf_atom_offset(r, chunk >> 1, C / 16)] = (uint8_t)bits;
+      }
+      if (t == 0) a.hs[r] = s;
+    } else {
+      const float s = fmaxf(am / kFp8Max, kMinScaleFp8);
+      const float inv = 1.f / s;
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        const int chunk = t + G * k;
+        uint2 o;
+        o.x = e4m3x4(v[k][0] * inv, v[k][1] * inv, v[k][2] * inv, v[k][3] * inv);
+        o.y = e4m3x4(v[k][4] * inv, v[k][5] * inv, v[k][6] * inv, v[k][7] * inv);
+        *reinterpret_cast<uint2*>(a.h + r * C + chunk * 8) = o;
+      }
+      if (t == 0) a.hs[r] = s;
+    }
+  }
+}
+
 // Row-per-CTA LayerNorm launch: as many CTAs as are resident on the device (occupancy queried once per device).
 template <int C, bool FP4, bool IDX>
 int launch_ln_rows(const RowArgs& a, int sms, cudaStream_t st) {
@@ -718,11 +838,16 @@ int launch_resid_norm_quant(const RowArgs& a, bool branch, int norm, bool fp4, c
   if (norm == H3B_NORM_NONE) {
     H3B_RNQ(true, H3B_NORM_NONE, false);
   } else if (norm == H3B_NORM_RMS) {
+    constexpr int RG = rms_groups<C>();
+    const int64_t need = (a.rows + RG - 1) / RG;
+    const dim3 g3((unsigned)(need < sms ? need : sms)), b3(LnRowShape<C>::G * RG);
+#define H3B_RMS(B, Q) rms_norm_quant_groups_kernel<C, B, Q><<<g3, b3, 0, st>>>(a)
     if (branch) {
-      if (fp4) H3B_RNQ(true, H3B_NORM_RMS, true); else H3B_RNQ(true, H3B_NORM_RMS, false);
+      if (fp4) H3B_RMS(true, true); else H3B_RMS(true, false);
     } else {
-      if (fp4) H3B_RNQ(false, H3B_NORM_RMS, true); else H3B_RNQ(false, H3B_NORM_RMS, false);
+      if (fp4) H3B_RMS(false, true); else H3B_RMS(false, false);
     }
+#undef H3B_RMS
   } else {
     constexpr int LN_WARPS = ln_warps<C>();
     const int64_t blocks = (a.rows + LN_WARPS - 1) / LN_WARPS, cap = (int64_t)sms;
