@@ -456,8 +456,19 @@ __global__ void __launch_bounds__(NWARP * 32, 3) prologue_item_kernel(const ProA
       kmax = fmax3(kmax, fabsf(ko[j]), fabsf(ko[j + 1]));
       vmax = fmax3(vmax, fabsf(vf[j]), fabsf(vf[j + 1]));
     }
-    *reinterpret_cast<uint2*>(buf + (0 * TILE + i) * D + l * 4) = qw;
-    *reinterpret_cast<uint2*>(buf + (1 * TILE + i) * D + l * 4) = kw;
+    if constexpr (TILE_QK) {
+      *reinterpret_cast<uint2*>(buf + (0 * TILE + i) * D + l * 4) = qw;
+      *reinterpret_cast<uint2*>(buf + (1 * TILE + i) * D + l * 4) = kw;
+    } else {  // static Q/K scales: the codes need no tile maximum and are written at once (only V is staged)
+      const size_t dst = ((size_t)h * a.rows_pad + (size_t)ti * TILE + i) * D + l * 4;
+#pragma unroll
+      for (int j = 0; j < 4; j += 2) {
+        mul2(qo[j], qo[j + 1], a.inv_sq, a.inv_sq);
+        mul2(ko[j], ko[j + 1], a.inv_sk, a.inv_sk);
+      }
+      *reinterpret_cast<uint32_t*>(a.qb + dst) = e4m3x4(qo[0], qo[1], qo[2], qo[3]);
+      *reinterpret_cast<uint32_t*>(a.kb + dst) = e4m3x4(ko[0], ko[1], ko[2], ko[3]);
+    }
     *reinterpret_cast<uint2*>(buf + (2 * TILE + i) * D + l * 4) = vw;
   }
 #pragma unroll
@@ -510,23 +521,27 @@ __global__ void __launch_bounds__(NWARP * 32, 3) prologue_item_kernel(const ProA
     const int i = w + u * NWARP;
     if (i >= n) break;
     const size_t dst = (plane + i) * D + l * 4;
-    float qv[4], kv[4], vv[4];
-    unpack4(*reinterpret_cast<const uint2*>(buf + (0 * TILE + i) * D + l * 4), qv);
-    unpack4(*reinterpret_cast<const uint2*>(buf + (1 * TILE + i) * D + l * 4), kv);
+    if constexpr (TILE_QK) {
+      float qv[4], kv[4];
+      unpack4(*reinterpret_cast<const uint2*>(buf + (0 * TILE + i) * D + l * 4), qv);
+      unpack4(*reinterpret_cast<const uint2*>(buf + (1 * TILE + i) * D + l * 4), kv);
+#pragma unroll
+      for (int j = 0; j < 4; j += 2) {
+        mul2(qv[j], qv[j + 1], inv_q, inv_q);
+        mul2(kv[j], kv[j + 1], inv_k, inv_k);
+      }
+      if constexpr (QK_I8) {
+        *reinterpret_cast<uint32_t*>(a.qb + dst) = s8x4(qv[0], qv[1], qv[2], qv[3]);
+        *reinterpret_cast<uint32_t*>(a.kb + dst) = s8x4(kv[0], kv[1], kv[2], kv[3]);
+      } else {
+        *reinterpret_cast<uint32_t*>(a.qb + dst) = e4m3x4(qv[0], qv[1], qv[2], qv[3]);
+        *reinterpret_cast<uint32_t*>(a.kb + dst) = e4m3x4(kv[0], kv[1], kv[2], kv[3]);
+      }
+    }
+    float vv[4];
     unpack4(*reinterpret_cast<const uint2*>(buf + (2 * TILE + i) * D + l * 4), vv);
 #pragma unroll
-    for (int j = 0; j < 4; j += 2) {
-      mul2(qv[j], qv[j + 1], inv_q, inv_q);
-      mul2(kv[j], kv[j + 1], inv_k, inv_k);
-      mul2(vv[j], vv[j + 1], inv_v, inv_v);
-    }
-    if constexpr (QK_I8) {
-      *reinterpret_cast<uint32_t*>(a.qb + dst) = s8x4(qv[0], qv[1], qv[2], qv[3]);
-      *reinterpret_cast<uint32_t*>(a.kb + dst) = s8x4(kv[0], kv[1], kv[2], kv[3]);
-    } else {
-      *reinterpret_cast<uint32_t*>(a.qb + dst) = e4m3x4(qv[0], qv[1], qv[2], qv[3]);
-      *reinterpret_cast<uint32_t*>(a.kb + dst) = e4m3x4(kv[0], kv[1], kv[2], kv[3]);
-    }
+    for (int j = 0; j < 4; j += 2) mul2(vv[j], vv[j + 1], inv_v, inv_v);
     const uint32_t vcodes = e4m3x4(vv[0], vv[1], vv[2], vv[3]);
     if (a.v16)
       *reinterpret_cast<uint2*>(a.vb + 2 * dst) = e4m3x4_to_f16x4(vcodes);
