@@ -32,7 +32,7 @@ ROOT = Path(__file__).resolve().parent
 # a file so stdout keeps the one JSON line; rank 0 quotes its "nRanks" lines in the line. Set before torch is imported:
 # NCCL reads these variables once, at its first call.
 NCCL_LOG = None
-if int(os.environ.get("WORLD_SIZE", "1")) > 1 and "NCCL_DEBUG" not in os.environ:
+if int(os.environ.get("WORLD_SIZE", "1")) > 1 and os.environ.get("NCCL_DEBUG", "").upper() not in ("INFO", "TRACE"):
     NCCL_LOG = f"/tmp/h3b_bench_nccl.{os.getpid()}.log"
     os.environ.update(NCCL_DEBUG="INFO", NCCL_DEBUG_SUBSYS="INIT", NCCL_DEBUG_FILE=NCCL_LOG)
 sys.path.insert(0, str(ROOT))
@@ -320,9 +320,9 @@ def fp8_chain_secondary(pkg, dev, stream, args) -> dict:
 
 
 def sp_bitexact_check(pkg, dev, ws) -> dict:
-    """Two blocks on the (7, 16, 16) latent (32 tiles, 1792 tokens) sequence-parallel over every rank of this job (the
-    NCCL all-to-alls of the runner), compared bit for bit with one rank's runner on the same input, which every rank
-    also runs on its own GPU. Every step of the sharded block is row-, tile- or (head, tile)-local, so the two must
+    """Two blocks on the (7, 16, 16) latent (32 tiles, 1792 tokens) sequence-parallel over every rank of this job (with
+    the runner's default head exchange -- the peer transport where available -- and with NCCL all-to-alls), compared
+    bit for bit with one rank's runner on the same input, which every rank also runs on its own GPU. Every step of the sharded block is row-, tile- or (head, tile)-local, so the two must
     agree exactly; the result is the minimum over ranks. Also counts the ranks that answer one NCCL all-reduce."""
     import torch
     import torch.distributed as dist
@@ -335,15 +335,26 @@ def sp_bitexact_check(pkg, dev, ws) -> dict:
     temb = m.timestep_embedding(0.5)
     meta = pkg.runner.VsaMeta(grid=grid, topk=8)
     ref = pkg.runner.H3FastRunner(m).forward(x, temb, None, None, meta, context=ctx)
-    got = pkg.runner.H3FastRunner(m, pkg.sp.SeqParallel()).forward(x, temb, None, None, meta, context=ctx)
-    same = torch.tensor([1 if torch.equal(got.view(torch.int16), ref.view(torch.int16)) else 0], device=dev)
+    flags, transports = [], []
+    for exchange in ("auto", "nccl"):  # the transport the step uses (peer when available), then NCCL
+        if exchange == "nccl" and transports and transports[0] == "nccl":
+            break
+        r = pkg.runner.H3FastRunner(m, pkg.sp.SeqParallel(), exchange=exchange)
+        got = r.forward(x, temb, None, None, meta, context=ctx)
+        flags.append(1 if torch.equal(got.view(torch.int16), ref.view(torch.int16)) else 0)
+        transports.append(r.transport)
+        if ws > 1:
+            torch.cuda.synchronize()
+            r.close()
+    same = torch.tensor(flags, device=dev)
     seen = torch.ones(1, device=dev, dtype=torch.int32)
     if ws > 1:
         dist.all_reduce(same, op=dist.ReduceOp.MIN)
         dist.all_reduce(seen)
     del m, x, ctx, ref, got
     torch.cuda.empty_cache()
-    return {"sp_bitexact": bool(same.item()), "grid": list(grid), "blocks": 2, "ranks_in_nccl_allreduce": int(seen.item()),
+    return {"sp_bitexact": bool(same.min().item()), "per_transport": dict(zip(transports, map(bool, same.tolist()))),
+            "grid": list(grid), "blocks": 2, "ranks_in_nccl_allreduce": int(seen.item()),
             "backend": dist.get_backend() if ws > 1 else None}
 
 
@@ -384,7 +395,7 @@ def dit_step_secondary(pkg, dev, stream, args, ws) -> dict:
             torch.cuda.empty_cache()
         dist.barrier()
     sp = pkg.sp.SeqParallel() if ws > 1 else None
-    r = pkg.runner.H3FastRunner(m, sp)
+    r = pkg.runner.H3FastRunner(m, sp, exchange=args.dit_exchange)
     for _ in range(2):
         out = r.forward(x, temb, None, None, meta, context=ctx)
     torch.cuda.synchronize()
@@ -403,21 +414,51 @@ def dit_step_secondary(pkg, dev, stream, args, ws) -> dict:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
         dist.barrier()
-        # one more step with device events around every all-to-all: per-exchange time per step (max over ranks)
+        # one more step with device events around every exchange on the compute stream: per-kind time per step (max
+        # over ranks). NCCL: each all-to-all, waiting for the slowest rank included. Peer transport: the bounded waits
+        # for the peers' flags, i.e. the exchange time left exposed after the copies overlapped the attention
         r.ex.timing = []
         out = r.forward(x, temb, None, None, meta, context=ctx)
         torch.cuda.synchronize()
-        names = ["qkv_e4m3", "tile_stats", "attn_out_bf16"]
+        names = (["wait_tile_stats", "wait_qkv", "wait_attn_out"] if r.transport == "peer" else
+                 ["qkv_e4m3", "tile_stats", "attn_out_bf16"])
         per = {nm: 0.0 for nm in names}
         for nm, a, b in r.ex.timing:
             per[nm] += a.elapsed_time(b)
         r.ex.timing = None
         t = torch.tensor([per[nm] for nm in names], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        exchange = {"ms_per_step": dict(zip(names, t.tolist())),
-                    "note": "device time of each kind of all-to-all summed over the 50 blocks of one step (max over "
-                            "ranks); each exchange includes waiting for the slowest rank to reach it"}
+        exchange = {"transport": r.transport, "head_groups": r.head_groups, "ms_per_step": dict(zip(names, t.tolist())),
+                    "note": ("time the compute stream waited for the peers' flags (Q/K/V and outputs copied by the "
+                             "copy engines into peer-mapped buffers while attention ran), summed over the blocks of "
+                             "one step, max over ranks" if r.transport == "peer" else
+                             "device time of each kind of all-to-all summed over the blocks of one step (max over "
+                             "ranks); each exchange includes waiting for the slowest rank to reach it")}
+        if r.transport_note:
+            exchange["peer_unavailable"] = r.transport_note[:300]
         dist.barrier()
+        if r.transport == "peer" and not args.no_nccl_compare:
+            # the same step with the NCCL all-to-all transport (all heads at once, no overlap), same job
+            try:
+                rn = pkg.runner.H3FastRunner(m, sp, exchange="nccl")
+                for _ in range(2):
+                    out = rn.forward(x, temb, None, None, meta, context=ctx)
+                torch.cuda.synchronize()
+                dist.barrier()
+                e0.record(stream)
+                for _ in range(reps):
+                    out = rn.forward(x, temb, None, None, meta, context=ctx)
+                e1.record(stream)
+                torch.cuda.synchronize()
+                t = torch.tensor([e0.elapsed_time(e1) / reps], device=dev, dtype=torch.float64)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                exchange["nccl_transport_ms_per_step"] = float(t.item())
+            except Exception as exc:  # an extra timing must not cost the line; its error is reported
+                exchange["nccl_transport_error"] = repr(exc)[:300]
+            finally:
+                rn = None
+                torch.cuda.empty_cache()
+            dist.barrier()
     finite = bool(torch.isfinite(out.float()).all())
     reduced = None
     if args.dit_extras and ws == 1 and not args.dit_reduction:
@@ -521,6 +562,8 @@ def dit_step_secondary(pkg, dev, stream, args, ws) -> dict:
             rs = None
             torch.cuda.empty_cache()
     lin = 2.0 * S * (6 * cfg.hidden ** 2 + 2 * cfg.hidden * cfg.ffn) * cfg.blocks
+    if ws > 1:
+        r.close()
     del r, m, x, out
     torch.cuda.empty_cache()
     res = {"grid": list(grid), "tokens": S, "blocks": cfg.blocks, "topk": args.dit_topk, "n_gpus": ws,
@@ -923,6 +966,12 @@ def main() -> None:
                     help="also time the config-5 step with INT8 QK^T in the self-attention")
     ap.add_argument("--dit-ffn-static", action="store_true",
                     help="also time the config-5 step with the FFN re-quantized in fc_in's epilogue (static scales)")
+    ap.add_argument("--dit-exchange", choices=["auto", "peer", "nccl"], default="auto",
+                    help="head exchange of the sequence-parallel config-5 step: peer-mapped buffers written by the "
+                         "copy engines with head groups pipelined behind the attention (auto: when every rank maps "
+                         "every other's memory), or NCCL all-to-alls")
+    ap.add_argument("--no-nccl-compare", action="store_true",
+                    help="with the peer transport, skip timing the same config-5 step over NCCL in the same job")
     ap.add_argument("--dit-reduction", default="", metavar="BEGIN:END[:SCALE]",
                     help="also time the config-5 step with token reduction over blocks [BEGIN, END) (one GPU)")
     ap.add_argument("--steps", type=int, default=100)

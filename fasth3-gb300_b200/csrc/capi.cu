@@ -25,6 +25,7 @@ namespace h3b {
 int gemm_status_async(int* dst, int clear, cudaStream_t stream);
 int attn_status_async(int* dst, int clear, cudaStream_t stream);
 int rows_status_async(int* dst, int clear, cudaStream_t stream);
+int peer_status_async(int* dst, int clear, cudaStream_t stream);
 }  // namespace h3b
 
 extern "C" const char* h3b_last_error(void) { return h3b::g_last_error; }
@@ -34,7 +35,8 @@ extern "C" int h3b_status_async(int* dst, int clear, cudaStream_t stream) {
   H3B_REQUIRE(dst, "status_async: null destination");
   if (int rc = h3b::gemm_status_async(dst, clear, stream)) return rc;
   if (int rc = h3b::attn_status_async(dst + 1, clear, stream)) return rc;
-  return h3b::rows_status_async(dst + 2, clear, stream);
+  if (int rc = h3b::rows_status_async(dst + 2, clear, stream)) return rc;
+  return h3b::peer_status_async(dst + 3, clear, stream);
 }
 
 extern "C" const char* h3b_version(void) { return "h3b 0.1 sm_100a"; }

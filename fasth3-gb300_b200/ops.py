@@ -278,18 +278,19 @@ _status_bufs: dict = {}
 
 def check_status(device: torch.device | str | None = None) -> None:
     """Reads the kernels' device status words after everything enqueued so far on the current stream (one host sync)
-    and raises ``RuntimeError`` if a GEMM, attention or row kernel reported a failure since the last check (the words are
+    and raises ``RuntimeError`` if a GEMM, attention, row kernel or exchange wait reported a failure since the last check (the words are
     cleared by the read). The runner calls this once per step, after the step's last kernel."""
     dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
     if dev.index is None:
         dev = torch.device("cuda", torch.cuda.current_device())
     buf = _status_bufs.get(dev.index)
     if buf is None:
-        buf = _status_bufs[dev.index] = torch.zeros(3, dtype=torch.int32).pin_memory()
+        buf = _status_bufs[dev.index] = torch.zeros(4, dtype=torch.int32).pin_memory()
     stream = torch.cuda.current_stream(dev)
     call("h3b_status_async", buf.data_ptr(), 1, stream.cuda_stream)
     stream.synchronize()
-    words = (("GEMM", int(buf[0])), ("attention", int(buf[1])), ("row kernels", int(buf[2])))
+    words = (("GEMM", int(buf[0])), ("attention", int(buf[1])), ("row kernels", int(buf[2])),
+             ("exchange waits", int(buf[3])))
     if any(v for _, v in words):
         parts = [f"{who}: {_STATUS_NAMES.get(v, v)}" for who, v in words if v]
         raise RuntimeError("h3b device status after the step -- " + "; ".join(parts))

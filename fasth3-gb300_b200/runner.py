@@ -32,7 +32,7 @@ from . import ops
 from .layout import TILE, TileLayout, compute_topk, rope_3d, rope_positions, tile_layout, tile_layout_from_metadata
 from .model import DiTModel, QuantLinear
 from .reduction import TokenReduction, pair_maps
-from .sp import SeqParallel
+from .sp import PeerArena, SeqParallel, peer_copy_plan
 
 LOG2E = 1.4426950408889634
 
@@ -156,6 +156,47 @@ class _Exchange:
             for p in range(P):
                 outs[r][p * Hl:(p + 1) * Hl].copy_(ys[p][r])
 
+    def heads_exchange(self, xs: list[torch.Tensor], outs: list[torch.Tensor], name: str = "qkv_e4m3") -> None:
+        """One plane of Q, K or V: [H, R, D] per rank -> [G, P, Hg, R, D] per rank (head group g, source rank p: heads
+        p*Hl + g*Hg .. of rank p's rows). Over NCCL G is 1 ([1, P, Hl, R, D] is the all-to-all's [P, Hl, R, D])."""
+        P = self.world
+        G = outs[0].shape[0]
+        if not self.virtual:
+            if P == 1:
+                if outs[0].data_ptr() != xs[0].data_ptr():
+                    outs[0].view(xs[0].shape).copy_(xs[0])
+                return
+            if G != 1:
+                raise ValueError("the NCCL exchange sends all heads at once (one head group)")
+            self._a2a(name, outs[0][0], xs[0])
+            return
+        Hl = xs[0].shape[0] // P
+        Hg = Hl // G
+        for r in range(P):
+            for g in range(G):
+                for p in range(P):
+                    outs[r][g, p].copy_(xs[p][r * Hl + g * Hg:r * Hl + (g + 1) * Hg])
+
+    def heads_return(self, ys: list[torch.Tensor], outs: list[torch.Tensor], name: str = "attn_out_bf16") -> None:
+        """The attention output: [G, P, Hg, R, D] per rank -> [H, R, D] per rank (heads-first order)."""
+        P = self.world
+        G = ys[0].shape[0]
+        if not self.virtual:
+            if P == 1:
+                if outs[0].data_ptr() != ys[0].data_ptr():
+                    outs[0].copy_(ys[0].view(outs[0].shape))
+                return
+            if G != 1:
+                raise ValueError("the NCCL exchange sends all heads at once (one head group)")
+            self._a2a(name, outs[0], ys[0][0])
+            return
+        Hg = ys[0].shape[2]
+        Hl = G * Hg
+        for r in range(P):
+            for g in range(G):
+                for p in range(P):
+                    outs[r][p * Hl + g * Hg:p * Hl + (g + 1) * Hg].copy_(ys[p][g, r])
+
     def all_gather_rows(self, xs: list[torch.Tensor], rows: list[int]) -> torch.Tensor:
         """Concatenation over ranks (in rank order) of each rank's [rows_r, C] block; ``rows`` holds every rank's
         row count."""
@@ -183,6 +224,7 @@ class _RankState:
     n_local: int
     tok_index: torch.Tensor  # int64 [rows] global token of each local row
     b: dict = field(default_factory=dict)
+    arena: PeerArena | None = None  # the receive buffers and flags of the peer transport
 
 
 def _fused_rows(lins: list[QuantLinear]) -> dict:
@@ -217,7 +259,7 @@ class H3FastRunner:
     (exact scores; E4M3 otherwise). ``v_f16``: V tiles as f16 (see below)."""
 
     def __init__(self, model: DiTModel, sp: SeqParallel | VirtualSeqParallel | None = None, qk_int8: bool = False,
-                 v_f16: bool = False, ffn_requant: str = "rows"):
+                 v_f16: bool = False, ffn_requant: str = "rows", exchange: str = "auto", head_groups: int | None = None):
         self.model = model
         self.qk_int8 = bool(qk_int8)
         # FFN re-quantization between fc_in and fc_out: "rows" -- the reference's rule, the bf16 fc_in output
@@ -263,6 +305,58 @@ class H3FastRunner:
         # read the kernels' device status words after each forward's last kernel and raise on a failure (a bounded
         # wait that expired, a selection list longer than the attention kernel holds); costs one host sync per step
         self.check_status = True
+        # the head exchange's transport: "local" (one rank), "virtual" (emulated ranks), "nccl" (all_to_all_single),
+        # or "peer" (copy engines into peer-mapped receive buffers with flag words, sp.PeerArena); "auto" takes
+        # "peer" when every rank can map every other rank's memory, else NCCL
+        if exchange not in ("auto", "peer", "nccl"):
+            raise ValueError(f"exchange must be 'auto', 'peer' or 'nccl', not {exchange!r}")
+        P = self.ex.world
+        self.transport_note = None
+        if P == 1:
+            self.transport = "local"
+        elif self.ex.virtual:
+            self.transport = "virtual"
+        elif exchange == "nccl":
+            self.transport = "nccl"
+        else:
+            why = self._peer_probe()
+            if why is not None and exchange == "peer":
+                raise RuntimeError(f"peer exchange unavailable: {why}")
+            self.transport, self.transport_note = ("peer", None) if why is None else ("nccl", why)
+        # head groups of the attention pipeline: with the peer transport, group g's attention runs while later groups'
+        # Q/K/V are still arriving and earlier groups' outputs are on their way back (the virtual transport uses the
+        # same layout, so one GPU tests it); NCCL and one rank take all heads at once
+        Hl = self.heads // P
+        if head_groups is None:
+            G = 1 if self.transport in ("local", "nccl") else \
+                next(d for d in range(min(4, Hl), Hl + 1) if Hl % d == 0)
+        else:
+            G = int(head_groups)
+            if G < 1 or Hl % G or (G > 1 and self.transport in ("local", "nccl")):
+                raise ValueError(f"head_groups={G}: must divide the {Hl} heads per rank; more than one group needs "
+                                 f"the peer or virtual transport")
+        self.head_groups = G
+        self._epoch = 0  # exchanges so far (the peer transport's flag value), the same count on every rank
+        self._copy_streams: list | None = None
+
+    def _peer_probe(self) -> str | None:
+        """Maps a small arena over the ranks and releases it (collective): None when every rank can map every other
+        rank's memory, else why not."""
+        try:
+            ar = PeerArena(self.ex.sp, self.dev, {"probe": ((4096,), torch.uint8)}, 1)
+        except RuntimeError as exc:
+            return str(exc)
+        ar.close(self.ex.sp.group)
+        return None
+
+    def close(self) -> None:
+        """Releases the peer arenas of every layout (collective over the ranks when the transport is "peer")."""
+        for _, states in self.layouts.values():
+            for st in states:
+                if st.arena is not None:
+                    st.arena.close(self.ex.sp.group)
+                    st.arena = None
+        self.layouts.clear()
 
     def refresh_weights(self) -> None:
         """(Re)builds the GEMM B operands of every block from its linears' packed weights: at construction, and after
@@ -355,40 +449,68 @@ class H3FastRunner:
             b["h_sf"] = torch.zeros(ops.sf_rows(R), C // 16, device=dev, dtype=u8) if self.fp4 else None
             b["hs"] = torch.empty(R, device=dev, dtype=f32)
             b["qkv"] = torch.empty(R, 3 * C, device=dev, dtype=bf)
-            for nm in ("qb", "kb", "vb"):
-                dt = self.v_dtype if nm == "vb" else u8
-                b[nm] = torch.zeros(H, rows_pad, D, device=dev, dtype=dt)
-                b[nm + "_x"] = torch.zeros(P, Hl, rows_pad, D, device=dev, dtype=dt) if P > 1 else \
-                    b[nm].view(1, H, rows_pad, D)
+            # E4M3 (or int8) Q, K and V planes [H, rows_pad, 128] of this rank's rows; Q/K (and an E4M3 V) are planes
+            # of one tensor so one 2D copy sends all of a head group's planes. Head-sharded side: [G, P, Hg, rows_pad,
+            # 128] per plane -- head group g, chunk p = rank p's rows (what the attention kernel reads with chunks=P)
+            G = self.head_groups
+            Hg = Hl // G
+            planes = 3 if self.v_dtype == u8 else 2
+            peer = self.transport == "peer"
+            stat_names = [("qs", ()), ("ks", ()), ("vs", ()), ("qp", (D,)), ("kp", (D,))]
+            if self.side is not None:
+                stat_names.append(("vp", (D,)))
+            b["qkv_s"] = torch.zeros(planes, H, rows_pad, D, device=dev, dtype=u8)
+            b["qb"], b["kb"] = b["qkv_s"][0], b["qkv_s"][1]
+            b["vb"] = b["qkv_s"][2] if planes == 3 else torch.zeros(H, rows_pad, D, device=dev, dtype=self.v_dtype)
+            if peer:  # every receive buffer in one allocation that the other ranks map
+                regions = {"qkv_x": ((planes, G, P, Hg, rows_pad, D), u8)}
+                if planes == 2:
+                    regions["v_x"] = ((G, P, Hg, rows_pad, D), self.v_dtype)
+                for nm, tail in stat_names:
+                    regions[nm + "_all"] = ((Hl, n_all, *tail), f32)
+                regions["ob"] = ((H, rows_pad, D), bf)
+                st.arena = PeerArena(self.ex.sp, dev, regions, 1 + 2 * G)
+                rx = st.arena.tensors
+            else:
+                rx = {}
+            if P == 1:
+                b["qkv_x"] = b["qkv_s"].view(planes, 1, 1, H, rows_pad, D)
+                v_x = b["vb"].view(1, 1, H, rows_pad, D)
+            else:
+                b["qkv_x"] = rx["qkv_x"] if peer else torch.zeros(planes, G, P, Hg, rows_pad, D, device=dev, dtype=u8)
+                v_x = None if planes == 3 else (rx["v_x"] if peer else
+                                                torch.zeros(G, P, Hg, rows_pad, D, device=dev, dtype=self.v_dtype))
+            b["qb_x"], b["kb_x"] = b["qkv_x"][0], b["qkv_x"][1]
+            b["vb_x"] = b["qkv_x"][2] if planes == 3 else v_x
             # per (head, tile) E4M3 scales and tile means, local tiles; their exchange buffers; all tiles
-            for nm, tail in (("qs", ()), ("ks", ()), ("vs", ()), ("qp", (D,)), ("kp", (D,))):
+            for nm, tail in stat_names:
                 b[nm] = torch.zeros(H, n_local, *tail, device=dev, dtype=f32)
-                if P > 1:
-                    b[nm + "_x"] = torch.zeros(P, Hl, n_local, *tail, device=dev, dtype=f32)
-                    b[nm + "_all"] = torch.zeros(Hl, n_all, *tail, device=dev, dtype=f32)
-                else:
+                if P == 1:
                     b[nm + "_x"] = b[nm].view(1, H, n_local, *tail)
                     b[nm + "_all"] = b[nm]
-            b["vp"] = torch.empty(H, n_local, D, device=dev, dtype=f32)
-            if self.side is not None:  # gate-compress branch
+                elif peer:  # written in global tile order by the senders' copies
+                    b[nm + "_all"] = rx[nm + "_all"]
+                else:
+                    b[nm + "_x"] = torch.zeros(P, Hl, n_local, *tail, device=dev, dtype=f32)
+                    b[nm + "_all"] = torch.zeros(Hl, n_all, *tail, device=dev, dtype=f32)
+            if self.side is None:
+                b["vp"] = torch.empty(H, n_local, D, device=dev, dtype=f32)
+            else:  # gate-compress branch
                 b["g"] = torch.empty(R, C, device=dev, dtype=bf)
                 b["oc"] = torch.zeros(H, n_local, D, device=dev, dtype=bf)
                 if P > 1:
-                    b["vp_x"] = torch.zeros(P, Hl, n_local, D, device=dev, dtype=f32)
-                    b["vp_all"] = torch.zeros(Hl, n_all, D, device=dev, dtype=f32)
                     b["oc_all"] = torch.zeros(Hl, n_all, D, device=dev, dtype=bf)
                     b["oc_x"] = torch.zeros(P, Hl, n_local, D, device=dev, dtype=bf)
                 else:
-                    b["vp_x"], b["vp_all"] = b["vp"].view(1, H, n_local, D), b["vp"]
                     b["oc_all"], b["oc_x"] = b["oc"], b["oc"].view(1, H, n_local, D)
             b["vs_head"] = torch.empty(Hl, device=dev, dtype=f32)
             b["sc"] = torch.empty(Hl, n_all, n_all, device=dev, dtype=f32)
             b["idx"] = torch.empty(Hl, n_all, n_all, device=dev, dtype=i32)
             b["num"] = torch.zeros(Hl, n_all, device=dev, dtype=i32)
             b["vbs_all"] = full.vbs.to(dev)
-            b["ob"] = torch.zeros(H, rows_pad, D, device=dev, dtype=bf)
-            b["ob_x"] = torch.zeros(P, Hl, rows_pad, D, device=dev, dtype=bf) if P > 1 else \
-                b["ob"].view(1, H, rows_pad, D)
+            b["ob"] = rx["ob"] if peer else torch.zeros(H, rows_pad, D, device=dev, dtype=bf)
+            b["ob_x"] = torch.zeros(G, P, Hg, rows_pad, D, device=dev, dtype=bf) if P > 1 else \
+                b["ob"].view(1, 1, H, rows_pad, D)
             b["a"] = torch.empty(R, hb, device=dev, dtype=u8)
             b["a_sf"] = torch.zeros(ops.sf_rows(R), C // 16, device=dev, dtype=u8) if self.fp4 else None
             b["as"] = torch.empty(R, device=dev, dtype=f32)
@@ -579,15 +701,26 @@ class H3FastRunner:
             self._t(i, "prologue", st, qb=b["qb"], kb=b["kb"], vb=b["vb"], qs=b["qs"], ks=b["ks"], vs=b["vs"],
                     qp=b["qp"], kp=b["kp"])
         # ---- sequence -> heads
-        for nm in ("qb", "kb", "vb"):
-            self.ex.seq_to_heads([st.b[nm] for st in states], [st.b[nm + "_x"] for st in states], "qkv_e4m3")
-        for nm in ("qs", "ks", "vs", "qp", "kp") + (("vp",) if gate else ()):
-            self.ex.seq_to_heads([st.b[nm] for st in states], [st.b[nm + "_x"] for st in states], "tile_stats")
+        G = self.head_groups
+        Hg = Hl // G
+        peer = self.transport == "peer"
+        stats = ("qs", "ks", "vs", "qp", "kp") + (("vp",) if gate else ())
+        if peer:
+            self._epoch += 1
+            self._peer_send_heads(states[0], stats)
+        else:
+            planes = [("qb", "qb_x"), ("kb", "kb_x"), ("vb", "vb_x")]
+            for src, dst in planes:
+                self.ex.heads_exchange([st.b[src] for st in states], [st.b[dst] for st in states], "qkv_e4m3")
+            for nm in stats:
+                self.ex.seq_to_heads([st.b[nm] for st in states], [st.b[nm + "_x"] for st in states], "tile_stats")
         # ---- coarse step and sparse attention over this rank's heads, every rank's rows
         for st in states:
             b = st.b
-            if P > 1:  # [P, Hl, n_local, ...] -> [Hl, n_all, ...] in global tile order
-                for nm in ("qs", "ks", "vs", "qp", "kp") + (("vp",) if gate else ()):
+            if peer:
+                self._peer_wait(st, 0, 1, "wait_tile_stats")
+            elif P > 1:  # [P, Hl, n_local, ...] -> [Hl, n_all, ...] in global tile order
+                for nm in stats:
                     src = b[nm + "_x"]
                     b[nm + "_all"].copy_(src.transpose(0, 1).reshape(b[nm + "_all"].shape))
             torch.amax(b["vs_all"], dim=1, out=b["vs_head"])
@@ -603,17 +736,27 @@ class H3FastRunner:
                     ks_all=b["ks_all"], vs_all=b["vs_all"], qp_all=b["qp_all"], kp_all=b["kp_all"],
                     vs_head=b["vs_head"], sc=b["sc"], idx=b["idx"], num=b["num"], vp_all=b.get("vp_all"))
             lse2 = self._buf(b, "lse2", (Hl, st.rows_pad), torch.float32) if sel["split"] else None
-            ops.vsa_fp8_ex(b["qb_x"], b["kb_x"], b["vb_x"], b["ob_x"], b["idx"], b["num"], b["vbs_all"],
-                           b["vbs_all"], b["vs_all"], b["vs_head"], sm_scale * LOG2E, Hl, n_all, n_all, st.rows_pad,
-                           st.rows_pad, chunks_q=P, chunks_kv=P, qs=b["qs_all"], ks=b["ks_all"], lse=lse2,
-                           idx_ld=n_all, q_scale_ld=n_all, kv_scale_ld=n_all, qk_int8=self.qk_int8)
+            for g in range(G):  # head group g: [P, Hg, rows_pad, 128] planes, heads g*Hg .. of this rank's
+                hs = slice(g * Hg, (g + 1) * Hg)
+                if peer:
+                    self._peer_wait(st, 1 + g, 1, "wait_qkv")
+                ops.vsa_fp8_ex(b["qb_x"][g], b["kb_x"][g], b["vb_x"][g], b["ob_x"][g], b["idx"][hs], b["num"][hs],
+                               b["vbs_all"], b["vbs_all"], b["vs_all"][hs], b["vs_head"][hs], sm_scale * LOG2E, Hg,
+                               n_all, n_all, st.rows_pad, st.rows_pad, chunks_q=P, chunks_kv=P, qs=b["qs_all"][hs],
+                               ks=b["ks_all"][hs], lse=None if lse2 is None else lse2[hs], idx_ld=n_all,
+                               q_scale_ld=n_all, kv_scale_ld=n_all, qk_int8=self.qk_int8)
+                if peer:
+                    self._peer_send_out(st, g)
             if sel["split"]:
                 self._dense_prefix(st, sel["prefix"], n_all, sm_scale)
                 self._t(i, "dense_prefix", st, o1=b["o1"], lse1a=b["lse1a"], lse1b=b["lse1b"], lse2=b["lse2"],
                         ob_x=b["ob_x"])
             self._t(i, "attn", st, ob_x=b["ob_x"])
         # ---- heads -> sequence
-        self.ex.heads_to_seq([st.b["ob_x"] for st in states], [st.b["ob"] for st in states], "attn_out_bf16")
+        if peer:
+            self._peer_wait(states[0], 1 + G, G, "wait_attn_out")
+        else:
+            self.ex.heads_return([st.b["ob_x"] for st in states], [st.b["ob"] for st in states], "attn_out_bf16")
         if gate:
             main.wait_stream(self.side)
             if P > 1:  # [Hl, n_all, D] -> [P, Hl, n_local, D] -> every head of this rank's tiles
@@ -747,6 +890,86 @@ class H3FastRunner:
         lse_rows = lse_b[:, slot] * math.log(2.0)  # log2 -> natural log
         self._buf(b, "lse1a", (H, n_pre_rows), torch.float32).copy_(lse_rows[:, :n_pre_rows])
         self._buf(b, "lse1b", (H, R - n_pre_rows), torch.float32).copy_(lse_rows[:, n_pre_rows:])
+
+    # ------------------------------------------------------------------------------------------------- peer transport
+    def _peer_streams(self) -> list:
+        """One copy stream per destination rank (this one included), so the copies to different ranks can run on
+        different copy engines."""
+        if self._copy_streams is None:
+            self._copy_streams = [torch.cuda.Stream(self.dev) for _ in range(self.ex.world)]
+        return self._copy_streams
+
+    def _peer_dims(self, st: _RankState) -> dict:
+        return {"P": self.ex.world, "H": self.heads, "G": self.head_groups, "R": st.rows_pad, "D": self.head_dim}
+
+    def _peer_send_heads(self, st: _RankState, stats: tuple) -> None:
+        """Sequence -> heads over the peer transport, enqueued after the prologue: to every rank p (itself included),
+        on p's copy stream, the tile statistics of p's heads into p's [Hl, n_all, ...] buffers at this rank's tile
+        columns, then flag slot 0; then head group by head group the Q/K/V planes of p's heads g*Hg .. into p's
+        [planes, G, P, Hg, rows_pad, 128] buffer at (g, this rank), then flag slot 1 + g. Nothing here overwrites
+        what a receiver still reads: a rank sends block i+1 only after its own gate quantizer of block i, which waited
+        for every rank's attention outputs of block i, i.e. after every rank's last read of its receive buffers."""
+        from ._lib import call
+        ar, b, P, r = st.arena, st.b, self.ex.world, self.ex.sp.rank
+        main = torch.cuda.current_stream(self.dev)
+        ready = torch.cuda.Event()
+        ready.record(main)
+        e = self._epoch
+        dims = self._peer_dims(st)
+        parts = [("qkv_x", b["qkv_s"], b["qkv_s"].shape[0], 1)]
+        if b["qkv_s"].shape[0] == 2:
+            parts.append(("v_x", b["vb"], 1, b["vb"].element_size()))
+        streams = self._peer_streams()
+        for k in range(P):
+            p = (r + 1 + k) % P
+            cs = streams[p]
+            cs.wait_event(ready)
+            h = cs.cuda_stream
+            for nm in stats:
+                src = b[nm]
+                T = src[0, 0].numel()
+                so, spitch, do, dpitch, w, rows = peer_copy_plan("stats", r, p, 0, dict(dims, n=st.n_local, T=T, es=4))
+                call("h3b_peer_copy2d", ar.ptr(p, nm + "_all", do), dpitch, src.data_ptr() + so, spitch, w, rows, h)
+            call("h3b_peer_signal", ar.flag(p, 0, r), e, h)
+            for g in range(self.head_groups):
+                for region, src, planes, es in parts:
+                    so, spitch, do, dpitch, w, rows = peer_copy_plan("qkv", r, p, g, dict(dims, planes=planes, es=es))
+                    call("h3b_peer_copy2d", ar.ptr(p, region, do), dpitch, src.data_ptr() + so, spitch, w, rows, h)
+                call("h3b_peer_signal", ar.flag(p, 1 + g, r), e, h)
+
+    def _peer_send_out(self, st: _RankState, g: int) -> None:
+        """Heads -> sequence of head group g, enqueued after its attention: chunk p of the group's output (rank p's
+        rows) into rank p's [H, rows_pad, 128] buffer at heads r*Hl + g*Hg .., then flag slot 1 + G + g."""
+        from ._lib import call
+        ar, b, P, r = st.arena, st.b, self.ex.world, self.ex.sp.rank
+        main = torch.cuda.current_stream(self.dev)
+        done = torch.cuda.Event()
+        done.record(main)
+        dims = dict(self._peer_dims(st), es=2)
+        src = b["ob_x"].data_ptr()
+        streams = self._peer_streams()
+        for k in range(P):
+            p = (r + 1 + k) % P
+            cs = streams[p]
+            cs.wait_event(done)
+            h = cs.cuda_stream
+            so, spitch, do, dpitch, w, rows = peer_copy_plan("out", r, p, g, dims)
+            call("h3b_peer_copy2d", ar.ptr(p, "ob", do), dpitch, src + so, spitch, w, rows, h)
+            call("h3b_peer_signal", ar.flag(p, 1 + self.head_groups + g, r), self._epoch, h)
+
+    def _peer_wait(self, st: _RankState, slot: int, n_slots: int, name: str) -> None:
+        """Bounded wait on the current stream until every rank's flags of slots [slot, slot + n_slots) hold this
+        exchange's epoch (h3b_peer_wait: an expired wait sets the exchange status word, raised after the step)."""
+        from ._lib import call
+        main = torch.cuda.current_stream(self.dev)
+        ar, r = st.arena, self.ex.sp.rank
+        if self.ex.timing is not None:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(main)
+        call("h3b_peer_wait", ar.flag(r, slot, 0), n_slots * self.ex.world, self._epoch, main.cuda_stream)
+        if self.ex.timing is not None:
+            e1.record(main)
+            self.ex.timing.append((name, e0, e1))
 
     def _t(self, i: int, stage: str, st: _RankState, **tensors) -> None:
         if self.trace is not None:

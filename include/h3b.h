@@ -356,6 +356,34 @@ int h3b_attn_gate_quant(const void* ob, const void* g, const float* sg, const vo
                         const void* o1, const float* lse1a, const float* lse1b, int n1, const float* lse2,
                         cudaStream_t stream);
 
+/* ---- Peer-memory transport of the sequence-parallel head exchange (no counterpart in the reference, whose fused
+ * runner is single-GPU: patches/fastvideo-a01c50a.patch:644-645; FastVideo's stock path runs the same exchange as NCCL
+ * all-to-alls, patch:12-13). One allocation per rank holds its receive buffers and flag words; every rank of the node
+ * maps every other rank's allocation (CUDA IPC), the sender's copy engines write chunks into the receiver's buffers,
+ * and a flag word written after the copies releases the receiver's bounded wait. */
+typedef struct h3b_peer_handle {
+  unsigned char bytes[64]; /* a CUDA IPC memory handle */
+} h3b_peer_handle;
+/* cudaMalloc of `bytes` on `device` (which must be the calling thread's current device), zero-filled. */
+int h3b_peer_alloc(int device, size_t bytes, void** ptr);
+int h3b_peer_free(void* ptr);
+/* The IPC handle of an allocation made by h3b_peer_alloc, for another process of the node to open. */
+int h3b_peer_export(const void* ptr, h3b_peer_handle* handle);
+/* Maps a peer's allocation into this process (peer access enabled on first use); *ptr is its base address here. */
+int h3b_peer_open(const h3b_peer_handle* handle, void** ptr);
+int h3b_peer_close(void* ptr);
+/* Stream-ordered 2D copy (height rows of `width` bytes, pitches in bytes) between any two of: local device memory,
+ * a mapped peer allocation. Runs on the copy engines. */
+int h3b_peer_copy2d(void* dst, size_t dpitch, const void* src, size_t spitch, size_t width, size_t height,
+                    cudaStream_t stream);
+/* Writes `epoch` to a flag word (local or in a mapped peer allocation) after the stream's earlier work, preceded by
+ * a system-scope fence, so a reader that sees the value also sees the data copied before it on this stream. */
+int h3b_peer_signal(uint32_t* flag, uint32_t epoch, cudaStream_t stream);
+/* Enqueues a one-block kernel that waits until every one of flags[0..count) reaches `epoch` (32-bit wrap-around
+ * compare). The wait is bounded (10 s per flag); when it expires the kernel sets the exchange status word (dst[3] of
+ * h3b_status_async) to H3B_ETIMEOUT and returns. Later work on the stream sees everything written before the flags. */
+int h3b_peer_wait(const uint32_t* flags, int count, uint32_t epoch, cudaStream_t stream);
+
 /* Status word written by kernels whose bounded waits expired (0 = none since the last reset); reset with
  * h3b_reset_device_status. Both synchronize the current device. */
 int h3b_device_status(int* status);
@@ -363,8 +391,9 @@ int h3b_reset_device_status(void);
 /* The kernels' device status words, read in stream order (no counterpart in the reference, whose kernels have no
  * bounded waits): dst[0] = the GEMMs' word (H3B_ETIMEOUT when a bounded wait expired), dst[1] = the attention's
  * (H3B_ETIMEOUT, or H3B_EINVAL when a selection list exceeded the 1024 key tiles the kernel holds), dst[2] = the row
- * kernels' (H3B_ETIMEOUT when a LayerNorm row copy never completed). dst is device memory or page-locked host memory
- * for three ints; with `clear` the words are reset after the read. A step that
+ * kernels' (H3B_ETIMEOUT when a LayerNorm row copy never completed), dst[3] = the exchange waits' (H3B_ETIMEOUT when a
+ * peer's flag did not arrive, h3b_peer_wait). dst is device memory or page-locked host memory for four ints; with
+ * `clear` the words are reset after the read. A step that
  * enqueues this after its last kernel and checks dst once the stream reaches it learns of any failure in the step. */
 int h3b_status_async(int* dst, int clear, cudaStream_t stream);
 /* Exercises the bounded-wait path without a fault: one warp waits on an mbarrier nothing arrives on, with the kernels'

@@ -176,7 +176,7 @@ def test_dense_prefix_pass_merged_by_lse_equals_one_pass(pkg, prefix):
         # the merge the gate quantizer performs, restated in float64 from the traced pieces: the dense pass (o1,
         # natural-log LSEs) and the sparse pass (its output and log2 LSE; prefix rows take the dense pass alone)
         d = cap[("dense", i)]
-        ob2 = d["ob_x"][0].double()[:, slot].transpose(0, 1)  # [rows, H, 128]
+        ob2 = _planes(d["ob_x"]).double()[:, slot].transpose(0, 1)  # [rows, H, 128]
         l1 = torch.cat([d["lse1a"], d["lse1b"]], 1).double().t() / math.log(2.0)  # [rows, H], log2
         l2 = d["lse2"].double()[:, slot].t()
         n1 = d["lse1a"].shape[1]
@@ -460,6 +460,11 @@ def _values(t) -> np.ndarray:
     return t.float().numpy() if t.dtype == torch.float16 else oq.e4m3_decode(t.numpy())
 
 
+def _planes(x: torch.Tensor) -> torch.Tensor:
+    """A one-rank runner's head-sharded buffer [G=1, P=1, H, rows, 128] as [H, rows, 128]."""
+    return x.reshape(-1, *x.shape[-2:])
+
+
 def _deq_tiles(codes: torch.Tensor, scales: torch.Tensor) -> np.ndarray:
     """E4M3 [H, n*64, 128] (codes, or f16 values) with per-(head, tile) scales [H, n] -> float32."""
     H, rows_pad, D = codes.shape
@@ -470,12 +475,12 @@ def _deq_tiles(codes: torch.Tensor, scales: torch.Tensor) -> np.ndarray:
 def test_stage_self_attention(traced):
     rec, st = traced["rec"], traced["st"]
     s, a = rec[(0, "select")], rec[(0, "attn")]
-    q = _deq_tiles(s["qb_x"][0], s["qs_all"])
-    k = _deq_tiles(s["kb_x"][0], s["ks_all"])
-    v = _deq_tiles(s["vb_x"][0], s["vs_all"])
+    q = _deq_tiles(_planes(s["qb_x"]), s["qs_all"])
+    k = _deq_tiles(_planes(s["kb_x"]), s["ks_all"])
+    v = _deq_tiles(_planes(s["vb_x"]), s["vs_all"])
     vbs = st.b["vbs"].cpu().numpy()
     want = ov.vsa_fine(q, k, v, s["idx"].cpu().numpy(), s["num"].cpu().numpy(), vbs, 1.0 / math.sqrt(128))
-    got = a["ob_x"][0].float().cpu().numpy()
+    got = _planes(a["ob_x"]).float().cpu().numpy()
     mask = (np.arange(got.shape[1]) % 64)[None, :] < np.repeat(vbs, 64)[None, :]
     g, w = got[:, mask[0]], want[:, mask[0]]
     err = np.linalg.norm(g - w) / np.linalg.norm(w)

@@ -29,7 +29,12 @@ def _worker(rank, world, port, fn_name, q):
         dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
         import __graft_entry__  # noqa: F401
         pkg = __graft_entry__.load_package()
-        globals()[fn_name](rank, world, pkg)
+        if ":" in fn_name:  # a rank body of another test module, "module:function"
+            import importlib
+            mod, fn = fn_name.split(":")
+            getattr(importlib.import_module(mod), fn)(rank, world, pkg)
+        else:
+            globals()[fn_name](rank, world, pkg)
         q.put((rank, "ok"))
     except Exception as e:  # noqa: BLE001
         q.put((rank, f"error: {type(e).__name__}: {e}\n{traceback.format_exc()}"))

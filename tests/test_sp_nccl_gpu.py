@@ -1,5 +1,6 @@
-"""The sequence-parallel block loop over NCCL on 2 GPUs: the output of two ranks (one process per GPU, head all-to-all
-around attention) equals the single-GPU output bit for bit. Skipped with fewer than two GPUs."""
+"""The sequence-parallel block loop on 2 GPUs: the output of two ranks (one process per GPU, head exchange around
+attention over the peer transport -- copy engines into peer-mapped buffers, head groups pipelined -- and over NCCL
+all-to-alls) equals the single-GPU output bit for bit. Skipped with fewer than two GPUs."""
 from __future__ import annotations
 
 import os
@@ -42,13 +43,20 @@ def _rank(rank, world, port, q):
         ctx = torch.randn(1, cfg.text_len, cfg.text_dim, device=dev, generator=g).bfloat16()
         temb = m.timestep_embedding(0.5)
         meta = pkg.runner.VsaMeta(grid=grid, topk=8)
-        out = pkg.runner.H3FastRunner(m, pkg.sp.SeqParallel()).forward(x, temb, None, None, meta, context=ctx)
-        torch.cuda.synchronize()
+        outs = {}
+        for exchange in ("peer", "nccl"):
+            r = pkg.runner.H3FastRunner(m, pkg.sp.SeqParallel(), exchange=exchange)
+            assert r.transport == exchange, (r.transport, r.transport_note)
+            # two forwards: the peer transport's flags carry on counting from the first into the second
+            outs[exchange] = [r.forward(x, temb, None, None, meta, context=ctx) for _ in range(2)]
+            torch.cuda.synchronize()
+            r.close()
         dist.barrier()
         ref = pkg.runner.H3FastRunner(m).forward(x, temb, None, None, meta, context=ctx)
         torch.cuda.synchronize()
-        same = bool(torch.equal(out.view(torch.int16), ref.view(torch.int16)))
-        q.put((rank, "ok" if same else f"mismatch: {int((out != ref).sum())} elements differ"))
+        bad = [f"{ex} forward {k}: {int((o != ref).sum())} elements differ" for ex, os_ in outs.items()
+               for k, o in enumerate(os_) if not torch.equal(o.view(torch.int16), ref.view(torch.int16))]
+        q.put((rank, "ok" if not bad else "mismatch: " + "; ".join(bad)))
     except Exception as e:  # noqa: BLE001
         q.put((rank, f"error: {type(e).__name__}: {e}\n{traceback.format_exc()}"))
     finally:
