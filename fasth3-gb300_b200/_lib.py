@@ -80,6 +80,7 @@ SIGNATURES: dict[str, list] = {
     "h3b_vsa_pair_v16": [ctypes.POINTER(VsaArgs), P, P],
     "h3b_vsa_fp8_shared": [ctypes.POINTER(VsaArgs), P],
     "h3b_vsa_fp8_shared_v16": [ctypes.POINTER(VsaArgs), P],
+    "h3b_vsa_fp8_ws": [ctypes.POINTER(VsaArgs), P],
     "h3b_qkv_prologue8_tiles": [P, P, P, I64, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, I32, I64, I32, I32,
                                 F32, I32, P],
     "h3b_vsa_tile_quant_v16": [P, P, P, I32, I64, P, P, P, P, P, P, P, P, P, P, P, P, P, I64, I32, I32, P],

@@ -803,6 +803,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 #undef warp_wait
 }
 
+#include "vsa_ws.cuh"
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
@@ -953,6 +955,57 @@ int vsa_launch(const h3b_vsa_args* x, const uint8_t* u_mem, bool v16, cudaStream
 }
 }  // namespace
 }  // namespace h3b
+
+namespace h3b {
+namespace {
+// The wide-step kernel (vsa_ws.cuh): E4M3 Q/K, f16 V, one key list per query tile.
+int vsa_ws_launch(const h3b_vsa_args* x, cudaStream_t stream) {
+  H3B_REQUIRE(x, "vsa_fp8_ws: null argument block");
+  H3B_REQUIRE(!x->qk_int8, "vsa_fp8_ws: E4M3 QK^T only");
+  H3B_REQUIRE(x->q && x->k && x->v && x->idx && x->num && x->vbs_q && x->vbs_kv && x->vs && x->vs_head && x->out,
+              "vsa_fp8_ws: null pointer");
+  H3B_REQUIRE((x->qs == nullptr) == (x->ks == nullptr), "vsa_fp8_ws: give both or neither per-tile Q/K scales");
+  H3B_REQUIRE(x->heads > 0 && x->n_q_ext > 0 && x->n_q_ext % 2 == 0, "vsa_fp8_ws: n_q_ext must be positive and even");
+  H3B_REQUIRE(x->n_kv > 0 && x->n_kv <= N_MAX, "vsa_fp8_ws: 1 <= n_kv <= %d key tiles", N_MAX);
+  H3B_REQUIRE(x->idx_ld >= 1 && x->kv_scale_ld >= x->n_kv && (!x->qs || x->q_scale_ld >= x->n_q_ext),
+              "vsa_fp8_ws: bad idx / scale strides");
+  H3B_REQUIRE(x->chunks_q > 0 && x->chunks_kv > 0 && x->rows_chunk_q > 0 && x->rows_chunk_kv > 0 &&
+                  x->rows_chunk_q % TILE == 0 && x->rows_chunk_kv % TILE == 0,
+              "vsa_fp8_ws: chunk row counts must be positive multiples of 64");
+  const int tpc_q = (int)(x->rows_chunk_q / TILE), tpc_kv = (int)(x->rows_chunk_kv / TILE);
+  H3B_REQUIRE((int64_t)tpc_q * x->chunks_q >= x->n_q_ext && (int64_t)tpc_kv * x->chunks_kv >= x->n_kv,
+              "vsa_fp8_ws: chunks do not cover the tiles");
+  H3B_REQUIRE(aligned(x->q, 16) && aligned(x->k, 16) && aligned(x->v, 16) && aligned(x->out, 16),
+              "vsa_fp8_ws: 16-byte aligned operands");
+  CUtensorMap mq, mk, mv;
+  if (int rc = make_map(&mq, x->q, (int64_t)x->chunks_q * x->heads, x->rows_chunk_q)) return rc;
+  if (int rc = make_map(&mk, x->k, (int64_t)x->chunks_kv * x->heads, x->rows_chunk_kv)) return rc;
+  if (int rc = make_map_v16(&mv, x->v, (int64_t)x->chunks_kv * x->heads, x->rows_chunk_kv)) return rc;
+  AttnArgs a{x->idx, x->num, x->vbs_q, x->vbs_kv, x->qs, x->ks, x->vs, x->vs_head, x->qk_coef,
+             static_cast<bf16*>(x->out), x->lse, x->heads, x->n_q_ext, x->n_kv, x->idx_ld, x->q_scale_ld,
+             x->kv_scale_ld, tpc_q, tpc_kv, x->rows_chunk_q, x->heads * (x->n_q_ext / 2), nullptr};
+  const int smem = (int)sizeof(ws::Smem) + 1024;
+  static PerDevice setup;  // the shared-memory reservation per device; the value is the SM count
+  int sms = 0;
+  if (int rc = setup.get([&](int* v) {
+        if (cudaFuncSetAttribute(vsa_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+          return set_error(H3B_ECUDA, "vsa_fp8_ws: cannot reserve %d bytes of shared memory", smem);
+        *v = current_sms();
+        return H3B_OK;
+      }, &sms))
+    return rc;
+  const int grid = a.items < sms ? a.items : sms;
+  vsa_ws_kernel<<<grid, ws::THREADS, smem, stream>>>(mq, mk, mv, a);
+  H3B_LAUNCH_CHECK("vsa_fp8_ws");
+  return H3B_OK;
+}
+}  // namespace
+}  // namespace h3b
+
+extern "C" int h3b_vsa_fp8_ws(const h3b_vsa_args* x, cudaStream_t stream) {
+  clear_error();
+  return h3b::vsa_ws_launch(x, stream);
+}
 
 extern "C" int h3b_vsa_fp8(const void* qb, const void* kb, const void* vb, const int32_t* idx, const int32_t* num,
                            const int32_t* vbs, const float* qs_blk, const float* ks_blk, const float* vs_blk,

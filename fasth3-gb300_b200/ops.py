@@ -443,11 +443,12 @@ def vsa_pair(q8, k8, v8, u_idx, u_mem, u_num, vbs, qk_coef, v_scale_blk, v_scale
 
 def vsa_fp8_ex(q, k, v, out, idx, num, vbs_q, vbs_kv, vs, vs_head, qk_coef, heads, n_q_ext, n_kv, rows_chunk_q,
                rows_chunk_kv, chunks_q=1, chunks_kv=1, qs=None, ks=None, lse=None, idx_ld=None, q_scale_ld=None,
-               kv_scale_ld=None, qk_int8: bool = False, _u_mem=None, shared_lists: bool = False):
+               kv_scale_ld=None, qk_int8: bool = False, _u_mem=None, shared_lists: bool = False, wide: bool = False):
     """General FP8 block-sparse attention (h3b_vsa_fp8_ex): chunked [chunks * heads, rows_chunk, 128] layouts (the
     all-to-all layout of sequence parallelism) and separate key/value tiles (cross-attention). ``shared_lists``: the
     list of each even query tile applies to it and the next tile (h3b_vsa_fp8_shared: one M=128 MMA stream per pair;
-    cross-attention, dense layers)."""
+    cross-attention, dense layers). ``wide``: the wide-step kernel (h3b_vsa_fp8_ws: one weight-stationary M=64 MMA
+    advances both key streams of a query tile per step; f16 V and E4M3 Q/K only)."""
     import ctypes
 
     from ._lib import VsaArgs
@@ -464,7 +465,11 @@ def vsa_fp8_ex(q, k, v, out, idx, num, vbs_q, vbs_kv, vs, vs_head, qk_coef, head
     x.chunks_q, x.chunks_kv = int(chunks_q), int(chunks_kv)
     x.qk_int8 = int(bool(qk_int8))
     v16 = "_v16" if v.dtype == torch.float16 else ""  # f16 V (decoded E4M3 values) or E4M3 codes
-    if _u_mem is not None:
+    if wide:
+        if not v16 or qk_int8 or shared_lists or _u_mem is not None:
+            raise ValueError("the wide-step kernel takes f16 V, E4M3 Q/K and one key list per query tile")
+        call("h3b_vsa_fp8_ws", ctypes.byref(x), _stream(q))
+    elif _u_mem is not None:
         call("h3b_vsa_pair" + v16, ctypes.byref(x), _p(_u_mem), _stream(q))
     elif shared_lists:
         call("h3b_vsa_fp8_shared" + v16, ctypes.byref(x), _stream(q))

@@ -259,7 +259,8 @@ class H3FastRunner:
     (exact scores; E4M3 otherwise). ``v_f16``: V tiles as f16 (see below)."""
 
     def __init__(self, model: DiTModel, sp: SeqParallel | VirtualSeqParallel | None = None, qk_int8: bool = False,
-                 v_f16: bool = False, ffn_requant: str = "rows", exchange: str = "auto", head_groups: int | None = None):
+                 v_f16: bool = False, ffn_requant: str = "rows", exchange: str = "auto", head_groups: int | None = None,
+                 attn_kernel: str = "wide"):
         self.model = model
         self.qk_int8 = bool(qk_int8)
         # FFN re-quantization between fc_in and fc_out: "rows" -- the reference's rule, the bf16 fc_in output
@@ -270,11 +271,17 @@ class H3FastRunner:
             raise ValueError(f"ffn_requant must be 'rows' or 'static', not {ffn_requant!r}")
         self.ffn_requant = ffn_requant
         self.ffn_headroom = 2.0
-        # self-attention V tiles as E4M3 codes converted by the attention kernel on every use (default: half the bytes
-        # in the prologue's writes and the sequence-parallel exchange), or as f16 holding the E4M3 values (decoded
-        # once by the prologue, loaded by the PV MMAs as is); the results are bit-identical and the attention time
-        # equal. The cross-attention's text V is always f16.
-        self.v_dtype = torch.float16 if v_f16 else torch.uint8
+        # self-attention kernel: "wide" (h3b_vsa_fp8_ws: one weight-stationary M=64 MMA advances both key streams of
+        # a query tile; needs f16 V and E4M3 Q/K) or "tile" (h3b_vsa_fp8_ex: two M=64 streams, E4M3 or f16 V, int8
+        # Q/K). The two give the same output.
+        if attn_kernel not in ("wide", "tile"):
+            raise ValueError(f"attn_kernel must be 'wide' or 'tile', not {attn_kernel!r}")
+        self.attn_kernel = "tile" if self.qk_int8 else attn_kernel
+        # self-attention V tiles as f16 holding the E4M3 values (decoded once by the prologue, loaded by the PV MMAs as
+        # is; the wide kernel's form), or, with the tile kernel, as E4M3 codes converted by the attention kernel on
+        # every use (half the bytes in the prologue's writes and the exchange); the results are bit-identical. The
+        # cross-attention's text V is always f16.
+        self.v_dtype = torch.float16 if (v_f16 or self.attn_kernel == "wide") else torch.uint8
         self.blocks = list(model.transformer_blocks)
         cfg = model.config
         self.cfg = cfg
@@ -744,7 +751,8 @@ class H3FastRunner:
                                b["vbs_all"], b["vbs_all"], b["vs_all"][hs], b["vs_head"][hs], sm_scale * LOG2E, Hg,
                                n_all, n_all, st.rows_pad, st.rows_pad, chunks_q=P, chunks_kv=P, qs=b["qs_all"][hs],
                                ks=b["ks_all"][hs], lse=None if lse2 is None else lse2[hs], idx_ld=n_all,
-                               q_scale_ld=n_all, kv_scale_ld=n_all, qk_int8=self.qk_int8)
+                               q_scale_ld=n_all, kv_scale_ld=n_all, qk_int8=self.qk_int8,
+                               wide=self.attn_kernel == "wide")
                 if peer:
                     self._peer_send_out(st, g)
             if sel["split"]:

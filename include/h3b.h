@@ -319,6 +319,12 @@ int h3b_vsa_pair_v16(const h3b_vsa_args* args, const uint8_t* u_mem, cudaStream_
  * h3b_vsa_fp8_ex; qk_int8 must be 0. The _v16 form takes f16 V like h3b_vsa_fp8_ex_v16. */
 int h3b_vsa_fp8_shared(const h3b_vsa_args* args, cudaStream_t stream);
 int h3b_vsa_fp8_shared_v16(const h3b_vsa_args* args, cudaStream_t stream);
+/* Replaces vsa_fp8_op (fastvideo/models/dits/h3fast/h3attn8.cu:1-42) like h3b_vsa_fp8_ex_v16 --
+ * same arguments (f16 V holding the E4M3 values, E4M3 Q/K: qk_int8 must be 0), same outputs within the accumulation
+ * order inside the MMAs -- on the wide-step kernel: each query tile's key tiles run as two streams (even and odd list
+ * entries) that one weight-stationary M = 64 MMA advances together (S: N = 128, PV: N = 256), so the whole 128-lane
+ * datapath works on one query tile; the streams are merged by log-sum-exp in the epilogue. */
+int h3b_vsa_fp8_ws(const h3b_vsa_args* args, cudaStream_t stream);
 /* Status word of the attention kernel's bounded waits (0 = none); reset != 0 clears it. Synchronizes the device. */
 int h3b_vsa_status(int* status, int reset);
 

@@ -197,18 +197,35 @@ def test_dense_prefix_pass_merged_by_lse_equals_one_pass(pkg, prefix):
 
 
 def test_f16_v_runner_equals_e4m3_v_runner(pkg):
-    """The runner with V tiles as f16 (decoded once by the prologue) and with E4M3 V tiles (converted by the attention
-    kernel): the same values reach the tensor cores, so the block loop's output is identical bit for bit, sharded
-    too."""
+    """The tile kernel's runner with V tiles as f16 (decoded once by the prologue) and with E4M3 V tiles (converted by
+    the attention kernel): the same values reach the tensor cores, so the block loop's output is identical bit for bit,
+    sharded too; the default runner (wide-step kernel) agrees with them."""
     _, runner = pkg
     m, x, ctx, temb, meta = make(pkg, blocks=2, grid=(7, 16, 16))
-    a = runner.H3FastRunner(m, v_f16=True).forward(x, temb, None, None, meta, context=ctx)
-    b = runner.H3FastRunner(m, v_f16=False).forward(x, temb, None, None, meta, context=ctx)
-    c = runner.H3FastRunner(m, runner.VirtualSeqParallel(2), v_f16=True).forward(x, temb, None, None, meta,
-                                                                                  context=ctx)
+    a = runner.H3FastRunner(m, v_f16=True, attn_kernel="tile").forward(x, temb, None, None, meta, context=ctx)
+    b = runner.H3FastRunner(m, v_f16=False, attn_kernel="tile").forward(x, temb, None, None, meta, context=ctx)
+    c = runner.H3FastRunner(m, runner.VirtualSeqParallel(2), v_f16=True, attn_kernel="tile").forward(
+        x, temb, None, None, meta, context=ctx)
     torch.cuda.synchronize()
     assert torch.equal(a.view(torch.int16), b.view(torch.int16))
     assert torch.equal(a.view(torch.int16), c.view(torch.int16))
+    # the default runner (wide-step kernel: the tile kernel's two streams and merge, two key tiles per running-maximum
+    # update) against the tile kernel's: block 0's attention output within 3e-3; the final output after two blocks of
+    # NVFP4 re-quantization (a 4-bit code that flips moves its element by up to half) only within a gross bound
+    attn = {}
+
+    def keep(tag):
+        return lambda i, stage, rank, t: attn.__setitem__(tag, t["ob_x"].float().clone()) if (i, stage) == (0, "attn") \
+            else None
+
+    rw, rt = runner.H3FastRunner(m), runner.H3FastRunner(m, v_f16=True, attn_kernel="tile")
+    rw.trace, rt.trace = keep("wide"), keep("tile")
+    w = rw.forward(x, temb, None, None, meta, context=ctx)
+    t = rt.forward(x, temb, None, None, meta, context=ctx)
+    torch.cuda.synchronize()
+    assert torch.equal(t.view(torch.int16), a.view(torch.int16))
+    assert float((attn["wide"] - attn["tile"]).norm() / attn["tile"].norm()) < 3e-3
+    assert float((w.float() - a.float()).norm() / a.float().norm()) < 0.2
 
 
 def test_static_ffn_requant_runner(pkg):

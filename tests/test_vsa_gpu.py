@@ -716,3 +716,96 @@ def test_f16_v_path_is_bit_identical(ops):
     assert torch.equal(o8.view(torch.int16), o16.view(torch.int16))
     assert torch.equal(l8, l16)
     assert torch.equal(p8.view(torch.int16), p16.view(torch.int16))
+
+
+# ------------------------------------------------------------------------------------------------ wide-step kernel
+def _wide_case(heads, vbs, k, seed, empty_every=0):
+    """Quantized Q/K/V tiles (E4M3, per (head, tile) scales), f16 V holding the E4M3 values, top-k lists (every
+    ``empty_every``-th query tile's list emptied, and the next one cut to one entry)."""
+    g = torch.Generator().manual_seed(seed)
+    n = len(vbs)
+    n_ext = n + n % 2
+    rows = n_ext * 64
+    x = lambda: torch.randn(heads, rows, 128, generator=g)  # noqa: E731
+
+    def quant(t):
+        tt = t.view(heads, n_ext, 64, 128)
+        s = (tt.abs().amax((2, 3)) / 448).clamp_min(1e-30)
+        codes = (tt / s[:, :, None, None]).clamp(-448, 448).to(torch.float8_e4m3fn)
+        return codes.view(torch.uint8).view(heads, rows, 128), s
+
+    (q8, qs), (k8, ks), (v8, vs) = quant(x()), quant(x()), quant(x())
+    v16 = v8.view(torch.float8_e4m3fn).half()
+    vbs_ext = torch.cat([vbs, torch.zeros(n_ext - n, dtype=torch.int32)])
+    sc = torch.rand(heads, n_ext, n, generator=g)
+    order = sc.argsort(-1, descending=True)[..., :k].sort(-1).values.to(torch.int32)
+    idx = torch.full((heads, n_ext, n), -1, dtype=torch.int32)
+    idx[..., :k] = order
+    num = torch.full((heads, n_ext), k, dtype=torch.int32)
+    num[:, n:] = 0
+    if empty_every:
+        num[:, ::empty_every] = 0
+        num[:, 1::empty_every] = 1
+    return {"q8": q8, "k8": k8, "v8": v8, "v16": v16, "qs": qs, "ks": ks, "vs": vs, "vs_head": vs.amax(1),
+            "idx": idx, "num": num, "vbs": vbs_ext, "n": n, "n_ext": n_ext, "rows": rows}
+
+
+def _run_attn(ops, c, heads, wide, v16=True, chunks=1):
+    dv = lambda t: t.to(DEV)  # noqa: E731
+    rows, n_ext = c["rows"], c["n_ext"]
+    P = chunks
+    ch = (lambda t: t.view(heads, P, rows // P, 128).permute(1, 0, 2, 3).contiguous()) if P > 1 else (lambda t: t)
+    out = torch.zeros(P, heads, rows // P, 128, device=DEV, dtype=torch.bfloat16)
+    lse = torch.zeros(heads, rows, device=DEV)
+    coef = math.log2(math.e) / math.sqrt(128)
+    ops.vsa_fp8_ex(dv(ch(c["q8"])), dv(ch(c["k8"])), dv(ch(c["v16"] if v16 else c["v8"])), out, dv(c["idx"]),
+                   dv(c["num"]), dv(c["vbs"]), dv(c["vbs"]), dv(c["vs"]), dv(c["vs_head"]), coef, heads, n_ext, n_ext,
+                   rows // P, rows // P, chunks_q=P, chunks_kv=P, qs=dv(c["qs"]), ks=dv(c["ks"]),
+                   lse=lse if P == 1 else None, idx_ld=c["n"], wide=wide)
+    torch.cuda.synchronize()
+    ops.check_status()
+    return out.permute(1, 0, 2, 3).reshape(heads, rows, 128).cpu(), lse.cpu()
+
+
+@pytest.mark.parametrize("case", ["config4_k32", "config4_k127", "ragged_odd_empty"])
+def test_vsa_wide_step_matches_tile_kernel_and_exact_attention(ops, case):
+    """The wide-step kernel (h3b_vsa_fp8_ws) against the two-stream tile kernel with f16 V (the same two streams and
+    merge; the wide kernel takes each stream's key tiles two at a time under one running maximum, which moves the
+    points where f16 P is rounded: within 3e-3) and against exact float64 attention over the same dequantized operands
+    (2e-2; both kernels are within ~2^-9); LSE likewise. Cases: BASELINE config 4's 512 tiles at top-32 and an odd top-127 (streams of
+    unequal length), and variable tiles (partial key tiles) with an odd tile count, odd k and lists of length 0 and 1."""
+    if case.startswith("config4"):
+        heads, vbs, k, empty = 2, torch.full((512,), 64, dtype=torch.int32), int(case.split("_k")[1]), 0
+    else:
+        heads, vbs, k, empty = 3, vbs_pattern(37), 5, 6
+    c = _wide_case(heads, vbs, k, 90 + k, empty)
+    got, lse = _run_attn(ops, c, heads, wide=True)
+    ref_tile, lse_tile = _run_attn(ops, c, heads, wide=False)
+    rows = c["rows"]
+    valid = np.zeros((heads, rows), dtype=bool)
+    for t in range(c["n"]):
+        valid[:, t * 64:t * 64 + int(vbs[t])] = True
+    g_, r_ = got.float().numpy(), ref_tile.float().numpy()
+    assert _rel(g_[valid], r_[valid]) < 3e-3
+    assert (g_[~valid] == 0).all()  # rows past a tile's length are written as zeros
+    deq = lambda codes, s: (codes.view(torch.float8_e4m3fn).float().view(heads, c["n_ext"], 64, 128)  # noqa: E731
+                            * s[:, :, None, None]).view(heads, rows, 128).numpy()
+    ref = ov.vsa_fine(deq(c["q8"], c["qs"]), deq(c["k8"], c["ks"]), deq(c["v8"], c["vs"]), c["idx"].numpy(),
+                      c["num"].numpy(), c["vbs"].numpy(), 1.0 / math.sqrt(128))
+    assert _rel(g_[valid], ref[valid]) < 1e-2  # north-star bar: 2e-2
+    lv, lt = lse.numpy()[valid], lse_tile.numpy()[valid]
+    fin = np.isfinite(lt)
+    assert (np.isfinite(lv) == fin).all()
+    np.testing.assert_allclose(lv[fin], lt[fin], atol=2e-3)
+    if empty:  # empty lists: zero rows and an LSE of -inf
+        t0 = 0
+        assert (g_[:, t0 * 64:(t0 + 1) * 64] == 0).all() and np.isneginf(lse.numpy()[:, :int(vbs[0])]).all()
+
+
+def test_vsa_wide_step_chunked_layout_matches_plain(ops):
+    """The all-to-all layout (chunks = 4) gives the wide-step kernel's plain-layout bytes."""
+    heads = 2
+    c = _wide_case(heads, torch.full((32,), 64, dtype=torch.int32), 7, 61)
+    plain, _ = _run_attn(ops, c, heads, wide=True)
+    chunked, _ = _run_attn(ops, c, heads, wide=True, chunks=4)
+    assert torch.equal(plain.view(torch.int16), chunked.view(torch.int16))
