@@ -40,6 +40,9 @@ constexpr int THREADS = WARPS * 32;
 constexpr int K_SLOT = 4 * TILE * D;
 constexpr int V_PLANE = TILE * 128;
 constexpr int V_SLOT = 4 * V_PLANE;
+// score of a masked key (past a tile's length, or a slot with no tile): finite, below any E4M3 dot product (|S| <=
+// 128 * 448 * 448 < 2.6e7) by far, and still finite once multiplied by a Q/K scale coefficient (< 1e8)
+constexpr float kMaskedScore = -1.0e30f;
 
 struct __align__(1024) Smem {
   uint8_t q[2][TILE * D];            // [query tile] E4M3, 128-byte swizzle
@@ -370,8 +373,8 @@ __global__ void __launch_bounds__(ws::THREADS, 1)
       };
       fetch(0);
       for (int j = 0; j < steps; ++j) {
-        const int vbs_j[2] = {vbs_n[0], vbs_n[1]};
-        const float ks_j[2] = {ks_n[0], ks_n[1]}, vs_j[2] = {vs_n[0], vs_n[1]};
+        const int vbs_j0 = vbs_n[0], vbs_j1 = vbs_n[1];
+        const float ks_j0 = ks_n[0], ks_j1 = ks_n[1], vs_j0 = vs_n[0], vs_j1 = vs_n[1];
         fetch(j + 1);
         if (!warp_wait_bounded(&sm.s_full[m], sph & 1u, abort_flag, lane)) {
           ok = false;
@@ -381,14 +384,22 @@ __global__ void __launch_bounds__(ws::THREADS, 1)
         tc_fence_after();
         // two passes over the step's 128 scores (64 at a time, to stay within the registers of 11 warps): the row
         // maximum, then the exponentials from a second read of the same columns
+        // (the per-tile scalars are picked with selects: a runtime index into the small arrays would put them in
+        // local memory, which the 64-column mask below would then reload per column)
+        // Keys past a tile's length are left out per 8-column chunk: chunk k counts if 8k < vbt (a warp-uniform
+        // predicate, since every lane of a warp has the same key tile), in the row maximum as a selected chunk
+        // maximum and in P as a mask word ANDed into the chunk's four packed pairs before they are summed. A length
+        // that is not a multiple of 8 first sets the scores of its partial chunk's tail to a sentinel (a per-element
+        // select, on those tiles only).
         auto load_tile = [&](int t, uint32_t (&st)[64]) {
           tmem_ld_32cols(tmem + lane_off + cS + 64u * t, *reinterpret_cast<uint32_t(*)[32]>(&st[0]));
           tmem_ld_32cols(tmem + lane_off + cS + 64u * t + 32u, *reinterpret_cast<uint32_t(*)[32]>(&st[32]));
           tmem_ld_wait();
-          if (__any_sync(0xffffffffu, vbs_j[t] < TILE)) {
+          const int vbt = t ? vbs_j1 : vbs_j0;
+          if (vbt & 7) {
+            const uint32_t masked = __float_as_uint(kMaskedScore);
 #pragma unroll
-            for (int c = 0; c < 64; ++c)
-              if (c >= vbs_j[t]) st[c] = __float_as_uint(-INFINITY);
+            for (int c = 0; c < 64; ++c) st[c] = c >= vbt ? masked : st[c];
           }
         };
         float mx = -INFINITY;
@@ -396,14 +407,18 @@ __global__ void __launch_bounds__(ws::THREADS, 1)
         for (int t = 0; t < 2; ++t) {
           uint32_t st[64];
           load_tile(t, st);
-          float m4[4];
+          const int vbt = t ? vbs_j1 : vbs_j0;
+          float mraw = kMaskedScore;
 #pragma unroll
-          for (int c = 0; c < 4; ++c) m4[c] = fmaxf(__uint_as_float(st[2 * c]), __uint_as_float(st[2 * c + 1]));
-#pragma unroll
-          for (int c = 4; c < 32; ++c)
-            m4[c & 3] = fmax3(m4[c & 3], __uint_as_float(st[2 * c]), __uint_as_float(st[2 * c + 1]));
-          const float mraw = fmax3(m4[0], m4[1], fmaxf(m4[2], m4[3]));
-          if (mraw != -INFINITY) mx = fmaxf(mx, mraw * (qcoef * ks_j[t]));  // coef > 0
+          for (int k = 0; k < 8; ++k) {
+            const uint32_t* c8 = st + 8 * k;
+            const float cm = fmaxf(fmax3(__uint_as_float(c8[0]), __uint_as_float(c8[1]), __uint_as_float(c8[2])),
+                                   fmax3(__uint_as_float(c8[3]), __uint_as_float(c8[4]),
+                                         fmaxf(__uint_as_float(c8[5]), fmaxf(__uint_as_float(c8[6]),
+                                                                             __uint_as_float(c8[7])))));
+            mraw = 8 * k < vbt ? fmaxf(mraw, cm) : mraw;
+          }
+          if (mraw > kMaskedScore) mx = fmaxf(mx, mraw * (qcoef * (t ? ks_j1 : ks_j0)));  // coef > 0
         }
         const bool grow = mx > m_ref + RESCALE_LOG2;
         const bool had_mass = m_ref != -INFINITY;
@@ -434,14 +449,16 @@ __global__ void __launch_bounds__(ws::THREADS, 1)
           } else {
             uint32_t st[64];
             load_tile(t, st);
-            const float coef = qcoef * ks_j[t];
+            const float coef = qcoef * (t ? ks_j1 : ks_j0);
             uint32_t acc[4] = {0u, 0u, 0u, 0u};
-            const __half2 vr2 = __float2half2_rn(vs_j[t] * inv_vhead);  // P' = P * sv_b / sv_head
+            const __half2 vr2 = __float2half2_rn((t ? vs_j1 : vs_j0) * inv_vhead);  // P' = P * sv_b / sv_head
             const uint32_t vr = *reinterpret_cast<const uint32_t*>(&vr2);
             const uint64_t coef2 = pack_f32x2(coef, coef), nb2 = pack_f32x2(-m_ref, -m_ref);
+            const int vbt = t ? vbs_j1 : vbs_j0;
 #pragma unroll
             for (int c = 0; c < 32; ++c) {
-              const uint32_t e = ex2_pair(st[2 * c], st[2 * c + 1], coef2, nb2);
+              const uint32_t keep = 8 * (c >> 2) < vbt ? 0xFFFFFFFFu : 0u;  // chunk c/4 of the tile's 8 chunks
+              const uint32_t e = ex2_pair(st[2 * c], st[2 * c + 1], coef2, nb2) & keep;
               acc[c & 3] = hadd2(acc[c & 3], e);
               pw[c] = hmul2(e, vr);
             }

@@ -7,7 +7,7 @@ Kernels (reference file:line -> this library):
   qkv_prologue8 (40 heads, static Q/K scales)       h3fast.cu:376-510      -> h3b_qkv_prologue8
   topk_rows (top-32 of 512 and of 2016 tiles)       h3fast.cu:524-588      -> h3b_topk_rows
   attn_gate_quant<5120, FP8>                        h3fast.cu:688-741      -> h3b_attn_gate_quant
-  VSA forward: the reference's BF16 kernel           vsa_bf16.cuh:197-1131  -> h3b_vsa_fp8 (E4M3 Q/K/V)
+  VSA forward: the reference's BF16 kernel           vsa_bf16.cuh:197-1131  -> h3b_vsa_fp8 (E4M3 Q/K/V), h3b_vsa_fp8_ws
                (h3attn16.cu, built with VSA_LDRED off: tcgen05.ld.red is sm_103a-only)
 
 Prints one line per kernel (``-s`` shows them): median milliseconds of 10 launches after 3 warm-ups (CUDA events) for
@@ -222,11 +222,18 @@ def test_vsa_attention_timing_config4(ops):
         ops.vsa_fp8(qb, kb, vb, idx, num, vbs, sm_scale * math.log2(math.e), vs, vs_head, q_scale_blk=qs,
                     k_scale_blk=ks, out=out)
 
-    t_ref, t_ours = _time(ref), _time(ours)
+    def ours_wide():  # the runner's kernel: h3b_vsa_fp8_ws
+        ops.vsa_fp8_ex(qb, kb, vb, out[0], idx, num, vbs, vbs, vs, vs_head, sm_scale * math.log2(math.e), H, n, n, S, S,
+                       qs=qs, ks=ks, idx_ld=n, q_scale_ld=n, kv_scale_ld=n, wide=True)
+
+    t_ref, t_ours, t_wide = _time(ref), _time(ours), _time(ours_wide)
     ref_out = ref()
+    ours_wide()
     torch.cuda.synchronize()
     err = float((out.double() - ref_out.double()).norm() / ref_out.double().norm())
-    print(f"\nrel-Frobenius(FP8 h3b vs BF16 reference) = {err:.4f}")
+    print(f"\nrel-Frobenius(FP8 h3b wide-step vs BF16 reference) = {err:.4f}")
     assert err < 0.1
-    _report(f"VSA forward config 4 (reference BF16 vs h3b E4M3), top-{k} of {n}", t_ref, t_ours,
+    _report(f"VSA forward config 4 (reference BF16 vs h3b E4M3, tile kernel), top-{k} of {n}", t_ref, t_ours,
+            4.0 * S * (k * 64) * D * H, "TFLOP/s")
+    _report(f"VSA forward config 4 (reference BF16 vs h3b E4M3, wide-step kernel), top-{k} of {n}", t_ref, t_wide,
             4.0 * S * (k * 64) * D * H, "TFLOP/s")

@@ -767,17 +767,21 @@ def _run_attn(ops, c, heads, wide, v16=True, chunks=1):
     return out.permute(1, 0, 2, 3).reshape(heads, rows, 128).cpu(), lse.cpu()
 
 
-@pytest.mark.parametrize("case", ["config4_k32", "config4_k127", "ragged_odd_empty"])
+@pytest.mark.parametrize("case", ["config4_k32", "config4_k127", "ragged_odd_empty", "lengths_not_multiple_of_8"])
 def test_vsa_wide_step_matches_tile_kernel_and_exact_attention(ops, case):
     """The wide-step kernel (h3b_vsa_fp8_ws) against the two-stream tile kernel with f16 V (the same two streams and
     merge; the wide kernel takes each stream's key tiles two at a time under one running maximum, which moves the
     points where f16 P is rounded: within 3e-3) and against exact float64 attention over the same dequantized operands
     (2e-2; both kernels are within ~2^-9); LSE likewise. Cases: BASELINE config 4's 512 tiles at top-32 and an odd top-127 (streams of
-    unequal length), and variable tiles (partial key tiles) with an odd tile count, odd k and lists of length 0 and 1."""
+    unequal length), variable tiles (partial key tiles) with an odd tile count, odd k and lists of length 0 and 1, and
+    tile lengths that are not multiples of 8."""
     if case.startswith("config4"):
         heads, vbs, k, empty = 2, torch.full((512,), 64, dtype=torch.int32), int(case.split("_k")[1]), 0
-    else:
+    elif case.startswith("ragged"):
         heads, vbs, k, empty = 3, vbs_pattern(37), 5, 6
+    else:  # tile lengths the kernel masks per key rather than per 8-key chunk
+        heads, k, empty = 2, 7, 0
+        vbs = torch.tensor([64, 37, 5, 64, 63, 1, 40, 64] * 5, dtype=torch.int32)
     c = _wide_case(heads, vbs, k, 90 + k, empty)
     got, lse = _run_attn(ops, c, heads, wide=True)
     ref_tile, lse_tile = _run_attn(ops, c, heads, wide=False)
