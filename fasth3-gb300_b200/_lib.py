@@ -100,7 +100,7 @@ SIGNATURES: dict[str, list] = {
     "h3b_peer_close": [P],
     "h3b_peer_copy2d": [P, SZ, P, SZ, SZ, SZ, P],
     "h3b_peer_signal": [P, ctypes.c_uint32, P],
-    "h3b_peer_wait": [P, I32, ctypes.c_uint32, P],
+    "h3b_peer_wait": [P, I32, ctypes.c_uint32, ctypes.c_uint64, P],
     "h3b_selftest_wait_timeout": [ctypes.c_uint64, P],
 }
 _RESTYPES = {"h3b_last_error": ctypes.c_char_p, "h3b_version": ctypes.c_char_p,

@@ -155,11 +155,13 @@ extern "C" int h3b_peer_signal(uint32_t* flag, uint32_t epoch, cudaStream_t stre
   return H3B_OK;
 }
 
-extern "C" int h3b_peer_wait(const uint32_t* flags, int count, uint32_t epoch, cudaStream_t stream) {
+extern "C" int h3b_peer_wait(const uint32_t* flags, int count, uint32_t epoch, uint64_t limit_ns, cudaStream_t stream) {
   h3b::clear_error();
   H3B_REQUIRE(flags && count > 0 && count <= 4096, "peer_wait: null flags or count %d outside 1..4096", count);
+  H3B_REQUIRE(limit_ns <= h3b::kPeerWaitLimitNs, "peer_wait: limit above %llu ns",
+              (unsigned long long)h3b::kPeerWaitLimitNs);
   const int threads = count < 128 ? ((count + 31) / 32) * 32 : 128;
-  h3b::peer_wait_kernel<<<1, threads, 0, stream>>>(flags, count, epoch, h3b::kPeerWaitLimitNs);
+  h3b::peer_wait_kernel<<<1, threads, 0, stream>>>(flags, count, epoch, limit_ns ? limit_ns : h3b::kPeerWaitLimitNs);
   H3B_LAUNCH_CHECK("peer_wait");
   return H3B_OK;
 }

@@ -296,6 +296,13 @@ def check_status(device: torch.device | str | None = None) -> None:
         raise RuntimeError("h3b device status after the step -- " + "; ".join(parts))
 
 
+def peer_wait(flags: torch.Tensor, epoch: int, limit_ns: int = 0) -> None:
+    """Bounded wait on the current stream until every int32 word of ``flags`` reaches ``epoch`` (h3b_peer_wait: the
+    peer transport's wait; limit_ns 0 = 10 s). An expired wait sets the exchange status word (raised by
+    ``check_status``)."""
+    call("h3b_peer_wait", _p(flags), int(flags.numel()), int(epoch) & 0xFFFFFFFF, int(limit_ns), _stream(flags))
+
+
 def selftest_wait_timeout(limit_ns: int, device: torch.device | str = "cuda") -> None:
     """Launches the bounded-wait self-test (a wait that nothing completes, given up after ``limit_ns``)."""
     call("h3b_selftest_wait_timeout", int(limit_ns), torch.cuda.current_stream(device).cuda_stream)

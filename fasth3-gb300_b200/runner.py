@@ -974,7 +974,7 @@ class H3FastRunner:
         if self.ex.timing is not None:
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(main)
-        call("h3b_peer_wait", ar.flag(r, slot, 0), n_slots * self.ex.world, self._epoch, main.cuda_stream)
+        call("h3b_peer_wait", ar.flag(r, slot, 0), n_slots * self.ex.world, self._epoch, 0, main.cuda_stream)
         if self.ex.timing is not None:
             e1.record(main)
             self.ex.timing.append((name, e0, e1))

@@ -386,9 +386,10 @@ int h3b_peer_copy2d(void* dst, size_t dpitch, const void* src, size_t spitch, si
  * a system-scope fence, so a reader that sees the value also sees the data copied before it on this stream. */
 int h3b_peer_signal(uint32_t* flag, uint32_t epoch, cudaStream_t stream);
 /* Enqueues a one-block kernel that waits until every one of flags[0..count) reaches `epoch` (32-bit wrap-around
- * compare). The wait is bounded (10 s per flag); when it expires the kernel sets the exchange status word (dst[3] of
- * h3b_status_async) to H3B_ETIMEOUT and returns. Later work on the stream sees everything written before the flags. */
-int h3b_peer_wait(const uint32_t* flags, int count, uint32_t epoch, cudaStream_t stream);
+ * compare). The wait is bounded (limit_ns per flag, at most 10 s; 0 means 10 s); when it expires the kernel sets the
+ * exchange status word (dst[3] of h3b_status_async) to H3B_ETIMEOUT and returns, and later waits return at once
+ * until the word is cleared. Later work on the stream sees everything written before the flags. */
+int h3b_peer_wait(const uint32_t* flags, int count, uint32_t epoch, uint64_t limit_ns, cudaStream_t stream);
 
 /* Status word written by kernels whose bounded waits expired (0 = none since the last reset); reset with
  * h3b_reset_device_status. Both synchronize the current device. */

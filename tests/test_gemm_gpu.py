@@ -298,3 +298,27 @@ def test_check_status_raises_after_an_expired_wait(ops):
         ops.check_status()
     ops.check_status()
     assert ops.device_status() == 0
+
+
+def test_exchange_wait_expires_raises_and_later_waits_skip(ops):
+    """The peer transport's wait (h3b_peer_wait) on a flag that nothing sets gives up after its limit, sets the
+    exchange status word (check_status raises "exchange waits"), makes the waits after it return at once instead of
+    each waiting out its own limit, and the context stays usable; a flag that holds the epoch passes without waiting."""
+    import time
+
+    ops.check_status()
+    flags = torch.zeros(4, device=DEV, dtype=torch.int32)
+    t0 = time.time()
+    ops.peer_wait(flags, 1, 200_000_000)  # 200 ms, nothing sets the flags
+    for _ in range(5):  # skipped: the word is already set
+        ops.peer_wait(flags, 1, 200_000_000)
+    torch.cuda.synchronize()
+    waited = time.time() - t0
+    assert 0.15 < waited < 0.8, waited  # one limit, not six
+    with pytest.raises(RuntimeError, match="exchange waits: H3B_ETIMEOUT"):
+        ops.check_status()
+    flags.fill_(7)
+    ops.peer_wait(flags, 7, 30_000_000)   # reached
+    ops.peer_wait(flags, 3, 30_000_000)   # passed long ago (wrap-around compare)
+    torch.cuda.synchronize()
+    ops.check_status()
