@@ -333,9 +333,11 @@ def fp8_chain_secondary(pkg, dev, stream, args) -> dict:
 
 def sp_bitexact_check(pkg, dev, ws) -> dict:
     """Two blocks on the (7, 16, 16) latent (32 tiles, 1792 tokens) sequence-parallel over every rank of this job (with
-    the runner's default head exchange -- the peer transport where available -- and with NCCL all-to-alls), compared
-    bit for bit with one rank's runner on the same input, which every rank also runs on its own GPU. Every step of the sharded block is row-, tile- or (head, tile)-local, so the two must
-    agree exactly; the result is the minimum over ranks. Also counts the ranks that answer one NCCL all-reduce."""
+    the runner's default head exchange -- the peer transport where available -- and with NCCL all-to-alls; and with
+    the default exchange in the balanced tile order), compared bit for bit with one rank's runner in the same tile order
+    on the same input, which every rank also runs on its own GPU. Every step of the sharded block is row-, tile- or
+    (head, tile)-local, so the two must agree exactly; the result is the minimum over ranks. Also counts the ranks that
+    answer one NCCL all-reduce."""
     import torch
     import torch.distributed as dist
     cfg = pkg.model.DiTConfig(blocks=2, fmt="nvfp4")
@@ -346,15 +348,18 @@ def sp_bitexact_check(pkg, dev, ws) -> dict:
     ctx = torch.randn(1, cfg.text_len, cfg.text_dim, device=dev, generator=g).bfloat16()
     temb = m.timestep_embedding(0.5)
     meta = pkg.runner.VsaMeta(grid=grid, topk=8)
-    ref = pkg.runner.H3FastRunner(m).forward(x, temb, None, None, meta, context=ctx)
+    refs = {order: pkg.runner.H3FastRunner(m, tile_order=order).forward(x, temb, None, None, meta, context=ctx)
+            for order in ("reference", "balanced")}
     flags, transports = [], []
-    for exchange in ("auto", "nccl"):  # the transport the step uses (peer when available), then NCCL
+    # the transport the step uses (peer when available), then NCCL, in the reference tile order; then the step's
+    # transport in the balanced tile order (the config-5 step's order under sequence parallelism)
+    for exchange, order in (("auto", "reference"), ("nccl", "reference"), ("auto", "balanced")):
         if exchange == "nccl" and transports and transports[0] == "nccl":
-            break
-        r = pkg.runner.H3FastRunner(m, pkg.sp.SeqParallel(), exchange=exchange)
+            continue
+        r = pkg.runner.H3FastRunner(m, pkg.sp.SeqParallel(), exchange=exchange, tile_order=order)
         got = r.forward(x, temb, None, None, meta, context=ctx)
-        flags.append(1 if torch.equal(got.view(torch.int16), ref.view(torch.int16)) else 0)
-        transports.append(r.transport)
+        flags.append(1 if torch.equal(got.view(torch.int16), refs[order].view(torch.int16)) else 0)
+        transports.append(r.transport if order == "reference" else f"{r.transport}+balanced")
         if ws > 1:
             torch.cuda.synchronize()
             r.close()
@@ -363,7 +368,7 @@ def sp_bitexact_check(pkg, dev, ws) -> dict:
     if ws > 1:
         dist.all_reduce(same, op=dist.ReduceOp.MIN)
         dist.all_reduce(seen)
-    del m, x, ctx, ref, got
+    del m, x, ctx, refs, got
     torch.cuda.empty_cache()
     return {"sp_bitexact": bool(same.min().item()), "per_transport": dict(zip(transports, map(bool, same.tolist()))),
             "grid": list(grid), "blocks": 2, "ranks_in_nccl_allreduce": int(seen.item()),
@@ -386,6 +391,10 @@ def dit_step_secondary(pkg, dev, stream, args, ws) -> dict:
     ctx = torch.randn(1, cfg.text_len, cfg.text_dim, device=dev, generator=g).bfloat16()
     temb = m.timestep_embedding(0.5)
     meta = pkg.runner.VsaMeta(grid=grid, topk=args.dit_topk)
+    # under sequence parallelism the tiles go in the balanced order (the 3-frame slab's 48-row tiles spread over the
+    # ranks instead of filling the last one), the one-GPU denominator in the same order; one GPU alone keeps the
+    # reference order (the token-reduction timing pairs tiles in it)
+    order = args.dit_tile_order if ws > 1 else "reference"
     reps = max(2, min(args.steps, 3))
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     one_gpu = None
@@ -393,7 +402,7 @@ def dit_step_secondary(pkg, dev, stream, args, ws) -> dict:
         # the denominator of the strong-scaling ratio, in the same job: rank 0 alone runs the step on one GPU (the
         # other ranks wait at the barrier)
         if dist.get_rank() == 0:
-            r1 = pkg.runner.H3FastRunner(m)
+            r1 = pkg.runner.H3FastRunner(m, tile_order=order)
             for _ in range(2):
                 out = r1.forward(x, temb, None, None, meta, context=ctx)
             torch.cuda.synchronize()
@@ -407,7 +416,7 @@ def dit_step_secondary(pkg, dev, stream, args, ws) -> dict:
             torch.cuda.empty_cache()
         dist.barrier()
     sp = pkg.sp.SeqParallel() if ws > 1 else None
-    r = pkg.runner.H3FastRunner(m, sp, exchange=args.dit_exchange)
+    r = pkg.runner.H3FastRunner(m, sp, exchange=args.dit_exchange, tile_order=order)
     for _ in range(2):
         out = r.forward(x, temb, None, None, meta, context=ctx)
     torch.cuda.synchronize()
@@ -452,7 +461,7 @@ def dit_step_secondary(pkg, dev, stream, args, ws) -> dict:
         if r.transport == "peer" and not args.no_nccl_compare:
             # the same step with the NCCL all-to-all transport (all heads at once, no overlap), same job
             try:
-                rn = pkg.runner.H3FastRunner(m, sp, exchange="nccl")
+                rn = pkg.runner.H3FastRunner(m, sp, exchange="nccl", tile_order=order)
                 for _ in range(2):
                     out = rn.forward(x, temb, None, None, meta, context=ctx)
                 torch.cuda.synchronize()
@@ -515,7 +524,7 @@ def dit_step_secondary(pkg, dev, stream, args, ws) -> dict:
     if args.dit_qk_int8 or (args.dit_extras and ws == 1):
         try:
             # the same step with INT8 QK^T in the self-attention (tcgen05 kind::i8 scores)
-            r8 = pkg.runner.H3FastRunner(m, sp, qk_int8=True)
+            r8 = pkg.runner.H3FastRunner(m, sp, qk_int8=True, tile_order=order)
             for _ in range(2):
                 out = r8.forward(x, temb, None, None, meta, context=ctx)
             torch.cuda.synchronize()
@@ -546,7 +555,7 @@ def dit_step_secondary(pkg, dev, stream, args, ws) -> dict:
         try:
             # the same step with the FFN intermediate re-quantized in fc_in's epilogue under fixed per-block global
             # scales (recorded by the first forward) instead of the bf16 store + per-row quantization pass
-            rs = pkg.runner.H3FastRunner(m, sp, ffn_requant="static")
+            rs = pkg.runner.H3FastRunner(m, sp, ffn_requant="static", tile_order=order)
             for _ in range(2):
                 out = rs.forward(x, temb, None, None, meta, context=ctx)
             torch.cuda.synchronize()
@@ -581,7 +590,7 @@ def dit_step_secondary(pkg, dev, stream, args, ws) -> dict:
     res = {"grid": list(grid), "tokens": S, "blocks": cfg.blocks, "topk": args.dit_topk, "n_gpus": ws,
            "ms_per_step": ms, "steps": reps, "linear_tflop_per_step": lin / 1e12,
            "linear_share_tflops": lin / (ms * 1e-3) / 1e12, "output_finite": finite, "scaling": "strong",
-           "parallelism": f"sp{ws}"}
+           "parallelism": f"sp{ws}", "tile_order": order}
     if one_gpu is not None:
         res["one_gpu_ms_per_step_same_job"] = one_gpu
     if exchange is not None:
@@ -982,6 +991,9 @@ def main() -> None:
                     help="head exchange of the sequence-parallel config-5 step: peer-mapped buffers written by the "
                          "copy engines with head groups pipelined behind the attention (auto: when every rank maps "
                          "every other's memory), or NCCL all-to-alls")
+    ap.add_argument("--dit-tile-order", choices=["balanced", "reference"], default="balanced",
+                    help="tile order of the sequence-parallel config-5 step (N > 1): balanced (the edge tiles spread "
+                         "evenly over the ranks' shards) or the reference's (t, h, w) order")
     ap.add_argument("--no-nccl-compare", action="store_true",
                     help="with the peer transport, skip timing the same config-5 step over NCCL in the same job")
     ap.add_argument("--dit-reduction", default="", metavar="BEGIN:END[:SCALE]",

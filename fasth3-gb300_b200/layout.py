@@ -29,6 +29,9 @@ class TileLayout:
     n_tiles: int             # real tiles
     n_ext: int               # padded tile count
     rows: int
+    # int64 [n_tiles]: the (t, h, w)-order index of each tile when the tiles were reordered (``balanced_order``);
+    # None in the reference order
+    source: torch.Tensor | None = None
 
     def shard(self, first: int, last: int) -> "TileLayout":
         """The layout of tiles [first, last) as a standalone layout (rows renumbered from 0)."""
@@ -40,7 +43,8 @@ class TileLayout:
         slot = torch.cat([torch.arange(int(v)) + i * TILE for i, v in enumerate(vbs.tolist())]).to(torch.int32) \
             if rows else torch.zeros(0, dtype=torch.int32)
         real = min(max(self.n_tiles - first, 0), last - first)
-        return TileLayout(self.grid, perm, vbs, row0, slot, real, last - first, rows)
+        src = None if self.source is None else self.source[first:first + real].clone()
+        return TileLayout(self.grid, perm, vbs, row0, slot, real, last - first, rows, src)
 
 
 def tile_layout(T: int, H: int, W: int, pad_to: int = 2, cube=(4, 4, 4)) -> TileLayout:
@@ -61,6 +65,37 @@ def tile_layout(T: int, H: int, W: int, pad_to: int = 2, cube=(4, 4, 4)) -> Tile
     row0 = (vbs.cumsum(0) - vbs).to(torch.int32)
     slot = torch.cat([torch.arange(int(v)) + i * TILE for i, v in enumerate(vbs.tolist())]).to(torch.int32)
     return TileLayout((T, H, W), perm, vbs, row0, slot, n, n_ext, int(perm.numel()))
+
+
+def balanced_order(layout: TileLayout) -> TileLayout:
+    """The same tiles in an order that spreads the tiles of each size (valid-row count) evenly through the list, so
+    that every contiguous run of tiles -- one rank's shard under sequence parallelism -- holds close to its share of
+    the rows. In (t, h, w) order the smaller cubes of a latent's far edges sit together (the 48-row tiles of a
+    3-frame last time slab fill the last ranks' shards), and the ranks with only full tiles bound the step.
+
+    Each size class's k-th tile (of n in that class, in (t, h, w) order) takes the position key (k + 1/2) / n; tiles
+    are ordered by key, ties by their (t, h, w) index. Empty padding tiles stay at the end. Tokens inside a tile keep
+    their order, so per-tile work (quantization scales, tile means, scores of a tile pair) is unchanged; what moves is
+    the tile numbering, hence the order of each query tile's selected key tiles and, for equal scores, which tile the
+    top-k keeps."""
+    n = layout.n_tiles
+    vbs = layout.vbs[:n].to(torch.int64)
+    key = torch.empty(n, dtype=torch.float64)
+    for v in torch.unique(vbs).tolist():
+        idx = (vbs == v).nonzero().reshape(-1)
+        key[idx] = (torch.arange(idx.numel(), dtype=torch.float64) + 0.5) / idx.numel()
+    order = torch.sort(key, stable=True).indices
+    src = order if layout.source is None else layout.source[order]
+    pad = layout.n_ext - n
+    vbs_new = torch.cat([layout.vbs[:n][order], torch.zeros(pad, dtype=torch.int32)])
+    row0 = (vbs_new.cumsum(0) - vbs_new).to(torch.int32)
+    old0 = layout.tile_row0[:n].to(torch.int64)
+    rows = torch.cat([torch.arange(int(old0[t]), int(old0[t]) + int(vbs[t])) for t in order.tolist()]) if n else \
+        torch.zeros(0, dtype=torch.int64)
+    perm = layout.perm[rows]
+    slot = torch.cat([torch.arange(int(v)) + i * TILE for i, v in enumerate(vbs_new.tolist())]).to(torch.int32) \
+        if layout.rows else torch.zeros(0, dtype=torch.int32)
+    return TileLayout(layout.grid, perm, vbs_new, row0, slot, n, layout.n_ext, layout.rows, src)
 
 
 def rope_3d(layout: TileLayout, rot_dims: int = 96, theta: float = 10000.0) -> tuple[torch.Tensor, torch.Tensor]:

@@ -29,7 +29,8 @@ import torch
 import torch.distributed as dist
 
 from . import ops
-from .layout import TILE, TileLayout, compute_topk, rope_3d, rope_positions, tile_layout, tile_layout_from_metadata
+from .layout import (TILE, TileLayout, balanced_order, compute_topk, rope_3d, rope_positions, tile_layout,
+                     tile_layout_from_metadata)
 from .model import DiTModel, QuantLinear
 from .reduction import TokenReduction, pair_maps
 from .sp import PeerArena, SeqParallel, peer_copy_plan
@@ -260,7 +261,7 @@ class H3FastRunner:
 
     def __init__(self, model: DiTModel, sp: SeqParallel | VirtualSeqParallel | None = None, qk_int8: bool = False,
                  v_f16: bool = False, ffn_requant: str = "rows", exchange: str = "auto", head_groups: int | None = None,
-                 attn_kernel: str = "wide"):
+                 attn_kernel: str = "wide", tile_order: str = "reference"):
         self.model = model
         self.qk_int8 = bool(qk_int8)
         # FFN re-quantization between fc_in and fc_out: "rows" -- the reference's rule, the bf16 fc_in output
@@ -277,6 +278,13 @@ class H3FastRunner:
         if attn_kernel not in ("wide", "tile"):
             raise ValueError(f"attn_kernel must be 'wide' or 'tile', not {attn_kernel!r}")
         self.attn_kernel = "tile" if self.qk_int8 else attn_kernel
+        # tile order of a layout built from meta.grid: "reference" -- (t, h, w), the reference runner's; "balanced" --
+        # layout.balanced_order, the edge cubes' smaller tiles spread evenly so every rank's contiguous shard holds its
+        # share of rows (per token the same attention up to the order of each query tile's selected key tiles; a
+        # forward's result is the same at every rank count for either order)
+        if tile_order not in ("reference", "balanced"):
+            raise ValueError(f"tile_order must be 'reference' or 'balanced', not {tile_order!r}")
+        self.tile_order = tile_order
         # self-attention V tiles as f16 holding the E4M3 values (decoded once by the prologue, loaded by the PV MMAs as
         # is; the wide kernel's form), or, with the tile kernel, as E4M3 codes converted by the attention kernel on
         # every use (half the bytes in the prologue's writes and the exchange); the results are bit-identical. The
@@ -424,6 +432,11 @@ class H3FastRunner:
             full = tile_layout_from_metadata(meta.untile_combined_index, meta.variable_block_sizes, pad_to=2 * P)
         else:
             full = tile_layout(*meta.grid, pad_to=2 * P)
+        if self.tile_order == "balanced":
+            if by_meta:
+                raise ValueError("tile_order='balanced' needs a layout from meta.grid (metadata layouts keep their "
+                                 "prefix tiles first)")
+            full = balanced_order(full)
         if full.n_ext != full.n_tiles:
             raise ValueError(f"{full.n_tiles} tiles do not split into an even count per rank over {P} ranks")
         if rotary is None:
@@ -654,6 +667,8 @@ class H3FastRunner:
         maps between it and the full layout (``_pair_maps``, __init__.py:262-278), cached per plan."""
         if self.ex.world != 1:
             raise ValueError("token reduction runs on one rank (the reference runner is single-GPU)")
+        if self.tile_order != "reference":
+            raise ValueError("token reduction pairs tiles in the reference tile order")
         if tuple(plan.grid) != tuple(meta.grid) or plan.video_start != 0:
             raise ValueError(f"the reduction plan's grid {plan.grid} (video_start {plan.video_start}) is not "
                              f"the sequence's {tuple(meta.grid)}")

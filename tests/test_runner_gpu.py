@@ -228,6 +228,51 @@ def test_f16_v_runner_equals_e4m3_v_runner(pkg):
     assert float((w.float() - a.float()).norm() / a.float().norm()) < 0.2
 
 
+def test_balanced_tile_order(pkg):
+    """tile_order="balanced" (the 48-row tiles of the 3-frame slab spread through the list): the sharded forward equals
+    one rank's bit for bit; against the reference order, block 0's per-tile statistics and tile scores are the same
+    values renumbered, every query tile selects the same key tiles, and the output differs only by the order in which
+    each query tile's key tiles are accumulated (a gross bound after two blocks of NVFP4 re-quantization)."""
+    _, runner = pkg
+    from fasth3_b200 import layout
+    m, x, ctx, temb, meta = make(pkg, blocks=2, grid=(7, 16, 16))
+    rec = {}
+
+    def keep(tag):
+        def f(i, stage, rank, t):
+            if i == 0 and stage in ("prologue", "select"):
+                rec[(tag, stage)] = {k: v.clone() for k, v in t.items() if v is not None}
+        return f
+
+    rr, rb = runner.H3FastRunner(m), runner.H3FastRunner(m, tile_order="balanced")
+    rr.trace, rb.trace = keep("ref"), keep("bal")
+    ref = rr.forward(x, temb, None, None, meta, context=ctx)
+    bal = rb.forward(x, temb, None, None, meta, context=ctx)
+    for P in (2, 4):
+        got = runner.H3FastRunner(m, runner.VirtualSeqParallel(P), tile_order="balanced").forward(
+            x, temb, None, None, meta, context=ctx)
+        torch.cuda.synchronize()
+        assert torch.equal(got.view(torch.int16), bal.view(torch.int16)), P
+    src = layout.balanced_order(layout.tile_layout(*meta.grid)).source.to(DEV)
+    assert not torch.equal(src, torch.arange(src.numel(), device=DEV))
+    pb, pr = rec[("bal", "prologue")], rec[("ref", "prologue")]
+    for k in ("qs", "ks", "vs", "qp", "kp"):
+        assert torch.equal(pb[k], pr[k][:, src]), k
+    sb, sr = rec[("bal", "select")], rec[("ref", "select")]
+    assert torch.equal(sb["sc"], sr["sc"][:, src][:, :, src])
+    assert torch.equal(sb["num"], sr["num"][:, src])
+    k = meta.topk
+    assert bool((sb["num"] == k).all())
+    chosen_bal = torch.sort(src[sb["idx"][:, :, :k].long()], -1).values
+    chosen_ref = torch.sort(sr["idx"][:, src, :k].long(), -1).values
+    assert torch.equal(chosen_bal, chosen_ref)
+    assert float((bal.float() - ref.float()).norm() / ref.float().norm()) < 0.2
+    # a layout from metadata keeps its prefix tiles first: no balanced order
+    mp, xp, ctxp, tp, metap, rot = make_prefixed(pkg, blocks=1)
+    with pytest.raises(ValueError, match="balanced"):
+        runner.H3FastRunner(mp, tile_order="balanced").forward(xp, tp, None, rot, metap, context=ctxp)
+
+
 def test_static_ffn_requant_runner(pkg):
     """ffn_requant="static": the first forward runs the per-row path (its output equals the default runner's bit for
     bit) and records each block's fixed FFN global scale; later forwards quantize fc_in's output in its epilogue under
