@@ -28,6 +28,14 @@ class VsaArgs(ctypes.Structure):
     ]
 
 
+class PeerCopy(ctypes.Structure):
+    """Mirror of ``h3b_peer_copy``."""
+    _fields_ = [("dst", P), ("src", P), ("dpitch", SZ), ("spitch", SZ), ("width", SZ), ("height", SZ)]
+
+
+PEER_PUT_MAX_COPIES, PEER_PUT_MAX_FLAGS = 64, 16
+
+
 class Epilogue(ctypes.Structure):
     """Mirror of ``h3b_epilogue``."""
     _fields_ = [
@@ -101,6 +109,7 @@ SIGNATURES: dict[str, list] = {
     "h3b_peer_copy2d": [P, SZ, P, SZ, SZ, SZ, P],
     "h3b_peer_signal": [P, ctypes.c_uint32, P],
     "h3b_peer_wait": [P, I32, ctypes.c_uint32, ctypes.c_uint64, P],
+    "h3b_peer_put": [ctypes.POINTER(PeerCopy), I32, ctypes.POINTER(P), I32, ctypes.c_uint32, P, P],
     "h3b_selftest_wait_timeout": [ctypes.c_uint64, P],
 }
 _RESTYPES = {"h3b_last_error": ctypes.c_char_p, "h3b_version": ctypes.c_char_p,

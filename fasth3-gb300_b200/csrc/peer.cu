@@ -48,6 +48,66 @@ __global__ void peer_wait_kernel(const uint32_t* __restrict__ flags, int count, 
   }
 }
 
+// h3b_peer_put: the copies (row geometry in units of 1 << shift bytes) and flags, passed by value
+struct PutCopy {
+  char* dst;
+  const char* src;
+  uint64_t dpitch, spitch;
+  uint64_t row_units, units;
+};
+struct PutArgs {
+  PutCopy c[H3B_PEER_PUT_MAX_COPIES];
+  uint32_t* flags[H3B_PEER_PUT_MAX_FLAGS];
+  uint32_t* counter;
+  int n, n_flags;
+  uint32_t epoch;
+};
+
+// Every thread copies a grid-strided share of each region, four units in flight at a time; then each thread fences at
+// system scope, and the block's thread 0 (after the barrier and its own system fence, which covers the writes of the
+// block it observed) counts the block in. The block that counts last fences again and writes the flags with release
+// semantics at system scope: a reader whose acquire load sees a flag sees every byte of every copy. The counter is
+// left at zero for the next put. Nothing here waits on another block or GPU.
+template <typename U>
+__global__ void __launch_bounds__(256) peer_put_kernel(const __grid_constant__ PutArgs a) {
+  const uint64_t nthr = (uint64_t)gridDim.x * blockDim.x;
+  const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (int c = 0; c < a.n; ++c) {
+    const PutCopy& d = a.c[c];
+    for (uint64_t u0 = tid; u0 < d.units; u0 += 4 * nthr) {
+      U v[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint64_t u = u0 + k * nthr;
+        if (u < d.units) {
+          const uint64_t row = u / d.row_units, col = u - row * d.row_units;
+          v[k] = *reinterpret_cast<const U*>(d.src + row * d.spitch + col * sizeof(U));
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint64_t u = u0 + k * nthr;
+        if (u < d.units) {
+          const uint64_t row = u / d.row_units, col = u - row * d.row_units;
+          *reinterpret_cast<U*>(d.dst + row * d.dpitch + col * sizeof(U)) = v[k];
+        }
+      }
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const unsigned prev = atomicAdd(a.counter, 1u);
+    if (prev == gridDim.x - 1) {
+      __threadfence_system();
+      for (int f = 0; f < a.n_flags; ++f)
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.flags[f]), "r"(a.epoch) : "memory");
+      atomicExch(a.counter, 0u);
+    }
+  }
+}
+
 typedef CUresult (*WriteValueFn)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
 
 WriteValueFn write_value_fn() {
@@ -152,6 +212,63 @@ extern "C" int h3b_peer_signal(uint32_t* flag, uint32_t epoch, cudaStream_t stre
   // default flags: the write is ordered after the stream's earlier work and preceded by a system-wide fence
   if (fn(reinterpret_cast<CUstream>(stream), reinterpret_cast<CUdeviceptr>(flag), epoch, 0) != CUDA_SUCCESS)
     return set_error(H3B_ECUDA, "peer_signal: cuStreamWriteValue32 failed");
+  return H3B_OK;
+}
+
+extern "C" int h3b_peer_put(const h3b_peer_copy* copies, int n_copies, uint32_t* const* flags, int n_flags,
+                            uint32_t epoch, uint32_t* counter, cudaStream_t stream) {
+  h3b::clear_error();
+  H3B_REQUIRE(n_copies >= 0 && n_copies <= H3B_PEER_PUT_MAX_COPIES, "peer_put: %d copies (at most %d)", n_copies,
+              H3B_PEER_PUT_MAX_COPIES);
+  H3B_REQUIRE(n_flags >= 0 && n_flags <= H3B_PEER_PUT_MAX_FLAGS, "peer_put: %d flags (at most %d)", n_flags,
+              H3B_PEER_PUT_MAX_FLAGS);
+  H3B_REQUIRE(n_copies == 0 || copies, "peer_put: null copies");
+  H3B_REQUIRE(n_flags == 0 || flags, "peer_put: null flags");
+  H3B_REQUIRE(counter && (reinterpret_cast<uintptr_t>(counter) & 3u) == 0, "peer_put: null or unaligned counter");
+  h3b::PutArgs a;
+  memset(&a, 0, sizeof(a));
+  // 16-byte units when every address, pitch and width allows them, else 4-byte units
+  uintptr_t bits = 0;
+  for (int i = 0; i < n_copies; ++i) {
+    const h3b_peer_copy& c = copies[i];
+    if (c.width == 0 || c.height == 0) continue;
+    H3B_REQUIRE(c.dst && c.src, "peer_put: copy %d has a null pointer", i);
+    H3B_REQUIRE(c.width <= c.dpitch && c.width <= c.spitch, "peer_put: copy %d's width exceeds a pitch", i);
+    bits |= reinterpret_cast<uintptr_t>(c.dst) | reinterpret_cast<uintptr_t>(c.src) | c.dpitch | c.spitch | c.width;
+  }
+  H3B_REQUIRE((bits & 3u) == 0, "peer_put: addresses, pitches and widths must be multiples of 4 bytes");
+  const int shift = (bits & 15u) == 0 ? 4 : 2;
+  uint64_t total = 0;
+  for (int i = 0; i < n_copies; ++i) {
+    const h3b_peer_copy& c = copies[i];
+    if (c.width == 0 || c.height == 0) continue;
+    h3b::PutCopy& d = a.c[a.n++];
+    d.dst = static_cast<char*>(c.dst);
+    d.src = static_cast<const char*>(c.src);
+    d.dpitch = c.dpitch;
+    d.spitch = c.spitch;
+    d.row_units = c.width >> shift;
+    d.units = d.row_units * c.height;
+    total += d.units;
+  }
+  for (int f = 0; f < n_flags; ++f) {
+    H3B_REQUIRE(flags[f] && (reinterpret_cast<uintptr_t>(flags[f]) & 3u) == 0, "peer_put: flag %d null or unaligned",
+                f);
+    a.flags[f] = flags[f];
+  }
+  a.n_flags = n_flags;
+  a.counter = counter;
+  a.epoch = epoch;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const uint64_t want = (total + 4 * 256 - 1) / (4 * 256);
+  const int blocks = (int)(want < 1 ? 1 : (want > (uint64_t)(2 * sms) ? 2 * sms : want));
+  if (shift == 4)
+    h3b::peer_put_kernel<int4><<<blocks, 256, 0, stream>>>(a);
+  else
+    h3b::peer_put_kernel<uint32_t><<<blocks, 256, 0, stream>>>(a);
+  H3B_LAUNCH_CHECK("peer_put");
   return H3B_OK;
 }
 

@@ -21,6 +21,7 @@ the all-to-all (NCCL), the timestep MLP and the token permutation.
 """
 from __future__ import annotations
 
+import ctypes
 import dataclasses
 import math
 from dataclasses import dataclass, field
@@ -351,6 +352,11 @@ class H3FastRunner:
                 raise ValueError(f"head_groups={G}: must divide the {Hl} heads per rank; more than one group needs "
                                  f"the peer or virtual transport")
         self.head_groups = G
+        # peer transport: send the tile statistics (about 1 MB per receiver at 8 ranks) with one SM kernel
+        # (h3b_peer_put) instead of five copies and a flag write per receiver on the copy engines. Off by default: on
+        # 2 GPUs it left the wait for the statistics unchanged (the wait there is skew between the ranks, not copy
+        # latency), and the copy-engine form is the one measured on 8
+        self.stats_put = False
         self._epoch = 0  # exchanges so far (the peer transport's flag value), the same count on every rank
         self._copy_streams: list | None = None
 
@@ -943,22 +949,54 @@ class H3FastRunner:
         if b["qkv_s"].shape[0] == 2:
             parts.append(("v_x", b["vb"], 1, b["vb"].element_size()))
         streams = self._peer_streams()
+        put = self._peer_stats_put(st, stats) if self.stats_put else None
+        if put is not None:
+            # the tile statistics to every rank in one SM kernel on the compute stream, which raises each receiver's
+            # flag slot 0 after the last byte; the Q/K/V planes (large) on the copy engines beside it
+            arr, n, flags, n_flags, counter = put
+            call("h3b_peer_put", arr, n, flags, n_flags, e, counter.data_ptr(), main.cuda_stream)
         for k in range(P):
             p = (r + 1 + k) % P
             cs = streams[p]
             cs.wait_event(ready)
             h = cs.cuda_stream
-            for nm in stats:
-                src = b[nm]
-                T = src[0, 0].numel()
-                so, spitch, do, dpitch, w, rows = peer_copy_plan("stats", r, p, 0, dict(dims, n=st.n_local, T=T, es=4))
-                call("h3b_peer_copy2d", ar.ptr(p, nm + "_all", do), dpitch, src.data_ptr() + so, spitch, w, rows, h)
-            call("h3b_peer_signal", ar.flag(p, 0, r), e, h)
+            if put is None:
+                for nm in stats:
+                    so, spitch, do, dpitch, w, rows = self._stats_plan(st, nm, p)
+                    call("h3b_peer_copy2d", ar.ptr(p, nm + "_all", do), dpitch, b[nm].data_ptr() + so, spitch, w,
+                         rows, h)
+                call("h3b_peer_signal", ar.flag(p, 0, r), e, h)
             for g in range(self.head_groups):
                 for region, src, planes, es in parts:
                     so, spitch, do, dpitch, w, rows = peer_copy_plan("qkv", r, p, g, dict(dims, planes=planes, es=es))
                     call("h3b_peer_copy2d", ar.ptr(p, region, do), dpitch, src.data_ptr() + so, spitch, w, rows, h)
                 call("h3b_peer_signal", ar.flag(p, 1 + g, r), e, h)
+
+    def _stats_plan(self, st: _RankState, nm: str, p: int) -> tuple:
+        """peer_copy_plan of tile statistic ``nm`` from this rank to rank p."""
+        T = st.b[nm][0, 0].numel()
+        return peer_copy_plan("stats", self.ex.sp.rank, p, 0, dict(self._peer_dims(st), n=st.n_local, T=T, es=4))
+
+    def _peer_stats_put(self, st: _RankState, stats: tuple):
+        """h3b_peer_put's arguments for this rank's tile statistics to every rank (flag slot 0 of each), built once
+        per layout; None when they exceed one put (more than 64 copies)."""
+        from ._lib import PEER_PUT_MAX_COPIES, PeerCopy
+        hit = st.b.get("_stats_put")
+        if hit is not None and hit[0] == stats:
+            return hit[1]
+        P, r, ar, b = self.ex.world, self.ex.sp.rank, st.arena, st.b
+        put = None
+        if P * len(stats) <= PEER_PUT_MAX_COPIES:
+            copies = []
+            for p in range(P):
+                for nm in stats:
+                    so, spitch, do, dpitch, w, rows = self._stats_plan(st, nm, p)
+                    copies.append(PeerCopy(ar.ptr(p, nm + "_all", do), b[nm].data_ptr() + so, dpitch, spitch, w, rows))
+            flags = (ctypes.c_void_p * P)(*[ar.flag(p, 0, r) for p in range(P)])
+            counter = torch.zeros(1, device=self.dev, dtype=torch.int32)
+            put = ((PeerCopy * len(copies))(*copies), len(copies), flags, P, counter)
+        b["_stats_put"] = (stats, put)
+        return put
 
     def _peer_send_out(self, st: _RankState, g: int) -> None:
         """Heads -> sequence of head group g, enqueued after its attention: chunk p of the group's output (rank p's

@@ -385,6 +385,25 @@ int h3b_peer_copy2d(void* dst, size_t dpitch, const void* src, size_t spitch, si
 /* Writes `epoch` to a flag word (local or in a mapped peer allocation) after the stream's earlier work, preceded by
  * a system-scope fence, so a reader that sees the value also sees the data copied before it on this stream. */
 int h3b_peer_signal(uint32_t* flag, uint32_t epoch, cudaStream_t stream);
+/* One 2D region of h3b_peer_put: `height` rows of `width` bytes, pitches in bytes. */
+typedef struct h3b_peer_copy {
+  void* dst;
+  const void* src;
+  size_t dpitch;
+  size_t spitch;
+  size_t width;
+  size_t height;
+} h3b_peer_copy;
+#define H3B_PEER_PUT_MAX_COPIES 64
+#define H3B_PEER_PUT_MAX_FLAGS 16
+/* Stream-ordered: copies up to 64 2D regions with the SMs (stores into a mapped peer allocation travel over NVLink),
+ * then writes `epoch` into each of flags[0..n_flags) once every copied byte is visible system-wide, so a reader that
+ * sees a flag sees all the copies. One kernel, for small transfers to many peers, where a run of h3b_peer_copy2d and
+ * h3b_peer_signal calls is bound by the copy engines' per-copy latency. Addresses, pitches and widths are multiples
+ * of 4 bytes. `counter` is a device word of the caller, zero before the call and left zero after it, with at most
+ * one put in flight per counter. The copies and flags arrays are read on the host. */
+int h3b_peer_put(const h3b_peer_copy* copies, int n_copies, uint32_t* const* flags, int n_flags, uint32_t epoch,
+                 uint32_t* counter, cudaStream_t stream);
 /* Enqueues a one-block kernel that waits until every one of flags[0..count) reaches `epoch` (32-bit wrap-around
  * compare). The wait is bounded (limit_ns per flag, at most 10 s; 0 means 10 s); when it expires the kernel sets the
  * exchange status word (dst[3] of h3b_status_async) to H3B_ETIMEOUT and returns, and later waits return at once

@@ -79,3 +79,22 @@ def test_ops_refuse_cpu_tensors(ops):
     x = torch.zeros(4, 64, dtype=torch.bfloat16)
     with pytest.raises(RuntimeError, match="CUDA"):
         ops.quant_fp8_rows(x, torch.zeros(4, 64, dtype=torch.uint8), torch.zeros(4))
+
+
+def test_peer_put_rejects(h3b):
+    """h3b_peer_put checks its arguments on the host before any launch: unaligned widths, too many copies or flags,
+    a missing counter."""
+    from fasth3_b200._lib import PEER_PUT_MAX_COPIES, PeerCopy
+    lib = h3b.lib()
+    fake = 1 << 20  # never dereferenced: every call below fails its checks first
+    ok = PeerCopy(fake, fake, 64, 64, 32, 2)
+    odd = PeerCopy(fake, fake, 64, 64, 30, 2)
+    flags = (ctypes.c_void_p * 1)(fake)
+    cases = [((PeerCopy * 1)(odd), 1, flags, 1, fake, "multiples of 4"),
+             ((PeerCopy * 1)(ok), PEER_PUT_MAX_COPIES + 1, flags, 1, fake, "copies"),
+             ((PeerCopy * 1)(ok), 1, flags, 17, fake, "flags"),
+             ((PeerCopy * 1)(ok), 1, flags, 1, None, "counter"),
+             ((PeerCopy * 1)(PeerCopy(fake, fake, 16, 64, 32, 2)), 1, flags, 1, fake, "pitch")]
+    for arr, n, fl, nf, counter, what in cases:
+        assert lib.h3b_peer_put(arr, n, fl, nf, 1, counter, None) == 1, what
+        assert what in _err(lib), (what, _err(lib))

@@ -322,3 +322,38 @@ def test_exchange_wait_expires_raises_and_later_waits_skip(ops):
     ops.peer_wait(flags, 3, 30_000_000)   # passed long ago (wrap-around compare)
     torch.cuda.synchronize()
     ops.check_status()
+
+
+@pytest.mark.parametrize("aligned", [True, False])
+def test_peer_put_copies_then_raises_the_flags(ops, aligned):
+    """h3b_peer_put (the SM form of the peer transport's small copies): 2D regions of several geometries land where
+    cudaMemcpy2D would put them (16-byte units when every address, pitch and width allows, else 4-byte units), every
+    flag holds the epoch afterwards, the counter is back at zero, and a bounded wait on the flags passes at once."""
+    import ctypes
+
+    from fasth3_b200._lib import PeerCopy, call
+    g = torch.Generator(device=DEV).manual_seed(5)
+    src = torch.randint(0, 2 ** 31 - 1, (3 << 20,), device=DEV, generator=g, dtype=torch.int32)
+    dst = torch.zeros(4 << 20, device=DEV, dtype=torch.int32)
+    want = dst.clone()
+    sb, db = src.view(torch.uint8), want.view(torch.uint8)
+    e = 0 if aligned else 4  # byte skew of every address, pitch and width
+    geo = [(0, 4096, 0, 8192, 1008, 40), (64 << 10, 65536 + e, 1 << 20, 131072 + e, 64512 + e, 5),
+           (2 << 20, 512 + e, 3 << 20, 768, 256 + e, 700), (1 << 10, 64, 6 << 20, 64, 16, 1), (0, 16, 0, 16, 0, 3)]
+    copies = []
+    for so, sp, do, dp, w, h in geo:
+        so, do = so + e, do + e
+        for row in range(h):
+            db[do + row * dp:do + row * dp + w] = sb[so + row * sp:so + row * sp + w]
+        copies.append(PeerCopy(dst.data_ptr() + do, src.data_ptr() + so, dp, sp, w, h))
+    flags = torch.zeros(3, device=DEV, dtype=torch.int32)
+    counter = torch.zeros(1, device=DEV, dtype=torch.int32)
+    fl = (ctypes.c_void_p * 3)(*[flags.data_ptr() + 4 * i for i in range(3)])
+    s = torch.cuda.current_stream().cuda_stream
+    for epoch in (11, 12):
+        call("h3b_peer_put", (PeerCopy * len(copies))(*copies), len(copies), fl, 3, epoch, counter.data_ptr(), s)
+        ops.peer_wait(flags, epoch, 100_000_000)
+        torch.cuda.synchronize()
+        assert torch.equal(dst, want)
+        assert flags.tolist() == [epoch] * 3 and int(counter) == 0
+    ops.check_status()

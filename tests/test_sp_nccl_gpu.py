@@ -1,6 +1,7 @@
 """The sequence-parallel block loop on 2 GPUs: the output of two ranks (one process per GPU, head exchange around
-attention over the peer transport -- copy engines into peer-mapped buffers, head groups pipelined -- and over NCCL
-all-to-alls) equals the single-GPU output bit for bit. Skipped with fewer than two GPUs."""
+attention over the peer transport -- copy engines into peer-mapped buffers, head groups pipelined; also with the tile
+statistics sent by the SM put kernel -- and over NCCL all-to-alls) equals the single-GPU output bit for bit. Skipped
+with fewer than two GPUs."""
 from __future__ import annotations
 
 import os
@@ -44,11 +45,13 @@ def _rank(rank, world, port, q):
         temb = m.timestep_embedding(0.5)
         meta = pkg.runner.VsaMeta(grid=grid, topk=8)
         outs = {}
-        for exchange in ("peer", "nccl"):
+        for name in ("peer", "nccl", "peer+put"):
+            exchange = name.split("+")[0]
             r = pkg.runner.H3FastRunner(m, pkg.sp.SeqParallel(), exchange=exchange)
             assert r.transport == exchange, (r.transport, r.transport_note)
+            r.stats_put = name.endswith("+put")  # tile statistics by the SM kernel (h3b_peer_put)
             # two forwards: the peer transport's flags carry on counting from the first into the second
-            outs[exchange] = [r.forward(x, temb, None, None, meta, context=ctx) for _ in range(2)]
+            outs[name] = [r.forward(x, temb, None, None, meta, context=ctx) for _ in range(2)]
             torch.cuda.synchronize()
             r.close()
         dist.barrier()
