@@ -934,7 +934,8 @@ class H3FastRunner:
     def _peer_send_heads(self, st: _RankState, stats: tuple) -> None:
         """Sequence -> heads over the peer transport, enqueued after the prologue: to every rank p (itself included),
         on p's copy stream, the tile statistics of p's heads into p's [Hl, n_all, ...] buffers at this rank's tile
-        columns, then flag slot 0; then head group by head group the Q/K/V planes of p's heads g*Hg .. into p's
+        columns, then flag slot 0 (with ``stats_put``: all ranks' statistics and flags by one h3b_peer_put kernel on
+        the compute stream instead); then head group by head group the Q/K/V planes of p's heads g*Hg .. into p's
         [planes, G, P, Hg, rows_pad, 128] buffer at (g, this rank), then flag slot 1 + g. Nothing here overwrites
         what a receiver still reads: a rank sends block i+1 only after its own gate quantizer of block i, which waited
         for every rank's attention outputs of block i, i.e. after every rank's last read of its receive buffers."""

@@ -107,3 +107,52 @@ def body_arena_alloc_fails_on_one_rank(rank, world, pkg):
 def test_arena_setup_failure_reaches_every_rank():
     res = _run("test_peer_plan:body_arena_alloc_fails_on_one_rank")
     assert all(v == "ok" for v in res.values()), res
+
+
+# ------------------------------------------------------------------------------------------------ SM statistics put
+class _FakeArena:
+    """Addresses only: rank p's allocation at (p + 1) << 40, region k of ``names`` at k << 32, flags at 1 << 39."""
+
+    def __init__(self, names, world):
+        self.names, self.world = list(names), world
+
+    def ptr(self, p, name, off=0):
+        return ((p + 1) << 40) + (self.names.index(name) << 32) + off
+
+    def flag(self, p, slot, sender):
+        return ((p + 1) << 40) + (1 << 39) + 4 * (slot * self.world + sender)
+
+
+_S5, _S6 = ("qs", "ks", "vs", "qp", "kp"), ("qs", "ks", "vs", "qp", "kp", "vp")
+
+
+@pytest.mark.parametrize("P,r,stats", [(8, 3, _S5), (2, 1, _S6), (11, 0, _S6)])
+def test_stats_put_arguments_follow_the_copy_plan(h3b, P, r, stats):
+    """The tile statistics' h3b_peer_put arguments (runner.stats_put): one copy per (receiver, statistic) with the
+    geometry the copy-engine path uses, each receiver's flag slot 0 for this sender, built once per layout; when
+    the copies exceed one put (64) the runner keeps the copy-engine path."""
+    import types
+
+    from fasth3_b200._lib import PEER_PUT_MAX_COPIES
+    from fasth3_b200.runner import H3FastRunner
+    H, n, D = 8 * P, 6, 128
+    b = {nm: torch.zeros(H, n, *((D,) if nm.endswith("p") else ()), dtype=torch.float32) for nm in stats}
+    st = types.SimpleNamespace(b=b, n_local=n, rows_pad=n * 64, arena=_FakeArena([nm + "_all" for nm in stats], P))
+    me = types.SimpleNamespace(ex=types.SimpleNamespace(world=P, sp=types.SimpleNamespace(rank=r)), dev="cpu",
+                               heads=H, head_groups=1, head_dim=D)
+    me._peer_dims = types.MethodType(H3FastRunner._peer_dims, me)
+    me._stats_plan = types.MethodType(H3FastRunner._stats_plan, me)
+    put = H3FastRunner._peer_stats_put(me, st, stats)
+    if P * len(stats) > PEER_PUT_MAX_COPIES:
+        assert put is None
+        return
+    arr, count, flags, n_flags, counter = put
+    assert count == P * len(stats) and n_flags == P and int(counter) == 0
+    for p in range(P):
+        assert flags[p] == st.arena.flag(p, 0, r)
+        for j, nm in enumerate(stats):
+            c = arr[p * len(stats) + j]
+            so, sp_, do, dp, w, rows = me._stats_plan(st, nm, p)
+            want = (st.arena.ptr(p, nm + "_all", do), b[nm].data_ptr() + so, dp, sp_, w, rows)
+            assert (c.dst, c.src, c.dpitch, c.spitch, c.width, c.height) == want, (p, nm)
+    assert H3FastRunner._peer_stats_put(me, st, stats) is put  # cached per layout
